@@ -1,0 +1,353 @@
+#!/usr/bin/env python
+"""Decode throughput of DISMOEN's per-token decode step on B200 (libdismoen_cuda.so).
+
+Workload: the full 40-block Qwen3.6-35B-A3B-shaped model
+([GDN, GDN, GDN, GatedAttn] x 10, hidden 2048, 256 experts top-8 + 1 shared in 4-bit
+group-64, vocab 151936), random-init weights generated on the device, a 4096-token random
+prompt (seed 2) processed untimed, then W warm-up and K timed greedy decode steps, batch 1.
+
+  value    tokens/s of K decode steps replayed on the device (token fed back on the GPU,
+           every weight byte of a step read from HBM: the 4 GB per step is far larger than
+           the 126 MB L2, so no flush is needed), CUDA events on the library stream.
+  e2e      the same steps through the C ABI with host buffers: dm_decode_step(token_in) ->
+           token_out per step (4 B host->device, 8 B device->host inside the timed region).
+  roofline the GDN input-projection GEMV (12352 x 2048 bf16 = 50.6 MB per launch), timed
+           alone with CUDA events on the library stream, against MEASURED_PEAKS.json.
+
+Multi-GPU (torchrun, one process per GPU): batch-1 decode does not shard; every rank runs
+its own replica (scaling "weak"); value = total tokens of all ranks / max-over-ranks time.
+
+`--impl reference` times the CPU restatement of the reference engine (oracle/liboracle.so,
+all host threads) on a bounded sample of the same workload; the reference Mojo engine
+cannot be built here.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+ALG_BYTES_NOTE = ("weights 3.844 GB (GDN 2.023, attention 0.545, router/norms 0.042, "
+                  "9 active 4-bit experts x 40 layers 0.610, lm_head 0.622) + KV + GDN state")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--prompt-len", type=int, default=4096)
+    ap.add_argument("--seed", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-steps", type=int, default=2)
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+# ---- per-step algorithmic bytes (bs1, config 2) ------------------------------------------
+def step_bytes(cfg, ctx_len: int) -> int:
+    H, I, E, G = cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts, cfg.quant_group_size
+    n_att, n_gdn = cfg.num_attention_layers(), cfg.num_gdn_layers()
+    gdn_w = ((cfg.qkv_dim + cfg.z_dim + 2 * cfg.linear_num_value_heads) * H + cfg.qkv_dim * 4
+             + H * cfg.z_dim + cfg.linear_value_head_dim + 2 * H) * 2 + 8 * cfg.linear_num_value_heads
+    D, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+    att_w = ((2 * Hq * D + 2 * Hkv * D) * H + H * Hq * D + 2 * D + 2 * H) * 2
+    router = (E + 1) * H * 2 * cfg.num_hidden_layers
+    experts = (cfg.num_experts_per_tok + 1) * cfg.expert_bytes() * cfg.num_hidden_layers
+    head = cfg.vocab_size * H * 2 + H * 2 + H * 2  # lm_head, final norm, embedding row
+    kv = n_att * (ctx_len + 1) * 2 * Hkv * D * 2
+    state = n_gdn * (2 * cfg.linear_num_value_heads * cfg.linear_value_head_dim * cfg.linear_key_head_dim * 4
+                     + 4 * cfg.qkv_dim * 4)
+    return n_gdn * gdn_w + n_att * att_w + router + experts + head + kv + state
+
+
+# ---- clocks during the timed region -----------------------------------------------------
+class ClockSampler:
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, device: int, period_s: float = 0.01):
+        self.samples, self.reasons = [], 0
+        self.period = period_s
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: report null clocks
+            self.err = str(e)
+            self.max_mhz = None
+
+    def _run(self):
+        nv = self.nv
+        get_r = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= int(get_r(self.h))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._stop = threading.Event()
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        names = [n for b, n in self.REASONS.items() if self.reasons & b and b != 0x1]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+def measured_peak():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(name: str):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name>.md, if any."""
+    p = os.path.join(REPO, "profiles", name + ".md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("dram_bytes_per_launch:"):
+            return int(float(line.split(":", 1)[1].strip()))
+    return None
+
+
+# ---- CPU baseline: the oracle port on host cores ----------------------------------------
+def cpu_sample(cfg_full, seed: int, ctx_len: int, steps: int):
+    """Times one [GDN, GDN, GDN, GatedAttn] cycle at full shape and the lm_head on the host
+    (all OpenMP threads); a 40-block token costs 10 cycles + 1 head."""
+    import dataclasses
+
+    import oracle
+    from disk_streaming_moe_engine_b200 import synth
+    cyc = dataclasses.replace(cfg_full, num_hidden_layers=4)
+    m = synth.synth_model(cyc, seed)
+    om = oracle.OracleModel(m)
+    st = oracle.OracleState(cyc, ctx_len + steps + 4)
+    rng = np.random.default_rng(seed)
+    kv = rng.standard_normal(st.k[0, :ctx_len].shape).astype(np.float32)
+    st.k[0, :ctx_len] = synth.f32_to_bf16(kv)
+    st.v[0, :ctx_len] = synth.f32_to_bf16(kv[::-1].copy())
+    st.st.len = ctx_len
+    lib = oracle.load()
+    x = np.zeros(cyc.hidden_size, np.float32)
+    y = np.zeros_like(x)
+    logits = np.empty(cyc.vocab_size, np.float32)
+    t_cycle, t_head = [], []
+    for i in range(steps + 1):
+        x[:] = synth.bf16_to_f32(m["embed"][(7 * i) % cyc.vocab_size])
+        t0 = time.perf_counter()
+        for l in range(4):
+            lib.or_block_forward(oracle.C.byref(om.model), oracle.C.byref(st.st), l, x.ctypes.data, y.ctypes.data,
+                                 None)
+            x[:] = y
+        t1 = time.perf_counter()
+        lib.or_head(oracle.C.byref(om.model), x.ctypes.data, logits.ctypes.data)
+        t2 = time.perf_counter()
+        st.st.len += 1
+        if i > 0:  # the first iteration warms caches
+            t_cycle.append(t1 - t0)
+            t_head.append(t2 - t1)
+    tc = statistics.median(t_cycle)
+    th = statistics.median(t_head)
+    per_token = 10 * tc + th
+    return {"per_token_s": per_token, "cycle_s": tc, "head_s": th, "cores": oracle.get_threads(),
+            "steps": steps}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    from disk_streaming_moe_engine_b200 import build, preset
+    build.build_oracle()
+    cfg = preset("full")
+    k = max(1, min(args.steps, 8))
+    s = cpu_sample(cfg, args.seed, args.prompt_len, k)
+    tps = 1.0 / s["per_token_s"]
+    line = {
+        "impl": "reference", "metric": "decode tok/s, 35B-A3B-shape 4-bit, bs1", "value": tps, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": s["steps"], "warmup": 1, "ms_per_step": s["per_token_s"] * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit experts, bs1, ctx 4096",
+                   "global_batch": 1, "seq_len": args.prompt_len, "parallelism": "host threads"},
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": s["cores"], "kind": "port",
+                         "sample": f"CPU restatement (oracle/liboracle.so) of the reference decode step: one "
+                                   f"[GDN,GDN,GDN,Attn] cycle at full shape + lm_head, median of {s['steps']} "
+                                   f"tokens at ctx {args.prompt_len}; token time = 10 x cycle + head "
+                                   f"(cycle {s['cycle_s']*1e3:.1f} ms, head {s['head_s']*1e3:.1f} ms)"},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, rank, local, world):
+    import torch
+
+    from disk_streaming_moe_engine_b200 import Engine, RuntimeConfig, _lib, build, preset
+    build.build()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    cfg = preset("full")
+    ctx_cap = args.prompt_len + args.warmup + 2 * args.steps + 64
+    eng = Engine(cfg, RuntimeConfig.for_context(ctx_cap), device=local)
+    eng.synth_on_device(args.seed)
+    eng.weights_check()
+    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+    prompt = np.random.default_rng(args.seed).integers(0, cfg.vocab_size, args.prompt_len).astype(np.int32)
+    eng.seq_reset(0)
+    t0 = time.perf_counter()
+    _, nxt = eng.forward(prompt, want_logits=False)  # untimed prefill, one decode step per token
+    prefill_s = time.perf_counter() - t0
+    eng.set_token(nxt)
+    eng.enqueue_decode(args.warmup)
+    eng.sync()
+
+    # ---- value: device-resident greedy decode ----
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        ev0.record(stream)
+        eng.enqueue_decode(args.steps)
+        ev1.record(stream)
+        ev1.synchronize()
+    eng.sync()
+    barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ctx_mid = args.prompt_len + args.warmup + args.steps // 2
+    value = world * args.steps / (ms / 1e3)
+
+    # ---- e2e: through the C ABI with host buffers ----
+    tok = int(nxt)
+    barrier()
+    with ClockSampler(local, 0.02) as clocks_e2e:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            tok, _ = eng.decode_step(tok)
+        ev1.record(stream)
+        ev1.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(ev0.elapsed_time(ev1))
+    e2e = world * args.steps / (ms_e2e / 1e3)
+
+    # ---- roofline of the dominant kernel and the per-kernel breakdown ----
+    peak, peak_kind = measured_peak()
+    kernels = {}
+    names = {_lib.DM_KERNEL_MIXER_IN: "in_proj", _lib.DM_KERNEL_MIXER_OUT: "out_proj",
+             _lib.DM_KERNEL_MIXER_CORE: "core", _lib.DM_KERNEL_ROUTER: "router", _lib.DM_KERNEL_MOE_UP: "moe_up",
+             _lib.DM_KERNEL_MOE_DOWN: "moe_down"}
+    for layer, tag in ((0, "gdn"), (3, "attn")):
+        for which, nm in names.items():
+            kms, kb = eng.time_kernel(which, layer, 20)
+            kernels[f"{tag}_{nm}"] = {"us": round(kms * 1e3, 2), "bytes": kb, "GBps": round(kb / kms / 1e6, 1)}
+    kms, kb = eng.time_kernel(_lib.DM_KERNEL_HEAD, 0, 10)
+    kernels["lm_head"] = {"us": round(kms * 1e3, 2), "bytes": kb, "GBps": round(kb / kms / 1e6, 1)}
+    dom = kernels["gdn_in_proj"]
+    achieved = dom["bytes"] / (dom["us"] * 1e-6) / 1e9
+    traffic = profiled_traffic("gemv_gdn_in_proj_config2")
+    sb = step_bytes(cfg, ctx_mid)
+    per_gpu_tps = args.steps / (ms / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        build.build_oracle()
+        s = cpu_sample(cfg, args.seed, args.prompt_len, args.cpu_sample_steps)
+        cpu = {"value": 1.0 / s["per_token_s"], "unit": "tokens/s", "cores": s["cores"], "kind": "port",
+               "sample": f"oracle/liboracle.so on host cores: one full-shape [GDN,GDN,GDN,Attn] cycle + lm_head, "
+                         f"median of {s['steps']} tokens at ctx {args.prompt_len}; token = 10 x cycle + head"}
+
+    kps = eng.kernels_per_step()
+    c = clocks.summary()
+    line = {
+        "metric": "decode tok/s, 35B-A3B-shape 4-bit, bs1", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init weights on device, random prompt, seed 2)",
+        "config": {"workload": "config2: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit g64 experts, bs1",
+                   "global_batch": world, "seq_len": args.prompt_len, "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2 (4 GB of weights per step)"},
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "peak_source": peak_kind,
+                     "kernel": "gemv_bf16_kernel<2048,RMSNORM> GDN in-projection, 50.6 MB/launch"},
+        "step_roofline": {"bytes_per_token": sb, "achieved_GBps": sb * per_gpu_tps / 1e9,
+                          "frac": sb * per_gpu_tps / 1e9 / peak, "bytes": ALG_BYTES_NOTE},
+        "kernels": kernels,
+        "cpu_baseline": cpu,
+        "clocks": c,
+        "clocks_e2e": clocks_e2e.summary(),
+        "gpu_launches": kps * args.steps,
+        "prefill_s": round(prefill_s, 2),
+    }
+    eng.close()
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    rank, local, world = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, local, world)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

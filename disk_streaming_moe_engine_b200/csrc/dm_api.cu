@@ -1,0 +1,1252 @@
+// dm_api.cu — host runtime and C ABI of libdismoen_cuda.so.
+//
+// The context owns one device arena holding every weight, state and scratch buffer; it is
+// sized from the config at creation, so no allocation happens on the decode path.  Layer
+// kernels are issued on the context stream with programmatic dependent launch; the decode
+// step (embedding, all blocks, head) is captured once per sequence slot into a CUDA graph
+// and replayed per token.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "dismoen_cuda.h"
+#include "dm_internal.h"
+#include "dm_kernels.h"
+#include "dm_synth.h"
+
+namespace dm {
+cudaError_t launch_dequant_q4_canonical(cudaStream_t st, const uint8_t* q, const uint16_t* s,
+                                        const uint8_t* z, int rows, int cols, int group, float* out);
+cudaError_t launch_repack_rows(cudaStream_t st, const uint8_t* q, const uint16_t* s, const uint8_t* z,
+                               int rows, int cols, int group, int kind, uint8_t* dst);
+bool moe_supported(int H, int I, int G);
+bool attn_supported(int D, int grp);
+int attn_scores_cap(int max_pages, int nsplit);
+int attn_nsplit(int num_sms, int Hkv);
+cudaError_t launch_kv_copy(cudaStream_t st, uint16_t* kv_layer, const int* page_table_row, int Hkv,
+                           int D, uint16_t* k, uint16_t* v, int n_tokens, int to_cache);
+cudaError_t launch_synth_bf16(cudaStream_t st, uint16_t* dst, uint64_t n, uint64_t seed,
+                              uint64_t stream_id, float mean, float std);
+cudaError_t launch_synth_f32(cudaStream_t st, float* dst, uint64_t n, uint64_t seed, uint64_t stream_id,
+                             float mean, float std);
+cudaError_t launch_synth_u8(cudaStream_t st, uint8_t* dst, uint64_t n, uint64_t seed, uint64_t stream_id);
+cudaError_t launch_synth_f16abs(cudaStream_t st, uint16_t* dst, uint64_t n, uint64_t seed,
+                                uint64_t stream_id, float std);
+}  // namespace dm
+
+using namespace dm;
+
+struct dm_ctx {
+    dm_model_config mc{};
+    dm_runtime_config rc{};
+    Dims d{};
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    uint8_t* arena = nullptr;
+    size_t arena_bytes = 0;
+    std::vector<LayerW> layers;
+    uint16_t* embed = nullptr;
+    uint16_t* final_norm = nullptr;
+    uint16_t* lm_head = nullptr;
+    Buffers b{};
+    // upload staging for one expert projection
+    uint8_t* stage_q = nullptr;
+    uint16_t* stage_s = nullptr;
+    uint8_t* stage_z = nullptr;
+    // pinned host staging for per-step transfers
+    int* h_io = nullptr;  // [0] token in, [1] token out, [2] error word, [3] pos
+    // coverage
+    std::vector<uint8_t> have_dense;   // [(L+1) * DM_T_COUNT]
+    std::vector<uint8_t> have_expert;  // [L * (E+1) * 3]
+    // host mirror of sequence state
+    std::vector<int> slot_len;         // [max_seqs]
+    std::vector<int> att_len;          // [n_att * max_seqs]
+    std::vector<int> dev_pos_valid;    // device pos[slot] == slot_len[slot]
+    std::vector<cudaGraphExec_t> graphs;  // decode step per slot
+    std::string last_error;
+};
+
+// ------------------------------------------------------------------------------------
+static int set_err(dm_ctx* c, int code, const char* type, const char* stage, int layer, const char* fmt, ...) {
+    char detail[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(detail, sizeof detail, fmt, ap);
+    va_end(ap);
+    for (char* p = detail; *p; ++p)
+        if (*p == '"' || *p == '\\') *p = '\'';
+    char buf[768];
+    snprintf(buf, sizeof buf, "{\"error_type\":\"%s\",\"detail\":\"%s\",\"stage\":\"%s\",\"layer\":%d}", type,
+             detail, stage, layer);
+    if (c) c->last_error = buf;
+    return code;
+}
+
+#define DM_CUDA(c, call, stage)                                                                    \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess)                                                                     \
+            return set_err((c), DM_ERR_CUDA, "CUDA_ERROR", (stage), -1, "%s: %s", #call,           \
+                           cudaGetErrorString(e_));                                                \
+    } while (0)
+
+static int validate_config(const dm_model_config* m, char* msg, size_t n) {
+    auto fail = [&](const char* type, const char* what) {
+        if (msg && n) snprintf(msg, n, "{\"error_type\":\"%s\",\"detail\":\"%s\",\"stage\":\"config\",\"layer\":-1}", type, what);
+        return DM_ERR_INVALID_ARG;
+    };
+    if (!m) return fail("CONFIG_ERROR", "null config");
+    // reference ModelConfig.__init__ checks (config.mojo:31-147)
+    if (m->hidden_size <= 0 || m->num_hidden_layers <= 0 || m->num_attention_heads <= 0 || m->vocab_size <= 0)
+        return fail("CONFIG_ERROR", "invalid model dimensions: all sizes must be > 0");
+    if (m->num_experts <= 0 || m->num_experts_per_tok <= 0 || m->num_experts_per_tok > m->num_experts)
+        return fail("CONFIG_ERROR", "invalid MoE topology: 0 < num_experts_per_tok <= num_experts");
+    if (m->moe_intermediate_size <= 0 || m->shared_expert_intermediate_size <= 0)
+        return fail("CONFIG_ERROR", "invalid MoE intermediate sizes: must be > 0");
+    if (m->num_key_value_heads <= 0 || m->num_attention_heads % m->num_key_value_heads != 0)
+        return fail("CONFIG_ERROR", "num_attention_heads must be divisible by num_key_value_heads");
+    if (m->norm_topk_prob)
+        return fail("ROUTER_ERROR", "norm_topk_prob=true forbidden; unrenormalized routing invariant violated");
+    if (!(m->rms_norm_eps > 0.0f) || std::isinf(m->rms_norm_eps))
+        return fail("CONFIG_ERROR", "rms_norm_eps must be finite and > 0");
+    if (m->full_attention_interval <= 0) return fail("CONFIG_ERROR", "full_attention_interval must be > 0");
+    // shape limits of the sm_100a kernels
+    if (!gemv_supported_k(m->hidden_size)) return fail("CONFIG_ERROR", "hidden_size must be 256, 512, 1024, 2048 or 4096");
+    if (m->head_dim <= 0 || m->linear_key_head_dim <= 0) return fail("CONFIG_ERROR", "head dims must be > 0");
+    if (!attn_supported(m->head_dim, m->num_attention_heads / m->num_key_value_heads))
+        return fail("CONFIG_ERROR", "unsupported (head_dim, GQA group) for the decode attention kernel");
+    if (!gemv_supported_k(m->num_attention_heads * m->head_dim))
+        return fail("CONFIG_ERROR", "num_attention_heads * head_dim must be 256..4096 (power of two)");
+    if (m->linear_key_head_dim != m->linear_value_head_dim ||
+        (m->linear_key_head_dim != 64 && m->linear_key_head_dim != 128))
+        return fail("CONFIG_ERROR", "GDN key/value head dims must be equal and 64 or 128");
+    if (m->linear_num_key_heads <= 0 || m->linear_num_value_heads % m->linear_num_key_heads != 0)
+        return fail("CONFIG_ERROR", "linear_num_value_heads must be a multiple of linear_num_key_heads");
+    if (!gemv_supported_k(m->linear_num_value_heads * m->linear_value_head_dim))
+        return fail("CONFIG_ERROR", "linear_num_value_heads * linear_value_head_dim must be 256..4096");
+    if (m->linear_conv_kernel_dim != 4) return fail("CONFIG_ERROR", "linear_conv_kernel_dim must be 4");
+    if (m->shared_expert_intermediate_size != m->moe_intermediate_size)
+        return fail("CONFIG_ERROR", "shared_expert_intermediate_size must equal moe_intermediate_size");
+    if (!moe_supported(m->hidden_size, m->moe_intermediate_size, m->quant_group_size))
+        return fail("CONFIG_ERROR", "unsupported (hidden, moe_intermediate, group) for the 4-bit expert kernels");
+    if (m->num_experts > 1023 || m->num_experts_per_tok > kMaxTopK)
+        return fail("CONFIG_ERROR", "num_experts <= 1023 and num_experts_per_tok <= 16 required");
+    const int rot = static_cast<int>(static_cast<float>(m->head_dim) * m->partial_rotary_factor);
+    if (rot < 2 || rot > m->head_dim || (rot & 1)) return fail("CONFIG_ERROR", "invalid partial_rotary_factor");
+    return DM_OK;
+}
+
+static Dims make_dims(const dm_model_config& m, const dm_runtime_config& r) {
+    Dims d{};
+    d.H = m.hidden_size;
+    d.L = m.num_hidden_layers;
+    d.interval = m.full_attention_interval;
+    d.V = m.vocab_size;
+    d.eps = m.rms_norm_eps;
+    d.Hq = m.num_attention_heads;
+    d.Hkv = m.num_key_value_heads;
+    d.D = m.head_dim;
+    d.rot_dim = static_cast<int>(static_cast<float>(m.head_dim) * m.partial_rotary_factor);
+    d.theta = m.rope_theta;
+    d.nk = m.linear_num_key_heads;
+    d.nv = m.linear_num_value_heads;
+    d.dk = m.linear_key_head_dim;
+    d.dv = m.linear_value_head_dim;
+    d.conv_k = m.linear_conv_kernel_dim;
+    d.qkv_dim = 2 * d.nk * d.dk + d.nv * d.dv;
+    d.z_dim = d.nv * d.dv;
+    d.gdn_in_rows = d.qkv_dim + d.z_dim + 2 * d.nv;
+    d.attn_in_rows = 2 * d.Hq * d.D + 2 * d.Hkv * d.D;
+    d.E = m.num_experts;
+    d.topk = m.num_experts_per_tok;
+    d.I = m.moe_intermediate_size;
+    d.G = m.quant_group_size;
+    d.max_seqs = r.max_seqs;
+    d.num_pages = r.kv_num_pages;
+    d.max_pages = r.max_pages_per_seq;
+    d.n_att = 0;
+    for (int l = 0; l < d.L; ++l)
+        if (l % d.interval == d.interval - 1) ++d.n_att;
+    d.n_gdn = d.L - d.n_att;
+    auto chunk = [&](int K) { return static_cast<int64_t>(16) * (K / 2 + 2 * (K / d.G) + K / d.G / 2); };
+    d.gu_chunk_bytes = chunk(d.H);
+    d.d_chunk_bytes = chunk(d.I);
+    d.gu_chunks = d.I / 8;
+    d.d_chunks = d.H / 16;
+    d.expert_bytes = d.gu_chunks * d.gu_chunk_bytes + d.d_chunks * d.d_chunk_bytes;
+    return d;
+}
+
+static inline bool is_attn_layer(const Dims& d, int l) { return l % d.interval == d.interval - 1; }
+
+// Sub-allocator over the arena (256-byte alignment).
+struct Plan {
+    size_t off = 0;
+    size_t take(size_t bytes) {
+        size_t o = off;
+        off += (bytes + 255) & ~static_cast<size_t>(255);
+        return o;
+    }
+};
+
+static int plan_memory(dm_ctx* c, bool commit) {
+    Dims& d = c->d;
+    Plan p;
+    const size_t H = d.H;
+    std::vector<size_t> offs;
+    auto T = [&](size_t bytes) {
+        offs.push_back(p.take(bytes));
+        return offs.back();
+    };
+    struct LayerOffs {
+        size_t in_norm, post_norm, w_in, conv, dt, alog, gnorm, qn, kn, w_out, router, experts, shared;
+    };
+    std::vector<LayerOffs> lo(d.L);
+    for (int l = 0; l < d.L; ++l) {
+        LayerOffs& o = lo[l];
+        o.in_norm = T(H * 2);
+        o.post_norm = T(H * 2);
+        if (is_attn_layer(d, l)) {
+            o.w_in = T(static_cast<size_t>(d.attn_in_rows) * H * 2);
+            o.qn = T(d.D * 2);
+            o.kn = T(d.D * 2);
+            o.w_out = T(H * d.Hq * d.D * 2);
+        } else {
+            o.w_in = T(static_cast<size_t>(d.gdn_in_rows) * H * 2);
+            o.conv = T(static_cast<size_t>(d.qkv_dim) * 4 * 2);
+            o.dt = T(d.nv * 4);
+            o.alog = T(d.nv * 4);
+            o.gnorm = T(d.dv * 2);
+            o.w_out = T(H * d.z_dim * 2);
+        }
+        o.router = T(static_cast<size_t>(d.E + 1) * H * 2);
+        o.experts = T(static_cast<size_t>(d.E) * d.expert_bytes);
+        o.shared = T(static_cast<size_t>(d.expert_bytes));
+    }
+    const size_t o_embed = T(static_cast<size_t>(d.V) * H * 2);
+    const size_t o_fnorm = T(H * 2);
+    const size_t o_head = T(static_cast<size_t>(d.V) * H * 2);
+    const size_t S = d.max_seqs;
+    const size_t o_xres = T(S * H * 4), o_xmid = T(S * H * 4);
+    const size_t o_ring = T(static_cast<size_t>(d.n_gdn) * S * kConvRing * d.qkv_dim * 4);
+    const size_t o_S = T(static_cast<size_t>(d.n_gdn) * S * d.nv * d.dv * d.dk * 4);
+    const size_t o_kv = T(static_cast<size_t>(d.n_att) * d.num_pages * 2 * d.Hkv * kPageTokens * d.D * 2);
+    const size_t o_pt = T(S * d.max_pages * 4);
+    const size_t o_pos = T(S * 4), o_tok = T(S * 4);
+    const int gen_cap = 1 << 16;
+    const size_t o_gen = T(gen_cap * 4), o_genidx = T(4), o_prompt = T(gen_cap * 4);
+    const size_t o_z = T(d.z_dim * 4), o_ab = T(2 * d.nv * 4), o_o = T(d.z_dim * 4);
+    const size_t o_qg = T(2 * d.Hq * d.D * 4), o_kvnew = T(2 * d.Hkv * d.D * 4);
+    const size_t o_part = T(static_cast<size_t>(d.Hq) * kMaxSplits * (d.D + 2) * 4);
+    const size_t o_aout = T(std::max(d.Hq * d.D, d.H) * 4);
+    const size_t o_xn = T(H * 4), o_rl = T((d.E + 1) * 4), o_ids = T(kMaxTopK * 4), o_p = T(kMaxTopK * 4);
+    const size_t o_sg = T(4), o_h = T(static_cast<size_t>(d.topk + 1) * d.I * 4), o_logits = T(static_cast<size_t>(d.V) * 4);
+    const size_t o_cv = T(kMaxCtas * 4), o_ci = T(kMaxCtas * 4), o_cnt = T(64 * 4), o_err = T(4);
+    const size_t o_sq = T(static_cast<size_t>(d.I) * H / 2), o_ss = T(static_cast<size_t>(d.I) * H / d.G * 2),
+                 o_sz = T(static_cast<size_t>(d.I) * H / d.G / 2 + 16);
+    c->arena_bytes = p.off;
+    if (!commit) return DM_OK;
+
+    uint8_t* A = c->arena;
+    c->layers.assign(d.L, LayerW{});
+    int gi = 0, ai = 0;
+    for (int l = 0; l < d.L; ++l) {
+        LayerW& w = c->layers[l];
+        const LayerOffs& o = lo[l];
+        w.is_attn = is_attn_layer(d, l);
+        w.sub = w.is_attn ? ai++ : gi++;
+        w.in_norm = reinterpret_cast<uint16_t*>(A + o.in_norm);
+        w.post_norm = reinterpret_cast<uint16_t*>(A + o.post_norm);
+        w.w_in = reinterpret_cast<uint16_t*>(A + o.w_in);
+        w.w_out = reinterpret_cast<uint16_t*>(A + o.w_out);
+        if (w.is_attn) {
+            w.q_norm = reinterpret_cast<uint16_t*>(A + o.qn);
+            w.k_norm = reinterpret_cast<uint16_t*>(A + o.kn);
+        } else {
+            w.conv_w = reinterpret_cast<uint16_t*>(A + o.conv);
+            w.dt_bias = reinterpret_cast<float*>(A + o.dt);
+            w.a_log = reinterpret_cast<float*>(A + o.alog);
+            w.gdn_norm = reinterpret_cast<uint16_t*>(A + o.gnorm);
+        }
+        w.w_router = reinterpret_cast<uint16_t*>(A + o.router);
+        w.experts = A + o.experts;
+        w.shared = A + o.shared;
+    }
+    c->embed = reinterpret_cast<uint16_t*>(A + o_embed);
+    c->final_norm = reinterpret_cast<uint16_t*>(A + o_fnorm);
+    c->lm_head = reinterpret_cast<uint16_t*>(A + o_head);
+    Buffers& b = c->b;
+    b.xres = reinterpret_cast<float*>(A + o_xres);
+    b.xmid = reinterpret_cast<float*>(A + o_xmid);
+    b.ring = reinterpret_cast<float*>(A + o_ring);
+    b.S = reinterpret_cast<float*>(A + o_S);
+    b.kv = reinterpret_cast<uint16_t*>(A + o_kv);
+    b.page_table = reinterpret_cast<int*>(A + o_pt);
+    b.pos = reinterpret_cast<int*>(A + o_pos);
+    b.token = reinterpret_cast<int*>(A + o_tok);
+    b.gen_out = reinterpret_cast<int*>(A + o_gen);
+    b.gen_idx = reinterpret_cast<int*>(A + o_genidx);
+    b.gen_capacity = gen_cap;
+    b.prompt = reinterpret_cast<int*>(A + o_prompt);
+    b.z = reinterpret_cast<float*>(A + o_z);
+    b.ab = reinterpret_cast<float*>(A + o_ab);
+    b.o = reinterpret_cast<float*>(A + o_o);
+    b.qg = reinterpret_cast<float*>(A + o_qg);
+    b.kvnew = reinterpret_cast<float*>(A + o_kvnew);
+    b.attn_part = reinterpret_cast<float*>(A + o_part);
+    b.attn_out = reinterpret_cast<float*>(A + o_aout);
+    b.xn = reinterpret_cast<float*>(A + o_xn);
+    b.rlogits = reinterpret_cast<float*>(A + o_rl);
+    b.topk_ids = reinterpret_cast<int*>(A + o_ids);
+    b.topk_p = reinterpret_cast<float*>(A + o_p);
+    b.shared_g = reinterpret_cast<float*>(A + o_sg);
+    b.h = reinterpret_cast<float*>(A + o_h);
+    b.logits = reinterpret_cast<float*>(A + o_logits);
+    b.cand_val = reinterpret_cast<float*>(A + o_cv);
+    b.cand_idx = reinterpret_cast<int*>(A + o_ci);
+    b.counters = reinterpret_cast<unsigned*>(A + o_cnt);
+    b.err = reinterpret_cast<uint32_t*>(A + o_err);
+    c->stage_q = A + o_sq;
+    c->stage_s = reinterpret_cast<uint16_t*>(A + o_ss);
+    c->stage_z = A + o_sz;
+    return DM_OK;
+}
+
+static LaunchCfg lcfg(const dm_ctx* c) { return LaunchCfg{c->stream, c->num_sms, true}; }
+
+// Reads and clears the device error word; maps it to a status.
+static int check_device_error(dm_ctx* c, const char* stage) {
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", stage, -1, "%s", cudaGetErrorString(e));
+    uint32_t w = 0;
+    e = cudaMemcpy(&w, c->b.err, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", stage, -1, "%s", cudaGetErrorString(e));
+    if (w == 0) return DM_OK;
+    cudaMemset(c->b.err, 0, 4);
+    if (w & DM_DEVERR_TIMEOUT) return set_err(c, DM_ERR_TIMEOUT, "DEVICE_TIMEOUT", stage, -1, "a bounded device wait ran out (word 0x%x)", w);
+    if (w & DM_DEVERR_CAPACITY) return set_err(c, DM_ERR_CAPACITY, "M5_ERR_CONTEXT_SIZE", stage, -1, "KV cache capacity exceeded on token append");
+    if (w & DM_DEVERR_PAGE) return set_err(c, DM_ERR_CAPACITY, "KV_PAGE_ERROR", stage, -1, "page table entry outside the page pool");
+    if (w & DM_DEVERR_TOKEN) return set_err(c, DM_ERR_INVALID_ARG, "M4_ERR_INPUT", stage, -1, "token id out of range [0, vocab)");
+    return set_err(c, DM_ERR_NONFINITE, "NONFINITE_ERROR", stage, -1, "non-finite value detected (word 0x%x)", w);
+}
+
+template <typename F>
+static void host_parallel(uint64_t n, F&& f) {
+    unsigned nt = std::thread::hardware_concurrency();
+    if (nt == 0) nt = 1;
+    if (nt > 64) nt = 64;
+    if (n < (1u << 16)) nt = 1;
+    std::vector<std::thread> th;
+    for (unsigned t = 0; t < nt; ++t) {
+        const uint64_t a = n * t / nt, b = n * (t + 1) / nt;
+        th.emplace_back([=, &f] { f(a, b); });
+    }
+    for (auto& x : th) x.join();
+}
+
+// ------------------------------------------------------------------------------------
+extern "C" {
+
+int32_t dm_abi_version(void) { return DM_ABI_VERSION; }
+
+int32_t dm_config_validate(const dm_model_config* model, char* buf, uint64_t buf_size) {
+    if (buf && buf_size) buf[0] = 0;
+    return validate_config(model, buf, buf_size);
+}
+
+int32_t dm_last_error(const dm_ctx* ctx, char* buf, uint64_t buf_size) {
+    if (!ctx || !buf || buf_size == 0) return DM_ERR_INVALID_ARG;
+    snprintf(buf, buf_size, "%s", ctx->last_error.c_str());
+    return DM_OK;
+}
+
+int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt, int32_t device,
+                      dm_ctx** out_ctx) {
+    if (!out_ctx || !rt) return DM_ERR_INVALID_ARG;
+    *out_ctx = nullptr;
+    char msg[512];
+    int rc = validate_config(model, msg, sizeof msg);
+    if (rc != DM_OK) {
+        fprintf(stderr, "%s\n", msg);
+        return rc;
+    }
+    if (rt->max_seqs <= 0 || rt->kv_page_tokens != kPageTokens || rt->kv_num_pages <= 0 || rt->max_pages_per_seq <= 0)
+        return DM_ERR_INVALID_ARG;
+    dm_ctx* c = new dm_ctx();
+    c->mc = *model;
+    c->rc = *rt;
+    c->d = make_dims(*model, *rt);
+    c->device = device;
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = gemv_set_attrs();
+    if (e == cudaSuccess) e = moe_set_attrs();
+    const int nsplit = attn_nsplit(c->num_sms, c->d.Hkv);
+    const int cap = attn_scores_cap(c->d.max_pages, nsplit);
+    const int score_smem = (c->d.Hq / c->d.Hkv) * cap * 4;
+    if (score_smem > 160 * 1024) {
+        fprintf(stderr, "dm_ctx_create: max_pages_per_seq too large for the decode attention kernel\n");
+        delete c;
+        return DM_ERR_INVALID_ARG;
+    }
+    if (e == cudaSuccess) e = attn_set_attrs(std::max(score_smem, 1024));
+    if (e != cudaSuccess) {
+        fprintf(stderr, "dm_ctx_create: %s\n", cudaGetErrorString(e));
+        delete c;
+        return DM_ERR_CUDA;
+    }
+    plan_memory(c, false);
+    e = cudaMalloc(&c->arena, c->arena_bytes);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "dm_ctx_create: cudaMalloc(%zu): %s\n", c->arena_bytes, cudaGetErrorString(e));
+        cudaStreamDestroy(c->stream);
+        delete c;
+        return DM_ERR_OOM;
+    }
+    plan_memory(c, true);
+    // zero everything (weights stay zero until uploaded; state starts empty)
+    e = cudaMemsetAsync(c->arena, 0, c->arena_bytes, c->stream);
+    if (e == cudaSuccess) e = cudaMallocHost(&c->h_io, 64);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "dm_ctx_create: %s\n", cudaGetErrorString(e));
+        cudaFree(c->arena);
+        delete c;
+        return DM_ERR_CUDA;
+    }
+    c->have_dense.assign(static_cast<size_t>(c->d.L + 1) * DM_T_COUNT, 0);
+    c->have_expert.assign(static_cast<size_t>(c->d.L) * (c->d.E + 1) * 3, 0);
+    c->slot_len.assign(c->d.max_seqs, 0);
+    c->att_len.assign(static_cast<size_t>(c->d.n_att) * c->d.max_seqs, 0);
+    c->dev_pos_valid.assign(c->d.max_seqs, 0);
+    c->graphs.assign(c->d.max_seqs, nullptr);
+    for (int s = 0; s < c->d.max_seqs; ++s) {
+        int r2 = dm_seq_reset(c, s);
+        if (r2 != DM_OK) {
+            fprintf(stderr, "dm_ctx_create: %s\n", c->last_error.c_str());
+            dm_ctx_destroy(c);
+            return r2;
+        }
+    }
+    *out_ctx = c;
+    return DM_OK;
+}
+
+int32_t dm_ctx_destroy(dm_ctx* c) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (auto& g : c->graphs)
+        if (g) cudaGraphExecDestroy(g);
+    if (c->arena) cudaFree(c->arena);
+    if (c->h_io) cudaFreeHost(c->h_io);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+    return DM_OK;
+}
+
+int32_t dm_ctx_device_bytes(const dm_ctx* c, uint64_t* out) {
+    if (!c || !out) return DM_ERR_INVALID_ARG;
+    *out = c->arena_bytes;
+    return DM_OK;
+}
+
+int32_t dm_get_stream(dm_ctx* c, void** s) {
+    if (!c || !s) return DM_ERR_INVALID_ARG;
+    *s = c->stream;
+    return DM_OK;
+}
+
+int32_t dm_kernels_per_step(dm_ctx* c, int32_t* out) {
+    if (!c || !out) return DM_ERR_INVALID_ARG;
+    *out = 1 + 6 * c->d.L + 1;  // embed, 3 mixer + 3 MoE kernels per block, head
+    return DM_OK;
+}
+
+// ---- weights ------------------------------------------------------------------------
+static int tensor_target(dm_ctx* c, int layer, int id, int dtype, uint64_t n, void** dst, size_t* bytes) {
+    const Dims& d = c->d;
+    const size_t H = d.H;
+    auto want = [&](uint64_t expect, int dt, void* p) {
+        if (n != expect) return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                                        "tensor %d: expected %llu elements, got %llu", id,
+                                        (unsigned long long)expect, (unsigned long long)n);
+        if (dtype != dt) return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                                        "tensor %d: wrong dtype", id);
+        *dst = p;
+        *bytes = expect * (dt == DM_DTYPE_F32 ? 4 : 2);
+        return DM_OK;
+    };
+    if (layer == -1) {
+        switch (id) {
+            case DM_T_EMBED: return want(static_cast<uint64_t>(d.V) * H, DM_DTYPE_BF16, c->embed);
+            case DM_T_FINAL_NORM: return want(H, DM_DTYPE_BF16, c->final_norm);
+            case DM_T_LM_HEAD: return want(static_cast<uint64_t>(d.V) * H, DM_DTYPE_BF16, c->lm_head);
+            default: return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer, "tensor %d is per-layer", id);
+        }
+    }
+    if (layer < 0 || layer >= d.L) return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer, "layer out of range");
+    LayerW& w = c->layers[layer];
+    uint16_t* win = const_cast<uint16_t*>(w.w_in);
+    switch (id) {
+        case DM_T_INPUT_NORM: return want(H, DM_DTYPE_BF16, const_cast<uint16_t*>(w.in_norm));
+        case DM_T_POST_NORM: return want(H, DM_DTYPE_BF16, const_cast<uint16_t*>(w.post_norm));
+        case DM_T_ROUTER: return want(static_cast<uint64_t>(d.E) * H, DM_DTYPE_BF16, const_cast<uint16_t*>(w.w_router));
+        case DM_T_SHARED_GATE: return want(H, DM_DTYPE_BF16, const_cast<uint16_t*>(w.w_router) + static_cast<size_t>(d.E) * H);
+        default: break;
+    }
+    if (w.is_attn) {
+        switch (id) {
+            case DM_T_ATTN_Q: return want(static_cast<uint64_t>(2) * d.Hq * d.D * H, DM_DTYPE_BF16, win);
+            case DM_T_ATTN_K: return want(static_cast<uint64_t>(d.Hkv) * d.D * H, DM_DTYPE_BF16, win + static_cast<size_t>(2) * d.Hq * d.D * H);
+            case DM_T_ATTN_V: return want(static_cast<uint64_t>(d.Hkv) * d.D * H, DM_DTYPE_BF16, win + static_cast<size_t>(2 * d.Hq * d.D + d.Hkv * d.D) * H);
+            case DM_T_ATTN_Q_NORM: return want(d.D, DM_DTYPE_BF16, const_cast<uint16_t*>(w.q_norm));
+            case DM_T_ATTN_K_NORM: return want(d.D, DM_DTYPE_BF16, const_cast<uint16_t*>(w.k_norm));
+            case DM_T_ATTN_O: return want(H * d.Hq * d.D, DM_DTYPE_BF16, const_cast<uint16_t*>(w.w_out));
+            default: break;
+        }
+    } else {
+        switch (id) {
+            case DM_T_GDN_QKV: return want(static_cast<uint64_t>(d.qkv_dim) * H, DM_DTYPE_BF16, win);
+            case DM_T_GDN_Z: return want(static_cast<uint64_t>(d.z_dim) * H, DM_DTYPE_BF16, win + static_cast<size_t>(d.qkv_dim) * H);
+            case DM_T_GDN_A: return want(static_cast<uint64_t>(d.nv) * H, DM_DTYPE_BF16, win + static_cast<size_t>(d.qkv_dim + d.z_dim) * H);
+            case DM_T_GDN_B: return want(static_cast<uint64_t>(d.nv) * H, DM_DTYPE_BF16, win + static_cast<size_t>(d.qkv_dim + d.z_dim + d.nv) * H);
+            case DM_T_GDN_CONV: return want(static_cast<uint64_t>(d.qkv_dim) * 4, DM_DTYPE_BF16, const_cast<uint16_t*>(w.conv_w));
+            case DM_T_GDN_DT_BIAS: return want(d.nv, DM_DTYPE_F32, const_cast<float*>(w.dt_bias));
+            case DM_T_GDN_A_LOG: return want(d.nv, DM_DTYPE_F32, const_cast<float*>(w.a_log));
+            case DM_T_GDN_NORM: return want(d.dv, DM_DTYPE_BF16, const_cast<uint16_t*>(w.gdn_norm));
+            case DM_T_GDN_OUT: return want(H * d.z_dim, DM_DTYPE_BF16, const_cast<uint16_t*>(w.w_out));
+            default: break;
+        }
+    }
+    return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                   "tensor %d does not belong to a %s layer", id, w.is_attn ? "gated-attention" : "GDN");
+}
+
+int32_t dm_upload_tensor(dm_ctx* c, int32_t layer, int32_t id, int32_t dtype, const void* data, uint64_t n) {
+    if (!c || !data) return DM_ERR_INVALID_ARG;
+    void* dst = nullptr;
+    size_t bytes = 0;
+    int rc = tensor_target(c, layer, id, dtype, n, &dst, &bytes);
+    if (rc != DM_OK) return rc;
+    cudaSetDevice(c->device);
+    DM_CUDA(c, cudaMemcpy(dst, data, bytes, cudaMemcpyHostToDevice), "loader");
+    c->have_dense[static_cast<size_t>(layer + 1) * DM_T_COUNT + id] = 1;
+    return DM_OK;
+}
+
+static uint8_t* expert_record(dm_ctx* c, int layer, int expert) {
+    LayerW& w = c->layers[layer];
+    return expert < 0 ? const_cast<uint8_t*>(w.shared)
+                      : const_cast<uint8_t*>(w.experts) + static_cast<size_t>(expert) * c->d.expert_bytes;
+}
+
+int32_t dm_expert_upload(dm_ctx* c, int32_t layer, int32_t expert, int32_t proj, const uint8_t* q,
+                         const uint16_t* s, const uint8_t* z) {
+    if (!c || !q || !s || !z) return DM_ERR_INVALID_ARG;
+    const Dims& d = c->d;
+    if (layer < 0 || layer >= d.L || expert < -1 || expert >= d.E || proj < 0 || proj > 2)
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer, "expert index out of range");
+    const int rows = proj == DM_PROJ_DOWN ? d.H : d.I;
+    const int cols = proj == DM_PROJ_DOWN ? d.I : d.H;
+    const size_t qb = static_cast<size_t>(rows) * cols / 2, sb = static_cast<size_t>(rows) * (cols / d.G) * 2,
+                 zb = static_cast<size_t>(rows) * (cols / d.G) / 2;
+    cudaSetDevice(c->device);
+    DM_CUDA(c, cudaMemcpyAsync(c->stage_q, q, qb, cudaMemcpyHostToDevice, c->stream), "loader");
+    DM_CUDA(c, cudaMemcpyAsync(c->stage_s, s, sb, cudaMemcpyHostToDevice, c->stream), "loader");
+    DM_CUDA(c, cudaMemcpyAsync(c->stage_z, z, zb, cudaMemcpyHostToDevice, c->stream), "loader");
+    uint8_t* rec = expert_record(c, layer, expert);
+    uint8_t* dst = proj == DM_PROJ_DOWN ? rec + static_cast<size_t>(d.gu_chunks) * d.gu_chunk_bytes : rec;
+    DM_CUDA(c, launch_repack_rows(c->stream, c->stage_q, c->stage_s, c->stage_z, rows, cols, d.G, proj, dst), "loader");
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
+    c->have_expert[(static_cast<size_t>(layer) * (d.E + 1) + (expert + 1)) * 3 + proj] = 1;
+    return DM_OK;
+}
+
+static const char* tensor_name(int id) {
+    static const char* names[DM_T_COUNT] = {
+        "input_layernorm.weight", "post_attention_layernorm.weight", "linear_attn.in_proj_qkv.weight",
+        "linear_attn.conv1d.weight", "linear_attn.in_proj_z.weight", "linear_attn.in_proj_a.weight",
+        "linear_attn.in_proj_b.weight", "linear_attn.dt_bias", "linear_attn.A_log", "linear_attn.norm.weight",
+        "linear_attn.out_proj.weight", "self_attn.q_proj.weight", "self_attn.k_proj.weight",
+        "self_attn.v_proj.weight", "self_attn.q_norm.weight", "self_attn.k_norm.weight",
+        "self_attn.o_proj.weight", "mlp.gate.weight", "mlp.shared_expert_gate.weight",
+        "embed_tokens.weight", "norm.weight", "lm_head.weight"};
+    return (id >= 0 && id < DM_T_COUNT) ? names[id] : "?";
+}
+
+int32_t dm_weights_check(dm_ctx* c) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    const Dims& d = c->d;
+    const int glob[] = {DM_T_EMBED, DM_T_FINAL_NORM, DM_T_LM_HEAD};
+    for (int id : glob)
+        if (!c->have_dense[id])
+            return set_err(c, DM_ERR_NOT_READY, "WEIGHT_LOAD_FAILED", "loader", -1, "missing tensor %s", tensor_name(id));
+    const int gdn_ids[] = {DM_T_INPUT_NORM, DM_T_POST_NORM, DM_T_GDN_QKV, DM_T_GDN_CONV, DM_T_GDN_Z, DM_T_GDN_A,
+                           DM_T_GDN_B, DM_T_GDN_DT_BIAS, DM_T_GDN_A_LOG, DM_T_GDN_NORM, DM_T_GDN_OUT,
+                           DM_T_ROUTER, DM_T_SHARED_GATE};
+    const int att_ids[] = {DM_T_INPUT_NORM, DM_T_POST_NORM, DM_T_ATTN_Q, DM_T_ATTN_K, DM_T_ATTN_V,
+                           DM_T_ATTN_Q_NORM, DM_T_ATTN_K_NORM, DM_T_ATTN_O, DM_T_ROUTER, DM_T_SHARED_GATE};
+    for (int l = 0; l < d.L; ++l) {
+        const bool att = c->layers[l].is_attn;
+        const int* ids = att ? att_ids : gdn_ids;
+        const int n = att ? 10 : 13;
+        for (int i = 0; i < n; ++i)
+            if (!c->have_dense[static_cast<size_t>(l + 1) * DM_T_COUNT + ids[i]])
+                return set_err(c, DM_ERR_NOT_READY, "WEIGHT_LOAD_FAILED", "loader", l, "missing tensor layers.%d.%s", l,
+                               tensor_name(ids[i]));
+        for (int e = -1; e < d.E; ++e)
+            for (int p = 0; p < 3; ++p)
+                if (!c->have_expert[(static_cast<size_t>(l) * (d.E + 1) + (e + 1)) * 3 + p])
+                    return set_err(c, DM_ERR_NOT_READY, "WEIGHT_LOAD_FAILED", "loader", l,
+                                   "missing expert %d projection %d of layer %d", e, p, l);
+    }
+    return DM_OK;
+}
+
+int32_t dm_dequant_q4(dm_ctx* c, const uint8_t* q, const uint16_t* s, const uint8_t* z, int32_t rows,
+                      int32_t cols, int32_t group, float* out) {
+    if (!c || !q || !s || !z || !out || rows <= 0 || cols <= 0 || group <= 0 || cols % (2 * group) != 0)
+        return c ? set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1, "invalid dequant arguments")
+                 : DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    const size_t n = static_cast<size_t>(rows) * cols;
+    const size_t qb = n / 2, sb = static_cast<size_t>(rows) * (cols / group) * 2, zb = static_cast<size_t>(rows) * (cols / group) / 2;
+    uint8_t* tmp = nullptr;
+    DM_CUDA(c, cudaMalloc(&tmp, qb + sb + zb + n * 4 + 1024), "dequant");
+    uint8_t* dq = tmp;
+    uint16_t* ds = reinterpret_cast<uint16_t*>(tmp + ((qb + 255) & ~size_t(255)));
+    uint8_t* dz = reinterpret_cast<uint8_t*>(ds) + ((sb + 255) & ~size_t(255));
+    float* dout = reinterpret_cast<float*>(dz + ((zb + 255) & ~size_t(255)));
+    cudaError_t e = cudaMemcpyAsync(dq, q, qb, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(ds, s, sb, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dz, z, zb, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = launch_dequant_q4_canonical(c->stream, dq, ds, dz, rows, cols, group, dout);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "dequant", -1, "%s", cudaGetErrorString(e));
+    return DM_OK;
+}
+
+// ---- sequence state -------------------------------------------------------------------
+static int check_slot(dm_ctx* c, int slot) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    if (slot < 0 || slot >= c->d.max_seqs)
+        return set_err(c, DM_ERR_INVALID_ARG, "M5_ERR_INPUT", "kv_alloc", -1, "slot %d out of range", slot);
+    return DM_OK;
+}
+
+int32_t dm_seq_reset(dm_ctx* c, int32_t slot) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    const Dims& d = c->d;
+    cudaSetDevice(c->device);
+    for (int g = 0; g < d.n_gdn; ++g) {
+        const size_t ls = static_cast<size_t>(g) * d.max_seqs + slot;
+        DM_CUDA(c, cudaMemsetAsync(c->b.ring + ls * kConvRing * d.qkv_dim, 0, sizeof(float) * kConvRing * d.qkv_dim, c->stream), "kv_alloc");
+        DM_CUDA(c, cudaMemsetAsync(c->b.S + ls * d.nv * d.dv * d.dk, 0, sizeof(float) * d.nv * d.dv * d.dk, c->stream), "kv_alloc");
+    }
+    // identity page table when the pool holds max_pages per slot
+    std::vector<int> pt(d.max_pages, -1);
+    if (static_cast<int64_t>(d.max_seqs) * d.max_pages <= d.num_pages)
+        for (int p = 0; p < d.max_pages; ++p) pt[p] = slot * d.max_pages + p;
+    DM_CUDA(c, cudaMemcpyAsync(c->b.page_table + static_cast<size_t>(slot) * d.max_pages, pt.data(), pt.size() * 4,
+                               cudaMemcpyHostToDevice, c->stream), "kv_alloc");
+    DM_CUDA(c, cudaMemsetAsync(c->b.pos + slot, 0, 4, c->stream), "kv_alloc");
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "kv_alloc");
+    c->slot_len[slot] = 0;
+    for (int a = 0; a < d.n_att; ++a) c->att_len[static_cast<size_t>(a) * d.max_seqs + slot] = 0;
+    c->dev_pos_valid[slot] = 1;
+    return DM_OK;
+}
+
+int32_t dm_seq_set_page_table(dm_ctx* c, int32_t slot, const int32_t* pages, int32_t n) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    const Dims& d = c->d;
+    if (!pages || n < 0 || n > d.max_pages)
+        return set_err(c, DM_ERR_INVALID_ARG, "M5_ERR_INPUT", "kv_alloc", -1, "page count %d outside [0, %d]", n, d.max_pages);
+    std::vector<int> pt(d.max_pages, -1);
+    for (int i = 0; i < n; ++i) {
+        if (pages[i] < 0 || pages[i] >= d.num_pages)
+            return set_err(c, DM_ERR_INVALID_ARG, "KV_PAGE_ERROR", "kv_alloc", -1, "page %d outside the pool", pages[i]);
+        pt[i] = pages[i];
+    }
+    cudaSetDevice(c->device);
+    DM_CUDA(c, cudaMemcpy(c->b.page_table + static_cast<size_t>(slot) * d.max_pages, pt.data(), pt.size() * 4,
+                          cudaMemcpyHostToDevice), "kv_alloc");
+    return DM_OK;
+}
+
+int32_t dm_seq_get_len(dm_ctx* c, int32_t slot, int32_t* len) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    if (!len) return DM_ERR_INVALID_ARG;
+    *len = c->slot_len[slot];
+    return DM_OK;
+}
+
+int32_t dm_seq_set_len(dm_ctx* c, int32_t slot, int32_t len) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    if (len < 0 || len > c->d.max_pages * kPageTokens)
+        return set_err(c, DM_ERR_CAPACITY, "M5_ERR_CONTEXT_SIZE", "kv_alloc", -1, "length %d exceeds capacity", len);
+    c->slot_len[slot] = len;
+    c->dev_pos_valid[slot] = 0;
+    return DM_OK;
+}
+
+int32_t dm_kv_import(dm_ctx* c, int32_t att, int32_t slot, const uint16_t* k, const uint16_t* v, int32_t n) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    const Dims& d = c->d;
+    if (att < 0 || att >= d.n_att || !k || !v || n < 0 || n > d.max_pages * kPageTokens)
+        return set_err(c, DM_ERR_INVALID_ARG, "M5_ERR_INPUT", "kv_import", -1, "invalid kv import arguments");
+    cudaSetDevice(c->device);
+    if (n > 0) {
+        const size_t bytes = static_cast<size_t>(n) * d.Hkv * d.D * 2;
+        uint16_t* tmp = nullptr;
+        DM_CUDA(c, cudaMalloc(&tmp, 2 * bytes), "kv_import");
+        cudaError_t e = cudaMemcpyAsync(tmp, k, bytes, cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(tmp + bytes / 2, v, bytes, cudaMemcpyHostToDevice, c->stream);
+        uint16_t* kvl = c->b.kv + static_cast<size_t>(att) * d.num_pages * 2 * d.Hkv * kPageTokens * d.D;
+        if (e == cudaSuccess)
+            e = launch_kv_copy(c->stream, kvl, c->b.page_table + static_cast<size_t>(slot) * d.max_pages, d.Hkv, d.D,
+                               tmp, tmp + bytes / 2, n, 1);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        cudaFree(tmp);
+        if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "kv_import", -1, "%s", cudaGetErrorString(e));
+        rc = check_device_error(c, "kv_import");
+        if (rc != DM_OK) return rc;
+    }
+    c->att_len[static_cast<size_t>(att) * d.max_seqs + slot] = n;
+    return DM_OK;
+}
+
+int32_t dm_kv_export(dm_ctx* c, int32_t att, int32_t slot, uint16_t* k, uint16_t* v, int32_t n) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    const Dims& d = c->d;
+    if (att < 0 || att >= d.n_att || !k || !v || n < 0 || n > c->att_len[static_cast<size_t>(att) * d.max_seqs + slot])
+        return set_err(c, DM_ERR_INVALID_ARG, "M5_ERR_DECODE", "kv_export", -1, "invalid slice length %d", n);
+    if (n == 0) return DM_OK;
+    cudaSetDevice(c->device);
+    const size_t bytes = static_cast<size_t>(n) * d.Hkv * d.D * 2;
+    uint16_t* tmp = nullptr;
+    DM_CUDA(c, cudaMalloc(&tmp, 2 * bytes), "kv_export");
+    uint16_t* kvl = c->b.kv + static_cast<size_t>(att) * d.num_pages * 2 * d.Hkv * kPageTokens * d.D;
+    cudaError_t e = launch_kv_copy(c->stream, kvl, c->b.page_table + static_cast<size_t>(slot) * d.max_pages, d.Hkv,
+                                   d.D, tmp, tmp + bytes / 2, n, 0);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(k, tmp, bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(v, tmp + bytes / 2, bytes, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "kv_export", -1, "%s", cudaGetErrorString(e));
+    return check_device_error(c, "kv_export");
+}
+
+static int gdn_state_ptrs(dm_ctx* c, int g, int slot, float** S, float** ring) {
+    const Dims& d = c->d;
+    if (g < 0 || g >= d.n_gdn) return set_err(c, DM_ERR_INVALID_ARG, "GDN_ERROR", "gdn_state", -1, "gdn layer %d out of range", g);
+    const size_t ls = static_cast<size_t>(g) * d.max_seqs + slot;
+    *S = c->b.S + ls * d.nv * d.dv * d.dk;
+    *ring = c->b.ring + ls * kConvRing * d.qkv_dim;
+    return DM_OK;
+}
+
+int32_t dm_gdn_state_import(dm_ctx* c, int32_t g, int32_t slot, const float* S_host, const float* conv_host) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    float *S, *ring;
+    if ((rc = gdn_state_ptrs(c, g, slot, &S, &ring)) != DM_OK) return rc;
+    const Dims& d = c->d;
+    cudaSetDevice(c->device);
+    if (S_host) DM_CUDA(c, cudaMemcpy(S, S_host, sizeof(float) * d.nv * d.dv * d.dk, cudaMemcpyHostToDevice), "gdn_state");
+    DM_CUDA(c, cudaMemset(ring, 0, sizeof(float) * kConvRing * d.qkv_dim), "gdn_state");
+    if (conv_host) {
+        const int L = c->slot_len[slot];
+        for (int j = 0; j < 3; ++j) {
+            const int p = L - 3 + j;
+            if (p < 0) continue;
+            DM_CUDA(c, cudaMemcpy(ring + static_cast<size_t>(p & 3) * d.qkv_dim, conv_host + static_cast<size_t>(j) * d.qkv_dim,
+                                  sizeof(float) * d.qkv_dim, cudaMemcpyHostToDevice), "gdn_state");
+        }
+    }
+    return DM_OK;
+}
+
+int32_t dm_gdn_state_export(dm_ctx* c, int32_t g, int32_t slot, float* S_host, float* conv_host) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    float *S, *ring;
+    if ((rc = gdn_state_ptrs(c, g, slot, &S, &ring)) != DM_OK) return rc;
+    const Dims& d = c->d;
+    cudaSetDevice(c->device);
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "gdn_state");
+    if (S_host) DM_CUDA(c, cudaMemcpy(S_host, S, sizeof(float) * d.nv * d.dv * d.dk, cudaMemcpyDeviceToHost), "gdn_state");
+    if (conv_host) {
+        const int L = c->slot_len[slot];
+        for (int j = 0; j < 3; ++j) {
+            const int p = L - 3 + j;
+            float* dst = conv_host + static_cast<size_t>(j) * d.qkv_dim;
+            if (p < 0) {
+                memset(dst, 0, sizeof(float) * d.qkv_dim);
+                continue;
+            }
+            DM_CUDA(c, cudaMemcpy(dst, ring + static_cast<size_t>(p & 3) * d.qkv_dim, sizeof(float) * d.qkv_dim,
+                                  cudaMemcpyDeviceToHost), "gdn_state");
+        }
+    }
+    return DM_OK;
+}
+
+// ---- compute ------------------------------------------------------------------------
+static cudaError_t enqueue_mixer(dm_ctx* c, int layer, int slot) {
+    const LaunchCfg lc = lcfg(c);
+    const LayerW& w = c->layers[layer];
+    cudaError_t e;
+    if (w.is_attn) {
+        if ((e = launch_attn_in(lc, c->d, w, c->b, slot)) != cudaSuccess) return e;
+        if ((e = launch_attn_decode(lc, c->d, w, c->b, slot)) != cudaSuccess) return e;
+        return launch_attn_out(lc, c->d, w, c->b, slot);
+    }
+    if ((e = launch_gdn_in(lc, c->d, w, c->b, slot)) != cudaSuccess) return e;
+    if ((e = launch_gdn_rec(lc, c->d, w, c->b, slot)) != cudaSuccess) return e;
+    return launch_gdn_out(lc, c->d, w, c->b, slot);
+}
+
+static cudaError_t enqueue_moe(dm_ctx* c, int layer, int slot) {
+    const LaunchCfg lc = lcfg(c);
+    const LayerW& w = c->layers[layer];
+    const size_t xo = static_cast<size_t>(slot) * c->d.H;
+    cudaError_t e;
+    if ((e = launch_router(lc, c->d, w, c->b, slot, 1)) != cudaSuccess) return e;
+    if ((e = launch_moe_up(lc, c->d, w, c->b)) != cudaSuccess) return e;
+    return launch_moe_down(lc, c->d, w, c->b, c->b.xmid + xo, c->b.xres + xo);
+}
+
+static cudaError_t enqueue_step(dm_ctx* c, int slot) {
+    const LaunchCfg lc = lcfg(c);
+    cudaError_t e = launch_embed(lc, c->d, c->embed, c->b, slot);
+    for (int l = 0; l < c->d.L && e == cudaSuccess; ++l) {
+        e = enqueue_mixer(c, l, slot);
+        if (e == cudaSuccess) e = enqueue_moe(c, l, slot);
+    }
+    if (e == cudaSuccess) e = launch_head(lc, c->d, c->final_norm, c->lm_head, c->b, slot, 1, 1);
+    return e;
+}
+
+static int ensure_graph(dm_ctx* c, int slot) {
+    if (c->graphs[slot]) return DM_OK;
+    cudaGraph_t g = nullptr;
+    DM_CUDA(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "decode");
+    cudaError_t e = enqueue_step(c, slot);
+    cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+    if (e != cudaSuccess || e2 != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "decode", -1, "graph capture failed: %s",
+                       cudaGetErrorString(e != cudaSuccess ? e : e2));
+    }
+    cudaGraphExec_t ge = nullptr;
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "decode", -1, "graph instantiate: %s", cudaGetErrorString(e));
+    c->graphs[slot] = ge;
+    return DM_OK;
+}
+
+// Decode-step preconditions: weights present, every attention layer at the slot length,
+// room for the new tokens, device position in sync.
+static int prepare_decode(dm_ctx* c, int slot, int n_steps) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    const Dims& d = c->d;
+    for (int a = 0; a < d.n_att; ++a) {
+        const int al = c->att_len[static_cast<size_t>(a) * d.max_seqs + slot];
+        if (al != c->slot_len[slot])
+            return set_err(c, DM_ERR_POSITION, "M5_ERR_DECODE", "decode", -1,
+                           "Position mismatch on KV append: expected current_len %d, actual_pos %d (attention layer %d)",
+                           al, c->slot_len[slot], a);
+    }
+    if (c->slot_len[slot] + n_steps > d.max_pages * kPageTokens)
+        return set_err(c, DM_ERR_CAPACITY, "M5_ERR_CONTEXT_SIZE", "kv_alloc", -1,
+                       "KV cache capacity exceeded on token append: current_len %d + %d > capacity %d",
+                       c->slot_len[slot], n_steps, d.max_pages * kPageTokens);
+    cudaSetDevice(c->device);
+    if (!c->dev_pos_valid[slot]) {
+        c->h_io[3] = c->slot_len[slot];
+        DM_CUDA(c, cudaMemcpyAsync(c->b.pos + slot, &c->h_io[3], 4, cudaMemcpyHostToDevice, c->stream), "decode");
+        DM_CUDA(c, cudaStreamSynchronize(c->stream), "decode");
+        c->dev_pos_valid[slot] = 1;
+    }
+    return ensure_graph(c, slot);
+}
+
+static void advance_lens(dm_ctx* c, int slot, int n) {
+    c->slot_len[slot] += n;
+    for (int a = 0; a < c->d.n_att; ++a) c->att_len[static_cast<size_t>(a) * c->d.max_seqs + slot] += n;
+}
+
+int32_t dm_set_token(dm_ctx* c, int32_t slot, int32_t token) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    if (token < 0 || token >= c->d.V)
+        return set_err(c, DM_ERR_INVALID_ARG, "M4_ERR_INPUT", "input", -1, "token %d out of range [0, %d)", token, c->d.V);
+    cudaSetDevice(c->device);
+    c->h_io[0] = token;
+    DM_CUDA(c, cudaMemcpyAsync(c->b.token + slot, &c->h_io[0], 4, cudaMemcpyHostToDevice, c->stream), "input");
+    return DM_OK;
+}
+
+int32_t dm_enqueue_decode(dm_ctx* c, int32_t slot, int32_t n_steps) {
+    if (n_steps < 0) return DM_ERR_INVALID_ARG;
+    int rc = prepare_decode(c, slot, n_steps);
+    if (rc != DM_OK) return rc;
+    for (int i = 0; i < n_steps; ++i) DM_CUDA(c, cudaGraphLaunch(c->graphs[slot], c->stream), "decode");
+    advance_lens(c, slot, n_steps);
+    return DM_OK;
+}
+
+int32_t dm_sync(dm_ctx* c) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    return check_device_error(c, "decode");
+}
+
+int32_t dm_decode_step(dm_ctx* c, int32_t slot, int32_t token_in, int32_t* token_out, float* logits) {
+    int rc = prepare_decode(c, slot, 1);
+    if (rc != DM_OK) return rc;
+    if ((rc = dm_set_token(c, slot, token_in)) != DM_OK) return rc;
+    DM_CUDA(c, cudaGraphLaunch(c->graphs[slot], c->stream), "decode");
+    DM_CUDA(c, cudaMemcpyAsync(&c->h_io[1], c->b.token + slot, 4, cudaMemcpyDeviceToHost, c->stream), "decode");
+    DM_CUDA(c, cudaMemcpyAsync(&c->h_io[2], c->b.err, 4, cudaMemcpyDeviceToHost, c->stream), "decode");
+    if (logits)
+        DM_CUDA(c, cudaMemcpyAsync(logits, c->b.logits, sizeof(float) * c->d.V, cudaMemcpyDeviceToHost, c->stream), "decode");
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "decode");
+    advance_lens(c, slot, 1);
+    if (c->h_io[2] != 0) return check_device_error(c, "decode");
+    if (token_out) *token_out = c->h_io[1];
+    return DM_OK;
+}
+
+int32_t dm_generate(dm_ctx* c, int32_t slot, int32_t token_in, int32_t n_steps, int32_t* out) {
+    if (!c || !out || n_steps <= 0 || n_steps > c->b.gen_capacity) return DM_ERR_INVALID_ARG;
+    int rc = prepare_decode(c, slot, n_steps);
+    if (rc != DM_OK) return rc;
+    if ((rc = dm_set_token(c, slot, token_in)) != DM_OK) return rc;
+    DM_CUDA(c, cudaMemsetAsync(c->b.gen_idx, 0, 4, c->stream), "decode");
+    for (int i = 0; i < n_steps; ++i) DM_CUDA(c, cudaGraphLaunch(c->graphs[slot], c->stream), "decode");
+    DM_CUDA(c, cudaMemcpyAsync(out, c->b.gen_out, sizeof(int) * n_steps, cudaMemcpyDeviceToHost, c->stream), "decode");
+    advance_lens(c, slot, n_steps);
+    return check_device_error(c, "decode");
+}
+
+int32_t dm_forward(dm_ctx* c, int32_t slot, const int32_t* tokens, int32_t n, float* logits, int32_t* next) {
+    if (!c || !tokens || n <= 0) return DM_ERR_INVALID_ARG;
+    int rc = prepare_decode(c, slot, n);
+    if (rc != DM_OK) return rc;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= c->d.V)
+            return set_err(c, DM_ERR_INVALID_ARG, "M4_ERR_INPUT", "input", -1, "token %d at index %d out of range [0, %d)",
+                           tokens[i], i, c->d.V);
+    // stage the prompt on the device, copy one id per step into the slot's token
+    if (n > c->b.gen_capacity) return DM_ERR_INVALID_ARG;
+    cudaError_t e = cudaMemcpyAsync(c->b.prompt, tokens, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream);
+    for (int i = 0; i < n && e == cudaSuccess; ++i) {
+        e = cudaMemcpyAsync(c->b.token + slot, c->b.prompt + i, 4, cudaMemcpyDeviceToDevice, c->stream);
+        if (e == cudaSuccess) e = cudaGraphLaunch(c->graphs[slot], c->stream);
+    }
+    if (e == cudaSuccess && logits) e = cudaMemcpyAsync(logits, c->b.logits, sizeof(float) * c->d.V, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&c->h_io[1], c->b.token + slot, 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "decode", -1, "%s", cudaGetErrorString(e));
+    advance_lens(c, slot, n);
+    rc = check_device_error(c, "decode");
+    if (rc == DM_OK && next) *next = c->h_io[1];
+    return rc;
+}
+
+// Layer-level entry points: one token at a time, host activations in and out.
+static int layer_args_ok(dm_ctx* c, int layer, const float* x, int n, float* y) {
+    if (!c || !x || !y || n <= 0) return DM_ERR_INVALID_ARG;
+    if (layer < 0 || layer >= c->d.L)
+        return set_err(c, DM_ERR_INVALID_ARG, "LAYER_ERROR", "block", layer, "layer out of range");
+    return DM_OK;
+}
+
+static int mixer_tokens(dm_ctx* c, int layer, int slot, int pos_offset, const float* x, int n, float* y, bool with_moe) {
+    const Dims& d = c->d;
+    const LayerW& w = c->layers[layer];
+    int* alen = w.is_attn ? &c->att_len[static_cast<size_t>(w.sub) * d.max_seqs + slot] : nullptr;
+    if (alen && pos_offset != *alen)
+        return set_err(c, DM_ERR_POSITION, "M5_ERR_DECODE", "decode", layer,
+                       "Position mismatch on KV append: expected current_len %d, actual_pos %d", *alen, pos_offset);
+    if (pos_offset < 0 || pos_offset + n > d.max_pages * kPageTokens)
+        return set_err(c, DM_ERR_CAPACITY, "M5_ERR_CONTEXT_SIZE", "kv_alloc", layer,
+                       "KV cache capacity exceeded on token append");
+    cudaSetDevice(c->device);
+    const size_t xo = static_cast<size_t>(slot) * d.H;
+    for (int t = 0; t < n; ++t) {
+        c->h_io[3] = pos_offset + t;
+        DM_CUDA(c, cudaMemcpyAsync(c->b.pos + slot, &c->h_io[3], 4, cudaMemcpyHostToDevice, c->stream), "block");
+        DM_CUDA(c, cudaMemcpyAsync(c->b.xres + xo, x + static_cast<size_t>(t) * d.H, sizeof(float) * d.H,
+                                   cudaMemcpyHostToDevice, c->stream), "block");
+        DM_CUDA(c, enqueue_mixer(c, layer, slot), "block");
+        const float* src = c->b.xmid + xo;
+        if (with_moe) {
+            DM_CUDA(c, enqueue_moe(c, layer, slot), "block");
+            src = c->b.xres + xo;
+        }
+        DM_CUDA(c, cudaMemcpyAsync(y + static_cast<size_t>(t) * d.H, src, sizeof(float) * d.H, cudaMemcpyDeviceToHost,
+                                   c->stream), "block");
+        DM_CUDA(c, cudaStreamSynchronize(c->stream), "block");
+        if (alen) *alen += 1;
+    }
+    c->dev_pos_valid[slot] = 0;
+    return check_device_error(c, "block");
+}
+
+int32_t dm_mixer_block(dm_ctx* c, int32_t layer, int32_t slot, int32_t pos_offset, const float* x, int32_t n, float* y) {
+    int rc = layer_args_ok(c, layer, x, n, y);
+    if (rc == DM_OK) rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    return mixer_tokens(c, layer, slot, pos_offset, x, n, y, false);
+}
+
+int32_t dm_block_forward(dm_ctx* c, int32_t layer, int32_t slot, int32_t pos_offset, const float* x, int32_t n, float* y) {
+    int rc = layer_args_ok(c, layer, x, n, y);
+    if (rc == DM_OK) rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    return mixer_tokens(c, layer, slot, pos_offset, x, n, y, true);
+}
+
+int32_t dm_moe_block(dm_ctx* c, int32_t layer, const float* x_mid, int32_t n, float* y) {
+    int rc = layer_args_ok(c, layer, x_mid, n, y);
+    if (rc != DM_OK) return rc;
+    cudaSetDevice(c->device);
+    const int H = c->d.H;
+    for (int t = 0; t < n; ++t) {
+        DM_CUDA(c, cudaMemcpyAsync(c->b.xmid, x_mid + static_cast<size_t>(t) * H, sizeof(float) * H, cudaMemcpyHostToDevice, c->stream), "moe");
+        DM_CUDA(c, enqueue_moe(c, layer, 0), "moe");
+        DM_CUDA(c, cudaMemcpyAsync(y + static_cast<size_t>(t) * H, c->b.xres, sizeof(float) * H, cudaMemcpyDeviceToHost, c->stream), "moe");
+        DM_CUDA(c, cudaStreamSynchronize(c->stream), "moe");
+    }
+    return check_device_error(c, "moe");
+}
+
+int32_t dm_router(dm_ctx* c, int32_t layer, const float* x, int32_t n, int32_t* ids, float* probs, float* sg) {
+    if (!c || !x || !ids || !probs || n <= 0) return DM_ERR_INVALID_ARG;
+    if (layer < 0 || layer >= c->d.L) return set_err(c, DM_ERR_INVALID_ARG, "ROUTER_ERROR", "router", layer, "layer out of range");
+    cudaSetDevice(c->device);
+    const Dims& d = c->d;
+    const LaunchCfg lc = lcfg(c);
+    for (int t = 0; t < n; ++t) {
+        DM_CUDA(c, cudaMemcpyAsync(c->b.xn, x + static_cast<size_t>(t) * d.H, sizeof(float) * d.H, cudaMemcpyHostToDevice, c->stream), "router");
+        DM_CUDA(c, launch_router(lc, d, c->layers[layer], c->b, 0, 0), "router");
+        DM_CUDA(c, cudaMemcpyAsync(ids + static_cast<size_t>(t) * d.topk, c->b.topk_ids, sizeof(int) * d.topk, cudaMemcpyDeviceToHost, c->stream), "router");
+        DM_CUDA(c, cudaMemcpyAsync(probs + static_cast<size_t>(t) * d.topk, c->b.topk_p, sizeof(float) * d.topk, cudaMemcpyDeviceToHost, c->stream), "router");
+        if (sg) DM_CUDA(c, cudaMemcpyAsync(sg + t, c->b.shared_g, sizeof(float), cudaMemcpyDeviceToHost, c->stream), "router");
+        DM_CUDA(c, cudaStreamSynchronize(c->stream), "router");
+    }
+    return check_device_error(c, "router");
+}
+
+// ---- kernel timing (roofline measurement) ----------------------------------------------
+int32_t dm_time_kernel(dm_ctx* c, int32_t which, int32_t layer, int32_t iters, float* avg_ms, uint64_t* bytes) {
+    if (!c || !avg_ms || !bytes || iters <= 0) return DM_ERR_INVALID_ARG;
+    const Dims& d = c->d;
+    if (layer < 0 || layer >= d.L) return set_err(c, DM_ERR_INVALID_ARG, "PROFILE", "profile", layer, "layer out of range");
+    const LayerW& w = c->layers[layer];
+    const LaunchCfg lc = lcfg(c);
+    const int slot = 0;
+    const uint64_t H = d.H;
+    auto launch = [&]() -> cudaError_t {
+        switch (which) {
+            case DM_KERNEL_MIXER_IN:
+                return w.is_attn ? launch_attn_in(lc, d, w, c->b, slot) : launch_gdn_in(lc, d, w, c->b, slot);
+            case DM_KERNEL_MIXER_OUT:
+                return w.is_attn ? launch_attn_out(lc, d, w, c->b, slot) : launch_gdn_out(lc, d, w, c->b, slot);
+            case DM_KERNEL_MIXER_CORE:
+                return w.is_attn ? launch_attn_decode(lc, d, w, c->b, slot) : launch_gdn_rec(lc, d, w, c->b, slot);
+            case DM_KERNEL_ROUTER: return launch_router(lc, d, w, c->b, slot, 1);
+            case DM_KERNEL_MOE_UP: return launch_moe_up(lc, d, w, c->b);
+            case DM_KERNEL_MOE_DOWN:
+                return launch_moe_down(lc, d, w, c->b, c->b.xmid + slot * d.H, c->b.attn_out);
+            case DM_KERNEL_HEAD: return launch_head(lc, d, c->final_norm, c->lm_head, c->b, slot, 0, 0);
+            default: return cudaErrorInvalidValue;
+        }
+    };
+    // algorithmic bytes per launch (weights + state the kernel must move)
+    const uint64_t eb = static_cast<uint64_t>(d.expert_bytes);
+    const uint64_t gu = static_cast<uint64_t>(d.gu_chunks) * d.gu_chunk_bytes;
+    switch (which) {
+        case DM_KERNEL_MIXER_IN: *bytes = (w.is_attn ? d.attn_in_rows : d.gdn_in_rows) * H * 2; break;
+        case DM_KERNEL_MIXER_OUT: *bytes = H * (w.is_attn ? d.Hq * d.D : d.z_dim) * 2; break;
+        case DM_KERNEL_MIXER_CORE: {
+            int len = c->slot_len[slot];
+            *bytes = w.is_attn ? static_cast<uint64_t>(len + 1) * 2 * d.Hkv * d.D * 2
+                               : 2ull * d.nv * d.dv * d.dk * 4 + 4ull * d.qkv_dim * 4;
+            break;
+        }
+        case DM_KERNEL_ROUTER: *bytes = (d.E + 1) * H * 2; break;
+        case DM_KERNEL_MOE_UP: *bytes = (d.topk + 1) * gu; break;
+        case DM_KERNEL_MOE_DOWN: *bytes = (d.topk + 1) * (eb - gu); break;
+        case DM_KERNEL_HEAD: *bytes = static_cast<uint64_t>(d.V) * H * 2; break;
+        default: return DM_ERR_INVALID_ARG;
+    }
+    cudaSetDevice(c->device);
+    cudaEvent_t e0, e1;
+    DM_CUDA(c, cudaEventCreate(&e0), "profile");
+    DM_CUDA(c, cudaEventCreate(&e1), "profile");
+    cudaError_t e = launch();  // warm-up
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(e0, c->stream);
+    for (int i = 0; i < iters && e == cudaSuccess; ++i) e = launch();
+    if (e == cudaSuccess) e = cudaEventRecord(e1, c->stream);
+    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+    float ms = 0.0f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "profile", layer, "%s", cudaGetErrorString(e));
+    *avg_ms = ms / iters;
+    return check_device_error(c, "profile");
+}
+
+// ---- synthetic checkpoint -------------------------------------------------------------
+int32_t dm_synth_bf16(uint64_t seed, uint64_t sid, uint64_t n, float mean, float std, uint16_t* out) {
+    if (!out) return DM_ERR_INVALID_ARG;
+    const uint64_t key = synth_key(seed, sid);
+    host_parallel(n, [&](uint64_t a, uint64_t b) {
+        for (uint64_t i = a; i < b; ++i) out[i] = synth_f32_to_bf16(mean + std * synth_normal(synth_hash(key, i)));
+    });
+    return DM_OK;
+}
+
+int32_t dm_synth_f32(uint64_t seed, uint64_t sid, uint64_t n, float mean, float std, float* out) {
+    if (!out) return DM_ERR_INVALID_ARG;
+    const uint64_t key = synth_key(seed, sid);
+    host_parallel(n, [&](uint64_t a, uint64_t b) {
+        for (uint64_t i = a; i < b; ++i) out[i] = mean + std * synth_normal(synth_hash(key, i));
+    });
+    return DM_OK;
+}
+
+int32_t dm_synth_u8(uint64_t seed, uint64_t sid, uint64_t n, uint8_t* out) {
+    if (!out) return DM_ERR_INVALID_ARG;
+    const uint64_t key = synth_key(seed, sid);
+    host_parallel(n, [&](uint64_t a, uint64_t b) {
+        for (uint64_t i = a; i < b; ++i) out[i] = synth_byte(key, i);
+    });
+    return DM_OK;
+}
+
+int32_t dm_synth_f16_absnormal(uint64_t seed, uint64_t sid, uint64_t n, float std, uint16_t* out) {
+    if (!out) return DM_ERR_INVALID_ARG;
+    const uint64_t key = synth_key(seed, sid);
+    host_parallel(n, [&](uint64_t a, uint64_t b) {
+        for (uint64_t i = a; i < b; ++i) out[i] = synth_f32_to_f16(fabsf(std * synth_normal(synth_hash(key, i))));
+    });
+    return DM_OK;
+}
+
+int32_t dm_synth_model_device(dm_ctx* c, uint64_t seed) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    const Dims& d = c->d;
+    const float rstd = 1.0f / sqrtf(static_cast<float>(d.H));
+    auto dense = [&](int layer, int id, float mean, float std) -> int {
+        void* dst = nullptr;
+        size_t bytes = 0;
+        const int dt = (id == DM_T_GDN_DT_BIAS || id == DM_T_GDN_A_LOG) ? DM_DTYPE_F32 : DM_DTYPE_BF16;
+        // element count from the tensor table
+        uint64_t n = 0;
+        const size_t H = d.H;
+        switch (id) {
+            case DM_T_INPUT_NORM: case DM_T_POST_NORM: case DM_T_SHARED_GATE: case DM_T_FINAL_NORM: n = H; break;
+            case DM_T_ROUTER: n = static_cast<uint64_t>(d.E) * H; break;
+            case DM_T_GDN_QKV: n = static_cast<uint64_t>(d.qkv_dim) * H; break;
+            case DM_T_GDN_Z: n = static_cast<uint64_t>(d.z_dim) * H; break;
+            case DM_T_GDN_A: case DM_T_GDN_B: n = static_cast<uint64_t>(d.nv) * H; break;
+            case DM_T_GDN_CONV: n = static_cast<uint64_t>(d.qkv_dim) * 4; break;
+            case DM_T_GDN_DT_BIAS: case DM_T_GDN_A_LOG: n = d.nv; break;
+            case DM_T_GDN_NORM: n = d.dv; break;
+            case DM_T_GDN_OUT: n = H * d.z_dim; break;
+            case DM_T_ATTN_Q: n = static_cast<uint64_t>(2) * d.Hq * d.D * H; break;
+            case DM_T_ATTN_K: case DM_T_ATTN_V: n = static_cast<uint64_t>(d.Hkv) * d.D * H; break;
+            case DM_T_ATTN_Q_NORM: case DM_T_ATTN_K_NORM: n = d.D; break;
+            case DM_T_ATTN_O: n = H * d.Hq * d.D; break;
+            case DM_T_EMBED: case DM_T_LM_HEAD: n = static_cast<uint64_t>(d.V) * H; break;
+            default: return DM_ERR_INVALID_ARG;
+        }
+        int rc = tensor_target(c, layer, id, dt, n, &dst, &bytes);
+        if (rc != DM_OK) return rc;
+        const uint64_t sid = synth_dense_stream(layer, id);
+        cudaError_t e = dt == DM_DTYPE_F32 ? launch_synth_f32(c->stream, static_cast<float*>(dst), n, seed, sid, mean, std)
+                                           : launch_synth_bf16(c->stream, static_cast<uint16_t*>(dst), n, seed, sid, mean, std);
+        if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "synth", layer, "%s", cudaGetErrorString(e));
+        c->have_dense[static_cast<size_t>(layer + 1) * DM_T_COUNT + id] = 1;
+        return DM_OK;
+    };
+    int rc;
+#define DM_TRY(x) \
+    if ((rc = (x)) != DM_OK) return rc;
+    DM_TRY(dense(-1, DM_T_EMBED, 0.0f, 0.02f));
+    DM_TRY(dense(-1, DM_T_FINAL_NORM, 1.0f, 0.02f));
+    DM_TRY(dense(-1, DM_T_LM_HEAD, 0.0f, 0.02f));
+    for (int l = 0; l < d.L; ++l) {
+        DM_TRY(dense(l, DM_T_INPUT_NORM, 1.0f, 0.02f));
+        DM_TRY(dense(l, DM_T_POST_NORM, 1.0f, 0.02f));
+        DM_TRY(dense(l, DM_T_ROUTER, 0.0f, rstd));
+        DM_TRY(dense(l, DM_T_SHARED_GATE, 0.0f, 0.02f));
+        if (c->layers[l].is_attn) {
+            DM_TRY(dense(l, DM_T_ATTN_Q, 0.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_ATTN_K, 0.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_ATTN_V, 0.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_ATTN_Q_NORM, 1.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_ATTN_K_NORM, 1.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_ATTN_O, 0.0f, 0.02f));
+        } else {
+            DM_TRY(dense(l, DM_T_GDN_QKV, 0.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_GDN_Z, 0.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_GDN_A, 0.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_GDN_B, 0.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_GDN_CONV, 0.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_GDN_DT_BIAS, 0.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_GDN_A_LOG, 0.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_GDN_NORM, 1.0f, 0.02f));
+            DM_TRY(dense(l, DM_T_GDN_OUT, 0.0f, 0.02f));
+        }
+        for (int e = -1; e < d.E; ++e) {
+            for (int p = 0; p < 3; ++p) {
+                const int rows = p == DM_PROJ_DOWN ? d.H : d.I;
+                const int cols = p == DM_PROJ_DOWN ? d.I : d.H;
+                const uint64_t nq = static_cast<uint64_t>(rows) * cols / 2, ns = static_cast<uint64_t>(rows) * (cols / d.G),
+                               nz = ns / 2;
+                cudaError_t ce = launch_synth_u8(c->stream, c->stage_q, nq, seed, synth_expert_stream(l, e, p, 0));
+                if (ce == cudaSuccess) ce = launch_synth_f16abs(c->stream, c->stage_s, ns, seed, synth_expert_stream(l, e, p, 1), 0.02f);
+                if (ce == cudaSuccess) ce = launch_synth_u8(c->stream, c->stage_z, nz, seed, synth_expert_stream(l, e, p, 2));
+                uint8_t* rec = expert_record(c, l, e);
+                uint8_t* dst = p == DM_PROJ_DOWN ? rec + static_cast<size_t>(d.gu_chunks) * d.gu_chunk_bytes : rec;
+                if (ce == cudaSuccess) ce = launch_repack_rows(c->stream, c->stage_q, c->stage_s, c->stage_z, rows, cols, d.G, p, dst);
+                if (ce != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "synth", l, "%s", cudaGetErrorString(ce));
+                c->have_expert[(static_cast<size_t>(l) * (d.E + 1) + (e + 1)) * 3 + p] = 1;
+            }
+        }
+    }
+#undef DM_TRY
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "synth");
+    return DM_OK;
+}
+
+}  // extern "C"

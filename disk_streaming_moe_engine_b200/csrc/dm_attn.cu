@@ -1,0 +1,319 @@
+// dm_attn.cu — gated-attention decode step over a paged bf16 KV cache (sm_100a).
+//
+// Semantics of reference forward_attention_qwen36 (src/layers/attention.mojo:219-435) for
+// the token at position `pos`, with the KV cache of LayerKVCache (kv_cache.mojo:302-375):
+//   q, gate = halves of q_proj (first Hq*D rows q, next Hq*D rows gate)
+//   per-head RMSNorm of q and k with q_norm / k_norm            (attention.mojo:282-316)
+//   partial RoPE on the first rotary_dim = int(D * factor) dims, rotate-half pairs
+//   (i, i + rotary_dim/2), inv_freq_i = 1 / theta^(2i / rotary_dim)   (:318-354)
+//   k, v rounded once to bf16 and appended at pos (pos == current length)
+//   softmax(q k^T / sqrt(D)) over positions [0, pos] of the KV head (GQA: query head h
+//   reads KV head h / (Hq / Hkv)), output * sigmoid(gate)          (:356-427)
+//
+// Grid (Hkv, nsplit): CTA (g, s) normalises and rotates the Hq/Hkv query heads of KV head
+// g, scores its share of the positions (a whole number of 16-token pages) for all of them
+// at once, and writes an unnormalised partial (max, sum, acc[D]) per head; the last CTA
+// of KV head g (atomic counter) merges the partials and applies the output gate.  The
+// current token's k/v come from shared memory, so the append by CTA (g, 0) never races
+// with the reads of the other CTAs, which only touch positions < pos.
+#include "dm_common.cuh"
+#include "dm_kernels.h"
+
+namespace dm {
+
+struct AttnArgs {
+    const float* qg;          // [2*Hq*D]
+    const float* kvnew;       // [2*Hkv*D] k then v (raw projections)
+    const uint16_t* q_norm;   // [D]
+    const uint16_t* k_norm;   // [D]
+    uint16_t* kv;             // layer base [num_pages][2][Hkv][16][D]
+    const int* page_table;    // [max_pages] for the slot
+    const int* pos;
+    int Hq, Hkv, rot_dim, max_pages, num_pages, nsplit, cap;
+    float theta, eps;
+    float* part;              // [Hq][kMaxSplits][D+2]
+    float* out;               // [Hq*D]
+    unsigned* counters;       // [Hkv]
+    uint32_t* err;
+};
+
+// Loads the RMS-normalised, rotated head vector `src` (length D) into dst (smem).
+template <int D>
+__device__ __forceinline__ void norm_rope_head(const float* src, const uint16_t* w, float* dst,
+                                               int lane, int rot_dim, float theta, float eps, int pos) {
+    float ss = 0.0f;
+    for (int d = lane; d < D; d += 32) ss = fmaf(src[d], src[d], ss);
+    ss = warp_sum(ss);
+    const float rs = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+    for (int d = lane; d < D; d += 32) dst[d] = src[d] * rs * bf16_to_f32(w[d]);
+    __syncwarp();
+    const int half = rot_dim / 2;
+    const float m = static_cast<float>(pos);
+    for (int i = lane; i < half; i += 32) {
+        const float inv_freq = 1.0f / powf(theta, static_cast<float>(2 * i) / static_cast<float>(rot_dim));
+        float sn, cs;
+        sincosf(m * inv_freq, &sn, &cs);
+        const float x0 = dst[i], x1 = dst[i + half];
+        dst[i] = x0 * cs - x1 * sn;
+        dst[i + half] = x0 * sn + x1 * cs;
+    }
+    __syncwarp();
+}
+
+template <int D, int GRP>
+__global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+    constexpr int EPL = D / 32;  // k elements per lane in the score loop
+    __shared__ __align__(16) float qsm[GRP][D];
+    __shared__ __align__(16) float knew[D], vnew[D];
+    __shared__ uint16_t kbits[D], vbits[D];
+    __shared__ float hm[GRP], hl[GRP];
+    __shared__ int is_last;
+    extern __shared__ float scores[];  // [GRP][cap]
+    const int g = blockIdx.x, s = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+
+    pdl_wait();
+    const int pos = *a.pos;
+    const int n_tok = pos + 1;
+    const int capacity = a.max_pages * kPageTokens;
+
+    // ---- q heads of this KV group, new k, new v ----
+    for (int hh = warp; hh < GRP; hh += 4)
+        norm_rope_head<D>(a.qg + static_cast<size_t>(g * GRP + hh) * D, a.q_norm, qsm[hh], lane,
+                          a.rot_dim, a.theta, a.eps, pos);
+    if (warp == 0) {
+        norm_rope_head<D>(a.kvnew + static_cast<size_t>(g) * D, a.k_norm, knew, lane, a.rot_dim,
+                          a.theta, a.eps, pos);
+        for (int d = lane; d < D; d += 32) {
+            const uint16_t kb = f32_to_bf16(knew[d]);
+            kbits[d] = kb;
+            knew[d] = bf16_to_f32(kb);
+        }
+    } else if (warp == 1) {
+        const float* vsrc = a.kvnew + static_cast<size_t>(a.Hkv + g) * D;
+        for (int d = lane; d < D; d += 32) {
+            const uint16_t vb = f32_to_bf16(vsrc[d]);
+            vbits[d] = vb;
+            vnew[d] = bf16_to_f32(vb);
+        }
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    // ---- append at pos (one CTA per KV head) ----
+    if (s == 0) {
+        const int pidx = pos / kPageTokens;
+        const int page = (pos >= 0 && pos < capacity) ? a.page_table[pidx] : -1;
+        if (pos < 0 || pos >= capacity) {
+            if (tid == 0) raise_error(a.err, DM_DEVERR_CAPACITY);
+        } else if (page < 0 || page >= a.num_pages) {
+            if (tid == 0) raise_error(a.err, DM_DEVERR_PAGE);
+        } else {
+            uint16_t* kd = a.kv + ((static_cast<size_t>(page) * 2 + 0) * a.Hkv + g) * kPageTokens * D +
+                           static_cast<size_t>(pos % kPageTokens) * D;
+            uint16_t* vd = a.kv + ((static_cast<size_t>(page) * 2 + 1) * a.Hkv + g) * kPageTokens * D +
+                           static_cast<size_t>(pos % kPageTokens) * D;
+            for (int d = tid; d < D; d += 128) {
+                kd[d] = kbits[d];
+                vd[d] = vbits[d];
+            }
+        }
+    }
+
+    // ---- this split's positions ----
+    int chunk = (n_tok + a.nsplit - 1) / a.nsplit;
+    chunk = (chunk + kPageTokens - 1) / kPageTokens * kPageTokens;
+    const int t0 = s * chunk;
+    const int t1 = min(n_tok, t0 + chunk);
+    const int T = t1 > t0 ? t1 - t0 : 0;
+    const float scale = 1.0f / sqrtf(static_cast<float>(D));
+
+    // scores: warp per position, lanes own EPL contiguous dims
+    for (int ti = warp; ti < T; ti += 4) {
+        const int t = t0 + ti;
+        float kf[EPL];
+        if (t == pos) {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) kf[e] = knew[lane * EPL + e];
+        } else {
+            const int page = a.page_table[t / kPageTokens];
+            const bool ok = page >= 0 && page < a.num_pages;
+            if (!ok && lane == 0) raise_error(a.err, DM_DEVERR_PAGE);
+            const uint16_t* kr = a.kv + ((static_cast<size_t>(ok ? page : 0) * 2 + 0) * a.Hkv + g) * kPageTokens * D +
+                                 static_cast<size_t>(t % kPageTokens) * D + lane * EPL;
+            if (EPL == 8) {
+                const uint4 u = *reinterpret_cast<const uint4*>(kr);
+                kf[0] = bf16lo(u.x); kf[1] = bf16hi(u.x); kf[2] = bf16lo(u.y); kf[3] = bf16hi(u.y);
+                kf[4] = bf16lo(u.z); kf[5] = bf16hi(u.z); kf[6] = bf16lo(u.w); kf[7] = bf16hi(u.w);
+            } else {
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) kf[e] = bf16_to_f32(kr[e]);
+            }
+            if (!ok) {
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) kf[e] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int hh = 0; hh < GRP; ++hh) {
+            float p = 0.0f;
+#pragma unroll
+            for (int e = 0; e < EPL; ++e) p = fmaf(qsm[hh][lane * EPL + e], kf[e], p);
+            p = warp_sum(p);
+            if (lane == 0) scores[hh * a.cap + ti] = p * scale;
+        }
+    }
+    __syncthreads();
+
+    // softmax partial per head
+    for (int hh = warp; hh < GRP; hh += 4) {
+        float m = -INFINITY;
+        for (int ti = lane; ti < T; ti += 32) m = fmaxf(m, scores[hh * a.cap + ti]);
+        m = warp_max(m);
+        float l = 0.0f;
+        for (int ti = lane; ti < T; ti += 32) {
+            const float e = (T > 0) ? expf(scores[hh * a.cap + ti] - m) : 0.0f;
+            scores[hh * a.cap + ti] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            hm[hh] = m;
+            hl[hh] = l;
+        }
+    }
+    __syncthreads();
+
+    // weighted V sum: thread owns dims d = tid, tid + 128, ...
+    for (int d = tid; d < D; d += 128) {
+        float acc[GRP];
+#pragma unroll
+        for (int hh = 0; hh < GRP; ++hh) acc[hh] = 0.0f;
+        for (int ti = 0; ti < T; ++ti) {
+            const int t = t0 + ti;
+            float v;
+            if (t == pos) {
+                v = vnew[d];
+            } else {
+                const int page = a.page_table[t / kPageTokens];
+                const bool ok = page >= 0 && page < a.num_pages;
+                v = ok ? bf16_to_f32(a.kv[((static_cast<size_t>(page) * 2 + 1) * a.Hkv + g) * kPageTokens * D +
+                                          static_cast<size_t>(t % kPageTokens) * D + d])
+                       : 0.0f;
+            }
+#pragma unroll
+            for (int hh = 0; hh < GRP; ++hh) acc[hh] = fmaf(scores[hh * a.cap + ti], v, acc[hh]);
+        }
+#pragma unroll
+        for (int hh = 0; hh < GRP; ++hh)
+            a.part[(static_cast<size_t>(g * GRP + hh) * kMaxSplits + s) * (D + 2) + d] = acc[hh];
+    }
+    if (tid < GRP) {
+        float* p = a.part + (static_cast<size_t>(g * GRP + tid) * kMaxSplits + s) * (D + 2);
+        p[D] = hm[tid];
+        p[D + 1] = hl[tid];
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(a.counters + g, 1u);
+        is_last = (prev == gridDim.y - 1);
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+
+    // ---- merge the splits of every head of this group, apply the output gate ----
+    const int ns = gridDim.y;
+    for (int hh = warp; hh < GRP; hh += 4) {
+        const int hq = g * GRP + hh;
+        const float* ph = a.part + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
+        float M = -INFINITY;
+        for (int sp = 0; sp < ns; ++sp) {
+            const float l = __ldcg(ph + sp * (D + 2) + D + 1);
+            if (l > 0.0f) M = fmaxf(M, __ldcg(ph + sp * (D + 2) + D));
+        }
+        float L = 0.0f;
+        for (int sp = 0; sp < ns; ++sp) {
+            const float l = __ldcg(ph + sp * (D + 2) + D + 1);
+            if (l > 0.0f) L += expf(__ldcg(ph + sp * (D + 2) + D) - M) * l;
+        }
+        const float invL = 1.0f / L;
+        for (int d = lane; d < D; d += 32) {
+            float acc = 0.0f;
+            for (int sp = 0; sp < ns; ++sp) {
+                const float l = __ldcg(ph + sp * (D + 2) + D + 1);
+                if (l > 0.0f) acc += expf(__ldcg(ph + sp * (D + 2) + D) - M) * __ldcg(ph + sp * (D + 2) + d);
+            }
+            const float gate = a.qg[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
+            a.out[static_cast<size_t>(hq) * D + d] = acc * invL * sigmoid_f(gate);
+        }
+    }
+    if (tid == 0) a.counters[g] = 0u;
+}
+
+int attn_scores_cap(int max_pages, int nsplit) {
+    const int max_tok = max_pages * kPageTokens;
+    int chunk = (max_tok + nsplit - 1) / nsplit;
+    return (chunk + kPageTokens - 1) / kPageTokens * kPageTokens;
+}
+
+int attn_nsplit(int num_sms, int Hkv) {
+    int ns = num_sms / (Hkv > 0 ? Hkv : 1);
+    if (ns < 1) ns = 1;
+    if (ns > kMaxSplits) ns = kMaxSplits;
+    return ns;
+}
+
+bool attn_supported(int D, int grp) {
+    return (D == 256 && (grp == 8 || grp == 4 || grp == 16)) || (D == 128 && (grp == 8 || grp == 4)) ||
+           (D == 64 && (grp == 4 || grp == 8));
+}
+
+#define DM_ATTN_INSTANCES(X) X(256, 8) X(256, 4) X(256, 16) X(128, 8) X(128, 4) X(64, 4) X(64, 8)
+
+cudaError_t attn_set_attrs(int max_scores_smem) {
+    cudaError_t e = cudaSuccess;
+#define DM_ATTN_ATTR(DD, GG)                                                                      \
+    if (e == cudaSuccess)                                                                         \
+        e = cudaFuncSetAttribute(attn_decode_kernel<DD, GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 max_scores_smem);
+    DM_ATTN_INSTANCES(DM_ATTN_ATTR)
+#undef DM_ATTN_ATTR
+    return e;
+}
+
+cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                               const Buffers& b, int slot) {
+    AttnArgs a{};
+    a.qg = b.qg;
+    a.kvnew = b.kvnew;
+    a.q_norm = w.q_norm;
+    a.k_norm = w.k_norm;
+    a.kv = b.kv + static_cast<size_t>(w.sub) * d.num_pages * 2 * d.Hkv * kPageTokens * d.D;
+    a.page_table = b.page_table + static_cast<size_t>(slot) * d.max_pages;
+    a.pos = b.pos + slot;
+    a.Hq = d.Hq;
+    a.Hkv = d.Hkv;
+    a.rot_dim = d.rot_dim;
+    a.max_pages = d.max_pages;
+    a.num_pages = d.num_pages;
+    a.nsplit = attn_nsplit(lc.num_sms, d.Hkv);
+    a.cap = attn_scores_cap(d.max_pages, a.nsplit);
+    a.theta = d.theta;
+    a.eps = d.eps;
+    a.part = b.attn_part;
+    a.out = b.attn_out;
+    a.counters = b.counters + kCntAttnBase;
+    a.err = b.err;
+    const int grp = d.Hq / d.Hkv;
+    const dim3 grid(d.Hkv, a.nsplit);
+    const size_t smem = static_cast<size_t>(grp) * a.cap * sizeof(float);
+#define DM_ATTN_LAUNCH(DD, GG) \
+    if (d.D == DD && grp == GG) return launch_kernel(lc, attn_decode_kernel<DD, GG>, grid, dim3(128), smem, a);
+    DM_ATTN_INSTANCES(DM_ATTN_LAUNCH)
+#undef DM_ATTN_LAUNCH
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace dm

@@ -1,0 +1,162 @@
+// dm_common.cuh — device helpers shared by every kernel of libdismoen_cuda.so (sm_100a).
+//
+//  * 1-D bulk copies (cp.async.bulk, the TMA engine's untiled mode) completing on
+//    shared-memory mbarriers, never with cluster multicast;
+//  * bounded mbarrier waits: every wait gives up after DM_WAIT_NS of %globaltimer time,
+//    raises DM_DEVERR_TIMEOUT in the context's error word and lets the kernel finish;
+//  * programmatic dependent launch (griddepcontrol) so that a kernel can stream its
+//    weights while the previous kernel of the decode step is still running.
+#pragma once
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "dm_internal.h"
+#include "dm_kernels.h"
+
+#define DM_DEV __device__ __forceinline__
+
+namespace dm {
+
+constexpr uint64_t DM_WAIT_NS = 1000000000ull;  // 1 s bound on any device-side wait
+
+DM_DEV uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+DM_DEV void raise_error(uint32_t* err, uint32_t code) {
+    if (err) atomicOr(err, code);
+}
+
+// ---- programmatic dependent launch -------------------------------------------------
+// wait: blocks until every grid this one depends on has completed and its writes are
+// visible.  launch_dependents: lets the next kernel in the stream be scheduled.
+DM_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+DM_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// Named barrier over `count` threads (multiple of 32) that excludes the other warps.
+DM_DEV void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ---- shared-memory address helpers ---------------------------------------------------
+DM_DEV uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier ----------------------------------------------------------------------
+DM_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+DM_DEV void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+DM_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\t"
+        "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+        : "memory");
+}
+DM_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\t"
+        "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+        "r"(bytes)
+        : "memory");
+}
+DM_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for phase `parity` of `bar`.  Returns false (and raises the timeout bit)
+// if DM_WAIT_NS elapsed; `abort_flag` (shared) short-circuits waits after a failure.
+DM_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* err,
+                              volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t0 = globaltimer_ns();
+    uint32_t polls = 0;
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (++polls % 64 == 0) {
+            if (abort_flag && *abort_flag) return false;
+            if (globaltimer_ns() - t0 > DM_WAIT_NS) {
+                raise_error(err, DM_DEVERR_TIMEOUT);
+                if (abort_flag) *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+// ---- bulk copy global -> shared (TMA, untiled) ----------------------------------------
+// Both addresses 16-byte aligned and bytes a multiple of 16 (checked by the callers'
+// layout: every chunk is a multiple of 16 bytes and every base is 256-byte aligned).
+DM_DEV void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+// L2 prefetch of a global range (no shared memory involved).
+DM_DEV void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes)
+                 : "memory");
+}
+
+// ---- loads ---------------------------------------------------------------------------
+DM_DEV uint4 ldg_nc_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// bf16 pair (packed in a u32, element 0 in the low half) -> two floats (exact).
+DM_DEV float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
+DM_DEV float bf16hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+DM_DEV float bf16_to_f32(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
+// fp32 -> bf16 round-to-nearest-even (NaN stays NaN).
+DM_DEV uint16_t f32_to_bf16(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+// ---- warp reductions -----------------------------------------------------------------
+// Butterfly: every lane ends with the same value; addition order is fixed
+// (xor 16, 8, 4, 2, 1), so the result is deterministic.
+DM_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+DM_DEV float warp_max(float v) {
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+    return v;
+}
+
+// Numerically stable logistic and SiLU (reference src/layers/swiglu.mojo:11-40).
+DM_DEV float sigmoid_f(float z) {
+    if (z < -88.0f) return 0.0f;
+    if (z > 88.0f) return 1.0f;
+    if (z < 0.0f) {
+        float e = expf(z);
+        return e / (1.0f + e);
+    }
+    return 1.0f / (1.0f + expf(-z));
+}
+DM_DEV float silu_f(float z) { return z * sigmoid_f(z); }
+
+}  // namespace dm

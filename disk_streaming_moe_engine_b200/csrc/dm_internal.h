@@ -1,0 +1,144 @@
+// dm_internal.h — device data layout and kernel launch interface of libdismoen_cuda.so.
+//
+// HBM layout (one context = one model + its sequence slots):
+//   dense weights   bf16, row-major [out_rows][in_cols], per layer; the token-mixer input
+//                   projections of a layer are one concatenated matrix so that a single
+//                   GEMV streams them (GDN: qkv | z | a | b; attention: q+gate | k | v),
+//                   and the router rows are followed by the shared-expert gate row.
+//   experts         per layer E routed + 1 shared record of the asymmetric 4-bit format in
+//                   16-row chunks: [nibbles 16 x cols/2][fp16 scales 16 x cols/g]
+//                   [uint4 zeros 16 x cols/2g]; gate_up chunk c holds gate rows 8c..8c+7
+//                   then up rows 8c..8c+7 (so one CTA owns both halves of SwiGLU), then the
+//                   down projection in chunks of 16 output rows.
+//   GDN state       fp32 [gdn_layer][slot][nv][dv][dk]; conv window as a ring of the last
+//                   4 pre-convolution projections, slot of position p = p % 4.
+//   KV cache        bf16 pages [att_layer][page][K|V][Hkv][16][D], page table per slot.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+// Device error word bits (OR-ed by kernels, read by the host after a step).
+#define DM_DEVERR_TIMEOUT 0x1u
+#define DM_DEVERR_NONFINITE 0x2u
+#define DM_DEVERR_CAPACITY 0x4u
+#define DM_DEVERR_PAGE 0x8u
+#define DM_DEVERR_TOKEN 0x10u
+
+namespace dm {
+
+constexpr int kPageTokens = 16;
+constexpr int kConvRing = 4;       // ring slots for the causal conv window (kernel 4)
+constexpr int kMaxTopK = 16;
+constexpr int kMaxSplits = 64;     // split-K partitions of decode attention
+constexpr int kGemvRowsPerStage = 4;
+
+struct Dims {
+    int H, L, interval, V;
+    float eps;
+    int Hq, Hkv, D, rot_dim;
+    float theta;
+    int nk, nv, dk, dv, conv_k;
+    int qkv_dim, z_dim, gdn_in_rows;     // 2*nk*dk + nv*dv, nv*dv, qkv+z+2nv
+    int attn_in_rows;                    // 2*Hq*D + 2*Hkv*D
+    int E, topk, I, G;
+    int max_seqs, num_pages, max_pages;
+    int n_gdn, n_att;
+    // expert record geometry (bytes)
+    int64_t gu_chunk_bytes, d_chunk_bytes, expert_bytes;
+    int gu_chunks, d_chunks;
+};
+
+struct LayerW {
+    int is_attn;
+    int sub;                         // index among GDN layers or among attention layers
+    const uint16_t* in_norm;
+    const uint16_t* post_norm;
+    const uint16_t* w_in;            // concatenated input projections
+    const uint16_t* conv_w;          // GDN [qkv_dim][conv_k]
+    const float* dt_bias;            // GDN [nv]
+    const float* a_log;              // GDN [nv]
+    const uint16_t* gdn_norm;        // GDN [dv]
+    const uint16_t* q_norm;          // attn [D]
+    const uint16_t* k_norm;          // attn [D]
+    const uint16_t* w_out;           // [H][nv*dv] or [H][Hq*D]
+    const uint16_t* w_router;        // [E+1][H]
+    const uint8_t* experts;          // [E] records
+    const uint8_t* shared;           // 1 record
+};
+
+// Per-context scratch and state (device pointers).
+struct Buffers {
+    float* xres;          // [max_seqs][H] residual stream (layer input/output)
+    float* xmid;          // [max_seqs][H] after the token mixer
+    float* ring;          // [n_gdn][max_seqs][4][qkv_dim]
+    float* S;             // [n_gdn][max_seqs][nv][dv][dk]
+    uint16_t* kv;         // [n_att][num_pages][2][Hkv][16][D]
+    int* page_table;      // [max_seqs][max_pages]
+    int* pos;             // [max_seqs] current length
+    int* token;           // [max_seqs] token to embed next
+    int* gen_out;         // [gen_capacity] generated tokens (device loop)
+    int* gen_idx;         // [1] write index into gen_out
+    int gen_capacity;
+    int* prompt;          // [gen_capacity] prompt ids staged for dm_forward
+    // scratch for one token
+    float* z;             // [z_dim]   SiLU(W_z x)
+    float* ab;            // [2*nv]    a then b
+    float* o;             // [nv*dv]   S q per head
+    float* qg;            // [2*Hq*D]  q rows then gate rows
+    float* kvnew;         // [2*Hkv*D] k then v (raw projections)
+    float* attn_part;     // [Hq][kMaxSplits][D + 2]
+    float* attn_out;      // [Hq*D]    gated attention output
+    float* xn;            // [H]       post-attention RMSNorm output (MoE input)
+    float* rlogits;       // [E+1]     router logits + shared gate logit
+    int* topk_ids;        // [topk]
+    float* topk_p;        // [topk]
+    float* shared_g;      // [1]
+    float* h;             // [(topk+1)][I]  SwiGLU activations
+    float* logits;        // [V]
+    float* cand_val;      // [kMaxCtas]
+    int* cand_idx;        // [kMaxCtas]
+    unsigned* counters;   // [64]
+    uint32_t* err;        // [1]
+};
+
+constexpr int kMaxCtas = 1024;
+// counter slots
+constexpr int kCntRouter = 0;
+constexpr int kCntHead = 1;
+constexpr int kCntAttnBase = 8;   // + kv head (< 32)
+
+struct Ctx;  // host-side context (dm_api.cu)
+
+struct LaunchCfg {
+    cudaStream_t stream;
+    int num_sms;
+    bool pdl;
+};
+
+// Kernel launchers (dm_kernels.cu).  `slot` selects the sequence.
+cudaError_t launch_embed(const LaunchCfg& lc, const Dims& d, const uint16_t* embed,
+                         const Buffers& b, int slot);
+cudaError_t launch_gdn_in(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                          const Buffers& b, int slot);
+cudaError_t launch_gdn_rec(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                           const Buffers& b, int slot);
+cudaError_t launch_gdn_out(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                           const Buffers& b, int slot);
+cudaError_t launch_attn_in(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                           const Buffers& b, int slot);
+cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                               const Buffers& b, int slot);
+cudaError_t launch_attn_out(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                            const Buffers& b, int slot);
+// router: normalise_input = 1 applies post_norm to b.xmid[slot]; 0 takes b.xn as given.
+cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                          const Buffers& b, int slot, int normalise_input);
+cudaError_t launch_moe_up(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                          const Buffers& b);
+// down projection + weighted sum + residual: x_out = x_res + sum
+cudaError_t launch_moe_down(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                            const Buffers& b, const float* x_res, float* x_out);
+cudaError_t launch_head(const LaunchCfg& lc, const Dims& d, const uint16_t* final_norm,
+                        const uint16_t* lm_head, const Buffers& b, int slot, int advance,
+                        int record_gen);
+}  // namespace dm

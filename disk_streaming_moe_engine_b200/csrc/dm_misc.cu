@@ -1,0 +1,94 @@
+// dm_misc.cu — KV page scatter/gather and the device-side synthetic weight fill.
+#include "dm_common.cuh"
+#include "dm_kernels.h"
+#include "dm_synth.h"
+
+namespace dm {
+
+// Contiguous [n][Hkv][D] K and V <-> pages [page][K|V][Hkv][16][D] through a page table
+// (the gather of reference LayerKVCache.get_k_slice, kv_cache.mojo:377, over pages).
+__global__ void kv_copy_kernel(uint16_t* kv, const int* page_table, int Hkv, int D, uint16_t* k,
+                               uint16_t* v, int n_tokens, int to_cache, uint32_t* err) {
+    const int64_t per_tok = static_cast<int64_t>(Hkv) * D;
+    const int64_t total = per_tok * n_tokens;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int t = static_cast<int>(i / per_tok);
+        const int hd = static_cast<int>(i % per_tok);
+        const int h = hd / D, d = hd % D;
+        const int page = page_table[t / kPageTokens];
+        if (page < 0) {
+            if (err) atomicOr(err, DM_DEVERR_PAGE);
+            continue;
+        }
+        const size_t kk = ((static_cast<size_t>(page) * 2 + 0) * Hkv + h) * kPageTokens * D +
+                          static_cast<size_t>(t % kPageTokens) * D + d;
+        const size_t vv = kk + static_cast<size_t>(Hkv) * kPageTokens * D;
+        if (to_cache) {
+            kv[kk] = k[i];
+            kv[vv] = v[i];
+        } else {
+            k[i] = kv[kk];
+            v[i] = kv[vv];
+        }
+    }
+}
+
+cudaError_t launch_kv_copy(cudaStream_t st, uint16_t* kv_layer, const int* page_table_row, int Hkv, int D,
+                           uint16_t* k, uint16_t* v, int n_tokens, int to_cache) {
+    const int64_t total = static_cast<int64_t>(n_tokens) * Hkv * D;
+    int blocks = static_cast<int>((total + 255) / 256);
+    if (blocks > 8192) blocks = 8192;
+    if (blocks < 1) blocks = 1;
+    kv_copy_kernel<<<blocks, 256, 0, st>>>(kv_layer, page_table_row, Hkv, D, k, v, n_tokens, to_cache, nullptr);
+    return cudaGetLastError();
+}
+
+__global__ void synth_bf16_kernel(uint16_t* dst, uint64_t n, uint64_t key, float mean, float std) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        dst[i] = synth_f32_to_bf16(mean + std * synth_normal(synth_hash(key, i)));
+}
+__global__ void synth_f32_kernel(float* dst, uint64_t n, uint64_t key, float mean, float std) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        dst[i] = mean + std * synth_normal(synth_hash(key, i));
+}
+__global__ void synth_u8_kernel(uint8_t* dst, uint64_t n, uint64_t key) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        dst[i] = synth_byte(key, i);
+}
+__global__ void synth_f16abs_kernel(uint16_t* dst, uint64_t n, uint64_t key, float std) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        dst[i] = synth_f32_to_f16(fabsf(std * synth_normal(synth_hash(key, i))));
+}
+
+static int grid_for(uint64_t n) {
+    uint64_t b = (n + 255) / 256;
+    if (b > 16384) b = 16384;
+    if (b < 1) b = 1;
+    return static_cast<int>(b);
+}
+
+cudaError_t launch_synth_bf16(cudaStream_t st, uint16_t* dst, uint64_t n, uint64_t seed, uint64_t sid, float mean,
+                              float std) {
+    synth_bf16_kernel<<<grid_for(n), 256, 0, st>>>(dst, n, synth_key(seed, sid), mean, std);
+    return cudaGetLastError();
+}
+cudaError_t launch_synth_f32(cudaStream_t st, float* dst, uint64_t n, uint64_t seed, uint64_t sid, float mean,
+                             float std) {
+    synth_f32_kernel<<<grid_for(n), 256, 0, st>>>(dst, n, synth_key(seed, sid), mean, std);
+    return cudaGetLastError();
+}
+cudaError_t launch_synth_u8(cudaStream_t st, uint8_t* dst, uint64_t n, uint64_t seed, uint64_t sid) {
+    synth_u8_kernel<<<grid_for(n), 256, 0, st>>>(dst, n, synth_key(seed, sid));
+    return cudaGetLastError();
+}
+cudaError_t launch_synth_f16abs(cudaStream_t st, uint16_t* dst, uint64_t n, uint64_t seed, uint64_t sid, float std) {
+    synth_f16abs_kernel<<<grid_for(n), 256, 0, st>>>(dst, n, synth_key(seed, sid), std);
+    return cudaGetLastError();
+}
+
+}  // namespace dm

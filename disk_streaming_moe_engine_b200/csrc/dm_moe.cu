@@ -1,0 +1,495 @@
+// dm_moe.cu — MoE channel mixer of the decode step on sm_100a.
+//
+//  router_kernel   post-attention RMSNorm + router GEMV (E rows + shared-gate row) in a
+//                  fixed reduction order, then in the last CTA: fp32 softmax with the
+//                  deterministic exponential, top-k on probabilities with ties to the lower
+//                  expert id, no renormalisation, shared gate sigmoid
+//                  (reference router.mojo:15-185, topk.mojo:11-131, moe.mojo:17).
+//  moe_up_kernel   for the k routed experts and the shared expert: nibble unpack + group
+//                  scale/zero dequant fused into the gate and up GEMVs, h = SiLU(g) * u
+//                  (reference swiglu.mojo:52, dequant order of quant_format.md:831-854).
+//  moe_down_kernel down GEMV of every selected expert for a 16-row output chunk, weighted
+//                  by the router probability (shared expert by its sigmoid gate), plus the
+//                  residual (reference moe_aggregate_forward, moe.mojo:105-177).
+//
+// 4-bit dot product: with F(n) = bits(0x4B000000 | n) = 2^23 + n, F(q) - F(z) = q - z is
+// exact, so each weight costs one byte-permute, one subtract and one fma; the group scale
+// multiplies the 32-weight partial sum once.
+#include <cuda_fp16.h>
+
+#include "dismoen_cuda.h"
+#include "dismoen_detmath.h"
+#include "dm_common.cuh"
+#include "dm_kernels.h"
+
+namespace dm {
+
+struct RouterArgs {
+    const uint16_t* W;      // [E+1][K]
+    int E, topk;
+    const float* x;         // input activation
+    const uint16_t* gamma;  // post-attention norm (nullptr: x already normalised)
+    float eps;
+    float* xn_out;          // normalised activation for the experts (written by CTA 0)
+    float* logits;          // [E+1]
+    int* ids;
+    float* probs;
+    float* shared_g;
+    unsigned* counter;
+    uint32_t* err;
+};
+
+__device__ __forceinline__ void xs_store_split(float* xs, int K, int k, float v) {
+    int j = k >> 3, e = k & 7;
+    xs[(e < 4 ? 0 : K / 2) + j * 4 + (e & 3)] = v;
+}
+
+template <int K>
+__global__ void __launch_bounds__(256) router_kernel(const __grid_constant__ RouterArgs a) {
+    __shared__ __align__(16) float xs[K];
+    __shared__ float red4[4];
+    __shared__ int is_last;
+    __shared__ float pe[1024];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int row = blockIdx.x * 8 + warp;
+    const int nrows = a.E + 1;
+
+    // weights do not depend on the previous kernel: load them first
+    uint4 wreg[K / 256];
+    if (row < nrows) {
+        const uint4* wr = reinterpret_cast<const uint4*>(a.W + static_cast<size_t>(row) * K);
+#pragma unroll
+        for (int i = 0; i < K / 256; ++i) wreg[i] = ldg_nc_v4(wr + lane + 32 * i);
+    }
+    pdl_wait();
+    if (a.gamma) {
+        if (tid < 128) {
+            float acc = 0.0f;
+            for (int k = tid; k < K; k += 128) acc = __fmaf_rn(a.x[k], a.x[k], acc);
+            acc = warp_sum(acc);
+            if (lane == 0) red4[warp] = acc;
+            named_bar_sync(1, 128);
+            const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red4[0], red4[1]), red4[2]), red4[3]);
+            const float denom = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), a.eps));
+            for (int k = tid; k < K; k += 128) {
+                const float y = __fmul_rn(__fdiv_rn(a.x[k], denom), bf16_to_f32(a.gamma[k]));
+                xs_store_split(xs, K, k, y);
+                if (blockIdx.x == 0) a.xn_out[k] = y;
+            }
+        }
+    } else {
+        for (int k = tid; k < K; k += 256) {
+            xs_store_split(xs, K, k, a.x[k]);
+            if (blockIdx.x == 0) a.xn_out[k] = a.x[k];
+        }
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (row < nrows) {
+        // canonical order: one accumulator per lane, elements 8(lane+32i)+j, i then j
+        const float4* xlo = reinterpret_cast<const float4*>(xs);
+        const float4* xhi = reinterpret_cast<const float4*>(xs + K / 2);
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < K / 256; ++i) {
+            const int j = lane + 32 * i;
+            const uint4 w = wreg[i];
+            const float4 x0 = xlo[j], x1 = xhi[j];
+            acc = __fmaf_rn(bf16lo(w.x), x0.x, acc);
+            acc = __fmaf_rn(bf16hi(w.x), x0.y, acc);
+            acc = __fmaf_rn(bf16lo(w.y), x0.z, acc);
+            acc = __fmaf_rn(bf16hi(w.y), x0.w, acc);
+            acc = __fmaf_rn(bf16lo(w.z), x1.x, acc);
+            acc = __fmaf_rn(bf16hi(w.z), x1.y, acc);
+            acc = __fmaf_rn(bf16lo(w.w), x1.z, acc);
+            acc = __fmaf_rn(bf16hi(w.w), x1.w, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) a.logits[row] = acc;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(a.counter, 1u);
+        is_last = (prev == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!is_last || warp != 0) return;
+    __threadfence();
+
+    // ---- softmax + top-k in one warp (fixed order, restated by the CPU oracle) ----
+    const int E = a.E;
+    float m = -INFINITY;
+    for (int e = lane; e < E; e += 32) m = fmaxf(m, __ldcg(a.logits + e));
+    m = warp_max(m);
+    float s = 0.0f;
+    for (int e = lane; e < E; e += 32) {
+        const float ev = dm_det_exp(DM_DET_SUB(__ldcg(a.logits + e), m));
+        pe[e] = ev;
+        s = DM_DET_ADD(s, ev);
+    }
+    s = warp_sum(s);
+    const float inv = DM_DET_DIV(1.0f, s);
+    for (int e = lane; e < E; e += 32) pe[e] = DM_DET_MUL(pe[e], inv);
+    __syncwarp();
+    for (int r = 0; r < a.topk; ++r) {
+        float bv = -1.0f;
+        int bi = 0x7fffffff;
+        for (int e = lane; e < E; e += 32) {
+            const float p = pe[e];
+            if (p > bv) { bv = p; bi = e; }
+        }
+#pragma unroll
+        for (int mm = 16; mm >= 1; mm >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, mm);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, mm);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) {
+            a.ids[r] = bi;
+            a.probs[r] = bv;
+            pe[bi] = -2.0f;
+        }
+        __syncwarp();
+    }
+    if (lane == 0) {
+        const float zs = __ldcg(a.logits + E);
+        if (a.shared_g) *a.shared_g = sigmoid_f(zs);
+        if (s != s || isinf(s)) raise_error(a.err, DM_DEVERR_NONFINITE);
+        *a.counter = 0u;
+    }
+}
+
+cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                          const Buffers& b, int slot, int normalise_input) {
+    RouterArgs a{};
+    a.W = w.w_router;
+    a.E = d.E;
+    a.topk = d.topk;
+    a.x = normalise_input ? b.xmid + static_cast<size_t>(slot) * d.H : b.xn;
+    a.gamma = normalise_input ? w.post_norm : nullptr;
+    a.eps = d.eps;
+    a.xn_out = normalise_input ? b.xn : b.attn_out;  // pre-normalised input: copy to scratch
+    a.logits = b.rlogits;
+    a.ids = b.topk_ids;
+    a.probs = b.topk_p;
+    a.shared_g = b.shared_g;
+    a.counter = b.counters + kCntRouter;
+    a.err = b.err;
+    const int grid = (d.E + 1 + 7) / 8;
+    switch (d.H) {
+        case 256: return launch_kernel(lc, router_kernel<256>, dim3(grid), dim3(256), 0, a);
+        case 512: return launch_kernel(lc, router_kernel<512>, dim3(grid), dim3(256), 0, a);
+        case 1024: return launch_kernel(lc, router_kernel<1024>, dim3(grid), dim3(256), 0, a);
+        case 2048: return launch_kernel(lc, router_kernel<2048>, dim3(grid), dim3(256), 0, a);
+        case 4096: return launch_kernel(lc, router_kernel<4096>, dim3(grid), dim3(256), 0, a);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// 4-bit chunk geometry: 16 rows of `K` columns, group G.
+template <int K, int G>
+struct Q4 {
+    static constexpr int NV = K / 32;                 // 16-byte vectors per row
+    static constexpr int LPR = NV < 32 ? NV : 32;     // lanes per row
+    static constexpr int RPP = 32 / LPR;              // rows per warp pass
+    static constexpr int VPL = NV / LPR;              // vectors per lane per row
+    static constexpr int Q_BYTES = 16 * K / 2;
+    static constexpr int S_OFF = Q_BYTES;
+    static constexpr int S_BYTES = 16 * (K / G) * 2;
+    static constexpr int Z_OFF = S_OFF + S_BYTES;
+    static constexpr int Z_BYTES = 16 * (K / G) / 2;
+    static constexpr int CHUNK = Z_OFF + Z_BYTES;
+    static_assert(G % 32 == 0 && K % (2 * G) == 0, "group geometry");
+};
+
+// x4 layout of an activation vector for the 4-bit dot: x4[c * NV + v] = x[32v+4c .. +3].
+template <int K>
+__device__ __forceinline__ void x4_store(float* x4, int k, float v) {
+    constexpr int NV = K / 32;
+    const int vv = k >> 5, c = (k >> 2) & 7, e = k & 3;
+    x4[(c * NV + vv) * 4 + e] = v;
+}
+
+__device__ __forceinline__ float nib(uint32_t word_masked, int b) {
+    return __uint_as_float(__byte_perm(word_masked, 0x4B000000u, 0x7540u | b));
+}
+
+// Partial dot of one row of a chunk for the lane's vectors (v = vl + LPR * i).
+template <int K, int G>
+__device__ __forceinline__ float q4_partial(const uint8_t* __restrict__ chunk, int r, int vl,
+                                            const float4* __restrict__ x4) {
+    using Q = Q4<K, G>;
+    const uint8_t* qrow = chunk + r * (K / 2);
+    const uint16_t* srow = reinterpret_cast<const uint16_t*>(chunk + Q::S_OFF) + r * (K / G);
+    const uint8_t* zrow = chunk + Q::Z_OFF + r * (K / G / 2);
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < Q::VPL; ++i) {
+        const int v = vl + Q::LPR * i;
+        const int g = (v * 32) / G;
+        const uint4 q = ldg_nc_v4(qrow + 16 * v);
+        const float s = __half2float(__ushort_as_half(__ldg(srow + g)));
+        const uint32_t zb = __ldg(zrow + (g >> 1));
+        const uint32_t z = (g & 1) ? (zb >> 4) : (zb & 15u);
+        const float fz = __uint_as_float(0x4B000000u | z);
+        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
+        float av = 0.0f;
+#pragma unroll
+        for (int wd = 0; wd < 4; ++wd) {
+            const uint32_t lo = words[wd] & 0x0F0F0F0Fu;
+            const uint32_t hi = (words[wd] >> 4) & 0x0F0F0F0Fu;
+            const float4 xa = x4[(2 * wd) * Q::NV + v];
+            const float4 xb = x4[(2 * wd + 1) * Q::NV + v];
+            av = fmaf(nib(lo, 0) - fz, xa.x, av);
+            av = fmaf(nib(hi, 0) - fz, xa.y, av);
+            av = fmaf(nib(lo, 1) - fz, xa.z, av);
+            av = fmaf(nib(hi, 1) - fz, xa.w, av);
+            av = fmaf(nib(lo, 2) - fz, xb.x, av);
+            av = fmaf(nib(hi, 2) - fz, xb.y, av);
+            av = fmaf(nib(lo, 3) - fz, xb.z, av);
+            av = fmaf(nib(hi, 3) - fz, xb.w, av);
+        }
+        acc = fmaf(s, av, acc);
+    }
+    return acc;
+}
+
+template <int LPR>
+__device__ __forceinline__ float lane_group_sum(float v) {
+#pragma unroll
+    for (int m = LPR / 2; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
+struct MoeArgs {
+    const uint8_t* experts;   // layer base: [E] records
+    const uint8_t* shared;    // shared expert record
+    int64_t expert_bytes, gu_part_bytes;
+    int gu_chunks, d_chunks, topk, I, H;
+    const int* ids;
+    const float* probs;
+    const float* shared_g;
+    const float* xn;          // [H] normalised MoE input
+    float* h;                 // [(topk+1)][I]
+    const float* x_res;       // [H]
+    float* x_out;             // [H]
+};
+
+template <int K, int G>
+__global__ void __launch_bounds__(128) moe_up_kernel(const __grid_constant__ MoeArgs a) {
+    using Q = Q4<K, G>;
+    __shared__ __align__(16) float x4[K];
+    __shared__ int sid[kMaxTopK];
+    __shared__ float dots[4][4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    for (int k = threadIdx.x; k < K; k += 128) x4_store<K>(x4, k, a.xn[k]);
+    if (threadIdx.x < a.topk) sid[threadIdx.x] = a.ids[threadIdx.x];
+    __syncthreads();
+    pdl_launch_dependents();
+    const float4* x4v = reinterpret_cast<const float4*>(x4);
+
+    const int n_items = (a.topk + 1) * a.gu_chunks;
+    const int i0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * n_items / gridDim.x);
+    const int i1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * n_items / gridDim.x);
+    for (int item = i0; item < i1; ++item) {
+        const int j = item / a.gu_chunks, c = item % a.gu_chunks;
+        const uint8_t* rec = (j < a.topk) ? a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes
+                                          : a.shared;
+        const uint8_t* chunk = rec + static_cast<int64_t>(c) * Q::CHUNK;
+        // warp rows in the chunk: gate 2w, 2w+1 and up 8+2w, 8+2w+1
+        const int myrows[4] = {2 * warp, 2 * warp + 1, 8 + 2 * warp, 9 + 2 * warp};
+#pragma unroll
+        for (int p = 0; p < 4; p += Q::RPP) {
+            const int sub = lane / Q::LPR, vl = lane % Q::LPR;
+            const int ri = p + sub;
+            float v = 0.0f;
+            if (ri < 4) v = q4_partial<K, G>(chunk, myrows[ri], vl, x4v);
+            v = lane_group_sum<Q::LPR>(v);
+            if (vl == 0 && ri < 4) dots[warp][ri] = v;
+        }
+        __syncwarp();
+        if (lane < 2) {
+            const float g = dots[warp][lane], u = dots[warp][2 + lane];
+            a.h[j * a.I + 8 * c + 2 * warp + lane] = silu_f(g) * u;
+        }
+        __syncwarp();
+    }
+}
+
+template <int KI, int G>
+__global__ void __launch_bounds__(128) moe_down_kernel(const __grid_constant__ MoeArgs a) {
+    using Q = Q4<KI, G>;
+    extern __shared__ __align__(16) float hs[];  // (topk+1) x4 vectors of length KI
+    __shared__ int sid[kMaxTopK];
+    __shared__ float sp[kMaxTopK + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    const int nexp = a.topk + 1;
+    for (int t = threadIdx.x; t < nexp * KI; t += 128) {
+        const int j = t / KI, k = t % KI;
+        x4_store<KI>(hs + j * KI, k, a.h[t]);
+    }
+    if (threadIdx.x < a.topk) {
+        sid[threadIdx.x] = a.ids[threadIdx.x];
+        sp[threadIdx.x] = a.probs[threadIdx.x];
+    }
+    if (threadIdx.x == 0) sp[a.topk] = *a.shared_g;
+    __syncthreads();
+    pdl_launch_dependents();
+
+    const int c = blockIdx.x;  // 16-row output chunk
+#pragma unroll
+    for (int p = 0; p < 4; p += Q::RPP) {
+        const int sub = lane / Q::LPR, vl = lane % Q::LPR;
+        const int ri = p + sub;
+        const int r = 4 * warp + (ri < 4 ? ri : 0);
+        float routed = 0.0f, shared_v = 0.0f;
+        for (int j = 0; j < nexp; ++j) {
+            const uint8_t* rec = (j < a.topk) ? a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes
+                                              : a.shared;
+            const uint8_t* chunk = rec + a.gu_part_bytes + static_cast<int64_t>(c) * Q::CHUNK;
+            float v = q4_partial<KI, G>(chunk, r, vl, reinterpret_cast<const float4*>(hs + j * KI));
+            v = lane_group_sum<Q::LPR>(v);
+            if (j < a.topk) routed = fmaf(sp[j], v, routed);
+            else shared_v = v;
+        }
+        if (vl == 0 && ri < 4) {
+            const int orow = 16 * c + r;
+            a.x_out[orow] = (routed + sp[a.topk] * shared_v) + a.x_res[orow];
+        }
+    }
+}
+
+template <int K, int KI, int G>
+static cudaError_t launch_moe_t(const LaunchCfg& lc, const MoeArgs& a, bool up) {
+    if (up) {
+        const int n_items = (a.topk + 1) * a.gu_chunks;
+        const int grid = n_items < lc.num_sms ? n_items : lc.num_sms;
+        return launch_kernel(lc, moe_up_kernel<K, G>, dim3(grid), dim3(128), 0, a);
+    }
+    const size_t smem = static_cast<size_t>(a.topk + 1) * KI * sizeof(float);
+    return launch_kernel(lc, moe_down_kernel<KI, G>, dim3(a.d_chunks), dim3(128), smem, a);
+}
+
+static MoeArgs moe_args(const Dims& d, const LayerW& w, const Buffers& b) {
+    MoeArgs a{};
+    a.experts = w.experts;
+    a.shared = w.shared;
+    a.expert_bytes = d.expert_bytes;
+    a.gu_part_bytes = static_cast<int64_t>(d.gu_chunks) * d.gu_chunk_bytes;
+    a.gu_chunks = d.gu_chunks;
+    a.d_chunks = d.d_chunks;
+    a.topk = d.topk;
+    a.I = d.I;
+    a.H = d.H;
+    a.ids = b.topk_ids;
+    a.probs = b.topk_p;
+    a.shared_g = b.shared_g;
+    a.xn = b.xn;
+    a.h = b.h;
+    return a;
+}
+
+static cudaError_t launch_moe(const LaunchCfg& lc, const Dims& d, const MoeArgs& a, bool up) {
+    if (d.G != 64) return cudaErrorInvalidValue;
+    if (d.H == 2048 && d.I == 512) return launch_moe_t<2048, 512, 64>(lc, a, up);
+    if (d.H == 256 && d.I == 128) return launch_moe_t<256, 128, 64>(lc, a, up);
+    if (d.H == 1024 && d.I == 256) return launch_moe_t<1024, 256, 64>(lc, a, up);
+    if (d.H == 2048 && d.I == 256) return launch_moe_t<2048, 256, 64>(lc, a, up);
+    if (d.H == 4096 && d.I == 512) return launch_moe_t<4096, 512, 64>(lc, a, up);
+    return cudaErrorInvalidValue;
+}
+
+bool moe_supported(int H, int I, int G) {
+    return G == 64 && ((H == 2048 && I == 512) || (H == 256 && I == 128) || (H == 1024 && I == 256) ||
+                       (H == 2048 && I == 256) || (H == 4096 && I == 512));
+}
+
+cudaError_t moe_set_attrs() {
+    cudaError_t e;
+    if ((e = cudaFuncSetAttribute(moe_down_kernel<512, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (kMaxTopK + 1) * 512 * 4)) != cudaSuccess)
+        return e;
+    if ((e = cudaFuncSetAttribute(moe_down_kernel<256, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (kMaxTopK + 1) * 256 * 4)) != cudaSuccess)
+        return e;
+    return cudaFuncSetAttribute(moe_down_kernel<128, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (kMaxTopK + 1) * 128 * 4);
+}
+
+cudaError_t launch_moe_up(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b) {
+    return launch_moe(lc, d, moe_args(d, w, b), true);
+}
+
+cudaError_t launch_moe_down(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                            const Buffers& b, const float* x_res, float* x_out) {
+    MoeArgs a = moe_args(d, w, b);
+    a.x_res = x_res;
+    a.x_out = x_out;
+    return launch_moe(lc, d, a, false);
+}
+
+// ---------------------------------------------------------------------------------------
+// Stand-alone dequantisation of a canonical (row-major, unchunked) 4-bit tensor.
+__global__ void dequant_q4_kernel(const uint8_t* q, const uint16_t* s, const uint8_t* z, int rows,
+                                  int cols, int group, float* out) {
+    const int64_t n = static_cast<int64_t>(rows) * cols;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / cols;
+        const int c = static_cast<int>(i % cols);
+        const uint8_t byte = q[r * (cols / 2) + c / 2];
+        const int qv = (c & 1) ? (byte >> 4) : (byte & 15);
+        const int g = c / group;
+        const int ng = cols / group;
+        const uint8_t zb = z[r * (ng / 2) + g / 2];
+        const int zv = (g & 1) ? (zb >> 4) : (zb & 15);
+        const float sc = __half2float(__ushort_as_half(s[r * ng + g]));
+        out[i] = sc * static_cast<float>(qv - zv);
+    }
+}
+
+cudaError_t launch_dequant_q4_canonical(cudaStream_t st, const uint8_t* q, const uint16_t* s,
+                                        const uint8_t* z, int rows, int cols, int group, float* out) {
+    const int64_t n = static_cast<int64_t>(rows) * cols;
+    int blocks = static_cast<int>((n + 255) / 256);
+    if (blocks > 4096) blocks = 4096;
+    dequant_q4_kernel<<<blocks, 256, 0, st>>>(q, s, z, rows, cols, group, out);
+    return cudaGetLastError();
+}
+
+// Canonical rows -> chunked expert record (see dm_internal.h).  One block per source row.
+__global__ void repack_rows_kernel(const uint8_t* q, const uint16_t* s, const uint8_t* z, int rows,
+                                   int cols, int group, int kind, uint8_t* dst) {
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const int ng = cols / group;
+    const int qb = cols / 2, sb = ng * 2, zb = ng / 2;
+    const int64_t chunk_bytes = 16LL * (qb + sb + zb);
+    int chunk, rin;
+    if (kind == DM_PROJ_DOWN) {
+        chunk = r / 16;
+        rin = r % 16;
+    } else {
+        chunk = r / 8;
+        rin = (kind == DM_PROJ_UP ? 8 : 0) + r % 8;
+    }
+    uint8_t* cbase = dst + chunk * chunk_bytes;
+    for (int i = threadIdx.x; i < qb; i += blockDim.x) cbase[rin * qb + i] = q[static_cast<int64_t>(r) * qb + i];
+    uint16_t* sdst = reinterpret_cast<uint16_t*>(cbase + 16 * qb);
+    for (int i = threadIdx.x; i < ng; i += blockDim.x) sdst[rin * ng + i] = s[static_cast<int64_t>(r) * ng + i];
+    uint8_t* zdst = cbase + 16 * qb + 16 * sb;
+    for (int i = threadIdx.x; i < zb; i += blockDim.x) zdst[rin * zb + i] = z[static_cast<int64_t>(r) * zb + i];
+}
+
+cudaError_t launch_repack_rows(cudaStream_t st, const uint8_t* q, const uint16_t* s, const uint8_t* z,
+                               int rows, int cols, int group, int kind, uint8_t* dst) {
+    repack_rows_kernel<<<rows, 128, 0, st>>>(q, s, z, rows, cols, group, kind, dst);
+    return cudaGetLastError();
+}
+
+}  // namespace dm

@@ -1,0 +1,302 @@
+"""Host-side mirror of the reference engine's layer API over libdismoen_cuda.so.
+
+The reference Mojo engine exposes, per layer (src/layers/port_scheduler.mojo,
+gguf_port_loader.mojo, router.mojo, gated_attention.mojo, gdn.mojo):
+
+  forward_port_block(x, block, gdn_states, kv_cache, layer_idx, pos_offset, seq_len, ...)
+  forward_port_macro_scheduler_gguf(x, index, gdn_states, kv_cache, pos_offset, seq_len, ...)
+  router_forward(x, w_router, seq_len, hidden, RouterConfig, layer_idx) -> RoutingInfo
+  GatedAttnKVCache(capacity, l_att, h_kv, head_dim): store_tokens / get_k / get_v / zero
+  GDNState(layers, dv, dk): zero / clone / check_finite
+
+Here the weights live in the device context (uploaded once instead of streamed per
+step), so the per-call weight arguments disappear; argument meaning, shapes and error
+behaviour follow the reference: errors raise `DmError` carrying the library's JSON
+message in the reference shape {"error_type", "detail", "stage", "layer"}.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import dataclasses
+
+import numpy as np
+
+from . import _lib
+from .config import ModelConfig, RuntimeConfig
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+@dataclasses.dataclass
+class RoutingInfo:
+    """reference src/layers/router_types.mojo:48 (selected experts, probabilities)."""
+    selected_experts: np.ndarray   # [seq_len, top_k] int32
+    routing_weights: np.ndarray    # [seq_len, top_k] fp32, not renormalised
+    shared_gate: np.ndarray        # [seq_len] sigmoid(w_sh . x)
+    seq_len: int
+    top_k: int
+
+
+class Engine:
+    """One device context: model weights in HBM plus `max_seqs` sequence slots."""
+
+    def __init__(self, cfg: ModelConfig, rt: RuntimeConfig | None = None, device: int = 0):
+        self.cfg = cfg
+        self.rt = rt or RuntimeConfig.for_context(1024)
+        self.lib = _lib.load()
+        self._mc = cfg.to_c()
+        self._rc = self.rt.to_c()
+        buf = C.create_string_buffer(512)
+        if self.lib.dm_config_validate(C.byref(self._mc), buf, 512) != 0:
+            raise _lib.DmError(_lib.DM_ERR_INVALID_ARG, buf.value.decode())
+        h = C.c_void_p()
+        rc = self.lib.dm_ctx_create(C.byref(self._mc), C.byref(self._rc), device, C.byref(h))
+        if rc != 0:
+            raise _lib.DmError(rc, "dm_ctx_create failed (see stderr)")
+        self.ctx = h
+
+    # ---- plumbing ----
+    def close(self):
+        if getattr(self, "ctx", None):
+            self.lib.dm_ctx_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def last_error(self) -> str:
+        buf = C.create_string_buffer(1024)
+        self.lib.dm_last_error(self.ctx, buf, 1024)
+        return buf.value.decode()
+
+    def _ok(self, rc: int):
+        if rc != 0:
+            raise _lib.DmError(rc, self.last_error())
+
+    def device_bytes(self) -> int:
+        v = C.c_uint64()
+        self._ok(self.lib.dm_ctx_device_bytes(self.ctx, C.byref(v)))
+        return v.value
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        self._ok(self.lib.dm_get_stream(self.ctx, C.byref(s)))
+        return s.value or 0
+
+    def time_kernel(self, which: int, layer: int, iters: int = 20):
+        """(mean ms per launch, algorithmic bytes per launch) of one kernel kind."""
+        ms, nb = C.c_float(), C.c_uint64()
+        self._ok(self.lib.dm_time_kernel(self.ctx, which, layer, iters, C.byref(ms), C.byref(nb)))
+        return ms.value, nb.value
+
+    def kernels_per_step(self) -> int:
+        v = C.c_int32()
+        self._ok(self.lib.dm_kernels_per_step(self.ctx, C.byref(v)))
+        return v.value
+
+    # ---- weights (quant loader / tensor-name contract) ----
+    def upload_tensor(self, layer: int, tensor_id: int, arr: np.ndarray):
+        arr = np.ascontiguousarray(arr)
+        dt = _lib.DM_DTYPE_F32 if arr.dtype == np.float32 else _lib.DM_DTYPE_BF16
+        if arr.dtype not in (np.float32, np.uint16):
+            raise TypeError("dense tensors are bf16 bit patterns (uint16) or float32")
+        self._ok(self.lib.dm_upload_tensor(self.ctx, layer, tensor_id, dt, _ptr(arr), arr.size))
+
+    def upload_expert(self, layer: int, expert: int, proj: int, q: np.ndarray, s: np.ndarray, z: np.ndarray):
+        q, s, z = (np.ascontiguousarray(a) for a in (q, s, z))
+        self._ok(self.lib.dm_expert_upload(self.ctx, layer, expert, proj, _ptr(q), _ptr(s), _ptr(z)))
+
+    _GDN = {"qkv": _lib.DM_T_GDN_QKV, "z": _lib.DM_T_GDN_Z, "a": _lib.DM_T_GDN_A, "b": _lib.DM_T_GDN_B,
+            "conv": _lib.DM_T_GDN_CONV, "dt_bias": _lib.DM_T_GDN_DT_BIAS, "a_log": _lib.DM_T_GDN_A_LOG,
+            "gnorm": _lib.DM_T_GDN_NORM, "out": _lib.DM_T_GDN_OUT}
+    _ATT = {"q": _lib.DM_T_ATTN_Q, "k": _lib.DM_T_ATTN_K, "v": _lib.DM_T_ATTN_V, "qn": _lib.DM_T_ATTN_Q_NORM,
+            "kn": _lib.DM_T_ATTN_K_NORM, "o": _lib.DM_T_ATTN_O}
+    _COMMON = {"in_norm": _lib.DM_T_INPUT_NORM, "post_norm": _lib.DM_T_POST_NORM, "router": _lib.DM_T_ROUTER,
+               "shared_gate": _lib.DM_T_SHARED_GATE}
+
+    def load_layer(self, layer: int, t: dict):
+        """Binds one layer's tensors (the role of load_port_block_from_gguf,
+        reference gguf_port_loader.mojo:115)."""
+        table = dict(self._COMMON)
+        table.update(self._ATT if self.cfg.is_attention_layer(layer) else self._GDN)
+        for name, tid in table.items():
+            self.upload_tensor(layer, tid, t[name])
+        if "gq" in t:
+            E = self.cfg.num_experts
+            for idx in range(E + 1):
+                e = idx if idx < E else -1
+                self.upload_expert(layer, e, _lib.DM_PROJ_GATE, t["gq"][idx], t["gs"][idx], t["gz"][idx])
+                self.upload_expert(layer, e, _lib.DM_PROJ_UP, t["uq"][idx], t["us"][idx], t["uz"][idx])
+                self.upload_expert(layer, e, _lib.DM_PROJ_DOWN, t["dq"][idx], t["ds"][idx], t["dz"][idx])
+
+    def load_model(self, m: dict):
+        for l, t in m["layers"].items():
+            self.load_layer(l, t)
+        if "embed" in m:
+            self.upload_tensor(-1, _lib.DM_T_EMBED, m["embed"])
+            self.upload_tensor(-1, _lib.DM_T_FINAL_NORM, m["final_norm"])
+            self.upload_tensor(-1, _lib.DM_T_LM_HEAD, m["lm_head"])
+
+    def synth_on_device(self, seed: int):
+        self._ok(self.lib.dm_synth_model_device(self.ctx, seed))
+
+    def weights_check(self):
+        self._ok(self.lib.dm_weights_check(self.ctx))
+
+    def dequant_q4(self, q: np.ndarray, s: np.ndarray, z: np.ndarray, rows: int, cols: int, group: int = 64):
+        out = np.empty((rows, cols), np.float32)
+        q, s, z = (np.ascontiguousarray(a) for a in (q, s, z))
+        self._ok(self.lib.dm_dequant_q4(self.ctx, _ptr(q), _ptr(s), _ptr(z), rows, cols, group, _ptr(out)))
+        return out
+
+    # ---- sequence state (KV-cache object, GDN state) ----
+    def seq_reset(self, slot: int = 0):
+        self._ok(self.lib.dm_seq_reset(self.ctx, slot))
+
+    def seq_len(self, slot: int = 0) -> int:
+        v = C.c_int32()
+        self._ok(self.lib.dm_seq_get_len(self.ctx, slot, C.byref(v)))
+        return v.value
+
+    def seq_set_len(self, slot: int, n: int):
+        self._ok(self.lib.dm_seq_set_len(self.ctx, slot, n))
+
+    def set_page_table(self, slot: int, pages):
+        p = np.ascontiguousarray(pages, dtype=np.int32)
+        self._ok(self.lib.dm_seq_set_page_table(self.ctx, slot, _ptr(p), p.size))
+
+    def kv_import(self, att_layer: int, slot: int, k_bf16: np.ndarray, v_bf16: np.ndarray):
+        k, v = np.ascontiguousarray(k_bf16, np.uint16), np.ascontiguousarray(v_bf16, np.uint16)
+        n = k.shape[0]
+        self._ok(self.lib.dm_kv_import(self.ctx, att_layer, slot, _ptr(k), _ptr(v), n))
+
+    def kv_export(self, att_layer: int, slot: int, n: int):
+        shape = (n, self.cfg.num_key_value_heads, self.cfg.head_dim)
+        k, v = np.empty(shape, np.uint16), np.empty(shape, np.uint16)
+        self._ok(self.lib.dm_kv_export(self.ctx, att_layer, slot, _ptr(k), _ptr(v), n))
+        return k, v
+
+    def gdn_state_import(self, gdn_layer: int, slot: int, S: np.ndarray | None, conv: np.ndarray | None = None):
+        s = None if S is None else np.ascontiguousarray(S, np.float32)
+        c = None if conv is None else np.ascontiguousarray(conv, np.float32)
+        self._ok(self.lib.dm_gdn_state_import(self.ctx, gdn_layer, slot, None if s is None else _ptr(s),
+                                              None if c is None else _ptr(c)))
+
+    def gdn_state_export(self, gdn_layer: int, slot: int):
+        cfg = self.cfg
+        S = np.empty((cfg.linear_num_value_heads, cfg.linear_value_head_dim, cfg.linear_key_head_dim), np.float32)
+        conv = np.empty((3, cfg.qkv_dim), np.float32)
+        self._ok(self.lib.dm_gdn_state_export(self.ctx, gdn_layer, slot, _ptr(S), _ptr(conv)))
+        return S, conv
+
+    # ---- compute: reference-facing ----
+    def router_forward(self, x: np.ndarray, layer_idx: int) -> RoutingInfo:
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        n, k = x.shape[0], self.cfg.num_experts_per_tok
+        ids, probs, sg = np.empty((n, k), np.int32), np.empty((n, k), np.float32), np.empty(n, np.float32)
+        self._ok(self.lib.dm_router(self.ctx, layer_idx, _ptr(x), n, _ptr(ids), _ptr(probs), _ptr(sg)))
+        return RoutingInfo(ids, probs, sg, n, k)
+
+    def moe_block(self, x_mid: np.ndarray, layer_idx: int) -> np.ndarray:
+        x = np.ascontiguousarray(np.atleast_2d(x_mid), np.float32)
+        y = np.empty_like(x)
+        self._ok(self.lib.dm_moe_block(self.ctx, layer_idx, _ptr(x), x.shape[0], _ptr(y)))
+        return y
+
+    def mixer_block(self, x: np.ndarray, layer_idx: int, pos_offset: int, slot: int = 0) -> np.ndarray:
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        y = np.empty_like(x)
+        self._ok(self.lib.dm_mixer_block(self.ctx, layer_idx, slot, pos_offset, _ptr(x), x.shape[0], _ptr(y)))
+        return y
+
+    def forward_port_block(self, x: np.ndarray, layer_idx: int, pos_offset: int, slot: int = 0) -> np.ndarray:
+        """reference forward_port_block (port_scheduler.mojo:286) for seq_len = len(x)."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        y = np.empty_like(x)
+        self._ok(self.lib.dm_block_forward(self.ctx, layer_idx, slot, pos_offset, _ptr(x), x.shape[0], _ptr(y)))
+        return y
+
+    def forward(self, tokens, slot: int = 0, want_logits: bool = True):
+        """Macro scheduler over all blocks for `tokens` appended to `slot` (reference
+        forward_port_macro_scheduler_gguf, gguf_port_loader.mojo:329) -> (logits, argmax)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(self.cfg.vocab_size, np.float32) if want_logits else None
+        nxt = C.c_int32()
+        self._ok(self.lib.dm_forward(self.ctx, slot, _ptr(t), t.size, None if logits is None else _ptr(logits),
+                                     C.byref(nxt)))
+        return logits, nxt.value
+
+    def decode_step(self, token: int, slot: int = 0, want_logits: bool = False):
+        logits = np.empty(self.cfg.vocab_size, np.float32) if want_logits else None
+        out = C.c_int32()
+        self._ok(self.lib.dm_decode_step(self.ctx, slot, int(token), C.byref(out),
+                                         None if logits is None else _ptr(logits)))
+        return out.value, logits
+
+    def generate(self, token: int, n_steps: int, slot: int = 0) -> np.ndarray:
+        out = np.empty(n_steps, np.int32)
+        self._ok(self.lib.dm_generate(self.ctx, slot, int(token), n_steps, _ptr(out)))
+        return out
+
+    def enqueue_decode(self, n_steps: int, slot: int = 0):
+        self._ok(self.lib.dm_enqueue_decode(self.ctx, slot, n_steps))
+
+    def set_token(self, token: int, slot: int = 0):
+        self._ok(self.lib.dm_set_token(self.ctx, slot, int(token)))
+
+    def sync(self):
+        self._ok(self.lib.dm_sync(self.ctx))
+
+
+class GatedAttnKVCache:
+    """View of one slot's paged KV cache with the reference object's surface
+    (gated_attention.mojo:38-153 / kv_cache.mojo:213-420)."""
+
+    def __init__(self, engine: Engine, slot: int = 0):
+        self.engine, self.slot = engine, slot
+
+    def zero(self):
+        self.engine.seq_reset(self.slot)
+
+    def store_prefill(self, att_layer: int, k_bf16: np.ndarray, v_bf16: np.ndarray):
+        self.engine.kv_import(att_layer, self.slot, k_bf16, v_bf16)
+
+    def get_k(self, att_layer: int, length: int) -> np.ndarray:
+        return self.engine.kv_export(att_layer, self.slot, length)[0]
+
+    def get_v(self, att_layer: int, length: int) -> np.ndarray:
+        return self.engine.kv_export(att_layer, self.slot, length)[1]
+
+    @property
+    def current_len(self) -> int:
+        return self.engine.seq_len(self.slot)
+
+
+class GDNState:
+    """View of one slot's GDN recurrent state (reference GDNState, gdn.mojo:64-124)."""
+
+    def __init__(self, engine: Engine, slot: int = 0):
+        self.engine, self.slot = engine, slot
+
+    def zero(self):
+        self.engine.seq_reset(self.slot)
+
+    def get(self, gdn_layer: int):
+        return self.engine.gdn_state_export(gdn_layer, self.slot)
+
+    def set(self, gdn_layer: int, S: np.ndarray, conv: np.ndarray | None = None):
+        self.engine.gdn_state_import(gdn_layer, self.slot, S, conv)
+
+    def check_finite(self) -> bool:
+        return all(np.isfinite(self.get(g)[0]).all() for g in range(self.engine.cfg.num_gdn_layers()))

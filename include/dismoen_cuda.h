@@ -1,0 +1,318 @@
+/*
+ * dismoen_cuda.h — C ABI of libdismoen_cuda.so, the B200 (sm_100a) implementation of
+ * DISMOEN's per-token decode step for a Qwen3.6-35B-A3B-shaped hybrid MoE
+ * (blocks [GDN, GDN, GDN, GatedAttn] x N, MoE top-k + 1 shared expert per block).
+ *
+ * The reference engine is Mojo and reaches native code through `external_call`
+ * (reference src/core/worker_pool.mojo:202-457, src/cli/cmd_decode.mojo:78).  Every
+ * symbol below is a plain `extern "C"` function taking plain pointers and sizes so that
+ * the same binding works from Mojo `external_call`, Python `ctypes` or C.
+ *
+ * Conventions
+ *  - Every function returns int32 status: DM_OK (0) or one of DM_ERR_*.  The message of
+ *    the last failure is a JSON object in the reference error shape
+ *    {"error_type":..., "detail":..., "stage":..., "layer":...}
+ *    (reference src/layers/router.mojo:28-33), read with dm_last_error().
+ *  - Pointers named *_host are host memory owned by the caller; the library never keeps
+ *    or frees them.  All device memory is owned by the context.
+ *  - One host thread per context; all work runs on the context's CUDA stream.  Calls
+ *    with host outputs synchronise that stream before returning.
+ *  - Activations are fp32, dense weights bf16 (raw uint16 bit patterns), routed and
+ *    shared experts in the asymmetric 4-bit group format described at
+ *    dm_expert_upload().
+ */
+#ifndef DISMOEN_CUDA_H
+#define DISMOEN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DM_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------------------ */
+#define DM_OK 0
+#define DM_ERR_INVALID_ARG 1   /* bad pointer, size, index or config                  */
+#define DM_ERR_CUDA 2          /* a CUDA runtime call failed                           */
+#define DM_ERR_OOM 3           /* device allocation failed                             */
+#define DM_ERR_POSITION 4      /* KV append position contract violated                 */
+#define DM_ERR_CAPACITY 5      /* KV capacity / page table exhausted                   */
+#define DM_ERR_NONFINITE 6     /* NaN/Inf reached a checked output (logits)            */
+#define DM_ERR_TIMEOUT 7       /* a bounded device-side wait ran out                   */
+#define DM_ERR_NOT_READY 8     /* weights missing for the requested computation        */
+#define DM_ERR_ROUTER 9        /* router contract violated (e.g. norm_topk_prob)       */
+
+/* ---- configuration ----------------------------------------------------------------- */
+/* Field names and meaning follow the reference ModelConfig
+ * (reference src/core/config.mojo:11-175) plus the GDN shape fields that the reference
+ * hard-codes in forward_gdn_block (reference src/layers/gdn.mojo:897-1183). */
+typedef struct dm_model_config {
+    int32_t hidden_size;                     /* H                                    */
+    int32_t num_hidden_layers;               /* L                                    */
+    int32_t full_attention_interval;         /* layer l is attention iff l%I == I-1  */
+    int32_t vocab_size;                      /* V                                    */
+    float rms_norm_eps;                      /* > 0                                  */
+    /* gated attention */
+    int32_t num_attention_heads;             /* Hq                                   */
+    int32_t num_key_value_heads;             /* Hkv, Hq % Hkv == 0                   */
+    int32_t head_dim;                        /* D (multiple of 64)                   */
+    float rope_theta;
+    float partial_rotary_factor;             /* rotary_dim = int(D * factor)         */
+    /* gated DeltaNet */
+    int32_t linear_num_key_heads;            /* QK heads                             */
+    int32_t linear_num_value_heads;          /* V heads (multiple of QK heads)       */
+    int32_t linear_key_head_dim;             /* dk (64 or 128)                       */
+    int32_t linear_value_head_dim;           /* dv (== dk)                           */
+    int32_t linear_conv_kernel_dim;          /* 4                                    */
+    /* MoE */
+    int32_t num_experts;                     /* E                                    */
+    int32_t num_experts_per_tok;             /* top-k                                */
+    int32_t moe_intermediate_size;           /* I                                    */
+    int32_t shared_expert_intermediate_size; /* must equal I                         */
+    int32_t norm_topk_prob;                  /* must be 0 (no renormalisation)       */
+    int32_t quant_group_size;                /* 64                                   */
+} dm_model_config;
+
+typedef struct dm_runtime_config {
+    int32_t max_seqs;          /* number of sequence slots (KV + GDN state owners)     */
+    int32_t kv_page_tokens;    /* tokens per KV page; must be 16                       */
+    int32_t kv_num_pages;      /* pages in the shared pool (per attention layer)       */
+    int32_t max_pages_per_seq; /* page-table width; capacity = this * 16 tokens        */
+} dm_runtime_config;
+
+typedef struct dm_ctx dm_ctx;
+
+/* ---- lifecycle ----------------------------------------------------------------------- */
+/* Validates the config (the checks of reference ModelConfig.__init__, config.mojo:31-147,
+ * plus kernel shape limits), selects `device`, allocates every weight, state and scratch
+ * buffer up front (no allocation happens during compute). */
+int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
+                      int32_t device, dm_ctx** out_ctx);
+int32_t dm_ctx_destroy(dm_ctx* ctx);
+/* Copies the JSON message of the last failure (empty string if none) into buf. */
+int32_t dm_last_error(const dm_ctx* ctx, char* buf, uint64_t buf_size);
+/* Validation only, no GPU use: writes the JSON error into buf on failure. */
+int32_t dm_config_validate(const dm_model_config* model, char* buf, uint64_t buf_size);
+int32_t dm_abi_version(void);
+/* Bytes of device memory held by the context. */
+int32_t dm_ctx_device_bytes(const dm_ctx* ctx, uint64_t* out_bytes);
+
+/* ---- weights: the quant-loader / tensor-name contract ---------------------------------
+ * Replaces the per-layer streaming loader load_port_block_from_gguf
+ * (reference src/layers/gguf_port_loader.mojo:115) and stream_gguf_tensor_f32
+ * (reference src/format/gguf.mojo:563): tensors are uploaded once into an HBM-resident
+ * pool instead of being read and dequantised per layer per step.  Tensor ids mirror the
+ * checkpoint names the reference loads (gdn.mojo:785-795, attention.mojo:504,
+ * router.mojo:213, gguf_port_loader.mojo:274-326). */
+enum dm_tensor_id {
+    DM_T_INPUT_NORM = 0,     /* input_layernorm.weight            [H]                  */
+    DM_T_POST_NORM = 1,      /* post_attention_layernorm.weight   [H]                  */
+    DM_T_GDN_QKV = 2,        /* linear_attn.in_proj_qkv.weight    [2*nk*dk + nv*dv, H] */
+    DM_T_GDN_CONV = 3,       /* linear_attn.conv1d.weight         [2*nk*dk + nv*dv, 4] */
+    DM_T_GDN_Z = 4,          /* linear_attn.in_proj_z.weight      [nv*dv, H]           */
+    DM_T_GDN_A = 5,          /* linear_attn.in_proj_a.weight      [nv, H]              */
+    DM_T_GDN_B = 6,          /* linear_attn.in_proj_b.weight      [nv, H]              */
+    DM_T_GDN_DT_BIAS = 7,    /* linear_attn.dt_bias               [nv]      (f32)      */
+    DM_T_GDN_A_LOG = 8,      /* linear_attn.A_log                 [nv]      (f32)      */
+    DM_T_GDN_NORM = 9,       /* linear_attn.norm.weight           [dv]                 */
+    DM_T_GDN_OUT = 10,       /* linear_attn.out_proj.weight       [H, nv*dv]           */
+    DM_T_ATTN_Q = 11,        /* self_attn.q_proj.weight (q rows then gate rows) [2*Hq*D, H] */
+    DM_T_ATTN_K = 12,        /* self_attn.k_proj.weight           [Hkv*D, H]           */
+    DM_T_ATTN_V = 13,        /* self_attn.v_proj.weight           [Hkv*D, H]           */
+    DM_T_ATTN_Q_NORM = 14,   /* self_attn.q_norm.weight           [D]                  */
+    DM_T_ATTN_K_NORM = 15,   /* self_attn.k_norm.weight           [D]                  */
+    DM_T_ATTN_O = 16,        /* self_attn.o_proj.weight           [H, Hq*D]            */
+    DM_T_ROUTER = 17,        /* mlp.gate.weight                   [E, H]               */
+    DM_T_SHARED_GATE = 18,   /* mlp.shared_expert_gate.weight     [1, H]               */
+    DM_T_EMBED = 19,         /* embed_tokens.weight (layer -1)    [V, H]               */
+    DM_T_FINAL_NORM = 20,    /* norm.weight (layer -1)            [H]                  */
+    DM_T_LM_HEAD = 21,       /* lm_head.weight (layer -1)         [V, H]               */
+    DM_T_COUNT = 22
+};
+
+#define DM_DTYPE_BF16 0
+#define DM_DTYPE_F32 1
+
+/* Uploads one dense tensor.  `dtype` is DM_DTYPE_BF16 for every tensor except
+ * DM_T_GDN_DT_BIAS / DM_T_GDN_A_LOG, which are DM_DTYPE_F32.  `n_elems` must equal the
+ * tensor's element count.  layer = -1 for the global tensors (embed, final norm, lm_head). */
+int32_t dm_upload_tensor(dm_ctx* ctx, int32_t layer, int32_t tensor_id, int32_t dtype,
+                         const void* data_host, uint64_t n_elems);
+
+/* Uploads one projection of one expert into the HBM-resident 4-bit expert pool.
+ *   expert: 0..E-1 for routed experts, -1 for the shared expert of the layer.
+ *   proj:   DM_PROJ_GATE [I, H], DM_PROJ_UP [I, H], DM_PROJ_DOWN [H, I]  (rows, cols).
+ * Format (asymmetric 4-bit, group g = quant_group_size along the column axis):
+ *   q_host      uint8  [rows, cols/2]   two weights per byte, LOW nibble first
+ *                                       (weight 2j in bits 0-3, 2j+1 in bits 4-7; the
+ *                                       nibble order of reference docs/format/
+ *                                       quant_format.md:831-854)
+ *   scales_host fp16   [rows, cols/g]   raw IEEE binary16 bit patterns
+ *   zeros_host  uint8  [rows, cols/g/2] uint4 zero points, low nibble first
+ *   w[r, c] = fp32(scale[r, c/g]) * (q[r, c] - zero[r, c/g])
+ * The library repacks rows into its chunked HBM layout (16-row chunks, nibbles then
+ * scales then zeros) so that one contiguous bulk copy feeds one chunk of a GEMV. */
+#define DM_PROJ_GATE 0
+#define DM_PROJ_UP 1
+#define DM_PROJ_DOWN 2
+int32_t dm_expert_upload(dm_ctx* ctx, int32_t layer, int32_t expert, int32_t proj,
+                         const uint8_t* q_host, const uint16_t* scales_host,
+                         const uint8_t* zeros_host);
+
+/* Coverage check over every tensor the configured model needs (the role of
+ * validate_gguf_port_coverage, reference gguf_port_loader.mojo:70).  DM_ERR_NOT_READY
+ * names the first missing tensor. */
+int32_t dm_weights_check(dm_ctx* ctx);
+
+/* Dequantises `rows x cols` weights of the 4-bit format above on the GPU and writes fp32
+ * to out_host (the role of pread_and_dequant_tensor_f32, reference
+ * src/format/quant_reader.mojo:710, and dequant_kernel_simd,
+ * reference src/quant/dequant_kernel.mojo:22). */
+int32_t dm_dequant_q4(dm_ctx* ctx, const uint8_t* q_host, const uint16_t* scales_host,
+                      const uint8_t* zeros_host, int32_t rows, int32_t cols,
+                      int32_t group, float* out_host);
+
+/* ---- sequence state: the KV-cache object and GDN state -------------------------------
+ * KV cache: paged bf16, 16-token pages.  Page p of slot s holds tokens
+ * [16p, 16p+16) at physical page page_table[s][p]; layout per attention layer
+ * [page][K|V][Hkv][16][D].  Append contract of reference LayerKVCache.append_decode_token
+ * (reference src/layers/kv_cache.mojo:302-345): pos == current_len and
+ * current_len + 1 <= capacity; bf16 store by single round-to-nearest-even. */
+
+/* Resets slot: length 0, GDN recurrent state and conv window zeroed (reference
+ * GDNState.zero, gdn.mojo:64-124; GatedAttnKVCache.zero, gated_attention.mojo:148), and
+ * assigns the identity page table [s*max_pages_per_seq + p] when the pool is large enough
+ * (otherwise the caller must set one with dm_seq_set_page_table). */
+int32_t dm_seq_reset(dm_ctx* ctx, int32_t slot);
+/* Installs an explicit page table (pages[n_pages], each in [0, kv_num_pages)). */
+int32_t dm_seq_set_page_table(dm_ctx* ctx, int32_t slot, const int32_t* pages_host,
+                              int32_t n_pages);
+/* Current length (= position of the next token) of the slot. */
+int32_t dm_seq_get_len(dm_ctx* ctx, int32_t slot, int32_t* len_out);
+/* Sets the slot length (position of the next decode token) without touching KV or GDN
+ * contents, e.g. before importing a KV cache and GDN state for an existing context.  The
+ * GDN conv window of dm_gdn_state_import/export is relative to this length. */
+int32_t dm_seq_set_len(dm_ctx* ctx, int32_t slot, int32_t len);
+/* Writes n_tokens of K and V (bf16 bits, [n_tokens][Hkv][D] each) for attention layer
+ * att_layer (0-based among attention layers) into the slot's pages, positions
+ * [0, n_tokens), and sets the slot length to n_tokens (reference store_prefill,
+ * kv_cache.mojo:245). */
+int32_t dm_kv_import(dm_ctx* ctx, int32_t att_layer, int32_t slot, const uint16_t* k_host,
+                     const uint16_t* v_host, int32_t n_tokens);
+/* Gathers positions [0, n_tokens) back through the page table (reference get_k_slice,
+ * kv_cache.mojo:377). */
+int32_t dm_kv_export(dm_ctx* ctx, int32_t att_layer, int32_t slot, uint16_t* k_host,
+                     uint16_t* v_host, int32_t n_tokens);
+/* GDN state of gdn_layer (0-based among GDN layers) for slot:
+ *   S_host    fp32 [nv][dv][dk] (row = dv, col = dk as reference GDNState, gdn.mojo:64)
+ *   conv_host fp32 [conv_k-1][2*nk*dk + nv*dv]: pre-convolution projections of the last
+ *             conv_k-1 tokens, oldest first (may be NULL = zeros / not exported). */
+int32_t dm_gdn_state_import(dm_ctx* ctx, int32_t gdn_layer, int32_t slot, const float* S_host,
+                            const float* conv_host);
+int32_t dm_gdn_state_export(dm_ctx* ctx, int32_t gdn_layer, int32_t slot, float* S_host,
+                            float* conv_host);
+
+/* ---- compute: reference-facing entry points (host buffers, one sequence) -------------- */
+
+/* router_forward (reference src/layers/router.mojo:188): logits = W_router x, fp32
+ * softmax over all experts (max-shift, exp, multiply by 1/sum; router.mojo:109-185),
+ * top-k on probabilities with ties to the lower expert id and no renormalisation
+ * (reference src/layers/topk.mojo:11-131), plus the shared-expert gate
+ * sigmoid(w_sh . x) (reference src/layers/moe.mojo:17).  x_host [n][H] is the
+ * post-attention-normalised activation; outputs ids [n][k], probs [n][k],
+ * shared_gate [n] (may be NULL). */
+int32_t dm_router(dm_ctx* ctx, int32_t layer, const float* x_host, int32_t n,
+                  int32_t* ids_host, float* probs_host, float* shared_gate_host);
+
+/* MoE channel mixer with residual (reference forward_port_block second half,
+ * port_scheduler.mojo:286, with swiglu_forward swiglu.mojo:52, shared_gate_forward
+ * moe.mojo:17 and moe_aggregate_forward moe.mojo:105):
+ *   x_out = x_mid + sum_k p_k E_k(norm(x_mid)) + sigmoid(w_sh . norm(x_mid)) E_sh(norm(x_mid)) */
+int32_t dm_moe_block(dm_ctx* ctx, int32_t layer, const float* x_mid_host, int32_t n,
+                     float* x_out_host);
+
+/* Token mixer with residual for layer `layer` (GDN or gated attention by layer type),
+ * tokens at positions [pos_offset, pos_offset + n) of `slot`:
+ *   GDN:  forward_gdn_block semantics (reference gdn.mojo:897-1183) carried across
+ *         calls by the slot's conv window and recurrent state;
+ *   attn: forward_attention_qwen36 semantics (reference attention.mojo:219-435) with the
+ *         slot's paged KV cache (append contract above). */
+int32_t dm_mixer_block(dm_ctx* ctx, int32_t layer, int32_t slot, int32_t pos_offset,
+                       const float* x_host, int32_t n, float* x_mid_host);
+
+/* forward_port_block (reference src/layers/port_scheduler.mojo:286): mixer + residual +
+ * MoE + residual for one layer. */
+int32_t dm_block_forward(dm_ctx* ctx, int32_t layer, int32_t slot, int32_t pos_offset,
+                         const float* x_host, int32_t n, float* x_out_host);
+
+/* Macro scheduler over all layers for n tokens appended to `slot` at its current length
+ * (reference forward_port_macro_scheduler_gguf, gguf_port_loader.mojo:329, with the
+ * embedding gguf_embed_tokens :274, final norm + lm_head gguf_logits_from_hidden :291 and
+ * argmax_sample cmd_decode.mojo:115).  Tokens are processed one at a time through the
+ * captured decode graph.  logits_host [V] receives the logits of the last token (may be
+ * NULL); next_token receives their argmax (first maximum wins). */
+int32_t dm_forward(dm_ctx* ctx, int32_t slot, const int32_t* tokens_host, int32_t n,
+                   float* logits_host, int32_t* next_token);
+
+/* One decode step (the per-step call of reference cmd_decode.mojo:2014-2045): embeds
+ * token_in at the slot's current position, runs every block and the head, appends KV,
+ * advances the slot by one and returns the greedy next token (and logits if non-NULL). */
+int32_t dm_decode_step(dm_ctx* ctx, int32_t slot, int32_t token_in, int32_t* token_out,
+                       float* logits_host);
+
+/* Greedy generation: n_steps decode steps fed back on the device (no host round trip
+ * between steps); tokens_out_host [n_steps] receives the generated ids. */
+int32_t dm_generate(dm_ctx* ctx, int32_t slot, int32_t token_in, int32_t n_steps,
+                    int32_t* tokens_out_host);
+
+/* ---- device-resident entry points (for callers that keep data in HBM) ---------------- */
+/* Enqueues n_steps greedy decode steps for `slot` on the context stream with the input
+ * token already on the device (the token produced by the previous step, or the one set by
+ * dm_set_token); returns without synchronising. */
+int32_t dm_enqueue_decode(dm_ctx* ctx, int32_t slot, int32_t n_steps);
+int32_t dm_set_token(dm_ctx* ctx, int32_t slot, int32_t token);
+/* Waits for the context stream and returns the device error word as a status. */
+int32_t dm_sync(dm_ctx* ctx);
+/* The context's CUDA stream (cudaStream_t) for event timing by the caller. */
+int32_t dm_get_stream(dm_ctx* ctx, void** stream_out);
+/* Number of kernel launches one decode step performs (for launch accounting). */
+int32_t dm_kernels_per_step(dm_ctx* ctx, int32_t* out);
+
+/* Times `iters` back-to-back launches of one kernel kind of layer `layer` (inputs as left
+ * by the last step) with CUDA events on the context stream; avg_ms = mean launch time,
+ * bytes = the algorithmic HBM bytes one launch must move (weights, state, KV). */
+#define DM_KERNEL_MIXER_IN 0   /* GDN or attention input projection GEMV (+RMSNorm)     */
+#define DM_KERNEL_MIXER_OUT 1  /* output projection GEMV (+head norm / gate, residual)  */
+#define DM_KERNEL_MIXER_CORE 2 /* GDN recurrence or paged decode attention              */
+#define DM_KERNEL_ROUTER 3
+#define DM_KERNEL_MOE_UP 4
+#define DM_KERNEL_MOE_DOWN 5
+#define DM_KERNEL_HEAD 6
+int32_t dm_time_kernel(dm_ctx* ctx, int32_t which, int32_t layer, int32_t iters, float* avg_ms,
+                       uint64_t* bytes);
+
+/* ---- synthetic checkpoint (seeded; host and device generate the same distributions) --
+ * Counter-based generator: element i of stream `stream_id` under `seed` is a pure
+ * function of (seed, stream_id, i), so any subrange can be produced independently. */
+/* bf16 N(mean, std) */
+int32_t dm_synth_bf16(uint64_t seed, uint64_t stream_id, uint64_t n, float mean, float std,
+                      uint16_t* out_host);
+/* f32 N(mean, std) */
+int32_t dm_synth_f32(uint64_t seed, uint64_t stream_id, uint64_t n, float mean, float std,
+                     float* out_host);
+/* uniform bytes (two uniform nibbles per byte) */
+int32_t dm_synth_u8(uint64_t seed, uint64_t stream_id, uint64_t n, uint8_t* out_host);
+/* fp16 |N(0, std)| scales */
+int32_t dm_synth_f16_absnormal(uint64_t seed, uint64_t stream_id, uint64_t n, float std,
+                               uint16_t* out_host);
+/* Fills every weight of the context with the synthetic distributions of the benchmark
+ * configs directly on the device (same generator; used for multi-GB models). */
+int32_t dm_synth_model_device(dm_ctx* ctx, uint64_t seed);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DISMOEN_CUDA_H */

@@ -1,0 +1,86 @@
+"""CPU tests of the C-ABI library: it loads without a GPU, exports every symbol declared
+in include/dismoen_cuda.h, validates configs like reference ModelConfig, and its
+synthetic generator is deterministic.  No device compute is called here."""
+import ctypes as C
+import json
+import os
+import re
+
+import numpy as np
+import pytest
+
+from disk_streaming_moe_engine_b200 import _lib, preset
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "dismoen_cuda.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*int32_t\s+(dm_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    syms = declared_symbols()
+    assert len(syms) >= 30
+    for s in syms:
+        assert hasattr(lib, s), s
+        assert s in _lib.SIGNATURES, f"{s} missing from the ctypes binding"
+
+
+def test_abi_version(lib):
+    assert lib.dm_abi_version() == 1
+
+
+def _validate(lib, cfg):
+    buf = C.create_string_buffer(512)
+    rc = lib.dm_config_validate(C.byref(cfg.to_c()), buf, 512)
+    return rc, buf.value.decode()
+
+
+@pytest.mark.parametrize("name", ["mini", "layer", "full"])
+def test_presets_validate(lib, name):
+    rc, msg = _validate(lib, preset(name))
+    assert rc == 0, msg
+
+
+def test_config_errors_use_reference_json_shape(lib):
+    cfg = preset("mini")
+    cfg.num_experts_per_tok = 17
+    rc, msg = _validate(lib, cfg)
+    assert rc == _lib.DM_ERR_INVALID_ARG
+    err = json.loads(msg)
+    assert set(err) == {"error_type", "detail", "stage", "layer"}
+    assert err["error_type"] == "CONFIG_ERROR"
+    cfg = preset("mini")
+    cfg.norm_topk_prob = True
+    rc, msg = _validate(lib, cfg)
+    assert rc != 0 and json.loads(msg)["error_type"] == "ROUTER_ERROR"
+    cfg = preset("mini")
+    cfg.rms_norm_eps = 0.0
+    assert _validate(lib, cfg)[0] != 0
+    cfg = preset("mini")
+    cfg.num_key_value_heads = 3
+    assert _validate(lib, cfg)[0] != 0
+
+
+def test_synth_is_counter_based(lib):
+    a = np.empty(1000, np.uint16)
+    b = np.empty(400, np.uint16)
+    lib.dm_synth_bf16(5, 77, a.size, 0.0, 1.0, a.ctypes.data)
+    lib.dm_synth_bf16(5, 77, b.size, 0.0, 1.0, b.ctypes.data)
+    assert np.array_equal(a[:400], b)
+    f = (a.astype(np.uint32) << 16).view(np.float32)
+    assert abs(f.mean()) < 0.15 and 0.85 < f.std() < 1.15
+    u = np.empty(1 << 16, np.uint8)
+    lib.dm_synth_u8(5, 78, u.size, u.ctypes.data)
+    counts = np.bincount(u & 15, minlength=16)
+    assert counts.min() > 0.8 * counts.mean()
+    s = np.empty(4096, np.uint16)
+    lib.dm_synth_f16_absnormal(5, 79, s.size, 0.02, s.ctypes.data)
+    sf = s.view(np.float16).astype(np.float32)
+    assert (sf >= 0).all() and 0.012 < sf.mean() < 0.02
+
+
+def test_expert_bytes_match_baseline_figure():
+    # 4.3125 bits/weight: 1,695,744 B per full-shape expert (gate + up + down)
+    assert preset("full").expert_bytes() == 1695744
