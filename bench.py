@@ -59,6 +59,22 @@ def dist_env():
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
+# ---- multi-rank timing (one process per GPU) ---------------------------------------------
+def max_over_ranks(v: float, dist=None, device=None) -> float:
+    """Max of a per-rank time over all ranks (every rank takes part, in the same order)."""
+    if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64, device=device or "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def whole_job_rate(units_per_rank: int, world: int, max_ms: float) -> float:
+    """Units of all ranks / max-over-ranks elapsed time (weak scaling: fixed work per rank)."""
+    return world * units_per_rank / (max_ms / 1e3)
+
+
 # ---- per-step algorithmic bytes (bs1, config 2) ------------------------------------------
 def step_bytes(cfg, ctx_len: int) -> int:
     H, I, E, G = cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts, cfg.quant_group_size
@@ -228,12 +244,8 @@ def run_ours(args, rank, local, world):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
 
-    def max_over_ranks(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    def rank_max(v: float) -> float:
+        return max_over_ranks(v, dist, torch.device("cuda", local))
 
     def barrier():
         torch.cuda.synchronize()
@@ -266,9 +278,9 @@ def run_ours(args, rank, local, world):
         ev1.synchronize()
     eng.sync()
     barrier()
-    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms = rank_max(ev0.elapsed_time(ev1))
     ctx_mid = args.prompt_len + args.warmup + args.steps // 2
-    value = world * args.steps / (ms / 1e3)
+    value = whole_job_rate(args.steps, world, ms)
 
     # ---- e2e: through the C ABI with host buffers ----
     tok = int(nxt)
@@ -280,8 +292,8 @@ def run_ours(args, rank, local, world):
         ev1.record(stream)
         ev1.synchronize()
     barrier()
-    ms_e2e = max_over_ranks(ev0.elapsed_time(ev1))
-    e2e = world * args.steps / (ms_e2e / 1e3)
+    ms_e2e = rank_max(ev0.elapsed_time(ev1))
+    e2e = whole_job_rate(args.steps, world, ms_e2e)
 
     # ---- roofline of the dominant kernel and the per-kernel breakdown ----
     peak, peak_kind = measured_peak()

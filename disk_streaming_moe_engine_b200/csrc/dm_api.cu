@@ -393,12 +393,14 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     const int nsplit = attn_nsplit(c->num_sms, c->d.Hkv);
     const int cap = attn_scores_cap(c->d.max_pages, nsplit);
     const int score_smem = (c->d.Hq / c->d.Hkv) * cap * 4;
-    if (score_smem > 160 * 1024) {
+    if (score_smem > kAttnMaxScoreSmem) {
         fprintf(stderr, "dm_ctx_create: max_pages_per_seq too large for the decode attention kernel\n");
         delete c;
         return DM_ERR_INVALID_ARG;
     }
-    if (e == cudaSuccess) e = attn_set_attrs(std::max(score_smem, 1024));
+    // function attributes are per process: always the kernel's fixed maximum, never a
+    // per-context value that a later, smaller context would lower
+    if (e == cudaSuccess) e = attn_set_attrs(kAttnMaxScoreSmem);
     if (e != cudaSuccess) {
         fprintf(stderr, "dm_ctx_create: %s\n", cudaGetErrorString(e));
         delete c;

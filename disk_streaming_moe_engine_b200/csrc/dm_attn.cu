@@ -76,6 +76,10 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     const int pos = *a.pos;
     const int n_tok = pos + 1;
     const int capacity = a.max_pages * kPageTokens;
+    if (pos < 0 || pos >= capacity) {  // no room: report, touch nothing (the score buffer
+        if (tid == 0 && s == 0) raise_error(a.err, DM_DEVERR_CAPACITY);  // is sized for capacity)
+        return;
+    }
 
     // ---- q heads of this KV group, new k, new v ----
     for (int hh = warp; hh < GRP; hh += 4)
@@ -102,11 +106,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
 
     // ---- append at pos (one CTA per KV head) ----
     if (s == 0) {
-        const int pidx = pos / kPageTokens;
-        const int page = (pos >= 0 && pos < capacity) ? a.page_table[pidx] : -1;
-        if (pos < 0 || pos >= capacity) {
-            if (tid == 0) raise_error(a.err, DM_DEVERR_CAPACITY);
-        } else if (page < 0 || page >= a.num_pages) {
+        const int page = a.page_table[pos / kPageTokens];
+        if (page < 0 || page >= a.num_pages) {
             if (tid == 0) raise_error(a.err, DM_DEVERR_PAGE);
         } else {
             uint16_t* kd = a.kv + ((static_cast<size_t>(page) * 2 + 0) * a.Hkv + g) * kPageTokens * D +

@@ -31,6 +31,7 @@ constexpr int kConvRing = 4;       // ring slots for the causal conv window (ker
 constexpr int kMaxTopK = 16;
 constexpr int kMaxSplits = 64;     // split-K partitions of decode attention
 constexpr int kGemvRowsPerStage = 4;
+constexpr int kAttnMaxScoreSmem = 160 * 1024;  // dynamic smem bound of the decode attention
 
 struct Dims {
     int H, L, interval, V;

@@ -147,6 +147,11 @@ __global__ void __launch_bounds__(256) router_kernel(const __grid_constant__ Rou
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
         if (lane == 0) {
+            if (bi < 0 || bi >= E) {  // only when probabilities are NaN: keep ids in range
+                raise_error(a.err, DM_DEVERR_NONFINITE);
+                bi = r;
+                bv = 0.0f;
+            }
             a.ids[r] = bi;
             a.probs[r] = bv;
             pe[bi] = -2.0f;
@@ -268,7 +273,7 @@ struct MoeArgs {
     const uint8_t* experts;   // layer base: [E] records
     const uint8_t* shared;    // shared expert record
     int64_t expert_bytes, gu_part_bytes;
-    int gu_chunks, d_chunks, topk, I, H;
+    int gu_chunks, d_chunks, topk, I, H, E;
     const int* ids;
     const float* probs;
     const float* shared_g;
@@ -287,7 +292,7 @@ __global__ void __launch_bounds__(128) moe_up_kernel(const __grid_constant__ Moe
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
     for (int k = threadIdx.x; k < K; k += 128) x4_store<K>(x4, k, a.xn[k]);
-    if (threadIdx.x < a.topk) sid[threadIdx.x] = a.ids[threadIdx.x];
+    if (threadIdx.x < a.topk) sid[threadIdx.x] = min(max(a.ids[threadIdx.x], 0), a.E - 1);
     __syncthreads();
     pdl_launch_dependents();
     const float4* x4v = reinterpret_cast<const float4*>(x4);
@@ -334,7 +339,7 @@ __global__ void __launch_bounds__(128) moe_down_kernel(const __grid_constant__ M
         x4_store<KI>(hs + j * KI, k, a.h[t]);
     }
     if (threadIdx.x < a.topk) {
-        sid[threadIdx.x] = a.ids[threadIdx.x];
+        sid[threadIdx.x] = min(max(a.ids[threadIdx.x], 0), a.E - 1);
         sp[threadIdx.x] = a.probs[threadIdx.x];
     }
     if (threadIdx.x == 0) sp[a.topk] = *a.shared_g;
@@ -386,6 +391,7 @@ static MoeArgs moe_args(const Dims& d, const LayerW& w, const Buffers& b) {
     a.topk = d.topk;
     a.I = d.I;
     a.H = d.H;
+    a.E = d.E;
     a.ids = b.topk_ids;
     a.probs = b.topk_p;
     a.shared_g = b.shared_g;
