@@ -67,6 +67,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     __shared__ __align__(16) float knew[D], vnew[D];
     __shared__ uint16_t kbits[D], vbits[D];
     __shared__ float hm[GRP], hl[GRP];
+    __shared__ float wsp[GRP][kMaxSplits];
     __shared__ int is_last;
     extern __shared__ float scores[];  // [GRP][cap]
     const int g = blockIdx.x, s = blockIdx.y;
@@ -225,30 +226,46 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     __threadfence();
 
     // ---- merge the splits of every head of this group, apply the output gate ----
+    // per-split weights w_s = exp(m_s - M) / L once per head, then every output element
+    // is an independent, coalesced sum over the splits.
     const int ns = gridDim.y;
     for (int hh = warp; hh < GRP; hh += 4) {
-        const int hq = g * GRP + hh;
-        const float* ph = a.part + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
+        const float* ph = a.part + static_cast<size_t>(g * GRP + hh) * kMaxSplits * (D + 2);
+        float ml[2], ll[2];
         float M = -INFINITY;
-        for (int sp = 0; sp < ns; ++sp) {
-            const float l = __ldcg(ph + sp * (D + 2) + D + 1);
-            if (l > 0.0f) M = fmaxf(M, __ldcg(ph + sp * (D + 2) + D));
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int sp = lane + 32 * k;
+            ml[k] = sp < ns ? __ldcg(ph + sp * (D + 2) + D) : -INFINITY;
+            ll[k] = sp < ns ? __ldcg(ph + sp * (D + 2) + D + 1) : 0.0f;
+            if (ll[k] > 0.0f) M = fmaxf(M, ml[k]);
         }
-        float L = 0.0f;
-        for (int sp = 0; sp < ns; ++sp) {
-            const float l = __ldcg(ph + sp * (D + 2) + D + 1);
-            if (l > 0.0f) L += expf(__ldcg(ph + sp * (D + 2) + D) - M) * l;
+        M = warp_max(M);
+        float wk[2], L = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            wk[k] = ll[k] > 0.0f ? expf(ml[k] - M) : 0.0f;
+            L += wk[k] * ll[k];
         }
+        L = warp_sum(L);
         const float invL = 1.0f / L;
-        for (int d = lane; d < D; d += 32) {
-            float acc = 0.0f;
-            for (int sp = 0; sp < ns; ++sp) {
-                const float l = __ldcg(ph + sp * (D + 2) + D + 1);
-                if (l > 0.0f) acc += expf(__ldcg(ph + sp * (D + 2) + D) - M) * __ldcg(ph + sp * (D + 2) + d);
-            }
-            const float gate = a.qg[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
-            a.out[static_cast<size_t>(hq) * D + d] = acc * invL * sigmoid_f(gate);
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+            if (lane + 32 * k < kMaxSplits) wsp[hh][lane + 32 * k] = wk[k] * invL;
+    }
+    __syncthreads();
+    for (int o = tid; o < GRP * D; o += 128) {
+        const int hh = o / D, d = o % D;
+        const int hq = g * GRP + hh;
+        const float* ph = a.part + static_cast<size_t>(hq) * kMaxSplits * (D + 2) + d;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int sp = 0; sp < ns; ++sp) {
+            const float w = wsp[hh][sp];
+            if (w != 0.0f) acc = fmaf(w, __ldcg(ph + static_cast<size_t>(sp) * (D + 2)), acc);
         }
+        const float gate = a.qg[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
+        a.out[static_cast<size_t>(hq) * D + d] = acc * sigmoid_f(gate);
     }
     if (tid == 0) a.counters[g] = 0u;
 }

@@ -222,10 +222,31 @@ __device__ __forceinline__ float nib(uint32_t word_masked, int b) {
     return __uint_as_float(__byte_perm(word_masked, 0x4B000000u, 0x7540u | b));
 }
 
-// Partial dot of one row of a chunk for the lane's vectors (v = vl + LPR * i).
+template <int LPR>
+__device__ __forceinline__ float lane_group_sum(float v) {
+#pragma unroll
+    for (int m = LPR / 2; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+    return v;
+}
+
+struct MoeArgs {
+    const uint8_t* experts;   // layer base: [E] records
+    const uint8_t* shared;    // shared expert record
+    int64_t expert_bytes, gu_part_bytes;
+    int gu_chunks, d_chunks, topk, I, H, E, slots;
+    const int* ids;
+    const float* probs;
+    const float* shared_g;
+    const float* xn;          // [H] normalised MoE input
+    float* h;                 // [(topk+1)][I]
+    const float* x_res;       // [H]
+    float* x_out;             // [H]
+    uint32_t* err;
+};
+
+// Partial dot of row r of a chunk staged in shared memory.
 template <int K, int G>
-__device__ __forceinline__ float q4_partial(const uint8_t* __restrict__ chunk, int r, int vl,
-                                            const float4* __restrict__ x4) {
+__device__ __forceinline__ float q4_partial_smem(const uint8_t* chunk, int r, int vl, const float4* x4) {
     using Q = Q4<K, G>;
     const uint8_t* qrow = chunk + r * (K / 2);
     const uint16_t* srow = reinterpret_cast<const uint16_t*>(chunk + Q::S_OFF) + r * (K / G);
@@ -235,9 +256,9 @@ __device__ __forceinline__ float q4_partial(const uint8_t* __restrict__ chunk, i
     for (int i = 0; i < Q::VPL; ++i) {
         const int v = vl + Q::LPR * i;
         const int g = (v * 32) / G;
-        const uint4 q = ldg_nc_v4(qrow + 16 * v);
-        const float s = __half2float(__ushort_as_half(__ldg(srow + g)));
-        const uint32_t zb = __ldg(zrow + (g >> 1));
+        const uint4 q = *reinterpret_cast<const uint4*>(qrow + 16 * v);
+        const float s = __half2float(__ushort_as_half(srow[g]));
+        const uint32_t zb = zrow[g >> 1];
         const uint32_t z = (g & 1) ? (zb >> 4) : (zb & 15u);
         const float fz = __uint_as_float(0x4B000000u | z);
         const uint32_t words[4] = {q.x, q.y, q.z, q.w};
@@ -262,122 +283,171 @@ __device__ __forceinline__ float q4_partial(const uint8_t* __restrict__ chunk, i
     return acc;
 }
 
-template <int LPR>
-__device__ __forceinline__ float lane_group_sum(float v) {
-#pragma unroll
-    for (int m = LPR / 2; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
-    return v;
-}
+constexpr int kMoeMaxSlots = 16;   // chunk slots (mbarriers) per CTA
 
-struct MoeArgs {
-    const uint8_t* experts;   // layer base: [E] records
-    const uint8_t* shared;    // shared expert record
-    int64_t expert_bytes, gu_part_bytes;
-    int gu_chunks, d_chunks, topk, I, H, E;
-    const int* ids;
-    const float* probs;
-    const float* shared_g;
-    const float* xn;          // [H] normalised MoE input
-    float* h;                 // [(topk+1)][I]
-    const float* x_res;       // [H]
-    float* x_out;             // [H]
-};
-
+// Gate/up projections of the k routed experts and the shared expert.  Work item =
+// (expert slot j, 8 output rows c): one 16-row chunk (8 gate + 8 up rows).  CTA b owns a
+// contiguous item range; thread 0 bulk-copies every chunk of the range into shared memory
+// at once (the shared expert's before griddepcontrol.wait: it does not depend on the
+// router), then 8 warps each reduce one (gate, up) row pair per chunk.
 template <int K, int G>
-__global__ void __launch_bounds__(128) moe_up_kernel(const __grid_constant__ MoeArgs a) {
+__global__ void __launch_bounds__(256) moe_up_kernel(const __grid_constant__ MoeArgs a) {
     using Q = Q4<K, G>;
-    __shared__ __align__(16) float x4[K];
+    extern __shared__ __align__(128) uint8_t dsm[];     // [slots][CHUNK] then x4[K]
+    __shared__ __align__(8) uint64_t bar[kMoeMaxSlots];
     __shared__ int sid[kMaxTopK];
-    __shared__ float dots[4][4];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_items = (a.topk + 1) * a.gu_chunks;
+    const int i0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * n_items / gridDim.x);
+    const int i1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * n_items / gridDim.x);
+    const int nloc = i1 - i0;
+    float* x4 = reinterpret_cast<float*>(dsm + static_cast<size_t>(a.slots) * Q::CHUNK);
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < nloc; ++k) mbar_init(&bar[k], 1);
+        mbar_fence_init();
+        for (int k = 0; k < nloc; ++k) {  // shared-expert chunks first, no dependency
+            const int item = i0 + k;
+            if (item / a.gu_chunks != a.topk) continue;
+            mbar_arrive_expect_tx(&bar[k], Q::CHUNK);
+            bulk_g2s(dsm + static_cast<size_t>(k) * Q::CHUNK,
+                     a.shared + static_cast<int64_t>(item % a.gu_chunks) * Q::CHUNK, Q::CHUNK, &bar[k]);
+        }
+    }
     pdl_wait();
-    for (int k = threadIdx.x; k < K; k += 128) x4_store<K>(x4, k, a.xn[k]);
     if (threadIdx.x < a.topk) sid[threadIdx.x] = min(max(a.ids[threadIdx.x], 0), a.E - 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 0; k < nloc; ++k) {
+            const int item = i0 + k;
+            const int j = item / a.gu_chunks;
+            if (j == a.topk) continue;
+            mbar_arrive_expect_tx(&bar[k], Q::CHUNK);
+            bulk_g2s(dsm + static_cast<size_t>(k) * Q::CHUNK,
+                     a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes +
+                         static_cast<int64_t>(item % a.gu_chunks) * Q::CHUNK,
+                     Q::CHUNK, &bar[k]);
+        }
+    }
+    for (int k = threadIdx.x; k < K; k += 256) x4_store<K>(x4, k, a.xn[k]);
     __syncthreads();
     pdl_launch_dependents();
     const float4* x4v = reinterpret_cast<const float4*>(x4);
 
-    const int n_items = (a.topk + 1) * a.gu_chunks;
-    const int i0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * n_items / gridDim.x);
-    const int i1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * n_items / gridDim.x);
-    for (int item = i0; item < i1; ++item) {
+    for (int k = 0; k < nloc; ++k) {
+        const int item = i0 + k;
         const int j = item / a.gu_chunks, c = item % a.gu_chunks;
-        const uint8_t* rec = (j < a.topk) ? a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes
-                                          : a.shared;
-        const uint8_t* chunk = rec + static_cast<int64_t>(c) * Q::CHUNK;
-        // warp rows in the chunk: gate 2w, 2w+1 and up 8+2w, 8+2w+1
-        const int myrows[4] = {2 * warp, 2 * warp + 1, 8 + 2 * warp, 9 + 2 * warp};
+        const bool ok = mbar_wait_bounded(&bar[k], 0, a.err, nullptr);
+        const uint8_t* chunk = dsm + static_cast<size_t>(k) * Q::CHUNK;
+        // warp w: gate row w and up row 8 + w of the chunk (output row 8c + w)
+        float dots[2];
 #pragma unroll
-        for (int p = 0; p < 4; p += Q::RPP) {
+        for (int p = 0; p < 2; p += Q::RPP) {
             const int sub = lane / Q::LPR, vl = lane % Q::LPR;
             const int ri = p + sub;
             float v = 0.0f;
-            if (ri < 4) v = q4_partial<K, G>(chunk, myrows[ri], vl, x4v);
+            if (ri < 2 && ok) v = q4_partial_smem<K, G>(chunk, ri == 0 ? warp : 8 + warp, vl, x4v);
             v = lane_group_sum<Q::LPR>(v);
-            if (vl == 0 && ri < 4) dots[warp][ri] = v;
+            if (Q::RPP == 1) dots[p] = v;
+            else {  // lanes of row ri hold its sum; move the up-row sum to row 0's lanes
+                const float other = __shfl_sync(0xffffffffu, v, Q::LPR);
+                dots[0] = __shfl_sync(0xffffffffu, v, 0);
+                dots[1] = other;
+            }
         }
-        __syncwarp();
-        if (lane < 2) {
-            const float g = dots[warp][lane], u = dots[warp][2 + lane];
-            a.h[j * a.I + 8 * c + 2 * warp + lane] = silu_f(g) * u;
-        }
-        __syncwarp();
+        if (lane == 0) a.h[j * a.I + 8 * c + warp] = silu_f(dots[0]) * dots[1];
     }
 }
 
+// Down projection of every selected expert for one 16-row output chunk per CTA, weighted
+// by the router probability (shared expert: sigmoid gate), plus the residual.
 template <int KI, int G>
-__global__ void __launch_bounds__(128) moe_down_kernel(const __grid_constant__ MoeArgs a) {
+__global__ void __launch_bounds__(256) moe_down_kernel(const __grid_constant__ MoeArgs a) {
     using Q = Q4<KI, G>;
-    extern __shared__ __align__(16) float hs[];  // (topk+1) x4 vectors of length KI
+    extern __shared__ __align__(128) uint8_t dsm[];  // [(topk+1)][CHUNK] then h x4 [(topk+1)][KI]
+    __shared__ __align__(8) uint64_t bar[kMaxTopK + 1];
     __shared__ int sid[kMaxTopK];
     __shared__ float sp[kMaxTopK + 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_wait();
     const int nexp = a.topk + 1;
-    for (int t = threadIdx.x; t < nexp * KI; t += 128) {
-        const int j = t / KI, k = t % KI;
-        x4_store<KI>(hs + j * KI, k, a.h[t]);
+    const int c = blockIdx.x;
+    float* hs = reinterpret_cast<float*>(dsm + static_cast<size_t>(nexp) * Q::CHUNK);
+    if (threadIdx.x == 0) {
+        for (int j = 0; j < nexp; ++j) mbar_init(&bar[j], 1);
+        mbar_fence_init();
+        mbar_arrive_expect_tx(&bar[a.topk], Q::CHUNK);
+        bulk_g2s(dsm + static_cast<size_t>(a.topk) * Q::CHUNK,
+                 a.shared + a.gu_part_bytes + static_cast<int64_t>(c) * Q::CHUNK, Q::CHUNK, &bar[a.topk]);
     }
+    pdl_wait();
     if (threadIdx.x < a.topk) {
         sid[threadIdx.x] = min(max(a.ids[threadIdx.x], 0), a.E - 1);
         sp[threadIdx.x] = a.probs[threadIdx.x];
     }
     if (threadIdx.x == 0) sp[a.topk] = *a.shared_g;
     __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int j = 0; j < a.topk; ++j) {
+            mbar_arrive_expect_tx(&bar[j], Q::CHUNK);
+            bulk_g2s(dsm + static_cast<size_t>(j) * Q::CHUNK,
+                     a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes + a.gu_part_bytes +
+                         static_cast<int64_t>(c) * Q::CHUNK,
+                     Q::CHUNK, &bar[j]);
+        }
+    }
+    for (int t = threadIdx.x; t < nexp * KI; t += 256) {
+        const int j = t / KI, k = t % KI;
+        x4_store<KI>(hs + j * KI, k, a.h[t]);
+    }
+    __syncthreads();
     pdl_launch_dependents();
 
-    const int c = blockIdx.x;  // 16-row output chunk
+    // warp w: output rows 2w, 2w+1 of the chunk
+    const int sub = lane / Q::LPR, vl = lane % Q::LPR;
+    float routed[2] = {0.0f, 0.0f}, shared_v[2] = {0.0f, 0.0f};
+    for (int j = 0; j < nexp; ++j) {
+        const bool ok = mbar_wait_bounded(&bar[j], 0, a.err, nullptr);
+        const uint8_t* chunk = dsm + static_cast<size_t>(j) * Q::CHUNK;
+        const float4* hv = reinterpret_cast<const float4*>(hs + j * KI);
 #pragma unroll
-    for (int p = 0; p < 4; p += Q::RPP) {
-        const int sub = lane / Q::LPR, vl = lane % Q::LPR;
-        const int ri = p + sub;
-        const int r = 4 * warp + (ri < 4 ? ri : 0);
-        float routed = 0.0f, shared_v = 0.0f;
-        for (int j = 0; j < nexp; ++j) {
-            const uint8_t* rec = (j < a.topk) ? a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes
-                                              : a.shared;
-            const uint8_t* chunk = rec + a.gu_part_bytes + static_cast<int64_t>(c) * Q::CHUNK;
-            float v = q4_partial<KI, G>(chunk, r, vl, reinterpret_cast<const float4*>(hs + j * KI));
+        for (int p = 0; p < 2; p += Q::RPP) {
+            const int ri = p + sub;
+            float v = 0.0f;
+            if (ri < 2 && ok) v = q4_partial_smem<KI, G>(chunk, 2 * warp + ri, vl, hv);
             v = lane_group_sum<Q::LPR>(v);
-            if (j < a.topk) routed = fmaf(sp[j], v, routed);
-            else shared_v = v;
+            if (ri < 2) {
+                if (j < a.topk) routed[ri & 1] = fmaf(sp[j], v, routed[ri & 1]);
+                else shared_v[ri & 1] = v;
+            }
         }
-        if (vl == 0 && ri < 4) {
-            const int orow = 16 * c + r;
-            a.x_out[orow] = (routed + sp[a.topk] * shared_v) + a.x_res[orow];
+    }
+    if (vl == 0) {
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            const int ri = (Q::RPP == 1) ? p : sub;
+            if (Q::RPP != 1 && p > 0) break;
+            if (ri >= 2) continue;
+            const int orow = 16 * c + 2 * warp + ri;
+            a.x_out[orow] = (routed[ri & 1] + sp[a.topk] * shared_v[ri & 1]) + a.x_res[orow];
         }
     }
 }
 
 template <int K, int KI, int G>
-static cudaError_t launch_moe_t(const LaunchCfg& lc, const MoeArgs& a, bool up) {
+static cudaError_t launch_moe_t(const LaunchCfg& lc, const MoeArgs& a0, bool up) {
+    MoeArgs a = a0;
     if (up) {
         const int n_items = (a.topk + 1) * a.gu_chunks;
-        const int grid = n_items < lc.num_sms ? n_items : lc.num_sms;
-        return launch_kernel(lc, moe_up_kernel<K, G>, dim3(grid), dim3(128), 0, a);
+        int grid = n_items < lc.num_sms ? n_items : lc.num_sms;
+        a.slots = (n_items + grid - 1) / grid;
+        if (a.slots > kMoeMaxSlots) {
+            grid = (n_items + kMoeMaxSlots - 1) / kMoeMaxSlots;
+            a.slots = (n_items + grid - 1) / grid;
+        }
+        const size_t smem = static_cast<size_t>(a.slots) * Q4<K, G>::CHUNK + K * sizeof(float);
+        return launch_kernel(lc, moe_up_kernel<K, G>, dim3(grid), dim3(256), smem, a);
     }
-    const size_t smem = static_cast<size_t>(a.topk + 1) * KI * sizeof(float);
-    return launch_kernel(lc, moe_down_kernel<KI, G>, dim3(a.d_chunks), dim3(128), smem, a);
+    const size_t smem = static_cast<size_t>(a.topk + 1) * (Q4<KI, G>::CHUNK + KI * sizeof(float));
+    return launch_kernel(lc, moe_down_kernel<KI, G>, dim3(a.d_chunks), dim3(256), smem, a);
 }
 
 static MoeArgs moe_args(const Dims& d, const LayerW& w, const Buffers& b) {
@@ -397,6 +467,7 @@ static MoeArgs moe_args(const Dims& d, const LayerW& w, const Buffers& b) {
     a.shared_g = b.shared_g;
     a.xn = b.xn;
     a.h = b.h;
+    a.err = b.err;
     return a;
 }
 
@@ -415,16 +486,22 @@ bool moe_supported(int H, int I, int G) {
                        (H == 2048 && I == 256) || (H == 4096 && I == 512));
 }
 
+#define DM_MOE_INSTANCES(X) X(2048, 512) X(256, 128) X(1024, 256) X(2048, 256) X(4096, 512)
+
 cudaError_t moe_set_attrs() {
-    cudaError_t e;
-    if ((e = cudaFuncSetAttribute(moe_down_kernel<512, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (kMaxTopK + 1) * 512 * 4)) != cudaSuccess)
-        return e;
-    if ((e = cudaFuncSetAttribute(moe_down_kernel<256, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (kMaxTopK + 1) * 256 * 4)) != cudaSuccess)
-        return e;
-    return cudaFuncSetAttribute(moe_down_kernel<128, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (kMaxTopK + 1) * 128 * 4);
+    cudaError_t e = cudaSuccess;
+#define DM_MOE_ATTR(KK, II)                                                                           \
+    if (e == cudaSuccess)                                                                             \
+        e = cudaFuncSetAttribute(moe_up_kernel<KK, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                 kMoeMaxSlots * Q4<KK, 64>::CHUNK + KK * 4 > 200 * 1024                \
+                                     ? 200 * 1024                                                     \
+                                     : kMoeMaxSlots * Q4<KK, 64>::CHUNK + KK * 4);                    \
+    if (e == cudaSuccess)                                                                             \
+        e = cudaFuncSetAttribute(moe_down_kernel<II, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 (kMaxTopK + 1) * (Q4<II, 64>::CHUNK + II * 4));
+    DM_MOE_INSTANCES(DM_MOE_ATTR)
+#undef DM_MOE_ATTR
+    return e;
 }
 
 cudaError_t launch_moe_up(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b) {

@@ -1,0 +1,57 @@
+"""Times one decode-step kernel in isolation (CUDA events on the library stream).
+
+    python -m disk_streaming_moe_engine_b200.kernel_bench --preset layer --kernel in_proj \
+        --layer 0 --iters 20
+
+The model is synthesised on the device; with --warm the layer first runs one real token
+(so router ids, activations and the KV position are those of a real step).  Prints one
+JSON line: mean microseconds per launch, algorithmic bytes per launch and GB/s.  This is
+the small-case driver for ncu captures of a single kernel.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+
+from . import _lib
+from .config import RuntimeConfig, preset
+from .engine import Engine
+
+KERNELS = {"in_proj": _lib.DM_KERNEL_MIXER_IN, "out_proj": _lib.DM_KERNEL_MIXER_OUT,
+           "core": _lib.DM_KERNEL_MIXER_CORE, "router": _lib.DM_KERNEL_ROUTER, "moe_up": _lib.DM_KERNEL_MOE_UP,
+           "moe_down": _lib.DM_KERNEL_MOE_DOWN, "head": _lib.DM_KERNEL_HEAD}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--preset", default="layer")
+    ap.add_argument("--kernel", default="in_proj", choices=sorted(KERNELS))
+    ap.add_argument("--layer", type=int, default=0)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--ctx", type=int, default=0, help="tokens already in the KV cache / GDN state")
+    ap.add_argument("--warm", action="store_true")
+    ap.add_argument("--seed", type=int, default=1)
+    a = ap.parse_args()
+    cfg = preset(a.preset)
+    with Engine(cfg, RuntimeConfig.for_context(a.ctx + 64)) as eng:
+        eng.synth_on_device(a.seed)
+        eng.seq_reset(0)
+        if a.ctx:
+            n_att = cfg.num_attention_layers()
+            rng = np.random.default_rng(a.seed)
+            k = rng.integers(0x3000, 0x3F80, (a.ctx, cfg.num_key_value_heads, cfg.head_dim), dtype=np.uint16)
+            for att in range(n_att):
+                eng.kv_import(att, 0, k, k[::-1].copy())
+            eng.seq_set_len(0, a.ctx)
+        if a.warm:
+            x = np.random.default_rng(a.seed).standard_normal((1, cfg.hidden_size)).astype(np.float32)
+            eng.forward_port_block(x, a.layer, a.ctx)
+        us_ms, nbytes = eng.time_kernel(KERNELS[a.kernel], a.layer, a.iters)
+    print(json.dumps({"kernel": a.kernel, "preset": a.preset, "layer": a.layer, "ctx": a.ctx,
+                      "us": us_ms * 1e3, "bytes": nbytes, "GBps": nbytes / us_ms / 1e6}))
+
+
+if __name__ == "__main__":
+    main()
