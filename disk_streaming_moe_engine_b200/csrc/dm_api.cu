@@ -390,6 +390,7 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = gemv_set_attrs();
     if (e == cudaSuccess) e = moe_set_attrs();
+    if (e == cudaSuccess) e = router_set_attrs();
     const int nsplit = attn_nsplit(c->num_sms, c->d.Hkv);
     const int cap = attn_scores_cap(c->d.max_pages, nsplit);
     const int score_smem = (c->d.Hq / c->d.Hkv) * cap * 4;

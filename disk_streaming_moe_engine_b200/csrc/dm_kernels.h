@@ -51,6 +51,7 @@ cudaError_t launch_gemv(const LaunchCfg& lc, int K, int pro, const GemvArgs& a);
 bool gemv_supported_k(int K);
 cudaError_t gemv_set_attrs();
 cudaError_t moe_set_attrs();
+cudaError_t router_set_attrs();
 cudaError_t attn_set_attrs(int max_scores_smem);
 
 // Launch with the programmatic-stream-serialization attribute when lc.pdl is set, so the

@@ -15,6 +15,7 @@
 // 4-bit dot product: with F(n) = bits(0x4B000000 | n) = 2^23 + n, F(q) - F(z) = q - z is
 // exact, so each weight costs one byte-permute, one subtract and one fma; the group scale
 // multiplies the 32-weight partial sum once.
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 #include "dismoen_cuda.h"
@@ -31,68 +32,94 @@ struct RouterArgs {
     const uint16_t* gamma;  // post-attention norm (nullptr: x already normalised)
     float eps;
     float* xn_out;          // normalised activation for the experts (written by CTA 0)
-    float* logits;          // [E+1]
     int* ids;
     float* probs;
     float* shared_g;
-    unsigned* counter;
     uint32_t* err;
 };
+
+constexpr int kRouterCluster = 16;   // CTAs of the router cluster (non-portable size)
+constexpr int kRouterThreads = 512;
 
 __device__ __forceinline__ void xs_store_split(float* xs, int K, int k, float v) {
     int j = k >> 3, e = k & 7;
     xs[(e < 4 ? 0 : K / 2) + j * 4 + (e & 3)] = v;
 }
 
+// Router as one thread-block cluster.  CTA r of the cluster owns rows r*R .. r*R+R-1 of
+// [W_router; w_shared_gate] (R = ceil((E+1)/16)), holds their weights in registers from
+// before griddepcontrol.wait, normalises x itself, and stores its logits straight into
+// CTA 0's shared memory (distributed shared memory); after one cluster barrier CTA 0
+// computes the softmax and the top-k.  No global round trip between the two phases.
+//
+// Canonical reduction orders (restated by the CPU oracle for bit-exact ids):
+//   RMSNorm: 512 threads, thread t: fma-accumulate x[k]^2 for k = t, t+512, ...; warp
+//            butterfly (xor 16..1); the 16 warp sums added in warp order; denom =
+//            sqrt(ss / K + eps); y = (x / denom) * gamma.
+//   dot:     lane l: fma over elements 8(l + 32i) + j, i then j ascending; butterfly.
+//   softmax: m = max; e = det_exp(z - m); lane l sums e[l], e[l+32], ... in order;
+//            butterfly; p = e * (1 / sum).  Top-k: max p, ties to the lower id.
 template <int K>
-__global__ void __launch_bounds__(256) router_kernel(const __grid_constant__ RouterArgs a) {
+__global__ void __launch_bounds__(kRouterThreads, 2) router_kernel(const __grid_constant__ RouterArgs a) {
+    constexpr int VPL = K / 256;
     __shared__ __align__(16) float xs[K];
-    __shared__ float red4[4];
-    __shared__ int is_last;
-    __shared__ float pe[1024];
+    __shared__ float red[kRouterThreads / 32];
+    __shared__ float lg[1024];                      // logits, used in CTA 0 only
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = static_cast<int>(cluster.block_rank());
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-    const int row = blockIdx.x * 8 + warp;
     const int nrows = a.E + 1;
+    const int R = (nrows + kRouterCluster - 1) / kRouterCluster;
+    const int r0 = rank * R, r1 = min(nrows, r0 + R);
 
-    // weights do not depend on the previous kernel: load them first
-    uint4 wreg[K / 256];
-    if (row < nrows) {
+    uint4 wreg[VPL];
+    int row = r0 + warp;
+    if (row < r1) {
         const uint4* wr = reinterpret_cast<const uint4*>(a.W + static_cast<size_t>(row) * K);
 #pragma unroll
-        for (int i = 0; i < K / 256; ++i) wreg[i] = ldg_nc_v4(wr + lane + 32 * i);
+        for (int i = 0; i < VPL; ++i) wreg[i] = ldg_nc_v4(wr + lane + 32 * i);
     }
     pdl_wait();
     if (a.gamma) {
-        if (tid < 128) {
-            float acc = 0.0f;
-            for (int k = tid; k < K; k += 128) acc = __fmaf_rn(a.x[k], a.x[k], acc);
-            acc = warp_sum(acc);
-            if (lane == 0) red4[warp] = acc;
-            named_bar_sync(1, 128);
-            const float ss = __fadd_rn(__fadd_rn(__fadd_rn(red4[0], red4[1]), red4[2]), red4[3]);
-            const float denom = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), a.eps));
-            for (int k = tid; k < K; k += 128) {
-                const float y = __fmul_rn(__fdiv_rn(a.x[k], denom), bf16_to_f32(a.gamma[k]));
-                xs_store_split(xs, K, k, y);
-                if (blockIdx.x == 0) a.xn_out[k] = y;
-            }
+        float xv[(K + kRouterThreads - 1) / kRouterThreads];
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i * kRouterThreads + tid < K; ++i) {
+            xv[i] = a.x[i * kRouterThreads + tid];
+            acc = __fmaf_rn(xv[i], xv[i], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) red[warp] = acc;
+        __syncthreads();
+        float ss = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kRouterThreads / 32; ++w) ss = __fadd_rn(ss, red[w]);
+        const float denom = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), a.eps));
+#pragma unroll
+        for (int i = 0; i * kRouterThreads + tid < K; ++i) {
+            const int k = i * kRouterThreads + tid;
+            const float y = __fmul_rn(__fdiv_rn(xv[i], denom), bf16_to_f32(a.gamma[k]));
+            xs_store_split(xs, K, k, y);
+            if (rank == 0) a.xn_out[k] = y;
         }
     } else {
-        for (int k = tid; k < K; k += 256) {
-            xs_store_split(xs, K, k, a.x[k]);
-            if (blockIdx.x == 0) a.xn_out[k] = a.x[k];
+        for (int k = tid; k < K; k += kRouterThreads) {
+            const float v = a.x[k];
+            xs_store_split(xs, K, k, v);
+            if (rank == 0) a.xn_out[k] = v;
         }
     }
     __syncthreads();
     pdl_launch_dependents();
 
-    if (row < nrows) {
-        // canonical order: one accumulator per lane, elements 8(lane+32i)+j, i then j
-        const float4* xlo = reinterpret_cast<const float4*>(xs);
-        const float4* xhi = reinterpret_cast<const float4*>(xs + K / 2);
+    float* lg0 = cluster.map_shared_rank(lg, 0);
+    const float4* xlo = reinterpret_cast<const float4*>(xs);
+    const float4* xhi = reinterpret_cast<const float4*>(xs + K / 2);
+    while (row < r1) {
         float acc = 0.0f;
 #pragma unroll
-        for (int i = 0; i < K / 256; ++i) {
+        for (int i = 0; i < VPL; ++i) {
             const int j = lane + 32 * i;
             const uint4 w = wreg[i];
             const float4 x0 = xlo[j], x1 = xhi[j];
@@ -106,26 +133,26 @@ __global__ void __launch_bounds__(256) router_kernel(const __grid_constant__ Rou
             acc = __fmaf_rn(bf16hi(w.w), x1.w, acc);
         }
         acc = warp_sum(acc);
-        if (lane == 0) a.logits[row] = acc;
+        if (lane == 0) lg0[row] = acc;
+        row += kRouterThreads / 32;
+        if (row < r1) {
+            const uint4* wr = reinterpret_cast<const uint4*>(a.W + static_cast<size_t>(row) * K);
+#pragma unroll
+            for (int i = 0; i < VPL; ++i) wreg[i] = ldg_nc_v4(wr + lane + 32 * i);
+        }
     }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(a.counter, 1u);
-        is_last = (prev == gridDim.x - 1);
-    }
-    __syncthreads();
-    if (!is_last || warp != 0) return;
-    __threadfence();
+    cluster.sync();
+    if (rank != 0 || warp != 0) return;
 
-    // ---- softmax + top-k in one warp (fixed order, restated by the CPU oracle) ----
+    // ---- softmax + top-k in one warp of CTA 0 ----
     const int E = a.E;
     float m = -INFINITY;
-    for (int e = lane; e < E; e += 32) m = fmaxf(m, __ldcg(a.logits + e));
+    for (int e = lane; e < E; e += 32) m = fmaxf(m, lg[e]);
     m = warp_max(m);
     float s = 0.0f;
+    float* pe = lg;  // probabilities overwrite the logits in place (shared gate at lg[E] kept)
     for (int e = lane; e < E; e += 32) {
-        const float ev = dm_det_exp(DM_DET_SUB(__ldcg(a.logits + e), m));
+        const float ev = dm_det_exp(DM_DET_SUB(lg[e], m));
         pe[e] = ev;
         s = DM_DET_ADD(s, ev);
     }
@@ -136,22 +163,20 @@ __global__ void __launch_bounds__(256) router_kernel(const __grid_constant__ Rou
     for (int r = 0; r < a.topk; ++r) {
         float bv = -1.0f;
         int bi = 0x7fffffff;
-        for (int e = lane; e < E; e += 32) {
-            const float p = pe[e];
-            if (p > bv) { bv = p; bi = e; }
-        }
+        for (int e = lane; e < E; e += 32)
+            if (pe[e] > bv) { bv = pe[e]; bi = e; }
 #pragma unroll
         for (int mm = 16; mm >= 1; mm >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, mm);
             const int oi = __shfl_xor_sync(0xffffffffu, bi, mm);
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
+        if (bi < 0 || bi >= E) {  // only when probabilities are NaN: keep ids in range
+            if (lane == 0) raise_error(a.err, DM_DEVERR_NONFINITE);
+            bi = r;
+            bv = 0.0f;
+        }
         if (lane == 0) {
-            if (bi < 0 || bi >= E) {  // only when probabilities are NaN: keep ids in range
-                raise_error(a.err, DM_DEVERR_NONFINITE);
-                bi = r;
-                bv = 0.0f;
-            }
             a.ids[r] = bi;
             a.probs[r] = bv;
             pe[bi] = -2.0f;
@@ -159,10 +184,8 @@ __global__ void __launch_bounds__(256) router_kernel(const __grid_constant__ Rou
         __syncwarp();
     }
     if (lane == 0) {
-        const float zs = __ldcg(a.logits + E);
-        if (a.shared_g) *a.shared_g = sigmoid_f(zs);
+        if (a.shared_g) *a.shared_g = sigmoid_f(lg[E]);
         if (s != s || isinf(s)) raise_error(a.err, DM_DEVERR_NONFINITE);
-        *a.counter = 0u;
     }
 }
 
@@ -176,21 +199,42 @@ cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.gamma = normalise_input ? w.post_norm : nullptr;
     a.eps = d.eps;
     a.xn_out = normalise_input ? b.xn : b.attn_out;  // pre-normalised input: copy to scratch
-    a.logits = b.rlogits;
     a.ids = b.topk_ids;
     a.probs = b.topk_p;
     a.shared_g = b.shared_g;
-    a.counter = b.counters + kCntRouter;
     a.err = b.err;
-    const int grid = (d.E + 1 + 7) / 8;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(kRouterCluster);
+    cfg.blockDim = dim3(kRouterThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = lc.stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = lc.pdl ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = kRouterCluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     switch (d.H) {
-        case 256: return launch_kernel(lc, router_kernel<256>, dim3(grid), dim3(256), 0, a);
-        case 512: return launch_kernel(lc, router_kernel<512>, dim3(grid), dim3(256), 0, a);
-        case 1024: return launch_kernel(lc, router_kernel<1024>, dim3(grid), dim3(256), 0, a);
-        case 2048: return launch_kernel(lc, router_kernel<2048>, dim3(grid), dim3(256), 0, a);
-        case 4096: return launch_kernel(lc, router_kernel<4096>, dim3(grid), dim3(256), 0, a);
+        case 256: return cudaLaunchKernelEx(&cfg, router_kernel<256>, a);
+        case 512: return cudaLaunchKernelEx(&cfg, router_kernel<512>, a);
+        case 1024: return cudaLaunchKernelEx(&cfg, router_kernel<1024>, a);
+        case 2048: return cudaLaunchKernelEx(&cfg, router_kernel<2048>, a);
+        case 4096: return cudaLaunchKernelEx(&cfg, router_kernel<4096>, a);
         default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t router_set_attrs() {
+    cudaError_t e = cudaSuccess;
+#define DM_ROUTER_ATTR(KK)                                                                            \
+    if (e == cudaSuccess)                                                                             \
+        e = cudaFuncSetAttribute(router_kernel<KK>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    DM_ROUTER_ATTR(256) DM_ROUTER_ATTR(512) DM_ROUTER_ATTR(1024) DM_ROUTER_ATTR(2048) DM_ROUTER_ATTR(4096)
+#undef DM_ROUTER_ATTR
+    return e;
 }
 
 // ---------------------------------------------------------------------------------------

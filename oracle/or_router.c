@@ -35,15 +35,14 @@ static float butterfly32(float* v) {
 }
 
 void or_rmsnorm_canonical(const float* x, const uint16_t* gamma, int n, float eps, float* y) {
-    float lanes[4][32];
-    for (int t = 0; t < 128; ++t) {
+    float lanes[16][32];
+    for (int t = 0; t < 512; ++t) {
         float acc = 0.0f;
-        for (int k = t; k < n; k += 128) acc = fmaf(x[k], x[k], acc);
+        for (int k = t; k < n; k += 512) acc = fmaf(x[k], x[k], acc);
         lanes[t >> 5][t & 31] = acc;
     }
-    float w[4];
-    for (int i = 0; i < 4; ++i) w[i] = butterfly32(lanes[i]);
-    const float ss = ((w[0] + w[1]) + w[2]) + w[3];
+    float ss = 0.0f;
+    for (int w = 0; w < 16; ++w) ss = ss + butterfly32(lanes[w]);
     const float denom = sqrtf(ss / (float)n + eps);
     for (int k = 0; k < n; ++k) y[k] = (x[k] / denom) * bf16f(gamma[k]);
 }
