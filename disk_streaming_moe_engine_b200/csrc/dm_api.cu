@@ -391,14 +391,6 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     if (e == cudaSuccess) e = gemv_set_attrs();
     if (e == cudaSuccess) e = moe_set_attrs();
     if (e == cudaSuccess) e = router_set_attrs();
-    const int nsplit = attn_nsplit(c->num_sms, c->d.Hkv);
-    const int cap = attn_scores_cap(c->d.max_pages, nsplit);
-    const int score_smem = (c->d.Hq / c->d.Hkv) * cap * 4;
-    if (score_smem > kAttnMaxScoreSmem) {
-        fprintf(stderr, "dm_ctx_create: max_pages_per_seq too large for the decode attention kernel\n");
-        delete c;
-        return DM_ERR_INVALID_ARG;
-    }
     // function attributes are per process: always the kernel's fixed maximum, never a
     // per-context value that a later, smaller context would lower
     if (e == cudaSuccess) e = attn_set_attrs(kAttnMaxScoreSmem);
@@ -835,7 +827,15 @@ static cudaError_t enqueue_moe(dm_ctx* c, int layer, int slot) {
     cudaError_t e;
     if ((e = launch_router(lc, c->d, w, c->b, slot, 1)) != cudaSuccess) return e;
     if ((e = launch_moe_up(lc, c->d, w, c->b)) != cudaSuccess) return e;
-    return launch_moe_down(lc, c->d, w, c->b, c->b.xmid + xo, c->b.xres + xo);
+    // the next layer's input projection is the next large stream: start it into L2
+    const void* next_w = nullptr;
+    size_t next_bytes = 0;
+    if (layer + 1 < c->d.L) {
+        const LayerW& nw = c->layers[layer + 1];
+        next_w = nw.w_in;
+        next_bytes = static_cast<size_t>(nw.is_attn ? c->d.attn_in_rows : c->d.gdn_in_rows) * c->d.H * 2;
+    }
+    return launch_moe_down(lc, c->d, w, c->b, c->b.xmid + xo, c->b.xres + xo, next_w, next_bytes);
 }
 
 static cudaError_t enqueue_step(dm_ctx* c, int slot) {

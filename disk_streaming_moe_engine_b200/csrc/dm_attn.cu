@@ -34,6 +34,8 @@ struct AttnArgs {
     float* part;              // [Hq][kMaxSplits][D+2]
     float* out;               // [Hq*D]
     unsigned* counters;       // [Hkv]
+    const void* next_w;       // o_proj weights, prefetched into L2
+    size_t next_bytes;
     uint32_t* err;
 };
 
@@ -60,25 +62,72 @@ __device__ __forceinline__ void norm_rope_head(const float* src, const uint16_t*
     __syncwarp();
 }
 
+constexpr int kAttnStages = 6;   // K+V page tiles in flight per CTA
+
+// One KV page tile (16 tokens x D, K then V) per ring stage.
+template <int D>
+struct AttnGeom {
+    static constexpr int TILE = kPageTokens * D * 2;     // bytes of K (or V) of one page, one head
+    static constexpr int STAGE = 2 * TILE;
+    static constexpr int RING = kAttnStages * STAGE;
+};
+
 template <int D, int GRP>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
-    constexpr int EPL = D / 32;  // k elements per lane in the score loop
+    using AG = AttnGeom<D>;
+    constexpr int EPL = D / 32;  // q/k elements per lane in the score loop
+    extern __shared__ __align__(128) uint8_t ring[];
+    __shared__ __align__(8) uint64_t bar[kAttnStages];
     __shared__ __align__(16) float qsm[GRP][D];
     __shared__ __align__(16) float knew[D], vnew[D];
     __shared__ uint16_t kbits[D], vbits[D];
-    __shared__ float hm[GRP], hl[GRP];
+    __shared__ float sc[GRP][kPageTokens];
+    __shared__ float m_run[GRP], l_run[GRP], scale[GRP];
     __shared__ float wsp[GRP][kMaxSplits];
     __shared__ int is_last;
-    extern __shared__ float scores[];  // [GRP][cap]
     const int g = blockIdx.x, s = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
 
-    pdl_wait();
+    // positions < pos were written by earlier steps and the page table is fixed: the
+    // range of this split and its first page tiles do not depend on the previous kernel
     const int pos = *a.pos;
     const int n_tok = pos + 1;
     const int capacity = a.max_pages * kPageTokens;
-    if (pos < 0 || pos >= capacity) {  // no room: report, touch nothing (the score buffer
-        if (tid == 0 && s == 0) raise_error(a.err, DM_DEVERR_CAPACITY);  // is sized for capacity)
+    const bool in_range = pos >= 0 && pos < capacity;
+    int chunk = (n_tok + a.nsplit - 1) / a.nsplit;
+    chunk = (chunk + kPageTokens - 1) / kPageTokens * kPageTokens;
+    const int t0 = in_range ? s * chunk : 0;
+    const int t1 = in_range ? min(n_tok, t0 + chunk) : 0;
+    const int np = t1 > t0 ? (t1 - 1) / kPageTokens - t0 / kPageTokens + 1 : 0;
+    const int pg0 = t0 / kPageTokens;
+    auto issue = [&](int i) {  // page i of this split into its ring stage (thread 0 only)
+        const int slot = i % kAttnStages;
+        uint8_t* dst = ring + static_cast<size_t>(slot) * AG::STAGE;
+        const int page = a.page_table[pg0 + i];
+        if (page < 0 || page >= a.num_pages) {
+            raise_error(a.err, DM_DEVERR_PAGE);
+            mbar_arrive(&bar[slot]);  // no copy: the tile is left as is and masked below
+            return;
+        }
+        mbar_arrive_expect_tx(&bar[slot], AG::STAGE);
+        const uint16_t* kt = a.kv + ((static_cast<size_t>(page) * 2 + 0) * a.Hkv + g) * kPageTokens * D;
+        const uint16_t* vt = a.kv + ((static_cast<size_t>(page) * 2 + 1) * a.Hkv + g) * kPageTokens * D;
+        bulk_g2s(dst, kt, AG::TILE, &bar[slot]);
+        bulk_g2s(dst + AG::TILE, vt, AG::TILE, &bar[slot]);
+    };
+    prefetch_l2_share(a.next_w, a.next_bytes, s * gridDim.x + g, gridDim.x * gridDim.y, tid);
+    if (tid == 0) {
+        for (int i = 0; i < kAttnStages; ++i) mbar_init(&bar[i], 1);
+        mbar_fence_init();
+        for (int i = 0; i < np && i < kAttnStages; ++i) issue(i);
+    }
+    if (tid < GRP) {
+        m_run[tid] = -INFINITY;
+        l_run[tid] = 0.0f;
+    }
+    pdl_wait();
+    if (!in_range) {  // no room: report, touch nothing
+        if (tid == 0 && s == 0) raise_error(a.err, DM_DEVERR_CAPACITY);
         return;
     }
 
@@ -122,98 +171,100 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         }
     }
 
-    // ---- this split's positions ----
-    int chunk = (n_tok + a.nsplit - 1) / a.nsplit;
-    chunk = (chunk + kPageTokens - 1) / kPageTokens * kPageTokens;
-    const int t0 = s * chunk;
-    const int t1 = min(n_tok, t0 + chunk);
-    const int T = t1 > t0 ? t1 - t0 : 0;
-    const float scale = 1.0f / sqrtf(static_cast<float>(D));
-
-    // scores: warp per position, lanes own EPL contiguous dims
-    for (int ti = warp; ti < T; ti += 4) {
-        const int t = t0 + ti;
-        float kf[EPL];
-        if (t == pos) {
+    // q of this warp's lanes in registers: element e of head hh = q[hh][lane*EPL + e]
+    float qr[GRP][EPL];
 #pragma unroll
-            for (int e = 0; e < EPL; ++e) kf[e] = knew[lane * EPL + e];
-        } else {
-            const int page = a.page_table[t / kPageTokens];
-            const bool ok = page >= 0 && page < a.num_pages;
-            if (!ok && lane == 0) raise_error(a.err, DM_DEVERR_PAGE);
-            const uint16_t* kr = a.kv + ((static_cast<size_t>(ok ? page : 0) * 2 + 0) * a.Hkv + g) * kPageTokens * D +
-                                 static_cast<size_t>(t % kPageTokens) * D + lane * EPL;
-            if (EPL == 8) {
-                const uint4 u = *reinterpret_cast<const uint4*>(kr);
+    for (int hh = 0; hh < GRP; ++hh)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) qr[hh][e] = qsm[hh][lane * EPL + e];
+    const float sm_scale = 1.0f / sqrtf(static_cast<float>(D));
+    constexpr int DPT = (D + 127) / 128;  // V dims per thread
+    float acc[GRP][DPT];
+#pragma unroll
+    for (int hh = 0; hh < GRP; ++hh)
+#pragma unroll
+        for (int j = 0; j < DPT; ++j) acc[hh][j] = 0.0f;
+
+    for (int i = 0; i < np; ++i) {
+        const int slot = i % kAttnStages;
+        const bool ok = mbar_wait_bounded(&bar[slot], (i / kAttnStages) & 1, a.err, nullptr);
+        const uint16_t* kt = reinterpret_cast<const uint16_t*>(ring + static_cast<size_t>(slot) * AG::STAGE);
+        const uint16_t* vt = kt + kPageTokens * D;
+        const int tp = (pg0 + i) * kPageTokens;  // position of the page's first token
+        // scores: warp w -> tokens w, w+4, w+8, w+12 of the page
+        for (int tt = warp; tt < kPageTokens; tt += 4) {
+            const int t = tp + tt;
+            float kf[EPL];
+            if (t == pos) {
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) kf[e] = knew[lane * EPL + e];
+            } else if (EPL == 8) {
+                const uint4 u = *reinterpret_cast<const uint4*>(kt + tt * D + lane * 8);
                 kf[0] = bf16lo(u.x); kf[1] = bf16hi(u.x); kf[2] = bf16lo(u.y); kf[3] = bf16hi(u.y);
                 kf[4] = bf16lo(u.z); kf[5] = bf16hi(u.z); kf[6] = bf16lo(u.w); kf[7] = bf16hi(u.w);
             } else {
 #pragma unroll
-                for (int e = 0; e < EPL; ++e) kf[e] = bf16_to_f32(kr[e]);
+                for (int e = 0; e < EPL; ++e) kf[e] = bf16_to_f32(kt[tt * D + lane * EPL + e]);
             }
-            if (!ok) {
+            const bool valid = ok && t >= t0 && t < t1;
 #pragma unroll
-                for (int e = 0; e < EPL; ++e) kf[e] = 0.0f;
+            for (int hh = 0; hh < GRP; ++hh) {
+                float p = 0.0f;
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) p = fmaf(qr[hh][e], kf[e], p);
+                p = warp_sum(p);
+                if (lane == 0) sc[hh][tt] = valid ? p * sm_scale : -INFINITY;
             }
         }
-#pragma unroll
-        for (int hh = 0; hh < GRP; ++hh) {
-            float p = 0.0f;
-#pragma unroll
-            for (int e = 0; e < EPL; ++e) p = fmaf(qsm[hh][lane * EPL + e], kf[e], p);
-            p = warp_sum(p);
-            if (lane == 0) scores[hh * a.cap + ti] = p * scale;
+        __syncthreads();
+        // online softmax update, one warp per head: lanes 0..15 hold the page's scores
+        for (int hh = warp; hh < GRP; hh += 4) {
+            const float sv = lane < kPageTokens ? sc[hh][lane] : -INFINITY;
+            const float mp = warp_max(sv);
+            const float mo = m_run[hh];
+            const float mn = fmaxf(mo, mp);
+            const float pv = (lane < kPageTokens && sv != -INFINITY) ? expf(sv - mn) : 0.0f;
+            const float ls = warp_sum(pv);
+            if (lane < kPageTokens) sc[hh][lane] = pv;
+            if (lane == 0) {
+                const float f = (mo == -INFINITY) ? 0.0f : expf(mo - mn);
+                scale[hh] = f;
+                l_run[hh] = l_run[hh] * f + ls;
+                m_run[hh] = mn;
+            }
         }
+        __syncthreads();
+        // V: thread owns dims tid, tid + 128, ...
+#pragma unroll
+        for (int j = 0; j < DPT; ++j) {
+            const int d = tid + 128 * j;
+            if (d < D) {
+#pragma unroll
+                for (int hh = 0; hh < GRP; ++hh) acc[hh][j] *= scale[hh];
+                for (int tt = 0; tt < kPageTokens; ++tt) {
+                    const int t = tp + tt;
+                    const float v = (t == pos) ? vnew[d] : bf16_to_f32(vt[tt * D + d]);
+#pragma unroll
+                    for (int hh = 0; hh < GRP; ++hh) acc[hh][j] = fmaf(sc[hh][tt], v, acc[hh][j]);
+                }
+            }
+        }
+        __syncthreads();  // stage free and sc reusable
+        if (tid == 0 && i + kAttnStages < np) issue(i + kAttnStages);
     }
-    __syncthreads();
 
-    // softmax partial per head
-    for (int hh = warp; hh < GRP; hh += 4) {
-        float m = -INFINITY;
-        for (int ti = lane; ti < T; ti += 32) m = fmaxf(m, scores[hh * a.cap + ti]);
-        m = warp_max(m);
-        float l = 0.0f;
-        for (int ti = lane; ti < T; ti += 32) {
-            const float e = (T > 0) ? expf(scores[hh * a.cap + ti] - m) : 0.0f;
-            scores[hh * a.cap + ti] = e;
-            l += e;
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            hm[hh] = m;
-            hl[hh] = l;
-        }
-    }
-    __syncthreads();
-
-    // weighted V sum: thread owns dims d = tid, tid + 128, ...
-    for (int d = tid; d < D; d += 128) {
-        float acc[GRP];
 #pragma unroll
-        for (int hh = 0; hh < GRP; ++hh) acc[hh] = 0.0f;
-        for (int ti = 0; ti < T; ++ti) {
-            const int t = t0 + ti;
-            float v;
-            if (t == pos) {
-                v = vnew[d];
-            } else {
-                const int page = a.page_table[t / kPageTokens];
-                const bool ok = page >= 0 && page < a.num_pages;
-                v = ok ? bf16_to_f32(a.kv[((static_cast<size_t>(page) * 2 + 1) * a.Hkv + g) * kPageTokens * D +
-                                          static_cast<size_t>(t % kPageTokens) * D + d])
-                       : 0.0f;
-            }
+    for (int j = 0; j < DPT; ++j) {
+        const int d = tid + 128 * j;
+        if (d < D)
 #pragma unroll
-            for (int hh = 0; hh < GRP; ++hh) acc[hh] = fmaf(scores[hh * a.cap + ti], v, acc[hh]);
-        }
-#pragma unroll
-        for (int hh = 0; hh < GRP; ++hh)
-            a.part[(static_cast<size_t>(g * GRP + hh) * kMaxSplits + s) * (D + 2) + d] = acc[hh];
+            for (int hh = 0; hh < GRP; ++hh)
+                a.part[(static_cast<size_t>(g * GRP + hh) * kMaxSplits + s) * (D + 2) + d] = acc[hh][j];
     }
     if (tid < GRP) {
         float* p = a.part + (static_cast<size_t>(g * GRP + tid) * kMaxSplits + s) * (D + 2);
-        p[D] = hm[tid];
-        p[D + 1] = hl[tid];
+        p[D] = np > 0 ? m_run[tid] : -INFINITY;
+        p[D + 1] = np > 0 ? l_run[tid] : 0.0f;
     }
     __syncthreads();
     if (tid == 0) {
@@ -270,6 +321,10 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     if (tid == 0) a.counters[g] = 0u;
 }
 
+size_t attn_ring_bytes(int D) {
+    return static_cast<size_t>(kAttnStages) * 2 * 2 * kPageTokens * D;
+}
+
 int attn_scores_cap(int max_pages, int nsplit) {
     const int max_tok = max_pages * kPageTokens;
     int chunk = (max_tok + nsplit - 1) / nsplit;
@@ -323,10 +378,12 @@ cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW&
     a.part = b.attn_part;
     a.out = b.attn_out;
     a.counters = b.counters + kCntAttnBase;
+    a.next_w = w.w_out;
+    a.next_bytes = static_cast<size_t>(d.H) * d.Hq * d.D * 2;
     a.err = b.err;
     const int grp = d.Hq / d.Hkv;
     const dim3 grid(d.Hkv, a.nsplit);
-    const size_t smem = static_cast<size_t>(grp) * a.cap * sizeof(float);
+    const size_t smem = attn_ring_bytes(d.D);
 #define DM_ATTN_LAUNCH(DD, GG) \
     if (d.D == DD && grp == GG) return launch_kernel(lc, attn_decode_kernel<DD, GG>, grid, dim3(128), smem, a);
     DM_ATTN_INSTANCES(DM_ATTN_LAUNCH)

@@ -114,6 +114,22 @@ DM_DEV void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
                  : "memory");
 }
 
+// Prefetches this CTA's share [part/nparts] of [base, base + bytes) into L2 in 64 KB bulk
+// prefetches issued by threads tid < 32 (fire and forget; no shared memory involved).
+DM_DEV void prefetch_l2_share(const void* base, size_t bytes, int part, int nparts, int tid) {
+    if (base == nullptr || bytes == 0 || tid >= 32) return;
+    const size_t per = ((bytes + nparts - 1) / nparts + 15) & ~static_cast<size_t>(15);
+    const size_t b0 = per * part;
+    if (b0 >= bytes) return;
+    const size_t b1 = b0 + per < bytes ? b0 + per : bytes;
+    constexpr size_t kPiece = 64 * 1024;
+    const char* p = static_cast<const char*>(base);
+    for (size_t o = b0 + tid * kPiece; o < b1; o += 32 * kPiece) {
+        const size_t n = (b1 - o) < kPiece ? (b1 - o) : kPiece;
+        bulk_prefetch_l2(p + o, static_cast<uint32_t>(n & ~static_cast<size_t>(15)));
+    }
+}
+
 // ---- loads ---------------------------------------------------------------------------
 DM_DEV uint4 ldg_nc_v4(const void* p) {
     uint4 r;

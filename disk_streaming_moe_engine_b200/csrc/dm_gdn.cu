@@ -31,6 +31,8 @@ struct GdnRecArgs {
     const int* pos;
     int nk, nv, qkv_dim;
     float eps;
+    const void* next_w;     // out_proj weights, prefetched into L2
+    size_t next_bytes;
 };
 
 __device__ __forceinline__ float softplus_ref(float v) {
@@ -49,6 +51,8 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g_qk = h / (a.nv / a.nk);
 
+    prefetch_l2_share(a.next_w, a.next_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y,
+                      threadIdx.x);
     // ---- prologue: this CTA's state rows (4 per warp) into registers ----
     float* Sh = a.S + static_cast<size_t>(h) * DV * DK;
     float srow[4][CPL];
@@ -149,6 +153,8 @@ cudaError_t launch_gdn_rec(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.nv = d.nv;
     a.qkv_dim = d.qkv_dim;
     a.eps = d.eps;
+    a.next_w = w.w_out;
+    a.next_bytes = static_cast<size_t>(d.H) * d.z_dim * 2;
     const dim3 grid(d.nv, d.dv / 16);
     if (d.dk == 128) return launch_kernel(lc, gdn_rec_kernel<128>, grid, dim3(128), 0, a);
     if (d.dk == 64) return launch_kernel(lc, gdn_rec_kernel<64>, grid, dim3(128), 0, a);

@@ -137,8 +137,10 @@ cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
 cudaError_t launch_moe_up(const LaunchCfg& lc, const Dims& d, const LayerW& w,
                           const Buffers& b);
 // down projection + weighted sum + residual: x_out = x_res + sum
+// next_w/next_bytes: weights of the following kernel, prefetched into L2 (may be null)
 cudaError_t launch_moe_down(const LaunchCfg& lc, const Dims& d, const LayerW& w,
-                            const Buffers& b, const float* x_res, float* x_out);
+                            const Buffers& b, const float* x_res, float* x_out,
+                            const void* next_w = nullptr, size_t next_bytes = 0);
 cudaError_t launch_head(const LaunchCfg& lc, const Dims& d, const uint16_t* final_norm,
                         const uint16_t* lm_head, const Buffers& b, int slot, int advance,
                         int record_gen);

@@ -35,6 +35,8 @@ struct RouterArgs {
     int* ids;
     float* probs;
     float* shared_g;
+    const uint8_t* experts;   // L2 prefetch of the selected experts' records
+    int64_t expert_bytes;
     uint32_t* err;
 };
 
@@ -182,6 +184,8 @@ __global__ void __launch_bounds__(kRouterThreads, 2) router_kernel(const __grid_
             pe[bi] = -2.0f;
         }
         __syncwarp();
+        if (a.experts)  // the expert kernels will read this record next: start it now
+            prefetch_l2_share(a.experts + static_cast<int64_t>(bi) * a.expert_bytes, a.expert_bytes, 0, 1, lane);
     }
     if (lane == 0) {
         if (a.shared_g) *a.shared_g = sigmoid_f(lg[E]);
@@ -202,6 +206,8 @@ cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.ids = b.topk_ids;
     a.probs = b.topk_p;
     a.shared_g = b.shared_g;
+    a.experts = w.experts;
+    a.expert_bytes = d.expert_bytes;
     a.err = b.err;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(kRouterCluster);
@@ -285,6 +291,8 @@ struct MoeArgs {
     float* h;                 // [(topk+1)][I]
     const float* x_res;       // [H]
     float* x_out;             // [H]
+    const void* next_w;       // weights the next kernel streams (L2 prefetch), may be null
+    size_t next_bytes;
     uint32_t* err;
 };
 
@@ -415,6 +423,7 @@ __global__ void __launch_bounds__(256) moe_down_kernel(const __grid_constant__ M
     const int nexp = a.topk + 1;
     const int c = blockIdx.x;
     float* hs = reinterpret_cast<float*>(dsm + static_cast<size_t>(nexp) * Q::CHUNK);
+    prefetch_l2_share(a.next_w, a.next_bytes, blockIdx.x, gridDim.x, threadIdx.x);
     if (threadIdx.x == 0) {
         for (int j = 0; j < nexp; ++j) mbar_init(&bar[j], 1);
         mbar_fence_init();
@@ -553,10 +562,13 @@ cudaError_t launch_moe_up(const LaunchCfg& lc, const Dims& d, const LayerW& w, c
 }
 
 cudaError_t launch_moe_down(const LaunchCfg& lc, const Dims& d, const LayerW& w,
-                            const Buffers& b, const float* x_res, float* x_out) {
+                            const Buffers& b, const float* x_res, float* x_out, const void* next_w,
+                            size_t next_bytes) {
     MoeArgs a = moe_args(d, w, b);
     a.x_res = x_res;
     a.x_out = x_out;
+    a.next_w = next_w;
+    a.next_bytes = next_bytes;
     return launch_moe(lc, d, a, false);
 }
 
