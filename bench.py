@@ -299,8 +299,7 @@ def run_ours(args, rank, local, world):
     peak, peak_kind = measured_peak()
     kernels = {}
     names = {_lib.DM_KERNEL_MIXER_IN: "in_proj", _lib.DM_KERNEL_MIXER_OUT: "out_proj",
-             _lib.DM_KERNEL_MIXER_CORE: "core", _lib.DM_KERNEL_ROUTER: "router", _lib.DM_KERNEL_MOE_UP: "moe_up",
-             _lib.DM_KERNEL_MOE_DOWN: "moe_down"}
+             _lib.DM_KERNEL_MIXER_CORE: "core", _lib.DM_KERNEL_MOE: "moe"}
     for layer, tag in ((0, "gdn"), (3, "attn")):
         for which, nm in names.items():
             kms, kb = eng.time_kernel(which, layer, 20)

@@ -22,8 +22,8 @@ DM_ERR_TIMEOUT = 7
 DM_ERR_NOT_READY = 8
 DM_ERR_ROUTER = 9
 
-(DM_KERNEL_MIXER_IN, DM_KERNEL_MIXER_OUT, DM_KERNEL_MIXER_CORE, DM_KERNEL_ROUTER, DM_KERNEL_MOE_UP,
- DM_KERNEL_MOE_DOWN, DM_KERNEL_HEAD) = range(7)
+DM_KERNEL_MIXER_IN, DM_KERNEL_MIXER_OUT, DM_KERNEL_MIXER_CORE = 0, 1, 2
+DM_KERNEL_ROUTER, DM_KERNEL_MOE, DM_KERNEL_HEAD = 3, 4, 6
 
 DM_DTYPE_BF16 = 0
 DM_DTYPE_F32 = 1

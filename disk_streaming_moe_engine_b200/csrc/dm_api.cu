@@ -30,6 +30,7 @@ bool moe_supported(int H, int I, int G);
 bool attn_supported(int D, int grp);
 int attn_scores_cap(int max_pages, int nsplit);
 int attn_nsplit(int num_sms, int Hkv);
+cudaError_t launch_rope_table(cudaStream_t st, float2* tab, int capacity, int rot_dim, float theta);
 cudaError_t launch_kv_copy(cudaStream_t st, uint16_t* kv_layer, const int* page_table_row, int Hkv,
                            int D, uint16_t* k, uint16_t* v, int n_tokens, int to_cache);
 cudaError_t launch_synth_bf16(cudaStream_t st, uint16_t* dst, uint64_t n, uint64_t seed,
@@ -250,6 +251,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t o_xn = T(H * 4), o_rl = T((d.E + 1) * 4), o_ids = T(kMaxTopK * 4), o_p = T(kMaxTopK * 4);
     const size_t o_sg = T(4), o_h = T(static_cast<size_t>(d.topk + 1) * d.I * 4), o_logits = T(static_cast<size_t>(d.V) * 4);
     const size_t o_cv = T(kMaxCtas * 4), o_ci = T(kMaxCtas * 4), o_cnt = T(64 * 4), o_err = T(4);
+    const size_t o_rope = T(static_cast<size_t>(d.max_pages) * kPageTokens * (d.rot_dim / 2) * 8);
     const size_t o_sq = T(static_cast<size_t>(d.I) * H / 2), o_ss = T(static_cast<size_t>(d.I) * H / d.G * 2),
                  o_sz = T(static_cast<size_t>(d.I) * H / d.G / 2 + 16);
     c->arena_bytes = p.off;
@@ -314,6 +316,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     b.cand_idx = reinterpret_cast<int*>(A + o_ci);
     b.counters = reinterpret_cast<unsigned*>(A + o_cnt);
     b.err = reinterpret_cast<uint32_t*>(A + o_err);
+    b.rope = reinterpret_cast<float2*>(A + o_rope);
     c->stage_q = A + o_sq;
     c->stage_s = reinterpret_cast<uint16_t*>(A + o_ss);
     c->stage_z = A + o_sz;
@@ -410,6 +413,8 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     plan_memory(c, true);
     // zero everything (weights stay zero until uploaded; state starts empty)
     e = cudaMemsetAsync(c->arena, 0, c->arena_bytes, c->stream);
+    if (e == cudaSuccess)
+        e = launch_rope_table(c->stream, c->b.rope, c->d.max_pages * kPageTokens, c->d.rot_dim, c->d.theta);
     if (e == cudaSuccess) e = cudaMallocHost(&c->h_io, 64);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) {
@@ -463,7 +468,7 @@ int32_t dm_get_stream(dm_ctx* c, void** s) {
 
 int32_t dm_kernels_per_step(dm_ctx* c, int32_t* out) {
     if (!c || !out) return DM_ERR_INVALID_ARG;
-    *out = 1 + 6 * c->d.L + 1;  // embed, 3 mixer + 3 MoE kernels per block, head
+    *out = 1 + 4 * c->d.L + 1;  // embed, 3 mixer kernels + 1 MoE kernel per block, head
     return DM_OK;
 }
 
@@ -823,10 +828,6 @@ static cudaError_t enqueue_mixer(dm_ctx* c, int layer, int slot) {
 static cudaError_t enqueue_moe(dm_ctx* c, int layer, int slot) {
     const LaunchCfg lc = lcfg(c);
     const LayerW& w = c->layers[layer];
-    const size_t xo = static_cast<size_t>(slot) * c->d.H;
-    cudaError_t e;
-    if ((e = launch_router(lc, c->d, w, c->b, slot, 1)) != cudaSuccess) return e;
-    if ((e = launch_moe_up(lc, c->d, w, c->b)) != cudaSuccess) return e;
     // the next layer's input projection is the next large stream: start it into L2
     const void* next_w = nullptr;
     size_t next_bytes = 0;
@@ -835,7 +836,7 @@ static cudaError_t enqueue_moe(dm_ctx* c, int layer, int slot) {
         next_w = nw.w_in;
         next_bytes = static_cast<size_t>(nw.is_attn ? c->d.attn_in_rows : c->d.gdn_in_rows) * c->d.H * 2;
     }
-    return launch_moe_down(lc, c->d, w, c->b, c->b.xmid + xo, c->b.xres + xo, next_w, next_bytes);
+    return launch_moe_fused(lc, c->d, w, c->b, slot, next_w, next_bytes);
 }
 
 static cudaError_t enqueue_step(dm_ctx* c, int slot) {
@@ -1082,16 +1083,13 @@ int32_t dm_time_kernel(dm_ctx* c, int32_t which, int32_t layer, int32_t iters, f
             case DM_KERNEL_MIXER_CORE:
                 return w.is_attn ? launch_attn_decode(lc, d, w, c->b, slot) : launch_gdn_rec(lc, d, w, c->b, slot);
             case DM_KERNEL_ROUTER: return launch_router(lc, d, w, c->b, slot, 1);
-            case DM_KERNEL_MOE_UP: return launch_moe_up(lc, d, w, c->b);
-            case DM_KERNEL_MOE_DOWN:
-                return launch_moe_down(lc, d, w, c->b, c->b.xmid + slot * d.H, c->b.attn_out);
+            case DM_KERNEL_MOE: return launch_moe_fused(lc, d, w, c->b, slot);
             case DM_KERNEL_HEAD: return launch_head(lc, d, c->final_norm, c->lm_head, c->b, slot, 0, 0);
             default: return cudaErrorInvalidValue;
         }
     };
     // algorithmic bytes per launch (weights + state the kernel must move)
     const uint64_t eb = static_cast<uint64_t>(d.expert_bytes);
-    const uint64_t gu = static_cast<uint64_t>(d.gu_chunks) * d.gu_chunk_bytes;
     switch (which) {
         case DM_KERNEL_MIXER_IN: *bytes = (w.is_attn ? d.attn_in_rows : d.gdn_in_rows) * H * 2; break;
         case DM_KERNEL_MIXER_OUT: *bytes = H * (w.is_attn ? d.Hq * d.D : d.z_dim) * 2; break;
@@ -1102,8 +1100,7 @@ int32_t dm_time_kernel(dm_ctx* c, int32_t which, int32_t layer, int32_t iters, f
             break;
         }
         case DM_KERNEL_ROUTER: *bytes = (d.E + 1) * H * 2; break;
-        case DM_KERNEL_MOE_UP: *bytes = (d.topk + 1) * gu; break;
-        case DM_KERNEL_MOE_DOWN: *bytes = (d.topk + 1) * (eb - gu); break;
+        case DM_KERNEL_MOE: *bytes = (d.E + 1) * H * 2 + (d.topk + 1) * eb; break;
         case DM_KERNEL_HEAD: *bytes = static_cast<uint64_t>(d.V) * H * 2; break;
         default: return DM_ERR_INVALID_ARG;
     }

@@ -16,10 +16,14 @@
 // of KV head g (atomic counter) merges the partials and applies the output gate.  The
 // current token's k/v come from shared memory, so the append by CTA (g, 0) never races
 // with the reads of the other CTAs, which only touch positions < pos.
+#include <cooperative_groups.h>
+
 #include "dm_common.cuh"
 #include "dm_kernels.h"
 
 namespace dm {
+
+constexpr int kAttnCluster = 8;  // splits merged on chip per cluster
 
 struct AttnArgs {
     const float* qg;          // [2*Hq*D]
@@ -34,15 +38,17 @@ struct AttnArgs {
     float* part;              // [Hq][kMaxSplits][D+2]
     float* out;               // [Hq*D]
     unsigned* counters;       // [Hkv]
+    const float2* rope;       // [capacity][rot_dim/2] (cos, sin)
     const void* next_w;       // o_proj weights, prefetched into L2
     size_t next_bytes;
     uint32_t* err;
 };
 
 // Loads the RMS-normalised, rotated head vector `src` (length D) into dst (smem).
+// cs: the position's row of the RoPE table, (cos, sin) of fp32(pos) * inv_freq_i.
 template <int D>
 __device__ __forceinline__ void norm_rope_head(const float* src, const uint16_t* w, float* dst,
-                                               int lane, int rot_dim, float theta, float eps, int pos) {
+                                               int lane, int rot_dim, float eps, const float2* cs) {
     float ss = 0.0f;
     for (int d = lane; d < D; d += 32) ss = fmaf(src[d], src[d], ss);
     ss = warp_sum(ss);
@@ -50,19 +56,40 @@ __device__ __forceinline__ void norm_rope_head(const float* src, const uint16_t*
     for (int d = lane; d < D; d += 32) dst[d] = src[d] * rs * bf16_to_f32(w[d]);
     __syncwarp();
     const int half = rot_dim / 2;
-    const float m = static_cast<float>(pos);
     for (int i = lane; i < half; i += 32) {
-        const float inv_freq = 1.0f / powf(theta, static_cast<float>(2 * i) / static_cast<float>(rot_dim));
-        float sn, cs;
-        sincosf(m * inv_freq, &sn, &cs);
+        const float2 c = cs[i];
         const float x0 = dst[i], x1 = dst[i + half];
-        dst[i] = x0 * cs - x1 * sn;
-        dst[i + half] = x0 * sn + x1 * cs;
+        dst[i] = x0 * c.x - x1 * c.y;
+        dst[i + half] = x0 * c.y + x1 * c.x;
     }
     __syncwarp();
 }
 
+// RoPE table [capacity][rot_dim / 2] of (cos, sin) of fp32(pos) * inv_freq_i with
+// inv_freq_i = 1 / theta^(2i / rot_dim) (reference attention.mojo:318-354), filled once
+// per context so the decode step never evaluates trigonometry of large arguments.
+__global__ void rope_table_kernel(float2* tab, int capacity, int rot_dim, float theta) {
+    const int half = rot_dim / 2;
+    const int64_t n = static_cast<int64_t>(capacity) * half;
+    for (int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; k < n;
+         k += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(k / half), i = static_cast<int>(k % half);
+        const float inv_freq = 1.0f / powf(theta, static_cast<float>(2 * i) / static_cast<float>(rot_dim));
+        const float ang = static_cast<float>(p) * inv_freq;
+        tab[k] = make_float2(cosf(ang), sinf(ang));
+    }
+}
+
+cudaError_t launch_rope_table(cudaStream_t st, float2* tab, int capacity, int rot_dim, float theta) {
+    int blocks = (capacity * (rot_dim / 2) + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    if (blocks < 1) blocks = 1;
+    rope_table_kernel<<<blocks, 256, 0, st>>>(tab, capacity, rot_dim, theta);
+    return cudaGetLastError();
+}
+
 constexpr int kAttnStages = 6;   // K+V page tiles in flight per CTA
+constexpr int kMaxPagesPerSplit = 256;  // page ids staged in shared memory
 
 // One KV page tile (16 tokens x D, K then V) per ring stage.
 template <int D>
@@ -100,10 +127,13 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     const int t1 = in_range ? min(n_tok, t0 + chunk) : 0;
     const int np = t1 > t0 ? (t1 - 1) / kPageTokens - t0 / kPageTokens + 1 : 0;
     const int pg0 = t0 / kPageTokens;
+    __shared__ int pages[kMaxPagesPerSplit];
+    for (int i = tid; i < np && i < kMaxPagesPerSplit; i += 128) pages[i] = a.page_table[pg0 + i];
+    __syncthreads();
     auto issue = [&](int i) {  // page i of this split into its ring stage (thread 0 only)
         const int slot = i % kAttnStages;
         uint8_t* dst = ring + static_cast<size_t>(slot) * AG::STAGE;
-        const int page = a.page_table[pg0 + i];
+        const int page = i < kMaxPagesPerSplit ? pages[i] : a.page_table[pg0 + i];
         if (page < 0 || page >= a.num_pages) {
             raise_error(a.err, DM_DEVERR_PAGE);
             mbar_arrive(&bar[slot]);  // no copy: the tile is left as is and masked below
@@ -131,13 +161,14 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         return;
     }
 
+    const float2* cs_row = a.rope + static_cast<size_t>(pos) * (a.rot_dim / 2);
     // ---- q heads of this KV group, new k, new v ----
     for (int hh = warp; hh < GRP; hh += 4)
         norm_rope_head<D>(a.qg + static_cast<size_t>(g * GRP + hh) * D, a.q_norm, qsm[hh], lane,
-                          a.rot_dim, a.theta, a.eps, pos);
+                          a.rot_dim, a.eps, cs_row);
     if (warp == 0) {
         norm_rope_head<D>(a.kvnew + static_cast<size_t>(g) * D, a.k_norm, knew, lane, a.rot_dim,
-                          a.theta, a.eps, pos);
+                          a.eps, cs_row);
         for (int d = lane; d < D; d += 32) {
             const uint16_t kb = f32_to_bf16(knew[d]);
             kbits[d] = kb;
@@ -253,70 +284,95 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         if (tid == 0 && i + kAttnStages < np) issue(i + kAttnStages);
     }
 
+    // ---- merge 1: the kAttnCluster splits of this cluster through distributed shared
+    // memory: every CTA pushes its partial into rank 0's (free) ring, rank 0 merges
+    // locally and writes one partial (max, sum, acc) per head for the cluster ----
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int crank = static_cast<int>(cluster.block_rank());
+    constexpr int PSZ = GRP * D + 2 * GRP;            // floats of one pushed partial
+    static_assert(kAttnCluster * PSZ * 4 <= AG::RING, "ring too small for the cluster merge");
+    cluster.sync();                                    // every ring is free from here on
+    float* dst0 = cluster.map_shared_rank(reinterpret_cast<float*>(ring), 0) + crank * PSZ;
 #pragma unroll
     for (int j = 0; j < DPT; ++j) {
         const int d = tid + 128 * j;
         if (d < D)
 #pragma unroll
-            for (int hh = 0; hh < GRP; ++hh)
-                a.part[(static_cast<size_t>(g * GRP + hh) * kMaxSplits + s) * (D + 2) + d] = acc[hh][j];
+            for (int hh = 0; hh < GRP; ++hh) dst0[hh * D + d] = acc[hh][j];
     }
     if (tid < GRP) {
-        float* p = a.part + (static_cast<size_t>(g * GRP + tid) * kMaxSplits + s) * (D + 2);
-        p[D] = np > 0 ? m_run[tid] : -INFINITY;
-        p[D + 1] = np > 0 ? l_run[tid] : 0.0f;
+        dst0[GRP * D + tid] = np > 0 ? m_run[tid] : -INFINITY;
+        dst0[GRP * D + GRP + tid] = np > 0 ? l_run[tid] : 0.0f;
+    }
+    const int ccount = gridDim.y / kAttnCluster;   // clusters per KV head
+    const int cid = s / kAttnCluster;
+    cluster.sync();                                    // all partials are in rank 0
+    if (crank != 0) return;
+    {
+        const float* P = reinterpret_cast<const float*>(ring);
+        __shared__ float cw[GRP][kAttnCluster];
+        __shared__ float cm[GRP], cl[GRP];
+        if (tid < GRP) {
+            float M = -INFINITY;
+            for (int r = 0; r < kAttnCluster; ++r) {
+                const float lr = P[r * PSZ + GRP * D + GRP + tid];
+                if (lr > 0.0f) M = fmaxf(M, P[r * PSZ + GRP * D + tid]);
+            }
+            float L = 0.0f;
+            for (int r = 0; r < kAttnCluster; ++r) {
+                const float lr = P[r * PSZ + GRP * D + GRP + tid];
+                const float w = lr > 0.0f ? expf(P[r * PSZ + GRP * D + tid] - M) : 0.0f;
+                cw[tid][r] = w;
+                L += w * lr;
+            }
+            cm[tid] = M;
+            cl[tid] = L;
+        }
+        __syncthreads();
+        for (int o = tid; o < GRP * D; o += 128) {
+            const int hh = o / D;
+            float v = 0.0f;
+#pragma unroll
+            for (int r = 0; r < kAttnCluster; ++r) v = fmaf(cw[hh][r], P[r * PSZ + o], v);
+            a.part[(static_cast<size_t>(g * GRP + hh) * kMaxSplits + cid) * (D + 2) + (o % D)] = v;
+        }
+        if (tid < GRP) {
+            float* p = a.part + (static_cast<size_t>(g * GRP + tid) * kMaxSplits + cid) * (D + 2);
+            p[D] = cm[tid];
+            p[D + 1] = cl[tid];
+        }
     }
     __syncthreads();
     if (tid == 0) {
         __threadfence();
         const unsigned prev = atomicAdd(a.counters + g, 1u);
-        is_last = (prev == gridDim.y - 1);
+        is_last = (prev == static_cast<unsigned>(ccount) - 1);
     }
     __syncthreads();
     if (!is_last) return;
     __threadfence();
 
-    // ---- merge the splits of every head of this group, apply the output gate ----
-    // per-split weights w_s = exp(m_s - M) / L once per head, then every output element
-    // is an independent, coalesced sum over the splits.
-    const int ns = gridDim.y;
+    // ---- merge 2: the cluster partials of every head of this KV group, output gate ----
+    const int ns = ccount;
     for (int hh = warp; hh < GRP; hh += 4) {
         const float* ph = a.part + static_cast<size_t>(g * GRP + hh) * kMaxSplits * (D + 2);
-        float ml[2], ll[2];
-        float M = -INFINITY;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int sp = lane + 32 * k;
-            ml[k] = sp < ns ? __ldcg(ph + sp * (D + 2) + D) : -INFINITY;
-            ll[k] = sp < ns ? __ldcg(ph + sp * (D + 2) + D + 1) : 0.0f;
-            if (ll[k] > 0.0f) M = fmaxf(M, ml[k]);
-        }
-        M = warp_max(M);
-        float wk[2], L = 0.0f;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            wk[k] = ll[k] > 0.0f ? expf(ml[k] - M) : 0.0f;
-            L += wk[k] * ll[k];
-        }
-        L = warp_sum(L);
-        const float invL = 1.0f / L;
-#pragma unroll
-        for (int k = 0; k < 2; ++k)
-            if (lane + 32 * k < kMaxSplits) wsp[hh][lane + 32 * k] = wk[k] * invL;
+        const float ml = lane < ns ? __ldcg(ph + lane * (D + 2) + D) : -INFINITY;
+        const float ll = lane < ns ? __ldcg(ph + lane * (D + 2) + D + 1) : 0.0f;
+        const float M = warp_max(ll > 0.0f ? ml : -INFINITY);
+        const float wk = ll > 0.0f ? expf(ml - M) : 0.0f;
+        const float L = warp_sum(wk * ll);
+        if (lane < kMaxSplits) wsp[hh][lane] = wk / L;
     }
     __syncthreads();
     for (int o = tid; o < GRP * D; o += 128) {
         const int hh = o / D, d = o % D;
         const int hq = g * GRP + hh;
         const float* ph = a.part + static_cast<size_t>(hq) * kMaxSplits * (D + 2) + d;
-        float acc = 0.0f;
-#pragma unroll 8
-        for (int sp = 0; sp < ns; ++sp) {
-            const float w = wsp[hh][sp];
-            if (w != 0.0f) acc = fmaf(w, __ldcg(ph + static_cast<size_t>(sp) * (D + 2)), acc);
-        }
+        float acc2 = 0.0f;
+        for (int c = 0; c < ns; ++c) acc2 = fmaf(wsp[hh][c], __ldcg(ph + static_cast<size_t>(c) * (D + 2)), acc2);
         const float gate = a.qg[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
-        a.out[static_cast<size_t>(hq) * D + d] = acc * sigmoid_f(gate);
+        a.out[static_cast<size_t>(hq) * D + d] = acc2 * sigmoid_f(gate);
     }
     if (tid == 0) a.counters[g] = 0u;
 }
@@ -333,17 +389,18 @@ int attn_scores_cap(int max_pages, int nsplit) {
 
 int attn_nsplit(int num_sms, int Hkv) {
     int ns = num_sms / (Hkv > 0 ? Hkv : 1);
-    if (ns < 1) ns = 1;
     if (ns > kMaxSplits) ns = kMaxSplits;
+    ns = ns / kAttnCluster * kAttnCluster;  // whole clusters
+    if (ns < kAttnCluster) ns = kAttnCluster;
     return ns;
 }
 
 bool attn_supported(int D, int grp) {
-    return (D == 256 && (grp == 8 || grp == 4 || grp == 16)) || (D == 128 && (grp == 8 || grp == 4)) ||
+    return (D == 256 && (grp == 8 || grp == 4)) || (D == 128 && (grp == 8 || grp == 4)) ||
            (D == 64 && (grp == 4 || grp == 8));
 }
 
-#define DM_ATTN_INSTANCES(X) X(256, 8) X(256, 4) X(256, 16) X(128, 8) X(128, 4) X(64, 4) X(64, 8)
+#define DM_ATTN_INSTANCES(X) X(256, 8) X(256, 4) X(128, 8) X(128, 4) X(64, 4) X(64, 8)
 
 cudaError_t attn_set_attrs(int max_scores_smem) {
     cudaError_t e = cudaSuccess;
@@ -378,14 +435,29 @@ cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW&
     a.part = b.attn_part;
     a.out = b.attn_out;
     a.counters = b.counters + kCntAttnBase;
+    a.rope = b.rope;
     a.next_w = w.w_out;
     a.next_bytes = static_cast<size_t>(d.H) * d.Hq * d.D * 2;
     a.err = b.err;
     const int grp = d.Hq / d.Hkv;
     const dim3 grid(d.Hkv, a.nsplit);
     const size_t smem = attn_ring_bytes(d.D);
-#define DM_ATTN_LAUNCH(DD, GG) \
-    if (d.D == DD && grp == GG) return launch_kernel(lc, attn_decode_kernel<DD, GG>, grid, dim3(128), smem, a);
+#define DM_ATTN_LAUNCH(DD, GG)                                                                 \
+    if (d.D == DD && grp == GG) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<DD, GG>, a);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = lc.stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = lc.pdl ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = kAttnCluster;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     DM_ATTN_INSTANCES(DM_ATTN_LAUNCH)
 #undef DM_ATTN_LAUNCH
     return cudaErrorInvalidValue;

@@ -100,6 +100,7 @@ struct Buffers {
     int* cand_idx;        // [kMaxCtas]
     unsigned* counters;   // [64]
     uint32_t* err;        // [1]
+    float2* rope;         // [max_pages*16][rot_dim/2] (cos, sin) per position
 };
 
 constexpr int kMaxCtas = 1024;
@@ -107,6 +108,7 @@ constexpr int kMaxCtas = 1024;
 constexpr int kCntRouter = 0;
 constexpr int kCntHead = 1;
 constexpr int kCntAttnBase = 8;   // + kv head (< 32)
+constexpr int kCntMoeSync = 48;   // 4 words of grid-wide flags of the fused MoE kernel
 
 struct Ctx;  // host-side context (dm_api.cu)
 
@@ -134,13 +136,9 @@ cudaError_t launch_attn_out(const LaunchCfg& lc, const Dims& d, const LayerW& w,
 // router: normalise_input = 1 applies post_norm to b.xmid[slot]; 0 takes b.xn as given.
 cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
                           const Buffers& b, int slot, int normalise_input);
-cudaError_t launch_moe_up(const LaunchCfg& lc, const Dims& d, const LayerW& w,
-                          const Buffers& b);
-// down projection + weighted sum + residual: x_out = x_res + sum
-// next_w/next_bytes: weights of the following kernel, prefetched into L2 (may be null)
-cudaError_t launch_moe_down(const LaunchCfg& lc, const Dims& d, const LayerW& w,
-                            const Buffers& b, const float* x_res, float* x_out,
-                            const void* next_w = nullptr, size_t next_bytes = 0);
+// Whole MoE mixer of one layer (router, experts, residual) in one kernel; x_mid -> xres.
+cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot,
+                             const void* next_w = nullptr, size_t next_bytes = 0);
 cudaError_t launch_head(const LaunchCfg& lc, const Dims& d, const uint16_t* final_norm,
                         const uint16_t* lm_head, const Buffers& b, int slot, int advance,
                         int record_gen);

@@ -5,12 +5,13 @@
 //                  deterministic exponential, top-k on probabilities with ties to the lower
 //                  expert id, no renormalisation, shared gate sigmoid
 //                  (reference router.mojo:15-185, topk.mojo:11-131, moe.mojo:17).
-//  moe_up_kernel   for the k routed experts and the shared expert: nibble unpack + group
-//                  scale/zero dequant fused into the gate and up GEMVs, h = SiLU(g) * u
-//                  (reference swiglu.mojo:52, dequant order of quant_format.md:831-854).
-//  moe_down_kernel down GEMV of every selected expert for a 16-row output chunk, weighted
-//                  by the router probability (shared expert by its sigmoid gate), plus the
-//                  residual (reference moe_aggregate_forward, moe.mojo:105-177).
+//  moe_fused_kernel the whole MoE mixer of a layer in one kernel: RMSNorm, router and
+//                  top-k, then for the k routed experts and the shared expert: nibble
+//                  unpack + group scale/zero dequant fused into the gate/up GEMVs, h =
+//                  SiLU(g) * u (reference swiglu.mojo:52, nibble order of
+//                  quant_format.md:831-854), the down GEMVs weighted by the router
+//                  probability (shared expert by its sigmoid gate) and the residual
+//                  (reference moe_aggregate_forward, moe.mojo:105-177).
 //
 // 4-bit dot product: with F(n) = bits(0x4B000000 | n) = 2^23 + n, F(q) - F(z) = q - z is
 // exact, so each weight costs one byte-permute, one subtract and one fma; the group scale
@@ -35,8 +36,6 @@ struct RouterArgs {
     int* ids;
     float* probs;
     float* shared_g;
-    const uint8_t* experts;   // L2 prefetch of the selected experts' records
-    int64_t expert_bytes;
     uint32_t* err;
 };
 
@@ -184,8 +183,6 @@ __global__ void __launch_bounds__(kRouterThreads, 2) router_kernel(const __grid_
             pe[bi] = -2.0f;
         }
         __syncwarp();
-        if (a.experts)  // the expert kernels will read this record next: start it now
-            prefetch_l2_share(a.experts + static_cast<int64_t>(bi) * a.expert_bytes, a.expert_bytes, 0, 1, lane);
     }
     if (lane == 0) {
         if (a.shared_g) *a.shared_g = sigmoid_f(lg[E]);
@@ -206,8 +203,6 @@ cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.ids = b.topk_ids;
     a.probs = b.topk_p;
     a.shared_g = b.shared_g;
-    a.experts = w.experts;
-    a.expert_bytes = d.expert_bytes;
     a.err = b.err;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(kRouterCluster);
@@ -279,24 +274,6 @@ __device__ __forceinline__ float lane_group_sum(float v) {
     return v;
 }
 
-struct MoeArgs {
-    const uint8_t* experts;   // layer base: [E] records
-    const uint8_t* shared;    // shared expert record
-    int64_t expert_bytes, gu_part_bytes;
-    int gu_chunks, d_chunks, topk, I, H, E, slots;
-    const int* ids;
-    const float* probs;
-    const float* shared_g;
-    const float* xn;          // [H] normalised MoE input
-    float* h;                 // [(topk+1)][I]
-    const float* x_res;       // [H]
-    float* x_out;             // [H]
-    const void* next_w;       // weights the next kernel streams (L2 prefetch), may be null
-    size_t next_bytes;
-    uint32_t* err;
-};
-
-// Partial dot of row r of a chunk staged in shared memory.
 template <int K, int G>
 __device__ __forceinline__ float q4_partial_smem(const uint8_t* chunk, int r, int vl, const float4* x4) {
     using Q = Q4<K, G>;
@@ -335,241 +312,448 @@ __device__ __forceinline__ float q4_partial_smem(const uint8_t* chunk, int r, in
     return acc;
 }
 
-constexpr int kMoeMaxSlots = 16;   // chunk slots (mbarriers) per CTA
-
-// Gate/up projections of the k routed experts and the shared expert.  Work item =
-// (expert slot j, 8 output rows c): one 16-row chunk (8 gate + 8 up rows).  CTA b owns a
-// contiguous item range; thread 0 bulk-copies every chunk of the range into shared memory
-// at once (the shared expert's before griddepcontrol.wait: it does not depend on the
-// router), then 8 warps each reduce one (gate, up) row pair per chunk.
-template <int K, int G>
-__global__ void __launch_bounds__(256) moe_up_kernel(const __grid_constant__ MoeArgs a) {
-    using Q = Q4<K, G>;
-    extern __shared__ __align__(128) uint8_t dsm[];     // [slots][CHUNK] then x4[K]
-    __shared__ __align__(8) uint64_t bar[kMoeMaxSlots];
-    __shared__ int sid[kMaxTopK];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_items = (a.topk + 1) * a.gu_chunks;
-    const int i0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * n_items / gridDim.x);
-    const int i1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * n_items / gridDim.x);
-    const int nloc = i1 - i0;
-    float* x4 = reinterpret_cast<float*>(dsm + static_cast<size_t>(a.slots) * Q::CHUNK);
-    if (threadIdx.x == 0) {
-        for (int k = 0; k < nloc; ++k) mbar_init(&bar[k], 1);
-        mbar_fence_init();
-        for (int k = 0; k < nloc; ++k) {  // shared-expert chunks first, no dependency
-            const int item = i0 + k;
-            if (item / a.gu_chunks != a.topk) continue;
-            mbar_arrive_expect_tx(&bar[k], Q::CHUNK);
-            bulk_g2s(dsm + static_cast<size_t>(k) * Q::CHUNK,
-                     a.shared + static_cast<int64_t>(item % a.gu_chunks) * Q::CHUNK, Q::CHUNK, &bar[k]);
-        }
-    }
-    pdl_wait();
-    if (threadIdx.x < a.topk) sid[threadIdx.x] = min(max(a.ids[threadIdx.x], 0), a.E - 1);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int k = 0; k < nloc; ++k) {
-            const int item = i0 + k;
-            const int j = item / a.gu_chunks;
-            if (j == a.topk) continue;
-            mbar_arrive_expect_tx(&bar[k], Q::CHUNK);
-            bulk_g2s(dsm + static_cast<size_t>(k) * Q::CHUNK,
-                     a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes +
-                         static_cast<int64_t>(item % a.gu_chunks) * Q::CHUNK,
-                     Q::CHUNK, &bar[k]);
-        }
-    }
-    for (int k = threadIdx.x; k < K; k += 256) x4_store<K>(x4, k, a.xn[k]);
-    __syncthreads();
-    pdl_launch_dependents();
-    const float4* x4v = reinterpret_cast<const float4*>(x4);
-
-    for (int k = 0; k < nloc; ++k) {
-        const int item = i0 + k;
-        const int j = item / a.gu_chunks, c = item % a.gu_chunks;
-        const bool ok = mbar_wait_bounded(&bar[k], 0, a.err, nullptr);
-        const uint8_t* chunk = dsm + static_cast<size_t>(k) * Q::CHUNK;
-        // warp w: gate row w and up row 8 + w of the chunk (output row 8c + w)
-        float dots[2];
-#pragma unroll
-        for (int p = 0; p < 2; p += Q::RPP) {
-            const int sub = lane / Q::LPR, vl = lane % Q::LPR;
-            const int ri = p + sub;
-            float v = 0.0f;
-            if (ri < 2 && ok) v = q4_partial_smem<K, G>(chunk, ri == 0 ? warp : 8 + warp, vl, x4v);
-            v = lane_group_sum<Q::LPR>(v);
-            if (Q::RPP == 1) dots[p] = v;
-            else {  // lanes of row ri hold its sum; move the up-row sum to row 0's lanes
-                const float other = __shfl_sync(0xffffffffu, v, Q::LPR);
-                dots[0] = __shfl_sync(0xffffffffu, v, 0);
-                dots[1] = other;
-            }
-        }
-        if (lane == 0) a.h[j * a.I + 8 * c + warp] = silu_f(dots[0]) * dots[1];
-    }
-}
-
-// Down projection of every selected expert for one 16-row output chunk per CTA, weighted
-// by the router probability (shared expert: sigmoid gate), plus the residual.
-template <int KI, int G>
-__global__ void __launch_bounds__(256) moe_down_kernel(const __grid_constant__ MoeArgs a) {
-    using Q = Q4<KI, G>;
-    extern __shared__ __align__(128) uint8_t dsm[];  // [(topk+1)][CHUNK] then h x4 [(topk+1)][KI]
-    __shared__ __align__(8) uint64_t bar[kMaxTopK + 1];
-    __shared__ int sid[kMaxTopK];
-    __shared__ float sp[kMaxTopK + 1];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nexp = a.topk + 1;
-    const int c = blockIdx.x;
-    float* hs = reinterpret_cast<float*>(dsm + static_cast<size_t>(nexp) * Q::CHUNK);
-    prefetch_l2_share(a.next_w, a.next_bytes, blockIdx.x, gridDim.x, threadIdx.x);
-    if (threadIdx.x == 0) {
-        for (int j = 0; j < nexp; ++j) mbar_init(&bar[j], 1);
-        mbar_fence_init();
-        mbar_arrive_expect_tx(&bar[a.topk], Q::CHUNK);
-        bulk_g2s(dsm + static_cast<size_t>(a.topk) * Q::CHUNK,
-                 a.shared + a.gu_part_bytes + static_cast<int64_t>(c) * Q::CHUNK, Q::CHUNK, &bar[a.topk]);
-    }
-    pdl_wait();
-    if (threadIdx.x < a.topk) {
-        sid[threadIdx.x] = min(max(a.ids[threadIdx.x], 0), a.E - 1);
-        sp[threadIdx.x] = a.probs[threadIdx.x];
-    }
-    if (threadIdx.x == 0) sp[a.topk] = *a.shared_g;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int j = 0; j < a.topk; ++j) {
-            mbar_arrive_expect_tx(&bar[j], Q::CHUNK);
-            bulk_g2s(dsm + static_cast<size_t>(j) * Q::CHUNK,
-                     a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes + a.gu_part_bytes +
-                         static_cast<int64_t>(c) * Q::CHUNK,
-                     Q::CHUNK, &bar[j]);
-        }
-    }
-    for (int t = threadIdx.x; t < nexp * KI; t += 256) {
-        const int j = t / KI, k = t % KI;
-        x4_store<KI>(hs + j * KI, k, a.h[t]);
-    }
-    __syncthreads();
-    pdl_launch_dependents();
-
-    // warp w: output rows 2w, 2w+1 of the chunk
-    const int sub = lane / Q::LPR, vl = lane % Q::LPR;
-    float routed[2] = {0.0f, 0.0f}, shared_v[2] = {0.0f, 0.0f};
-    for (int j = 0; j < nexp; ++j) {
-        const bool ok = mbar_wait_bounded(&bar[j], 0, a.err, nullptr);
-        const uint8_t* chunk = dsm + static_cast<size_t>(j) * Q::CHUNK;
-        const float4* hv = reinterpret_cast<const float4*>(hs + j * KI);
-#pragma unroll
-        for (int p = 0; p < 2; p += Q::RPP) {
-            const int ri = p + sub;
-            float v = 0.0f;
-            if (ri < 2 && ok) v = q4_partial_smem<KI, G>(chunk, 2 * warp + ri, vl, hv);
-            v = lane_group_sum<Q::LPR>(v);
-            if (ri < 2) {
-                if (j < a.topk) routed[ri & 1] = fmaf(sp[j], v, routed[ri & 1]);
-                else shared_v[ri & 1] = v;
-            }
-        }
-    }
-    if (vl == 0) {
-#pragma unroll
-        for (int p = 0; p < 2; ++p) {
-            const int ri = (Q::RPP == 1) ? p : sub;
-            if (Q::RPP != 1 && p > 0) break;
-            if (ri >= 2) continue;
-            const int orow = 16 * c + 2 * warp + ri;
-            a.x_out[orow] = (routed[ri & 1] + sp[a.topk] * shared_v[ri & 1]) + a.x_res[orow];
-        }
-    }
-}
-
-template <int K, int KI, int G>
-static cudaError_t launch_moe_t(const LaunchCfg& lc, const MoeArgs& a0, bool up) {
-    MoeArgs a = a0;
-    if (up) {
-        const int n_items = (a.topk + 1) * a.gu_chunks;
-        int grid = n_items < lc.num_sms ? n_items : lc.num_sms;
-        a.slots = (n_items + grid - 1) / grid;
-        if (a.slots > kMoeMaxSlots) {
-            grid = (n_items + kMoeMaxSlots - 1) / kMoeMaxSlots;
-            a.slots = (n_items + grid - 1) / grid;
-        }
-        const size_t smem = static_cast<size_t>(a.slots) * Q4<K, G>::CHUNK + K * sizeof(float);
-        return launch_kernel(lc, moe_up_kernel<K, G>, dim3(grid), dim3(256), smem, a);
-    }
-    const size_t smem = static_cast<size_t>(a.topk + 1) * (Q4<KI, G>::CHUNK + KI * sizeof(float));
-    return launch_kernel(lc, moe_down_kernel<KI, G>, dim3(a.d_chunks), dim3(256), smem, a);
-}
-
-static MoeArgs moe_args(const Dims& d, const LayerW& w, const Buffers& b) {
-    MoeArgs a{};
-    a.experts = w.experts;
-    a.shared = w.shared;
-    a.expert_bytes = d.expert_bytes;
-    a.gu_part_bytes = static_cast<int64_t>(d.gu_chunks) * d.gu_chunk_bytes;
-    a.gu_chunks = d.gu_chunks;
-    a.d_chunks = d.d_chunks;
-    a.topk = d.topk;
-    a.I = d.I;
-    a.H = d.H;
-    a.E = d.E;
-    a.ids = b.topk_ids;
-    a.probs = b.topk_p;
-    a.shared_g = b.shared_g;
-    a.xn = b.xn;
-    a.h = b.h;
-    a.err = b.err;
-    return a;
-}
-
-static cudaError_t launch_moe(const LaunchCfg& lc, const Dims& d, const MoeArgs& a, bool up) {
-    if (d.G != 64) return cudaErrorInvalidValue;
-    if (d.H == 2048 && d.I == 512) return launch_moe_t<2048, 512, 64>(lc, a, up);
-    if (d.H == 256 && d.I == 128) return launch_moe_t<256, 128, 64>(lc, a, up);
-    if (d.H == 1024 && d.I == 256) return launch_moe_t<1024, 256, 64>(lc, a, up);
-    if (d.H == 2048 && d.I == 256) return launch_moe_t<2048, 256, 64>(lc, a, up);
-    if (d.H == 4096 && d.I == 512) return launch_moe_t<4096, 512, 64>(lc, a, up);
-    return cudaErrorInvalidValue;
-}
+constexpr int kMoeMaxSlots = 16;   // gate/up chunk slots (mbarriers) per CTA
 
 bool moe_supported(int H, int I, int G) {
     return G == 64 && ((H == 2048 && I == 512) || (H == 256 && I == 128) || (H == 1024 && I == 256) ||
                        (H == 2048 && I == 256) || (H == 4096 && I == 512));
 }
 
+// ---------------------------------------------------------------------------------------
+// The whole MoE channel mixer of one layer in one kernel (router -> top-k -> gate/up ->
+// down -> weighted sum + residual), one 512-thread CTA per SM, phases separated by
+// grid-wide flags in global memory (every wait bounded by DM_WAIT_NS):
+//   pre-wait  : router rows of this CTA into registers; shared-expert chunks of this
+//               CTA into shared memory (bulk copies); next layer's input projection into
+//               L2.  Then griddepcontrol.wait, and launch_dependents right away so the
+//               next kernel can start streaming its weights during the MoE latency.
+//   phase 1   : every CTA normalises x_mid (canonical order); CTAs 0..R-1 compute the
+//               router logits (canonical order) and count in; CTA 0 waits for them, runs
+//               the softmax / top-k and publishes ids with a release flag.
+//   issue     : every CTA bulk-copies its routed gate/up chunks and its 16-row down
+//               chunk of every selected expert (the down data lands during phase 2).
+//   phase 2   : gate/up GEMVs, h = SiLU(g) * u to global; grid barrier.
+//   phase 3   : CTAs 0..H/16-1 reduce their 16 output rows over all experts (two warp
+//               groups split the experts, combined in a fixed order) + residual.
+//   exit      : the last CTA out resets the flags for the next launch.
+struct MoeFusedArgs {
+    const uint16_t* Wr;       // [E+1][H] router rows + shared-gate row
+    const uint16_t* gamma;    // post-attention norm
+    float eps;
+    const float* x_mid;       // [H]
+    float* x_out;             // [H]
+    float* xn_out;            // [H] normalised input (written by CTA 0, for inspection)
+    const uint8_t* experts;
+    const uint8_t* shared;
+    int64_t expert_bytes, gu_part_bytes;
+    int E, topk, I, gu_chunks, d_chunks, up_slots;
+    float* logits;            // [E+1]
+    int* ids;
+    float* probs;
+    float* shared_g;
+    float* h;                 // [(topk+1)][I]
+    unsigned* sync;           // [4]: router count, ids flag, up count, exit count
+    const void* next_w;
+    size_t next_bytes;
+    uint32_t* err;
+};
+
+DM_DEV unsigned ld_acquire_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+DM_DEV void st_release_u32(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *p >= target (thread-level; callers use one thread per CTA).
+DM_DEV bool spin_geq(const unsigned* p, unsigned target, uint32_t* err) {
+    if (ld_acquire_u32(p) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t n = 0;
+    while (true) {
+        __nanosleep(32);
+        if (ld_acquire_u32(p) >= target) return true;
+        if (++n % 64 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
+            raise_error(err, DM_DEVERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+constexpr int kMoeThreads = 512;
+
+template <int K, int KI, int G>
+struct MoeFusedSmem {
+    using QU = Q4<K, G>;
+    using QD = Q4<KI, G>;
+    __host__ __device__ static size_t up_off() { return 0; }
+    __host__ __device__ static size_t dn_off(int up_slots) { return static_cast<size_t>(up_slots) * QU::CHUNK; }
+    __host__ __device__ static size_t xn_off(int up_slots, int nexp) { return dn_off(up_slots) + static_cast<size_t>(nexp) * QD::CHUNK; }
+    __host__ __device__ static size_t xs_off(int up_slots, int nexp) { return xn_off(up_slots, nexp) + K * 4; }
+    __host__ __device__ static size_t h_off(int up_slots, int nexp) { return xs_off(up_slots, nexp) + K * 4; }
+    __host__ __device__ static size_t total(int up_slots, int nexp) { return h_off(up_slots, nexp) + static_cast<size_t>(nexp) * KI * 4; }
+};
+
+template <int K, int KI, int G>
+__global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_constant__ MoeFusedArgs a) {
+    using QU = Q4<K, G>;
+    using QD = Q4<KI, G>;
+    using SM = MoeFusedSmem<K, KI, G>;
+    constexpr int VPL = K / 256;
+    extern __shared__ __align__(128) uint8_t dsm[];
+    __shared__ __align__(8) uint64_t bar_up[kMoeMaxSlots];
+    __shared__ __align__(8) uint64_t bar_dn[kMaxTopK + 1];
+    __shared__ int sid[kMaxTopK];
+    __shared__ float sp[kMaxTopK + 1];
+    __shared__ float red[kMoeThreads / 32];
+    __shared__ float dnp[2][16];  // per warp-group partial of routed sums
+    __shared__ float dsh[16];     // shared-expert dots
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int nblk = gridDim.x, c = blockIdx.x;
+    const int nexp = a.topk + 1;
+    const int nrows = a.E + 1;
+    const int R = (nrows + 15) / 16;                 // router CTAs, 16 rows each
+    const int n_items = nexp * a.gu_chunks;
+    const int i0 = static_cast<int>(static_cast<int64_t>(c) * n_items / nblk);
+    const int i1 = static_cast<int>(static_cast<int64_t>(c + 1) * n_items / nblk);
+    const bool has_down = c < a.d_chunks;
+    uint8_t* up_s = dsm + SM::up_off();
+    uint8_t* dn_s = dsm + SM::dn_off(a.up_slots);
+    float* xn4 = reinterpret_cast<float*>(dsm + SM::xn_off(a.up_slots, nexp));
+    float* xsr = reinterpret_cast<float*>(dsm + SM::xs_off(a.up_slots, nexp));
+    float* h4 = reinterpret_cast<float*>(dsm + SM::h_off(a.up_slots, nexp));
+
+    // ---- pre-wait: nothing here depends on the previous kernel ----
+    prefetch_l2_share(a.next_w, a.next_bytes, c, nblk, tid);
+    const int rrow = c * 16 + warp;
+    const bool router_cta = c < R;
+    uint4 wreg[VPL];
+    if (router_cta && warp < 16 && rrow < nrows) {
+        const uint4* wr = reinterpret_cast<const uint4*>(a.Wr + static_cast<size_t>(rrow) * K);
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) wreg[i] = ldg_nc_v4(wr + lane + 32 * i);
+    }
+    if (tid == 0) {
+        for (int k = 0; k < i1 - i0; ++k) mbar_init(&bar_up[k], 1);
+        for (int j = 0; j < nexp; ++j) mbar_init(&bar_dn[j], 1);
+        mbar_fence_init();
+        for (int k = 0; k < i1 - i0; ++k) {
+            const int item = i0 + k;
+            if (item / a.gu_chunks != a.topk) continue;
+            mbar_arrive_expect_tx(&bar_up[k], QU::CHUNK);
+            bulk_g2s(up_s + static_cast<size_t>(k) * QU::CHUNK,
+                     a.shared + static_cast<int64_t>(item % a.gu_chunks) * QU::CHUNK, QU::CHUNK, &bar_up[k]);
+        }
+        if (has_down) {
+            mbar_arrive_expect_tx(&bar_dn[a.topk], QD::CHUNK);
+            bulk_g2s(dn_s + static_cast<size_t>(a.topk) * QD::CHUNK,
+                     a.shared + a.gu_part_bytes + static_cast<int64_t>(c) * QD::CHUNK, QD::CHUNK, &bar_dn[a.topk]);
+        }
+    }
+    pdl_wait();
+    pdl_launch_dependents();
+
+    // ---- phase 1: canonical RMSNorm (512 threads), router rows ----
+    {
+        constexpr int XPT = (K + kMoeThreads - 1) / kMoeThreads;
+        float xv[XPT];
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < XPT; ++i) {
+            const int k = i * kMoeThreads + tid;
+            xv[i] = k < K ? a.x_mid[k] : 0.0f;
+            if (k < K) acc = __fmaf_rn(xv[i], xv[i], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) red[warp] = acc;
+        __syncthreads();
+        float ss = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kMoeThreads / 32; ++w) ss = __fadd_rn(ss, red[w]);
+        const float denom = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), a.eps));
+#pragma unroll
+        for (int i = 0; i < XPT; ++i) {
+            const int k = i * kMoeThreads + tid;
+            if (k < K) {
+                const float y = __fmul_rn(__fdiv_rn(xv[i], denom), bf16_to_f32(a.gamma[k]));
+                x4_store<K>(xn4, k, y);
+                xs_store_split(xsr, K, k, y);
+                if (c == 0 && a.xn_out) a.xn_out[k] = y;
+            }
+        }
+    }
+    __syncthreads();
+    if (router_cta) {
+        if (rrow < nrows) {
+            const float4* xlo = reinterpret_cast<const float4*>(xsr);
+            const float4* xhi = reinterpret_cast<const float4*>(xsr + K / 2);
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < VPL; ++i) {
+                const int j = lane + 32 * i;
+                const uint4 w = wreg[i];
+                const float4 x0 = xlo[j], x1 = xhi[j];
+                acc = __fmaf_rn(bf16lo(w.x), x0.x, acc);
+                acc = __fmaf_rn(bf16hi(w.x), x0.y, acc);
+                acc = __fmaf_rn(bf16lo(w.y), x0.z, acc);
+                acc = __fmaf_rn(bf16hi(w.y), x0.w, acc);
+                acc = __fmaf_rn(bf16lo(w.z), x1.x, acc);
+                acc = __fmaf_rn(bf16hi(w.z), x1.y, acc);
+                acc = __fmaf_rn(bf16lo(w.w), x1.z, acc);
+                acc = __fmaf_rn(bf16hi(w.w), x1.w, acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) __stcg(a.logits + rrow, acc);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            atomicAdd(&a.sync[0], 1u);
+        }
+    }
+    if (c == 0) {
+        if (tid == 0) spin_geq(&a.sync[0], static_cast<unsigned>(R), a.err);
+        __syncthreads();
+        if (warp == 0) {
+            // softmax + top-k (canonical order), probabilities staged in shared memory
+            float* pe = h4;  // free until phase 3
+            const int E = a.E;
+            float m = -INFINITY;
+            for (int e = lane; e < E; e += 32) m = fmaxf(m, __ldcg(a.logits + e));
+            m = warp_max(m);
+            float s = 0.0f;
+            for (int e = lane; e < E; e += 32) {
+                const float ev = dm_det_exp(DM_DET_SUB(__ldcg(a.logits + e), m));
+                pe[e] = ev;
+                s = DM_DET_ADD(s, ev);
+            }
+            s = warp_sum(s);
+            const float inv = DM_DET_DIV(1.0f, s);
+            for (int e = lane; e < E; e += 32) pe[e] = DM_DET_MUL(pe[e], inv);
+            __syncwarp();
+            for (int r = 0; r < a.topk; ++r) {
+                float bv = -1.0f;
+                int bi = 0x7fffffff;
+                for (int e = lane; e < E; e += 32)
+                    if (pe[e] > bv) { bv = pe[e]; bi = e; }
+#pragma unroll
+                for (int mm = 16; mm >= 1; mm >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, mm);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, mm);
+                    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                }
+                if (bi < 0 || bi >= E) {
+                    if (lane == 0) raise_error(a.err, DM_DEVERR_NONFINITE);
+                    bi = r;
+                    bv = 0.0f;
+                }
+                if (lane == 0) {
+                    a.ids[r] = bi;
+                    a.probs[r] = bv;
+                    sid[r] = bi;
+                    sp[r] = bv;
+                    pe[bi] = -2.0f;
+                }
+                __syncwarp();
+            }
+            if (lane == 0) {
+                const float sgv = sigmoid_f(__ldcg(a.logits + E));
+                *a.shared_g = sgv;
+                sp[a.topk] = sgv;
+                if (s != s || isinf(s)) raise_error(a.err, DM_DEVERR_NONFINITE);
+                __threadfence();
+                st_release_u32(&a.sync[1], 1u);
+            }
+        }
+        __syncthreads();
+    } else {
+        if (tid == 0) spin_geq(&a.sync[1], 1u, a.err);
+        __syncthreads();
+        if (tid < a.topk) {
+            sid[tid] = min(max(__ldcg(a.ids + tid), 0), a.E - 1);
+            sp[tid] = __ldcg(a.probs + tid);
+        }
+        if (tid == 0) sp[a.topk] = __ldcg(a.shared_g);
+        __syncthreads();
+    }
+
+    // ---- issue the routed chunks: gate/up items and this CTA's down chunk ----
+    if (tid == 0) {
+        for (int k = 0; k < i1 - i0; ++k) {
+            const int item = i0 + k;
+            const int j = item / a.gu_chunks;
+            if (j == a.topk) continue;
+            mbar_arrive_expect_tx(&bar_up[k], QU::CHUNK);
+            bulk_g2s(up_s + static_cast<size_t>(k) * QU::CHUNK,
+                     a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes +
+                         static_cast<int64_t>(item % a.gu_chunks) * QU::CHUNK,
+                     QU::CHUNK, &bar_up[k]);
+        }
+        if (has_down) {
+            for (int j = 0; j < a.topk; ++j) {
+                mbar_arrive_expect_tx(&bar_dn[j], QD::CHUNK);
+                bulk_g2s(dn_s + static_cast<size_t>(j) * QD::CHUNK,
+                         a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes + a.gu_part_bytes +
+                             static_cast<int64_t>(c) * QD::CHUNK,
+                         QD::CHUNK, &bar_dn[j]);
+            }
+        }
+    }
+
+    // ---- phase 2: gate/up; two warp groups take alternate items ----
+    {
+        const float4* xv4 = reinterpret_cast<const float4*>(xn4);
+        const int wgrp = warp >> 3, wg = warp & 7;
+        for (int k = wgrp; k < i1 - i0; k += 2) {
+            const int item = i0 + k;
+            const int j = item / a.gu_chunks, cc = item % a.gu_chunks;
+            const bool ok = mbar_wait_bounded(&bar_up[k], 0, a.err, nullptr);
+            const uint8_t* chunk = up_s + static_cast<size_t>(k) * QU::CHUNK;
+            float dots[2];
+#pragma unroll
+            for (int p = 0; p < 2; p += QU::RPP) {
+                const int sub = lane / QU::LPR, vl = lane % QU::LPR;
+                const int ri = p + sub;
+                float v = 0.0f;
+                if (ri < 2 && ok) v = q4_partial_smem<K, G>(chunk, ri == 0 ? wg : 8 + wg, vl, xv4);
+                v = lane_group_sum<QU::LPR>(v);
+                if (QU::RPP == 1) dots[p] = v;
+                else {
+                    const float other = __shfl_sync(0xffffffffu, v, QU::LPR);
+                    dots[0] = __shfl_sync(0xffffffffu, v, 0);
+                    dots[1] = other;
+                }
+            }
+            if (lane == 0) __stcg(a.h + j * a.I + 8 * cc + wg, silu_f(dots[0]) * dots[1]);
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        atomicAdd(&a.sync[2], 1u);
+        spin_geq(&a.sync[2], static_cast<unsigned>(nblk), a.err);
+    }
+    __syncthreads();
+
+    // ---- phase 3: 16 output rows of every selected expert + residual ----
+    if (has_down) {
+        for (int t = tid; t < nexp * KI; t += kMoeThreads) {
+            const int j = t / KI, k = t % KI;
+            x4_store<KI>(h4 + j * KI, k, __ldcg(a.h + t));
+        }
+        __syncthreads();
+        const int wgrp = warp >> 3, wg = warp & 7;
+        const int sub = lane / QD::LPR, vl = lane % QD::LPR;
+        float routed[2] = {0.0f, 0.0f}, shv[2] = {0.0f, 0.0f};
+        for (int j = wgrp; j < nexp; j += 2) {
+            const bool ok = mbar_wait_bounded(&bar_dn[j], 0, a.err, nullptr);
+            const uint8_t* chunk = dn_s + static_cast<size_t>(j) * QD::CHUNK;
+            const float4* hv = reinterpret_cast<const float4*>(h4 + j * KI);
+#pragma unroll
+            for (int p = 0; p < 2; p += QD::RPP) {
+                const int ri = p + sub;
+                float v = 0.0f;
+                if (ri < 2 && ok) v = q4_partial_smem<KI, G>(chunk, 2 * wg + ri, vl, hv);
+                v = lane_group_sum<QD::LPR>(v);
+                if (ri < 2) {
+                    if (j < a.topk) routed[ri] = fmaf(sp[j], v, routed[ri]);
+                    else shv[ri] = v;
+                }
+            }
+        }
+        if (vl == 0) {
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                const int ri = (QD::RPP == 1) ? p : sub;
+                if (QD::RPP != 1 && p > 0) break;
+                if (ri >= 2) continue;
+                dnp[wgrp][2 * wg + ri] = routed[ri];
+                if ((a.topk & 1) == wgrp) dsh[2 * wg + ri] = shv[ri];
+            }
+        }
+        __syncthreads();
+        if (tid < 16) {
+            const int orow = 16 * c + tid;
+            a.x_out[orow] = ((dnp[0][tid] + dnp[1][tid]) + sp[a.topk] * dsh[tid]) + a.x_mid[orow];
+        }
+    } else {
+        // no down rows here: drain this CTA's own shared-expert chunk copies (none issued)
+    }
+
+    // ---- exit: the last CTA resets the flags for the next launch ----
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(&a.sync[3], 1u);
+        if (prev == static_cast<unsigned>(nblk) - 1) {
+            a.sync[0] = 0u;
+            a.sync[1] = 0u;
+            a.sync[2] = 0u;
+            a.sync[3] = 0u;
+            __threadfence();
+        }
+    }
+}
+
+template <int K, int KI, int G>
+static cudaError_t launch_moe_fused_t(const LaunchCfg& lc, MoeFusedArgs a) {
+    const int nexp = a.topk + 1;
+    const int grid = lc.num_sms;
+    const int n_items = nexp * a.gu_chunks;
+    a.up_slots = (n_items + grid - 1) / grid;
+    if (a.up_slots > kMoeMaxSlots || a.d_chunks > grid || (a.E + 16) / 16 > grid) return cudaErrorInvalidValue;
+    const size_t smem = MoeFusedSmem<K, KI, G>::total(a.up_slots, nexp);
+    return launch_kernel(lc, moe_fused_kernel<K, KI, G>, dim3(grid), dim3(kMoeThreads), smem, a);
+}
+
+cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot,
+                             const void* next_w, size_t next_bytes) {
+    MoeFusedArgs a{};
+    a.Wr = w.w_router;
+    a.gamma = w.post_norm;
+    a.eps = d.eps;
+    a.x_mid = b.xmid + static_cast<size_t>(slot) * d.H;
+    a.x_out = b.xres + static_cast<size_t>(slot) * d.H;
+    a.xn_out = b.xn;
+    a.experts = w.experts;
+    a.shared = w.shared;
+    a.expert_bytes = d.expert_bytes;
+    a.gu_part_bytes = static_cast<int64_t>(d.gu_chunks) * d.gu_chunk_bytes;
+    a.E = d.E;
+    a.topk = d.topk;
+    a.I = d.I;
+    a.gu_chunks = d.gu_chunks;
+    a.d_chunks = d.d_chunks;
+    a.logits = b.rlogits;
+    a.ids = b.topk_ids;
+    a.probs = b.topk_p;
+    a.shared_g = b.shared_g;
+    a.h = b.h;
+    a.sync = b.counters + kCntMoeSync;
+    a.next_w = next_w;
+    a.next_bytes = next_bytes;
+    a.err = b.err;
+    if (d.G != 64) return cudaErrorInvalidValue;
+    if (d.H == 2048 && d.I == 512) return launch_moe_fused_t<2048, 512, 64>(lc, a);
+    if (d.H == 256 && d.I == 128) return launch_moe_fused_t<256, 128, 64>(lc, a);
+    if (d.H == 1024 && d.I == 256) return launch_moe_fused_t<1024, 256, 64>(lc, a);
+    if (d.H == 2048 && d.I == 256) return launch_moe_fused_t<2048, 256, 64>(lc, a);
+    if (d.H == 4096 && d.I == 512) return launch_moe_fused_t<4096, 512, 64>(lc, a);
+    return cudaErrorInvalidValue;
+}
+
 #define DM_MOE_INSTANCES(X) X(2048, 512) X(256, 128) X(1024, 256) X(2048, 256) X(4096, 512)
 
 cudaError_t moe_set_attrs() {
     cudaError_t e = cudaSuccess;
-#define DM_MOE_ATTR(KK, II)                                                                           \
-    if (e == cudaSuccess)                                                                             \
-        e = cudaFuncSetAttribute(moe_up_kernel<KK, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
-                                 kMoeMaxSlots * Q4<KK, 64>::CHUNK + KK * 4 > 200 * 1024                \
-                                     ? 200 * 1024                                                     \
-                                     : kMoeMaxSlots * Q4<KK, 64>::CHUNK + KK * 4);                    \
-    if (e == cudaSuccess)                                                                             \
-        e = cudaFuncSetAttribute(moe_down_kernel<II, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                 (kMaxTopK + 1) * (Q4<II, 64>::CHUNK + II * 4));
-    DM_MOE_INSTANCES(DM_MOE_ATTR)
-#undef DM_MOE_ATTR
+#define DM_MOE_FUSED_ATTR(KK, II)                                                                        \
+    if (e == cudaSuccess)                                                                                \
+        e = cudaFuncSetAttribute(moe_fused_kernel<KK, II, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 200 * 1024);
+    DM_MOE_INSTANCES(DM_MOE_FUSED_ATTR)
+#undef DM_MOE_FUSED_ATTR
     return e;
-}
-
-cudaError_t launch_moe_up(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b) {
-    return launch_moe(lc, d, moe_args(d, w, b), true);
-}
-
-cudaError_t launch_moe_down(const LaunchCfg& lc, const Dims& d, const LayerW& w,
-                            const Buffers& b, const float* x_res, float* x_out, const void* next_w,
-                            size_t next_bytes) {
-    MoeArgs a = moe_args(d, w, b);
-    a.x_res = x_res;
-    a.x_out = x_out;
-    a.next_w = next_w;
-    a.next_bytes = next_bytes;
-    return launch_moe(lc, d, a, false);
 }
 
 // ---------------------------------------------------------------------------------------

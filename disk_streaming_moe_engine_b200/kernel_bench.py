@@ -20,8 +20,8 @@ from .config import RuntimeConfig, preset
 from .engine import Engine
 
 KERNELS = {"in_proj": _lib.DM_KERNEL_MIXER_IN, "out_proj": _lib.DM_KERNEL_MIXER_OUT,
-           "core": _lib.DM_KERNEL_MIXER_CORE, "router": _lib.DM_KERNEL_ROUTER, "moe_up": _lib.DM_KERNEL_MOE_UP,
-           "moe_down": _lib.DM_KERNEL_MOE_DOWN, "head": _lib.DM_KERNEL_HEAD}
+           "core": _lib.DM_KERNEL_MIXER_CORE, "router": _lib.DM_KERNEL_ROUTER, "moe": _lib.DM_KERNEL_MOE,
+           "head": _lib.DM_KERNEL_HEAD}
 
 
 def main():

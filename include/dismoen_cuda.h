@@ -287,9 +287,8 @@ int32_t dm_kernels_per_step(dm_ctx* ctx, int32_t* out);
 #define DM_KERNEL_MIXER_IN 0   /* GDN or attention input projection GEMV (+RMSNorm)     */
 #define DM_KERNEL_MIXER_OUT 1  /* output projection GEMV (+head norm / gate, residual)  */
 #define DM_KERNEL_MIXER_CORE 2 /* GDN recurrence or paged decode attention              */
-#define DM_KERNEL_ROUTER 3
-#define DM_KERNEL_MOE_UP 4
-#define DM_KERNEL_MOE_DOWN 5
+#define DM_KERNEL_ROUTER 3     /* router + top-k alone (the dm_router kernel)           */
+#define DM_KERNEL_MOE 4        /* the whole MoE mixer: router, experts, residual        */
 #define DM_KERNEL_HEAD 6
 int32_t dm_time_kernel(dm_ctx* ctx, int32_t which, int32_t layer, int32_t iters, float* avg_ms,
                        uint64_t* bytes);
