@@ -51,6 +51,7 @@ def parse():
     ap.add_argument("--seed", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
+    ap.add_argument("--timeline", default="", help="also trace one decode step; write its launch timeline here")
     return ap.parse_args()
 
 
@@ -207,6 +208,34 @@ def cpu_sample(cfg_full, seed: int, ctx_len: int, steps: int):
             "steps": steps}
 
 
+def step_timeline(eng, steps: int):
+    """Traces `steps` decode steps (graph recaptured with timeline records) and returns the
+    last step's launches plus, per kernel kind, its share of the step's critical path: the
+    interval end[i-1] -> end[i] is charged to launch i."""
+    eng.trace_enable(True)
+    eng.enqueue_decode(steps)
+    eng.sync()
+    tl = eng.trace_timeline()
+    eng.trace_enable(False)
+    t0 = tl[0][2]
+    rows = [{"kind": k, "layer": l, "start_us": (s0 - t0) / 1e3, "ready_us": (r - t0) / 1e3, "end_us": (e - t0) / 1e3}
+            for (k, l, s0, r, e) in tl]
+    by = {}
+    prev_end = rows[0]["start_us"]
+    for r in rows:
+        d = by.setdefault(r["kind"], {"n": 0, "path_us": 0.0, "span_us": 0.0})
+        d["n"] += 1
+        d["path_us"] += max(r["end_us"] - prev_end, 0.0)
+        d["span_us"] += r["end_us"] - r["start_us"]
+        prev_end = max(prev_end, r["end_us"])
+    total = rows[-1]["end_us"] - rows[0]["start_us"]
+    for d in by.values():
+        d["path_us"] = round(d["path_us"], 1)
+        d["span_us"] = round(d["span_us"], 1)
+        d["path_share"] = round(d["path_us"] / total, 3)
+    return {"step_us": total, "by_kind": by, "launches": rows}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
@@ -320,6 +349,12 @@ def run_ours(args, rank, local, world):
                "sample": f"oracle/liboracle.so on host cores: one full-shape [GDN,GDN,GDN,Attn] cycle + lm_head, "
                          f"median of {s['steps']} tokens at ctx {args.prompt_len}; token = 10 x cycle + head"}
 
+    timeline = None
+    if args.timeline:
+        timeline = step_timeline(eng, 3)
+        with open(args.timeline, "w") as f:
+            json.dump(timeline, f)
+        timeline = timeline["by_kind"]
     kps = eng.kernels_per_step()
     c = clocks.summary()
     line = {
@@ -341,6 +376,7 @@ def run_ours(args, rank, local, world):
         "clocks": c,
         "clocks_e2e": clocks_e2e.summary(),
         "gpu_launches": kps * args.steps,
+        "timeline_by_kind": timeline,
         "prefill_s": round(prefill_s, 2),
     }
     eng.close()

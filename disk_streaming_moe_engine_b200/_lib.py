@@ -92,6 +92,9 @@ SIGNATURES = {
     "dm_sync": (I32, [P]),
     "dm_get_stream": (I32, [P, C.POINTER(P)]),
     "dm_kernels_per_step": (I32, [P, C.POINTER(I32)]),
+    "dm_trace_enable": (I32, [P, I32]),
+    "dm_trace_read": (I32, [P, P, I32]),
+    "dm_trace_timeline": (I32, [P, P, P, I32, C.POINTER(I32)]),
     "dm_time_kernel": (I32, [P, I32, I32, I32, C.POINTER(F32), C.POINTER(U64)]),
     "dm_synth_bf16": (I32, [U64, U64, U64, F32, F32, P]),
     "dm_synth_f32": (I32, [U64, U64, U64, F32, F32, P]),

@@ -72,6 +72,10 @@ struct dm_ctx {
     std::vector<int> att_len;          // [n_att * max_seqs]
     std::vector<int> dev_pos_valid;    // device pos[slot] == slot_len[slot]
     std::vector<cudaGraphExec_t> graphs;  // decode step per slot
+    uint64_t* trace_buf = nullptr;
+    uint64_t* ktrace_buf = nullptr;
+    int trace_n = 0;
+    std::vector<int> trace_kinds;
     std::string last_error;
 };
 
@@ -251,6 +255,8 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t o_xn = T(H * 4), o_rl = T((d.E + 1) * 4), o_ids = T(kMaxTopK * 4), o_p = T(kMaxTopK * 4);
     const size_t o_sg = T(4), o_h = T(static_cast<size_t>(d.topk + 1) * d.I * 4), o_logits = T(static_cast<size_t>(d.V) * 4);
     const size_t o_cv = T(kMaxCtas * 4), o_ci = T(kMaxCtas * 4), o_cnt = T(64 * 4), o_err = T(4);
+    const size_t o_trace = T(kTraceSlots * 8);
+    const size_t o_ktrace = T(kMaxTraceKernels * 4 * 8);
     const size_t o_rope = T(static_cast<size_t>(d.max_pages) * kPageTokens * (d.rot_dim / 2) * 8);
     const size_t o_sq = T(static_cast<size_t>(d.I) * H / 2), o_ss = T(static_cast<size_t>(d.I) * H / d.G * 2),
                  o_sz = T(static_cast<size_t>(d.I) * H / d.G / 2 + 16);
@@ -317,13 +323,28 @@ static int plan_memory(dm_ctx* c, bool commit) {
     b.counters = reinterpret_cast<unsigned*>(A + o_cnt);
     b.err = reinterpret_cast<uint32_t*>(A + o_err);
     b.rope = reinterpret_cast<float2*>(A + o_rope);
+    b.trace = nullptr;  // off until dm_trace_enable
+    c->trace_buf = reinterpret_cast<uint64_t*>(A + o_trace);
+    c->ktrace_buf = reinterpret_cast<uint64_t*>(A + o_ktrace);
+    b.ktrace = nullptr;
     c->stage_q = A + o_sq;
     c->stage_s = reinterpret_cast<uint16_t*>(A + o_ss);
     c->stage_z = A + o_sz;
     return DM_OK;
 }
 
-static LaunchCfg lcfg(const dm_ctx* c) { return LaunchCfg{c->stream, c->num_sms, true}; }
+static LaunchCfg lcfg(const dm_ctx* c) { return LaunchCfg{c->stream, c->num_sms, true, nullptr}; }
+
+// Launch config for the next kernel of a traced sequence (timeline record n of kind k).
+static LaunchCfg lcfg_traced(dm_ctx* c, int kind, int layer) {
+    LaunchCfg lc = lcfg(c);
+    if (c->b.ktrace && c->trace_n < kMaxTraceKernels) {
+        lc.kt = c->b.ktrace + 4 * c->trace_n;
+        c->trace_kinds.push_back((kind << 16) | (layer & 0xFFFF));
+        ++c->trace_n;
+    }
+    return lc;
+}
 
 // Reads and clears the device error word; maps it to a status.
 static int check_device_error(dm_ctx* c, const char* stage) {
@@ -812,21 +833,19 @@ int32_t dm_gdn_state_export(dm_ctx* c, int32_t g, int32_t slot, float* S_host, f
 
 // ---- compute ------------------------------------------------------------------------
 static cudaError_t enqueue_mixer(dm_ctx* c, int layer, int slot) {
-    const LaunchCfg lc = lcfg(c);
     const LayerW& w = c->layers[layer];
     cudaError_t e;
     if (w.is_attn) {
-        if ((e = launch_attn_in(lc, c->d, w, c->b, slot)) != cudaSuccess) return e;
-        if ((e = launch_attn_decode(lc, c->d, w, c->b, slot)) != cudaSuccess) return e;
-        return launch_attn_out(lc, c->d, w, c->b, slot);
+        if ((e = launch_attn_in(lcfg_traced(c, TK_ATTN_IN, layer), c->d, w, c->b, slot)) != cudaSuccess) return e;
+        if ((e = launch_attn_decode(lcfg_traced(c, TK_ATTN, layer), c->d, w, c->b, slot)) != cudaSuccess) return e;
+        return launch_attn_out(lcfg_traced(c, TK_ATTN_OUT, layer), c->d, w, c->b, slot);
     }
-    if ((e = launch_gdn_in(lc, c->d, w, c->b, slot)) != cudaSuccess) return e;
-    if ((e = launch_gdn_rec(lc, c->d, w, c->b, slot)) != cudaSuccess) return e;
-    return launch_gdn_out(lc, c->d, w, c->b, slot);
+    if ((e = launch_gdn_in(lcfg_traced(c, TK_GDN_IN, layer), c->d, w, c->b, slot)) != cudaSuccess) return e;
+    if ((e = launch_gdn_rec(lcfg_traced(c, TK_GDN_REC, layer), c->d, w, c->b, slot)) != cudaSuccess) return e;
+    return launch_gdn_out(lcfg_traced(c, TK_GDN_OUT, layer), c->d, w, c->b, slot);
 }
 
 static cudaError_t enqueue_moe(dm_ctx* c, int layer, int slot) {
-    const LaunchCfg lc = lcfg(c);
     const LayerW& w = c->layers[layer];
     // the next layer's input projection is the next large stream: start it into L2
     const void* next_w = nullptr;
@@ -836,17 +855,19 @@ static cudaError_t enqueue_moe(dm_ctx* c, int layer, int slot) {
         next_w = nw.w_in;
         next_bytes = static_cast<size_t>(nw.is_attn ? c->d.attn_in_rows : c->d.gdn_in_rows) * c->d.H * 2;
     }
-    return launch_moe_fused(lc, c->d, w, c->b, slot, next_w, next_bytes);
+    return launch_moe_fused(lcfg_traced(c, TK_MOE, layer), c->d, w, c->b, slot, next_w, next_bytes);
 }
 
 static cudaError_t enqueue_step(dm_ctx* c, int slot) {
-    const LaunchCfg lc = lcfg(c);
-    cudaError_t e = launch_embed(lc, c->d, c->embed, c->b, slot);
+    c->trace_n = 0;
+    c->trace_kinds.clear();
+    cudaError_t e = launch_embed(lcfg_traced(c, TK_EMBED, 0), c->d, c->embed, c->b, slot);
     for (int l = 0; l < c->d.L && e == cudaSuccess; ++l) {
         e = enqueue_mixer(c, l, slot);
         if (e == cudaSuccess) e = enqueue_moe(c, l, slot);
     }
-    if (e == cudaSuccess) e = launch_head(lc, c->d, c->final_norm, c->lm_head, c->b, slot, 1, 1);
+    if (e == cudaSuccess)
+        e = launch_head(lcfg_traced(c, TK_HEAD, c->d.L), c->d, c->final_norm, c->lm_head, c->b, slot, 1, 1);
     return e;
 }
 
@@ -1063,6 +1084,42 @@ int32_t dm_router(dm_ctx* c, int32_t layer, const float* x, int32_t n, int32_t* 
         DM_CUDA(c, cudaStreamSynchronize(c->stream), "router");
     }
     return check_device_error(c, "router");
+}
+
+// ---- phase tracing --------------------------------------------------------------------
+int32_t dm_trace_enable(dm_ctx* c, int32_t on) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "trace");
+    DM_CUDA(c, cudaMemset(c->trace_buf, 0, kTraceSlots * 8), "trace");
+    DM_CUDA(c, cudaMemset(c->ktrace_buf, 0, kMaxTraceKernels * 4 * 8), "trace");
+    c->b.trace = on ? c->trace_buf : nullptr;
+    c->b.ktrace = on ? c->ktrace_buf : nullptr;
+    for (auto& g : c->graphs)  // captured graphs hold the old pointer: recapture lazily
+        if (g) {
+            cudaGraphExecDestroy(g);
+            g = nullptr;
+        }
+    return DM_OK;
+}
+
+int32_t dm_trace_read(dm_ctx* c, uint64_t* out_host, int32_t n) {
+    if (!c || !out_host || n <= 0 || n > kTraceSlots) return DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "trace");
+    DM_CUDA(c, cudaMemcpy(out_host, c->trace_buf, static_cast<size_t>(n) * 8, cudaMemcpyDeviceToHost), "trace");
+    return DM_OK;
+}
+
+int32_t dm_trace_timeline(dm_ctx* c, uint64_t* rec_host, int32_t* kinds_host, int32_t n, int32_t* count) {
+    if (!c || !rec_host || !kinds_host || !count || n <= 0) return DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "trace");
+    const int m = std::min(n, c->trace_n);
+    DM_CUDA(c, cudaMemcpy(rec_host, c->ktrace_buf, static_cast<size_t>(m) * 4 * 8, cudaMemcpyDeviceToHost), "trace");
+    for (int i = 0; i < m; ++i) kinds_host[i] = c->trace_kinds[i];
+    *count = m;
+    return DM_OK;
 }
 
 // ---- kernel timing (roofline measurement) ----------------------------------------------

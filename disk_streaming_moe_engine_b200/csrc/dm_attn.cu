@@ -39,31 +39,12 @@ struct AttnArgs {
     float* out;               // [Hq*D]
     unsigned* counters;       // [Hkv]
     const float2* rope;       // [capacity][rot_dim/2] (cos, sin)
+    uint64_t* trace;          // phase stamps (CTA (0, last split), thread 0) or null
+    uint64_t* kt;             // launch timeline record or null
     const void* next_w;       // o_proj weights, prefetched into L2
     size_t next_bytes;
     uint32_t* err;
 };
-
-// Loads the RMS-normalised, rotated head vector `src` (length D) into dst (smem).
-// cs: the position's row of the RoPE table, (cos, sin) of fp32(pos) * inv_freq_i.
-template <int D>
-__device__ __forceinline__ void norm_rope_head(const float* src, const uint16_t* w, float* dst,
-                                               int lane, int rot_dim, float eps, const float2* cs) {
-    float ss = 0.0f;
-    for (int d = lane; d < D; d += 32) ss = fmaf(src[d], src[d], ss);
-    ss = warp_sum(ss);
-    const float rs = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
-    for (int d = lane; d < D; d += 32) dst[d] = src[d] * rs * bf16_to_f32(w[d]);
-    __syncwarp();
-    const int half = rot_dim / 2;
-    for (int i = lane; i < half; i += 32) {
-        const float2 c = cs[i];
-        const float x0 = dst[i], x1 = dst[i + half];
-        dst[i] = x0 * c.x - x1 * c.y;
-        dst[i + half] = x0 * c.y + x1 * c.x;
-    }
-    __syncwarp();
-}
 
 // RoPE table [capacity][rot_dim / 2] of (cos, sin) of fp32(pos) * inv_freq_i with
 // inv_freq_i = 1 / theta^(2i / rot_dim) (reference attention.mojo:318-354), filled once
@@ -115,6 +96,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     const int g = blockIdx.x, s = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
 
+    uint64_t* tr = (tid == 0 && g == 0 && s == gridDim.y - 1) ? a.trace : nullptr;
+    trace_stamp(tr, 0);
+    kt_start(a.kt);
     // positions < pos were written by earlier steps and the page table is fixed: the
     // range of this split and its first page tiles do not depend on the previous kernel
     const int pos = *a.pos;
@@ -155,35 +139,63 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         m_run[tid] = -INFINITY;
         l_run[tid] = 0.0f;
     }
+    __shared__ float qn_s[D], kn_s[D];
+    __shared__ float2 cs_s[D / 2];
+    for (int i = tid; i < D; i += 128) {
+        qn_s[i] = bf16_to_f32(a.q_norm[i]);
+        kn_s[i] = bf16_to_f32(a.k_norm[i]);
+    }
+    if (in_range)
+        for (int i = tid; i < a.rot_dim / 2; i += 128) cs_s[i] = a.rope[static_cast<size_t>(pos) * (a.rot_dim / 2) + i];
+    trace_stamp(tr, 1);
     pdl_wait();
+    kt_ready(a.kt);
+    trace_stamp(tr, 2);
     if (!in_range) {  // no room: report, touch nothing
         if (tid == 0 && s == 0) raise_error(a.err, DM_DEVERR_CAPACITY);
+        kt_end(a.kt);
         return;
     }
 
-    const float2* cs_row = a.rope + static_cast<size_t>(pos) * (a.rot_dim / 2);
-    // ---- q heads of this KV group, new k, new v ----
-    for (int hh = warp; hh < GRP; hh += 4)
-        norm_rope_head<D>(a.qg + static_cast<size_t>(g * GRP + hh) * D, a.q_norm, qsm[hh], lane,
-                          a.rot_dim, a.eps, cs_row);
-    if (warp == 0) {
-        norm_rope_head<D>(a.kvnew + static_cast<size_t>(g) * D, a.k_norm, knew, lane, a.rot_dim,
-                          a.eps, cs_row);
-        for (int d = lane; d < D; d += 32) {
-            const uint16_t kb = f32_to_bf16(knew[d]);
-            kbits[d] = kb;
-            knew[d] = bf16_to_f32(kb);
+    // ---- q heads of this KV group, new k, new v: one parallel load, then per-head
+    // RMSNorm + RoPE in shared memory (norm weights and the RoPE row were staged before
+    // the wait) ----
+    for (int i = tid; i < GRP * D; i += 128) qsm[i / D][i % D] = a.qg[static_cast<size_t>(g * GRP) * D + i];
+    for (int i = tid; i < D; i += 128) {
+        knew[i] = a.kvnew[static_cast<size_t>(g) * D + i];
+        vnew[i] = a.kvnew[static_cast<size_t>(a.Hkv + g) * D + i];
+    }
+    __syncthreads();
+    for (int hh = warp; hh < GRP + 1; hh += 4) {
+        float* v = hh < GRP ? qsm[hh] : knew;
+        const float* wn = hh < GRP ? qn_s : kn_s;
+        float ss = 0.0f;
+        for (int d = lane; d < D; d += 32) ss = fmaf(v[d], v[d], ss);
+        ss = warp_sum(ss);
+        const float rs = 1.0f / sqrtf(ss / static_cast<float>(D) + a.eps);
+        for (int d = lane; d < D; d += 32) v[d] = v[d] * rs * wn[d];
+        __syncwarp();
+        const int half = a.rot_dim / 2;
+        for (int i = lane; i < half; i += 32) {
+            const float2 c = cs_s[i];
+            const float x0 = v[i], x1 = v[i + half];
+            v[i] = x0 * c.x - x1 * c.y;
+            v[i + half] = x0 * c.y + x1 * c.x;
         }
-    } else if (warp == 1) {
-        const float* vsrc = a.kvnew + static_cast<size_t>(a.Hkv + g) * D;
-        for (int d = lane; d < D; d += 32) {
-            const uint16_t vb = f32_to_bf16(vsrc[d]);
-            vbits[d] = vb;
-            vnew[d] = bf16_to_f32(vb);
-        }
+        __syncwarp();
+    }
+    __syncthreads();
+    for (int d = tid; d < D; d += 128) {
+        const uint16_t kb = f32_to_bf16(knew[d]);
+        kbits[d] = kb;
+        knew[d] = bf16_to_f32(kb);
+        const uint16_t vb = f32_to_bf16(vnew[d]);
+        vbits[d] = vb;
+        vnew[d] = bf16_to_f32(vb);
     }
     __syncthreads();
     pdl_launch_dependents();
+    trace_stamp(tr, 3);
 
     // ---- append at pos (one CTA per KV head) ----
     if (s == 0) {
@@ -284,6 +296,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         if (tid == 0 && i + kAttnStages < np) issue(i + kAttnStages);
     }
 
+    trace_stamp(tr, 4);
     // ---- merge 1: the kAttnCluster splits of this cluster through distributed shared
     // memory: every CTA pushes its partial into rank 0's (free) ring, rank 0 merges
     // locally and writes one partial (max, sum, acc) per head for the cluster ----
@@ -308,7 +321,11 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     const int ccount = gridDim.y / kAttnCluster;   // clusters per KV head
     const int cid = s / kAttnCluster;
     cluster.sync();                                    // all partials are in rank 0
-    if (crank != 0) return;
+    trace_stamp(tr, 5);
+    if (crank != 0) {
+        kt_end(a.kt);
+        return;
+    }
     {
         const float* P = reinterpret_cast<const float*>(ring);
         __shared__ float cw[GRP][kAttnCluster];
@@ -350,7 +367,11 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         is_last = (prev == static_cast<unsigned>(ccount) - 1);
     }
     __syncthreads();
-    if (!is_last) return;
+    trace_stamp(tr, 6);
+    if (!is_last) {
+        kt_end(a.kt);
+        return;
+    }
     __threadfence();
 
     // ---- merge 2: the cluster partials of every head of this KV group, output gate ----
@@ -375,6 +396,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         a.out[static_cast<size_t>(hq) * D + d] = acc2 * sigmoid_f(gate);
     }
     if (tid == 0) a.counters[g] = 0u;
+    if (tid == 0 && a.trace) a.trace[7] = globaltimer_ns();
+    __syncthreads();
+    kt_end(a.kt);
 }
 
 size_t attn_ring_bytes(int D) {
@@ -436,6 +460,8 @@ cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW&
     a.out = b.attn_out;
     a.counters = b.counters + kCntAttnBase;
     a.rope = b.rope;
+    a.trace = b.trace ? b.trace + kTrAttn : nullptr;
+    a.kt = lc.kt;
     a.next_w = w.w_out;
     a.next_bytes = static_cast<size_t>(d.H) * d.Hq * d.D * 2;
     a.err = b.err;

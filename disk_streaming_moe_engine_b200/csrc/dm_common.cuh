@@ -27,6 +27,25 @@ DM_DEV uint64_t globaltimer_ns() {
     return t;
 }
 
+// Phase trace: stamp slot k with %globaltimer when tracing is on (tr != nullptr).
+DM_DEV void trace_stamp(uint64_t* tr, int k) {
+    if (tr) tr[k] = globaltimer_ns();
+}
+
+// Launch timeline: CTA (0,0) stamps its start and the end of griddepcontrol.wait; every
+// CTA folds its finish time into the record's end with atomicMax.
+DM_DEV bool kt_lead() { return blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0; }
+DM_DEV void kt_start(uint64_t* kt) {
+    if (kt && kt_lead()) kt[0] = globaltimer_ns();
+}
+DM_DEV void kt_ready(uint64_t* kt) {
+    if (kt && kt_lead()) kt[1] = globaltimer_ns();
+}
+DM_DEV void kt_end(uint64_t* kt) {  // call from thread 0 of the CTA once its work is done
+    if (kt && threadIdx.x == 0)
+        atomicMax(reinterpret_cast<unsigned long long*>(&kt[2]), static_cast<unsigned long long>(globaltimer_ns()));
+}
+
 DM_DEV void raise_error(uint32_t* err, uint32_t code) {
     if (err) atomicOr(err, code);
 }

@@ -33,6 +33,7 @@ struct GdnRecArgs {
     float eps;
     const void* next_w;     // out_proj weights, prefetched into L2
     size_t next_bytes;
+    uint64_t* kt;
 };
 
 __device__ __forceinline__ float softplus_ref(float v) {
@@ -51,6 +52,7 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g_qk = h / (a.nv / a.nk);
 
+    kt_start(a.kt);
     prefetch_l2_share(a.next_w, a.next_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y,
                       threadIdx.x);
     // ---- prologue: this CTA's state rows (4 per warp) into registers ----
@@ -69,6 +71,7 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
         }
     }
     pdl_wait();
+    kt_ready(a.kt);
     const int pos = *a.pos;
 
     // ---- causal conv + SiLU for q (DK), k (DK) and this CTA's 16 v channels ----
@@ -135,6 +138,10 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
         }
         if (lane == 0) a.o[h * DV + r] = oacc;
     }
+    if (a.kt) {
+        __syncthreads();
+        kt_end(a.kt);
+    }
 }
 
 cudaError_t launch_gdn_rec(const LaunchCfg& lc, const Dims& d, const LayerW& w,
@@ -155,6 +162,7 @@ cudaError_t launch_gdn_rec(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.eps = d.eps;
     a.next_w = w.w_out;
     a.next_bytes = static_cast<size_t>(d.H) * d.z_dim * 2;
+    a.kt = lc.kt;
     const dim3 grid(d.nv, d.dv / 16);
     if (d.dk == 128) return launch_kernel(lc, gdn_rec_kernel<128>, grid, dim3(128), 0, a);
     if (d.dk == 64) return launch_kernel(lc, gdn_rec_kernel<64>, grid, dim3(128), 0, a);

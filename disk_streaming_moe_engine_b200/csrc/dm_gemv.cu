@@ -77,11 +77,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __grid
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int nw = gridDim.x * kGemvWarps;
     int row = blockIdx.x * kGemvWarps + warp;
+    kt_start(a.kt);
 
     // weights do not depend on the previous kernel: first chunk in flight before the wait
     uint4 w[G::CH];
     if (row < a.N) load_chunk<G::CH>(w, a.W + static_cast<size_t>(row) * K, 0, lane);
     pdl_wait();
+    kt_ready(a.kt);
 
     if (PRO == PRO_RMSNORM) {
         float acc = 0.0f;
@@ -154,6 +156,10 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __grid
         row = next;
     }
 
+    if (a.kt) {
+        __syncthreads();
+        kt_end(a.kt);
+    }
     if (a.counter == nullptr) return;
     // ---- argmax across the grid: per-CTA candidate, last CTA reduces ----
     if (lane == 0) {
@@ -204,7 +210,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __grid
 }
 
 template <int K, int PRO>
-static cudaError_t launch_gemv_t(const LaunchCfg& lc, const GemvArgs& a) {
+static cudaError_t launch_gemv_t(const LaunchCfg& lc, GemvArgs a) {
+    a.kt = lc.kt;
     const int want = (a.N + kGemvWarps - 1) / kGemvWarps;
     int grid = want < lc.num_sms ? want : lc.num_sms;
     if (a.counter && grid > kMaxCtas) grid = kMaxCtas;
@@ -239,8 +246,10 @@ bool gemv_supported_k(int K) {
 // Embedding gather: xres[slot] = fp32(embed[token])  (reference gguf_embed_tokens,
 // gguf_port_loader.mojo:274).  Token outside [0, V) raises DM_DEVERR_TOKEN and embeds 0.
 __global__ void __launch_bounds__(256) embed_kernel(const uint16_t* __restrict__ embed, int H, int V,
-                                                    const int* token, float* x, uint32_t* err) {
+                                                    const int* token, float* x, uint32_t* err, uint64_t* kt) {
+    kt_start(kt);
     pdl_wait();
+    kt_ready(kt);
     int t = *token;
     if (t < 0 || t >= V) {
         if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(err, DM_DEVERR_TOKEN);
@@ -250,13 +259,14 @@ __global__ void __launch_bounds__(256) embed_kernel(const uint16_t* __restrict__
     const uint16_t* row = embed + static_cast<size_t>(t) * H;
     for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < H; k += gridDim.x * blockDim.x)
         x[k] = bf16_to_f32(row[k]);
+    kt_end(kt);
 }
 
 cudaError_t launch_embed(const LaunchCfg& lc, const Dims& d, const uint16_t* embed,
                          const Buffers& b, int slot) {
     const int blocks = (d.H + 255) / 256;
     return launch_kernel(lc, embed_kernel, dim3(blocks), dim3(256), 0, embed, d.H, d.V,
-                         b.token + slot, b.xres + static_cast<size_t>(slot) * d.H, b.err);
+                         b.token + slot, b.xres + static_cast<size_t>(slot) * d.H, b.err, lc.kt);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -101,14 +101,22 @@ struct Buffers {
     unsigned* counters;   // [64]
     uint32_t* err;        // [1]
     float2* rope;         // [max_pages*16][rot_dim/2] (cos, sin) per position
+    uint64_t* trace;      // [kTraceSlots] %globaltimer stamps of kernel phases, or null
+    uint64_t* ktrace;     // [kMaxTraceKernels][4] per-launch timeline records, or null
 };
+
+constexpr int kTraceSlots = 64;
+// trace slot bases per kernel kind
+constexpr int kTrAttn = 0;   // 8 stamps
+constexpr int kTrMoe = 16;   // 16 stamps
 
 constexpr int kMaxCtas = 1024;
 // counter slots
 constexpr int kCntRouter = 0;
 constexpr int kCntHead = 1;
 constexpr int kCntAttnBase = 8;   // + kv head (< 32)
-constexpr int kCntMoeSync = 48;   // 4 words of grid-wide flags of the fused MoE kernel
+constexpr int kCntMoeSync = 48;   // 4 words of grid-wide counters of the fused MoE kernel
+constexpr int kCntMoeFlag = 56;   // 8 words (4 x u64, 8-byte aligned) of released id words
 
 struct Ctx;  // host-side context (dm_api.cu)
 
@@ -116,7 +124,13 @@ struct LaunchCfg {
     cudaStream_t stream;
     int num_sms;
     bool pdl;
+    uint64_t* kt;   // timeline record of this launch (start, inputs ready, end) or null
 };
+
+// Timeline record kinds (dm_trace_timeline)
+enum TraceKind { TK_EMBED = 0, TK_GDN_IN = 1, TK_GDN_REC = 2, TK_GDN_OUT = 3, TK_ATTN_IN = 4, TK_ATTN = 5,
+                 TK_ATTN_OUT = 6, TK_MOE = 7, TK_HEAD = 8 };
+constexpr int kMaxTraceKernels = 512;
 
 // Kernel launchers (dm_kernels.cu).  `slot` selects the sequence.
 cudaError_t launch_embed(const LaunchCfg& lc, const Dims& d, const uint16_t* embed,

@@ -45,6 +45,7 @@ struct GemvArgs {
     int* gen_idx;
     int gen_cap;
     uint32_t* err;
+    uint64_t* kt;   // timeline record (set from LaunchCfg)
 };
 
 cudaError_t launch_gemv(const LaunchCfg& lc, int K, int pro, const GemvArgs& a);

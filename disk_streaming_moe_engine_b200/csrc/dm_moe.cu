@@ -352,7 +352,10 @@ struct MoeFusedArgs {
     float* probs;
     float* shared_g;
     float* h;                 // [(topk+1)][I]
-    unsigned* sync;           // [4]: router count, ids flag, up count, exit count
+    unsigned* sync;           // [4]: router count, (unused), up count, exit count
+    unsigned long long* idflag; // [4] released words: marker bit 63 | 4 ids x 15 bits
+    uint64_t* trace;          // phase stamps of CTA 0 and of the last CTA, or null
+    uint64_t* kt;             // launch timeline record or null
     const void* next_w;
     size_t next_bytes;
     uint32_t* err;
@@ -363,8 +366,31 @@ DM_DEV unsigned ld_acquire_u32(const unsigned* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-DM_DEV void st_release_u32(unsigned* p, unsigned v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+DM_DEV void st_release_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+DM_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+DM_DEV void red_release_add(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until bit 63 of *p is set; returns the word.
+DM_DEV unsigned long long spin_marker(const unsigned long long* p, uint32_t* err) {
+    unsigned long long v = ld_acquire_u64(p);
+    if (v >> 63) return v;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t n = 0;
+    while (true) {
+        v = ld_acquire_u64(p);
+        if (v >> 63) return v;
+        if (++n % 256 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
+            raise_error(err, DM_DEVERR_TIMEOUT);
+            return 0;
+        }
+    }
 }
 // Bounded wait until *p >= target (thread-level; callers use one thread per CTA).
 DM_DEV bool spin_geq(const unsigned* p, unsigned target, uint32_t* err) {
@@ -372,9 +398,8 @@ DM_DEV bool spin_geq(const unsigned* p, unsigned target, uint32_t* err) {
     const uint64_t t0 = globaltimer_ns();
     uint32_t n = 0;
     while (true) {
-        __nanosleep(32);
         if (ld_acquire_u32(p) >= target) return true;
-        if (++n % 64 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
+        if (++n % 256 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
             raise_error(err, DM_DEVERR_TIMEOUT);
             return false;
         }
@@ -424,6 +449,9 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     float* xsr = reinterpret_cast<float*>(dsm + SM::xs_off(a.up_slots, nexp));
     float* h4 = reinterpret_cast<float*>(dsm + SM::h_off(a.up_slots, nexp));
 
+    uint64_t* tr = tid == 0 ? (c == 0 ? a.trace : (c == nblk - 1 && a.trace ? a.trace + 10 : nullptr)) : nullptr;
+    trace_stamp(tr, 0);
+    kt_start(a.kt);
     // ---- pre-wait: nothing here depends on the previous kernel ----
     prefetch_l2_share(a.next_w, a.next_bytes, c, nblk, tid);
     const int rrow = c * 16 + warp;
@@ -453,6 +481,8 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     }
     pdl_wait();
     pdl_launch_dependents();
+    kt_ready(a.kt);
+    trace_stamp(tr, 1);
 
     // ---- phase 1: canonical RMSNorm (512 threads), router rows ----
     {
@@ -484,6 +514,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         }
     }
     __syncthreads();
+    trace_stamp(tr, 2);
     if (router_cta) {
         if (rrow < nrows) {
             const float4* xlo = reinterpret_cast<const float4*>(xsr);
@@ -512,30 +543,59 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             atomicAdd(&a.sync[0], 1u);
         }
     }
+    trace_stamp(tr, 3);
     if (c == 0) {
         if (tid == 0) spin_geq(&a.sync[0], static_cast<unsigned>(R), a.err);
+        trace_stamp(tr, 4);
         __syncthreads();
         if (warp == 0) {
-            // softmax + top-k (canonical order), probabilities staged in shared memory
-            float* pe = h4;  // free until phase 3
+            // softmax in the canonical order; lane l owns experts l, l+32, ... (<= 32 each)
             const int E = a.E;
+            constexpr int PL = 8;  // register slots per lane: E <= 256 here, larger E below
+            float pv[PL];
             float m = -INFINITY;
-            for (int e = lane; e < E; e += 32) m = fmaxf(m, __ldcg(a.logits + e));
+#pragma unroll
+            for (int i = 0; i < PL; ++i) {
+                const int e = lane + 32 * i;
+                pv[i] = e < E ? __ldcg(a.logits + e) : -INFINITY;
+                m = fmaxf(m, pv[i]);
+            }
+            for (int e = lane + 32 * PL; e < E; e += 32) m = fmaxf(m, __ldcg(a.logits + e));
             m = warp_max(m);
             float s = 0.0f;
-            for (int e = lane; e < E; e += 32) {
+#pragma unroll
+            for (int i = 0; i < PL; ++i) {
+                const int e = lane + 32 * i;
+                if (e < E) {
+                    pv[i] = dm_det_exp(DM_DET_SUB(pv[i], m));
+                    s = DM_DET_ADD(s, pv[i]);
+                } else {
+                    pv[i] = -2.0f;
+                }
+            }
+            float* pe = h4;  // experts beyond 32*PL per lane live in shared memory
+            for (int e = lane + 32 * PL; e < E; e += 32) {
                 const float ev = dm_det_exp(DM_DET_SUB(__ldcg(a.logits + e), m));
                 pe[e] = ev;
                 s = DM_DET_ADD(s, ev);
             }
             s = warp_sum(s);
             const float inv = DM_DET_DIV(1.0f, s);
-            for (int e = lane; e < E; e += 32) pe[e] = DM_DET_MUL(pe[e], inv);
+#pragma unroll
+            for (int i = 0; i < PL; ++i)
+                if (lane + 32 * i < E) pv[i] = DM_DET_MUL(pv[i], inv);
+            for (int e = lane + 32 * PL; e < E; e += 32) pe[e] = DM_DET_MUL(pe[e], inv);
             __syncwarp();
+            // top-k: each round every lane offers its best remaining (value, lower id on
+            // ties), the warp picks the best offer; ties go to the lower expert id
+            unsigned long long words[4] = {0ull, 0ull, 0ull, 0ull};
             for (int r = 0; r < a.topk; ++r) {
                 float bv = -1.0f;
                 int bi = 0x7fffffff;
-                for (int e = lane; e < E; e += 32)
+#pragma unroll
+                for (int i = 0; i < PL; ++i)
+                    if (pv[i] > bv) { bv = pv[i]; bi = lane + 32 * i; }
+                for (int e = lane + 32 * PL; e < E; e += 32)
                     if (pe[e] > bv) { bv = pe[e]; bi = e; }
 #pragma unroll
                 for (int mm = 16; mm >= 1; mm >>= 1) {
@@ -548,13 +608,19 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                     bi = r;
                     bv = 0.0f;
                 }
+                if ((bi & 31) == lane) {  // the owner retires the winner
+                    const int slot = bi >> 5;
+#pragma unroll
+                    for (int i = 0; i < PL; ++i)
+                        if (i == slot) pv[i] = -2.0f;
+                    if (slot >= PL) pe[bi] = -2.0f;
+                }
                 if (lane == 0) {
-                    a.ids[r] = bi;
                     a.probs[r] = bv;
                     sid[r] = bi;
                     sp[r] = bv;
-                    pe[bi] = -2.0f;
                 }
+                words[r >> 2] |= static_cast<unsigned long long>(bi) << (15 * (r & 3));
                 __syncwarp();
             }
             if (lane == 0) {
@@ -562,43 +628,42 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 *a.shared_g = sgv;
                 sp[a.topk] = sgv;
                 if (s != s || isinf(s)) raise_error(a.err, DM_DEVERR_NONFINITE);
-                __threadfence();
-                st_release_u32(&a.sync[1], 1u);
+                for (int r = 0; r < a.topk; ++r) a.ids[r] = sid[r];
+                // publish: the released words carry the ids; probs / gate are ordered before
+                for (int k = 0; k < (a.topk + 3) / 4; ++k) st_release_u64(&a.idflag[k], words[k] | (1ull << 63));
             }
         }
         __syncthreads();
     } else {
-        if (tid == 0) spin_geq(&a.sync[1], 1u, a.err);
-        __syncthreads();
-        if (tid < a.topk) {
-            sid[tid] = min(max(__ldcg(a.ids + tid), 0), a.E - 1);
-            sp[tid] = __ldcg(a.probs + tid);
+        if (tid < (a.topk + 3) / 4) {
+            const unsigned long long w = spin_marker(&a.idflag[tid], a.err);
+            for (int r = 4 * tid; r < a.topk && r < 4 * tid + 4; ++r)
+                sid[r] = min(static_cast<int>((w >> (15 * (r & 3))) & 0x7FFF), a.E - 1);
         }
-        if (tid == 0) sp[a.topk] = __ldcg(a.shared_g);
         __syncthreads();
     }
+    trace_stamp(tr, 5);
 
-    // ---- issue the routed chunks: gate/up items and this CTA's down chunk ----
-    if (tid == 0) {
-        for (int k = 0; k < i1 - i0; ++k) {
-            const int item = i0 + k;
-            const int j = item / a.gu_chunks;
-            if (j == a.topk) continue;
+    // ---- issue the routed chunks: gate/up items and this CTA's down chunk (one
+    // thread per copy) ----
+    if (tid < i1 - i0) {
+        const int k = tid;
+        const int item = i0 + k;
+        const int j = item / a.gu_chunks;
+        if (j != a.topk) {
             mbar_arrive_expect_tx(&bar_up[k], QU::CHUNK);
             bulk_g2s(up_s + static_cast<size_t>(k) * QU::CHUNK,
                      a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes +
                          static_cast<int64_t>(item % a.gu_chunks) * QU::CHUNK,
                      QU::CHUNK, &bar_up[k]);
         }
-        if (has_down) {
-            for (int j = 0; j < a.topk; ++j) {
-                mbar_arrive_expect_tx(&bar_dn[j], QD::CHUNK);
-                bulk_g2s(dn_s + static_cast<size_t>(j) * QD::CHUNK,
-                         a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes + a.gu_part_bytes +
-                             static_cast<int64_t>(c) * QD::CHUNK,
-                         QD::CHUNK, &bar_dn[j]);
-            }
-        }
+    } else if (has_down && tid >= 32 && tid < 32 + a.topk) {
+        const int j = tid - 32;
+        mbar_arrive_expect_tx(&bar_dn[j], QD::CHUNK);
+        bulk_g2s(dn_s + static_cast<size_t>(j) * QD::CHUNK,
+                 a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes + a.gu_part_bytes +
+                     static_cast<int64_t>(c) * QD::CHUNK,
+                 QD::CHUNK, &bar_dn[j]);
     }
 
     // ---- phase 2: gate/up; two warp groups take alternate items ----
@@ -629,15 +694,20 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         }
     }
     __syncthreads();
+    trace_stamp(tr, 6);
     if (tid == 0) {
-        __threadfence();
-        atomicAdd(&a.sync[2], 1u);
-        spin_geq(&a.sync[2], static_cast<unsigned>(nblk), a.err);
+        red_release_add(&a.sync[2], 1u);
+        if (has_down) spin_geq(&a.sync[2], static_cast<unsigned>(nblk), a.err);
     }
     __syncthreads();
+    trace_stamp(tr, 7);
 
     // ---- phase 3: 16 output rows of every selected expert + residual ----
     if (has_down) {
+        if (c != 0) {
+            if (tid < a.topk) sp[tid] = __ldcg(a.probs + tid);
+            if (tid == 0) sp[a.topk] = __ldcg(a.shared_g);
+        }
         for (int t = tid; t < nexp * KI; t += kMoeThreads) {
             const int j = t / KI, k = t % KI;
             x4_store<KI>(h4 + j * KI, k, __ldcg(a.h + t));
@@ -683,13 +753,15 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
 
     // ---- exit: the last CTA resets the flags for the next launch ----
     __syncthreads();
+    trace_stamp(tr, 8);
+    kt_end(a.kt);
     if (tid == 0) {
         __threadfence();
         const unsigned prev = atomicAdd(&a.sync[3], 1u);
         if (prev == static_cast<unsigned>(nblk) - 1) {
             a.sync[0] = 0u;
-            a.sync[1] = 0u;
             a.sync[2] = 0u;
+            for (int k = 0; k < 4; ++k) a.idflag[k] = 0ull;
             a.sync[3] = 0u;
             __threadfence();
         }
@@ -731,6 +803,9 @@ cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.shared_g = b.shared_g;
     a.h = b.h;
     a.sync = b.counters + kCntMoeSync;
+    a.idflag = reinterpret_cast<unsigned long long*>(b.counters + kCntMoeFlag);
+    a.trace = b.trace ? b.trace + kTrMoe : nullptr;
+    a.kt = lc.kt;
     a.next_w = next_w;
     a.next_bytes = next_bytes;
     a.err = b.err;

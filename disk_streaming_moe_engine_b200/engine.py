@@ -100,6 +100,28 @@ class Engine:
         self._ok(self.lib.dm_time_kernel(self.ctx, which, layer, iters, C.byref(ms), C.byref(nb)))
         return ms.value, nb.value
 
+    def trace_enable(self, on: bool = True):
+        self._ok(self.lib.dm_trace_enable(self.ctx, 1 if on else 0))
+
+    def trace_read(self, n: int = 64) -> np.ndarray:
+        out = np.zeros(n, np.uint64)
+        self._ok(self.lib.dm_trace_read(self.ctx, _ptr(out), n))
+        return out
+
+    TRACE_KINDS = ["embed", "gdn_in", "gdn_rec", "gdn_out", "attn_in", "attn", "attn_out", "moe", "head"]
+
+    def trace_timeline(self, n: int = 512):
+        """[(kind, layer, start_ns, ready_ns, end_ns)] of the last traced decode step."""
+        rec = np.zeros((n, 4), np.uint64)
+        kinds = np.zeros(n, np.int32)
+        cnt = C.c_int32()
+        self._ok(self.lib.dm_trace_timeline(self.ctx, _ptr(rec), _ptr(kinds), n, C.byref(cnt)))
+        out = []
+        for i in range(cnt.value):
+            k = int(kinds[i])
+            out.append((self.TRACE_KINDS[k >> 16], k & 0xFFFF, int(rec[i, 0]), int(rec[i, 1]), int(rec[i, 2])))
+        return out
+
     def kernels_per_step(self) -> int:
         v = C.c_int32()
         self._ok(self.lib.dm_kernels_per_step(self.ctx, C.byref(v)))

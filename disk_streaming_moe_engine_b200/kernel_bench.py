@@ -32,6 +32,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--ctx", type=int, default=0, help="tokens already in the KV cache / GDN state")
     ap.add_argument("--warm", action="store_true")
+    ap.add_argument("--trace", action="store_true", help="also report the kernel's phase stamps")
     ap.add_argument("--seed", type=int, default=1)
     a = ap.parse_args()
     cfg = preset(a.preset)
@@ -49,8 +50,20 @@ def main():
             x = np.random.default_rng(a.seed).standard_normal((1, cfg.hidden_size)).astype(np.float32)
             eng.forward_port_block(x, a.layer, a.ctx)
         us_ms, nbytes = eng.time_kernel(KERNELS[a.kernel], a.layer, a.iters)
+        phases = None
+        if a.trace:  # one more launch with phase stamps (ns relative to the kernel's start)
+            eng.trace_enable(True)
+            eng.time_kernel(KERNELS[a.kernel], a.layer, 1)
+            t = eng.trace_read(64).astype(np.int64)
+            eng.trace_enable(False)
+            base = {"core": 0, "moe": 16}.get(a.kernel, 0)
+            if a.kernel == "moe":
+                phases = {"cta0": [int(v - t[16]) if v else None for v in t[16:25]],
+                          "last": [int(v - t[26]) if v else None for v in t[26:35]]}
+            else:
+                phases = [int(v - t[base]) if v else None for v in t[base:base + 8]]
     print(json.dumps({"kernel": a.kernel, "preset": a.preset, "layer": a.layer, "ctx": a.ctx,
-                      "us": us_ms * 1e3, "bytes": nbytes, "GBps": nbytes / us_ms / 1e6}))
+                      "us": us_ms * 1e3, "bytes": nbytes, "GBps": nbytes / us_ms / 1e6, "phases_ns": phases}))
 
 
 if __name__ == "__main__":

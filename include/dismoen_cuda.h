@@ -293,6 +293,23 @@ int32_t dm_kernels_per_step(dm_ctx* ctx, int32_t* out);
 int32_t dm_time_kernel(dm_ctx* ctx, int32_t which, int32_t layer, int32_t iters, float* avg_ms,
                        uint64_t* bytes);
 
+/* Phase tracing (the role of the reference's SchedulerTimings, port_scheduler.mojo:46):
+ * when on, kernels stamp %globaltimer (ns) at their phase boundaries into a 64-slot
+ * device buffer; slots 0-7 decode attention (start, page loads issued, inputs ready,
+ * q/k ready, pages done, cluster merged, counted in, output), slots 16-24 the MoE kernel
+ * of CTA 0 (start, inputs ready, normalised, router rows done, router complete, ids known,
+ * experts up done, barrier passed, done) and 26-34 the same for the last CTA.  Turning
+ * tracing on or off drops captured decode graphs (they are recaptured on next use). */
+int32_t dm_trace_enable(dm_ctx* ctx, int32_t on);
+int32_t dm_trace_read(dm_ctx* ctx, uint64_t* stamps_host, int32_t n);
+/* Timeline of the last traced decode step: for launch i, rec[4i..4i+2] = %globaltimer ns at
+ * the first CTA's start, at the end of its griddepcontrol.wait and at the last CTA's end;
+ * kinds[i] = (kind << 16) | layer with kind 0 embed, 1 GDN in-proj, 2 GDN recurrence,
+ * 3 GDN out-proj, 4 attention in-proj, 5 decode attention, 6 attention out-proj, 7 MoE,
+ * 8 head.  count receives the number of records (<= n). */
+int32_t dm_trace_timeline(dm_ctx* ctx, uint64_t* rec_host, int32_t* kinds_host, int32_t n,
+                          int32_t* count);
+
 /* ---- synthetic checkpoint (seeded; host and device generate the same distributions) --
  * Counter-based generator: element i of stream `stream_id` under `seed` is a pure
  * function of (seed, stream_id, i), so any subrange can be produced independently. */
