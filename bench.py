@@ -216,6 +216,7 @@ def step_timeline(eng, steps: int):
     eng.enqueue_decode(steps)
     eng.sync()
     tl = eng.trace_timeline()
+    ph = eng.trace_read(64).astype(np.int64)
     eng.trace_enable(False)
     t0 = tl[0][2]
     rows = [{"kind": k, "layer": l, "start_us": (s0 - t0) / 1e3, "ready_us": (r - t0) / 1e3, "end_us": (e - t0) / 1e3}
@@ -233,7 +234,12 @@ def step_timeline(eng, steps: int):
         d["path_us"] = round(d["path_us"], 1)
         d["span_us"] = round(d["span_us"], 1)
         d["path_share"] = round(d["path_us"] / total, 3)
-    return {"step_us": total, "by_kind": by, "launches": rows}
+    rel = lambda a, b: [round((int(v) - int(ph[b])) / 1e3, 2) if v else None for v in ph[a:b + 9]] if ph[b] else None
+    phases = {"attn_last_split_cta": [round((int(v) - int(ph[0])) / 1e3, 2) if v else None for v in ph[0:10]],
+              "moe_topk_detail": [round((int(v) - int(ph[16])) / 1e3, 2) if v else None for v in ph[36:40]],
+              "moe_cta0": [round((int(v) - int(ph[16])) / 1e3, 2) if v else None for v in ph[16:25]],
+              "moe_last_cta": [round((int(v) - int(ph[26])) / 1e3, 2) if v else None for v in ph[26:35]]}
+    return {"step_us": total, "by_kind": by, "phases_us": phases, "launches": rows}
 
 
 def run_reference(args, rank, world):

@@ -11,6 +11,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <thread>
@@ -72,6 +73,8 @@ struct dm_ctx {
     std::vector<int> att_len;          // [n_att * max_seqs]
     std::vector<int> dev_pos_valid;    // device pos[slot] == slot_len[slot]
     std::vector<cudaGraphExec_t> graphs;  // decode step per slot
+    bool use_pdl = true;       // programmatic dependent launch between step kernels
+    bool l2_prefetch = true;   // latency-bound kernels prefetch upcoming weights into L2
     uint64_t* trace_buf = nullptr;
     uint64_t* ktrace_buf = nullptr;
     int trace_n = 0;
@@ -333,7 +336,9 @@ static int plan_memory(dm_ctx* c, bool commit) {
     return DM_OK;
 }
 
-static LaunchCfg lcfg(const dm_ctx* c) { return LaunchCfg{c->stream, c->num_sms, true, nullptr}; }
+static LaunchCfg lcfg(const dm_ctx* c) {
+    return LaunchCfg{c->stream, c->num_sms, c->use_pdl, nullptr, c->l2_prefetch};
+}
 
 // Launch config for the next kernel of a traced sequence (timeline record n of kind k).
 static LaunchCfg lcfg_traced(dm_ctx* c, int kind, int layer) {
@@ -405,6 +410,11 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     if (rt->max_seqs <= 0 || rt->kv_page_tokens != kPageTokens || rt->kv_num_pages <= 0 || rt->max_pages_per_seq <= 0)
         return DM_ERR_INVALID_ARG;
     dm_ctx* c = new dm_ctx();
+    // tuning knobs (environment, read once): DISMOEN_PDL=0 launches every kernel without
+    // programmatic dependent launch; DISMOEN_L2_PREFETCH=0 disables the L2 prefetch of
+    // upcoming weights by the latency-bound kernels
+    if (const char* v = getenv("DISMOEN_PDL")) c->use_pdl = atoi(v) != 0;
+    if (const char* v = getenv("DISMOEN_L2_PREFETCH")) c->l2_prefetch = atoi(v) != 0;
     c->mc = *model;
     c->rc = *rt;
     c->d = make_dims(*model, *rt);
@@ -850,7 +860,7 @@ static cudaError_t enqueue_moe(dm_ctx* c, int layer, int slot) {
     // the next layer's input projection is the next large stream: start it into L2
     const void* next_w = nullptr;
     size_t next_bytes = 0;
-    if (layer + 1 < c->d.L) {
+    if (layer + 1 < c->d.L && c->l2_prefetch) {
         const LayerW& nw = c->layers[layer + 1];
         next_w = nw.w_in;
         next_bytes = static_cast<size_t>(nw.is_attn ? c->d.attn_in_rows : c->d.gdn_in_rows) * c->d.H * 2;

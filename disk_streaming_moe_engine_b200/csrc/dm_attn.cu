@@ -160,12 +160,31 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     // ---- q heads of this KV group, new k, new v: one parallel load, then per-head
     // RMSNorm + RoPE in shared memory (norm weights and the RoPE row were staged before
     // the wait) ----
-    for (int i = tid; i < GRP * D; i += 128) qsm[i / D][i % D] = a.qg[static_cast<size_t>(g * GRP) * D + i];
-    for (int i = tid; i < D; i += 128) {
-        knew[i] = a.kvnew[static_cast<size_t>(g) * D + i];
-        vnew[i] = a.kvnew[static_cast<size_t>(a.Hkv + g) * D + i];
+    {   // all loads issued together (one round trip), then stored
+        constexpr int QPT = GRP * D / 128, KPT = (D + 127) / 128;
+        float qv[QPT], kv[KPT], vv[KPT];
+        const float* qsrc = a.qg + static_cast<size_t>(g * GRP) * D;
+#pragma unroll
+        for (int i = 0; i < QPT; ++i) qv[i] = qsrc[tid + 128 * i];
+#pragma unroll
+        for (int i = 0; i < KPT; ++i) {
+            const int d = tid + 128 * i;
+            kv[i] = d < D ? a.kvnew[static_cast<size_t>(g) * D + d] : 0.0f;
+            vv[i] = d < D ? a.kvnew[static_cast<size_t>(a.Hkv + g) * D + d] : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < QPT; ++i) (&qsm[0][0])[tid + 128 * i] = qv[i];
+#pragma unroll
+        for (int i = 0; i < KPT; ++i) {
+            const int d = tid + 128 * i;
+            if (d < D) {
+                knew[d] = kv[i];
+                vnew[d] = vv[i];
+            }
+        }
     }
     __syncthreads();
+    trace_stamp(tr, 8);
     for (int hh = warp; hh < GRP + 1; hh += 4) {
         float* v = hh < GRP ? qsm[hh] : knew;
         const float* wn = hh < GRP ? qn_s : kn_s;
@@ -185,6 +204,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         __syncwarp();
     }
     __syncthreads();
+    trace_stamp(tr, 9);
     for (int d = tid; d < D; d += 128) {
         const uint16_t kb = f32_to_bf16(knew[d]);
         kbits[d] = kb;
@@ -462,7 +482,7 @@ cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW&
     a.rope = b.rope;
     a.trace = b.trace ? b.trace + kTrAttn : nullptr;
     a.kt = lc.kt;
-    a.next_w = w.w_out;
+    a.next_w = lc.l2_prefetch ? w.w_out : nullptr;
     a.next_bytes = static_cast<size_t>(d.H) * d.Hq * d.D * 2;
     a.err = b.err;
     const int grp = d.Hq / d.Hkv;

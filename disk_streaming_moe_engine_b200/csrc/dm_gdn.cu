@@ -70,9 +70,11 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
             for (int c = 0; c < CPL; ++c) srow[i][c] = src[c];
         }
     }
+    const float alog = a.a_log[h], dtb = a.dt_bias[h];  // weights: before the wait
     pdl_wait();
     kt_ready(a.kt);
     const int pos = *a.pos;
+    const float av = a.ab[h], bv = a.ab[a.nv + h];
 
     // ---- causal conv + SiLU for q (DK), k (DK) and this CTA's 16 v channels ----
     const int q0 = g_qk * DK, k0 = a.nk * DK + g_qk * DK, v0 = 2 * a.nk * DK + h * DV + rb * RB;
@@ -106,8 +108,7 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
     const float inv_nk = 1.0f / (sqrtf(ss) + a.eps);
 #pragma unroll
     for (int c = 0; c < CPL; ++c) kl[c] *= inv_nk;
-    const float av = a.ab[h], bv = a.ab[a.nv + h];
-    const float g = expf(-expf(a.a_log[h]) * softplus_ref(av + a.dt_bias[h]));
+    const float g = expf(-expf(alog) * softplus_ref(av + dtb));
     const float beta = sigmoid_f(bv);
 
     // ---- delta-rule update and o = S q, one row at a time per warp ----
@@ -160,7 +161,7 @@ cudaError_t launch_gdn_rec(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.nv = d.nv;
     a.qkv_dim = d.qkv_dim;
     a.eps = d.eps;
-    a.next_w = w.w_out;
+    a.next_w = lc.l2_prefetch ? w.w_out : nullptr;
     a.next_bytes = static_cast<size_t>(d.H) * d.z_dim * 2;
     a.kt = lc.kt;
     const dim3 grid(d.nv, d.dv / 16);

@@ -82,12 +82,28 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __grid
     // weights do not depend on the previous kernel: first chunk in flight before the wait
     uint4 w[G::CH];
     if (row < a.N) load_chunk<G::CH>(w, a.W + static_cast<size_t>(row) * K, 0, lane);
+    constexpr int XPT = K / kGemvThreads;  // activations per thread (K >= 512) or 1
+    constexpr int XN = XPT > 0 ? XPT : 1;
+    float gv[XN];  // norm gains are weights: fetched before the wait
+    if (PRO == PRO_RMSNORM) {
+#pragma unroll
+        for (int i = 0; i < XN; ++i) {
+            const int k = tid + kGemvThreads * i;
+            gv[i] = k < K ? bf16_to_f32(a.gamma[k]) : 0.0f;
+        }
+    }
     pdl_wait();
     kt_ready(a.kt);
 
     if (PRO == PRO_RMSNORM) {
+        float xv[XN];
         float acc = 0.0f;
-        for (int k = tid; k < K; k += kGemvThreads) acc = fmaf(a.x[k], a.x[k], acc);
+#pragma unroll
+        for (int i = 0; i < XN; ++i) {
+            const int k = tid + kGemvThreads * i;
+            xv[i] = k < K ? a.x[k] : 0.0f;
+            acc = fmaf(xv[i], xv[i], acc);
+        }
         acc = warp_sum(acc);
         if (lane == 0) red[warp] = acc;
         __syncthreads();
@@ -95,23 +111,49 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __grid
 #pragma unroll
         for (int i = 0; i < kGemvWarps; ++i) ss += red[i];
         const float denom = sqrtf(ss / static_cast<float>(K) + a.eps);
-        for (int k = tid; k < K; k += kGemvThreads)
-            xs_store(xs, K, k, (a.x[k] / denom) * bf16_to_f32(a.gamma[k]));
+#pragma unroll
+        for (int i = 0; i < XN; ++i) {
+            const int k = tid + kGemvThreads * i;
+            if (k < K) xs_store(xs, K, k, (xv[i] / denom) * gv[i]);
+        }
     } else if (PRO == PRO_HEADNORM) {
+        // warp h handles heads h, h + 16, ...; the o and z values of a head (dv <= 128)
+        // are loaded in one batch per lane
         const int dv = a.hn_dim, nh = K / dv;
         for (int h = warp; h < nh; h += kGemvWarps) {
             const float* oh = a.hn_o + h * dv;
+            const float* zh = a.hn_z + h * dv;
+            float ov[4], zv[4], wv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int d = lane + 32 * i;
+                ov[i] = d < dv ? oh[d] : 0.0f;
+                zv[i] = d < dv ? zh[d] : 0.0f;
+                wv[i] = d < dv ? bf16_to_f32(a.hn_w[d]) : 0.0f;
+            }
             float acc = 0.0f;
-            for (int d = lane; d < dv; d += 32) acc = fmaf(oh[d], oh[d], acc);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc = fmaf(ov[i], ov[i], acc);
             acc = warp_sum(acc);
             const float rs = 1.0f / sqrtf(acc / static_cast<float>(dv) + a.eps);
-            for (int d = lane; d < dv; d += 32) {
-                const float nrm = oh[d] * rs * bf16_to_f32(a.hn_w[d]);
-                xs_store(xs, K, h * dv + d, nrm * a.hn_z[h * dv + d]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int d = lane + 32 * i;
+                if (d < dv) xs_store(xs, K, h * dv + d, ov[i] * rs * wv[i] * zv[i]);
             }
         }
     } else {
-        for (int k = tid; k < K; k += kGemvThreads) xs_store(xs, K, k, a.x[k]);
+        float xv[XN];
+#pragma unroll
+        for (int i = 0; i < XN; ++i) {
+            const int k = tid + kGemvThreads * i;
+            xv[i] = k < K ? a.x[k] : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < XN; ++i) {
+            const int k = tid + kGemvThreads * i;
+            if (k < K) xs_store(xs, K, k, xv[i]);
+        }
     }
     __syncthreads();
     pdl_launch_dependents();

@@ -125,6 +125,7 @@ struct LaunchCfg {
     int num_sms;
     bool pdl;
     uint64_t* kt;   // timeline record of this launch (start, inputs ready, end) or null
+    bool l2_prefetch = true;
 };
 
 // Timeline record kinds (dm_trace_timeline)

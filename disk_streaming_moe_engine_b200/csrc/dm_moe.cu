@@ -479,6 +479,13 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                      a.shared + a.gu_part_bytes + static_cast<int64_t>(c) * QD::CHUNK, QD::CHUNK, &bar_dn[a.topk]);
         }
     }
+    constexpr int XPT = (K + kMoeThreads - 1) / kMoeThreads;
+    float gv[XPT];  // post-attention norm gains (weights) before the wait
+#pragma unroll
+    for (int i = 0; i < XPT; ++i) {
+        const int k = i * kMoeThreads + tid;
+        gv[i] = k < K ? bf16_to_f32(a.gamma[k]) : 0.0f;
+    }
     pdl_wait();
     pdl_launch_dependents();
     kt_ready(a.kt);
@@ -486,7 +493,6 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
 
     // ---- phase 1: canonical RMSNorm (512 threads), router rows ----
     {
-        constexpr int XPT = (K + kMoeThreads - 1) / kMoeThreads;
         float xv[XPT];
         float acc = 0.0f;
 #pragma unroll
@@ -506,7 +512,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         for (int i = 0; i < XPT; ++i) {
             const int k = i * kMoeThreads + tid;
             if (k < K) {
-                const float y = __fmul_rn(__fdiv_rn(xv[i], denom), bf16_to_f32(a.gamma[k]));
+                const float y = __fmul_rn(__fdiv_rn(xv[i], denom), gv[i]);
                 x4_store<K>(xn4, k, y);
                 xs_store_split(xsr, K, k, y);
                 if (c == 0 && a.xn_out) a.xn_out[k] = y;
@@ -562,6 +568,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             }
             for (int e = lane + 32 * PL; e < E; e += 32) m = fmaxf(m, __ldcg(a.logits + e));
             m = warp_max(m);
+            if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 0);
             float s = 0.0f;
 #pragma unroll
             for (int i = 0; i < PL; ++i) {
@@ -584,53 +591,99 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
 #pragma unroll
             for (int i = 0; i < PL; ++i)
                 if (lane + 32 * i < E) pv[i] = DM_DET_MUL(pv[i], inv);
+            if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 1);
             for (int e = lane + 32 * PL; e < E; e += 32) pe[e] = DM_DET_MUL(pe[e], inv);
             __syncwarp();
-            // top-k: each round every lane offers its best remaining (value, lower id on
-            // ties), the warp picks the best offer; ties go to the lower expert id
-            unsigned long long words[4] = {0ull, 0ull, 0ull, 0ull};
+            // top-k: each lane sorts its 8 (probability, id) pairs in registers (compare-
+            // exchange network, ties to the lower id); every round the warp takes the
+            // maximum probability over the lanes' heads (redux on the bit patterns, which
+            // order like the values for p >= 0) and the lowest id holding it, and the
+            // owning lane pops its head.
+            uint32_t kb[PL];
+            int ki[PL];
+#pragma unroll
+            for (int i = 0; i < PL; ++i) {
+                const int e = lane + 32 * i;
+                kb[i] = (e < E && pv[i] > 0.0f) ? __float_as_uint(pv[i]) : 0u;
+                ki[i] = e < E ? e : 0x7fffffff;
+            }
+#define DM_CX(x, y)                                                                        \
+    {                                                                                      \
+        const bool sw = kb[y] > kb[x] || (kb[y] == kb[x] && ki[y] < ki[x]);                \
+        const uint32_t tb = sw ? kb[y] : kb[x];                                            \
+        const int ti = sw ? ki[y] : ki[x];                                                 \
+        kb[y] = sw ? kb[x] : kb[y];                                                        \
+        ki[y] = sw ? ki[x] : ki[y];                                                        \
+        kb[x] = tb;                                                                        \
+        ki[x] = ti;                                                                        \
+    }
+            // Batcher odd-even merge sort network for 8 elements (19 compare-exchanges)
+            DM_CX(0, 1) DM_CX(2, 3) DM_CX(4, 5) DM_CX(6, 7)
+            DM_CX(0, 2) DM_CX(1, 3) DM_CX(4, 6) DM_CX(5, 7)
+            DM_CX(1, 2) DM_CX(5, 6)
+            DM_CX(0, 4) DM_CX(1, 5) DM_CX(2, 6) DM_CX(3, 7)
+            DM_CX(2, 4) DM_CX(3, 5)
+            DM_CX(1, 2) DM_CX(3, 4) DM_CX(5, 6)
+#undef DM_CX
             for (int r = 0; r < a.topk; ++r) {
-                float bv = -1.0f;
-                int bi = 0x7fffffff;
+                // this lane's best: its register head, or an expert beyond 32*PL (E > 256,
+                // shared memory; a taken one holds -2)
+                uint32_t hb = kb[0];
+                int hi = ki[0];
+                for (int e = lane + 32 * PL; e < E; e += 32) {
+                    const float v = pe[e];
+                    const uint32_t b = v > 0.0f ? __float_as_uint(v) : 0u;
+                    const int id = v >= 0.0f ? e : 0x7fffffff;
+                    if (b > hb || (b == hb && id < hi)) {
+                        hb = b;
+                        hi = id;
+                    }
+                }
+                const uint32_t mb = __reduce_max_sync(0xffffffffu, hb);
+                const int cand = hb == mb ? hi : 0x7fffffff;
+                int bi = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(cand)));
+                float bv = __uint_as_float(mb);
+                if (hi == bi && bi >= 32 * PL) {
+                    pe[bi] = -2.0f;
+                } else if (ki[0] == bi) {  // pop the head
 #pragma unroll
-                for (int i = 0; i < PL; ++i)
-                    if (pv[i] > bv) { bv = pv[i]; bi = lane + 32 * i; }
-                for (int e = lane + 32 * PL; e < E; e += 32)
-                    if (pe[e] > bv) { bv = pe[e]; bi = e; }
-#pragma unroll
-                for (int mm = 16; mm >= 1; mm >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, bv, mm);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, mm);
-                    if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                    for (int i = 0; i < PL - 1; ++i) {
+                        kb[i] = kb[i + 1];
+                        ki[i] = ki[i + 1];
+                    }
+                    kb[PL - 1] = 0u;
+                    ki[PL - 1] = 0x7fffffff;
                 }
                 if (bi < 0 || bi >= E) {
                     if (lane == 0) raise_error(a.err, DM_DEVERR_NONFINITE);
                     bi = r;
                     bv = 0.0f;
                 }
-                if ((bi & 31) == lane) {  // the owner retires the winner
-                    const int slot = bi >> 5;
-#pragma unroll
-                    for (int i = 0; i < PL; ++i)
-                        if (i == slot) pv[i] = -2.0f;
-                    if (slot >= PL) pe[bi] = -2.0f;
-                }
                 if (lane == 0) {
                     a.probs[r] = bv;
                     sid[r] = bi;
                     sp[r] = bv;
                 }
-                words[r >> 2] |= static_cast<unsigned long long>(bi) << (15 * (r & 3));
-                __syncwarp();
             }
+            __syncwarp();
+            if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 2);
             if (lane == 0) {
                 const float sgv = sigmoid_f(__ldcg(a.logits + E));
                 *a.shared_g = sgv;
                 sp[a.topk] = sgv;
                 if (s != s || isinf(s)) raise_error(a.err, DM_DEVERR_NONFINITE);
-                for (int r = 0; r < a.topk; ++r) a.ids[r] = sid[r];
+                unsigned long long words[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+                for (int r = 0; r < kMaxTopK; ++r)
+                    if (r < a.topk) {
+                        a.ids[r] = sid[r];
+                        words[r >> 2] |= static_cast<unsigned long long>(sid[r]) << (15 * (r & 3));
+                    }
                 // publish: the released words carry the ids; probs / gate are ordered before
-                for (int k = 0; k < (a.topk + 3) / 4; ++k) st_release_u64(&a.idflag[k], words[k] | (1ull << 63));
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (k < (a.topk + 3) / 4) st_release_u64(&a.idflag[k], words[k] | (1ull << 63));
+                trace_stamp(tr ? tr + 20 : nullptr, 3);
             }
         }
         __syncthreads();
@@ -708,9 +761,20 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             if (tid < a.topk) sp[tid] = __ldcg(a.probs + tid);
             if (tid == 0) sp[a.topk] = __ldcg(a.shared_g);
         }
-        for (int t = tid; t < nexp * KI; t += kMoeThreads) {
-            const int j = t / KI, k = t % KI;
-            x4_store<KI>(h4 + j * KI, k, __ldcg(a.h + t));
+        {
+            constexpr int HPT = ((kMaxTopK + 1) * KI + kMoeThreads - 1) / kMoeThreads;
+            const int nh = nexp * KI;
+            float hv[HPT];
+#pragma unroll
+            for (int i = 0; i < HPT; ++i) {
+                const int t = tid + kMoeThreads * i;
+                hv[i] = t < nh ? __ldcg(a.h + t) : 0.0f;
+            }
+#pragma unroll
+            for (int i = 0; i < HPT; ++i) {
+                const int t = tid + kMoeThreads * i;
+                if (t < nh) x4_store<KI>(h4 + (t / KI) * KI, t % KI, hv[i]);
+            }
         }
         __syncthreads();
         const int wgrp = warp >> 3, wg = warp & 7;
