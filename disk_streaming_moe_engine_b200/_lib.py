@@ -101,6 +101,7 @@ SIGNATURES = {
     "dm_synth_u8": (I32, [U64, U64, U64, P]),
     "dm_synth_f16_absnormal": (I32, [U64, U64, U64, F32, P]),
     "dm_synth_model_device": (I32, [P, U64]),
+    "dm_moe_layer_noalloc": (I32, [I32, I32, I32, I32, F32, P, P, P, P, P, P, P, P, P, C.c_char_p, U64]),
 }
 
 _LIB = None

@@ -310,6 +310,48 @@ int32_t dm_trace_read(dm_ctx* ctx, uint64_t* stamps_host, int32_t n);
 int32_t dm_trace_timeline(dm_ctx* ctx, uint64_t* rec_host, int32_t* kinds_host, int32_t n,
                           int32_t* count);
 
+/* ---- MoE mixer without allocation ---------------------------------------------------
+ * No counterpart in the reference: its MoE block (forward_port_block second half,
+ * port_scheduler.mojo:286) always runs inside its own engine, which owns every buffer.
+ *
+ * dm_moe_layer_noalloc computes what dm_moe_block computes for one token (post-attention
+ * RMSNorm, router, top-k, the k routed experts and the shared expert, residual) with the
+ * same fused kernel, but over buffers the CALLER owns on the current device, and it
+ * allocates nothing: no cudaMalloc/cudaFree and no allocating library routine.  It is for
+ * a host runtime that keeps expert records in a cache of its own (streamed from disk) and
+ * has committed the rest of device memory to that cache, and so cannot let a library
+ * allocate during a step.  No dm_ctx is involved.
+ *
+ * Scratch: one fixed array of DM_NOALLOC_SCRATCH_BYTES (64 KiB) compiled into the library,
+ * per device.  A layer needs 512 + 4096 + 256 + 4*H + 4*(k + 1)*I bytes of it; larger
+ * layers are rejected with DM_ERR_INVALID_ARG and a SCRATCH_LIMIT message.  Supported
+ * (hidden, intermediate) pairs: (256,128) (1024,256) (2048,256) (2048,512) (4096,512);
+ * num_experts <= 1023, num_experts_per_tok <= 16, group size 64.
+ *   - Calls that overlap on the GPU (two host threads, or two streams of one device)
+ *     share the one array and race; serialise them.
+ *   - The array keeps what the last call left in it; each call clears the part that must
+ *     start at zero (counters, flags, error word) on `stream` before its launch.
+ *   - The first call on a device does the set-up (scratch address, kernel attributes)
+ *     with that device current; make it before any stream capture.
+ * Buffers (device memory of the current device):
+ *   router_dev    bf16 [num_experts + 1][H]: router rows, then the shared-expert gate row
+ *   post_norm_dev bf16 [H]
+ *   experts_dev   num_experts expert records, shared_dev one record, each in the chunked
+ *                 4-bit layout dm_expert_upload writes (gate/up chunks, then down chunks;
+ *                 record bytes = (I/8) * 16*(H/2 + H/32 + H/128) + (H/16) * 16*(I/2 + I/32 + I/128))
+ *   x_mid_dev fp32 [H] in, x_out_dev fp32 [H] out (must not overlap x_mid_dev)
+ *   ids_dev int32 [k], probs_dev fp32 [k]: top-k ids / probabilities, or NULL
+ * The call runs on `stream` (a cudaStream_t, NULL = legacy default stream) and returns
+ * after it has synchronised that stream.  err_buf (may be NULL) receives a JSON error
+ * object like dm_last_error's. */
+#define DM_NOALLOC_SCRATCH_BYTES 65536
+int32_t dm_moe_layer_noalloc(int32_t hidden_size, int32_t moe_intermediate_size,
+                             int32_t num_experts, int32_t num_experts_per_tok, float rms_norm_eps,
+                             const uint16_t* router_dev, const uint16_t* post_norm_dev,
+                             const uint8_t* experts_dev, const uint8_t* shared_dev,
+                             const float* x_mid_dev, float* x_out_dev, int32_t* ids_dev,
+                             float* probs_dev, void* stream, char* err_buf, uint64_t err_buf_size);
+
 /* ---- synthetic checkpoint (seeded; host and device generate the same distributions) --
  * Counter-based generator: element i of stream `stream_id` under `seed` is a pure
  * function of (seed, stream_id, i), so any subrange can be produced independently. */
