@@ -3,16 +3,22 @@
 
 Workload: the full 40-block Qwen3.6-35B-A3B-shaped model
 ([GDN, GDN, GDN, GatedAttn] x 10, hidden 2048, 256 experts top-8 + 1 shared in 4-bit
-group-64, vocab 151936), random-init weights generated on the device, a 4096-token random
-prompt (seed 2) processed untimed, then W warm-up and K timed greedy decode steps, batch 1.
+group-64, vocab 151936), random-init weights generated on the device, a 4096-token context,
+then W warm-up and K timed greedy decode steps, batch 1.  The context is by default
+imported as seeded synthetic state (bf16 N(0,1) K/V pages of every attention layer, fp32
+N(0, 0.05) GDN recurrent states and conv windows): a decode step's cost depends on the
+context length only, and this keeps the run short enough for an ncu launch list;
+`--context prefill` instead runs the 4096-token random prompt through the decode graph.
 
   value    tokens/s of K decode steps replayed on the device (token fed back on the GPU,
            every weight byte of a step read from HBM: the 4 GB per step is far larger than
            the 126 MB L2, so no flush is needed), CUDA events on the library stream.
   e2e      the same steps through the C ABI with host buffers: dm_decode_step(token_in) ->
            token_out per step (4 B host->device, 8 B device->host inside the timed region).
-  roofline the GDN input-projection GEMV (12352 x 2048 bf16 = 50.6 MB per launch), timed
-           alone with CUDA events on the library stream, against MEASURED_PEAKS.json.
+  roofline the fused MoE kernel (router rows 1.05 MB + 9 expert records 15.26 MB = 16.3 MB
+           per launch; the largest share of the step), each launch timed alone after an L2
+           flush with CUDA events on the library stream, against MEASURED_PEAKS.json;
+           `kernels` lists the same figure for every kernel kind.
 
 Multi-GPU (torchrun, one process per GPU): batch-1 decode does not shard; every rank runs
 its own replica (scaling "weak"); value = total tokens of all ranks / max-over-ranks time.
@@ -48,6 +54,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt-len", type=int, default=4096)
+    ap.add_argument("--context", default="synthetic", choices=["synthetic", "prefill"])
     ap.add_argument("--seed", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
@@ -216,7 +223,7 @@ def step_timeline(eng, steps: int):
     eng.enqueue_decode(steps)
     eng.sync()
     tl = eng.trace_timeline()
-    ph = eng.trace_read(64).astype(np.int64)
+    ph = eng.trace_read(1024).astype(np.int64)
     eng.trace_enable(False)
     t0 = tl[0][2]
     rows = [{"kind": k, "layer": l, "start_us": (s0 - t0) / 1e3, "ready_us": (r - t0) / 1e3, "end_us": (e - t0) / 1e3}
@@ -237,9 +244,40 @@ def step_timeline(eng, steps: int):
     rel = lambda a, b: [round((int(v) - int(ph[b])) / 1e3, 2) if v else None for v in ph[a:b + 9]] if ph[b] else None
     phases = {"attn_last_split_cta": [round((int(v) - int(ph[0])) / 1e3, 2) if v else None for v in ph[0:10]],
               "moe_topk_detail": [round((int(v) - int(ph[16])) / 1e3, 2) if v else None for v in ph[36:40]],
+              "attn_pages": [round((int(v) - int(ph[0])) / 1e3, 2) if v else None for v in ph[40:56]],
               "moe_cta0": [round((int(v) - int(ph[16])) / 1e3, 2) if v else None for v in ph[16:25]],
               "moe_last_cta": [round((int(v) - int(ph[26])) / 1e3, 2) if v else None for v in ph[26:35]]}
+    cta = ph[64:].reshape(-1, 6)
+    cta = cta[cta[:, 0] != 0]
+    if len(cta):  # decode attention of the last attention layer, per CTA (start-relative)
+        c0 = cta[:, 0].min()
+        q = lambda v: [round(float(np.min(v)), 2), round(float(np.median(v)), 2), round(float(np.max(v)), 2)]
+        phases["attn_ctas"] = {k: q((cta[:, i] - c0) / 1e3) for i, k in
+                               enumerate(["start", "ready", "pages_done", "merged", "end"])}
+        order = np.argsort(cta[:, 0])
+        phases["attn_ctas"]["by_start"] = [[round((cta[i, 0] - c0) / 1e3, 2), round((cta[i, 1] - c0) / 1e3, 2),
+                                            round((cta[i, 2] - c0) / 1e3, 2), round((cta[i, 4] - c0) / 1e3, 2),
+                                            int(cta[i, 5])] for i in order]
     return {"step_us": total, "by_kind": by, "phases_us": phases, "launches": rows}
+
+
+def synthetic_context(eng, cfg, n: int, seed: int) -> int:
+    """Imports n tokens of seeded synthetic context into slot 0 (KV pages of every attention
+    layer, recurrent state and conv window of every GDN layer) and returns a start token."""
+    from disk_streaming_moe_engine_b200 import synth
+    rng = np.random.default_rng(seed)
+    shape = (n, cfg.num_key_value_heads, cfg.head_dim)
+    for att in range(cfg.num_attention_layers()):
+        k = synth.f32_to_bf16(rng.standard_normal(shape, dtype=np.float32))
+        v = synth.f32_to_bf16(rng.standard_normal(shape, dtype=np.float32))
+        eng.kv_import(att, 0, k, v)
+    sshape = (cfg.linear_num_value_heads, cfg.linear_value_head_dim, cfg.linear_key_head_dim)
+    for g in range(cfg.num_gdn_layers()):
+        S = rng.standard_normal(sshape, dtype=np.float32) * np.float32(0.05)
+        conv = rng.standard_normal((3, cfg.qkv_dim), dtype=np.float32) * np.float32(0.05)
+        eng.gdn_state_import(g, 0, S, conv)
+    eng.seq_set_len(0, n)
+    return int(rng.integers(0, cfg.vocab_size))
 
 
 def run_reference(args, rank, world):
@@ -294,10 +332,13 @@ def run_ours(args, rank, local, world):
     eng.synth_on_device(args.seed)
     eng.weights_check()
     stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
-    prompt = np.random.default_rng(args.seed).integers(0, cfg.vocab_size, args.prompt_len).astype(np.int32)
     eng.seq_reset(0)
     t0 = time.perf_counter()
-    _, nxt = eng.forward(prompt, want_logits=False)  # untimed prefill, one decode step per token
+    if args.context == "prefill":
+        prompt = np.random.default_rng(args.seed).integers(0, cfg.vocab_size, args.prompt_len).astype(np.int32)
+        _, nxt = eng.forward(prompt, want_logits=False)  # untimed prefill, one decode step per token
+    else:
+        nxt = synthetic_context(eng, cfg, args.prompt_len, args.seed)
     prefill_s = time.perf_counter() - t0
     eng.set_token(nxt)
     eng.enqueue_decode(args.warmup)
@@ -341,9 +382,11 @@ def run_ours(args, rank, local, world):
             kernels[f"{tag}_{nm}"] = {"us": round(kms * 1e3, 2), "bytes": kb, "GBps": round(kb / kms / 1e6, 1)}
     kms, kb = eng.time_kernel(_lib.DM_KERNEL_HEAD, 0, 10)
     kernels["lm_head"] = {"us": round(kms * 1e3, 2), "bytes": kb, "GBps": round(kb / kms / 1e6, 1)}
-    dom = kernels["gdn_in_proj"]
+    for k in kernels.values():
+        k["frac"] = round(k["GBps"] / peak, 3)
+    dom = kernels["gdn_moe"]
     achieved = dom["bytes"] / (dom["us"] * 1e-6) / 1e9
-    traffic = profiled_traffic("gemv_gdn_in_proj_config2")
+    traffic = profiled_traffic("moe_fused_config1")
     sb = step_bytes(cfg, ctx_mid)
     per_gpu_tps = args.steps / (ms / 1e3)
 
@@ -367,14 +410,17 @@ def run_ours(args, rank, local, world):
         "metric": "decode tok/s, 35B-A3B-shape 4-bit, bs1", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (random-init weights on device, random prompt, seed 2)",
+        "data": "synthetic (random-init weights on device, seed 2)",
         "config": {"workload": "config2: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit g64 experts, bs1",
                    "global_batch": world, "seq_len": args.prompt_len, "parallelism": f"replicas x{world}",
+                   "context": ("synthetic KV pages + GDN state imported" if args.context == "synthetic"
+                               else "random prompt prefilled through the decode graph"),
                    "l2": "inputs larger than L2 (4 GB of weights per step)"},
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": peak_kind,
-                     "kernel": "gemv_bf16_kernel<2048,RMSNORM> GDN in-projection, 50.6 MB/launch"},
+                     "kernel": "moe_fused_kernel<2048,512,64> (layer 0): router + 8 routed + 1 shared expert, "
+                               "16.3 MB/launch, timed alone after an L2 flush"},
         "step_roofline": {"bytes_per_token": sb, "achieved_GBps": sb * per_gpu_tps / 1e9,
                           "frac": sb * per_gpu_tps / 1e9 / peak, "bytes": ALG_BYTES_NOTE},
         "kernels": kernels,
@@ -383,7 +429,7 @@ def run_ours(args, rank, local, world):
         "clocks_e2e": clocks_e2e.summary(),
         "gpu_launches": kps * args.steps,
         "timeline_by_kind": timeline,
-        "prefill_s": round(prefill_s, 2),
+        "context_setup_s": round(prefill_s, 2),
     }
     eng.close()
     if dist is not None:

@@ -32,6 +32,7 @@ bool attn_supported(int D, int grp);
 int attn_scores_cap(int max_pages, int nsplit);
 int attn_nsplit(int num_sms, int Hkv);
 cudaError_t launch_rope_table(cudaStream_t st, float2* tab, int capacity, int rot_dim, float theta);
+cudaError_t launch_l2_flush_read(cudaStream_t st, const void* buf, size_t bytes, int num_sms);
 cudaError_t launch_kv_copy(cudaStream_t st, uint16_t* kv_layer, const int* page_table_row, int Hkv,
                            int D, uint16_t* k, uint16_t* v, int n_tokens, int to_cache);
 cudaError_t launch_synth_bf16(cudaStream_t st, uint16_t* dst, uint64_t n, uint64_t seed,
@@ -77,6 +78,7 @@ struct dm_ctx {
     bool l2_prefetch = true;   // latency-bound kernels prefetch upcoming weights into L2
     uint64_t* trace_buf = nullptr;
     uint64_t* ktrace_buf = nullptr;
+    uint8_t* flush_buf = nullptr;  // L2 flush target of dm_time_kernel (allocated on first use)
     int trace_n = 0;
     std::vector<int> trace_kinds;
     std::string last_error;
@@ -479,6 +481,7 @@ int32_t dm_ctx_destroy(dm_ctx* c) {
     for (auto& g : c->graphs)
         if (g) cudaGraphExecDestroy(g);
     if (c->arena) cudaFree(c->arena);
+    if (c->flush_buf) cudaFree(c->flush_buf);
     if (c->h_io) cudaFreeHost(c->h_io);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -1138,7 +1141,8 @@ int32_t dm_time_kernel(dm_ctx* c, int32_t which, int32_t layer, int32_t iters, f
     const Dims& d = c->d;
     if (layer < 0 || layer >= d.L) return set_err(c, DM_ERR_INVALID_ARG, "PROFILE", "profile", layer, "layer out of range");
     const LayerW& w = c->layers[layer];
-    const LaunchCfg lc = lcfg(c);
+    LaunchCfg lc = lcfg(c);
+    lc.pdl = false;  // timed alone: nothing to overlap with
     const int slot = 0;
     const uint64_t H = d.H;
     auto launch = [&]() -> cudaError_t {
@@ -1172,17 +1176,31 @@ int32_t dm_time_kernel(dm_ctx* c, int32_t which, int32_t layer, int32_t iters, f
         default: return DM_ERR_INVALID_ARG;
     }
     cudaSetDevice(c->device);
+    // Each launch is timed alone after a read of kFlushBytes (twice the L2) has evicted
+    // what the previous launch left in L2, so every weight byte comes from HBM; a read
+    // leaves clean lines, as the weight streams of a decode step do, so the timed kernel
+    // pays no write-back for the flush.
+    constexpr size_t kFlushBytes = 256ull << 20;
+    if (!c->flush_buf) {
+        DM_CUDA(c, cudaMalloc(&c->flush_buf, kFlushBytes), "profile");
+        DM_CUDA(c, cudaMemsetAsync(c->flush_buf, 0, kFlushBytes, c->stream), "profile");
+    }
     cudaEvent_t e0, e1;
     DM_CUDA(c, cudaEventCreate(&e0), "profile");
     DM_CUDA(c, cudaEventCreate(&e1), "profile");
     cudaError_t e = launch();  // warm-up
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
-    if (e == cudaSuccess) e = cudaEventRecord(e0, c->stream);
-    for (int i = 0; i < iters && e == cudaSuccess; ++i) e = launch();
-    if (e == cudaSuccess) e = cudaEventRecord(e1, c->stream);
-    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
     float ms = 0.0f;
-    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    for (int i = 0; i < iters && e == cudaSuccess; ++i) {
+        e = launch_l2_flush_read(c->stream, c->flush_buf, kFlushBytes, c->num_sms);
+        if (e == cudaSuccess) e = cudaEventRecord(e0, c->stream);
+        if (e == cudaSuccess) e = launch();
+        if (e == cudaSuccess) e = cudaEventRecord(e1, c->stream);
+        if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+        float one = 0.0f;
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&one, e0, e1);
+        ms += one;
+    }
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "profile", layer, "%s", cudaGetErrorString(e));

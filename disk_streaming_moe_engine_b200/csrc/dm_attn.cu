@@ -23,7 +23,9 @@
 
 namespace dm {
 
-constexpr int kAttnCluster = 8;  // splits merged on chip per cluster
+constexpr int kAttnCluster = 4;  // splits merged on chip per cluster
+constexpr int kAT = 512;          // threads of a decode-attention CTA
+constexpr int kAW = kAT / 32;     // its warps
 
 struct AttnArgs {
     const float* qg;          // [2*Hq*D]
@@ -40,6 +42,7 @@ struct AttnArgs {
     unsigned* counters;       // [Hkv]
     const float2* rope;       // [capacity][rot_dim/2] (cos, sin)
     uint64_t* trace;          // phase stamps (CTA (0, last split), thread 0) or null
+    uint64_t* cta_trace;      // per-CTA stamps (kTrCtaSlots per CTA, thread 0) or null
     uint64_t* kt;             // launch timeline record or null
     const void* next_w;       // o_proj weights, prefetched into L2
     size_t next_bytes;
@@ -81,12 +84,12 @@ struct AttnGeom {
 };
 
 template <int D, int GRP>
-__global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+__global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
     using AG = AttnGeom<D>;
-    constexpr int EPL = D / 32;  // q/k elements per lane in the score loop
     extern __shared__ __align__(128) uint8_t ring[];
     __shared__ __align__(8) uint64_t bar[kAttnStages];
-    __shared__ __align__(16) float qsm[GRP][D];
+    constexpr int QST = D + 4;  // padded q row: the 8 heads of a score step hit 8 bank groups
+    __shared__ __align__(16) float qsm[GRP][QST];
     __shared__ __align__(16) float knew[D], vnew[D];
     __shared__ uint16_t kbits[D], vbits[D];
     __shared__ float sc[GRP][kPageTokens];
@@ -97,7 +100,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
 
     uint64_t* tr = (tid == 0 && g == 0 && s == gridDim.y - 1) ? a.trace : nullptr;
+    uint64_t* ct = (tid == 0 && a.cta_trace) ? a.cta_trace + (s * gridDim.x + g) * kTrCtaSlots : nullptr;
     trace_stamp(tr, 0);
+    trace_stamp(ct, 0);
     kt_start(a.kt);
     // positions < pos were written by earlier steps and the page table is fixed: the
     // range of this split and its first page tiles do not depend on the previous kernel
@@ -105,14 +110,15 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     const int n_tok = pos + 1;
     const int capacity = a.max_pages * kPageTokens;
     const bool in_range = pos >= 0 && pos < capacity;
-    int chunk = (n_tok + a.nsplit - 1) / a.nsplit;
-    chunk = (chunk + kPageTokens - 1) / kPageTokens * kPageTokens;
-    const int t0 = in_range ? s * chunk : 0;
-    const int t1 = in_range ? min(n_tok, t0 + chunk) : 0;
-    const int np = t1 > t0 ? (t1 - 1) / kPageTokens - t0 / kPageTokens + 1 : 0;
-    const int pg0 = t0 / kPageTokens;
+    // pages spread evenly over the splits (every split gets floor or ceil of the mean)
+    const int n_pg = in_range ? (n_tok + kPageTokens - 1) / kPageTokens : 0;
+    const int pg0 = static_cast<int>(static_cast<long long>(s) * n_pg / a.nsplit);
+    const int pg1 = static_cast<int>(static_cast<long long>(s + 1) * n_pg / a.nsplit);
+    const int np = pg1 - pg0;
+    const int t0 = pg0 * kPageTokens;
+    const int t1 = min(n_tok, pg1 * kPageTokens);
     __shared__ int pages[kMaxPagesPerSplit];
-    for (int i = tid; i < np && i < kMaxPagesPerSplit; i += 128) pages[i] = a.page_table[pg0 + i];
+    for (int i = tid; i < np && i < kMaxPagesPerSplit; i += kAT) pages[i] = a.page_table[pg0 + i];
     __syncthreads();
     auto issue = [&](int i) {  // page i of this split into its ring stage (thread 0 only)
         const int slot = i % kAttnStages;
@@ -141,16 +147,17 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     }
     __shared__ float qn_s[D], kn_s[D];
     __shared__ float2 cs_s[D / 2];
-    for (int i = tid; i < D; i += 128) {
+    for (int i = tid; i < D; i += kAT) {
         qn_s[i] = bf16_to_f32(a.q_norm[i]);
         kn_s[i] = bf16_to_f32(a.k_norm[i]);
     }
     if (in_range)
-        for (int i = tid; i < a.rot_dim / 2; i += 128) cs_s[i] = a.rope[static_cast<size_t>(pos) * (a.rot_dim / 2) + i];
+        for (int i = tid; i < a.rot_dim / 2; i += kAT) cs_s[i] = a.rope[static_cast<size_t>(pos) * (a.rot_dim / 2) + i];
     trace_stamp(tr, 1);
     pdl_wait();
     kt_ready(a.kt);
     trace_stamp(tr, 2);
+    trace_stamp(ct, 1);
     if (!in_range) {  // no room: report, touch nothing
         if (tid == 0 && s == 0) raise_error(a.err, DM_DEVERR_CAPACITY);
         kt_end(a.kt);
@@ -161,22 +168,23 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     // RMSNorm + RoPE in shared memory (norm weights and the RoPE row were staged before
     // the wait) ----
     {   // all loads issued together (one round trip), then stored
-        constexpr int QPT = GRP * D / 128, KPT = (D + 127) / 128;
+        constexpr int QPT = (GRP * D + kAT - 1) / kAT, KPT = (D + kAT - 1) / kAT;
         float qv[QPT], kv[KPT], vv[KPT];
         const float* qsrc = a.qg + static_cast<size_t>(g * GRP) * D;
 #pragma unroll
-        for (int i = 0; i < QPT; ++i) qv[i] = qsrc[tid + 128 * i];
+        for (int i = 0; i < QPT; ++i) qv[i] = tid + kAT * i < GRP * D ? qsrc[tid + kAT * i] : 0.0f;
 #pragma unroll
         for (int i = 0; i < KPT; ++i) {
-            const int d = tid + 128 * i;
+            const int d = tid + kAT * i;
             kv[i] = d < D ? a.kvnew[static_cast<size_t>(g) * D + d] : 0.0f;
             vv[i] = d < D ? a.kvnew[static_cast<size_t>(a.Hkv + g) * D + d] : 0.0f;
         }
 #pragma unroll
-        for (int i = 0; i < QPT; ++i) (&qsm[0][0])[tid + 128 * i] = qv[i];
+        for (int i = 0; i < QPT; ++i)
+            if (tid + kAT * i < GRP * D) qsm[(tid + kAT * i) / D][(tid + kAT * i) % D] = qv[i];
 #pragma unroll
         for (int i = 0; i < KPT; ++i) {
-            const int d = tid + 128 * i;
+            const int d = tid + kAT * i;
             if (d < D) {
                 knew[d] = kv[i];
                 vnew[d] = vv[i];
@@ -185,7 +193,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     }
     __syncthreads();
     trace_stamp(tr, 8);
-    for (int hh = warp; hh < GRP + 1; hh += 4) {
+    for (int hh = warp; hh < GRP + 1; hh += kAW) {
         float* v = hh < GRP ? qsm[hh] : knew;
         const float* wn = hh < GRP ? qn_s : kn_s;
         float ss = 0.0f;
@@ -205,7 +213,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     }
     __syncthreads();
     trace_stamp(tr, 9);
-    for (int d = tid; d < D; d += 128) {
+    for (int d = tid; d < D; d += kAT) {
         const uint16_t kb = f32_to_bf16(knew[d]);
         kbits[d] = kb;
         knew[d] = bf16_to_f32(kb);
@@ -227,61 +235,79 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
                            static_cast<size_t>(pos % kPageTokens) * D;
             uint16_t* vd = a.kv + ((static_cast<size_t>(page) * 2 + 1) * a.Hkv + g) * kPageTokens * D +
                            static_cast<size_t>(pos % kPageTokens) * D;
-            for (int d = tid; d < D; d += 128) {
+            for (int d = tid; d < D; d += kAT) {
                 kd[d] = kbits[d];
                 vd[d] = vbits[d];
             }
         }
     }
 
-    // q of this warp's lanes in registers: element e of head hh = q[hh][lane*EPL + e]
-    float qr[GRP][EPL];
-#pragma unroll
-    for (int hh = 0; hh < GRP; ++hh)
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) qr[hh][e] = qsm[hh][lane * EPL + e];
     const float sm_scale = 1.0f / sqrtf(static_cast<float>(D));
-    constexpr int DPT = (D + 127) / 128;  // V dims per thread
-    float acc[GRP][DPT];
+    // V mapping: accumulator element idx = tid + kAT * k (k < NA) is head idx / D, dim
+    // idx % D; D divides kAT, so a thread's elements share the dim v_d = tid % D
+    static_assert(kAT % D == 0, "D must divide the CTA size");
+    constexpr int NA = (GRP * D + kAT - 1) / kAT;
+    const int v_d = tid % D, v_h0 = tid / D;
+    constexpr int VHS = kAT / D;  // head stride between a thread's elements
+    const bool v_on = v_h0 < GRP;
+    float acc[NA];
 #pragma unroll
-    for (int hh = 0; hh < GRP; ++hh)
-#pragma unroll
-        for (int j = 0; j < DPT; ++j) acc[hh][j] = 0.0f;
+    for (int k = 0; k < NA; ++k) acc[k] = 0.0f;
+    // score mapping: TPP threads per (token, head) pair, thread part p takes the 8-dim
+    // blocks p, p + TPP, ... (adjacent parts read adjacent 16-byte words)
+    constexpr int TPP = kAT / (kPageTokens * GRP);
+    static_assert(TPP >= 1 && kAT % (kPageTokens * GRP) == 0 && (D / 8) % TPP == 0,
+                  "the CTA must cover 16 tokens x GRP heads");
+    const int pair = tid / TPP, part = tid % TPP;
+    const int s_tt = pair / GRP, s_hh = pair % GRP;
+    const float4* q4 = reinterpret_cast<const float4*>(qsm[s_hh]);
 
     for (int i = 0; i < np; ++i) {
         const int slot = i % kAttnStages;
         const bool ok = mbar_wait_bounded(&bar[slot], (i / kAttnStages) & 1, a.err, nullptr);
+        uint64_t* trp = (tr && i < 4) ? tr + 40 + 4 * i : nullptr;  // per-page stamps, pages 0-3
+        trace_stamp(trp, 0);
         const uint16_t* kt = reinterpret_cast<const uint16_t*>(ring + static_cast<size_t>(slot) * AG::STAGE);
         const uint16_t* vt = kt + kPageTokens * D;
         const int tp = (pg0 + i) * kPageTokens;  // position of the page's first token
-        // scores: warp w -> tokens w, w+4, w+8, w+12 of the page
-        for (int tt = warp; tt < kPageTokens; tt += 4) {
-            const int t = tp + tt;
-            float kf[EPL];
+        {   // score of token s_tt for head s_hh: eight independent partial sums
+            const int t = tp + s_tt;
+            float pa[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) pa[e] = 0.0f;
             if (t == pos) {
-#pragma unroll
-                for (int e = 0; e < EPL; ++e) kf[e] = knew[lane * EPL + e];
-            } else if (EPL == 8) {
-                const uint4 u = *reinterpret_cast<const uint4*>(kt + tt * D + lane * 8);
-                kf[0] = bf16lo(u.x); kf[1] = bf16hi(u.x); kf[2] = bf16lo(u.y); kf[3] = bf16hi(u.y);
-                kf[4] = bf16lo(u.z); kf[5] = bf16hi(u.z); kf[6] = bf16lo(u.w); kf[7] = bf16hi(u.w);
+                const float4* k4 = reinterpret_cast<const float4*>(knew);
+#pragma unroll 4
+                for (int j = part; j < D / 8; j += TPP) {
+                    const float4 k0 = k4[2 * j], k1 = k4[2 * j + 1];
+                    const float4 q0 = q4[2 * j], q1 = q4[2 * j + 1];
+                    pa[0] = fmaf(q0.x, k0.x, pa[0]); pa[1] = fmaf(q0.y, k0.y, pa[1]);
+                    pa[2] = fmaf(q0.z, k0.z, pa[2]); pa[3] = fmaf(q0.w, k0.w, pa[3]);
+                    pa[4] = fmaf(q1.x, k1.x, pa[4]); pa[5] = fmaf(q1.y, k1.y, pa[5]);
+                    pa[6] = fmaf(q1.z, k1.z, pa[6]); pa[7] = fmaf(q1.w, k1.w, pa[7]);
+                }
             } else {
-#pragma unroll
-                for (int e = 0; e < EPL; ++e) kf[e] = bf16_to_f32(kt[tt * D + lane * EPL + e]);
+                const uint4* kr = reinterpret_cast<const uint4*>(kt + s_tt * D);
+#pragma unroll 4
+                for (int j = part; j < D / 8; j += TPP) {
+                    const uint4 u = kr[j];
+                    const float4 q0 = q4[2 * j], q1 = q4[2 * j + 1];
+                    pa[0] = fmaf(q0.x, bf16lo(u.x), pa[0]); pa[1] = fmaf(q0.y, bf16hi(u.x), pa[1]);
+                    pa[2] = fmaf(q0.z, bf16lo(u.y), pa[2]); pa[3] = fmaf(q0.w, bf16hi(u.y), pa[3]);
+                    pa[4] = fmaf(q1.x, bf16lo(u.z), pa[4]); pa[5] = fmaf(q1.y, bf16hi(u.z), pa[5]);
+                    pa[6] = fmaf(q1.z, bf16lo(u.w), pa[6]); pa[7] = fmaf(q1.w, bf16hi(u.w), pa[7]);
+                }
             }
+            float p = ((pa[0] + pa[1]) + (pa[2] + pa[3])) + ((pa[4] + pa[5]) + (pa[6] + pa[7]));
+#pragma unroll
+            for (int m = 1; m < TPP; m <<= 1) p += __shfl_xor_sync(0xffffffffu, p, m);
             const bool valid = ok && t >= t0 && t < t1;
-#pragma unroll
-            for (int hh = 0; hh < GRP; ++hh) {
-                float p = 0.0f;
-#pragma unroll
-                for (int e = 0; e < EPL; ++e) p = fmaf(qr[hh][e], kf[e], p);
-                p = warp_sum(p);
-                if (lane == 0) sc[hh][tt] = valid ? p * sm_scale : -INFINITY;
-            }
+            if (part == 0) sc[s_hh][s_tt] = valid ? p * sm_scale : -INFINITY;
         }
         __syncthreads();
+        trace_stamp(trp, 1);
         // online softmax update, one warp per head: lanes 0..15 hold the page's scores
-        for (int hh = warp; hh < GRP; hh += 4) {
+        for (int hh = warp; hh < GRP; hh += kAW) {
             const float sv = lane < kPageTokens ? sc[hh][lane] : -INFINITY;
             const float mp = warp_max(sv);
             const float mo = m_run[hh];
@@ -297,26 +323,26 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
             }
         }
         __syncthreads();
-        // V: thread owns dims tid, tid + 128, ...
+        trace_stamp(trp, 2);
+        // V: the thread's NA accumulators (one dim, heads v_h0, v_h0 + VHS, ...)
+        if (v_on) {
 #pragma unroll
-        for (int j = 0; j < DPT; ++j) {
-            const int d = tid + 128 * j;
-            if (d < D) {
+            for (int k = 0; k < NA; ++k) acc[k] *= scale[v_h0 + VHS * k];
+#pragma unroll 4
+            for (int tt = 0; tt < kPageTokens; ++tt) {
+                const int t = tp + tt;
+                const float v = (t == pos) ? vnew[v_d] : bf16_to_f32(vt[tt * D + v_d]);
 #pragma unroll
-                for (int hh = 0; hh < GRP; ++hh) acc[hh][j] *= scale[hh];
-                for (int tt = 0; tt < kPageTokens; ++tt) {
-                    const int t = tp + tt;
-                    const float v = (t == pos) ? vnew[d] : bf16_to_f32(vt[tt * D + d]);
-#pragma unroll
-                    for (int hh = 0; hh < GRP; ++hh) acc[hh][j] = fmaf(sc[hh][tt], v, acc[hh][j]);
-                }
+                for (int k = 0; k < NA; ++k) acc[k] = fmaf(sc[v_h0 + VHS * k][tt], v, acc[k]);
             }
         }
         __syncthreads();  // stage free and sc reusable
+        trace_stamp(trp, 3);
         if (tid == 0 && i + kAttnStages < np) issue(i + kAttnStages);
     }
 
     trace_stamp(tr, 4);
+    trace_stamp(ct, 2);
     // ---- merge 1: the kAttnCluster splits of this cluster through distributed shared
     // memory: every CTA pushes its partial into rank 0's (free) ring, rank 0 merges
     // locally and writes one partial (max, sum, acc) per head for the cluster ----
@@ -327,13 +353,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     static_assert(kAttnCluster * PSZ * 4 <= AG::RING, "ring too small for the cluster merge");
     cluster.sync();                                    // every ring is free from here on
     float* dst0 = cluster.map_shared_rank(reinterpret_cast<float*>(ring), 0) + crank * PSZ;
+    if (v_on)
 #pragma unroll
-    for (int j = 0; j < DPT; ++j) {
-        const int d = tid + 128 * j;
-        if (d < D)
-#pragma unroll
-            for (int hh = 0; hh < GRP; ++hh) dst0[hh * D + d] = acc[hh][j];
-    }
+        for (int k = 0; k < NA; ++k) dst0[(v_h0 + VHS * k) * D + v_d] = acc[k];
     if (tid < GRP) {
         dst0[GRP * D + tid] = np > 0 ? m_run[tid] : -INFINITY;
         dst0[GRP * D + GRP + tid] = np > 0 ? l_run[tid] : 0.0f;
@@ -342,7 +364,14 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     const int cid = s / kAttnCluster;
     cluster.sync();                                    // all partials are in rank 0
     trace_stamp(tr, 5);
+    trace_stamp(ct, 3);
+    if (ct) {
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        ct[5] = smid;
+    }
     if (crank != 0) {
+        trace_stamp(ct, 4);
         kt_end(a.kt);
         return;
     }
@@ -367,7 +396,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
             cl[tid] = L;
         }
         __syncthreads();
-        for (int o = tid; o < GRP * D; o += 128) {
+        for (int o = tid; o < GRP * D; o += kAT) {
             const int hh = o / D;
             float v = 0.0f;
 #pragma unroll
@@ -389,6 +418,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
     __syncthreads();
     trace_stamp(tr, 6);
     if (!is_last) {
+        trace_stamp(ct, 4);
         kt_end(a.kt);
         return;
     }
@@ -396,7 +426,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
 
     // ---- merge 2: the cluster partials of every head of this KV group, output gate ----
     const int ns = ccount;
-    for (int hh = warp; hh < GRP; hh += 4) {
+    for (int hh = warp; hh < GRP; hh += kAW) {
         const float* ph = a.part + static_cast<size_t>(g * GRP + hh) * kMaxSplits * (D + 2);
         const float ml = lane < ns ? __ldcg(ph + lane * (D + 2) + D) : -INFINITY;
         const float ll = lane < ns ? __ldcg(ph + lane * (D + 2) + D + 1) : 0.0f;
@@ -406,23 +436,34 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const __grid_constant_
         if (lane < kMaxSplits) wsp[hh][lane] = wk / L;
     }
     __syncthreads();
-    for (int o = tid; o < GRP * D; o += 128) {
+    // every cluster partial of an output is loaded in one batch (fixed bound, unrolled)
+    constexpr int kMaxClusters = kMaxSplits / kAttnCluster;
+#pragma unroll 2
+    for (int o = tid; o < GRP * D; o += kAT) {
         const int hh = o / D, d = o % D;
         const int hq = g * GRP + hh;
         const float* ph = a.part + static_cast<size_t>(hq) * kMaxSplits * (D + 2) + d;
-        float acc2 = 0.0f;
-        for (int c = 0; c < ns; ++c) acc2 = fmaf(wsp[hh][c], __ldcg(ph + static_cast<size_t>(c) * (D + 2)), acc2);
+        float pv[kMaxClusters];
+#pragma unroll
+        for (int c = 0; c < kMaxClusters; ++c) pv[c] = c < ns ? __ldcg(ph + static_cast<size_t>(c) * (D + 2)) : 0.0f;
         const float gate = a.qg[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
+        float acc2 = 0.0f;
+#pragma unroll
+        for (int c = 0; c < kMaxClusters; ++c) acc2 = fmaf(wsp[hh][c], pv[c], acc2);
         a.out[static_cast<size_t>(hq) * D + d] = acc2 * sigmoid_f(gate);
     }
     if (tid == 0) a.counters[g] = 0u;
     if (tid == 0 && a.trace) a.trace[7] = globaltimer_ns();
+    trace_stamp(ct, 4);
     __syncthreads();
     kt_end(a.kt);
 }
 
+// Dynamic shared memory of a CTA: the page ring, and at least 120 KB so that one CTA
+// runs per SM (two would share an SM's issue slots while other SMs stay idle).
 size_t attn_ring_bytes(int D) {
-    return static_cast<size_t>(kAttnStages) * 2 * 2 * kPageTokens * D;
+    const size_t ring = static_cast<size_t>(kAttnStages) * 2 * 2 * kPageTokens * D;
+    return ring > 120 * 1024 ? ring : 120 * 1024;
 }
 
 int attn_scores_cap(int max_pages, int nsplit) {
@@ -451,7 +492,10 @@ cudaError_t attn_set_attrs(int max_scores_smem) {
 #define DM_ATTN_ATTR(DD, GG)                                                                      \
     if (e == cudaSuccess)                                                                         \
         e = cudaFuncSetAttribute(attn_decode_kernel<DD, GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                 max_scores_smem);
+                                 max_scores_smem);                                                \
+    if (e == cudaSuccess) /* largest shared-memory carve-out: two CTAs per SM */                    \
+        e = cudaFuncSetAttribute(attn_decode_kernel<DD, GG>,                                      \
+                                 cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     DM_ATTN_INSTANCES(DM_ATTN_ATTR)
 #undef DM_ATTN_ATTR
     return e;
@@ -481,18 +525,20 @@ cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW&
     a.counters = b.counters + kCntAttnBase;
     a.rope = b.rope;
     a.trace = b.trace ? b.trace + kTrAttn : nullptr;
+    a.cta_trace = b.trace ? b.trace + kTrCta : nullptr;
     a.kt = lc.kt;
     a.next_w = lc.l2_prefetch ? w.w_out : nullptr;
     a.next_bytes = static_cast<size_t>(d.H) * d.Hq * d.D * 2;
     a.err = b.err;
     const int grp = d.Hq / d.Hkv;
     const dim3 grid(d.Hkv, a.nsplit);
+    if (a.cta_trace && grid.x * grid.y * kTrCtaSlots > kTraceSlots - kTrCta) a.cta_trace = nullptr;
     const size_t smem = attn_ring_bytes(d.D);
 #define DM_ATTN_LAUNCH(DD, GG)                                                                 \
     if (d.D == DD && grp == GG) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<DD, GG>, a);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(kAT);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = lc.stream;
     cudaLaunchAttribute attr[2];

@@ -366,8 +366,8 @@ DM_DEV unsigned ld_acquire_u32(const unsigned* p) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-DM_DEV void st_release_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+DM_DEV void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 DM_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
     unsigned long long v;
@@ -679,10 +679,13 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                         a.ids[r] = sid[r];
                         words[r >> 2] |= static_cast<unsigned long long>(sid[r]) << (15 * (r & 3));
                     }
-                // publish: the released words carry the ids; probs / gate are ordered before
+                // publish: each 64-bit word carries its ids and the marker, so readers need
+                // nothing else from this thread before phase 3; probs and the shared gate
+                // reach phase 3 through this thread's release of the up-phase barrier.
+                // Relaxed stores: no fence on the critical path.
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                    if (k < (a.topk + 3) / 4) st_release_u64(&a.idflag[k], words[k] | (1ull << 63));
+                    if (k < (a.topk + 3) / 4) st_relaxed_u64(&a.idflag[k], words[k] | (1ull << 63));
                 trace_stamp(tr ? tr + 20 : nullptr, 3);
             }
         }

@@ -51,19 +51,34 @@ def main():
             eng.forward_port_block(x, a.layer, a.ctx)
         us_ms, nbytes = eng.time_kernel(KERNELS[a.kernel], a.layer, a.iters)
         phases = None
+        ctas = None
         if a.trace:  # one more launch with phase stamps (ns relative to the kernel's start)
             eng.trace_enable(True)
             eng.time_kernel(KERNELS[a.kernel], a.layer, 1)
-            t = eng.trace_read(64).astype(np.int64)
+            t = eng.trace_read(1024).astype(np.int64)
             eng.trace_enable(False)
             base = {"core": 0, "moe": 16}.get(a.kernel, 0)
+            cta = t[64:].reshape(-1, 6)
+            cta = cta[cta[:, 0] != 0]
+            if len(cta):  # per-CTA stamps (decode attention): start, ready, pages done, merged, end, SM
+                t0 = cta[:, 0].min()
+                rel = lambda c: np.round((cta[:, c] - t0) / 1e3, 2)
+                q = lambda v: [float(np.min(v)), float(np.median(v)), float(np.max(v))]
+                order = np.argsort(cta[:, 0])
+                ctas = {"n": int(len(cta)), "start_us": q(rel(0)), "ready_us": q(rel(1)), "pages_done_us": q(rel(2)),
+                        "merged_us": q(rel(3)), "end_us": q(rel(4)),
+                        "by_start": [[float(rel(0)[i]), float(rel(2)[i]), float(rel(4)[i]), int(cta[i, 5])]
+                                     for i in order]}
             if a.kernel == "moe":
                 phases = {"cta0": [int(v - t[16]) if v else None for v in t[16:25]],
                           "last": [int(v - t[26]) if v else None for v in t[26:35]]}
             else:
-                phases = [int(v - t[base]) if v else None for v in t[base:base + 8]]
+                phases = [int(v - t[base]) if v else None for v in t[base:base + 10]]
+                if a.kernel == "core":  # per-page stamps of the traced attention CTA
+                    phases += [int(v - t[0]) if v else None for v in t[40:56]]
     print(json.dumps({"kernel": a.kernel, "preset": a.preset, "layer": a.layer, "ctx": a.ctx,
-                      "us": us_ms * 1e3, "bytes": nbytes, "GBps": nbytes / us_ms / 1e6, "phases_ns": phases}))
+                      "us": us_ms * 1e3, "bytes": nbytes, "GBps": nbytes / us_ms / 1e6, "phases_ns": phases,
+                      "ctas": ctas}))
 
 
 if __name__ == "__main__":

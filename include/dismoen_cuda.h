@@ -281,9 +281,10 @@ int32_t dm_get_stream(dm_ctx* ctx, void** stream_out);
 /* Number of kernel launches one decode step performs (for launch accounting). */
 int32_t dm_kernels_per_step(dm_ctx* ctx, int32_t* out);
 
-/* Times `iters` back-to-back launches of one kernel kind of layer `layer` (inputs as left
- * by the last step) with CUDA events on the context stream; avg_ms = mean launch time,
- * bytes = the algorithmic HBM bytes one launch must move (weights, state, KV). */
+/* Times `iters` launches of one kernel kind of layer `layer` (inputs as left by the last
+ * step) with CUDA events on the context stream, each launch alone and after a 256 MB read
+ * that evicts the L2 (allocated on the first call, freed with the context); avg_ms = mean
+ * launch time, bytes = the algorithmic HBM bytes one launch must move (weights, state, KV). */
 #define DM_KERNEL_MIXER_IN 0   /* GDN or attention input projection GEMV (+RMSNorm)     */
 #define DM_KERNEL_MIXER_OUT 1  /* output projection GEMV (+head norm / gate, residual)  */
 #define DM_KERNEL_MIXER_CORE 2 /* GDN recurrence or paged decode attention              */
@@ -294,8 +295,9 @@ int32_t dm_time_kernel(dm_ctx* ctx, int32_t which, int32_t layer, int32_t iters,
                        uint64_t* bytes);
 
 /* Phase tracing (the role of the reference's SchedulerTimings, port_scheduler.mojo:46):
- * when on, kernels stamp %globaltimer (ns) at their phase boundaries into a 64-slot
- * device buffer; slots 0-7 decode attention (start, page loads issued, inputs ready,
+ * when on, kernels stamp %globaltimer (ns) at their phase boundaries into a 1024-slot
+ * device buffer; slots 64.. hold 6 per decode-attention CTA (CTA = split * Hkv + kv head:
+ * start, ready, pages done, cluster merged, end, SM id); slots 0-7 decode attention (start, page loads issued, inputs ready,
  * q/k ready, pages done, cluster merged, counted in, output), slots 16-24 the MoE kernel
  * of CTA 0 (start, inputs ready, normalised, router rows done, router complete, ids known,
  * experts up done, barrier passed, done) and 26-34 the same for the last CTA.  Turning
