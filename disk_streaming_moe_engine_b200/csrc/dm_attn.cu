@@ -76,28 +76,75 @@ constexpr int kAttnStages = 6;   // K+V page tiles in flight per CTA
 constexpr int kMaxPagesPerSplit = 256;  // page ids staged in shared memory
 
 // One KV page tile (16 tokens x D, K then V) per ring stage.
+// One KV page (16 tokens, one head) per ring stage: K rows then V rows, each row padded
+// to RS bytes so that the 8 rows an ldmatrix reads fall in distinct bank groups.
 template <int D>
 struct AttnGeom {
-    static constexpr int TILE = kPageTokens * D * 2;     // bytes of K (or V) of one page, one head
+    static constexpr int RS = (D + 8) * 2;               // bytes of one staged row
+    static constexpr int TILE = kPageTokens * RS;        // K (or V) of one page
     static constexpr int STAGE = 2 * TILE;
     static constexpr int RING = kAttnStages * STAGE;
 };
 
+// mma.sync m16n8k16, bf16 inputs, fp32 accumulate (fragment layouts of the PTX ISA:
+// g = lane / 4, t = lane % 4; A a0 = A[g][2t..2t+1], a1 = A[g+8][..], a2 = A[g][2t+8..],
+// a3 = A[g+8][2t+8..]; B b0 = B[2t..2t+1][g], b1 = B[2t+8..2t+9][g];
+// C c0 = C[g][2t], c1 = C[g][2t+1], c2 = C[g+8][2t], c3 = C[g+8][2t+1]).
+DM_DEV void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+DM_DEV void ldsm_x2(uint32_t& r0, uint32_t& r1, const void* row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r0), "=r"(r1)
+                 : "r"(smem_u32(row_addr)));
+}
+DM_DEV void ldsm_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(row_addr)));
+}
+DM_DEV uint32_t pack_bf16x2(uint16_t lo, uint16_t hi) { return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16); }
+DM_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Split-K ("flash-decoding") decode attention over the paged bf16 KV cache.
+// Grid (Hkv, nsplit), clusters of kAttnCluster splits, kAT threads, one CTA per SM.
+//   pre-wait  page ids of the split, every page of the split (up to kAttnStages) in
+//             flight as per-row bulk copies into padded shared rows, norm weights and the
+//             RoPE row staged
+//   post-wait q heads of the group, new k, v: per-head RMSNorm + RoPE (fp32), k/v rounded
+//             to bf16, appended at pos by split 0 and patched into the staged page
+//   scores    tensor cores: S = Q K^T with q = q_hi + q_lo (two bf16 terms, fp32
+//             accumulation; K is bf16), one warp per 8-token n-tile
+//   softmax   per head over the batch, online across batches (max shift, expf)
+//   P V       tensor cores: O += (p_hi + p_lo) V, each warp 16 output dims
+//   merge     splits of a cluster through distributed shared memory, then the cluster
+//             partials of a head by the CTAs of the last cluster to finish, with the
+//             sigmoid output gate (reference attention.mojo:219-435 in decode form).
 template <int D, int GRP>
 __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
     using AG = AttnGeom<D>;
+    static_assert(GRP <= 8, "heads of a KV group are rows 0..7 of the m16 tile");
     extern __shared__ __align__(128) uint8_t ring[];
     __shared__ __align__(8) uint64_t bar[kAttnStages];
-    constexpr int QST = D + 4;  // padded q row: the 8 heads of a score step hit 8 bank groups
+    constexpr int QST = D + 4;  // fp32 q rows (norm / RoPE)
     __shared__ __align__(16) float qsm[GRP][QST];
+    constexpr int QBS = D + 8;  // bf16 q rows: 8 rows of an A fragment hit distinct banks
+    __shared__ __align__(16) uint16_t qh[GRP][QBS], ql[GRP][QBS];
+    constexpr int NT = kAttnStages * kPageTokens;  // tokens of a full batch
+    constexpr int PBS = NT + 8;
+    __shared__ __align__(16) uint16_t ph[GRP][PBS], pl[GRP][PBS];
     __shared__ __align__(16) float knew[D], vnew[D];
-    __shared__ uint16_t kbits[D], vbits[D];
-    __shared__ float sc[GRP][kPageTokens];
+    __shared__ __align__(16) uint16_t kbits[D], vbits[D];
+    __shared__ float sc[GRP][NT];
     __shared__ float m_run[GRP], l_run[GRP], scale[GRP];
-    __shared__ float wsp[GRP][kMaxSplits];
-    __shared__ int is_last;
+    __shared__ int last_flag;
     const int g = blockIdx.x, s = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int fg = lane >> 2, ft = lane & 3;  // fragment row / column-pair of this lane
 
     uint64_t* tr = (tid == 0 && g == 0 && s == gridDim.y - 1) ? a.trace : nullptr;
     uint64_t* ct = (tid == 0 && a.cta_trace) ? a.cta_trace + (s * gridDim.x + g) * kTrCtaSlots : nullptr;
@@ -105,7 +152,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     trace_stamp(ct, 0);
     kt_start(a.kt);
     // positions < pos were written by earlier steps and the page table is fixed: the
-    // range of this split and its first page tiles do not depend on the previous kernel
+    // range of this split and its page tiles do not depend on the previous kernel
     const int pos = *a.pos;
     const int n_tok = pos + 1;
     const int capacity = a.max_pages * kPageTokens;
@@ -119,28 +166,36 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     const int t1 = min(n_tok, pg1 * kPageTokens);
     __shared__ int pages[kMaxPagesPerSplit];
     for (int i = tid; i < np && i < kMaxPagesPerSplit; i += kAT) pages[i] = a.page_table[pg0 + i];
-    __syncthreads();
-    auto issue = [&](int i) {  // page i of this split into its ring stage (thread 0 only)
-        const int slot = i % kAttnStages;
-        uint8_t* dst = ring + static_cast<size_t>(slot) * AG::STAGE;
-        const int page = i < kMaxPagesPerSplit ? pages[i] : a.page_table[pg0 + i];
-        if (page < 0 || page >= a.num_pages) {
-            raise_error(a.err, DM_DEVERR_PAGE);
-            mbar_arrive(&bar[slot]);  // no copy: the tile is left as is and masked below
-            return;
-        }
-        mbar_arrive_expect_tx(&bar[slot], AG::STAGE);
-        const uint16_t* kt = a.kv + ((static_cast<size_t>(page) * 2 + 0) * a.Hkv + g) * kPageTokens * D;
-        const uint16_t* vt = a.kv + ((static_cast<size_t>(page) * 2 + 1) * a.Hkv + g) * kPageTokens * D;
-        bulk_g2s(dst, kt, AG::TILE, &bar[slot]);
-        bulk_g2s(dst + AG::TILE, vt, AG::TILE, &bar[slot]);
-    };
-    prefetch_l2_share(a.next_w, a.next_bytes, s * gridDim.x + g, gridDim.x * gridDim.y, tid);
     if (tid == 0) {
         for (int i = 0; i < kAttnStages; ++i) mbar_init(&bar[i], 1);
         mbar_fence_init();
-        for (int i = 0; i < np && i < kAttnStages; ++i) issue(i);
     }
+    __syncthreads();
+    // page i of the split into its ring stage: 16 K rows and 16 V rows, one bulk copy
+    // each, by the 32 lanes of warp 0 (row r < 16: K row r; r >= 16: V row r - 16)
+    auto issue = [&](int i) {
+        const int slot = i % kAttnStages;
+        const int page = i < kMaxPagesPerSplit ? pages[i] : a.page_table[pg0 + i];
+        const bool good = page >= 0 && page < a.num_pages;
+        if (lane == 0) {
+            if (good) {
+                mbar_arrive_expect_tx(&bar[slot], 2 * kPageTokens * D * 2);
+            } else {
+                raise_error(a.err, DM_DEVERR_PAGE);
+                mbar_arrive(&bar[slot]);  // no copy: the tile is left as is and masked below
+            }
+        }
+        __syncwarp();
+        if (good) {
+            const int kv = lane >> 4, r = lane & 15;
+            const uint16_t* src =
+                a.kv + ((static_cast<size_t>(page) * 2 + kv) * a.Hkv + g) * kPageTokens * D + static_cast<size_t>(r) * D;
+            bulk_g2s(ring + static_cast<size_t>(slot) * AG::STAGE + kv * AG::TILE + r * AG::RS, src, D * 2, &bar[slot]);
+        }
+    };
+    if (warp == 0)
+        for (int i = 0; i < np && i < kAttnStages; ++i) issue(i);
+    prefetch_l2_share(a.next_w, a.next_bytes, s * gridDim.x + g, gridDim.x * gridDim.y, tid);
     if (tid < GRP) {
         m_run[tid] = -INFINITY;
         l_run[tid] = 0.0f;
@@ -167,7 +222,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     // ---- q heads of this KV group, new k, new v: one parallel load, then per-head
     // RMSNorm + RoPE in shared memory (norm weights and the RoPE row were staged before
     // the wait) ----
-    {   // all loads issued together (one round trip), then stored
+    {
         constexpr int QPT = (GRP * D + kAT - 1) / kAT, KPT = (D + kAT - 1) / kAT;
         float qv[QPT], kv[KPT], vv[KPT];
         const float* qsrc = a.qg + static_cast<size_t>(g * GRP) * D;
@@ -213,13 +268,19 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     }
     __syncthreads();
     trace_stamp(tr, 9);
+    // k, v rounded to bf16 (cache format); q as hi + lo bf16 terms for the tensor cores
+    const float sm_scale = 1.0f / sqrtf(static_cast<float>(D));
     for (int d = tid; d < D; d += kAT) {
         const uint16_t kb = f32_to_bf16(knew[d]);
         kbits[d] = kb;
-        knew[d] = bf16_to_f32(kb);
         const uint16_t vb = f32_to_bf16(vnew[d]);
         vbits[d] = vb;
-        vnew[d] = bf16_to_f32(vb);
+    }
+    for (int i = tid; i < GRP * D; i += kAT) {
+        const float q = qsm[i / D][i % D];
+        const uint16_t hi = f32_to_bf16(q);
+        qh[i / D][i % D] = hi;
+        ql[i / D][i % D] = f32_to_bf16(q - bf16_to_f32(hi));
     }
     __syncthreads();
     pdl_launch_dependents();
@@ -242,79 +303,91 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
         }
     }
 
-    const float sm_scale = 1.0f / sqrtf(static_cast<float>(D));
-    // V mapping: accumulator element idx = tid + kAT * k (k < NA) is head idx / D, dim
-    // idx % D; D divides kAT, so a thread's elements share the dim v_d = tid % D
-    static_assert(kAT % D == 0, "D must divide the CTA size");
-    constexpr int NA = (GRP * D + kAT - 1) / kAT;
-    const int v_d = tid % D, v_h0 = tid / D;
-    constexpr int VHS = kAT / D;  // head stride between a thread's elements
-    const bool v_on = v_h0 < GRP;
-    float acc[NA];
-#pragma unroll
-    for (int k = 0; k < NA; ++k) acc[k] = 0.0f;
-    // score mapping: TPP threads per (token, head) pair, thread part p takes the 8-dim
-    // blocks p, p + TPP, ... (adjacent parts read adjacent 16-byte words)
-    constexpr int TPP = kAT / (kPageTokens * GRP);
-    static_assert(TPP >= 1 && kAT % (kPageTokens * GRP) == 0 && (D / 8) % TPP == 0,
-                  "the CTA must cover 16 tokens x GRP heads");
-    const int pair = tid / TPP, part = tid % TPP;
-    const int s_tt = pair / GRP, s_hh = pair % GRP;
-    const float4* q4 = reinterpret_cast<const float4*>(qsm[s_hh]);
+    // output accumulators: warp w owns output dims [16w, 16w + 16) (two n8 tiles) while
+    // 16w < D; c0, c1 of tile u are head fg, dims 16w + 8u + 2ft, +1
+    const bool pv_on = 16 * warp < D;
+    float oacc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+    const int ip_new = pos / kPageTokens - pg0;  // page of the split holding pos, if any
 
-    for (int i = 0; i < np; ++i) {
-        const int slot = i % kAttnStages;
-        const bool ok = mbar_wait_bounded(&bar[slot], (i / kAttnStages) & 1, a.err, nullptr);
-        uint64_t* trp = (tr && i < 4) ? tr + 40 + 4 * i : nullptr;  // per-page stamps, pages 0-3
+    for (int b0 = 0; b0 < np; b0 += kAttnStages) {
+        const int nb = min(kAttnStages, np - b0);
+        unsigned okm = 0;
+        for (int i = 0; i < nb; ++i)
+            if (mbar_wait_bounded(&bar[(b0 + i) % kAttnStages], ((b0 + i) / kAttnStages) & 1, a.err, nullptr))
+                okm |= 1u << i;
+        uint64_t* trp = (tr && b0 == 0) ? tr + 40 : nullptr;
         trace_stamp(trp, 0);
-        const uint16_t* kt = reinterpret_cast<const uint16_t*>(ring + static_cast<size_t>(slot) * AG::STAGE);
-        const uint16_t* vt = kt + kPageTokens * D;
-        const int tp = (pg0 + i) * kPageTokens;  // position of the page's first token
-        {   // score of token s_tt for head s_hh: eight independent partial sums
-            const int t = tp + s_tt;
-            float pa[8];
+        // the staged copy of the page holding pos predates the append: patch its row
+        if (ip_new >= b0 && ip_new < b0 + nb) {
+            uint8_t* st = ring + static_cast<size_t>(ip_new % kAttnStages) * AG::STAGE;
+            uint16_t* kr = reinterpret_cast<uint16_t*>(st + (pos % kPageTokens) * AG::RS);
+            uint16_t* vr = reinterpret_cast<uint16_t*>(st + AG::TILE + (pos % kPageTokens) * AG::RS);
+            for (int d = tid; d < D; d += kAT) {
+                kr[d] = kbits[d];
+                vr[d] = vbits[d];
+            }
+        }
+        __syncthreads();
+        // scores: warp w < 2 nb takes n-tile w (tokens 8w..8w+7 of the batch)
+        if (warp < 2 * nb) {
+            const int pi = warp >> 1;  // page of the batch
+            const uint8_t* kt = ring + static_cast<size_t>((b0 + pi) % kAttnStages) * AG::STAGE;
+            // ldmatrix x2 row addresses: lanes 0-7 tokens of k-columns 0-7, lanes 8-15 of 8-15
+            const uint8_t* krow = kt + (8 * (warp & 1) + (lane & 7)) * AG::RS + ((lane >> 3) & 1) * 16;
+            float ch[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            const bool arow = fg < GRP;
+#pragma unroll 4
+            for (int ks = 0; ks < D / 16; ++ks) {
+                uint32_t b0r, b1r;
+                ldsm_x2(b0r, b1r, krow + ks * 32);
+                const int c0 = 16 * ks + 2 * ft;
+                const uint32_t ah0 = arow ? *reinterpret_cast<const uint32_t*>(&qh[fg][c0]) : 0u;
+                const uint32_t ah2 = arow ? *reinterpret_cast<const uint32_t*>(&qh[fg][c0 + 8]) : 0u;
+                const uint32_t al0 = arow ? *reinterpret_cast<const uint32_t*>(&ql[fg][c0]) : 0u;
+                const uint32_t al2 = arow ? *reinterpret_cast<const uint32_t*>(&ql[fg][c0 + 8]) : 0u;
+                mma_bf16_16816(ch, ah0, ah2, b0r, b1r);
+                mma_bf16_16816(cl, al0, al2, b0r, b1r);
+            }
+            if (arow) {
+                const bool okp = (okm >> pi) & 1u;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) pa[e] = 0.0f;
-            if (t == pos) {
-                const float4* k4 = reinterpret_cast<const float4*>(knew);
-#pragma unroll 4
-                for (int j = part; j < D / 8; j += TPP) {
-                    const float4 k0 = k4[2 * j], k1 = k4[2 * j + 1];
-                    const float4 q0 = q4[2 * j], q1 = q4[2 * j + 1];
-                    pa[0] = fmaf(q0.x, k0.x, pa[0]); pa[1] = fmaf(q0.y, k0.y, pa[1]);
-                    pa[2] = fmaf(q0.z, k0.z, pa[2]); pa[3] = fmaf(q0.w, k0.w, pa[3]);
-                    pa[4] = fmaf(q1.x, k1.x, pa[4]); pa[5] = fmaf(q1.y, k1.y, pa[5]);
-                    pa[6] = fmaf(q1.z, k1.z, pa[6]); pa[7] = fmaf(q1.w, k1.w, pa[7]);
-                }
-            } else {
-                const uint4* kr = reinterpret_cast<const uint4*>(kt + s_tt * D);
-#pragma unroll 4
-                for (int j = part; j < D / 8; j += TPP) {
-                    const uint4 u = kr[j];
-                    const float4 q0 = q4[2 * j], q1 = q4[2 * j + 1];
-                    pa[0] = fmaf(q0.x, bf16lo(u.x), pa[0]); pa[1] = fmaf(q0.y, bf16hi(u.x), pa[1]);
-                    pa[2] = fmaf(q0.z, bf16lo(u.y), pa[2]); pa[3] = fmaf(q0.w, bf16hi(u.y), pa[3]);
-                    pa[4] = fmaf(q1.x, bf16lo(u.z), pa[4]); pa[5] = fmaf(q1.y, bf16hi(u.z), pa[5]);
-                    pa[6] = fmaf(q1.z, bf16lo(u.w), pa[6]); pa[7] = fmaf(q1.w, bf16hi(u.w), pa[7]);
+                for (int e = 0; e < 2; ++e) {
+                    const int tb = 8 * warp + 2 * ft + e;  // token of the batch
+                    const int tpos = (pg0 + b0) * kPageTokens + tb;
+                    const bool valid = okp && tpos >= t0 && tpos < t1;
+                    sc[fg][tb] = valid ? (ch[e] + cl[e]) * sm_scale : -INFINITY;
                 }
             }
-            float p = ((pa[0] + pa[1]) + (pa[2] + pa[3])) + ((pa[4] + pa[5]) + (pa[6] + pa[7]));
-#pragma unroll
-            for (int m = 1; m < TPP; m <<= 1) p += __shfl_xor_sync(0xffffffffu, p, m);
-            const bool valid = ok && t >= t0 && t < t1;
-            if (part == 0) sc[s_hh][s_tt] = valid ? p * sm_scale : -INFINITY;
         }
         __syncthreads();
         trace_stamp(trp, 1);
-        // online softmax update, one warp per head: lanes 0..15 hold the page's scores
+        // softmax over the batch, one warp per head, online across batches
+        const int nt = nb * kPageTokens;
         for (int hh = warp; hh < GRP; hh += kAW) {
-            const float sv = lane < kPageTokens ? sc[hh][lane] : -INFINITY;
-            const float mp = warp_max(sv);
+            float sv[NT / 32];
+            float mp = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < NT / 32; ++j) {
+                const int tb = lane + 32 * j;
+                sv[j] = tb < nt ? sc[hh][tb] : -INFINITY;
+                mp = fmaxf(mp, sv[j]);
+            }
+            mp = warp_max(mp);
             const float mo = m_run[hh];
             const float mn = fmaxf(mo, mp);
-            const float pv = (lane < kPageTokens && sv != -INFINITY) ? expf(sv - mn) : 0.0f;
-            const float ls = warp_sum(pv);
-            if (lane < kPageTokens) sc[hh][lane] = pv;
+            float ls = 0.0f;
+#pragma unroll
+            for (int j = 0; j < NT / 32; ++j) {
+                const int tb = lane + 32 * j;
+                const float p = (sv[j] != -INFINITY) ? expf(sv[j] - mn) : 0.0f;
+                ls += p;
+                if (tb < NT) {
+                    const uint16_t hi = f32_to_bf16(p);
+                    ph[hh][tb] = hi;
+                    pl[hh][tb] = f32_to_bf16(p - bf16_to_f32(hi));
+                }
+            }
+            ls = warp_sum(ls);
             if (lane == 0) {
                 const float f = (mo == -INFINITY) ? 0.0f : expf(mo - mn);
                 scale[hh] = f;
@@ -324,21 +397,39 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
         }
         __syncthreads();
         trace_stamp(trp, 2);
-        // V: the thread's NA accumulators (one dim, heads v_h0, v_h0 + VHS, ...)
-        if (v_on) {
+        // P V: k-step = one page (16 tokens) of the batch
+        if (pv_on) {
+            const float f = fg < GRP ? scale[fg] : 0.0f;
 #pragma unroll
-            for (int k = 0; k < NA; ++k) acc[k] *= scale[v_h0 + VHS * k];
-#pragma unroll 4
-            for (int tt = 0; tt < kPageTokens; ++tt) {
-                const int t = tp + tt;
-                const float v = (t == pos) ? vnew[v_d] : bf16_to_f32(vt[tt * D + v_d]);
-#pragma unroll
-                for (int k = 0; k < NA; ++k) acc[k] = fmaf(sc[v_h0 + VHS * k][tt], v, acc[k]);
+            for (int u = 0; u < 2; ++u) {
+                oacc[u][0] *= f;
+                oacc[u][1] *= f;
+            }
+            const bool arow = fg < GRP;
+            for (int pi = 0; pi < nb; ++pi) {
+                const uint8_t* vt = ring + static_cast<size_t>((b0 + pi) % kAttnStages) * AG::STAGE + AG::TILE;
+                // ldmatrix x4 .trans: matrix m = lane / 8: tokens 8(m & 1).., dims 16w + 8(m >> 1)
+                const int m = lane >> 3;
+                const uint8_t* vrow = vt + (8 * (m & 1) + (lane & 7)) * AG::RS + (16 * warp + 8 * (m >> 1)) * 2;
+                uint32_t v0, v1, v2, v3;
+                ldsm_x4_trans(v0, v1, v2, v3, vrow);
+                const int c0 = kPageTokens * pi + 2 * ft;
+                const uint32_t ah0 = arow ? *reinterpret_cast<const uint32_t*>(&ph[fg][c0]) : 0u;
+                const uint32_t ah2 = arow ? *reinterpret_cast<const uint32_t*>(&ph[fg][c0 + 8]) : 0u;
+                const uint32_t al0 = arow ? *reinterpret_cast<const uint32_t*>(&pl[fg][c0]) : 0u;
+                const uint32_t al2 = arow ? *reinterpret_cast<const uint32_t*>(&pl[fg][c0 + 8]) : 0u;
+                mma_bf16_16816(oacc[0], ah0, ah2, v0, v1);
+                mma_bf16_16816(oacc[0], al0, al2, v0, v1);
+                mma_bf16_16816(oacc[1], ah0, ah2, v2, v3);
+                mma_bf16_16816(oacc[1], al0, al2, v2, v3);
             }
         }
-        __syncthreads();  // stage free and sc reusable
+        __syncthreads();  // stages and scores free
         trace_stamp(trp, 3);
-        if (tid == 0 && i + kAttnStages < np) issue(i + kAttnStages);
+        if (warp == 0 && b0 + kAttnStages < np) {
+            fence_proxy_async_smem();  // generic accesses of the stages before the next copies
+            for (int i = b0 + kAttnStages; i < np && i < b0 + 2 * kAttnStages; ++i) issue(i);
+        }
     }
 
     trace_stamp(tr, 4);
@@ -353,9 +444,14 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     static_assert(kAttnCluster * PSZ * 4 <= AG::RING, "ring too small for the cluster merge");
     cluster.sync();                                    // every ring is free from here on
     float* dst0 = cluster.map_shared_rank(reinterpret_cast<float*>(ring), 0) + crank * PSZ;
-    if (v_on)
+    if (pv_on && fg < GRP) {
 #pragma unroll
-        for (int k = 0; k < NA; ++k) dst0[(v_h0 + VHS * k) * D + v_d] = acc[k];
+        for (int u = 0; u < 2; ++u) {
+            const int d = 16 * warp + 8 * u + 2 * ft;
+            dst0[fg * D + d] = oacc[u][0];
+            dst0[fg * D + d + 1] = oacc[u][1];
+        }
+    }
     if (tid < GRP) {
         dst0[GRP * D + tid] = np > 0 ? m_run[tid] : -INFINITY;
         dst0[GRP * D + GRP + tid] = np > 0 ? l_run[tid] : 0.0f;
@@ -370,12 +466,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
         asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
         ct[5] = smid;
     }
-    if (crank != 0) {
-        trace_stamp(ct, 4);
-        kt_end(a.kt);
-        return;
-    }
-    {
+    if (crank == 0) {
         const float* P = reinterpret_cast<const float*>(ring);
         __shared__ float cw[GRP][kAttnCluster];
         __shared__ float cm[GRP], cl[GRP];
@@ -408,52 +499,56 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
             p[D] = cm[tid];
             p[D + 1] = cl[tid];
         }
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            const unsigned prev = atomicAdd(a.counters + g, 1u);
+            const int last = prev == static_cast<unsigned>(ccount) - 1;
+            if (last) __threadfence();
+            for (int r = 0; r < kAttnCluster; ++r) *cluster.map_shared_rank(&last_flag, r) = last;
+        }
     }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(a.counters + g, 1u);
-        is_last = (prev == static_cast<unsigned>(ccount) - 1);
-    }
-    __syncthreads();
+    cluster.sync();  // last_flag of every rank is set
     trace_stamp(tr, 6);
-    if (!is_last) {
+    if (!last_flag) {
         trace_stamp(ct, 4);
         kt_end(a.kt);
         return;
     }
-    __threadfence();
 
-    // ---- merge 2: the cluster partials of every head of this KV group, output gate ----
-    const int ns = ccount;
-    for (int hh = warp; hh < GRP; hh += kAW) {
-        const float* ph = a.part + static_cast<size_t>(g * GRP + hh) * kMaxSplits * (D + 2);
-        const float ml = lane < ns ? __ldcg(ph + lane * (D + 2) + D) : -INFINITY;
-        const float ll = lane < ns ? __ldcg(ph + lane * (D + 2) + D + 1) : 0.0f;
-        const float M = warp_max(ll > 0.0f ? ml : -INFINITY);
-        const float wk = ll > 0.0f ? expf(ml - M) : 0.0f;
-        const float L = warp_sum(wk * ll);
-        if (lane < kMaxSplits) wsp[hh][lane] = wk / L;
-    }
-    __syncthreads();
-    // every cluster partial of an output is loaded in one batch (fixed bound, unrolled)
+    // ---- merge 2 (the CTAs of the last cluster, each a slice of the outputs): the
+    // cluster partials of every head of this KV group, output gate; every load of an
+    // output (its partials and their max / sum) is issued in one batch ----
     constexpr int kMaxClusters = kMaxSplits / kAttnCluster;
-#pragma unroll 2
-    for (int o = tid; o < GRP * D; o += kAT) {
+    const int ns = ccount;
+    for (int o = crank * kAT + tid; o < GRP * D; o += kAttnCluster * kAT) {
         const int hh = o / D, d = o % D;
         const int hq = g * GRP + hh;
-        const float* ph = a.part + static_cast<size_t>(hq) * kMaxSplits * (D + 2) + d;
-        float pv[kMaxClusters];
+        const float* ph0 = a.part + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
+        float pv[kMaxClusters], ml[kMaxClusters], ll[kMaxClusters];
 #pragma unroll
-        for (int c = 0; c < kMaxClusters; ++c) pv[c] = c < ns ? __ldcg(ph + static_cast<size_t>(c) * (D + 2)) : 0.0f;
+        for (int c = 0; c < kMaxClusters; ++c) {
+            const bool on = c < ns;
+            pv[c] = on ? __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + d) : 0.0f;
+            ml[c] = on ? __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D) : -INFINITY;
+            ll[c] = on ? __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D + 1) : 0.0f;
+        }
         const float gate = a.qg[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
-        float acc2 = 0.0f;
+        float M = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kMaxClusters; ++c) acc2 = fmaf(wsp[hh][c], pv[c], acc2);
-        a.out[static_cast<size_t>(hq) * D + d] = acc2 * sigmoid_f(gate);
+        for (int c = 0; c < kMaxClusters; ++c)
+            if (ll[c] > 0.0f) M = fmaxf(M, ml[c]);
+        float L = 0.0f, acc2 = 0.0f;
+#pragma unroll
+        for (int c = 0; c < kMaxClusters; ++c) {
+            const float w = ll[c] > 0.0f ? expf(ml[c] - M) : 0.0f;
+            L = fmaf(w, ll[c], L);
+            acc2 = fmaf(w, pv[c], acc2);
+        }
+        a.out[static_cast<size_t>(hq) * D + d] = (L > 0.0f ? acc2 / L : 0.0f) * sigmoid_f(gate);
     }
-    if (tid == 0) a.counters[g] = 0u;
-    if (tid == 0 && a.trace) a.trace[7] = globaltimer_ns();
+    if (tid == 0 && crank == 0) a.counters[g] = 0u;
+    if (tid == 0 && crank == 0 && a.trace) a.trace[7] = globaltimer_ns();
     trace_stamp(ct, 4);
     __syncthreads();
     kt_end(a.kt);
@@ -462,7 +557,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
 // Dynamic shared memory of a CTA: the page ring, and at least 120 KB so that one CTA
 // runs per SM (two would share an SM's issue slots while other SMs stay idle).
 size_t attn_ring_bytes(int D) {
-    const size_t ring = static_cast<size_t>(kAttnStages) * 2 * 2 * kPageTokens * D;
+    const size_t ring = static_cast<size_t>(kAttnStages) * 2 * kPageTokens * (D + 8) * 2;
     return ring > 120 * 1024 ? ring : 120 * 1024;
 }
 
