@@ -75,7 +75,8 @@ struct dm_ctx {
     std::vector<int> dev_pos_valid;    // device pos[slot] == slot_len[slot]
     std::vector<cudaGraphExec_t> graphs;  // decode step per slot
     bool use_pdl = true;       // programmatic dependent launch between step kernels
-    bool l2_prefetch = true;   // latency-bound kernels prefetch upcoming weights into L2
+    bool l2_prefetch = false;  // latency-bound kernels prefetch upcoming weights into L2 (off:
+                               // measured slower, the prefetch competes with the step's reads)
     uint64_t* trace_buf = nullptr;
     uint64_t* ktrace_buf = nullptr;
     uint8_t* flush_buf = nullptr;  // L2 flush target of dm_time_kernel (allocated on first use)
@@ -413,7 +414,7 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
         return DM_ERR_INVALID_ARG;
     dm_ctx* c = new dm_ctx();
     // tuning knobs (environment, read once): DISMOEN_PDL=0 launches every kernel without
-    // programmatic dependent launch; DISMOEN_L2_PREFETCH=0 disables the L2 prefetch of
+    // programmatic dependent launch; DISMOEN_L2_PREFETCH=1 enables the L2 prefetch of
     // upcoming weights by the latency-bound kernels
     if (const char* v = getenv("DISMOEN_PDL")) c->use_pdl = atoi(v) != 0;
     if (const char* v = getenv("DISMOEN_L2_PREFETCH")) c->l2_prefetch = atoi(v) != 0;

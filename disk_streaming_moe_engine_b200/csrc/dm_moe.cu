@@ -567,6 +567,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 m = fmaxf(m, pv[i]);
             }
             for (int e = lane + 32 * PL; e < E; e += 32) m = fmaxf(m, __ldcg(a.logits + e));
+            const float zs = __ldcg(a.logits + E);  // shared-expert gate logit
             m = warp_max(m);
             if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 0);
             float s = 0.0f;
@@ -594,19 +595,25 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 1);
             for (int e = lane + 32 * PL; e < E; e += 32) pe[e] = DM_DET_MUL(pe[e], inv);
             __syncwarp();
-            // top-k: each lane sorts its 8 (probability, id) pairs in registers (compare-
-            // exchange network, ties to the lower id); every round the warp takes the
-            // maximum probability over the lanes' heads (redux on the bit patterns, which
-            // order like the values for p >= 0) and the lowest id holding it, and the
-            // owning lane pops its head.
-            uint32_t kb[PL];
-            int ki[PL];
+            // top-k on probabilities, ties to the lower expert id.  The probabilities are
+            // >= 0, so their bit patterns order like the values.
+            const int topk = a.topk;
+            int my_id = 0;      // lane r < topk ends with the round-r result
+            uint32_t my_p = 0u;
+            bool bad = false;
+            if (E <= 32 * PL) {
+                // each lane sorts its 8 (probability, id) pairs (compare-exchange network);
+                // every round the warp takes the maximum over the lanes' heads and the lowest
+                // id holding it, and the owning lane pops its head.  Branch-free rounds:
+                // divergence ahead of the warp reductions costs more than the selects.
+                uint32_t kb[PL];
+                int ki[PL];
 #pragma unroll
-            for (int i = 0; i < PL; ++i) {
-                const int e = lane + 32 * i;
-                kb[i] = (e < E && pv[i] > 0.0f) ? __float_as_uint(pv[i]) : 0u;
-                ki[i] = e < E ? e : 0x7fffffff;
-            }
+                for (int i = 0; i < PL; ++i) {
+                    const int e = lane + 32 * i;
+                    kb[i] = (e < E && pv[i] > 0.0f) ? __float_as_uint(pv[i]) : 0u;
+                    ki[i] = e < E ? e : 0x7fffffff;
+                }
 #define DM_CX(x, y)                                                                        \
     {                                                                                      \
         const bool sw = kb[y] > kb[x] || (kb[y] == kb[x] && ki[y] < ki[x]);                \
@@ -617,58 +624,87 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         kb[x] = tb;                                                                        \
         ki[x] = ti;                                                                        \
     }
-            // Batcher odd-even merge sort network for 8 elements (19 compare-exchanges)
-            DM_CX(0, 1) DM_CX(2, 3) DM_CX(4, 5) DM_CX(6, 7)
-            DM_CX(0, 2) DM_CX(1, 3) DM_CX(4, 6) DM_CX(5, 7)
-            DM_CX(1, 2) DM_CX(5, 6)
-            DM_CX(0, 4) DM_CX(1, 5) DM_CX(2, 6) DM_CX(3, 7)
-            DM_CX(2, 4) DM_CX(3, 5)
-            DM_CX(1, 2) DM_CX(3, 4) DM_CX(5, 6)
+                // Batcher odd-even merge sort network for 8 elements (19 compare-exchanges)
+                DM_CX(0, 1) DM_CX(2, 3) DM_CX(4, 5) DM_CX(6, 7)
+                DM_CX(0, 2) DM_CX(1, 3) DM_CX(4, 6) DM_CX(5, 7)
+                DM_CX(1, 2) DM_CX(5, 6)
+                DM_CX(0, 4) DM_CX(1, 5) DM_CX(2, 6) DM_CX(3, 7)
+                DM_CX(2, 4) DM_CX(3, 5)
+                DM_CX(1, 2) DM_CX(3, 4) DM_CX(5, 6)
 #undef DM_CX
-            for (int r = 0; r < a.topk; ++r) {
-                // this lane's best: its register head, or an expert beyond 32*PL (E > 256,
-                // shared memory; a taken one holds -2)
-                uint32_t hb = kb[0];
-                int hi = ki[0];
-                for (int e = lane + 32 * PL; e < E; e += 32) {
-                    const float v = pe[e];
-                    const uint32_t b = v > 0.0f ? __float_as_uint(v) : 0u;
-                    const int id = v >= 0.0f ? e : 0x7fffffff;
-                    if (b > hb || (b == hb && id < hi)) {
-                        hb = b;
-                        hi = id;
-                    }
-                }
-                const uint32_t mb = __reduce_max_sync(0xffffffffu, hb);
-                const int cand = hb == mb ? hi : 0x7fffffff;
-                int bi = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(cand)));
-                float bv = __uint_as_float(mb);
-                if (hi == bi && bi >= 32 * PL) {
-                    pe[bi] = -2.0f;
-                } else if (ki[0] == bi) {  // pop the head
+#pragma unroll
+                for (int r = 0; r < kMaxTopK; ++r) {
+                    if (r >= topk) break;
+                    const uint32_t mb = __reduce_max_sync(0xffffffffu, kb[0]);
+                    const int cand = kb[0] == mb ? ki[0] : 0x7fffffff;
+                    const int bi = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(cand)));
+                    const bool pop = ki[0] == bi;
 #pragma unroll
                     for (int i = 0; i < PL - 1; ++i) {
-                        kb[i] = kb[i + 1];
-                        ki[i] = ki[i + 1];
+                        kb[i] = pop ? kb[i + 1] : kb[i];
+                        ki[i] = pop ? ki[i + 1] : ki[i];
                     }
-                    kb[PL - 1] = 0u;
-                    ki[PL - 1] = 0x7fffffff;
+                    kb[PL - 1] = pop ? 0u : kb[PL - 1];
+                    ki[PL - 1] = pop ? 0x7fffffff : ki[PL - 1];
+                    const bool oob = bi < 0 || bi >= E;
+                    bad |= oob;
+                    my_id = lane == r ? (oob ? r : bi) : my_id;
+                    my_p = lane == r ? (oob ? 0u : mb) : my_p;
                 }
-                if (bi < 0 || bi >= E) {
-                    if (lane == 0) raise_error(a.err, DM_DEVERR_NONFINITE);
-                    bi = r;
-                    bv = 0.0f;
-                }
-                if (lane == 0) {
-                    a.probs[r] = bv;
-                    sid[r] = bi;
-                    sp[r] = bv;
+            } else {
+                // E > 256: experts beyond 32*PL per lane live in shared memory (taken = -2);
+                // each round every lane offers its best untaken one
+                unsigned avail = 0;
+#pragma unroll
+                for (int i = 0; i < PL; ++i)
+                    if (lane + 32 * i < E) avail |= 1u << i;
+                for (int r = 0; r < topk; ++r) {
+                    uint32_t hb = 0u;
+                    int hi = 0x7fffffff, hslot = -1;
+#pragma unroll
+                    for (int i = 0; i < PL; ++i) {
+                        const uint32_t b = pv[i] > 0.0f ? __float_as_uint(pv[i]) : 0u;
+                        if (((avail >> i) & 1u) && (hslot < 0 || b > hb)) {
+                            hb = b;
+                            hi = lane + 32 * i;
+                            hslot = i;
+                        }
+                    }
+                    for (int e = lane + 32 * PL; e < E; e += 32) {
+                        const float v = pe[e];
+                        const uint32_t b = v > 0.0f ? __float_as_uint(v) : 0u;
+                        if (v >= 0.0f && (hi == 0x7fffffff || b > hb || (b == hb && e < hi))) {
+                            hb = b;
+                            hi = e;
+                            hslot = PL;
+                        }
+                    }
+                    const uint32_t mb = __reduce_max_sync(0xffffffffu, hb);
+                    const int cand = (hi != 0x7fffffff && hb == mb) ? hi : 0x7fffffff;
+                    const int bi = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(cand)));
+                    if (hi == bi) {
+                        if (hslot == PL) pe[bi] = -2.0f;
+                        else avail &= ~(1u << hslot);
+                    }
+                    const bool oob = bi < 0 || bi >= E;
+                    bad |= oob;
+                    if (lane == (r & 31) && r < 32) {
+                        my_id = oob ? r : bi;
+                        my_p = oob ? 0u : mb;
+                    }
+                    __syncwarp();
                 }
             }
+            if (lane < topk) {
+                sid[lane] = my_id;
+                sp[lane] = __uint_as_float(my_p);
+                a.probs[lane] = __uint_as_float(my_p);
+            }
+            if (bad && lane == 0) raise_error(a.err, DM_DEVERR_NONFINITE);
             __syncwarp();
             if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 2);
             if (lane == 0) {
-                const float sgv = sigmoid_f(__ldcg(a.logits + E));
+                const float sgv = sigmoid_f(zs);
                 *a.shared_g = sgv;
                 sp[a.topk] = sgv;
                 if (s != s || isinf(s)) raise_error(a.err, DM_DEVERR_NONFINITE);
