@@ -223,7 +223,7 @@ def step_timeline(eng, steps: int):
     eng.enqueue_decode(steps)
     eng.sync()
     tl = eng.trace_timeline()
-    ph = eng.trace_read(1024).astype(np.int64)
+    ph = eng.trace_read(2304).astype(np.int64)
     eng.trace_enable(False)
     t0 = tl[0][2]
     rows = [{"kind": k, "layer": l, "start_us": (s0 - t0) / 1e3, "ready_us": (r - t0) / 1e3, "end_us": (e - t0) / 1e3}
@@ -247,7 +247,20 @@ def step_timeline(eng, steps: int):
               "attn_pages": [round((int(v) - int(ph[0])) / 1e3, 2) if v else None for v in ph[40:56]],
               "moe_cta0": [round((int(v) - int(ph[16])) / 1e3, 2) if v else None for v in ph[16:25]],
               "moe_last_cta": [round((int(v) - int(ph[26])) / 1e3, 2) if v else None for v in ph[26:35]]}
-    cta = ph[64:].reshape(-1, 6)
+    mc = ph[1024:1024 + 8 * 148].reshape(-1, 8)
+    mc = mc[mc[:, 0] != 0]
+    if len(mc):  # fused MoE of the last layer, per CTA (start-relative): quantiles and the slowest
+        c0 = mc[:, 0].min()
+        rel = lambda i: (mc[:, i] - c0) / 1e3
+        q = lambda v: [round(float(np.min(v)), 2), round(float(np.median(v)), 2), round(float(np.max(v)), 2)]
+        phases["moe_ctas"] = {k: q(rel(i)) for i, k in
+                              enumerate(["start", "ready", "ids", "up_data", "up_done", "barrier", "end"])}
+        slow = np.argsort(-(mc[:, 4] - c0))[:8]
+        phases["moe_ctas"]["slowest_up"] = [[int(i), round(float(rel(2)[i]), 2), round(float(rel(3)[i]), 2),
+                                             round(float(rel(4)[i]), 2), int(mc[i, 7])] for i in slow]
+        phases["moe_ctas"]["up_data_minus_ids"] = q(rel(3) - rel(2))
+        phases["moe_ctas"]["up_done_minus_data"] = q(rel(4) - rel(3))
+    cta = ph[64:1024].reshape(-1, 6)
     cta = cta[cta[:, 0] != 0]
     if len(cta):  # decode attention of the last attention layer, per CTA (start-relative)
         c0 = cta[:, 0].min()

@@ -363,6 +363,8 @@ static int check_device_error(dm_ctx* c, const char* stage) {
     if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", stage, -1, "%s", cudaGetErrorString(e));
     if (w == 0) return DM_OK;
     cudaMemset(c->b.err, 0, 4);
+    // a launch that gave up waiting may have left router logit slots filled
+    cudaMemset(c->b.rlogits, 0xFF, static_cast<size_t>(c->d.E + 1) * 4);
     if (w & DM_DEVERR_TIMEOUT) return set_err(c, DM_ERR_TIMEOUT, "DEVICE_TIMEOUT", stage, -1, "a bounded device wait ran out (word 0x%x)", w);
     if (w & DM_DEVERR_CAPACITY) return set_err(c, DM_ERR_CAPACITY, "M5_ERR_CONTEXT_SIZE", stage, -1, "KV cache capacity exceeded on token append");
     if (w & DM_DEVERR_PAGE) return set_err(c, DM_ERR_CAPACITY, "KV_PAGE_ERROR", stage, -1, "page table entry outside the page pool");
@@ -447,6 +449,8 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     plan_memory(c, true);
     // zero everything (weights stay zero until uploaded; state starts empty)
     e = cudaMemsetAsync(c->arena, 0, c->arena_bytes, c->stream);
+    // router logit slots start empty (all-ones NaN pattern; the MoE kernel polls them)
+    if (e == cudaSuccess) e = cudaMemsetAsync(c->b.rlogits, 0xFF, static_cast<size_t>(c->d.E + 1) * 4, c->stream);
     if (e == cudaSuccess)
         e = launch_rope_table(c->stream, c->b.rope, c->d.max_pages * kPageTokens, c->d.rot_dim, c->d.theta);
     if (e == cudaSuccess) e = cudaMallocHost(&c->h_io, 64);

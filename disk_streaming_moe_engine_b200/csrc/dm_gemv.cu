@@ -18,6 +18,8 @@
 // Epilogues are per row segment: store, SiLU, residual add, ring-slot store (GDN conv
 // window) or logits + argmax (first maximum wins, reference cmd_decode.mojo:115).
 #include "dm_common.cuh"
+#include <cstdlib>
+
 #include "dm_kernels.h"
 
 namespace dm {
@@ -82,6 +84,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __grid
     // weights do not depend on the previous kernel: first chunk in flight before the wait
     uint4 w[G::CH];
     if (row < a.N) load_chunk<G::CH>(w, a.W + static_cast<size_t>(row) * K, 0, lane);
+    // L2 look-ahead: lane 0 keeps the rows pf strides ahead of the one in registers
+    // requested from HBM (no register or shared-memory cost)
+    if (lane == 0)
+        for (int q = 1; q <= a.pf; ++q)
+            if (row + q * nw < a.N) bulk_prefetch_l2(a.W + static_cast<size_t>(row + q * nw) * K, K * 2);
     constexpr int XPT = K / kGemvThreads;  // activations per thread (K >= 512) or 1
     constexpr int XN = XPT > 0 ? XPT : 1;
     float gv[XN];  // norm gains are weights: fetched before the wait
@@ -174,6 +181,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __grid
         }
         const int next = row + nw;
         if (next < a.N) load_chunk<G::CH>(w, a.W + static_cast<size_t>(next) * K, 0, lane);  // overlap the reduction
+        if (lane == 0 && a.pf > 0 && row + (a.pf + 1) * nw < a.N)
+            bulk_prefetch_l2(a.W + static_cast<size_t>(row + (a.pf + 1) * nw) * K, K * 2);
         const float acc = warp_sum(acc0 + acc1);
         if (lane == 0) {
             int s = 0, rstart = 0;
@@ -254,8 +263,22 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __grid
 template <int K, int PRO>
 static cudaError_t launch_gemv_t(const LaunchCfg& lc, GemvArgs a) {
     a.kt = lc.kt;
+    static const int pf = [] {  // L2 look-ahead rows (environment DISMOEN_GEMV_PF, 0..8)
+        const char* v = getenv("DISMOEN_GEMV_PF");
+        const int n = v ? atoi(v) : 0;
+        return n < 0 ? 0 : (n > 8 ? 8 : n);
+    }();
+    a.pf = pf;
     const int want = (a.N + kGemvWarps - 1) / kGemvWarps;
-    int grid = want < lc.num_sms ? want : lc.num_sms;
+    // CTAs per SM (environment DISMOEN_GEMV_CTAS_PER_SM, 1 or 2; default 2: measured faster
+    // in the decode step although one CTA per SM leaves room for the next kernel's prologue)
+    static const int per_sm = [] {
+        const char* v = getenv("DISMOEN_GEMV_CTAS_PER_SM");
+        const int n = v ? atoi(v) : 2;
+        return n == 1 ? 1 : 2;
+    }();
+    const int cap = lc.num_sms * per_sm;
+    int grid = want < cap ? want : cap;
     if (a.counter && grid > kMaxCtas) grid = kMaxCtas;
     return launch_kernel(lc, gemv_bf16_kernel<K, PRO>, dim3(grid), dim3(kGemvThreads), 0, a);
 }

@@ -105,9 +105,11 @@ struct Buffers {
     uint64_t* ktrace;     // [kMaxTraceKernels][4] per-launch timeline records, or null
 };
 
-constexpr int kTraceSlots = 1024;
+constexpr int kTraceSlots = 2304;
 constexpr int kTrCta = 64;        // per-CTA region: decode attention, 6 slots per CTA
 constexpr int kTrCtaSlots = 6;    // start, ready, pages done, cluster merged, end, SM id
+constexpr int kTrMoeCta = 1024;   // per-CTA region: fused MoE, 8 slots per CTA
+constexpr int kTrMoeCtaSlots = 8; // start, ready, ids known, up data in, up done, barrier, end, SM id
 // trace slot bases per kernel kind
 constexpr int kTrAttn = 0;   // 8 stamps
 constexpr int kTrMoe = 16;   // 16 stamps

@@ -46,6 +46,7 @@ struct GemvArgs {
     int gen_cap;
     uint32_t* err;
     uint64_t* kt;   // timeline record (set from LaunchCfg)
+    int pf;         // rows of L2 look-ahead per warp
 };
 
 cudaError_t launch_gemv(const LaunchCfg& lc, int K, int pro, const GemvArgs& a);

@@ -291,23 +291,23 @@ __device__ __forceinline__ float q4_partial_smem(const uint8_t* chunk, int r, in
         const uint32_t z = (g & 1) ? (zb >> 4) : (zb & 15u);
         const float fz = __uint_as_float(0x4B000000u | z);
         const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-        float av = 0.0f;
+        float av0 = 0.0f, av1 = 0.0f;  // two chains (low / high nibbles) halve the latency
 #pragma unroll
         for (int wd = 0; wd < 4; ++wd) {
             const uint32_t lo = words[wd] & 0x0F0F0F0Fu;
             const uint32_t hi = (words[wd] >> 4) & 0x0F0F0F0Fu;
             const float4 xa = x4[(2 * wd) * Q::NV + v];
             const float4 xb = x4[(2 * wd + 1) * Q::NV + v];
-            av = fmaf(nib(lo, 0) - fz, xa.x, av);
-            av = fmaf(nib(hi, 0) - fz, xa.y, av);
-            av = fmaf(nib(lo, 1) - fz, xa.z, av);
-            av = fmaf(nib(hi, 1) - fz, xa.w, av);
-            av = fmaf(nib(lo, 2) - fz, xb.x, av);
-            av = fmaf(nib(hi, 2) - fz, xb.y, av);
-            av = fmaf(nib(lo, 3) - fz, xb.z, av);
-            av = fmaf(nib(hi, 3) - fz, xb.w, av);
+            av0 = fmaf(nib(lo, 0) - fz, xa.x, av0);
+            av1 = fmaf(nib(hi, 0) - fz, xa.y, av1);
+            av0 = fmaf(nib(lo, 1) - fz, xa.z, av0);
+            av1 = fmaf(nib(hi, 1) - fz, xa.w, av1);
+            av0 = fmaf(nib(lo, 2) - fz, xb.x, av0);
+            av1 = fmaf(nib(hi, 2) - fz, xb.y, av1);
+            av0 = fmaf(nib(lo, 3) - fz, xb.z, av0);
+            av1 = fmaf(nib(hi, 3) - fz, xb.w, av1);
         }
-        acc = fmaf(s, av, acc);
+        acc = fmaf(s, av0 + av1, acc);
     }
     return acc;
 }
@@ -355,6 +355,7 @@ struct MoeFusedArgs {
     unsigned* sync;           // [4]: router count, (unused), up count, exit count
     unsigned long long* idflag; // [4] released words: marker bit 63 | 4 ids x 15 bits
     uint64_t* trace;          // phase stamps of CTA 0 and of the last CTA, or null
+    uint64_t* cta_trace;      // per-CTA stamps (kTrMoeCtaSlots per CTA, thread 0) or null
     uint64_t* kt;             // launch timeline record or null
     const void* next_w;
     size_t next_bytes;
@@ -377,6 +378,33 @@ DM_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
 DM_DEV void red_release_add(unsigned* p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+DM_DEV unsigned ld_relaxed_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+DM_DEV void st_relaxed_u32(unsigned* p, unsigned v) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Router logit slots hold kLogitEmpty (a NaN pattern the arithmetic never produces: NaN
+// results are 0x7FFFFFFF) until their router CTA stores the logit; CTA 0 polls the slots
+// themselves and puts kLogitEmpty back once it has read them.
+constexpr unsigned kLogitEmpty = 0xFFFFFFFFu;
+DM_DEV float poll_logit(const float* p, uint32_t* err) {
+    const unsigned* q = reinterpret_cast<const unsigned*>(p);
+    unsigned v = ld_relaxed_u32(q);
+    if (v != kLogitEmpty) return __uint_as_float(v);
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; ++n) {
+        v = ld_relaxed_u32(q);
+        if (v != kLogitEmpty) return __uint_as_float(v);
+        if (n % 256 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
+            raise_error(err, DM_DEVERR_TIMEOUT);
+            return 0.0f;
+        }
+    }
+}
+
 // Bounded wait until bit 63 of *p is set; returns the word.
 DM_DEV unsigned long long spin_marker(const unsigned long long* p, uint32_t* err) {
     unsigned long long v = ld_acquire_u64(p);
@@ -450,7 +478,9 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     float* h4 = reinterpret_cast<float*>(dsm + SM::h_off(a.up_slots, nexp));
 
     uint64_t* tr = tid == 0 ? (c == 0 ? a.trace : (c == nblk - 1 && a.trace ? a.trace + 10 : nullptr)) : nullptr;
+    uint64_t* ct = (tid == 0 && a.cta_trace) ? a.cta_trace + c * kTrMoeCtaSlots : nullptr;
     trace_stamp(tr, 0);
+    trace_stamp(ct, 0);
     kt_start(a.kt);
     // ---- pre-wait: nothing here depends on the previous kernel ----
     prefetch_l2_share(a.next_w, a.next_bytes, c, nblk, tid);
@@ -490,6 +520,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     pdl_launch_dependents();
     kt_ready(a.kt);
     trace_stamp(tr, 1);
+    trace_stamp(ct, 1);
 
     // ---- phase 1: canonical RMSNorm (512 threads), router rows ----
     {
@@ -541,37 +572,60 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 acc = __fmaf_rn(bf16hi(w.w), x1.w, acc);
             }
             acc = warp_sum(acc);
-            if (lane == 0) __stcg(a.logits + rrow, acc);
-        }
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();
-            atomicAdd(&a.sync[0], 1u);
+            if (lane == 0) {
+                const unsigned bits = __float_as_uint(acc);
+                st_relaxed_u32(reinterpret_cast<unsigned*>(a.logits) + rrow, bits == kLogitEmpty ? 0x7FFFFFFFu : bits);
+            }
         }
     }
     trace_stamp(tr, 3);
     if (c == 0) {
-        if (tid == 0) spin_geq(&a.sync[0], static_cast<unsigned>(R), a.err);
         trace_stamp(tr, 4);
-        __syncthreads();
         if (warp == 0) {
             // softmax in the canonical order; lane l owns experts l, l+32, ... (<= 32 each)
             const int E = a.E;
             constexpr int PL = 8;  // register slots per lane: E <= 256 here, larger E below
             float pv[PL];
             float m = -INFINITY;
-#pragma unroll
+            // poll the logit slots: every load of a round is in flight at once; a round
+            // repeats only the slots still empty
+            const unsigned* lg = reinterpret_cast<const unsigned*>(a.logits);
+            unsigned raw[PL + 1];
+        #pragma unroll
+            for (int i = 0; i <= PL; ++i) {
+                const int e = i < PL ? lane + 32 * i : E;  // slot E: shared-expert gate
+                raw[i] = e <= E ? ld_relaxed_u32(lg + e) : 0u;
+            }
+            {
+                const uint64_t t0 = globaltimer_ns();
+                for (uint32_t n = 0;; ++n) {
+                    bool miss = false;
+        #pragma unroll
+                    for (int i = 0; i <= PL; ++i) miss |= raw[i] == kLogitEmpty;
+                    if (!__any_sync(0xffffffffu, miss)) break;
+                    if (n % 64 == 63 && globaltimer_ns() - t0 > DM_WAIT_NS) {
+                        if (lane == 0) raise_error(a.err, DM_DEVERR_TIMEOUT);
+                        break;
+                    }
+        #pragma unroll
+                    for (int i = 0; i <= PL; ++i) {
+                        const int e = i < PL ? lane + 32 * i : E;
+                        if (raw[i] == kLogitEmpty) raw[i] = ld_relaxed_u32(lg + e);
+                    }
+                }
+            }
+        #pragma unroll
             for (int i = 0; i < PL; ++i) {
                 const int e = lane + 32 * i;
-                pv[i] = e < E ? __ldcg(a.logits + e) : -INFINITY;
+                pv[i] = e < E ? __uint_as_float(raw[i]) : -INFINITY;
                 m = fmaxf(m, pv[i]);
             }
-            for (int e = lane + 32 * PL; e < E; e += 32) m = fmaxf(m, __ldcg(a.logits + e));
-            const float zs = __ldcg(a.logits + E);  // shared-expert gate logit
+            for (int e = lane + 32 * PL; e < E; e += 32) m = fmaxf(m, poll_logit(a.logits + e, a.err));
+            const float zs = __uint_as_float(raw[PL]);  // shared-expert gate logit
             m = warp_max(m);
             if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 0);
             float s = 0.0f;
-#pragma unroll
+        #pragma unroll
             for (int i = 0; i < PL; ++i) {
                 const int e = lane + 32 * i;
                 if (e < E) {
@@ -583,13 +637,13 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             }
             float* pe = h4;  // experts beyond 32*PL per lane live in shared memory
             for (int e = lane + 32 * PL; e < E; e += 32) {
-                const float ev = dm_det_exp(DM_DET_SUB(__ldcg(a.logits + e), m));
+                const float ev = dm_det_exp(DM_DET_SUB(poll_logit(a.logits + e, a.err), m));
                 pe[e] = ev;
                 s = DM_DET_ADD(s, ev);
             }
             s = warp_sum(s);
             const float inv = DM_DET_DIV(1.0f, s);
-#pragma unroll
+        #pragma unroll
             for (int i = 0; i < PL; ++i)
                 if (lane + 32 * i < E) pv[i] = DM_DET_MUL(pv[i], inv);
             if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 1);
@@ -608,14 +662,14 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 // divergence ahead of the warp reductions costs more than the selects.
                 uint32_t kb[PL];
                 int ki[PL];
-#pragma unroll
+        #pragma unroll
                 for (int i = 0; i < PL; ++i) {
                     const int e = lane + 32 * i;
                     kb[i] = (e < E && pv[i] > 0.0f) ? __float_as_uint(pv[i]) : 0u;
                     ki[i] = e < E ? e : 0x7fffffff;
                 }
-#define DM_CX(x, y)                                                                        \
-    {                                                                                      \
+        #define DM_CX(x, y)                                                                        \
+            {                                                                                      \
         const bool sw = kb[y] > kb[x] || (kb[y] == kb[x] && ki[y] < ki[x]);                \
         const uint32_t tb = sw ? kb[y] : kb[x];                                            \
         const int ti = sw ? ki[y] : ki[x];                                                 \
@@ -623,7 +677,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         ki[y] = sw ? ki[x] : ki[y];                                                        \
         kb[x] = tb;                                                                        \
         ki[x] = ti;                                                                        \
-    }
+            }
                 // Batcher odd-even merge sort network for 8 elements (19 compare-exchanges)
                 DM_CX(0, 1) DM_CX(2, 3) DM_CX(4, 5) DM_CX(6, 7)
                 DM_CX(0, 2) DM_CX(1, 3) DM_CX(4, 6) DM_CX(5, 7)
@@ -631,15 +685,15 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 DM_CX(0, 4) DM_CX(1, 5) DM_CX(2, 6) DM_CX(3, 7)
                 DM_CX(2, 4) DM_CX(3, 5)
                 DM_CX(1, 2) DM_CX(3, 4) DM_CX(5, 6)
-#undef DM_CX
-#pragma unroll
+        #undef DM_CX
+        #pragma unroll
                 for (int r = 0; r < kMaxTopK; ++r) {
                     if (r >= topk) break;
                     const uint32_t mb = __reduce_max_sync(0xffffffffu, kb[0]);
                     const int cand = kb[0] == mb ? ki[0] : 0x7fffffff;
                     const int bi = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(cand)));
                     const bool pop = ki[0] == bi;
-#pragma unroll
+        #pragma unroll
                     for (int i = 0; i < PL - 1; ++i) {
                         kb[i] = pop ? kb[i + 1] : kb[i];
                         ki[i] = pop ? ki[i + 1] : ki[i];
@@ -655,13 +709,13 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 // E > 256: experts beyond 32*PL per lane live in shared memory (taken = -2);
                 // each round every lane offers its best untaken one
                 unsigned avail = 0;
-#pragma unroll
+        #pragma unroll
                 for (int i = 0; i < PL; ++i)
                     if (lane + 32 * i < E) avail |= 1u << i;
                 for (int r = 0; r < topk; ++r) {
                     uint32_t hb = 0u;
                     int hi = 0x7fffffff, hslot = -1;
-#pragma unroll
+        #pragma unroll
                     for (int i = 0; i < PL; ++i) {
                         const uint32_t b = pv[i] > 0.0f ? __float_as_uint(pv[i]) : 0u;
                         if (((avail >> i) & 1u) && (hslot < 0 || b > hb)) {
@@ -709,7 +763,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 sp[a.topk] = sgv;
                 if (s != s || isinf(s)) raise_error(a.err, DM_DEVERR_NONFINITE);
                 unsigned long long words[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
+        #pragma unroll
                 for (int r = 0; r < kMaxTopK; ++r)
                     if (r < a.topk) {
                         a.ids[r] = sid[r];
@@ -719,11 +773,13 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 // nothing else from this thread before phase 3; probs and the shared gate
                 // reach phase 3 through this thread's release of the up-phase barrier.
                 // Relaxed stores: no fence on the critical path.
-#pragma unroll
+        #pragma unroll
                 for (int k = 0; k < 4; ++k)
                     if (k < (a.topk + 3) / 4) st_relaxed_u64(&a.idflag[k], words[k] | (1ull << 63));
                 trace_stamp(tr ? tr + 20 : nullptr, 3);
             }
+            // every slot has been read: empty them for the next launch
+            for (int e = lane; e <= E; e += 32) reinterpret_cast<unsigned*>(a.logits)[e] = kLogitEmpty;
         }
         __syncthreads();
     } else {
@@ -735,6 +791,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         __syncthreads();
     }
     trace_stamp(tr, 5);
+    trace_stamp(ct, 2);
 
     // ---- issue the routed chunks: gate/up items and this CTA's down chunk (one
     // thread per copy) ----
@@ -749,14 +806,19 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                          static_cast<int64_t>(item % a.gu_chunks) * QU::CHUNK,
                      QU::CHUNK, &bar_up[k]);
         }
-    } else if (has_down && tid >= 32 && tid < 32 + a.topk) {
-        const int j = tid - 32;
+    }
+    // this CTA's routed down chunks are needed only after the grid barrier: they are
+    // issued once its first gate/up item has landed (or now, if it has none), so the
+    // gate/up bytes go first
+    auto issue_down = [&](int j) {
         mbar_arrive_expect_tx(&bar_dn[j], QD::CHUNK);
         bulk_g2s(dn_s + static_cast<size_t>(j) * QD::CHUNK,
                  a.experts + static_cast<int64_t>(sid[j]) * a.expert_bytes + a.gu_part_bytes +
                      static_cast<int64_t>(c) * QD::CHUNK,
                  QD::CHUNK, &bar_dn[j]);
-    }
+    };
+    const bool late_down = i1 > i0;
+    if (!late_down && has_down && tid >= 32 && tid < 32 + a.topk) issue_down(tid - 32);
 
     // ---- phase 2: gate/up; two warp groups take alternate items ----
     {
@@ -766,6 +828,8 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             const int item = i0 + k;
             const int j = item / a.gu_chunks, cc = item % a.gu_chunks;
             const bool ok = mbar_wait_bounded(&bar_up[k], 0, a.err, nullptr);
+            trace_stamp(ct, 3);
+            if (late_down && k == 0 && warp == 0 && has_down && lane < a.topk) issue_down(lane);
             const uint8_t* chunk = up_s + static_cast<size_t>(k) * QU::CHUNK;
             float dots[2];
 #pragma unroll
@@ -787,12 +851,19 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     }
     __syncthreads();
     trace_stamp(tr, 6);
+    trace_stamp(ct, 4);
     if (tid == 0) {
         red_release_add(&a.sync[2], 1u);
         if (has_down) spin_geq(&a.sync[2], static_cast<unsigned>(nblk), a.err);
     }
     __syncthreads();
     trace_stamp(tr, 7);
+    trace_stamp(ct, 5);
+    if (ct) {
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        ct[7] = smid;
+    }
 
     // ---- phase 3: 16 output rows of every selected expert + residual ----
     if (has_down) {
@@ -819,8 +890,12 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         const int wgrp = warp >> 3, wg = warp & 7;
         const int sub = lane / QD::LPR, vl = lane % QD::LPR;
         float routed[2] = {0.0f, 0.0f}, shv[2] = {0.0f, 0.0f};
-        for (int j = wgrp; j < nexp; j += 2) {
-            const bool ok = mbar_wait_bounded(&bar_dn[j], 0, a.err, nullptr);
+        bool ok = true;
+        for (int j = wgrp; j < nexp; j += 2) ok &= mbar_wait_bounded(&bar_dn[j], 0, a.err, nullptr);
+#pragma unroll
+        for (int jj = 0; jj < (kMaxTopK + 2) / 2; ++jj) {
+            const int j = wgrp + 2 * jj;
+            if (j >= nexp) break;
             const uint8_t* chunk = dn_s + static_cast<size_t>(j) * QD::CHUNK;
             const float4* hv = reinterpret_cast<const float4*>(h4 + j * KI);
 #pragma unroll
@@ -857,6 +932,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     // ---- exit: the last CTA resets the flags for the next launch ----
     __syncthreads();
     trace_stamp(tr, 8);
+    trace_stamp(ct, 6);
     kt_end(a.kt);
     if (tid == 0) {
         __threadfence();
@@ -878,6 +954,7 @@ static cudaError_t launch_moe_fused_t(const LaunchCfg& lc, MoeFusedArgs a) {
     const int n_items = nexp * a.gu_chunks;
     a.up_slots = (n_items + grid - 1) / grid;
     if (a.up_slots > kMoeMaxSlots || a.d_chunks > grid || (a.E + 16) / 16 > grid) return cudaErrorInvalidValue;
+    if (a.cta_trace && grid * kTrMoeCtaSlots > kTraceSlots - kTrMoeCta) a.cta_trace = nullptr;
     const size_t smem = MoeFusedSmem<K, KI, G>::total(a.up_slots, nexp);
     return launch_kernel(lc, moe_fused_kernel<K, KI, G>, dim3(grid), dim3(kMoeThreads), smem, a);
 }
@@ -908,6 +985,7 @@ cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.sync = b.counters + kCntMoeSync;
     a.idflag = reinterpret_cast<unsigned long long*>(b.counters + kCntMoeFlag);
     a.trace = b.trace ? b.trace + kTrMoe : nullptr;
+    a.cta_trace = b.trace ? b.trace + kTrMoeCta : nullptr;
     a.kt = lc.kt;
     a.next_w = next_w;
     a.next_bytes = next_bytes;

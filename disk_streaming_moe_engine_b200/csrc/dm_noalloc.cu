@@ -16,8 +16,9 @@
 //   512  router logits  [E + 1] fp32                     (<= 4 KiB for E <= 1023)
 //   512 + 4 KiB  top-k ids, probabilities, shared gate   (256 B)
 //   then normalised input [H] fp32 and SwiGLU activations [(k + 1) * I] fp32.
-// The array keeps what the last call left in it; only the control block has to start at
-// zero, and the entry point clears it before each launch.
+// The array keeps what the last call left in it; the control block has to start at zero
+// and the router logit slots empty (all-ones bytes): the entry point sets both before each
+// launch.
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -174,6 +175,8 @@ extern "C" int32_t dm_moe_layer_noalloc(int32_t H, int32_t I, int32_t E, int32_t
     lc.l2_prefetch = false;
 
     e = cudaMemsetAsync(base, 0, kCtlBytes, lc.stream);
+    // router logit slots start empty (all-ones NaN pattern; the kernel polls them)
+    if (e == cudaSuccess) e = cudaMemsetAsync(lg, 0xFF, static_cast<size_t>(E + 1) * 4, lc.stream);
     if (e == cudaSuccess) e = launch_moe_fused(lc, d, w, b, 0, nullptr, 0);
     if (e != cudaSuccess)
         return na_err(err_buf, err_buf_size, e == cudaErrorInvalidValue ? DM_ERR_INVALID_ARG : DM_ERR_CUDA,
