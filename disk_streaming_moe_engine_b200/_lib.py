@@ -72,6 +72,7 @@ SIGNATURES = {
     "dm_expert_upload": (I32, [P, I32, I32, I32, P, P, P]),
     "dm_weights_check": (I32, [P]),
     "dm_dequant_q4": (I32, [P, P, P, P, I32, I32, I32, P]),
+    "dm_dequant_sym4": (I32, [P, P, P, C.c_int64, I32, P, P]),
     "dm_seq_reset": (I32, [P, I32]),
     "dm_seq_set_page_table": (I32, [P, I32, P, I32]),
     "dm_seq_get_len": (I32, [P, I32, C.POINTER(I32)]),

@@ -32,6 +32,8 @@ bool attn_supported(int D, int grp);
 int attn_scores_cap(int max_pages, int nsplit);
 int attn_nsplit(int num_sms, int Hkv);
 cudaError_t launch_rope_table(cudaStream_t st, float2* tab, int capacity, int rot_dim, float theta);
+cudaError_t launch_dequant_sym4(cudaStream_t st, const uint8_t* packed, const uint16_t* scales, int64_t n, int group,
+                                uint16_t* out_bf16, float* out_f32, unsigned* bad);
 cudaError_t launch_l2_flush_read(cudaStream_t st, const void* buf, size_t bytes, int num_sms);
 cudaError_t launch_kv_copy(cudaStream_t st, uint16_t* kv_layer, const int* page_table_row, int Hkv,
                            int D, uint16_t* k, uint16_t* v, int n_tokens, int to_cache);
@@ -674,6 +676,56 @@ int32_t dm_dequant_q4(dm_ctx* c, const uint8_t* q, const uint16_t* s, const uint
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     cudaFree(tmp);
     if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "dequant", -1, "%s", cudaGetErrorString(e));
+    return DM_OK;
+}
+
+int32_t dm_dequant_sym4(dm_ctx* c, const uint8_t* packed, const uint16_t* scales, int64_t n, int32_t group,
+                        uint16_t* out_bf16, float* out_f32) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    if (!packed || !scales || (!out_bf16 && !out_f32))
+        return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1, "null buffer");
+    if (group != 32 && group != 64 && group != 128 && group != 256)
+        return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1,
+                       "group_size must be in {32, 64, 128, 256}, got %d", group);
+    if (n <= 0) return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1, "num_elements must be positive");
+    if (n % group != 0)
+        return set_err(c, DM_ERR_INVALID_ARG, "M6_ERR_INPUT", "dequant", -1,
+                       "N %% G != 0 (tail group not supported): N=%lld, G=%d", static_cast<long long>(n), group);
+    const int64_t ng = n / group;
+    for (int64_t g = 0; g < ng; ++g) {  // the reference validates every scale before any output
+        const uint16_t u = scales[g];
+        if (((u >> 10) & 0x1F) == 0x1F)
+            return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1, "scale is NaN or Inf at group %lld",
+                           static_cast<long long>(g));
+        if ((u & 0x8000u) || (u & 0x7FFFu) == 0)
+            return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1, "scale is non-positive at group %lld",
+                           static_cast<long long>(g));
+    }
+    cudaSetDevice(c->device);
+    const size_t pb = static_cast<size_t>(n / 2), sb = static_cast<size_t>(ng) * 2;
+    const size_t o_s = (pb + 255) & ~size_t(255), o_b = o_s + ((sb + 255) & ~size_t(255));
+    const size_t o_f = o_b + (out_bf16 ? ((static_cast<size_t>(n) * 2 + 255) & ~size_t(255)) : 0);
+    const size_t o_bad = o_f + (out_f32 ? ((static_cast<size_t>(n) * 4 + 255) & ~size_t(255)) : 0);
+    uint8_t* tmp = nullptr;
+    DM_CUDA(c, cudaMalloc(&tmp, o_bad + 256), "dequant");
+    uint16_t* dbf = out_bf16 ? reinterpret_cast<uint16_t*>(tmp + o_b) : nullptr;
+    float* df = out_f32 ? reinterpret_cast<float*>(tmp + o_f) : nullptr;
+    unsigned* dbad = reinterpret_cast<unsigned*>(tmp + o_bad);
+    unsigned bad = 0;
+    cudaError_t e = cudaMemcpyAsync(tmp, packed, pb, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tmp + o_s, scales, sb, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dbad, 0, 4, c->stream);
+    if (e == cudaSuccess)
+        e = launch_dequant_sym4(c->stream, tmp, reinterpret_cast<const uint16_t*>(tmp + o_s), n, group, dbf, df, dbad);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&bad, dbad, 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess && !bad && out_bf16) e = cudaMemcpy(out_bf16, dbf, static_cast<size_t>(n) * 2, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && !bad && out_f32) e = cudaMemcpy(out_f32, df, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "dequant", -1, "%s", cudaGetErrorString(e));
+    if (bad)
+        return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1,
+                       "reserved nibble 0b1000 (-8) encountered");
     return DM_OK;
 }
 

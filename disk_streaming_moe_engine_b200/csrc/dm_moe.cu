@@ -1032,6 +1032,54 @@ __global__ void dequant_q4_kernel(const uint8_t* q, const uint16_t* s, const uin
     }
 }
 
+// The reference's own custom 4-bit format (src/quant/dequant_kernel.mojo:22-121): signed
+// two's-complement nibbles in [-7, 7], low nibble first, one fp16 scale per group of G
+// elements; w = fp32(s_g) * q, written as bf16 by one round-to-nearest-even and/or as fp32.
+// Thread t handles packed bytes [8t, 8t + 8) (elements [16t, 16t + 16), inside one group
+// since G >= 32).  A reserved nibble 0b1000 sets *bad; the host then discards the output.
+__global__ void dequant_sym4_kernel(const uint2* __restrict__ packed, const uint16_t* __restrict__ scales,
+                                    int64_t n16, int group, uint4* __restrict__ out_bf16,
+                                    float4* __restrict__ out_f32, unsigned* bad) {
+    const int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+    if (t >= n16) return;
+    const uint2 raw = packed[t];
+    const float s = __half2float(__ushort_as_half(scales[(t * 16) / group]));
+    float y[16];
+    bool reserved = false;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+        const uint32_t byte = ((b < 4 ? raw.x : raw.y) >> (8 * (b & 3))) & 0xFFu;
+        const int lo = static_cast<int>(byte << 28) >> 28;  // sign-extended low nibble
+        const int hi = static_cast<int>(byte << 24) >> 28;  // sign-extended high nibble
+        reserved |= (lo == -8) | (hi == -8);
+        y[2 * b] = s * static_cast<float>(lo);
+        y[2 * b + 1] = s * static_cast<float>(hi);
+    }
+    if (reserved) atomicOr(bad, 1u);
+    if (out_bf16) {
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            w[i] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(y[2 * i]))) |
+                   (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(y[2 * i + 1]))) << 16);
+        out_bf16[2 * t] = make_uint4(w[0], w[1], w[2], w[3]);
+        out_bf16[2 * t + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+    if (out_f32)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) out_f32[4 * t + i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+}
+
+cudaError_t launch_dequant_sym4(cudaStream_t st, const uint8_t* packed, const uint16_t* scales, int64_t n, int group,
+                                uint16_t* out_bf16, float* out_f32, unsigned* bad) {
+    const int64_t n16 = n / 16;
+    const int64_t blocks = (n16 + 255) / 256;
+    dequant_sym4_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+        reinterpret_cast<const uint2*>(packed), scales, n16, group, reinterpret_cast<uint4*>(out_bf16),
+        reinterpret_cast<float4*>(out_f32), bad);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_dequant_q4_canonical(cudaStream_t st, const uint8_t* q, const uint16_t* s,
                                         const uint8_t* z, int rows, int cols, int group, float* out) {
     const int64_t n = static_cast<int64_t>(rows) * cols;

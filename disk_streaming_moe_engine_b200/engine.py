@@ -182,6 +182,18 @@ class Engine:
         self._ok(self.lib.dm_dequant_q4(self.ctx, _ptr(q), _ptr(s), _ptr(z), rows, cols, group, _ptr(out)))
         return out
 
+    def dequant_sym4(self, packed: np.ndarray, scales_f16_bits: np.ndarray, n: int, group: int = 128,
+                     want_bf16: bool = True, want_f32: bool = True):
+        """The reference's custom 4-bit format -> (bf16 bits uint16 [n] or None, fp32 [n] or None)
+        (dequant_kernel_simd / dequant_kernel_simd_f32)."""
+        p = np.ascontiguousarray(packed, np.uint8)
+        sc = np.ascontiguousarray(scales_f16_bits, np.uint16)
+        ob = np.empty(n, np.uint16) if want_bf16 else None
+        of = np.empty(n, np.float32) if want_f32 else None
+        self._ok(self.lib.dm_dequant_sym4(self.ctx, _ptr(p), _ptr(sc), n, group,
+                                          None if ob is None else _ptr(ob), None if of is None else _ptr(of)))
+        return ob, of
+
     # ---- sequence state (KV-cache object, GDN state) ----
     def seq_reset(self, slot: int = 0):
         self._ok(self.lib.dm_seq_reset(self.ctx, slot))

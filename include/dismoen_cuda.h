@@ -175,6 +175,20 @@ int32_t dm_dequant_q4(dm_ctx* ctx, const uint8_t* q_host, const uint16_t* scales
                       const uint8_t* zeros_host, int32_t rows, int32_t cols,
                       int32_t group, float* out_host);
 
+/* The reference's own custom 4-bit file format (reference docs quant_format.md, reader
+ * src/format/quant_reader.mojo:520-724): signed two's-complement nibbles in [-7, 7], low
+ * nibble first, one fp16 scale per group of G in {32, 64, 128, 256}.  Dequantises n
+ * elements on the GPU like dequant_kernel_simd (reference src/quant/dequant_kernel.mojo:22):
+ * out_bf16_host = bf16(fp32(s_g) * q) by one round-to-nearest-even, and/or
+ * out_f32_host = fp32(s_g) * q (dequant_kernel_simd_f32, :130); either may be NULL.
+ * Rejects what the reference rejects, with DM_ERR_INVALID_ARG and the reason in
+ * dm_last_error: G outside the set, N % G != 0, a NaN / Inf / non-positive scale (checked
+ * before any copy) and the reserved nibble 0b1000 (found by the kernel; nothing is
+ * written to the outputs). */
+int32_t dm_dequant_sym4(dm_ctx* ctx, const uint8_t* packed_host, const uint16_t* scales_host,
+                        int64_t num_elements, int32_t group_size, uint16_t* out_bf16_host,
+                        float* out_f32_host);
+
 /* ---- sequence state: the KV-cache object and GDN state -------------------------------
  * KV cache: paged bf16, 16-token pages.  Page p of slot s holds tokens
  * [16p, 16p+16) at physical page page_table[s][p]; layout per attention layer

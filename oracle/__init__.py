@@ -61,6 +61,8 @@ def load() -> C.CDLL:
         lib.or_router.argtypes = [C.POINTER(OrDims), C.POINTER(OrLayer), P, P, P, P, P]
         lib.or_rmsnorm_canonical.argtypes = [P, P, C.c_int, C.c_float, P]
         lib.or_dequant_q4.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, P]
+        lib.or_dequant_sym4.restype = C.c_int
+        lib.or_dequant_sym4.argtypes = [P, P, C.c_longlong, C.c_int, P, P]
         lib.or_head.restype = C.c_int
         lib.or_head.argtypes = [C.POINTER(OrModel), P, P]
         lib.or_det_exp.restype = C.c_float
@@ -178,6 +180,16 @@ def dequant_q4(q, s, z, rows, cols, group=64):
     load().or_dequant_q4(_p(np.ascontiguousarray(q)), _p(np.ascontiguousarray(s)), _p(np.ascontiguousarray(z)),
                          rows, cols, group, _p(out))
     return out
+
+
+def dequant_sym4(packed, scales_f16_bits, n, group=128):
+    """(bf16 bits uint16 [n], fp32 [n], status) for the reference's custom 4-bit format;
+    status 0 ok, -1 reserved nibble 0b1000, -2 NaN / Inf / non-positive scale."""
+    ob = np.empty(n, np.uint16)
+    of = np.empty(n, np.float32)
+    rc = load().or_dequant_sym4(_p(np.ascontiguousarray(packed, np.uint8)),
+                                _p(np.ascontiguousarray(scales_f16_bits, np.uint16)), n, group, _p(ob), _p(of))
+    return ob, of, rc
 
 
 def det_exp(x: float) -> float:

@@ -124,6 +124,30 @@ void or_dequant_q4(const uint8_t* q, const uint16_t* s, const uint8_t* z, int ro
     }
 }
 
+/* The reference's custom 4-bit format: restates dequant_kernel_simd
+ * (src/quant/dequant_kernel.mojo:22-121) and dequant_kernel_simd_f32: signed nibbles in
+ * [-7, 7], low nibble first, w = fp32(s_g) * q, bf16 by one round-to-nearest-even.
+ * Returns 0, -2 on a NaN / Inf / non-positive scale (nothing written), or -1 on a reserved
+ * nibble 0b1000 (the outputs are then incomplete). */
+int or_dequant_sym4(const uint8_t* packed, const uint16_t* scales, long long n, int group, uint16_t* out_bf16,
+                    float* out_f32) {
+    for (long long g = 0; g < n / group; ++g) { /* NaN / Inf / non-positive scales (:66-78) */
+        const uint16_t u = scales[g];
+        if (((u >> 10) & 0x1F) == 0x1F || (u & 0x8000u) || (u & 0x7FFFu) == 0) return -2;
+    }
+    int bad = 0;
+    for (long long i = 0; i < n; ++i) {
+        const uint8_t byte = packed[i / 2];
+        const int u = (i & 1) ? (byte >> 4) : (byte & 15);
+        if (u == 8) bad = 1;
+        const int q = u >= 8 ? u - 16 : u;
+        const float y = f16f(scales[i / group]) * (float)q;
+        if (out_bf16) out_bf16[i] = f2bf16(y);
+        if (out_f32) out_f32[i] = y;
+    }
+    return bad ? -1 : 0;
+}
+
 /* One row of a canonical 4-bit matrix dequantised then dotted with x (fp32). */
 static float q4_row_dot(const uint8_t* qrow, const uint16_t* srow, const uint8_t* zrow, int cols, int group,
                         const float* x, float* scratch) {

@@ -88,6 +88,11 @@ void or_router(const or_dims* d, const or_layer* w, const float* xn, int* ids, f
 void or_dequant_q4(const uint8_t* q, const uint16_t* s, const uint8_t* z, int rows, int cols,
                    int group, float* out);
 
+/* The reference's custom 4-bit format (dequant_kernel_simd): 0, -2 on a bad scale, or -1 on
+ * a reserved nibble. */
+int or_dequant_sym4(const uint8_t* packed, const uint16_t* scales, long long n, int group, uint16_t* out_bf16,
+                    float* out_f32);
+
 /* MoE sublayer with residual: x_out = x_mid + moe(norm(x_mid)); ids optional [topk]. */
 void or_moe_block(const or_dims* d, const or_layer* w, const float* x_mid, float* x_out, int* ids_out,
                   float* probs_out);
