@@ -244,6 +244,8 @@ def step_timeline(eng, steps: int):
     rel = lambda a, b: [round((int(v) - int(ph[b])) / 1e3, 2) if v else None for v in ph[a:b + 9]] if ph[b] else None
     phases = {"attn_last_split_cta": [round((int(v) - int(ph[0])) / 1e3, 2) if v else None for v in ph[0:10]],
               "moe_topk_detail": [round((int(v) - int(ph[16])) / 1e3, 2) if v else None for v in ph[36:40]],
+              "moe_down_detail": [round((int(v) - int(ph[16])) / 1e3, 2) if v else None for v in ph[56:59]] + [int(ph[59])],
+              "moe_topk_round_cycles": int(ph[60]),
               "attn_pages": [round((int(v) - int(ph[0])) / 1e3, 2) if v else None for v in ph[40:56]],
               "moe_cta0": [round((int(v) - int(ph[16])) / 1e3, 2) if v else None for v in ph[16:25]],
               "moe_last_cta": [round((int(v) - int(ph[26])) / 1e3, 2) if v else None for v in ph[26:35]]}

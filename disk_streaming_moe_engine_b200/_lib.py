@@ -113,7 +113,7 @@ def load(path: str | None = None) -> C.CDLL:
     global _LIB
     if _LIB is not None and path is None:
         return _LIB
-    p = path or LIB_PATH
+    p = path or os.environ.get("DISMOEN_LIB") or LIB_PATH  # DISMOEN_LIB: an alternative build
     if not os.path.exists(p):
         raise RuntimeError(
             f"libdismoen_cuda.so not found at {p}; build it with "

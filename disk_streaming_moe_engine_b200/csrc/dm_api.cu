@@ -77,6 +77,7 @@ struct dm_ctx {
     std::vector<int> dev_pos_valid;    // device pos[slot] == slot_len[slot]
     std::vector<cudaGraphExec_t> graphs;  // decode step per slot
     bool use_pdl = true;       // programmatic dependent launch between step kernels
+    bool gdn_fused = true;     // GDN recurrence + output projection as one kernel
     bool l2_prefetch = false;  // latency-bound kernels prefetch upcoming weights into L2 (off:
                                // measured slower, the prefetch competes with the step's reads)
     uint64_t* trace_buf = nullptr;
@@ -421,6 +422,7 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     // programmatic dependent launch; DISMOEN_L2_PREFETCH=1 enables the L2 prefetch of
     // upcoming weights by the latency-bound kernels
     if (const char* v = getenv("DISMOEN_PDL")) c->use_pdl = atoi(v) != 0;
+    if (const char* v = getenv("DISMOEN_GDN_FUSED")) c->gdn_fused = atoi(v) != 0;
     if (const char* v = getenv("DISMOEN_L2_PREFETCH")) c->l2_prefetch = atoi(v) != 0;
     c->mc = *model;
     c->rc = *rt;
@@ -431,6 +433,7 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = gemv_set_attrs();
     if (e == cudaSuccess) e = moe_set_attrs();
+    if (e == cudaSuccess) e = gdn_set_attrs();
     if (e == cudaSuccess) e = router_set_attrs();
     // function attributes are per process: always the kernel's fixed maximum, never a
     // per-context value that a later, smaller context would lower
@@ -507,9 +510,13 @@ int32_t dm_get_stream(dm_ctx* c, void** s) {
     return DM_OK;
 }
 
+static bool gdn_fused_on(const dm_ctx* c) { return c->gdn_fused && gdn_fused_supported(c->d, c->num_sms); }
+
 int32_t dm_kernels_per_step(dm_ctx* c, int32_t* out) {
     if (!c || !out) return DM_ERR_INVALID_ARG;
-    *out = 1 + 4 * c->d.L + 1;  // embed, 3 mixer kernels + 1 MoE kernel per block, head
+    // embed; per block the mixer kernels (attention 3; GDN 2 fused or 3) + 1 MoE kernel; head
+    const int gdn_k = gdn_fused_on(c) ? 2 : 3;
+    *out = 1 + c->d.n_att * 4 + c->d.n_gdn * (gdn_k + 1) + 1;
     return DM_OK;
 }
 
@@ -911,6 +918,7 @@ static cudaError_t enqueue_mixer(dm_ctx* c, int layer, int slot) {
         return launch_attn_out(lcfg_traced(c, TK_ATTN_OUT, layer), c->d, w, c->b, slot);
     }
     if ((e = launch_gdn_in(lcfg_traced(c, TK_GDN_IN, layer), c->d, w, c->b, slot)) != cudaSuccess) return e;
+    if (gdn_fused_on(c)) return launch_gdn_core_out(lcfg_traced(c, TK_GDN_CORE_OUT, layer), c->d, w, c->b, slot);
     if ((e = launch_gdn_rec(lcfg_traced(c, TK_GDN_REC, layer), c->d, w, c->b, slot)) != cudaSuccess) return e;
     return launch_gdn_out(lcfg_traced(c, TK_GDN_OUT, layer), c->d, w, c->b, slot);
 }
@@ -1208,8 +1216,9 @@ int32_t dm_time_kernel(dm_ctx* c, int32_t which, int32_t layer, int32_t iters, f
                 return w.is_attn ? launch_attn_in(lc, d, w, c->b, slot) : launch_gdn_in(lc, d, w, c->b, slot);
             case DM_KERNEL_MIXER_OUT:
                 return w.is_attn ? launch_attn_out(lc, d, w, c->b, slot) : launch_gdn_out(lc, d, w, c->b, slot);
-            case DM_KERNEL_MIXER_CORE:
-                return w.is_attn ? launch_attn_decode(lc, d, w, c->b, slot) : launch_gdn_rec(lc, d, w, c->b, slot);
+            case DM_KERNEL_MIXER_CORE:  // GDN: the recurrence, with the output projection when fused
+                if (w.is_attn) return launch_attn_decode(lc, d, w, c->b, slot);
+                return gdn_fused_on(c) ? launch_gdn_core_out(lc, d, w, c->b, slot) : launch_gdn_rec(lc, d, w, c->b, slot);
             case DM_KERNEL_ROUTER: return launch_router(lc, d, w, c->b, slot, 1);
             case DM_KERNEL_MOE: return launch_moe_fused(lc, d, w, c->b, slot);
             case DM_KERNEL_HEAD: return launch_head(lc, d, c->final_norm, c->lm_head, c->b, slot, 0, 0);
@@ -1224,7 +1233,8 @@ int32_t dm_time_kernel(dm_ctx* c, int32_t which, int32_t layer, int32_t iters, f
         case DM_KERNEL_MIXER_CORE: {
             int len = c->slot_len[slot];
             *bytes = w.is_attn ? static_cast<uint64_t>(len + 1) * 2 * d.Hkv * d.D * 2
-                               : 2ull * d.nv * d.dv * d.dk * 4 + 4ull * d.qkv_dim * 4;
+                               : 2ull * d.nv * d.dv * d.dk * 4 + 4ull * d.qkv_dim * 4 +
+                                     (gdn_fused_on(c) ? H * d.z_dim * 2 : 0);
             break;
         }
         case DM_KERNEL_ROUTER: *bytes = (d.E + 1) * H * 2; break;

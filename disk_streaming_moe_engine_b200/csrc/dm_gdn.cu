@@ -170,4 +170,264 @@ cudaError_t launch_gdn_rec(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     return cudaErrorInvalidValue;
 }
 
+// ---------------------------------------------------------------------------------------
+// GDN recurrence + output projection in one kernel (grid = #SMs, all CTAs co-resident).
+//   pre-wait  each CTA copies its contiguous block of out-projection rows into shared
+//             memory (one 1-D bulk copy per row): the projection's weights stream while
+//             the input projection and the recurrence run; each 128-thread group loads the
+//             state rows of its recurrence item (nv x dv/16 items: item = group * G + CTA)
+//   phase 1   the recurrence of gdn_rec_kernel per item (named barrier per group)
+//   barrier   grid-wide (release add + bounded acquire spin)
+//   phase 2   every CTA: head RMSNorm * w * SiLU(z) of the full o, then its rows of
+//             W_out from shared memory, + residual (one row per warp)
+//   exit      the last CTA out resets the counters for the next launch
+struct GdnFusedArgs {
+    GdnRecArgs rec;
+    const uint16_t* W_out;  // [H][nv*dv]
+    const float* z;         // [nv*dv] SiLU(z) from the input projection
+    const uint16_t* gnorm;  // [dv]
+    const float* x_res;     // [H]
+    float* x_mid;           // [H]
+    int H, rmax;
+    unsigned* sync;         // [2]: arrivals, exits
+    uint32_t* err;
+};
+
+constexpr int kGfThreads = 512;
+
+template <int DK>
+__global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __grid_constant__ GdnFusedArgs f) {
+    constexpr int DV = DK;
+    constexpr int RB = 16;
+    constexpr int CPL = DK / 32;
+    const GdnRecArgs& a = f.rec;
+    extern __shared__ __align__(128) uint8_t gsm[];
+    __shared__ float qs[4][DK], ks[4][DK], vs[4][RB];
+    __shared__ __align__(8) uint64_t wbar;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int grp = warp >> 2, gw = warp & 3, gt = tid & 127;
+    const int c = blockIdx.x, G = gridDim.x;
+    const int KO = a.nv * DV;
+    const int r0 = static_cast<int>(static_cast<long long>(c) * f.H / G);
+    const int r1 = static_cast<int>(static_cast<long long>(c + 1) * f.H / G);
+    const int nr = r1 - r0;
+    uint8_t* wsm = gsm;                                                       // [rmax][KO] bf16
+    float* xs = reinterpret_cast<float*>(gsm + static_cast<size_t>(f.rmax) * KO * 2);  // [KO]
+    kt_start(a.kt);
+
+    if (tid == 0) {
+        mbar_init(&wbar, 1);
+        mbar_fence_init();
+        if (nr > 0) {
+            mbar_arrive_expect_tx(&wbar, static_cast<uint32_t>(nr) * KO * 2);
+            for (int r = 0; r < nr; ++r)
+                bulk_g2s(wsm + static_cast<size_t>(r) * KO * 2, f.W_out + static_cast<size_t>(r0 + r) * KO, KO * 2, &wbar);
+        } else {
+            mbar_arrive(&wbar);
+        }
+    }
+    // this group's recurrence item
+    const int nrb = DV / RB;
+    const int item = grp * G + c;
+    const bool has_item = item < a.nv * nrb;
+    const int h = has_item ? item / nrb : 0, rb = has_item ? item % nrb : 0;
+    const int g_qk = h / (a.nv / a.nk);
+    float* Sh = a.S + static_cast<size_t>(h) * DV * DK;
+    float srow[4][CPL];
+    float alog = 0.0f, dtb = 0.0f;
+    if (has_item) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float* src = Sh + static_cast<size_t>(rb * RB + gw * 4 + i) * DK + lane * CPL;
+#pragma unroll
+            for (int cc = 0; cc < CPL; ++cc) srow[i][cc] = src[cc];
+        }
+        alog = a.a_log[h];
+        dtb = a.dt_bias[h];
+    }
+    pdl_wait();
+    kt_ready(a.kt);
+
+    // ---- phase 1: recurrence ----
+    if (has_item) {
+        const int pos = *a.pos;
+        const float av = a.ab[h], bv = a.ab[a.nv + h];
+        const int q0 = g_qk * DK, k0 = a.nk * DK + g_qk * DK, v0 = 2 * a.nk * DK + h * DV + rb * RB;
+        for (int t = gt; t < 2 * DK + RB; t += 128) {
+            const int ch = t < DK ? q0 + t : (t < 2 * DK ? k0 + (t - DK) : v0 + (t - 2 * DK));
+            const uint16_t* w = a.conv_w + static_cast<size_t>(ch) * 4;
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int tp = pos - 3 + j;
+                if (tp >= 0) acc += bf16_to_f32(w[j]) * a.ring[static_cast<size_t>(tp & 3) * a.qkv_dim + ch];
+            }
+            const float u = silu_f(acc);
+            if (t < DK) qs[grp][t] = u;
+            else if (t < 2 * DK) ks[grp][t - DK] = u;
+            else vs[grp][t - 2 * DK] = u;
+        }
+        named_bar_sync(1 + grp, 128);
+        float kl[CPL], ql[CPL];
+        float ss = 0.0f;
+#pragma unroll
+        for (int cc = 0; cc < CPL; ++cc) {
+            kl[cc] = ks[grp][lane * CPL + cc];
+            ql[cc] = qs[grp][lane * CPL + cc];
+            ss = fmaf(kl[cc], kl[cc], ss);
+        }
+        ss = warp_sum(ss);
+        const float inv_nk = 1.0f / (sqrtf(ss) + a.eps);
+#pragma unroll
+        for (int cc = 0; cc < CPL; ++cc) kl[cc] *= inv_nk;
+        const float g = expf(-expf(alog) * softplus_ref(av + dtb));
+        const float beta = sigmoid_f(bv);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int rl = gw * 4 + i;
+            const int r = rb * RB + rl;
+            float sk = 0.0f;
+#pragma unroll
+            for (int cc = 0; cc < CPL; ++cc) sk = fmaf(srow[i][cc], kl[cc], sk);
+            sk = warp_sum(sk);
+            const float vr = vs[grp][rl];
+            const float bsk = beta * sk, bvr = beta * vr;
+            float oacc = 0.0f;
+#pragma unroll
+            for (int cc = 0; cc < CPL; ++cc) {
+                const float sn = g * (srow[i][cc] - bsk * kl[cc]) + bvr * kl[cc];
+                srow[i][cc] = sn;
+                oacc = fmaf(sn, ql[cc], oacc);
+            }
+            oacc = warp_sum(oacc);
+            float* dst = Sh + static_cast<size_t>(r) * DK + lane * CPL;
+#pragma unroll
+            for (int cc = 0; cc < CPL; ++cc) dst[cc] = srow[i][cc];
+            if (lane == 0) a.o[h * DV + r] = oacc;
+        }
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    if (tid == 0) {
+        __threadfence();
+        red_release_add(&f.sync[0], 1u);
+        spin_geq(&f.sync[0], static_cast<unsigned>(G), f.err);
+    }
+    __syncthreads();
+
+    // ---- phase 2: head RMSNorm * w * SiLU(z) of the whole o (each warp a head at a time;
+    // dv <= 128, one batch of loads per head), then this CTA's rows ----
+    float* xlo = xs;
+    float* xhi = xs + KO / 2;
+    for (int hh = warp; hh < a.nv; hh += kGfThreads / 32) {
+        float ov[4], zv[4], wv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int d = lane + 32 * i;
+            ov[i] = d < DV ? __ldcg(a.o + hh * DV + d) : 0.0f;
+            zv[i] = d < DV ? __ldcg(f.z + hh * DV + d) : 0.0f;
+            wv[i] = d < DV ? bf16_to_f32(f.gnorm[d]) : 0.0f;
+        }
+        float acc = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc = fmaf(ov[i], ov[i], acc);
+        acc = warp_sum(acc);
+        const float rs = 1.0f / sqrtf(acc / static_cast<float>(DV) + a.eps);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int d = lane + 32 * i;
+            if (d < DV) {
+                const int k = hh * DV + d;  // element 8j + e goes to (e < 4 ? xlo : xhi)[4j + e % 4]
+                (((k & 7) < 4) ? xlo : xhi)[(k >> 3) * 4 + (k & 3)] = ov[i] * rs * wv[i] * zv[i];
+            }
+        }
+    }
+    __syncthreads();
+    const bool wok = mbar_wait_bounded(&wbar, 0, f.err, nullptr);
+    const float4* x4lo = reinterpret_cast<const float4*>(xlo);
+    const float4* x4hi = reinterpret_cast<const float4*>(xhi);
+    for (int r = warp; r < nr; r += kGfThreads / 32) {
+        const uint4* wr = reinterpret_cast<const uint4*>(wsm + static_cast<size_t>(r) * KO * 2);
+        float s0 = 0.0f, s1 = 0.0f;
+        for (int j = lane; j < KO / 8; j += 32) {
+            const uint4 w = wr[j];
+            const float4 lo = x4lo[j], hi = x4hi[j];
+            s0 = fmaf(bf16lo(w.x), lo.x, s0);
+            s1 = fmaf(bf16hi(w.x), lo.y, s1);
+            s0 = fmaf(bf16lo(w.y), lo.z, s0);
+            s1 = fmaf(bf16hi(w.y), lo.w, s1);
+            s0 = fmaf(bf16lo(w.z), hi.x, s0);
+            s1 = fmaf(bf16hi(w.z), hi.y, s1);
+            s0 = fmaf(bf16lo(w.w), hi.z, s0);
+            s1 = fmaf(bf16hi(w.w), hi.w, s1);
+        }
+        const float acc = warp_sum(s0 + s1);
+        if (lane == 0) f.x_mid[r0 + r] = f.x_res[r0 + r] + (wok ? acc : 0.0f);
+    }
+    __syncthreads();
+    kt_end(a.kt);
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(&f.sync[1], 1u);
+        if (prev == static_cast<unsigned>(G) - 1) {
+            f.sync[0] = 0u;
+            f.sync[1] = 0u;
+        }
+    }
+}
+
+static size_t gdn_fused_smem(const Dims& d, int G) {
+    const int rmax = (d.H + G - 1) / G;
+    return static_cast<size_t>(rmax) * d.z_dim * 2 + static_cast<size_t>(d.z_dim) * 4;
+}
+
+constexpr size_t kGdnFusedMaxSmem = 200 * 1024;
+
+bool gdn_fused_supported(const Dims& d, int num_sms) {
+    return (d.dk == 128 || d.dk == 64) && d.dv == d.dk && d.z_dim % 256 == 0 &&
+           d.nv * (d.dv / 16) <= 4 * num_sms && gdn_fused_smem(d, num_sms) <= kGdnFusedMaxSmem;
+}
+
+cudaError_t gdn_set_attrs() {
+    cudaError_t e = cudaFuncSetAttribute(gdn_core_out_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kGdnFusedMaxSmem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gdn_core_out_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(kGdnFusedMaxSmem));
+    return e;
+}
+
+cudaError_t launch_gdn_core_out(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot) {
+    if (!gdn_fused_supported(d, lc.num_sms)) return cudaErrorInvalidValue;
+    GdnFusedArgs f{};
+    GdnRecArgs& a = f.rec;
+    const size_t ls = static_cast<size_t>(w.sub) * d.max_seqs + slot;
+    a.ring = b.ring + ls * kConvRing * d.qkv_dim;
+    a.conv_w = w.conv_w;
+    a.S = b.S + ls * static_cast<size_t>(d.nv) * d.dv * d.dk;
+    a.a_log = w.a_log;
+    a.dt_bias = w.dt_bias;
+    a.ab = b.ab;
+    a.o = b.o;
+    a.pos = b.pos + slot;
+    a.nk = d.nk;
+    a.nv = d.nv;
+    a.qkv_dim = d.qkv_dim;
+    a.eps = d.eps;
+    a.kt = lc.kt;
+    f.W_out = w.w_out;
+    f.z = b.z;
+    f.gnorm = w.gdn_norm;
+    f.x_res = b.xres + static_cast<size_t>(slot) * d.H;
+    f.x_mid = b.xmid + static_cast<size_t>(slot) * d.H;
+    f.H = d.H;
+    const int G = lc.num_sms;
+    f.rmax = (d.H + G - 1) / G;
+    f.sync = b.counters + kCntGdnSync;
+    f.err = b.err;
+    const size_t smem = gdn_fused_smem(d, G);
+    if (d.dk == 128) return launch_kernel(lc, gdn_core_out_kernel<128>, dim3(G), dim3(kGfThreads), smem, f);
+    return launch_kernel(lc, gdn_core_out_kernel<64>, dim3(G), dim3(kGfThreads), smem, f);
+}
+
 }  // namespace dm

@@ -277,7 +277,12 @@ static cudaError_t launch_gemv_t(const LaunchCfg& lc, GemvArgs a) {
         const int n = v ? atoi(v) : 2;
         return n == 1 ? 1 : 2;
     }();
-    const int cap = lc.num_sms * per_sm;
+    static const int per_sm_wide = [] {  // K > 2048 (output projections); 0 = same as above
+        const char* v = getenv("DISMOEN_GEMV_CTAS_PER_SM_WIDE");
+        const int n = v ? atoi(v) : 0;
+        return (n == 1 || n == 2) ? n : 0;
+    }();
+    const int cap = lc.num_sms * ((K > 2048 && per_sm_wide) ? per_sm_wide : per_sm);
     int grid = want < cap ? want : cap;
     if (a.counter && grid > kMaxCtas) grid = kMaxCtas;
     return launch_kernel(lc, gemv_bf16_kernel<K, PRO>, dim3(grid), dim3(kGemvThreads), 0, a);

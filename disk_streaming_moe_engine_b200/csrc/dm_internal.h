@@ -119,6 +119,7 @@ constexpr int kMaxCtas = 1024;
 constexpr int kCntRouter = 0;
 constexpr int kCntHead = 1;
 constexpr int kCntAttnBase = 8;   // + kv head (< 32)
+constexpr int kCntGdnSync = 40;   // 2 words: arrivals / exits of the fused GDN core + out kernel
 constexpr int kCntMoeSync = 48;   // 4 words of grid-wide counters of the fused MoE kernel
 constexpr int kCntMoeFlag = 56;   // 8 words (4 x u64, 8-byte aligned) of released id words
 
@@ -134,7 +135,7 @@ struct LaunchCfg {
 
 // Timeline record kinds (dm_trace_timeline)
 enum TraceKind { TK_EMBED = 0, TK_GDN_IN = 1, TK_GDN_REC = 2, TK_GDN_OUT = 3, TK_ATTN_IN = 4, TK_ATTN = 5,
-                 TK_ATTN_OUT = 6, TK_MOE = 7, TK_HEAD = 8 };
+                 TK_ATTN_OUT = 6, TK_MOE = 7, TK_HEAD = 8, TK_GDN_CORE_OUT = 9 };
 constexpr int kMaxTraceKernels = 512;
 
 // Kernel launchers (dm_kernels.cu).  `slot` selects the sequence.
@@ -146,6 +147,12 @@ cudaError_t launch_gdn_rec(const LaunchCfg& lc, const Dims& d, const LayerW& w,
                            const Buffers& b, int slot);
 cudaError_t launch_gdn_out(const LaunchCfg& lc, const Dims& d, const LayerW& w,
                            const Buffers& b, int slot);
+// GDN recurrence + output projection fused (grid = #SMs); supported() says whether the
+// shapes fit it (else the two kernels above are used).
+cudaError_t launch_gdn_core_out(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                                const Buffers& b, int slot);
+bool gdn_fused_supported(const Dims& d, int num_sms);
+cudaError_t gdn_set_attrs();
 cudaError_t launch_attn_in(const LaunchCfg& lc, const Dims& d, const LayerW& w,
                            const Buffers& b, int slot);
 cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW& w,

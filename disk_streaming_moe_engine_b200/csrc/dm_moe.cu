@@ -362,11 +362,6 @@ struct MoeFusedArgs {
     uint32_t* err;
 };
 
-DM_DEV unsigned ld_acquire_u32(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 DM_DEV void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -374,9 +369,6 @@ DM_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
-}
-DM_DEV void red_release_add(unsigned* p, unsigned v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 DM_DEV unsigned ld_relaxed_u32(const unsigned* p) {
     unsigned v;
@@ -420,19 +412,6 @@ DM_DEV unsigned long long spin_marker(const unsigned long long* p, uint32_t* err
         }
     }
 }
-// Bounded wait until *p >= target (thread-level; callers use one thread per CTA).
-DM_DEV bool spin_geq(const unsigned* p, unsigned target, uint32_t* err) {
-    if (ld_acquire_u32(p) >= target) return true;
-    const uint64_t t0 = globaltimer_ns();
-    uint32_t n = 0;
-    while (true) {
-        if (ld_acquire_u32(p) >= target) return true;
-        if (++n % 256 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
-            raise_error(err, DM_DEVERR_TIMEOUT);
-            return false;
-        }
-    }
-}
 
 constexpr int kMoeThreads = 512;
 
@@ -460,8 +439,6 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     __shared__ int sid[kMaxTopK];
     __shared__ float sp[kMaxTopK + 1];
     __shared__ float red[kMoeThreads / 32];
-    __shared__ float dnp[2][16];  // per warp-group partial of routed sums
-    __shared__ float dsh[16];     // shared-expert dots
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int nblk = gridDim.x, c = blockIdx.x;
     const int nexp = a.topk + 1;
@@ -521,6 +498,8 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     kt_ready(a.kt);
     trace_stamp(tr, 1);
     trace_stamp(ct, 1);
+    // residual of this warp's output row (phase 3), fetched now, off the critical path
+    const float xm_row = (has_down && lane == 0) ? a.x_mid[16 * c + warp] : 0.0f;
 
     // ---- phase 1: canonical RMSNorm (512 threads), router rows ----
     {
@@ -686,7 +665,8 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 DM_CX(2, 4) DM_CX(3, 5)
                 DM_CX(1, 2) DM_CX(3, 4) DM_CX(5, 6)
         #undef DM_CX
-        #pragma unroll
+                        const long long tk0 = clock64();
+#pragma unroll
                 for (int r = 0; r < kMaxTopK; ++r) {
                     if (r >= topk) break;
                     const uint32_t mb = __reduce_max_sync(0xffffffffu, kb[0]);
@@ -705,6 +685,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                     my_id = lane == r ? (oob ? r : bi) : my_id;
                     my_p = lane == r ? (oob ? 0u : mb) : my_p;
                 }
+                if (lane == 0 && tr) tr[44] = static_cast<uint64_t>(clock64() - tk0);  // rounds, SM cycles (slot 60)
             } else {
                 // E > 256: experts beyond 32*PL per lane live in shared memory (taken = -2);
                 // each round every lane offers its best untaken one
@@ -865,8 +846,15 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         ct[7] = smid;
     }
 
-    // ---- phase 3: 16 output rows of every selected expert + residual ----
+    // ---- phase 3: 16 output rows of every selected expert + residual.  Warp w owns output
+    // row 16c + w; lane l covers the WPL = I/32 contiguous weights [l*WPL, l*WPL + WPL) of
+    // that row in every expert; the lane accumulates all experts, weighted by the router
+    // probability (the shared expert by its sigmoid gate), and one warp reduction ends the
+    // row.  h is restaged lane-major so every read is conflict-free.
     if (has_down) {
+        constexpr int WPL = KI / 32;   // weights per lane
+        constexpr int F4L = WPL / 4;   // float4 of h per lane
+        static_assert(WPL >= 4 && WPL % 4 == 0 && WPL <= G, "down-row lane geometry");
         if (c != 0) {
             if (tid < a.topk) sp[tid] = __ldcg(a.probs + tid);
             if (tid == 0) sp[a.topk] = __ldcg(a.shared_g);
@@ -883,48 +871,63 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
 #pragma unroll
             for (int i = 0; i < HPT; ++i) {
                 const int t = tid + kMoeThreads * i;
-                if (t < nh) x4_store<KI>(h4 + (t / KI) * KI, t % KI, hv[i]);
-            }
-        }
-        __syncthreads();
-        const int wgrp = warp >> 3, wg = warp & 7;
-        const int sub = lane / QD::LPR, vl = lane % QD::LPR;
-        float routed[2] = {0.0f, 0.0f}, shv[2] = {0.0f, 0.0f};
-        bool ok = true;
-        for (int j = wgrp; j < nexp; j += 2) ok &= mbar_wait_bounded(&bar_dn[j], 0, a.err, nullptr);
-#pragma unroll
-        for (int jj = 0; jj < (kMaxTopK + 2) / 2; ++jj) {
-            const int j = wgrp + 2 * jj;
-            if (j >= nexp) break;
-            const uint8_t* chunk = dn_s + static_cast<size_t>(j) * QD::CHUNK;
-            const float4* hv = reinterpret_cast<const float4*>(h4 + j * KI);
-#pragma unroll
-            for (int p = 0; p < 2; p += QD::RPP) {
-                const int ri = p + sub;
-                float v = 0.0f;
-                if (ri < 2 && ok) v = q4_partial_smem<KI, G>(chunk, 2 * wg + ri, vl, hv);
-                v = lane_group_sum<QD::LPR>(v);
-                if (ri < 2) {
-                    if (j < a.topk) routed[ri] = fmaf(sp[j], v, routed[ri]);
-                    else shv[ri] = v;
+                if (t < nh) {
+                    const int j = t / KI, k = t % KI, l = k / WPL, w = k % WPL;
+                    h4[((j * F4L + (w >> 2)) * 32 + l) * 4 + (w & 3)] = hv[i];
                 }
             }
         }
-        if (vl == 0) {
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-                const int ri = (QD::RPP == 1) ? p : sub;
-                if (QD::RPP != 1 && p > 0) break;
-                if (ri >= 2) continue;
-                dnp[wgrp][2 * wg + ri] = routed[ri];
-                if ((a.topk & 1) == wgrp) dsh[2 * wg + ri] = shv[ri];
-            }
-        }
         __syncthreads();
-        if (tid < 16) {
-            const int orow = 16 * c + tid;
-            a.x_out[orow] = ((dnp[0][tid] + dnp[1][tid]) + sp[a.topk] * dsh[tid]) + a.x_mid[orow];
+        trace_stamp(tr ? tr + 40 : nullptr, 0);  // down-phase detail of CTA 0 (slots 56..58)
+        bool ok = true;
+        for (int j = 0; j < nexp; ++j) ok &= mbar_wait_bounded(&bar_dn[j], 0, a.err, nullptr);
+        trace_stamp(tr ? tr + 40 : nullptr, 1);
+        const long long cyc0 = clock64();
+        const int gl = (lane * WPL) / G;  // this lane's scale group
+        const float4* h4v = reinterpret_cast<const float4*>(h4);
+        // one expert's contribution to this lane: s * sum (F(q) - F(z)) * h, times its weight
+        auto expert_part = [&](int j) -> float {
+            const uint8_t* chunk = dn_s + static_cast<size_t>(j) * QD::CHUNK;
+            const uint8_t* qrow = chunk + warp * (KI / 2) + lane * (WPL / 2);
+            const float s = __half2float(
+                __ushort_as_half(reinterpret_cast<const uint16_t*>(chunk + QD::S_OFF)[warp * (KI / G) + gl]));
+            const uint32_t zb = chunk[QD::Z_OFF + warp * (KI / G / 2) + (gl >> 1)];
+            const float fz = __uint_as_float(0x4B000000u | ((gl & 1) ? (zb >> 4) : (zb & 15u)));
+            uint32_t words[WPL / 8 > 0 ? WPL / 8 : 1];
+            if (WPL == 16) {
+                const uint2 q = *reinterpret_cast<const uint2*>(qrow);
+                words[0] = q.x;
+                words[WPL / 8 - 1] = q.y;
+            } else if (WPL == 8) {
+                words[0] = *reinterpret_cast<const uint32_t*>(qrow);
+            } else {
+                words[0] = *reinterpret_cast<const uint16_t*>(qrow);
+            }
+            float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+            for (int f = 0; f < F4L; ++f) {
+                const float4 xv = h4v[(j * F4L + f) * 32 + lane];
+                const uint32_t wd = words[f >> 1] >> (16 * (f & 1));  // 4 weights: 2 bytes
+                const uint32_t lo = wd & 0x0F0Fu, hi = (wd >> 4) & 0x0F0Fu;
+                d0 = fmaf(nib(lo, 0) - fz, xv.x, d0);
+                d1 = fmaf(nib(hi, 0) - fz, xv.y, d1);
+                d0 = fmaf(nib(lo, 1) - fz, xv.z, d0);
+                d1 = fmaf(nib(hi, 1) - fz, xv.w, d1);
+            }
+            return s * (d0 + d1) * (j < a.topk ? sp[j] : sp[a.topk]);
+        };
+        // rolled (the code runs once per launch and is fetched cold), two experts per
+        // iteration so their loads and chains overlap
+        float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 1
+        for (int j = 0; j < nexp; j += 2) {
+            acc0 += expert_part(j);
+            if (j + 1 < nexp) acc1 += expert_part(j + 1);
         }
+        const float acc = warp_sum(ok ? acc0 + acc1 : 0.0f);
+        trace_stamp(tr ? tr + 40 : nullptr, 2);
+        if (tr) tr[43] = static_cast<uint64_t>(clock64() - cyc0);  // down compute, SM cycles (slot 59)
+        if (lane == 0) a.x_out[16 * c + warp] = acc + xm_row;
     } else {
         // no down rows here: drain this CTA's own shared-expert chunk copies (none issued)
     }

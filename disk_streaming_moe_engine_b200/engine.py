@@ -108,7 +108,8 @@ class Engine:
         self._ok(self.lib.dm_trace_read(self.ctx, _ptr(out), n))
         return out
 
-    TRACE_KINDS = ["embed", "gdn_in", "gdn_rec", "gdn_out", "attn_in", "attn", "attn_out", "moe", "head"]
+    TRACE_KINDS = ["embed", "gdn_in", "gdn_rec", "gdn_out", "attn_in", "attn", "attn_out", "moe", "head",
+                   "gdn_core_out"]
 
     def trace_timeline(self, n: int = 512):
         """[(kind, layer, start_ns, ready_ns, end_ns)] of the last traced decode step."""

@@ -301,7 +301,8 @@ int32_t dm_kernels_per_step(dm_ctx* ctx, int32_t* out);
  * launch time, bytes = the algorithmic HBM bytes one launch must move (weights, state, KV). */
 #define DM_KERNEL_MIXER_IN 0   /* GDN or attention input projection GEMV (+RMSNorm)     */
 #define DM_KERNEL_MIXER_OUT 1  /* output projection GEMV (+head norm / gate, residual)  */
-#define DM_KERNEL_MIXER_CORE 2 /* GDN recurrence or paged decode attention              */
+#define DM_KERNEL_MIXER_CORE 2 /* paged decode attention; GDN recurrence (fused with the
+                                  output projection when the step runs them as one)    */
 #define DM_KERNEL_ROUTER 3     /* router + top-k alone (the dm_router kernel)           */
 #define DM_KERNEL_MOE 4        /* the whole MoE mixer: router, experts, residual        */
 #define DM_KERNEL_HEAD 6
@@ -314,7 +315,10 @@ int32_t dm_time_kernel(dm_ctx* ctx, int32_t which, int32_t layer, int32_t iters,
  * start, ready, pages done, cluster merged, end, SM id); slots 0-7 decode attention (start, page loads issued, inputs ready,
  * q/k ready, pages done, cluster merged, counted in, output), slots 16-24 the MoE kernel
  * of CTA 0 (start, inputs ready, normalised, router rows done, router complete, ids known,
- * experts up done, barrier passed, done) and 26-34 the same for the last CTA.  Turning
+ * experts up done, barrier passed, done) and 26-34 the same for the last CTA; 36-39 the
+ * top-k steps of CTA 0, 40-55 decode attention per page (pages 0-3: waited, scores,
+ * softmax, P V), 56-58 the MoE down phase of CTA 0 (h staged, chunks waited, computed),
+ * 59 / 60 SM cycles of the MoE down-phase arithmetic / top-k rounds, 1024.. 8 per MoE CTA.  Turning
  * tracing on or off drops captured decode graphs (they are recaptured on next use). */
 int32_t dm_trace_enable(dm_ctx* ctx, int32_t on);
 int32_t dm_trace_read(dm_ctx* ctx, uint64_t* stamps_host, int32_t n);
