@@ -685,7 +685,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                     my_id = lane == r ? (oob ? r : bi) : my_id;
                     my_p = lane == r ? (oob ? 0u : mb) : my_p;
                 }
-                if (lane == 0 && tr) tr[44] = static_cast<uint64_t>(clock64() - tk0);  // rounds, SM cycles (slot 60)
+                if (lane == 0 && tr && c == 0) tr[44] = static_cast<uint64_t>(clock64() - tk0);  // rounds, SM cycles (slot 60)
             } else {
                 // E > 256: experts beyond 32*PL per lane live in shared memory (taken = -2);
                 // each round every lane offers its best untaken one
@@ -878,10 +878,11 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             }
         }
         __syncthreads();
-        trace_stamp(tr ? tr + 40 : nullptr, 0);  // down-phase detail of CTA 0 (slots 56..58)
-        bool ok = true;
-        for (int j = 0; j < nexp; ++j) ok &= mbar_wait_bounded(&bar_dn[j], 0, a.err, nullptr);
-        trace_stamp(tr ? tr + 40 : nullptr, 1);
+        uint64_t* td = (tr && c == 0) ? tr + 40 : nullptr;  // down-phase detail of CTA 0 (slots 56..59)
+        trace_stamp(td, 0);
+        const bool okl = lane < nexp ? mbar_wait_bounded(&bar_dn[lane], 0, a.err, nullptr) : true;
+        const bool ok = __all_sync(0xffffffffu, okl);  // lane j waited for expert j's chunk
+        trace_stamp(td, 1);
         const long long cyc0 = clock64();
         const int gl = (lane * WPL) / G;  // this lane's scale group
         const float4* h4v = reinterpret_cast<const float4*>(h4);
@@ -925,8 +926,8 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             if (j + 1 < nexp) acc1 += expert_part(j + 1);
         }
         const float acc = warp_sum(ok ? acc0 + acc1 : 0.0f);
-        trace_stamp(tr ? tr + 40 : nullptr, 2);
-        if (tr) tr[43] = static_cast<uint64_t>(clock64() - cyc0);  // down compute, SM cycles (slot 59)
+        trace_stamp(td, 2);
+        if (td) td[3] = static_cast<uint64_t>(clock64() - cyc0);  // down compute, SM cycles (slot 59)
         if (lane == 0) a.x_out[16 * c + warp] = acc + xm_row;
     } else {
         // no down rows here: drain this CTA's own shared-expert chunk copies (none issued)
