@@ -103,6 +103,12 @@ SIGNATURES = {
     "dm_synth_f16_absnormal": (I32, [U64, U64, U64, F32, P]),
     "dm_synth_model_device": (I32, [P, U64]),
     "dm_moe_layer_noalloc": (I32, [I32, I32, I32, I32, F32, P, P, P, P, P, P, P, P, P, C.c_char_p, U64]),
+    "dm_batch_capacity": (I32, [P, C.POINTER(I32)]),
+    "dm_decode_batch": (I32, [P, P, P, I32, P, P]),
+    "dm_generate_batch": (I32, [P, P, P, I32, I32, P]),
+    "dm_enqueue_decode_batch": (I32, [P, P, P, I32, I32]),
+    "dm_batch_read_generated": (I32, [P, I32, I32, P]),
+    "dm_batch_kernels_per_step": (I32, [P, I32, C.POINTER(I32), C.POINTER(I32)]),
 }
 
 _LIB = None

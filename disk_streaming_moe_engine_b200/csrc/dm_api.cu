@@ -5,6 +5,7 @@
 // kernels are issued on the context stream with programmatic dependent launch; the decode
 // step (embedding, all blocks, head) is captured once per sequence slot into a CUDA graph
 // and replayed per token.
+#include <cublas_v2.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -76,6 +77,14 @@ struct dm_ctx {
     std::vector<int> att_len;          // [n_att * max_seqs]
     std::vector<int> dev_pos_valid;    // device pos[slot] == slot_len[slot]
     std::vector<cudaGraphExec_t> graphs;  // decode step per slot
+    // batched decode: scratch, the GEMM library handle on the context stream (workspace in
+    // the arena, so capture into a graph allocates nothing), one graph per (rows, logits)
+    BatchBuffers bb{};
+    cublasHandle_t blas = nullptr;
+    void* blas_ws = nullptr;
+    size_t blas_ws_bytes = 0;
+    std::vector<cudaGraphExec_t> bgraphs;  // [2 * (cap + 1)]
+    int* h_bio = nullptr;                  // pinned [4 * kMaxBatch]: slots, tokens in, tokens out
     bool use_pdl = true;       // programmatic dependent launch between step kernels
     bool gdn_fused = true;     // GDN recurrence + output projection as one kernel
     bool l2_prefetch = false;  // latency-bound kernels prefetch upcoming weights into L2 (off:
@@ -269,6 +278,27 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t o_rope = T(static_cast<size_t>(d.max_pages) * kPageTokens * (d.rot_dim / 2) * 8);
     const size_t o_sq = T(static_cast<size_t>(d.I) * H / 2), o_ss = T(static_cast<size_t>(d.I) * H / d.G * 2),
                  o_sz = T(static_cast<size_t>(d.I) * H / d.G / 2 + 16);
+    // batched decode scratch
+    const size_t BC = static_cast<size_t>(std::min(d.max_seqs, kMaxBatch));
+    const size_t kmax = std::max({static_cast<size_t>(d.H), static_cast<size_t>(d.z_dim), static_cast<size_t>(d.Hq) * d.D});
+    const size_t nmax = std::max({static_cast<size_t>(d.gdn_in_rows), static_cast<size_t>(d.attn_in_rows),
+                                  static_cast<size_t>(d.H), static_cast<size_t>(d.V)});
+    const size_t P = BC * (d.topk + 1);
+    const int max_segs = static_cast<int>((P + kSegTok - 1) / kSegTok) + std::min(d.E, static_cast<int>(BC) * d.topk) + 2;
+    const int bgen_cap = 1 << 16;
+    const size_t ob_slots = T(BC * 4), ob_tok = T(BC * 4), ob_x = T(BC * H * 4), ob_xm = T(BC * H * 4);
+    const size_t ob_xcat = T(2 * BC * kmax * 2), ob_c = T(2 * BC * nmax * 4);
+    const size_t ob_z = T(BC * d.z_dim * 4), ob_ab = T(BC * 2 * d.nv * 4), ob_o = T(BC * d.z_dim * 4);
+    const size_t ob_qg = T(BC * 2 * d.Hq * d.D * 4), ob_kvn = T(BC * 2 * d.Hkv * d.D * 4);
+    const size_t ob_part = T(BC * d.Hq * kMaxSplits * (d.D + 2) * 4), ob_aout = T(BC * d.Hq * d.D * 4);
+    const size_t ob_acnt = T(BC * d.Hkv * 4), ob_xn = T(BC * H * 4), ob_lg = T(BC * (d.E + 1) * 4);
+    const size_t ob_ids = T(BC * d.topk * 4), ob_pr = T(BC * d.topk * 4), ob_sg = T(BC * 4);
+    const size_t ob_segs = T(static_cast<size_t>(max_segs) * 16), ob_work = T(16);
+    const size_t ob_ptok = T(P * 4), ob_pof = T(P * 4), ob_h = T(P * d.I * 4), ob_epart = T(P * H * 4);
+    const size_t ob_cv = T(BC * kHeadChunks * 4), ob_ci = T(BC * kHeadChunks * 4), ob_hl = T(BC * d.V * 4);
+    const size_t ob_gen = T(static_cast<size_t>(bgen_cap) * 4), ob_genidx = T(4);
+    const size_t blas_ws = static_cast<size_t>(32) << 20;
+    const size_t ob_ws = T(blas_ws);
     c->arena_bytes = p.off;
     if (!commit) return DM_OK;
 
@@ -339,6 +369,42 @@ static int plan_memory(dm_ctx* c, bool commit) {
     c->stage_q = A + o_sq;
     c->stage_s = reinterpret_cast<uint16_t*>(A + o_ss);
     c->stage_z = A + o_sz;
+    BatchBuffers& bb = c->bb;
+    bb.cap = static_cast<int>(BC);
+    bb.max_segs = max_segs;
+    bb.slots = reinterpret_cast<int*>(A + ob_slots);
+    bb.tok = reinterpret_cast<int*>(A + ob_tok);
+    bb.x = reinterpret_cast<float*>(A + ob_x);
+    bb.xm = reinterpret_cast<float*>(A + ob_xm);
+    bb.xcat = reinterpret_cast<uint16_t*>(A + ob_xcat);
+    bb.c = reinterpret_cast<float*>(A + ob_c);
+    bb.z = reinterpret_cast<float*>(A + ob_z);
+    bb.ab = reinterpret_cast<float*>(A + ob_ab);
+    bb.o = reinterpret_cast<float*>(A + ob_o);
+    bb.qg = reinterpret_cast<float*>(A + ob_qg);
+    bb.kvnew = reinterpret_cast<float*>(A + ob_kvn);
+    bb.attn_part = reinterpret_cast<float*>(A + ob_part);
+    bb.attn_out = reinterpret_cast<float*>(A + ob_aout);
+    bb.attn_cnt = reinterpret_cast<unsigned*>(A + ob_acnt);
+    bb.xn = reinterpret_cast<float*>(A + ob_xn);
+    bb.logits = reinterpret_cast<float*>(A + ob_lg);
+    bb.ids = reinterpret_cast<int*>(A + ob_ids);
+    bb.probs = reinterpret_cast<float*>(A + ob_pr);
+    bb.sg = reinterpret_cast<float*>(A + ob_sg);
+    bb.segs = reinterpret_cast<int4*>(A + ob_segs);
+    bb.work = reinterpret_cast<int*>(A + ob_work);
+    bb.pair_tok = reinterpret_cast<int*>(A + ob_ptok);
+    bb.pair_of = reinterpret_cast<int*>(A + ob_pof);
+    bb.h = reinterpret_cast<float*>(A + ob_h);
+    bb.part = reinterpret_cast<float*>(A + ob_epart);
+    bb.cand_val = reinterpret_cast<float*>(A + ob_cv);
+    bb.cand_idx = reinterpret_cast<int*>(A + ob_ci);
+    bb.head_logits = reinterpret_cast<float*>(A + ob_hl);
+    bb.gen_out = reinterpret_cast<int*>(A + ob_gen);
+    bb.gen_idx = reinterpret_cast<int*>(A + ob_genidx);
+    bb.gen_cap = bgen_cap;
+    c->blas_ws = A + ob_ws;
+    c->blas_ws_bytes = blas_ws;
     return DM_OK;
 }
 
@@ -438,6 +504,7 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     // function attributes are per process: always the kernel's fixed maximum, never a
     // per-context value that a later, smaller context would lower
     if (e == cudaSuccess) e = attn_set_attrs(kAttnMaxScoreSmem);
+    if (e == cudaSuccess) e = batch_set_attrs();
     if (e != cudaSuccess) {
         fprintf(stderr, "dm_ctx_create: %s\n", cudaGetErrorString(e));
         delete c;
@@ -459,13 +526,31 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     if (e == cudaSuccess)
         e = launch_rope_table(c->stream, c->b.rope, c->d.max_pages * kPageTokens, c->d.rot_dim, c->d.theta);
     if (e == cudaSuccess) e = cudaMallocHost(&c->h_io, 64);
+    if (e == cudaSuccess) e = cudaMallocHost(&c->h_bio, 4 * kMaxBatch * sizeof(int));
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) {
         fprintf(stderr, "dm_ctx_create: %s\n", cudaGetErrorString(e));
+        if (c->h_io) cudaFreeHost(c->h_io);
+        if (c->h_bio) cudaFreeHost(c->h_bio);
         cudaFree(c->arena);
         delete c;
         return DM_ERR_CUDA;
     }
+    {
+        cublasStatus_t bs = cublasCreate(&c->blas);
+        if (bs == CUBLAS_STATUS_SUCCESS) bs = cublasSetStream(c->blas, c->stream);
+        if (bs == CUBLAS_STATUS_SUCCESS) bs = cublasSetWorkspace(c->blas, c->blas_ws, c->blas_ws_bytes);
+        if (bs != CUBLAS_STATUS_SUCCESS) {
+            fprintf(stderr, "dm_ctx_create: cuBLAS set-up failed (status %d)\n", static_cast<int>(bs));
+            if (c->blas) cublasDestroy(c->blas);
+            cudaFreeHost(c->h_io);
+            cudaFreeHost(c->h_bio);
+            cudaFree(c->arena);
+            delete c;
+            return DM_ERR_CUDA;
+        }
+    }
+    c->bgraphs.assign(2 * (c->bb.cap + 1), nullptr);
     c->have_dense.assign(static_cast<size_t>(c->d.L + 1) * DM_T_COUNT, 0);
     c->have_expert.assign(static_cast<size_t>(c->d.L) * (c->d.E + 1) * 3, 0);
     c->slot_len.assign(c->d.max_seqs, 0);
@@ -490,6 +575,10 @@ int32_t dm_ctx_destroy(dm_ctx* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     for (auto& g : c->graphs)
         if (g) cudaGraphExecDestroy(g);
+    for (auto& g : c->bgraphs)
+        if (g) cudaGraphExecDestroy(g);
+    if (c->blas) cublasDestroy(c->blas);
+    if (c->h_bio) cudaFreeHost(c->h_bio);
     if (c->arena) cudaFree(c->arena);
     if (c->flush_buf) cudaFree(c->flush_buf);
     if (c->h_io) cudaFreeHost(c->h_io);
@@ -1077,6 +1166,192 @@ int32_t dm_forward(dm_ctx* c, int32_t slot, const int32_t* tokens, int32_t n, fl
     rc = check_device_error(c, "decode");
     if (rc == DM_OK && next) *next = c->h_io[1];
     return rc;
+}
+
+// ---- batched decode ---------------------------------------------------------------------
+// One step of n sequences (rows): dense projections as bf16 tensor-core GEMMs of the hi/lo
+// split rows (cuBLAS, plain library GEMMs), the per-row kernels of dm_batch.cu, the GDN
+// recurrence and the attention with a row dimension, the experts on the tensor cores.
+static cudaError_t bgemm(dm_ctx* c, const uint16_t* W, int N, int K, int n) {
+    const float one = 1.0f, zero = 0.0f;
+    // C[2n][N] (row-major) = Xcat[2n][K] . W[N][K]^T, i.e. column-major C^T = W^T-op . Xcat
+    const cublasStatus_t s = cublasGemmEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, N, 2 * n, K, &one, W, CUDA_R_16BF, K,
+                                          c->bb.xcat, CUDA_R_16BF, K, &zero, c->bb.c, CUDA_R_32F, N,
+                                          CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+    return s == CUBLAS_STATUS_SUCCESS ? cudaSuccess : cudaErrorUnknown;
+}
+
+static cudaError_t enqueue_batch_step(dm_ctx* c, int n, int write_logits) {
+    const Dims& d = c->d;
+    BatchBuffers& bb = c->bb;
+    const LaunchCfg lc = lcfg(c);
+    cudaError_t e = launch_b_embed(lc, d, c->embed, bb, c->b, n);
+    for (int l = 0; l < d.L && e == cudaSuccess; ++l) {
+        const LayerW& w = c->layers[l];
+        if (w.is_attn) {
+            if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
+            if (e == cudaSuccess) e = bgemm(c, w.w_in, d.attn_in_rows, d.H, n);
+            if (e == cudaSuccess) e = launch_b_epi_attn_in(lc, d, bb, n);
+            if (e == cudaSuccess) e = launch_attn_decode_batch(lc, d, w, bb, c->b, n);
+            if (e == cudaSuccess)
+                e = launch_b_prep(lc, BPREP_COPY, bb.attn_out, d.Hq * d.D, nullptr, d.eps, nullptr, nullptr, 0, bb.xcat, n);
+            if (e == cudaSuccess) e = bgemm(c, w.w_out, d.H, d.Hq * d.D, n);
+        } else {
+            if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
+            if (e == cudaSuccess) e = bgemm(c, w.w_in, d.gdn_in_rows, d.H, n);
+            if (e == cudaSuccess) e = launch_b_epi_gdn_in(lc, d, w, bb, c->b, n);
+            if (e == cudaSuccess) e = launch_gdn_rec_batch(lc, d, w, bb, c->b, n);
+            if (e == cudaSuccess)
+                e = launch_b_prep(lc, BPREP_HEADNORM, bb.o, d.z_dim, nullptr, d.eps, bb.z, w.gdn_norm, d.dv, bb.xcat, n);
+            if (e == cudaSuccess) e = bgemm(c, w.w_out, d.H, d.z_dim, n);
+        }
+        if (e == cudaSuccess) e = launch_b_epi_resid(lc, bb.c, d.H, bb.x, bb.xm, n);
+        // MoE: canonical router, top-k + grouping, experts, weighted combine + residual
+        if (e == cudaSuccess) e = launch_b_router(lc, d, w, bb, bb.xm, 1, n);
+        if (e == cudaSuccess) e = launch_b_topk_group(lc, d, bb, c->b, n);
+        if (e == cudaSuccess) e = launch_b_experts(lc, d, w, bb, c->b, n);
+        if (e == cudaSuccess) e = launch_b_combine(lc, d, bb, bb.xm, bb.x, n);
+    }
+    if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, c->final_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
+    if (e == cudaSuccess) e = bgemm(c, c->lm_head, d.V, d.H, n);
+    if (e == cudaSuccess) e = launch_b_argmax(lc, d, bb, c->b, n, write_logits, 1);
+    return e;
+}
+
+static int ensure_bgraph(dm_ctx* c, int n, int write_logits) {
+    cudaGraphExec_t& ge = c->bgraphs[2 * n + (write_logits ? 1 : 0)];
+    if (ge) return DM_OK;
+    cudaGraph_t g = nullptr;
+    DM_CUDA(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal), "decode");
+    cudaError_t e = enqueue_batch_step(c, n, write_logits);
+    cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+    if (e != cudaSuccess || e2 != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "decode", -1, "batched graph capture failed: %s",
+                       e == cudaErrorUnknown ? "GEMM launch" : cudaGetErrorString(e != cudaSuccess ? e : e2));
+    }
+    e = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) {
+        ge = nullptr;
+        return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "decode", -1, "graph instantiate: %s", cudaGetErrorString(e));
+    }
+    return DM_OK;
+}
+
+// Batch preconditions: 1 <= n <= capacity, distinct valid slots, each slot ready to decode
+// n_steps tokens (attention layers at the slot length, room in its pages), tokens in range.
+// Stages slots and tokens on the device and brings every device position in sync.
+static int prepare_batch(dm_ctx* c, const int32_t* slots, const int32_t* tokens, int n, int n_steps) {
+    if (!c || !slots || !tokens || n_steps <= 0) return DM_ERR_INVALID_ARG;
+    if (n <= 0 || n > c->bb.cap)
+        return set_err(c, DM_ERR_INVALID_ARG, "M5_ERR_INPUT", "decode", -1, "batch of %d rows outside [1, %d]", n, c->bb.cap);
+    const Dims& d = c->d;
+    for (int i = 0; i < n; ++i) {
+        int rc = check_slot(c, slots[i]);
+        if (rc != DM_OK) return rc;
+        for (int j = 0; j < i; ++j)
+            if (slots[j] == slots[i])
+                return set_err(c, DM_ERR_INVALID_ARG, "M5_ERR_INPUT", "decode", -1, "slot %d appears twice in the batch", slots[i]);
+        if (tokens[i] < 0 || tokens[i] >= d.V)
+            return set_err(c, DM_ERR_INVALID_ARG, "M4_ERR_INPUT", "input", -1, "token %d at row %d out of range [0, %d)",
+                           tokens[i], i, d.V);
+        const int s = slots[i];
+        for (int a = 0; a < d.n_att; ++a) {
+            const int al = c->att_len[static_cast<size_t>(a) * d.max_seqs + s];
+            if (al != c->slot_len[s])
+                return set_err(c, DM_ERR_POSITION, "M5_ERR_DECODE", "decode", -1,
+                               "Position mismatch on KV append: expected current_len %d, actual_pos %d (attention layer %d)",
+                               al, c->slot_len[s], a);
+        }
+        if (c->slot_len[s] + n_steps > d.max_pages * kPageTokens)
+            return set_err(c, DM_ERR_CAPACITY, "M5_ERR_CONTEXT_SIZE", "kv_alloc", -1,
+                           "KV cache capacity exceeded on token append: current_len %d + %d > capacity %d", c->slot_len[s],
+                           n_steps, d.max_pages * kPageTokens);
+    }
+    if (static_cast<int64_t>(n) * n_steps > c->bb.gen_cap)
+        return set_err(c, DM_ERR_INVALID_ARG, "M5_ERR_INPUT", "decode", -1, "n * n_steps above %d", c->bb.gen_cap);
+    cudaSetDevice(c->device);
+    for (int i = 0; i < n; ++i) {
+        const int s = slots[i];
+        if (!c->dev_pos_valid[s]) {
+            c->h_io[3] = c->slot_len[s];
+            DM_CUDA(c, cudaMemcpyAsync(c->b.pos + s, &c->h_io[3], 4, cudaMemcpyHostToDevice, c->stream), "decode");
+            DM_CUDA(c, cudaStreamSynchronize(c->stream), "decode");
+            c->dev_pos_valid[s] = 1;
+        }
+    }
+    for (int i = 0; i < n; ++i) {
+        c->h_bio[i] = slots[i];
+        c->h_bio[kMaxBatch + i] = tokens[i];
+    }
+    DM_CUDA(c, cudaMemcpyAsync(c->bb.slots, c->h_bio, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream), "decode");
+    DM_CUDA(c, cudaMemcpyAsync(c->bb.tok, c->h_bio + kMaxBatch, sizeof(int) * n, cudaMemcpyHostToDevice, c->stream), "decode");
+    DM_CUDA(c, cudaMemsetAsync(c->bb.gen_idx, 0, 4, c->stream), "decode");
+    return DM_OK;
+}
+
+static void advance_batch(dm_ctx* c, const int32_t* slots, int n, int n_steps) {
+    for (int i = 0; i < n; ++i) advance_lens(c, slots[i], n_steps);
+}
+
+int32_t dm_batch_capacity(dm_ctx* c, int32_t* cap) {
+    if (!c || !cap) return DM_ERR_INVALID_ARG;
+    *cap = c->bb.cap;
+    return DM_OK;
+}
+
+int32_t dm_decode_batch(dm_ctx* c, const int32_t* slots, const int32_t* tokens_in, int32_t n, int32_t* tokens_out,
+                        float* logits) {
+    int rc = prepare_batch(c, slots, tokens_in, n, 1);
+    if (rc != DM_OK) return rc;
+    const int wl = logits ? 1 : 0;
+    if ((rc = ensure_bgraph(c, n, wl)) != DM_OK) return rc;
+    DM_CUDA(c, cudaGraphLaunch(c->bgraphs[2 * n + wl], c->stream), "decode");
+    DM_CUDA(c, cudaMemcpyAsync(c->h_bio + 2 * kMaxBatch, c->bb.tok, sizeof(int) * n, cudaMemcpyDeviceToHost, c->stream), "decode");
+    if (logits)
+        DM_CUDA(c, cudaMemcpyAsync(logits, c->bb.head_logits, sizeof(float) * n * c->d.V, cudaMemcpyDeviceToHost, c->stream),
+                "decode");
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "decode");
+    advance_batch(c, slots, n, 1);
+    rc = check_device_error(c, "decode");
+    if (rc == DM_OK && tokens_out)
+        for (int i = 0; i < n; ++i) tokens_out[i] = c->h_bio[2 * kMaxBatch + i];
+    return rc;
+}
+
+int32_t dm_enqueue_decode_batch(dm_ctx* c, const int32_t* slots, const int32_t* tokens_in, int32_t n, int32_t n_steps) {
+    int rc = prepare_batch(c, slots, tokens_in, n, n_steps);
+    if (rc != DM_OK) return rc;
+    if ((rc = ensure_bgraph(c, n, 0)) != DM_OK) return rc;
+    for (int i = 0; i < n_steps; ++i) DM_CUDA(c, cudaGraphLaunch(c->bgraphs[2 * n], c->stream), "decode");
+    advance_batch(c, slots, n, n_steps);
+    return DM_OK;
+}
+
+int32_t dm_batch_read_generated(dm_ctx* c, int32_t n, int32_t n_steps, int32_t* out) {
+    if (!c || !out || n <= 0 || n_steps <= 0 || static_cast<int64_t>(n) * n_steps > c->bb.gen_cap) return DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    DM_CUDA(c, cudaMemcpyAsync(out, c->bb.gen_out, sizeof(int) * n * n_steps, cudaMemcpyDeviceToHost, c->stream), "decode");
+    return check_device_error(c, "decode");
+}
+
+int32_t dm_generate_batch(dm_ctx* c, const int32_t* slots, const int32_t* tokens_in, int32_t n, int32_t n_steps,
+                          int32_t* out) {
+    if (!out) return DM_ERR_INVALID_ARG;
+    int rc = dm_enqueue_decode_batch(c, slots, tokens_in, n, n_steps);
+    if (rc != DM_OK) return rc;
+    return dm_batch_read_generated(c, n, n_steps, out);
+}
+
+int32_t dm_batch_kernels_per_step(dm_ctx* c, int32_t n, int32_t* own, int32_t* gemms) {
+    if (!c || !own || !gemms || n <= 0 || n > c->bb.cap) return DM_ERR_INVALID_ARG;
+    // embed; per block: prep, epilogue, mixer core (recurrence or attention), prep,
+    // residual epilogue, router, top-k + grouping, gate/up, down, combine; head: prep,
+    // two argmax kernels.  GEMMs: two per block and the head.
+    *own = 1 + 10 * c->d.L + 3;
+    *gemms = 2 * c->d.L + 1;
+    return DM_OK;
 }
 
 // Layer-level entry points: one token at a time, host activations in and out.

@@ -47,6 +47,12 @@ struct AttnArgs {
     const void* next_w;       // o_proj weights, prefetched into L2
     size_t next_bytes;
     uint32_t* err;
+    // batched launch (grid.z = batch rows): row b attends for sequence slots[b]; page table
+    // and pos advance by the slot, the q/k/v inputs, partials, outputs and counters by the
+    // row.  slots == nullptr: one sequence.
+    const int* slots;
+    int pt_ss, cnt_bs;
+    size_t qg_bs, kvn_bs, part_bs, out_bs;
 };
 
 // RoPE table [capacity][rot_dim / 2] of (cos, sin) of fp32(pos) * inv_freq_i with
@@ -124,8 +130,11 @@ DM_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::c
 //   merge     splits of a cluster through distributed shared memory, then the cluster
 //             partials of a head by the CTAs of the last cluster to finish, with the
 //             sigmoid output gate (reference attention.mojo:219-435 in decode form).
-template <int D, int GRP>
+// NB = pages scored per batch: kAttnStages (one sequence: every page of a split in flight at
+// once) or fewer, so that the next batch's pages load while this one is scored.
+template <int D, int GRP, int NB>
 __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+    static_assert(NB >= 1 && NB <= kAttnStages && kAttnStages % NB == 0, "batch of whole ring stages");
     using AG = AttnGeom<D>;
     static_assert(GRP <= 8, "heads of a KV group are rows 0..7 of the m16 tile");
     extern __shared__ __align__(128) uint8_t ring[];
@@ -134,7 +143,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     __shared__ __align__(16) float qsm[GRP][QST];
     constexpr int QBS = D + 8;  // bf16 q rows: 8 rows of an A fragment hit distinct banks
     __shared__ __align__(16) uint16_t qh[GRP][QBS], ql[GRP][QBS];
-    constexpr int NT = kAttnStages * kPageTokens;  // tokens of a full batch
+    constexpr int NT = NB * kPageTokens;  // tokens of a full batch
     constexpr int PBS = NT + 8;
     __shared__ __align__(16) uint16_t ph[GRP][PBS], pl[GRP][PBS];
     __shared__ __align__(16) float knew[D], vnew[D];
@@ -144,6 +153,14 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     __shared__ int last_flag;
     const int g = blockIdx.x, s = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int bz = blockIdx.z;
+    const int slot = a.slots ? a.slots[bz] : 0;  // host-written before the step
+    const float* qg_in = a.qg + bz * a.qg_bs;
+    const float* kvnew_in = a.kvnew + bz * a.kvn_bs;
+    const int* page_table = a.page_table + slot * a.pt_ss;
+    float* part_out = a.part + bz * a.part_bs;
+    float* attn_out = a.out + bz * a.out_bs;
+    unsigned* counters = a.counters + bz * a.cnt_bs;
     const int fg = lane >> 2, ft = lane & 3;  // fragment row / column-pair of this lane
 
     uint64_t* tr = (tid == 0 && g == 0 && s == gridDim.y - 1) ? a.trace : nullptr;
@@ -153,7 +170,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     kt_start(a.kt);
     // positions < pos were written by earlier steps and the page table is fixed: the
     // range of this split and its page tiles do not depend on the previous kernel
-    const int pos = *a.pos;
+    const int pos = a.pos[slot];
     const int n_tok = pos + 1;
     const int capacity = a.max_pages * kPageTokens;
     const bool in_range = pos >= 0 && pos < capacity;
@@ -165,7 +182,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     const int t0 = pg0 * kPageTokens;
     const int t1 = min(n_tok, pg1 * kPageTokens);
     __shared__ int pages[kMaxPagesPerSplit];
-    for (int i = tid; i < np && i < kMaxPagesPerSplit; i += kAT) pages[i] = a.page_table[pg0 + i];
+    for (int i = tid; i < np && i < kMaxPagesPerSplit; i += kAT) pages[i] = page_table[pg0 + i];
     if (tid == 0) {
         for (int i = 0; i < kAttnStages; ++i) mbar_init(&bar[i], 1);
         mbar_fence_init();
@@ -175,7 +192,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     // each, by the 32 lanes of warp 0 (row r < 16: K row r; r >= 16: V row r - 16)
     auto issue = [&](int i) {
         const int slot = i % kAttnStages;
-        const int page = i < kMaxPagesPerSplit ? pages[i] : a.page_table[pg0 + i];
+        const int page = i < kMaxPagesPerSplit ? pages[i] : page_table[pg0 + i];
         const bool good = page >= 0 && page < a.num_pages;
         if (lane == 0) {
             if (good) {
@@ -225,14 +242,14 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     {
         constexpr int QPT = (GRP * D + kAT - 1) / kAT, KPT = (D + kAT - 1) / kAT;
         float qv[QPT], kv[KPT], vv[KPT];
-        const float* qsrc = a.qg + static_cast<size_t>(g * GRP) * D;
+        const float* qsrc = qg_in + static_cast<size_t>(g * GRP) * D;
 #pragma unroll
         for (int i = 0; i < QPT; ++i) qv[i] = tid + kAT * i < GRP * D ? qsrc[tid + kAT * i] : 0.0f;
 #pragma unroll
         for (int i = 0; i < KPT; ++i) {
             const int d = tid + kAT * i;
-            kv[i] = d < D ? a.kvnew[static_cast<size_t>(g) * D + d] : 0.0f;
-            vv[i] = d < D ? a.kvnew[static_cast<size_t>(a.Hkv + g) * D + d] : 0.0f;
+            kv[i] = d < D ? kvnew_in[static_cast<size_t>(g) * D + d] : 0.0f;
+            vv[i] = d < D ? kvnew_in[static_cast<size_t>(a.Hkv + g) * D + d] : 0.0f;
         }
 #pragma unroll
         for (int i = 0; i < QPT; ++i)
@@ -288,7 +305,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
 
     // ---- append at pos (one CTA per KV head) ----
     if (s == 0) {
-        const int page = a.page_table[pos / kPageTokens];
+        const int page = page_table[pos / kPageTokens];
         if (page < 0 || page >= a.num_pages) {
             if (tid == 0) raise_error(a.err, DM_DEVERR_PAGE);
         } else {
@@ -309,8 +326,8 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     float oacc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
     const int ip_new = pos / kPageTokens - pg0;  // page of the split holding pos, if any
 
-    for (int b0 = 0; b0 < np; b0 += kAttnStages) {
-        const int nb = min(kAttnStages, np - b0);
+    for (int b0 = 0; b0 < np; b0 += NB) {
+        const int nb = min(NB, np - b0);
         unsigned okm = 0;
         for (int i = 0; i < nb; ++i)
             if (mbar_wait_bounded(&bar[(b0 + i) % kAttnStages], ((b0 + i) / kAttnStages) & 1, a.err, nullptr))
@@ -364,10 +381,10 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
         // softmax over the batch, one warp per head, online across batches
         const int nt = nb * kPageTokens;
         for (int hh = warp; hh < GRP; hh += kAW) {
-            float sv[NT / 32];
+            float sv[(NT + 31) / 32];
             float mp = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < NT / 32; ++j) {
+            for (int j = 0; j < (NT + 31) / 32; ++j) {
                 const int tb = lane + 32 * j;
                 sv[j] = tb < nt ? sc[hh][tb] : -INFINITY;
                 mp = fmaxf(mp, sv[j]);
@@ -377,7 +394,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
             const float mn = fmaxf(mo, mp);
             float ls = 0.0f;
 #pragma unroll
-            for (int j = 0; j < NT / 32; ++j) {
+            for (int j = 0; j < (NT + 31) / 32; ++j) {
                 const int tb = lane + 32 * j;
                 const float p = (sv[j] != -INFINITY) ? expf(sv[j] - mn) : 0.0f;
                 ls += p;
@@ -428,7 +445,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
         trace_stamp(trp, 3);
         if (warp == 0 && b0 + kAttnStages < np) {
             fence_proxy_async_smem();  // generic accesses of the stages before the next copies
-            for (int i = b0 + kAttnStages; i < np && i < b0 + 2 * kAttnStages; ++i) issue(i);
+            for (int i = b0 + kAttnStages; i < np && i < b0 + kAttnStages + nb; ++i) issue(i);
         }
     }
 
@@ -492,17 +509,17 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
             float v = 0.0f;
 #pragma unroll
             for (int r = 0; r < kAttnCluster; ++r) v = fmaf(cw[hh][r], P[r * PSZ + o], v);
-            a.part[(static_cast<size_t>(g * GRP + hh) * kMaxSplits + cid) * (D + 2) + (o % D)] = v;
+            part_out[(static_cast<size_t>(g * GRP + hh) * kMaxSplits + cid) * (D + 2) + (o % D)] = v;
         }
         if (tid < GRP) {
-            float* p = a.part + (static_cast<size_t>(g * GRP + tid) * kMaxSplits + cid) * (D + 2);
+            float* p = part_out + (static_cast<size_t>(g * GRP + tid) * kMaxSplits + cid) * (D + 2);
             p[D] = cm[tid];
             p[D + 1] = cl[tid];
         }
         __syncthreads();
         if (tid == 0) {
             __threadfence();
-            const unsigned prev = atomicAdd(a.counters + g, 1u);
+            const unsigned prev = atomicAdd(counters + g, 1u);
             const int last = prev == static_cast<unsigned>(ccount) - 1;
             if (last) __threadfence();
             for (int r = 0; r < kAttnCluster; ++r) *cluster.map_shared_rank(&last_flag, r) = last;
@@ -524,7 +541,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     for (int o = crank * kAT + tid; o < GRP * D; o += kAttnCluster * kAT) {
         const int hh = o / D, d = o % D;
         const int hq = g * GRP + hh;
-        const float* ph0 = a.part + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
+        const float* ph0 = part_out + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
         float pv[kMaxClusters], ml[kMaxClusters], ll[kMaxClusters];
 #pragma unroll
         for (int c = 0; c < kMaxClusters; ++c) {
@@ -533,7 +550,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
             ml[c] = on ? __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D) : -INFINITY;
             ll[c] = on ? __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D + 1) : 0.0f;
         }
-        const float gate = a.qg[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
+        const float gate = qg_in[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
         float M = -INFINITY;
 #pragma unroll
         for (int c = 0; c < kMaxClusters; ++c)
@@ -545,9 +562,9 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
             L = fmaf(w, ll[c], L);
             acc2 = fmaf(w, pv[c], acc2);
         }
-        a.out[static_cast<size_t>(hq) * D + d] = (L > 0.0f ? acc2 / L : 0.0f) * sigmoid_f(gate);
+        attn_out[static_cast<size_t>(hq) * D + d] = (L > 0.0f ? acc2 / L : 0.0f) * sigmoid_f(gate);
     }
-    if (tid == 0 && crank == 0) a.counters[g] = 0u;
+    if (tid == 0 && crank == 0) counters[g] = 0u;
     if (tid == 0 && crank == 0 && a.trace) a.trace[7] = globaltimer_ns();
     trace_stamp(ct, 4);
     __syncthreads();
@@ -581,60 +598,33 @@ bool attn_supported(int D, int grp) {
 }
 
 #define DM_ATTN_INSTANCES(X) X(256, 8) X(256, 4) X(128, 8) X(128, 4) X(64, 4) X(64, 8)
+constexpr int kAttnBatchNB = 3;  // pages per scored batch of the batched launch (two batches in flight)
+
+template <int D, int GRP, int NB>
+static cudaError_t attn_attr_one(int max_scores_smem) {
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, GRP, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         max_scores_smem);
+    if (e == cudaSuccess)  // largest shared-memory carve-out
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, GRP, NB>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    return e;
+}
 
 cudaError_t attn_set_attrs(int max_scores_smem) {
     cudaError_t e = cudaSuccess;
-#define DM_ATTN_ATTR(DD, GG)                                                                      \
-    if (e == cudaSuccess)                                                                         \
-        e = cudaFuncSetAttribute(attn_decode_kernel<DD, GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                 max_scores_smem);                                                \
-    if (e == cudaSuccess) /* largest shared-memory carve-out: two CTAs per SM */                    \
-        e = cudaFuncSetAttribute(attn_decode_kernel<DD, GG>,                                      \
-                                 cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+#define DM_ATTN_ATTR(DD, GG)                                                    \
+    if (e == cudaSuccess) e = attn_attr_one<DD, GG, kAttnStages>(max_scores_smem); \
+    if (e == cudaSuccess) e = attn_attr_one<DD, GG, kAttnBatchNB>(max_scores_smem);
     DM_ATTN_INSTANCES(DM_ATTN_ATTR)
 #undef DM_ATTN_ATTR
     return e;
 }
 
-cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW& w,
-                               const Buffers& b, int slot) {
-    AttnArgs a{};
-    a.qg = b.qg;
-    a.kvnew = b.kvnew;
-    a.q_norm = w.q_norm;
-    a.k_norm = w.k_norm;
-    a.kv = b.kv + static_cast<size_t>(w.sub) * d.num_pages * 2 * d.Hkv * kPageTokens * d.D;
-    a.page_table = b.page_table + static_cast<size_t>(slot) * d.max_pages;
-    a.pos = b.pos + slot;
-    a.Hq = d.Hq;
-    a.Hkv = d.Hkv;
-    a.rot_dim = d.rot_dim;
-    a.max_pages = d.max_pages;
-    a.num_pages = d.num_pages;
-    a.nsplit = attn_nsplit(lc.num_sms, d.Hkv);
-    a.cap = attn_scores_cap(d.max_pages, a.nsplit);
-    a.theta = d.theta;
-    a.eps = d.eps;
-    a.part = b.attn_part;
-    a.out = b.attn_out;
-    a.counters = b.counters + kCntAttnBase;
-    a.rope = b.rope;
-    a.trace = b.trace ? b.trace + kTrAttn : nullptr;
-    a.cta_trace = b.trace ? b.trace + kTrCta : nullptr;
-    a.kt = lc.kt;
-    a.next_w = lc.l2_prefetch ? w.w_out : nullptr;
-    a.next_bytes = static_cast<size_t>(d.H) * d.Hq * d.D * 2;
-    a.err = b.err;
+static cudaError_t attn_launch(const LaunchCfg& lc, const Dims& d, const AttnArgs& a, dim3 grid, bool batched) {
     const int grp = d.Hq / d.Hkv;
-    const dim3 grid(d.Hkv, a.nsplit);
-    if (a.cta_trace && grid.x * grid.y * kTrCtaSlots > kTraceSlots - kTrCta) a.cta_trace = nullptr;
-    const size_t smem = attn_ring_bytes(d.D);
-#define DM_ATTN_LAUNCH(DD, GG)                                                                 \
-    if (d.D == DD && grp == GG) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<DD, GG>, a);
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kAT);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = attn_ring_bytes(d.D);
     cfg.stream = lc.stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -645,9 +635,86 @@ cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW&
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
+#define DM_ATTN_LAUNCH(DD, GG)                                                                              \
+    if (d.D == DD && grp == GG)                                                                             \
+        return batched ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<DD, GG, kAttnBatchNB>, a)              \
+                       : cudaLaunchKernelEx(&cfg, attn_decode_kernel<DD, GG, kAttnStages>, a);
     DM_ATTN_INSTANCES(DM_ATTN_LAUNCH)
 #undef DM_ATTN_LAUNCH
     return cudaErrorInvalidValue;
+}
+
+static void attn_common_args(AttnArgs& a, const Dims& d, const LayerW& w, const Buffers& b) {
+    a.q_norm = w.q_norm;
+    a.k_norm = w.k_norm;
+    a.kv = b.kv + static_cast<size_t>(w.sub) * d.num_pages * 2 * d.Hkv * kPageTokens * d.D;
+    a.Hq = d.Hq;
+    a.Hkv = d.Hkv;
+    a.rot_dim = d.rot_dim;
+    a.max_pages = d.max_pages;
+    a.num_pages = d.num_pages;
+    a.theta = d.theta;
+    a.eps = d.eps;
+    a.rope = b.rope;
+    a.err = b.err;
+}
+
+cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW& w,
+                               const Buffers& b, int slot) {
+    AttnArgs a{};
+    attn_common_args(a, d, w, b);
+    a.qg = b.qg;
+    a.kvnew = b.kvnew;
+    a.page_table = b.page_table + static_cast<size_t>(slot) * d.max_pages;
+    a.pos = b.pos + slot;
+    a.nsplit = attn_nsplit(lc.num_sms, d.Hkv);
+    a.cap = attn_scores_cap(d.max_pages, a.nsplit);
+    a.part = b.attn_part;
+    a.out = b.attn_out;
+    a.counters = b.counters + kCntAttnBase;
+    a.trace = b.trace ? b.trace + kTrAttn : nullptr;
+    a.cta_trace = b.trace ? b.trace + kTrCta : nullptr;
+    a.kt = lc.kt;
+    a.next_w = lc.l2_prefetch ? w.w_out : nullptr;
+    a.next_bytes = static_cast<size_t>(d.H) * d.Hq * d.D * 2;
+    const dim3 grid(d.Hkv, a.nsplit);
+    if (a.cta_trace && grid.x * grid.y * kTrCtaSlots > kTraceSlots - kTrCta) a.cta_trace = nullptr;
+    return attn_launch(lc, d, a, grid, false);
+}
+
+// Splits per (row, KV head) of the batched launch: about two CTAs per SM over the whole
+// grid, in whole clusters.
+int attn_nsplit_batch(int num_sms, int Hkv, int n) {
+    const int units = (n > 0 ? n : 1) * (Hkv > 0 ? Hkv : 1);
+    int ns = (2 * num_sms + units - 1) / units;
+    ns = (ns + kAttnCluster - 1) / kAttnCluster * kAttnCluster;
+    if (ns > kMaxSplits) ns = kMaxSplits;
+    if (ns < kAttnCluster) ns = kAttnCluster;
+    return ns;
+}
+
+cudaError_t launch_attn_decode_batch(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                                     const Buffers& b, int n) {
+    AttnArgs a{};
+    attn_common_args(a, d, w, b);
+    a.qg = bb.qg;
+    a.kvnew = bb.kvnew;
+    a.page_table = b.page_table;
+    a.pos = b.pos;
+    a.nsplit = attn_nsplit_batch(lc.num_sms, d.Hkv, n);
+    a.cap = attn_scores_cap(d.max_pages, a.nsplit);
+    a.part = bb.attn_part;
+    a.out = bb.attn_out;
+    a.counters = bb.attn_cnt;
+    a.kt = lc.kt;
+    a.slots = bb.slots;
+    a.pt_ss = d.max_pages;
+    a.cnt_bs = d.Hkv;
+    a.qg_bs = static_cast<size_t>(2) * d.Hq * d.D;
+    a.kvn_bs = static_cast<size_t>(2) * d.Hkv * d.D;
+    a.part_bs = static_cast<size_t>(d.Hq) * kMaxSplits * (d.D + 2);
+    a.out_bs = static_cast<size_t>(d.Hq) * d.D;
+    return attn_launch(lc, d, a, dim3(d.Hkv, a.nsplit, n), true);
 }
 
 }  // namespace dm

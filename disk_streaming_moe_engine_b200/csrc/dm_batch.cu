@@ -1,0 +1,580 @@
+// dm_batch.cu — the batched decode step's small kernels (sm_100a): embedding, the
+// operand preparation and epilogues around the dense projections, the canonical batched
+// router, top-k + expert grouping, the MoE combine and the vocabulary argmax.
+//
+// Dense projections of a batch of n rows run as one tensor-core GEMM each (bf16 in, fp32
+// accumulate).  To keep fp32 activations, every activation row x is split into two bf16
+// rows, hi = bf16(x) and lo = bf16(x - hi) (|x - hi - lo| <= 2^-16 |x|), stacked as rows
+// b and n + b of the GEMM operand; the epilogue adds the two result rows.  The weights
+// are bf16 in the model, so the only rounding left is fp32 accumulation.
+//
+// Semantics per row are those of the single-token kernels (reference rmsnorm.mojo:10,
+// gdn.mojo:897-1183 for the GDN projections and head norm, attention.mojo:219-435 for the
+// attention projections, router.mojo:15-185 + topk.mojo:11-131 for routing, moe.mojo:105
+// for the weighted combine, cmd_decode.mojo:115 for the first-maximum argmax).
+#include <cuda_fp16.h>
+
+#include "dm_common.cuh"
+#include "dm_kernels.h"
+#include "dm_router.cuh"
+
+namespace dm {
+
+// ---- embedding -----------------------------------------------------------------------
+__global__ void __launch_bounds__(256) b_embed_kernel(const uint16_t* __restrict__ embed, int H, int V,
+                                                      const int* tok, float* x, uint32_t* err) {
+    const int b = blockIdx.y;
+    pdl_wait();
+    int t = tok[b];
+    if (t < 0 || t >= V) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(err, DM_DEVERR_TOKEN);
+        t = 0;
+    }
+    pdl_launch_dependents();
+    const uint16_t* row = embed + static_cast<size_t>(t) * H;
+    float* xo = x + static_cast<size_t>(b) * H;
+    for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < H; k += gridDim.x * blockDim.x) xo[k] = bf16_to_f32(row[k]);
+}
+
+cudaError_t launch_b_embed(const LaunchCfg& lc, const Dims& d, const uint16_t* embed, const BatchBuffers& bb,
+                           const Buffers& b, int n) {
+    const int blocks = (d.H + 255) / 256;
+    return launch_kernel(lc, b_embed_kernel, dim3(blocks, n), dim3(256), 0, embed, d.H, d.V, bb.tok, bb.x, b.err);
+}
+
+// ---- GEMM operand: hi / lo bf16 rows --------------------------------------------------
+struct BPrepArgs {
+    const float* x;        // [n][K] (head norm: o)
+    const uint16_t* gamma; // RMSNorm weight [K] / head-norm weight [dv]
+    const float* z;        // head norm: SiLU(z) [n][K]
+    float eps;
+    int K, dv, n;
+    uint16_t* xcat;        // [2n][K]
+};
+
+DM_DEV void split_store(uint16_t* xcat, int n, int K, int b, int k, float y) {
+    const uint16_t hi = f32_to_bf16(y);
+    xcat[static_cast<size_t>(b) * K + k] = hi;
+    xcat[static_cast<size_t>(n + b) * K + k] = f32_to_bf16(y - bf16_to_f32(hi));
+}
+
+constexpr int kPrepThreads = 256;
+
+// One CTA per row.  RMS: y = x / sqrt(mean(x^2) + eps) * gamma; HEADNORM: per head of dv
+// values y = o * rsqrt(mean_head(o^2) + eps) * w * z; COPY: y = x.
+template <int MODE>
+__global__ void __launch_bounds__(kPrepThreads) b_prep_kernel(const __grid_constant__ BPrepArgs a) {
+    const int b = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    pdl_wait();
+    const float* x = a.x + static_cast<size_t>(b) * a.K;
+    if (MODE == BPREP_RMS) {
+        __shared__ float red[kPrepThreads / 32];
+        float acc = 0.0f;
+        for (int k = tid; k < a.K; k += kPrepThreads) acc = fmaf(x[k], x[k], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) red[warp] = acc;
+        __syncthreads();
+        float ss = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kPrepThreads / 32; ++w) ss += red[w];
+        const float rs = 1.0f / sqrtf(ss / static_cast<float>(a.K) + a.eps);
+        pdl_launch_dependents();
+        for (int k = tid; k < a.K; k += kPrepThreads) split_store(a.xcat, a.n, a.K, b, k, x[k] * rs * bf16_to_f32(a.gamma[k]));
+    } else if (MODE == BPREP_HEADNORM) {
+        const float* z = a.z + static_cast<size_t>(b) * a.K;
+        const int nh = a.K / a.dv;
+        pdl_launch_dependents();
+        for (int h = warp; h < nh; h += kPrepThreads / 32) {
+            const float* oh = x + h * a.dv;
+            float acc = 0.0f;
+            for (int dd = lane; dd < a.dv; dd += 32) acc = fmaf(oh[dd], oh[dd], acc);
+            acc = warp_sum(acc);
+            const float rs = 1.0f / sqrtf(acc / static_cast<float>(a.dv) + a.eps);
+            for (int dd = lane; dd < a.dv; dd += 32)
+                split_store(a.xcat, a.n, a.K, b, h * a.dv + dd, oh[dd] * rs * bf16_to_f32(a.gamma[dd]) * z[h * a.dv + dd]);
+        }
+    } else {
+        pdl_launch_dependents();
+        for (int k = tid; k < a.K; k += kPrepThreads) split_store(a.xcat, a.n, a.K, b, k, x[k]);
+    }
+}
+
+cudaError_t launch_b_prep(const LaunchCfg& lc, int mode, const float* x, int K, const uint16_t* gamma, float eps,
+                          const float* z, const uint16_t* hw, int dv, uint16_t* xcat, int n) {
+    BPrepArgs a{};
+    a.x = x;
+    a.gamma = mode == BPREP_HEADNORM ? hw : gamma;
+    a.z = z;
+    a.eps = eps;
+    a.K = K;
+    a.dv = dv;
+    a.n = n;
+    a.xcat = xcat;
+    if (mode == BPREP_RMS) return launch_kernel(lc, b_prep_kernel<BPREP_RMS>, dim3(n), dim3(kPrepThreads), 0, a);
+    if (mode == BPREP_HEADNORM) return launch_kernel(lc, b_prep_kernel<BPREP_HEADNORM>, dim3(n), dim3(kPrepThreads), 0, a);
+    return launch_kernel(lc, b_prep_kernel<BPREP_COPY>, dim3(n), dim3(kPrepThreads), 0, a);
+}
+
+// ---- GEMM epilogues: v = C[b][col] + C[n + b][col] -------------------------------------
+struct BEpiArgs {
+    const float* c;    // [2n][N]
+    int N, n;
+    // GDN input projection: [qkv | z | a b] -> conv ring slot pos % 4, SiLU(z), a b
+    float* ring;       // layer base [max_seqs][4][qkv_dim]
+    const int* slots;
+    const int* pos;
+    int qkv_dim, z_dim;
+    float* z;          // [n][z_dim]
+    float* ab;         // [n][2 nv]
+    // attention input projection: [q gate | k v]
+    float* qg;         // [n][2 Hq D]
+    float* kvnew;      // [n][2 Hkv D]
+    int qg_rows;
+    // residual: out[b][col] = v + res[b][col]
+    const float* res;
+    float* out;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(256) b_epi_kernel(const __grid_constant__ BEpiArgs a) {
+    const int b = blockIdx.y;
+    const int col = blockIdx.x * 256 + threadIdx.x;
+    pdl_wait();
+    pdl_launch_dependents();
+    if (col >= a.N) return;
+    const float v = a.c[static_cast<size_t>(b) * a.N + col] + a.c[static_cast<size_t>(a.n + b) * a.N + col];
+    if (MODE == BEPI_GDN_IN) {
+        if (col < a.qkv_dim) {
+            const int slot = a.slots[b];
+            const int p = a.pos[slot];
+            a.ring[(static_cast<size_t>(slot) * kConvRing + (p & 3)) * a.qkv_dim + col] = v;
+        } else if (col < a.qkv_dim + a.z_dim) {
+            a.z[static_cast<size_t>(b) * a.z_dim + (col - a.qkv_dim)] = silu_f(v);
+        } else {
+            const int nab = a.N - a.qkv_dim - a.z_dim;
+            a.ab[static_cast<size_t>(b) * nab + (col - a.qkv_dim - a.z_dim)] = v;
+        }
+    } else if (MODE == BEPI_ATTN_IN) {
+        if (col < a.qg_rows) a.qg[static_cast<size_t>(b) * a.qg_rows + col] = v;
+        else a.kvnew[static_cast<size_t>(b) * (a.N - a.qg_rows) + (col - a.qg_rows)] = v;
+    } else {
+        a.out[static_cast<size_t>(b) * a.N + col] = v + a.res[static_cast<size_t>(b) * a.N + col];
+    }
+}
+
+cudaError_t launch_b_epi_gdn_in(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                                const Buffers& b, int n) {
+    BEpiArgs a{};
+    a.c = bb.c;
+    a.N = d.gdn_in_rows;
+    a.n = n;
+    a.ring = b.ring + static_cast<size_t>(w.sub) * d.max_seqs * kConvRing * d.qkv_dim;
+    a.slots = bb.slots;
+    a.pos = b.pos;
+    a.qkv_dim = d.qkv_dim;
+    a.z_dim = d.z_dim;
+    a.z = bb.z;
+    a.ab = bb.ab;
+    return launch_kernel(lc, b_epi_kernel<BEPI_GDN_IN>, dim3((a.N + 255) / 256, n), dim3(256), 0, a);
+}
+
+cudaError_t launch_b_epi_attn_in(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, int n) {
+    BEpiArgs a{};
+    a.c = bb.c;
+    a.N = d.attn_in_rows;
+    a.n = n;
+    a.qg = bb.qg;
+    a.kvnew = bb.kvnew;
+    a.qg_rows = 2 * d.Hq * d.D;
+    return launch_kernel(lc, b_epi_kernel<BEPI_ATTN_IN>, dim3((a.N + 255) / 256, n), dim3(256), 0, a);
+}
+
+cudaError_t launch_b_epi_resid(const LaunchCfg& lc, const float* c, int N, const float* res, float* out, int n) {
+    BEpiArgs a{};
+    a.c = c;
+    a.N = N;
+    a.n = n;
+    a.res = res;
+    a.out = out;
+    return launch_kernel(lc, b_epi_kernel<BEPI_RESID>, dim3((N + 255) / 256, n), dim3(256), 0, a);
+}
+
+// ---- batched router (canonical arithmetic, bit-identical logits to the one-token router)
+// Grid (ceil((E+1)/16), ceil(n/kBRTok)), 512 threads: warp w owns router row 16 bx + w
+// (weights in registers before griddepcontrol.wait); the CTA normalises its kBRTok rows
+// one after another into shared memory (split layout), then every warp dots its row with
+// each of them.  CTAs of row block 0 also write the normalised rows (the experts' input).
+constexpr int kBRThreads = 512;
+constexpr int kBRTok = 8;
+
+struct BRouterArgs {
+    const uint16_t* W;      // [E+1][K]
+    int E, n;
+    const float* x;         // [n][K]
+    const uint16_t* gamma;  // nullptr: x is already normalised
+    float eps;
+    float* xn;              // [n][K]
+    float* logits;          // [n][E+1]
+};
+
+template <int K>
+__global__ void __launch_bounds__(kBRThreads, 1) b_router_kernel(const __grid_constant__ BRouterArgs a) {
+    constexpr int VPL = K / 256;
+    extern __shared__ __align__(16) float xs_all[];  // [kBRTok][K]
+    __shared__ float red[kBRThreads / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int row = blockIdx.x * (kBRThreads / 32) + warp;
+    const int b0 = blockIdx.y * kBRTok;
+    const int nt = min(kBRTok, a.n - b0);
+    uint4 wreg[VPL];
+    if (row <= a.E) {
+        const uint4* wr = reinterpret_cast<const uint4*>(a.W + static_cast<size_t>(row) * K);
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) wreg[i] = ldg_nc_v4(wr + lane + 32 * i);
+    }
+    pdl_wait();
+    for (int t = 0; t < nt; ++t) {
+        float* xs = xs_all + static_cast<size_t>(t) * K;
+        const float* x = a.x + static_cast<size_t>(b0 + t) * K;
+        float* xn = blockIdx.x == 0 ? a.xn + static_cast<size_t>(b0 + t) * K : nullptr;
+        if (a.gamma) {
+            canon_rmsnorm_split<K, kBRThreads>(x, a.gamma, a.eps, xs, xn, red);
+        } else {
+            for (int k = tid; k < K; k += kBRThreads) {
+                const float v = x[k];
+                xs_store_split(xs, K, k, v);
+                if (xn) xn[k] = v;
+            }
+        }
+        __syncthreads();  // xs complete; red free for the next row
+    }
+    pdl_launch_dependents();
+    if (row > a.E) return;
+    for (int t = 0; t < nt; ++t) {
+        const float* xs = xs_all + static_cast<size_t>(t) * K;
+        const float acc = canon_router_dot<VPL>(wreg, reinterpret_cast<const float4*>(xs),
+                                                reinterpret_cast<const float4*>(xs + K / 2), lane);
+        if (lane == 0) a.logits[static_cast<size_t>(b0 + t) * (a.E + 1) + row] = acc;
+    }
+}
+
+cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                            const float* x, int normalise, int n) {
+    BRouterArgs a{};
+    a.W = w.w_router;
+    a.E = d.E;
+    a.n = n;
+    a.x = x;
+    a.gamma = normalise ? w.post_norm : nullptr;
+    a.eps = d.eps;
+    a.xn = bb.xn;
+    a.logits = bb.logits;
+    const dim3 grid((d.E + 1 + kBRThreads / 32 - 1) / (kBRThreads / 32), (n + kBRTok - 1) / kBRTok);
+    const size_t smem = static_cast<size_t>(kBRTok) * d.H * 4;
+    switch (d.H) {
+        case 256: return launch_kernel(lc, b_router_kernel<256>, grid, dim3(kBRThreads), smem, a);
+        case 512: return launch_kernel(lc, b_router_kernel<512>, grid, dim3(kBRThreads), smem, a);
+        case 1024: return launch_kernel(lc, b_router_kernel<1024>, grid, dim3(kBRThreads), smem, a);
+        case 2048: return launch_kernel(lc, b_router_kernel<2048>, grid, dim3(kBRThreads), smem, a);
+        case 4096: return launch_kernel(lc, b_router_kernel<4096>, grid, dim3(kBRThreads), smem, a);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// ---- top-k per row + grouping of the (expert, row) pairs by expert ---------------------
+// One CTA of 1024 threads.  Warp w selects for rows w, w + 32 (canonical softmax/top-k).
+// Then the pairs are grouped by expert in a fixed order: expert ascending (the shared
+// expert, id E, last), rows ascending within an expert (64-bit row masks make the rank of
+// a pair a population count).  Each expert's rows are cut into segments of kSegTok.
+struct BGroupArgs {
+    const float* logits;  // [n][E+1]
+    int E, topk, n, max_segs;
+    int* ids;
+    float* probs;
+    float* sg;
+    int4* segs;
+    int* work;            // [0] segments, [1] [2] work counters (reset here)
+    int* pair_tok;
+    int* pair_of;         // [n][topk+1]
+    uint32_t* err;
+};
+
+constexpr int kBGThreads = 1024;
+
+// Exclusive prefix sum of v over the 1024 threads (fixed order); *total gets the sum.
+DM_DEV int block_excl_scan(int v, int* wsum, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int s = wsum[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, s, o);
+            if (lane >= o) s += t;
+        }
+        wsum[lane] = s;  // inclusive over warps
+    }
+    __syncthreads();
+    const int base = warp > 0 ? wsum[warp - 1] : 0;
+    if (total) *total = wsum[31];
+    return base + incl - v;
+}
+
+__global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __grid_constant__ BGroupArgs a) {
+    extern __shared__ __align__(16) float lgw[];   // [32][E+1]
+    __shared__ unsigned long long mask[1024];       // per expert (E <= 1023) + shared
+    __shared__ int sids[kMaxBatch * kMaxTopK];
+    __shared__ int start[1024];
+    __shared__ int wsum[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int E = a.E, topk = a.topk, n = a.n;
+    pdl_wait();
+    for (int b = warp; b < n; b += 32) {
+        float* lg = lgw + static_cast<size_t>(warp) * (E + 1);
+        const float* src = a.logits + static_cast<size_t>(b) * (E + 1);
+        for (int e = lane; e <= E; e += 32) lg[e] = src[e];
+        __syncwarp();
+        canon_softmax_topk_warp(lg, E, topk, a.ids + b * topk, a.probs + b * topk, a.sg + b, a.err);
+        if (lane < topk) sids[b * topk + lane] = a.ids[b * topk + lane];
+        __syncwarp();
+    }
+    for (int e = tid; e <= E; e += kBGThreads) mask[e] = 0ull;
+    __syncthreads();
+    pdl_launch_dependents();
+    for (int i = tid; i < n * topk; i += kBGThreads) {
+        const int e = sids[i];
+        atomicOr(&mask[e], 1ull << (i / topk));
+    }
+    if (tid == 0) mask[E] = n >= 64 ? ~0ull : ((1ull << n) - 1ull);
+    __syncthreads();
+    const int e = tid;
+    const int cnt = e <= E ? __popcll(mask[e]) : 0;
+    const int nsg = (cnt + kSegTok - 1) / kSegTok;
+    int total_pairs = 0, total_segs = 0;
+    const int p0 = block_excl_scan(cnt, wsum, &total_pairs);
+    __syncthreads();
+    const int s0 = block_excl_scan(nsg, wsum, &total_segs);
+    if (e <= E) {
+        start[e] = p0;
+        unsigned long long m = mask[e];
+        int j = 0;
+        while (m) {
+            const int b = __ffsll(static_cast<long long>(m)) - 1;
+            m &= m - 1ull;
+            a.pair_tok[p0 + j] = b;
+            ++j;
+        }
+        for (int s = 0; s < nsg; ++s)
+            if (s0 + s < a.max_segs) a.segs[s0 + s] = make_int4(e, p0 + s * kSegTok, min(kSegTok, cnt - s * kSegTok), 0);
+    }
+    __syncthreads();
+    for (int i = tid; i < n * topk; i += kBGThreads) {
+        const int b = i / topk, k = i % topk;
+        const int ex = sids[i];
+        const unsigned long long below = b == 0 ? 0ull : (mask[ex] & (~0ull >> (64 - b)));
+        a.pair_of[b * (topk + 1) + k] = start[ex] + __popcll(below);
+    }
+    for (int b = tid; b < n; b += kBGThreads) a.pair_of[b * (topk + 1) + topk] = start[E] + b;
+    if (tid == 0) {
+        if (total_segs > a.max_segs) raise_error(a.err, DM_DEVERR_CAPACITY);
+        a.work[0] = min(total_segs, a.max_segs);
+        a.work[1] = 0;
+        a.work[2] = 0;
+    }
+}
+
+cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n) {
+    BGroupArgs a{};
+    a.logits = bb.logits;
+    a.E = d.E;
+    a.topk = d.topk;
+    a.n = n;
+    a.max_segs = bb.max_segs;
+    a.ids = bb.ids;
+    a.probs = bb.probs;
+    a.sg = bb.sg;
+    a.segs = bb.segs;
+    a.work = bb.work;
+    a.pair_tok = bb.pair_tok;
+    a.pair_of = bb.pair_of;
+    a.err = b.err;
+    const size_t smem = static_cast<size_t>(32) * (d.E + 1) * 4;
+    return launch_kernel(lc, b_topk_group_kernel, dim3(1), dim3(kBGThreads), smem, a);
+}
+
+// ---- combine: out[b] = xm[b] + sum_k p_k part[pair(b,k)] + g_sh part[pair(b,shared)] -----
+struct BCombineArgs {
+    const float* xm;
+    const float* part;
+    const int* pair_of;
+    const float* probs;
+    const float* sg;
+    float* out;
+    int H, topk;
+};
+
+__global__ void __launch_bounds__(256) b_combine_kernel(const __grid_constant__ BCombineArgs a) {
+    const int b = blockIdx.y;
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    pdl_wait();
+    pdl_launch_dependents();
+    if (i >= a.H) return;
+    const int* po = a.pair_of + b * (a.topk + 1);
+    float acc = 0.0f;
+    for (int k = 0; k < a.topk; ++k)
+        acc = fmaf(a.probs[b * a.topk + k], a.part[static_cast<size_t>(po[k]) * a.H + i], acc);
+    acc = fmaf(a.sg[b], a.part[static_cast<size_t>(po[a.topk]) * a.H + i], acc);
+    a.out[static_cast<size_t>(b) * a.H + i] = a.xm[static_cast<size_t>(b) * a.H + i] + acc;
+}
+
+cudaError_t launch_b_combine(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const float* xm, float* out,
+                             int n) {
+    BCombineArgs a{};
+    a.xm = xm;
+    a.part = bb.part;
+    a.pair_of = bb.pair_of;
+    a.probs = bb.probs;
+    a.sg = bb.sg;
+    a.out = out;
+    a.H = d.H;
+    a.topk = d.topk;
+    return launch_kernel(lc, b_combine_kernel, dim3((d.H + 255) / 256, n), dim3(256), 0, a);
+}
+
+// ---- vocabulary argmax: first maximum wins ----------------------------------------------
+struct BArgmaxArgs {
+    const float* c;       // [2n][V]
+    int V, n;
+    float* cand_val;      // [n][kHeadChunks]
+    int* cand_idx;
+    float* logits_out;    // [n][V] or null
+    int* tok;             // [n]
+    const int* slots;
+    int* pos;             // [max_seqs], advanced by one per row
+    int* token;           // [max_seqs]
+    int* gen_out;         // [gen_cap] or null
+    int* gen_idx;
+    int gen_cap;
+    uint32_t* err;
+};
+
+DM_DEV void argmax_merge(float& bv, int& bi, float ov, int oi) {
+    if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+    }
+}
+
+__global__ void __launch_bounds__(256) b_argmax_partial_kernel(const __grid_constant__ BArgmaxArgs a) {
+    const int b = blockIdx.y, ch = blockIdx.x;
+    const int per = (a.V + kHeadChunks - 1) / kHeadChunks;
+    const int v0 = ch * per, v1 = min(a.V, v0 + per);
+    pdl_wait();
+    pdl_launch_dependents();
+    const float* hi = a.c + static_cast<size_t>(b) * a.V;
+    const float* lo = a.c + static_cast<size_t>(a.n + b) * a.V;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    bool bad = false;
+    for (int v = v0 + threadIdx.x; v < v1; v += 256) {
+        const float x = hi[v] + lo[v];
+        if (x != x) bad = true;
+        if (a.logits_out) a.logits_out[static_cast<size_t>(b) * a.V + v] = x;
+        argmax_merge(bv, bi, x, v);
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1)
+        argmax_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, m), __shfl_xor_sync(0xffffffffu, bi, m));
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    if (bad) raise_error(a.err, DM_DEVERR_NONFINITE);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w) argmax_merge(bv, bi, sv[w], si[w]);
+        a.cand_val[b * kHeadChunks + ch] = bv;
+        a.cand_idx[b * kHeadChunks + ch] = bi;
+    }
+}
+
+__global__ void __launch_bounds__(1024) b_argmax_final_kernel(const __grid_constant__ BArgmaxArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int step = a.gen_out ? *a.gen_idx : 0;
+    for (int b = warp; b < a.n; b += 32) {
+        float bv = lane < kHeadChunks ? a.cand_val[b * kHeadChunks + lane] : -INFINITY;
+        int bi = lane < kHeadChunks ? a.cand_idx[b * kHeadChunks + lane] : 0x7fffffff;
+#pragma unroll
+        for (int m = 16; m >= 1; m >>= 1)
+            argmax_merge(bv, bi, __shfl_xor_sync(0xffffffffu, bv, m), __shfl_xor_sync(0xffffffffu, bi, m));
+        if (lane == 0) {
+            if (bi < 0 || bi >= a.V) {  // every logit NaN
+                raise_error(a.err, DM_DEVERR_NONFINITE);
+                bi = 0;
+            }
+            const int slot = a.slots[b];
+            a.tok[b] = bi;
+            a.token[slot] = bi;
+            a.pos[slot] += 1;
+            if (a.gen_out && (step + 1) * a.n <= a.gen_cap) a.gen_out[step * a.n + b] = bi;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && a.gen_out) *a.gen_idx = step + 1;
+}
+
+cudaError_t launch_b_argmax(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n,
+                            int write_logits, int record_gen) {
+    BArgmaxArgs a{};
+    a.c = bb.c;
+    a.V = d.V;
+    a.n = n;
+    a.cand_val = bb.cand_val;
+    a.cand_idx = bb.cand_idx;
+    a.logits_out = write_logits ? bb.head_logits : nullptr;
+    a.tok = bb.tok;
+    a.slots = bb.slots;
+    a.pos = b.pos;
+    a.token = b.token;
+    a.gen_out = record_gen ? bb.gen_out : nullptr;
+    a.gen_idx = bb.gen_idx;
+    a.gen_cap = bb.gen_cap;
+    a.err = b.err;
+    cudaError_t e = launch_kernel(lc, b_argmax_partial_kernel, dim3(kHeadChunks, n), dim3(256), 0, a);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(lc, b_argmax_final_kernel, dim3(1), dim3(1024), 0, a);
+}
+
+cudaError_t b_experts_set_attrs();
+
+cudaError_t batch_set_attrs() {
+    cudaError_t e = cudaSuccess;
+#define DM_BR_ATTR(KK)                                                                                      \
+    if (e == cudaSuccess)                                                                                   \
+        e = cudaFuncSetAttribute(b_router_kernel<KK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBRTok * KK * 4);
+    DM_BR_ATTR(256)
+    DM_BR_ATTR(512)
+    DM_BR_ATTR(1024)
+    DM_BR_ATTR(2048)
+    DM_BR_ATTR(4096)
+#undef DM_BR_ATTR
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(b_topk_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 32 * 1024 * 4);
+    if (e == cudaSuccess) e = b_experts_set_attrs();
+    return e;
+}
+
+}  // namespace dm

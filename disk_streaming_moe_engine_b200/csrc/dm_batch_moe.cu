@@ -1,0 +1,333 @@
+// dm_batch_moe.cu — routed + shared experts of the batched decode step on the tensor
+// cores (sm_100a, mma.sync m16n8k16 bf16 -> fp32), dequantising the asymmetric 4-bit
+// format in registers.
+//
+// Work: the (expert, row) pairs of a layer are grouped by expert into segments of at
+// most kSegTok rows (one n8 tile).  An item is a segment and 16 consecutive 16-row chunks
+// of the projection; the CTA (16 warps, one chunk each) stages the segment's activations
+// in shared memory and every warp streams its chunk: A = the 16 weight rows, B = the
+// activation rows, so the weights are read once per segment straight from HBM with
+// 8 groups of loads in flight per thread.
+//
+// Exact dequantisation.  Within a group of 64 columns every weight is s * (q - z) with one
+// fp16 scale s and one 4-bit zero z (reference quant_format.md:831-854, low nibble first).
+// A nibble q is turned into the bf16 number 128 + q by OR-ing it into the bits of 128.0
+// (bf16 has 7 mantissa bits, so 128..255 are exact); subtracting 128 + z in packed bf16
+// gives q - z exactly.  The tensor cores therefore multiply exact integers by the
+// activation, split as x = hi + lo (two bf16 terms, |x - hi - lo| <= 2^-16 |x|), and the
+// group's partial sum is scaled by s in fp32.  The columns a lane supplies to one MMA
+// are a permutation of the group's columns (8 nibbles of one 32-bit word feed two MMAs);
+// the activations are staged in the same permuted order, which leaves every dot product
+// unchanged.
+//
+// gate/up (K = H): chunk c holds gate rows 8c..8c+7 then up rows 8c..8c+7, so the lane
+//   holding C[g][*] also holds the matching up row C[g+8][*]: h = SiLU(gate) * up
+//   (reference swiglu.mojo:52) is formed in registers and stored per pair.
+// down (K = I): chunk c holds output rows 16c..16c+15 -> part[pair][row].
+#include <cuda_fp16.h>
+
+#include "dm_common.cuh"
+#include "dm_kernels.h"
+
+namespace dm {
+
+constexpr int kXThreads = 512;
+constexpr int kXWarps = kXThreads / 32;
+
+struct BExpArgs {
+    const uint8_t* experts;   // [E] records
+    const uint8_t* shared;    // shared-expert record
+    int64_t expert_bytes;
+    int64_t proj_off;         // offset of this projection inside a record
+    int64_t chunk_bytes;
+    int E, n_chunks;
+    const int4* segs;         // (expert, first pair, rows, 0)
+    int* work;                // [0] segments; [slot] work counter of this launch
+    int work_slot;
+    const int* pair_tok;      // pair -> batch row (gate/up input rows)
+    const float* act;         // gate/up: xn [n][K]; down: h [pairs][K]
+    int act_by_pair;
+    float* out;               // gate/up: h [pairs][I]; down: part [pairs][H]
+    int out_ld;
+};
+
+DM_DEV void mma_bf16_m16n8k16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                              uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// (q_j, q_{j+4}) of a word of 8 nibbles as bf16 (128 + q) pairs, minus the zero pair.
+DM_DEV uint32_t nib_pair_minus(uint32_t w, int shift, uint32_t zpair) {
+    const uint32_t p = ((w >> shift) & 0x000F000Fu) | 0x43004300u;
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(p), "r"(zpair));
+    return d;
+}
+
+DM_DEV uint2 ldg_nc_v2(const void* p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+DM_DEV uint32_t ldg_nc_u16(const void* p) {
+    unsigned short r;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return r;
+}
+DM_DEV uint4 lds128(const void* p) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(smem_u32(p)));
+    return r;
+}
+
+// Staged order of a 16-column run: [0,4,1,5,2,6,3,7, 8,12,9,13,10,14,11,15], so that
+// 32-bit word m holds the columns (j, j + 4) that MMA m/2 takes from lane ft (see above).
+template <int K>
+struct XGeom {
+    static constexpr int NG = K / 64;                  // groups of a row
+    static constexpr int PD = NG < 8 ? NG : 8;         // groups of loads in flight
+    static constexpr int ROWB = K * 2 + 16;            // bytes of a staged activation row
+    static constexpr int S_OFF = 16 * K / 2;           // scales [16][NG] fp16
+    static constexpr int Z_OFF = S_OFF + 16 * NG * 2;  // zeros [16][NG/2] bytes
+    static constexpr int ZB = NG / 2;                  // zero bytes per row
+    static constexpr int ZW = (ZB + 3) / 4;            // ... as 32-bit words
+    static constexpr size_t SMEM = 2 * kSegTok * ROWB;
+    static_assert(K % 128 == 0, "whole zero bytes per row");
+};
+
+template <int K>
+DM_DEV void load_zero_words(const uint8_t* zrow, uint32_t (&zw)[XGeom<K>::ZW]) {
+    using XG = XGeom<K>;
+    if (XG::ZB >= 4) {
+#pragma unroll
+        for (int i = 0; i < XG::ZW; ++i) zw[i] = __ldg(reinterpret_cast<const uint32_t*>(zrow) + i);
+    } else {
+        uint32_t v = 0;
+#pragma unroll
+        for (int i = 0; i < XG::ZB; ++i) v |= static_cast<uint32_t>(__ldg(zrow + i)) << (8 * i);
+        zw[0] = v;
+    }
+}
+
+template <int K, bool GATEUP>
+__global__ void __launch_bounds__(kXThreads, 1) b_expert_kernel(const __grid_constant__ BExpArgs a) {
+    using XG = XGeom<K>;
+    extern __shared__ __align__(16) uint8_t xsm[];  // hi rows [kSegTok][ROWB], then lo rows
+    __shared__ int s_item;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int fg = lane >> 2, ft = lane & 3;
+    const int ips = (a.n_chunks + kXWarps - 1) / kXWarps;  // items per segment
+    pdl_wait();
+    const int nitems = a.work[0] * ips;
+    pdl_launch_dependents();
+    uint8_t* xhi = xsm;
+    uint8_t* xlo = xsm + kSegTok * XG::ROWB;
+
+    while (true) {
+        if (tid == 0) s_item = atomicAdd(a.work + a.work_slot, 1);
+        __syncthreads();
+        const int item = s_item;
+        if (item >= nitems) break;
+        const int4 sg = a.segs[item / ips];
+        const int part = item % ips;
+        const int ex = sg.x, pair0 = sg.y, ntok = sg.z;
+
+        // ---- stage the segment's activation rows: 16 columns per task ----
+        for (int t = tid; t < kSegTok * (K / 16); t += kXThreads) {
+            const int r = t / (K / 16), c16 = t % (K / 16);
+            float v[16];
+            if (r < ntok) {
+                const int src_row = a.act_by_pair ? pair0 + r : a.pair_tok[pair0 + r];
+                const float4* src = reinterpret_cast<const float4*>(a.act + static_cast<size_t>(src_row) * K + 16 * c16);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float4 f = src[i];
+                    v[4 * i] = f.x;
+                    v[4 * i + 1] = f.y;
+                    v[4 * i + 2] = f.z;
+                    v[4 * i + 3] = f.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+            }
+            // word m of the staged run = (x[j], x[j + 4]), j = (m & 3) + 8 (m >> 2)
+            uint32_t hw[8], lw[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const int j = (m & 3) + 8 * (m >> 2);
+                const uint16_t h0 = f32_to_bf16(v[j]), h1 = f32_to_bf16(v[j + 4]);
+                const uint16_t l0 = f32_to_bf16(v[j] - bf16_to_f32(h0)), l1 = f32_to_bf16(v[j + 4] - bf16_to_f32(h1));
+                hw[m] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
+                lw[m] = static_cast<uint32_t>(l0) | (static_cast<uint32_t>(l1) << 16);
+            }
+            uint4* dh = reinterpret_cast<uint4*>(xhi + r * XG::ROWB + 32 * c16);
+            uint4* dl = reinterpret_cast<uint4*>(xlo + r * XG::ROWB + 32 * c16);
+            dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+        }
+        __syncthreads();
+
+        const int c = part * kXWarps + warp;
+        if (c < a.n_chunks) {
+            const uint8_t* rec = ex < a.E ? a.experts + static_cast<int64_t>(ex) * a.expert_bytes : a.shared;
+            const uint8_t* ch = rec + a.proj_off + static_cast<int64_t>(c) * a.chunk_bytes;
+            const uint8_t* q0 = ch + fg * (K / 2) + 8 * ft;
+            const uint8_t* q1 = ch + (fg + 8) * (K / 2) + 8 * ft;
+            const uint16_t* s0 = reinterpret_cast<const uint16_t*>(ch + XG::S_OFF) + fg * XG::NG;
+            const uint16_t* s1 = reinterpret_cast<const uint16_t*>(ch + XG::S_OFF) + (fg + 8) * XG::NG;
+            uint2 qa[XG::PD], qb[XG::PD];
+            uint32_t sa[XG::PD], sb[XG::PD];
+#pragma unroll
+            for (int i = 0; i < XG::PD; ++i) {
+                qa[i] = ldg_nc_v2(q0 + 32 * i);
+                qb[i] = ldg_nc_v2(q1 + 32 * i);
+                sa[i] = ldg_nc_u16(s0 + i);
+                sb[i] = ldg_nc_u16(s1 + i);
+            }
+            uint32_t za[XG::ZW], zb[XG::ZW];
+            load_zero_words<K>(ch + XG::Z_OFF + fg * XG::ZB, za);
+            load_zero_words<K>(ch + XG::Z_OFF + (fg + 8) * XG::ZB, zb);
+            const uint8_t* bh = xhi + fg * XG::ROWB + 32 * ft;
+            const uint8_t* bl = xlo + fg * XG::ROWB + 32 * ft;
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int g0 = 0; g0 < XG::NG; g0 += XG::PD) {
+#pragma unroll
+                for (int u = 0; u < XG::PD; ++u) {
+                    const int g = g0 + u;
+                    const uint2 wa = qa[u], wb = qb[u];
+                    const float sca = __half2float(__ushort_as_half(static_cast<unsigned short>(sa[u])));
+                    const float scb = __half2float(__ushort_as_half(static_cast<unsigned short>(sb[u])));
+                    if (g + XG::PD < XG::NG) {
+                        qa[u] = ldg_nc_v2(q0 + 32 * (g + XG::PD));
+                        qb[u] = ldg_nc_v2(q1 + 32 * (g + XG::PD));
+                        sa[u] = ldg_nc_u16(s0 + g + XG::PD);
+                        sb[u] = ldg_nc_u16(s1 + g + XG::PD);
+                    }
+                    const uint32_t zqa = (za[g >> 3] >> (4 * (g & 7))) & 15u;
+                    const uint32_t zqb = (zb[g >> 3] >> (4 * (g & 7))) & 15u;
+                    const uint32_t zpa = 0x43004300u | zqa | (zqa << 16);
+                    const uint32_t zpb = 0x43004300u | zqb | (zqb << 16);
+                    const uint4 h0 = lds128(bh + 128 * g), h1 = lds128(bh + 128 * g + 16);
+                    const uint4 l0 = lds128(bl + 128 * g), l1 = lds128(bl + 128 * g + 16);
+                    float ch_[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cl_[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    // MMA 0..3: word x (shifts 0/4, 8/12) then word y
+                    {
+                        const uint32_t a0 = nib_pair_minus(wa.x, 0, zpa), a1 = nib_pair_minus(wb.x, 0, zpb);
+                        const uint32_t a2 = nib_pair_minus(wa.x, 4, zpa), a3 = nib_pair_minus(wb.x, 4, zpb);
+                        mma_bf16_m16n8k16(ch_, a0, a1, a2, a3, h0.x, h0.y);
+                        mma_bf16_m16n8k16(cl_, a0, a1, a2, a3, l0.x, l0.y);
+                    }
+                    {
+                        const uint32_t a0 = nib_pair_minus(wa.x, 8, zpa), a1 = nib_pair_minus(wb.x, 8, zpb);
+                        const uint32_t a2 = nib_pair_minus(wa.x, 12, zpa), a3 = nib_pair_minus(wb.x, 12, zpb);
+                        mma_bf16_m16n8k16(ch_, a0, a1, a2, a3, h0.z, h0.w);
+                        mma_bf16_m16n8k16(cl_, a0, a1, a2, a3, l0.z, l0.w);
+                    }
+                    {
+                        const uint32_t a0 = nib_pair_minus(wa.y, 0, zpa), a1 = nib_pair_minus(wb.y, 0, zpb);
+                        const uint32_t a2 = nib_pair_minus(wa.y, 4, zpa), a3 = nib_pair_minus(wb.y, 4, zpb);
+                        mma_bf16_m16n8k16(ch_, a0, a1, a2, a3, h1.x, h1.y);
+                        mma_bf16_m16n8k16(cl_, a0, a1, a2, a3, l1.x, l1.y);
+                    }
+                    {
+                        const uint32_t a0 = nib_pair_minus(wa.y, 8, zpa), a1 = nib_pair_minus(wb.y, 8, zpb);
+                        const uint32_t a2 = nib_pair_minus(wa.y, 12, zpa), a3 = nib_pair_minus(wb.y, 12, zpb);
+                        mma_bf16_m16n8k16(ch_, a0, a1, a2, a3, h1.z, h1.w);
+                        mma_bf16_m16n8k16(cl_, a0, a1, a2, a3, l1.z, l1.w);
+                    }
+                    acc[0] = fmaf(sca, ch_[0] + cl_[0], acc[0]);
+                    acc[1] = fmaf(sca, ch_[1] + cl_[1], acc[1]);
+                    acc[2] = fmaf(scb, ch_[2] + cl_[2], acc[2]);
+                    acc[3] = fmaf(scb, ch_[3] + cl_[3], acc[3]);
+                }
+            }
+            // C rows fg / fg + 8, columns (rows of the segment) 2 ft, 2 ft + 1
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int t = 2 * ft + e;
+                if (t < ntok) {
+                    float* dst = a.out + static_cast<size_t>(pair0 + t) * a.out_ld;
+                    if (GATEUP) {
+                        dst[8 * c + fg] = silu_f(acc[e]) * acc[2 + e];
+                    } else {
+                        dst[16 * c + fg] = acc[e];
+                        dst[16 * c + fg + 8] = acc[2 + e];
+                    }
+                }
+            }
+        }
+        __syncthreads();  // staged rows free; s_item read by every thread
+    }
+}
+
+#define DM_XK_INSTANCES(X) X(128) X(256) X(512) X(1024) X(2048) X(4096)
+
+cudaError_t b_experts_set_attrs() {
+    cudaError_t e = cudaSuccess;
+#define DM_XK_ATTR(KK)                                                                                        \
+    if (e == cudaSuccess)                                                                                     \
+        e = cudaFuncSetAttribute(b_expert_kernel<KK, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,       \
+                                 static_cast<int>(XGeom<KK>::SMEM));                                          \
+    if (e == cudaSuccess)                                                                                     \
+        e = cudaFuncSetAttribute(b_expert_kernel<KK, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                                 static_cast<int>(XGeom<KK>::SMEM));
+    DM_XK_INSTANCES(DM_XK_ATTR)
+#undef DM_XK_ATTR
+    return e;
+}
+
+static cudaError_t launch_expert_proj(const LaunchCfg& lc, int K, bool gateup, const BExpArgs& a) {
+    const dim3 grid(lc.num_sms), block(kXThreads);
+#define DM_XK_LAUNCH(KK)                                                                                      \
+    if (K == KK)                                                                                              \
+        return gateup ? launch_kernel(lc, b_expert_kernel<KK, true>, grid, block, XGeom<KK>::SMEM, a)          \
+                      : launch_kernel(lc, b_expert_kernel<KK, false>, grid, block, XGeom<KK>::SMEM, a);
+    DM_XK_INSTANCES(DM_XK_LAUNCH)
+#undef DM_XK_LAUNCH
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                             const Buffers& b, int n) {
+    (void)b;
+    (void)n;
+    BExpArgs a{};
+    a.experts = w.experts;
+    a.shared = w.shared;
+    a.expert_bytes = d.expert_bytes;
+    a.E = d.E;
+    a.segs = bb.segs;
+    a.work = bb.work;
+    a.pair_tok = bb.pair_tok;
+    // gate/up: K = H, chunks of 8 gate + 8 up rows
+    a.proj_off = 0;
+    a.chunk_bytes = d.gu_chunk_bytes;
+    a.n_chunks = d.gu_chunks;
+    a.work_slot = 1;
+    a.act = bb.xn;
+    a.act_by_pair = 0;
+    a.out = bb.h;
+    a.out_ld = d.I;
+    cudaError_t e = launch_expert_proj(lc, d.H, true, a);
+    if (e != cudaSuccess) return e;
+    // down: K = I, chunks of 16 output rows
+    a.proj_off = static_cast<int64_t>(d.gu_chunks) * d.gu_chunk_bytes;
+    a.chunk_bytes = d.d_chunk_bytes;
+    a.n_chunks = d.d_chunks;
+    a.work_slot = 2;
+    a.act = bb.h;
+    a.act_by_pair = 1;
+    a.out = bb.part;
+    a.out_ld = d.H;
+    return launch_expert_proj(lc, d.I, false, a);
+}
+
+}  // namespace dm

@@ -34,6 +34,11 @@ struct GdnRecArgs {
     const void* next_w;     // out_proj weights, prefetched into L2
     size_t next_bytes;
     uint64_t* kt;
+    // batched launch (grid.z = batch rows): row b works on sequence slots[b]; ring, S and
+    // pos advance by the slot, ab and o by the row.  slots == nullptr: one sequence.
+    const int* slots;
+    size_t ring_ss, S_ss;
+    int ab_bs, o_bs;
 };
 
 __device__ __forceinline__ float softplus_ref(float v) {
@@ -51,12 +56,17 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
     const int h = blockIdx.x, rb = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g_qk = h / (a.nv / a.nk);
+    const int bz = blockIdx.z;
+    const int slot = a.slots ? a.slots[bz] : 0;  // host-written before the step
+    const float* ring = a.ring + slot * a.ring_ss;
+    const float* ab = a.ab + bz * a.ab_bs;
+    float* o_out = a.o + bz * a.o_bs;
 
     kt_start(a.kt);
     prefetch_l2_share(a.next_w, a.next_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y,
                       threadIdx.x);
     // ---- prologue: this CTA's state rows (4 per warp) into registers ----
-    float* Sh = a.S + static_cast<size_t>(h) * DV * DK;
+    float* Sh = a.S + slot * a.S_ss + static_cast<size_t>(h) * DV * DK;
     float srow[4][CPL];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -73,8 +83,8 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
     const float alog = a.a_log[h], dtb = a.dt_bias[h];  // weights: before the wait
     pdl_wait();
     kt_ready(a.kt);
-    const int pos = *a.pos;
-    const float av = a.ab[h], bv = a.ab[a.nv + h];
+    const int pos = a.pos[slot];
+    const float av = ab[h], bv = ab[a.nv + h];
 
     // ---- causal conv + SiLU for q (DK), k (DK) and this CTA's 16 v channels ----
     const int q0 = g_qk * DK, k0 = a.nk * DK + g_qk * DK, v0 = 2 * a.nk * DK + h * DV + rb * RB;
@@ -85,7 +95,7 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int tp = pos - 3 + j;
-            if (tp >= 0) acc += bf16_to_f32(w[j]) * a.ring[static_cast<size_t>(tp & 3) * a.qkv_dim + ch];
+            if (tp >= 0) acc += bf16_to_f32(w[j]) * ring[static_cast<size_t>(tp & 3) * a.qkv_dim + ch];
         }
         const float u = silu_f(acc);
         if (t < DK) qs[t] = u;
@@ -137,7 +147,7 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
 #pragma unroll
             for (int c = 0; c < CPL; ++c) dst[c] = srow[i][c];
         }
-        if (lane == 0) a.o[h * DV + r] = oacc;
+        if (lane == 0) o_out[h * DV + r] = oacc;
     }
     if (a.kt) {
         __syncthreads();
@@ -165,6 +175,34 @@ cudaError_t launch_gdn_rec(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.next_bytes = static_cast<size_t>(d.H) * d.z_dim * 2;
     a.kt = lc.kt;
     const dim3 grid(d.nv, d.dv / 16);
+    if (d.dk == 128) return launch_kernel(lc, gdn_rec_kernel<128>, grid, dim3(128), 0, a);
+    if (d.dk == 64) return launch_kernel(lc, gdn_rec_kernel<64>, grid, dim3(128), 0, a);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gdn_rec_batch(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                                 const Buffers& b, int n) {
+    GdnRecArgs a{};
+    const size_t ls = static_cast<size_t>(w.sub) * d.max_seqs;
+    a.ring = b.ring + ls * kConvRing * d.qkv_dim;
+    a.conv_w = w.conv_w;
+    a.S = b.S + ls * static_cast<size_t>(d.nv) * d.dv * d.dk;
+    a.a_log = w.a_log;
+    a.dt_bias = w.dt_bias;
+    a.ab = bb.ab;
+    a.o = bb.o;
+    a.pos = b.pos;
+    a.nk = d.nk;
+    a.nv = d.nv;
+    a.qkv_dim = d.qkv_dim;
+    a.eps = d.eps;
+    a.kt = lc.kt;
+    a.slots = bb.slots;
+    a.ring_ss = static_cast<size_t>(kConvRing) * d.qkv_dim;
+    a.S_ss = static_cast<size_t>(d.nv) * d.dv * d.dk;
+    a.ab_bs = 2 * d.nv;
+    a.o_bs = d.z_dim;
+    const dim3 grid(d.nv, d.dv / 16, n);
     if (d.dk == 128) return launch_kernel(lc, gdn_rec_kernel<128>, grid, dim3(128), 0, a);
     if (d.dk == 64) return launch_kernel(lc, gdn_rec_kernel<64>, grid, dim3(128), 0, a);
     return cudaErrorInvalidValue;

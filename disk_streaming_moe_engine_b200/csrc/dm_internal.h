@@ -105,6 +105,48 @@ struct Buffers {
     uint64_t* ktrace;     // [kMaxTraceKernels][4] per-launch timeline records, or null
 };
 
+// Scratch of the batched decode step: `n` sequences (n <= cap <= kMaxBatch), batch row b
+// decodes one token of sequence slot slots[b].  Per-sequence state (GDN state, conv ring,
+// KV pages, page table, position) stays in Buffers, indexed by the slot.
+constexpr int kMaxBatch = 64;       // token masks of the expert grouping are 64-bit
+constexpr int kSegTok = 8;          // tokens of one expert segment (one n8 MMA tile)
+constexpr int kHeadChunks = 32;     // vocabulary chunks of the batched argmax
+struct BatchBuffers {
+    int cap = 0;
+    int max_segs = 0;
+    int* slots;           // [cap] sequence slot of batch row b
+    int* tok;             // [cap] input token of row b, replaced by its argmax
+    float* x;             // [cap][H] residual stream (block input / output)
+    float* xm;            // [cap][H] after the token mixer
+    uint16_t* xcat;       // [2 cap][Kmax] bf16 GEMM operand: rows 0..n-1 = hi, n..2n-1 = lo
+    float* c;             // [2 cap][Nmax] fp32 GEMM result (same row split)
+    float* z;             // [cap][z_dim]
+    float* ab;            // [cap][2 nv]
+    float* o;             // [cap][z_dim]
+    float* qg;            // [cap][2 Hq D]
+    float* kvnew;         // [cap][2 Hkv D]
+    float* attn_part;     // [cap][Hq][kMaxSplits][D + 2]
+    float* attn_out;      // [cap][Hq D]
+    unsigned* attn_cnt;   // [cap][Hkv] last-CTA counters of the batched attention
+    float* xn;            // [cap][H] normalised MoE input (canonical RMSNorm)
+    float* logits;        // [cap][E + 1] router logits + shared gate logit
+    int* ids;             // [cap][topk]
+    float* probs;         // [cap][topk]
+    float* sg;            // [cap] shared-expert gate
+    int4* segs;           // [max_segs] (expert, first pair, tokens, 0); expert E = shared
+    int* work;            // [4] segments, gate/up work counter, down work counter, spare
+    int* pair_tok;        // [cap (topk + 1)] batch row of each (expert, token) pair
+    int* pair_of;         // [cap][topk + 1] pair index of row b's k-th expert (k = topk: shared)
+    float* h;             // [cap (topk + 1)][I] SwiGLU activations per pair
+    float* part;          // [cap (topk + 1)][H] expert outputs per pair
+    float* cand_val;      // [cap][kHeadChunks]
+    int* cand_idx;        // [cap][kHeadChunks]
+    float* head_logits;   // [cap][V] logits (written when requested)
+    int* gen_out;         // [gen_cap] tokens of a device loop, [step][n]
+    int* gen_idx;         // [1] step counter of the device loop
+    int gen_cap = 0;
+};
+
 constexpr int kTraceSlots = 2304;
 constexpr int kTrCta = 64;        // per-CTA region: decode attention, 6 slots per CTA
 constexpr int kTrCtaSlots = 6;    // start, ready, pages done, cluster merged, end, SM id
@@ -168,4 +210,35 @@ cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w
 cudaError_t launch_head(const LaunchCfg& lc, const Dims& d, const uint16_t* final_norm,
                         const uint16_t* lm_head, const Buffers& b, int slot, int advance,
                         int record_gen);
+
+// ---- batched decode step (dm_batch.cu, dm_batch_moe.cu and the batched variants of the
+// GDN recurrence and the attention).  n = batch rows of this step.
+enum BPrepMode { BPREP_RMS = 0, BPREP_HEADNORM = 1, BPREP_COPY = 2 };
+enum BEpiMode { BEPI_GDN_IN = 0, BEPI_ATTN_IN = 1, BEPI_RESID = 2 };
+cudaError_t launch_b_embed(const LaunchCfg& lc, const Dims& d, const uint16_t* embed, const BatchBuffers& bb,
+                           const Buffers& b, int n);
+// xcat rows from x [n][K]: RMSNorm with gamma, head norm (o = x, z, w), or a copy
+cudaError_t launch_b_prep(const LaunchCfg& lc, int mode, const float* x, int K, const uint16_t* gamma, float eps,
+                          const float* z, const uint16_t* hw, int dv, uint16_t* xcat, int n);
+cudaError_t launch_b_epi_gdn_in(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                                const Buffers& b, int n);
+cudaError_t launch_b_epi_attn_in(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, int n);
+cudaError_t launch_b_epi_resid(const LaunchCfg& lc, const float* c, int N, const float* res, float* out, int n);
+cudaError_t launch_gdn_rec_batch(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                                 const Buffers& b, int n);
+cudaError_t launch_attn_decode_batch(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                                     const Buffers& b, int n);
+int attn_nsplit_batch(int num_sms, int Hkv, int n);
+// MoE of one layer for n rows: router (canonical), top-k + grouping, experts, combine.
+cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                            const float* x, int normalise, int n);
+cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b,
+                                int n);
+cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                             const Buffers& b, int n);
+cudaError_t launch_b_combine(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const float* xm, float* out,
+                             int n);
+cudaError_t launch_b_argmax(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n,
+                            int write_logits, int record_gen);
+cudaError_t batch_set_attrs();
 }  // namespace dm

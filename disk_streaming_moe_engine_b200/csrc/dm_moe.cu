@@ -23,6 +23,7 @@
 #include "dismoen_detmath.h"
 #include "dm_common.cuh"
 #include "dm_kernels.h"
+#include "dm_router.cuh"
 
 namespace dm {
 
@@ -41,11 +42,6 @@ struct RouterArgs {
 
 constexpr int kRouterCluster = 16;   // CTAs of the router cluster (non-portable size)
 constexpr int kRouterThreads = 512;
-
-__device__ __forceinline__ void xs_store_split(float* xs, int K, int k, float v) {
-    int j = k >> 3, e = k & 7;
-    xs[(e < 4 ? 0 : K / 2) + j * 4 + (e & 3)] = v;
-}
 
 // Router as one thread-block cluster.  CTA r of the cluster owns rows r*R .. r*R+R-1 of
 // [W_router; w_shared_gate] (R = ceil((E+1)/16)), holds their weights in registers from
@@ -83,27 +79,7 @@ __global__ void __launch_bounds__(kRouterThreads, 2) router_kernel(const __grid_
     }
     pdl_wait();
     if (a.gamma) {
-        float xv[(K + kRouterThreads - 1) / kRouterThreads];
-        float acc = 0.0f;
-#pragma unroll
-        for (int i = 0; i * kRouterThreads + tid < K; ++i) {
-            xv[i] = a.x[i * kRouterThreads + tid];
-            acc = __fmaf_rn(xv[i], xv[i], acc);
-        }
-        acc = warp_sum(acc);
-        if (lane == 0) red[warp] = acc;
-        __syncthreads();
-        float ss = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kRouterThreads / 32; ++w) ss = __fadd_rn(ss, red[w]);
-        const float denom = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), a.eps));
-#pragma unroll
-        for (int i = 0; i * kRouterThreads + tid < K; ++i) {
-            const int k = i * kRouterThreads + tid;
-            const float y = __fmul_rn(__fdiv_rn(xv[i], denom), bf16_to_f32(a.gamma[k]));
-            xs_store_split(xs, K, k, y);
-            if (rank == 0) a.xn_out[k] = y;
-        }
+        canon_rmsnorm_split<K, kRouterThreads>(a.x, a.gamma, a.eps, xs, rank == 0 ? a.xn_out : nullptr, red);
     } else {
         for (int k = tid; k < K; k += kRouterThreads) {
             const float v = a.x[k];
@@ -118,22 +94,7 @@ __global__ void __launch_bounds__(kRouterThreads, 2) router_kernel(const __grid_
     const float4* xlo = reinterpret_cast<const float4*>(xs);
     const float4* xhi = reinterpret_cast<const float4*>(xs + K / 2);
     while (row < r1) {
-        float acc = 0.0f;
-#pragma unroll
-        for (int i = 0; i < VPL; ++i) {
-            const int j = lane + 32 * i;
-            const uint4 w = wreg[i];
-            const float4 x0 = xlo[j], x1 = xhi[j];
-            acc = __fmaf_rn(bf16lo(w.x), x0.x, acc);
-            acc = __fmaf_rn(bf16hi(w.x), x0.y, acc);
-            acc = __fmaf_rn(bf16lo(w.y), x0.z, acc);
-            acc = __fmaf_rn(bf16hi(w.y), x0.w, acc);
-            acc = __fmaf_rn(bf16lo(w.z), x1.x, acc);
-            acc = __fmaf_rn(bf16hi(w.z), x1.y, acc);
-            acc = __fmaf_rn(bf16lo(w.w), x1.z, acc);
-            acc = __fmaf_rn(bf16hi(w.w), x1.w, acc);
-        }
-        acc = warp_sum(acc);
+        const float acc = canon_router_dot<VPL>(wreg, xlo, xhi, lane);
         if (lane == 0) lg0[row] = acc;
         row += kRouterThreads / 32;
         if (row < r1) {
@@ -146,48 +107,7 @@ __global__ void __launch_bounds__(kRouterThreads, 2) router_kernel(const __grid_
     if (rank != 0 || warp != 0) return;
 
     // ---- softmax + top-k in one warp of CTA 0 ----
-    const int E = a.E;
-    float m = -INFINITY;
-    for (int e = lane; e < E; e += 32) m = fmaxf(m, lg[e]);
-    m = warp_max(m);
-    float s = 0.0f;
-    float* pe = lg;  // probabilities overwrite the logits in place (shared gate at lg[E] kept)
-    for (int e = lane; e < E; e += 32) {
-        const float ev = dm_det_exp(DM_DET_SUB(lg[e], m));
-        pe[e] = ev;
-        s = DM_DET_ADD(s, ev);
-    }
-    s = warp_sum(s);
-    const float inv = DM_DET_DIV(1.0f, s);
-    for (int e = lane; e < E; e += 32) pe[e] = DM_DET_MUL(pe[e], inv);
-    __syncwarp();
-    for (int r = 0; r < a.topk; ++r) {
-        float bv = -1.0f;
-        int bi = 0x7fffffff;
-        for (int e = lane; e < E; e += 32)
-            if (pe[e] > bv) { bv = pe[e]; bi = e; }
-#pragma unroll
-        for (int mm = 16; mm >= 1; mm >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, mm);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, mm);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-        }
-        if (bi < 0 || bi >= E) {  // only when probabilities are NaN: keep ids in range
-            if (lane == 0) raise_error(a.err, DM_DEVERR_NONFINITE);
-            bi = r;
-            bv = 0.0f;
-        }
-        if (lane == 0) {
-            a.ids[r] = bi;
-            a.probs[r] = bv;
-            pe[bi] = -2.0f;
-        }
-        __syncwarp();
-    }
-    if (lane == 0) {
-        if (a.shared_g) *a.shared_g = sigmoid_f(lg[E]);
-        if (s != s || isinf(s)) raise_error(a.err, DM_DEVERR_NONFINITE);
-    }
+    canon_softmax_topk_warp(lg, a.E, a.topk, a.ids, a.probs, a.shared_g, a.err);
 }
 
 cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,

@@ -293,6 +293,42 @@ class Engine:
     def sync(self):
         self._ok(self.lib.dm_sync(self.ctx))
 
+    # ---- batched decode: row i decodes one token of sequence slots[i] ----
+    def batch_capacity(self) -> int:
+        v = C.c_int32()
+        self._ok(self.lib.dm_batch_capacity(self.ctx, C.byref(v)))
+        return v.value
+
+    def decode_batch(self, slots, tokens, want_logits: bool = False):
+        s = np.ascontiguousarray(slots, np.int32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        if s.shape != t.shape or s.ndim != 1:
+            raise ValueError("slots and tokens must be 1-D of equal length")
+        out = np.empty(s.size, np.int32)
+        logits = np.empty((s.size, self.cfg.vocab_size), np.float32) if want_logits else None
+        self._ok(self.lib.dm_decode_batch(self.ctx, _ptr(s), _ptr(t), s.size, _ptr(out),
+                                          None if logits is None else _ptr(logits)))
+        return out, logits
+
+    def generate_batch(self, slots, tokens, n_steps: int) -> np.ndarray:
+        s = np.ascontiguousarray(slots, np.int32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        if s.shape != t.shape or s.ndim != 1:
+            raise ValueError("slots and tokens must be 1-D of equal length")
+        out = np.empty((n_steps, s.size), np.int32)
+        self._ok(self.lib.dm_generate_batch(self.ctx, _ptr(s), _ptr(t), s.size, n_steps, _ptr(out)))
+        return out
+
+    def enqueue_decode_batch(self, slots, tokens, n_steps: int):
+        s = np.ascontiguousarray(slots, np.int32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        self._ok(self.lib.dm_enqueue_decode_batch(self.ctx, _ptr(s), _ptr(t), s.size, n_steps))
+
+    def batch_kernels_per_step(self, n: int) -> tuple[int, int]:
+        own, gemms = C.c_int32(), C.c_int32()
+        self._ok(self.lib.dm_batch_kernels_per_step(self.ctx, n, C.byref(own), C.byref(gemms)))
+        return own.value, gemms.value
+
 
 class GatedAttnKVCache:
     """View of one slot's paged KV cache with the reference object's surface

@@ -282,6 +282,31 @@ int32_t dm_decode_step(dm_ctx* ctx, int32_t slot, int32_t token_in, int32_t* tok
 int32_t dm_generate(dm_ctx* ctx, int32_t slot, int32_t token_in, int32_t n_steps,
                     int32_t* tokens_out_host);
 
+/* ---- batched decode (B sequences, one token each per step) ---------------------------
+ * The batched form of the decode step the reference runs per sequence (cmd_decode.mojo
+ * 2014-2045 over forward_port_macro_scheduler_gguf, gguf_port_loader.mojo:329): row i
+ * decodes one token of sequence slot slots[i].  Per row the semantics equal
+ * dm_decode_step's; the dense projections run as tensor-core GEMMs of the rows (fp32
+ * activations split into two bf16 terms), the routing is the same canonical router, the
+ * experts run on the tensor cores grouped by expert.  Slots must be distinct; every slot
+ * must be ready to decode (as for dm_decode_step).  The batch holds at most
+ * dm_batch_capacity rows (min(max_seqs, 64)). */
+int32_t dm_batch_capacity(dm_ctx* ctx, int32_t* cap_out);
+/* One step: tokens_out_host [n] greedy next tokens; logits_host [n][V] (may be NULL). */
+int32_t dm_decode_batch(dm_ctx* ctx, const int32_t* slots_host, const int32_t* tokens_in_host, int32_t n,
+                        int32_t* tokens_out_host, float* logits_host);
+/* n_steps greedy steps fed back on the device; tokens_out_host [n_steps][n]. */
+int32_t dm_generate_batch(dm_ctx* ctx, const int32_t* slots_host, const int32_t* tokens_in_host, int32_t n,
+                          int32_t n_steps, int32_t* tokens_out_host);
+/* Enqueues n_steps batched steps without synchronising (tokens recorded on the device);
+ * dm_batch_read_generated copies the [n_steps][n] tokens of the last enqueue to the host
+ * after synchronising. */
+int32_t dm_enqueue_decode_batch(dm_ctx* ctx, const int32_t* slots_host, const int32_t* tokens_in_host, int32_t n,
+                                int32_t n_steps);
+int32_t dm_batch_read_generated(dm_ctx* ctx, int32_t n, int32_t n_steps, int32_t* tokens_out_host);
+/* Launches per batched step: own kernels and library GEMMs. */
+int32_t dm_batch_kernels_per_step(dm_ctx* ctx, int32_t n, int32_t* own_out, int32_t* gemms_out);
+
 /* ---- device-resident entry points (for callers that keep data in HBM) ---------------- */
 /* Enqueues n_steps greedy decode steps for `slot` on the context stream with the input
  * token already on the device (the token produced by the previous step, or the one set by
