@@ -59,6 +59,13 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
     ap.add_argument("--timeline", default="", help="also trace one decode step; write its launch timeline here")
+    ap.add_argument("--workload", default="c2", choices=["c2", "c3"],
+                    help="c2: bs1 decode (BASELINE config 2); c3: batched decode of 64 sequences at 32768 "
+                         "cached tokens each (config 3)")
+    ap.add_argument("--batch", type=int, default=64, help="c3: sequences per step")
+    ap.add_argument("--c3-ctx", type=int, default=32768, help="c3: cached tokens per sequence")
+    ap.add_argument("--router-skew", type=float, default=1.1,
+                    help="c3: Zipf exponent of the expert load (0: the synthetic router as drawn)")
     return ap.parse_args()
 
 
@@ -460,6 +467,9 @@ def main():
     rank, local, world = dist_env()
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.workload == "c3":
+        from disk_streaming_moe_engine_b200 import bench_batch
+        return bench_batch.run(args, rank, local, world)
     return run_ours(args, rank, local, world)
 
 

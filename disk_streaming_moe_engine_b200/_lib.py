@@ -24,6 +24,7 @@ DM_ERR_ROUTER = 9
 
 DM_KERNEL_MIXER_IN, DM_KERNEL_MIXER_OUT, DM_KERNEL_MIXER_CORE = 0, 1, 2
 DM_KERNEL_ROUTER, DM_KERNEL_MOE, DM_KERNEL_HEAD = 3, 4, 6
+DM_BKERNEL_ATTN, DM_BKERNEL_GDN_REC, DM_BKERNEL_EXPERTS = 0, 1, 2
 
 DM_DTYPE_BF16 = 0
 DM_DTYPE_F32 = 1
@@ -109,6 +110,11 @@ SIGNATURES = {
     "dm_enqueue_decode_batch": (I32, [P, P, P, I32, I32]),
     "dm_batch_read_generated": (I32, [P, I32, I32, P]),
     "dm_batch_kernels_per_step": (I32, [P, I32, C.POINTER(I32), C.POINTER(I32)]),
+    "dm_synth_state_device": (I32, [P, U64, F32, F32, I32]),
+    "dm_tensor_add_rank1": (I32, [P, I32, I32, P, C.c_int64, P, I32]),
+    "dm_batch_stats": (I32, [P, I32, P]),
+    "dm_set_router_bias": (I32, [P, I32, P, I32]),
+    "dm_time_batch_kernel": (I32, [P, I32, I32, I32, I32, C.POINTER(F32), C.POINTER(U64)]),
 }
 
 _LIB = None

@@ -6,6 +6,7 @@
 // step (embedding, all blocks, head) is captured once per sequence slot into a CUDA graph
 // and replayed per token.
 #include <cublas_v2.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -43,6 +44,8 @@ cudaError_t launch_synth_bf16(cudaStream_t st, uint16_t* dst, uint64_t n, uint64
 cudaError_t launch_synth_f32(cudaStream_t st, float* dst, uint64_t n, uint64_t seed, uint64_t stream_id,
                              float mean, float std);
 cudaError_t launch_synth_u8(cudaStream_t st, uint8_t* dst, uint64_t n, uint64_t seed, uint64_t stream_id);
+cudaError_t launch_rank1_add_bf16(cudaStream_t st, uint16_t* W, int64_t rows, int cols, const float* beta,
+                                  const float* u);
 cudaError_t launch_synth_f16abs(cudaStream_t st, uint16_t* dst, uint64_t n, uint64_t seed,
                                 uint64_t stream_id, float std);
 }  // namespace dm
@@ -50,6 +53,7 @@ cudaError_t launch_synth_f16abs(cudaStream_t st, uint16_t* dst, uint64_t n, uint
 using namespace dm;
 
 struct dm_ctx {
+    CUtensorMap kv_map{};  // 2-D tiled view of the KV arena for the attention page copies
     dm_model_config mc{};
     dm_runtime_config rc{};
     Dims d{};
@@ -85,6 +89,7 @@ struct dm_ctx {
     size_t blas_ws_bytes = 0;
     std::vector<cudaGraphExec_t> bgraphs;  // [2 * (cap + 1)]
     int* h_bio = nullptr;                  // pinned [4 * kMaxBatch]: slots, tokens in, tokens out
+    float* rbias = nullptr;                // [L][E] router logit offsets (dm_set_router_bias)
     bool use_pdl = true;       // programmatic dependent launch between step kernels
     bool gdn_fused = true;     // GDN recurrence + output projection as one kernel
     bool l2_prefetch = false;  // latency-bound kernels prefetch upcoming weights into L2 (off:
@@ -293,10 +298,11 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t ob_part = T(BC * d.Hq * kMaxSplits * (d.D + 2) * 4), ob_aout = T(BC * d.Hq * d.D * 4);
     const size_t ob_acnt = T(BC * d.Hkv * 4), ob_xn = T(BC * H * 4), ob_lg = T(BC * (d.E + 1) * 4);
     const size_t ob_ids = T(BC * d.topk * 4), ob_pr = T(BC * d.topk * 4), ob_sg = T(BC * 4);
-    const size_t ob_segs = T(static_cast<size_t>(max_segs) * 16), ob_work = T(16);
+    const size_t ob_segs = T(static_cast<size_t>(max_segs) * 16), ob_work = T(16), ob_stats = T(16);
     const size_t ob_ptok = T(P * 4), ob_pof = T(P * 4), ob_h = T(P * d.I * 4), ob_epart = T(P * H * 4);
     const size_t ob_cv = T(BC * kHeadChunks * 4), ob_ci = T(BC * kHeadChunks * 4), ob_hl = T(BC * d.V * 4);
     const size_t ob_gen = T(static_cast<size_t>(bgen_cap) * 4), ob_genidx = T(4);
+    const size_t o_rbias = T(static_cast<size_t>(d.L) * d.E * 4);
     const size_t blas_ws = static_cast<size_t>(32) << 20;
     const size_t ob_ws = T(blas_ws);
     c->arena_bytes = p.off;
@@ -393,6 +399,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     bb.sg = reinterpret_cast<float*>(A + ob_sg);
     bb.segs = reinterpret_cast<int4*>(A + ob_segs);
     bb.work = reinterpret_cast<int*>(A + ob_work);
+    bb.stats = reinterpret_cast<unsigned*>(A + ob_stats);
     bb.pair_tok = reinterpret_cast<int*>(A + ob_ptok);
     bb.pair_of = reinterpret_cast<int*>(A + ob_pof);
     bb.h = reinterpret_cast<float*>(A + ob_h);
@@ -404,6 +411,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     bb.gen_idx = reinterpret_cast<int*>(A + ob_genidx);
     bb.gen_cap = bgen_cap;
     c->blas_ws = A + ob_ws;
+    c->rbias = reinterpret_cast<float*>(A + o_rbias);
     c->blas_ws_bytes = blas_ws;
     return DM_OK;
 }
@@ -453,6 +461,43 @@ static void host_parallel(uint64_t n, F&& f) {
         th.emplace_back([=, &f] { f(a, b); });
     }
     for (auto& x : th) x.join();
+}
+
+// Tensor map of the KV arena for the attention kernel's page copies: rows of D bf16
+// ([att][page][K|V][Hkv][16] flattened), boxes of 16 rows x 64 columns (128 bytes, the
+// swizzle span), 128-byte swizzle.  The encoder comes from the driver entry point table.
+static bool encode_kv_map(dm_ctx* c) {
+    c->b.kv_tmap = &c->kv_map;
+    const Dims& d = c->d;
+    if (d.n_att == 0) return true;
+    typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn ||
+        q != cudaDriverEntryPointSuccess) {
+        fprintf(stderr, "dm_ctx_create: cuTensorMapEncodeTiled unavailable\n");
+        return false;
+    }
+    const uint64_t rows = static_cast<uint64_t>(d.n_att) * d.num_pages * 2 * d.Hkv * kPageTokens;
+    if (rows >= (1ull << 31)) {
+        fprintf(stderr, "dm_ctx_create: KV arena of %llu rows exceeds the 2^31 tensor-map coordinate range\n",
+                static_cast<unsigned long long>(rows));
+        return false;
+    }
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.D), rows};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.D) * 2};
+    const cuuint32_t box[2] = {64, kPageTokens};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = reinterpret_cast<EncodeFn>(fn)(&c->kv_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c->b.kv, dims, strides,
+                                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        fprintf(stderr, "dm_ctx_create: cuTensorMapEncodeTiled failed (%d)\n", static_cast<int>(r));
+        return false;
+    }
+    return true;
 }
 
 // ------------------------------------------------------------------------------------
@@ -527,6 +572,7 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
         e = launch_rope_table(c->stream, c->b.rope, c->d.max_pages * kPageTokens, c->d.rot_dim, c->d.theta);
     if (e == cudaSuccess) e = cudaMallocHost(&c->h_io, 64);
     if (e == cudaSuccess) e = cudaMallocHost(&c->h_bio, 4 * kMaxBatch * sizeof(int));
+    if (e == cudaSuccess && !encode_kv_map(c)) e = cudaErrorInvalidValue;
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) {
         fprintf(stderr, "dm_ctx_create: %s\n", cudaGetErrorString(e));
@@ -1295,6 +1341,28 @@ static void advance_batch(dm_ctx* c, const int32_t* slots, int n, int n_steps) {
     for (int i = 0; i < n; ++i) advance_lens(c, slots[i], n_steps);
 }
 
+// Captured graphs hold kernel arguments by value: drop them when an argument changes.
+static void drop_graphs(dm_ctx* c) {
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (auto& g : c->graphs)
+        if (g) cudaGraphExecDestroy(g), g = nullptr;
+    for (auto& g : c->bgraphs)
+        if (g) cudaGraphExecDestroy(g), g = nullptr;
+}
+
+int32_t dm_set_router_bias(dm_ctx* c, int32_t layer, const float* bias, int32_t n) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    if (layer < 0 || layer >= c->d.L) return set_err(c, DM_ERR_INVALID_ARG, "ROUTER_ERROR", "router", layer, "layer out of range");
+    if (bias && n != c->d.E)
+        return set_err(c, DM_ERR_INVALID_ARG, "ROUTER_ERROR", "router", layer, "bias of %d values, expected %d", n, c->d.E);
+    cudaSetDevice(c->device);
+    float* dst = c->rbias + static_cast<size_t>(layer) * c->d.E;
+    if (bias) DM_CUDA(c, cudaMemcpy(dst, bias, sizeof(float) * n, cudaMemcpyHostToDevice), "router");
+    drop_graphs(c);
+    c->layers[layer].router_bias = bias ? dst : nullptr;
+    return DM_OK;
+}
+
 int32_t dm_batch_capacity(dm_ctx* c, int32_t* cap) {
     if (!c || !cap) return DM_ERR_INVALID_ARG;
     *cap = c->bb.cap;
@@ -1342,6 +1410,18 @@ int32_t dm_generate_batch(dm_ctx* c, const int32_t* slots, const int32_t* tokens
     int rc = dm_enqueue_decode_batch(c, slots, tokens_in, n, n_steps);
     if (rc != DM_OK) return rc;
     return dm_batch_read_generated(c, n, n_steps, out);
+}
+
+int32_t dm_batch_stats(dm_ctx* c, int32_t reset, uint32_t* out4) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    if (out4) {
+        DM_CUDA(c, cudaMemcpyAsync(c->h_bio + 3 * kMaxBatch, c->bb.stats, 16, cudaMemcpyDeviceToHost, c->stream), "stats");
+        DM_CUDA(c, cudaStreamSynchronize(c->stream), "stats");
+        memcpy(out4, c->h_bio + 3 * kMaxBatch, 16);
+    }
+    if (reset) DM_CUDA(c, cudaMemsetAsync(c->bb.stats, 0, 16, c->stream), "stats");
+    return DM_OK;
 }
 
 int32_t dm_batch_kernels_per_step(dm_ctx* c, int32_t n, int32_t* own, int32_t* gemms) {
@@ -1550,6 +1630,79 @@ int32_t dm_time_kernel(dm_ctx* c, int32_t which, int32_t layer, int32_t iters, f
     return check_device_error(c, "profile");
 }
 
+// Times one kernel of the batched step for the n rows staged by the last batched call,
+// on the state that call left (attention and recurrence: a layer's kernel re-run on the
+// current positions; experts: gate/up + down of the grouping of the last layer).  Same
+// method as dm_time_kernel: each launch alone after an L2-evicting read, CUDA events.
+int32_t dm_time_batch_kernel(dm_ctx* c, int32_t n, int32_t which, int32_t layer, int32_t iters, float* avg_ms,
+                             uint64_t* bytes) {
+    if (!c || !avg_ms || !bytes || iters <= 0 || n <= 0 || n > c->bb.cap) return DM_ERR_INVALID_ARG;
+    const Dims& d = c->d;
+    if (layer < 0 || layer >= d.L) return set_err(c, DM_ERR_INVALID_ARG, "PROFILE", "profile", layer, "layer out of range");
+    const LayerW& w = c->layers[layer];
+    LaunchCfg lc = lcfg(c);
+    lc.pdl = false;
+    cudaSetDevice(c->device);
+    std::vector<int> slots(n);
+    DM_CUDA(c, cudaMemcpy(slots.data(), c->bb.slots, sizeof(int) * n, cudaMemcpyDeviceToHost), "profile");
+    uint64_t by = 0;
+    if (which == DM_BKERNEL_ATTN) {
+        if (!w.is_attn) return set_err(c, DM_ERR_INVALID_ARG, "PROFILE", "profile", layer, "not an attention layer");
+        // every row reads its whole history (positions 0..pos) once, K and V
+        for (int i = 0; i < n; ++i) by += static_cast<uint64_t>(c->slot_len[slots[i]] + 1) * 2 * d.Hkv * d.D * 2;
+    } else if (which == DM_BKERNEL_GDN_REC) {
+        if (w.is_attn) return set_err(c, DM_ERR_INVALID_ARG, "PROFILE", "profile", layer, "not a GDN layer");
+        by = static_cast<uint64_t>(n) * (2ull * d.nv * d.dv * d.dk * 4 + 4ull * d.qkv_dim * 4);
+    } else if (which == DM_BKERNEL_EXPERTS) {
+        std::vector<int> ids(static_cast<size_t>(n) * d.topk);
+        DM_CUDA(c, cudaMemcpy(ids.data(), c->bb.ids, sizeof(int) * ids.size(), cudaMemcpyDeviceToHost), "profile");
+        std::vector<uint8_t> seen(d.E, 0);
+        int uniq = 0;
+        for (int v : ids)
+            if (v >= 0 && v < d.E && !seen[v]) seen[v] = 1, ++uniq;
+        by = static_cast<uint64_t>(uniq + 1) * d.expert_bytes;  // + the shared expert
+    } else {
+        return DM_ERR_INVALID_ARG;
+    }
+    *bytes = by;
+    const LayerW& wl = c->layers[d.L - 1];  // the grouping in the buffers is the last layer's
+    auto launch = [&]() -> cudaError_t {
+        if (which == DM_BKERNEL_ATTN) return launch_attn_decode_batch(lc, d, w, c->bb, c->b, n);
+        if (which == DM_BKERNEL_GDN_REC) return launch_gdn_rec_batch(lc, d, w, c->bb, c->b, n);
+        cudaError_t e = cudaMemsetAsync(c->bb.work + 1, 0, 8, c->stream);
+        return e == cudaSuccess ? launch_b_experts(lc, d, wl, c->bb, c->b, n) : e;
+    };
+    constexpr size_t kFlushBytes = 256ull << 20;
+    if (!c->flush_buf) {
+        DM_CUDA(c, cudaMalloc(&c->flush_buf, kFlushBytes), "profile");
+        DM_CUDA(c, cudaMemsetAsync(c->flush_buf, 0, kFlushBytes, c->stream), "profile");
+    }
+    cudaEvent_t e0, e1;
+    DM_CUDA(c, cudaEventCreate(&e0), "profile");
+    DM_CUDA(c, cudaEventCreate(&e1), "profile");
+    cudaError_t e = launch();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    float ms = 0.0f;
+    for (int i = 0; i < iters && e == cudaSuccess; ++i) {
+        e = launch_l2_flush_read(c->stream, c->flush_buf, kFlushBytes, c->num_sms);
+        // the experts' work counters are reset before the start event
+        if (e == cudaSuccess && which == DM_BKERNEL_EXPERTS) e = cudaMemsetAsync(c->bb.work + 1, 0, 8, c->stream);
+        if (e == cudaSuccess) e = cudaEventRecord(e0, c->stream);
+        if (e == cudaSuccess)
+            e = which == DM_BKERNEL_EXPERTS ? launch_b_experts(lc, d, wl, c->bb, c->b, n) : launch();
+        if (e == cudaSuccess) e = cudaEventRecord(e1, c->stream);
+        if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+        float one = 0.0f;
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&one, e0, e1);
+        ms += one;
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "profile", layer, "%s", cudaGetErrorString(e));
+    *avg_ms = ms / iters;
+    return check_device_error(c, "profile");
+}
+
 // ---- synthetic checkpoint -------------------------------------------------------------
 int32_t dm_synth_bf16(uint64_t seed, uint64_t sid, uint64_t n, float mean, float std, uint16_t* out) {
     if (!out) return DM_ERR_INVALID_ARG;
@@ -1584,6 +1737,52 @@ int32_t dm_synth_f16_absnormal(uint64_t seed, uint64_t sid, uint64_t n, float st
     host_parallel(n, [&](uint64_t a, uint64_t b) {
         for (uint64_t i = a; i < b; ++i) out[i] = synth_f32_to_f16(fabsf(std * synth_normal(synth_hash(key, i))));
     });
+    return DM_OK;
+}
+
+// Seeded synthetic sequence state for every slot: the whole KV page pool bf16 N(0, kv_std),
+// every GDN recurrent state and conv window fp32 N(0, state_std); every slot's length (and
+// each attention layer's) becomes `len`.  Page tables are left as they are.
+int32_t dm_synth_state_device(dm_ctx* c, uint64_t seed, float kv_std, float state_std, int32_t len) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    const Dims& d = c->d;
+    if (len < 0 || len > d.max_pages * kPageTokens)
+        return set_err(c, DM_ERR_CAPACITY, "M5_ERR_CONTEXT_SIZE", "kv_alloc", -1, "length %d exceeds capacity", len);
+    cudaSetDevice(c->device);
+    const uint64_t nkv = static_cast<uint64_t>(d.n_att) * d.num_pages * 2 * d.Hkv * kPageTokens * d.D;
+    const uint64_t ns = static_cast<uint64_t>(d.n_gdn) * d.max_seqs * d.nv * d.dv * d.dk;
+    const uint64_t nr = static_cast<uint64_t>(d.n_gdn) * d.max_seqs * kConvRing * d.qkv_dim;
+    cudaError_t e = nkv ? launch_synth_bf16(c->stream, c->b.kv, nkv, seed, 0x5eed0001ull, 0.0f, kv_std) : cudaSuccess;
+    if (e == cudaSuccess && ns) e = launch_synth_f32(c->stream, c->b.S, ns, seed, 0x5eed0002ull, 0.0f, state_std);
+    if (e == cudaSuccess && nr) e = launch_synth_f32(c->stream, c->b.ring, nr, seed, 0x5eed0003ull, 0.0f, state_std);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "synth", -1, "%s", cudaGetErrorString(e));
+    for (int s = 0; s < d.max_seqs; ++s) {
+        c->slot_len[s] = len;
+        for (int a = 0; a < d.n_att; ++a) c->att_len[static_cast<size_t>(a) * d.max_seqs + s] = len;
+        c->dev_pos_valid[s] = 0;
+    }
+    return DM_OK;
+}
+
+// W += beta u^T for a bf16 dense tensor (rows x cols as uploaded): a rank-one change of
+// an uploaded weight, used to shape synthetic workloads (e.g. skewed expert load).
+int32_t dm_tensor_add_rank1(dm_ctx* c, int32_t layer, int32_t id, const float* beta_host, int64_t rows,
+                            const float* u_host, int32_t cols) {
+    if (!c || !beta_host || !u_host || rows <= 0 || cols <= 0) return DM_ERR_INVALID_ARG;
+    void* dst = nullptr;
+    size_t bytes = 0;
+    int rc = tensor_target(c, layer, id, DM_DTYPE_BF16, static_cast<uint64_t>(rows) * cols, &dst, &bytes);
+    if (rc != DM_OK) return rc;
+    cudaSetDevice(c->device);
+    float* tmp = nullptr;
+    DM_CUDA(c, cudaMalloc(&tmp, sizeof(float) * (rows + cols)), "synth");
+    cudaError_t e = cudaMemcpyAsync(tmp, beta_host, sizeof(float) * rows, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tmp + rows, u_host, sizeof(float) * cols, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = launch_rank1_add_bf16(c->stream, static_cast<uint16_t*>(dst), rows, cols, tmp, tmp + rows);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "synth", layer, "%s", cudaGetErrorString(e));
     return DM_OK;
 }
 

@@ -17,6 +17,7 @@
 // current token's k/v come from shared memory, so the append by CTA (g, 0) never races
 // with the reads of the other CTAs, which only touch positions < pos.
 #include <cooperative_groups.h>
+#include <cuda.h>
 
 #include "dm_common.cuh"
 #include "dm_kernels.h"
@@ -47,6 +48,10 @@ struct AttnArgs {
     const void* next_w;       // o_proj weights, prefetched into L2
     size_t next_bytes;
     uint32_t* err;
+    // 2-D tiled view of the whole KV arena (all attention layers): columns D, rows
+    // [att][page][K|V][Hkv][16]; boxes of 16 rows x 64 columns, 128-byte swizzle
+    CUtensorMap kv_map;
+    int kv_row0;              // first row of this layer
     // batched launch (grid.z = batch rows): row b attends for sequence slots[b]; page table
     // and pos advance by the slot, the q/k/v inputs, partials, outputs and counters by the
     // row.  slots == nullptr: one sequence.
@@ -78,19 +83,33 @@ cudaError_t launch_rope_table(cudaStream_t st, float2* tab, int capacity, int ro
     return cudaGetLastError();
 }
 
-constexpr int kAttnStages = 6;   // K+V page tiles in flight per CTA
+constexpr int kAttnStages = 6;   // K+V page tiles in flight per CTA (one sequence)
 constexpr int kMaxPagesPerSplit = 256;  // page ids staged in shared memory
 
-// One KV page tile (16 tokens x D, K then V) per ring stage.
-// One KV page (16 tokens, one head) per ring stage: K rows then V rows, each row padded
-// to RS bytes so that the 8 rows an ldmatrix reads fall in distinct bank groups.
+// One KV page (16 tokens, one head) per ring stage: the K tile then the V tile, each as
+// D/64 column chunks of [16 rows][128 bytes] written by the tensor-map copy with the
+// 128-byte swizzle (16-byte unit u of row r lands at unit u ^ (r & 7)), so the 8 rows an
+// ldmatrix reads at one column fall in 8 distinct bank groups.
 template <int D>
 struct AttnGeom {
-    static constexpr int RS = (D + 8) * 2;               // bytes of one staged row
-    static constexpr int TILE = kPageTokens * RS;        // K (or V) of one page
+    static constexpr int CHUNK = kPageTokens * 128;      // one 64-column chunk of a tile
+    static constexpr int TILE = (D / 64) * CHUNK;        // K (or V) of one page
     static constexpr int STAGE = 2 * TILE;
-    static constexpr int RING = kAttnStages * STAGE;
+    static_assert(D % 64 == 0, "whole 128-byte column chunks");
 };
+// Byte offset of (row, col) inside a staged tile.
+template <int D>
+DM_DEV uint32_t kv_tile_off(int row, int col) {
+    return (col >> 6) * AttnGeom<D>::CHUNK + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) + (col & 7) * 2;
+}
+// 2-D tiled tensor-map load (no multicast) completing on an mbarrier.
+DM_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
 
 // mma.sync m16n8k16, bf16 inputs, fp32 accumulate (fragment layouts of the PTX ISA:
 // g = lane / 4, t = lane % 4; A a0 = A[g][2t..2t+1], a1 = A[g+8][..], a2 = A[g][2t+8..],
@@ -113,8 +132,88 @@ DM_DEV void ldsm_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(smem_u32(row_addr)));
 }
+DM_DEV void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* row_addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(row_addr)));
+}
+// all four A registers (rows g and g + 8)
+DM_DEV void mma_bf16_16816_full(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 DM_DEV uint32_t pack_bf16x2(uint16_t lo, uint16_t hi) { return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16); }
 DM_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ---- per-CTA preparation of the new token (shared by the decode kernels) ---------------
+// q heads of KV group g, new k, new v: one parallel load, per-head RMSNorm (q_norm / k_norm)
+// and partial RoPE in fp32 (norm weights and the RoPE row staged by the caller), then k, v
+// rounded to bf16 (cache format) and q split into hi + lo bf16 terms for the tensor cores.
+// All NT threads of the CTA take part; ends with a barrier.
+template <int D, int GRP, int NT>
+DM_DEV void attn_prepare(const float* qsrc, const float* ksrc, const float* vsrc, const float* qn_s, const float* kn_s,
+                         const float2* cs_s, int rot_dim, float eps, float (*qsm)[D + 4], float* knew, float* vnew,
+                         uint16_t* kbits, uint16_t* vbits, uint16_t (*qh)[D + 8], uint16_t (*ql)[D + 8]) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    {
+        constexpr int QPT = (GRP * D + NT - 1) / NT, KPT = (D + NT - 1) / NT;
+        float qv[QPT], kv[KPT], vv[KPT];
+#pragma unroll
+        for (int i = 0; i < QPT; ++i) qv[i] = tid + NT * i < GRP * D ? qsrc[tid + NT * i] : 0.0f;
+#pragma unroll
+        for (int i = 0; i < KPT; ++i) {
+            const int d = tid + NT * i;
+            kv[i] = d < D ? ksrc[d] : 0.0f;
+            vv[i] = d < D ? vsrc[d] : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < QPT; ++i)
+            if (tid + NT * i < GRP * D) qsm[(tid + NT * i) / D][(tid + NT * i) % D] = qv[i];
+#pragma unroll
+        for (int i = 0; i < KPT; ++i) {
+            const int d = tid + NT * i;
+            if (d < D) {
+                knew[d] = kv[i];
+                vnew[d] = vv[i];
+            }
+        }
+    }
+    __syncthreads();
+    for (int hh = warp; hh < GRP + 1; hh += NT / 32) {
+        float* v = hh < GRP ? qsm[hh] : knew;
+        const float* wn = hh < GRP ? qn_s : kn_s;
+        float ss = 0.0f;
+        for (int d = lane; d < D; d += 32) ss = fmaf(v[d], v[d], ss);
+        ss = warp_sum(ss);
+        const float rs = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+        for (int d = lane; d < D; d += 32) v[d] = v[d] * rs * wn[d];
+        __syncwarp();
+        const int half = rot_dim / 2;
+        for (int i = lane; i < half; i += 32) {
+            const float2 c = cs_s[i];
+            const float x0 = v[i], x1 = v[i + half];
+            v[i] = x0 * c.x - x1 * c.y;
+            v[i + half] = x0 * c.y + x1 * c.x;
+        }
+        __syncwarp();
+    }
+    __syncthreads();
+    for (int d = tid; d < D; d += NT) {
+        kbits[d] = f32_to_bf16(knew[d]);
+        vbits[d] = f32_to_bf16(vnew[d]);
+    }
+    for (int i = tid; i < GRP * D; i += NT) {
+        const float q = qsm[i / D][i % D];
+        const uint16_t hi = f32_to_bf16(q);
+        qh[i / D][i % D] = hi;
+        ql[i / D][i % D] = f32_to_bf16(q - bf16_to_f32(hi));
+    }
+    __syncthreads();
+}
 
 // Split-K ("flash-decoding") decode attention over the paged bf16 KV cache.
 // Grid (Hkv, nsplit), clusters of kAttnCluster splits, kAT threads, one CTA per SM.
@@ -130,14 +229,17 @@ DM_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::c
 //   merge     splits of a cluster through distributed shared memory, then the cluster
 //             partials of a head by the CTAs of the last cluster to finish, with the
 //             sigmoid output gate (reference attention.mojo:219-435 in decode form).
-// NB = pages scored per batch: kAttnStages (one sequence: every page of a split in flight at
-// once) or fewer, so that the next batch's pages load while this one is scored.
-template <int D, int GRP, int NB>
+// NB = pages scored per batch, ST = ring stages: NB == ST (one sequence: every page of a
+// split in flight at once) or NB < ST, so that ST - NB pages load while a batch is scored.
+template <int D, int GRP, int NB, int ST>
 __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
-    static_assert(NB >= 1 && NB <= kAttnStages && kAttnStages % NB == 0, "batch of whole ring stages");
+    static_assert(NB >= 1 && NB <= ST && ST % NB == 0, "batch of whole ring stages");
+    constexpr int kAttnStages = ST;
     using AG = AttnGeom<D>;
     static_assert(GRP <= 8, "heads of a KV group are rows 0..7 of the m16 tile");
-    extern __shared__ __align__(128) uint8_t ring[];
+    extern __shared__ __align__(1024) uint8_t ring_raw[];
+    // the swizzled tiles need 1024-byte aligned stages (the launch adds the slack)
+    uint8_t* ring = ring_raw + ((1024u - (smem_u32(ring_raw) & 1023u)) & 1023u);
     __shared__ __align__(8) uint64_t bar[kAttnStages];
     constexpr int QST = D + 4;  // fp32 q rows (norm / RoPE)
     __shared__ __align__(16) float qsm[GRP][QST];
@@ -188,8 +290,8 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
         mbar_fence_init();
     }
     __syncthreads();
-    // page i of the split into its ring stage: 16 K rows and 16 V rows, one bulk copy
-    // each, by the 32 lanes of warp 0 (row r < 16: K row r; r >= 16: V row r - 16)
+    // page i of the split into its ring stage: K then V, D/64 tensor-map boxes each, all
+    // issued by lane 0 of warp 0
     auto issue = [&](int i) {
         const int slot = i % kAttnStages;
         const int page = i < kMaxPagesPerSplit ? pages[i] : page_table[pg0 + i];
@@ -197,17 +299,17 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
         if (lane == 0) {
             if (good) {
                 mbar_arrive_expect_tx(&bar[slot], 2 * kPageTokens * D * 2);
+                uint8_t* st = ring + static_cast<size_t>(slot) * AG::STAGE;
+#pragma unroll
+                for (int kv = 0; kv < 2; ++kv) {
+                    const int y = a.kv_row0 + ((page * 2 + kv) * a.Hkv + g) * kPageTokens;
+#pragma unroll
+                    for (int j = 0; j < D / 64; ++j) tma_load_2d(st + kv * AG::TILE + j * AG::CHUNK, &a.kv_map, 64 * j, y, &bar[slot]);
+                }
             } else {
                 raise_error(a.err, DM_DEVERR_PAGE);
                 mbar_arrive(&bar[slot]);  // no copy: the tile is left as is and masked below
             }
-        }
-        __syncwarp();
-        if (good) {
-            const int kv = lane >> 4, r = lane & 15;
-            const uint16_t* src =
-                a.kv + ((static_cast<size_t>(page) * 2 + kv) * a.Hkv + g) * kPageTokens * D + static_cast<size_t>(r) * D;
-            bulk_g2s(ring + static_cast<size_t>(slot) * AG::STAGE + kv * AG::TILE + r * AG::RS, src, D * 2, &bar[slot]);
         }
     };
     if (warp == 0)
@@ -236,69 +338,10 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
         return;
     }
 
-    // ---- q heads of this KV group, new k, new v: one parallel load, then per-head
-    // RMSNorm + RoPE in shared memory (norm weights and the RoPE row were staged before
-    // the wait) ----
-    {
-        constexpr int QPT = (GRP * D + kAT - 1) / kAT, KPT = (D + kAT - 1) / kAT;
-        float qv[QPT], kv[KPT], vv[KPT];
-        const float* qsrc = qg_in + static_cast<size_t>(g * GRP) * D;
-#pragma unroll
-        for (int i = 0; i < QPT; ++i) qv[i] = tid + kAT * i < GRP * D ? qsrc[tid + kAT * i] : 0.0f;
-#pragma unroll
-        for (int i = 0; i < KPT; ++i) {
-            const int d = tid + kAT * i;
-            kv[i] = d < D ? kvnew_in[static_cast<size_t>(g) * D + d] : 0.0f;
-            vv[i] = d < D ? kvnew_in[static_cast<size_t>(a.Hkv + g) * D + d] : 0.0f;
-        }
-#pragma unroll
-        for (int i = 0; i < QPT; ++i)
-            if (tid + kAT * i < GRP * D) qsm[(tid + kAT * i) / D][(tid + kAT * i) % D] = qv[i];
-#pragma unroll
-        for (int i = 0; i < KPT; ++i) {
-            const int d = tid + kAT * i;
-            if (d < D) {
-                knew[d] = kv[i];
-                vnew[d] = vv[i];
-            }
-        }
-    }
-    __syncthreads();
-    trace_stamp(tr, 8);
-    for (int hh = warp; hh < GRP + 1; hh += kAW) {
-        float* v = hh < GRP ? qsm[hh] : knew;
-        const float* wn = hh < GRP ? qn_s : kn_s;
-        float ss = 0.0f;
-        for (int d = lane; d < D; d += 32) ss = fmaf(v[d], v[d], ss);
-        ss = warp_sum(ss);
-        const float rs = 1.0f / sqrtf(ss / static_cast<float>(D) + a.eps);
-        for (int d = lane; d < D; d += 32) v[d] = v[d] * rs * wn[d];
-        __syncwarp();
-        const int half = a.rot_dim / 2;
-        for (int i = lane; i < half; i += 32) {
-            const float2 c = cs_s[i];
-            const float x0 = v[i], x1 = v[i + half];
-            v[i] = x0 * c.x - x1 * c.y;
-            v[i + half] = x0 * c.y + x1 * c.x;
-        }
-        __syncwarp();
-    }
-    __syncthreads();
-    trace_stamp(tr, 9);
-    // k, v rounded to bf16 (cache format); q as hi + lo bf16 terms for the tensor cores
     const float sm_scale = 1.0f / sqrtf(static_cast<float>(D));
-    for (int d = tid; d < D; d += kAT) {
-        const uint16_t kb = f32_to_bf16(knew[d]);
-        kbits[d] = kb;
-        const uint16_t vb = f32_to_bf16(vnew[d]);
-        vbits[d] = vb;
-    }
-    for (int i = tid; i < GRP * D; i += kAT) {
-        const float q = qsm[i / D][i % D];
-        const uint16_t hi = f32_to_bf16(q);
-        qh[i / D][i % D] = hi;
-        ql[i / D][i % D] = f32_to_bf16(q - bf16_to_f32(hi));
-    }
+    attn_prepare<D, GRP, kAT>(qg_in + static_cast<size_t>(g * GRP) * D, kvnew_in + static_cast<size_t>(g) * D,
+                              kvnew_in + static_cast<size_t>(a.Hkv + g) * D, qn_s, kn_s, cs_s, a.rot_dim, a.eps, qsm,
+                              knew, vnew, kbits, vbits, qh, ql);
     __syncthreads();
     pdl_launch_dependents();
     trace_stamp(tr, 3);
@@ -337,11 +380,10 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
         // the staged copy of the page holding pos predates the append: patch its row
         if (ip_new >= b0 && ip_new < b0 + nb) {
             uint8_t* st = ring + static_cast<size_t>(ip_new % kAttnStages) * AG::STAGE;
-            uint16_t* kr = reinterpret_cast<uint16_t*>(st + (pos % kPageTokens) * AG::RS);
-            uint16_t* vr = reinterpret_cast<uint16_t*>(st + AG::TILE + (pos % kPageTokens) * AG::RS);
+            const int r = pos % kPageTokens;
             for (int d = tid; d < D; d += kAT) {
-                kr[d] = kbits[d];
-                vr[d] = vbits[d];
+                *reinterpret_cast<uint16_t*>(st + kv_tile_off<D>(r, d)) = kbits[d];
+                *reinterpret_cast<uint16_t*>(st + AG::TILE + kv_tile_off<D>(r, d)) = vbits[d];
             }
         }
         __syncthreads();
@@ -350,13 +392,13 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
             const int pi = warp >> 1;  // page of the batch
             const uint8_t* kt = ring + static_cast<size_t>((b0 + pi) % kAttnStages) * AG::STAGE;
             // ldmatrix x2 row addresses: lanes 0-7 tokens of k-columns 0-7, lanes 8-15 of 8-15
-            const uint8_t* krow = kt + (8 * (warp & 1) + (lane & 7)) * AG::RS + ((lane >> 3) & 1) * 16;
+            const int krow = 8 * (warp & 1) + (lane & 7), kcol = 8 * ((lane >> 3) & 1);
             float ch[4] = {0.0f, 0.0f, 0.0f, 0.0f}, cl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
             const bool arow = fg < GRP;
 #pragma unroll 4
             for (int ks = 0; ks < D / 16; ++ks) {
                 uint32_t b0r, b1r;
-                ldsm_x2(b0r, b1r, krow + ks * 32);
+                ldsm_x2(b0r, b1r, kt + kv_tile_off<D>(krow, 16 * ks + kcol));
                 const int c0 = 16 * ks + 2 * ft;
                 const uint32_t ah0 = arow ? *reinterpret_cast<const uint32_t*>(&qh[fg][c0]) : 0u;
                 const uint32_t ah2 = arow ? *reinterpret_cast<const uint32_t*>(&qh[fg][c0 + 8]) : 0u;
@@ -427,7 +469,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
                 const uint8_t* vt = ring + static_cast<size_t>((b0 + pi) % kAttnStages) * AG::STAGE + AG::TILE;
                 // ldmatrix x4 .trans: matrix m = lane / 8: tokens 8(m & 1).., dims 16w + 8(m >> 1)
                 const int m = lane >> 3;
-                const uint8_t* vrow = vt + (8 * (m & 1) + (lane & 7)) * AG::RS + (16 * warp + 8 * (m >> 1)) * 2;
+                const uint8_t* vrow = vt + kv_tile_off<D>(8 * (m & 1) + (lane & 7), 16 * warp + 8 * (m >> 1));
                 uint32_t v0, v1, v2, v3;
                 ldsm_x4_trans(v0, v1, v2, v3, vrow);
                 const int c0 = kPageTokens * pi + 2 * ft;
@@ -458,7 +500,7 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     cg::cluster_group cluster = cg::this_cluster();
     const int crank = static_cast<int>(cluster.block_rank());
     constexpr int PSZ = GRP * D + 2 * GRP;            // floats of one pushed partial
-    static_assert(kAttnCluster * PSZ * 4 <= AG::RING, "ring too small for the cluster merge");
+    static_assert(kAttnCluster * PSZ * 4 <= ST * AG::STAGE, "ring too small for the cluster merge");
     cluster.sync();                                    // every ring is free from here on
     float* dst0 = cluster.map_shared_rank(reinterpret_cast<float*>(ring), 0) + crank * PSZ;
     if (pv_on && fg < GRP) {
@@ -571,10 +613,337 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     kt_end(a.kt);
 }
 
-// Dynamic shared memory of a CTA: the page ring, and at least 120 KB so that one CTA
-// runs per SM (two would share an SM's issue slots while other SMs stay idle).
-size_t attn_ring_bytes(int D) {
-    const size_t ring = static_cast<size_t>(kAttnStages) * 2 * kPageTokens * (D + 8) * 2;
+// ---------------------------------------------------------------------------------------
+// Batched decode attention for long histories ("flash-decoding" per warp).
+// Grid (Hkv, nsplit, rows), kWW warps per CTA, one CTA per SM.  The CTA prepares the new
+// token as the one-sequence kernel does; then every warp streams its own pages (page
+// i of the split goes to warp i % kWW) through its own kWStages-deep ring of tensor-map
+// copies and keeps its own online softmax, so the main loop has no block barrier:
+//   scores   S = Q K^T (8 query heads in rows 0..7 of the m16 tile, q = hi + lo bf16),
+//            the lane holding head fg keeps the running max / partial sum of that head
+//   P V      O^T += V^T P^T: A = V^T straight from the staged tile (ldmatrix .trans),
+//            B = P from the score fragments of the same lane (p = hi + lo bf16), so P
+//            never leaves registers; O^T is 16 x (D/16) fragments of (dims, heads)
+// The warps' partials merge in shared memory into one partial per (row, head, split),
+// and the last split CTA of (row, KV head) merges the splits with the output gate.
+constexpr int kWW = 4;        // warps per CTA
+constexpr int kWStages = 3;   // ring stages per warp
+
+template <int D>
+constexpr size_t attn_warp_ring_bytes() {
+    return static_cast<size_t>(kWW) * kWStages * AttnGeom<D>::STAGE + 1024;
+}
+
+template <int D, int GRP>
+__global__ void __launch_bounds__(kWW * 32, 1) attn_decode_warp_kernel(const __grid_constant__ AttnArgs a) {
+    using AG = AttnGeom<D>;
+    constexpr int NT = kWW * 32;
+    constexpr int KS = D / 16;  // k-steps of Q K^T, m-tiles of V^T P^T
+    static_assert(GRP <= 8, "heads of a KV group are rows 0..7 of the m16 tile");
+    extern __shared__ __align__(1024) uint8_t ring_raw[];
+    uint8_t* ring = ring_raw + ((1024u - (smem_u32(ring_raw) & 1023u)) & 1023u);
+    __shared__ __align__(8) uint64_t bar[kWW][kWStages];
+    __shared__ __align__(16) float qsm[GRP][D + 4];
+    __shared__ __align__(16) uint16_t qh[GRP][D + 8], ql[GRP][D + 8];
+    __shared__ __align__(16) float knew[D], vnew[D];
+    __shared__ __align__(16) uint16_t kbits[D], vbits[D];
+    __shared__ float qn_s[D], kn_s[D];
+    __shared__ float2 cs_s[D / 2];
+    __shared__ int pages[kMaxPagesPerSplit];
+    __shared__ float wm[kWW][8], wl[kWW][8];
+    __shared__ int last_flag;
+    const int g = blockIdx.x, s = blockIdx.y, bz = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int fg = lane >> 2, ft = lane & 3;
+    const int slot = a.slots ? a.slots[bz] : 0;
+    const float* qg_in = a.qg + bz * a.qg_bs;
+    const float* kvnew_in = a.kvnew + bz * a.kvn_bs;
+    const int* page_table = a.page_table + slot * a.pt_ss;
+    float* part_out = a.part + bz * a.part_bs;
+    float* attn_out = a.out + bz * a.out_bs;
+    unsigned* counters = a.counters + bz * a.cnt_bs;
+
+    kt_start(a.kt);
+    const int pos = a.pos[slot];
+    const int n_tok = pos + 1;
+    const int capacity = a.max_pages * kPageTokens;
+    const bool in_range = pos >= 0 && pos < capacity;
+    const int n_pg = in_range ? (n_tok + kPageTokens - 1) / kPageTokens : 0;
+    const int pg0 = static_cast<int>(static_cast<long long>(s) * n_pg / a.nsplit);
+    const int pg1 = static_cast<int>(static_cast<long long>(s + 1) * n_pg / a.nsplit);
+    const int np = pg1 - pg0;
+    const int t0 = pg0 * kPageTokens;
+    const int t1 = min(n_tok, pg1 * kPageTokens);
+    for (int i = tid; i < np && i < kMaxPagesPerSplit; i += NT) pages[i] = page_table[pg0 + i];
+    if (tid == 0) {
+        for (int i = 0; i < kWW * kWStages; ++i) mbar_init(&bar[i / kWStages][i % kWStages], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    uint8_t* my_ring = ring + static_cast<size_t>(warp) * kWStages * AG::STAGE;
+    // local page j of this warp = page warp + kWW j of the split, into stage j % kWStages
+    auto issue = [&](int j) {
+        const int i = warp + kWW * j;
+        const int st = j % kWStages;
+        const int page = i < kMaxPagesPerSplit ? pages[i] : page_table[pg0 + i];
+        const bool good = page >= 0 && page < a.num_pages;
+        if (good) {
+            mbar_arrive_expect_tx(&bar[warp][st], 2 * kPageTokens * D * 2);
+            uint8_t* dst = my_ring + static_cast<size_t>(st) * AG::STAGE;
+#pragma unroll
+            for (int kv = 0; kv < 2; ++kv) {
+                const int y = a.kv_row0 + ((page * 2 + kv) * a.Hkv + g) * kPageTokens;
+#pragma unroll
+                for (int c = 0; c < D / 64; ++c) tma_load_2d(dst + kv * AG::TILE + c * AG::CHUNK, &a.kv_map, 64 * c, y, &bar[warp][st]);
+            }
+        } else {
+            raise_error(a.err, DM_DEVERR_PAGE);
+            mbar_arrive(&bar[warp][st]);
+        }
+    };
+    const int my_np = np > warp ? (np - warp + kWW - 1) / kWW : 0;
+    if (lane == 0)
+        for (int j = 0; j < my_np && j < kWStages; ++j) issue(j);
+    for (int i = tid; i < D; i += NT) {
+        qn_s[i] = bf16_to_f32(a.q_norm[i]);
+        kn_s[i] = bf16_to_f32(a.k_norm[i]);
+    }
+    if (in_range)
+        for (int i = tid; i < a.rot_dim / 2; i += NT) cs_s[i] = a.rope[static_cast<size_t>(pos) * (a.rot_dim / 2) + i];
+    pdl_wait();
+    kt_ready(a.kt);
+    if (!in_range) {  // no room: report, touch nothing (no copy was issued)
+        if (tid == 0 && s == 0) raise_error(a.err, DM_DEVERR_CAPACITY);
+        kt_end(a.kt);
+        return;
+    }
+    attn_prepare<D, GRP, NT>(qg_in + static_cast<size_t>(g * GRP) * D, kvnew_in + static_cast<size_t>(g) * D,
+                             kvnew_in + static_cast<size_t>(a.Hkv + g) * D, qn_s, kn_s, cs_s, a.rot_dim, a.eps, qsm, knew,
+                             vnew, kbits, vbits, qh, ql);
+    pdl_launch_dependents();
+    if (s == 0) {  // append at pos (one CTA per row and KV head)
+        const int page = page_table[pos / kPageTokens];
+        if (page < 0 || page >= a.num_pages) {
+            if (tid == 0) raise_error(a.err, DM_DEVERR_PAGE);
+        } else {
+            uint16_t* kd = a.kv + ((static_cast<size_t>(page) * 2 + 0) * a.Hkv + g) * kPageTokens * D +
+                           static_cast<size_t>(pos % kPageTokens) * D;
+            uint16_t* vd = a.kv + ((static_cast<size_t>(page) * 2 + 1) * a.Hkv + g) * kPageTokens * D +
+                           static_cast<size_t>(pos % kPageTokens) * D;
+            for (int d = tid; d < D; d += NT) {
+                kd[d] = kbits[d];
+                vd[d] = vbits[d];
+            }
+        }
+    }
+
+    // ---- per-warp streaming ----
+    const float sm_scale = 1.0f / sqrtf(static_cast<float>(D));
+    const bool hrow = fg < GRP;  // this lane's score row is a real head
+    // A fragments of q (hi a0, hi a2, lo a0, lo a2 per k-step): held in registers up to
+    // D = 128; at D = 256 they would crowd out the O^T accumulators, so they are re-read
+    // from shared memory (padded rows: conflict-free) every page
+    constexpr bool kQRegs = D <= 128;
+    uint32_t qa[kQRegs ? KS : 1][4];
+    auto qfrag = [&](int ks, int r) -> uint32_t {
+        const int c0 = 16 * ks + 2 * ft + ((r & 1) ? 8 : 0);
+        if (!hrow) return 0u;
+        return (r < 2) ? *reinterpret_cast<const uint32_t*>(&qh[fg][c0]) : *reinterpret_cast<const uint32_t*>(&ql[fg][c0]);
+    };
+    if (kQRegs) {
+#pragma unroll
+        for (int ks = 0; ks < (kQRegs ? KS : 1); ++ks)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) qa[ks][r] = qfrag(ks, r);
+    }
+    float o[KS][4];
+#pragma unroll
+    for (int t = 0; t < KS; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+    float m_run = -INFINITY, l_part = 0.0f;  // head fg: running max; this lane's share of the sum
+    const int ip_new = pos / kPageTokens - pg0;
+    for (int j = 0; j < my_np; ++j) {
+        const int i = warp + kWW * j;
+        const int st = j % kWStages;
+        const bool ok = mbar_wait_bounded(&bar[warp][st], (j / kWStages) & 1, a.err, nullptr);
+        uint8_t* kt = my_ring + static_cast<size_t>(st) * AG::STAGE;
+        uint8_t* vt = kt + AG::TILE;
+        if (i == ip_new) {  // the staged copy of the page holding pos predates the append
+            const int r = pos % kPageTokens;
+            for (int d = lane; d < D; d += 32) {
+                *reinterpret_cast<uint16_t*>(kt + kv_tile_off<D>(r, d)) = kbits[d];
+                *reinterpret_cast<uint16_t*>(vt + kv_tile_off<D>(r, d)) = vbits[d];
+            }
+            __syncwarp();
+        }
+        // scores of the page's 16 tokens: n-tile 0 = tokens 0-7, n-tile 1 = tokens 8-15
+        float sh0[4] = {0.f, 0.f, 0.f, 0.f}, sl0[4] = {0.f, 0.f, 0.f, 0.f};
+        float sh1[4] = {0.f, 0.f, 0.f, 0.f}, sl1[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+            // ldmatrix x4: matrix lane / 8 = (tokens 8 (m >> 1) .., columns 8 (m & 1) ..)
+            const int mi = lane >> 3;
+            const int krow = 8 * (mi >> 1) + (lane & 7), kcol = 8 * (mi & 1);
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                uint32_t k0, k1, k2, k3;
+                ldsm_x4(k0, k1, k2, k3, kt + kv_tile_off<D>(krow, 16 * ks + kcol));
+                uint32_t q0, q1, q2, q3;
+                if (kQRegs) {
+                    q0 = qa[kQRegs ? ks : 0][0];
+                    q1 = qa[kQRegs ? ks : 0][1];
+                    q2 = qa[kQRegs ? ks : 0][2];
+                    q3 = qa[kQRegs ? ks : 0][3];
+                } else {
+                    q0 = qfrag(ks, 0);
+                    q1 = qfrag(ks, 1);
+                    q2 = qfrag(ks, 2);
+                    q3 = qfrag(ks, 3);
+                }
+                mma_bf16_16816(sh0, q0, q1, k0, k1);
+                mma_bf16_16816(sl0, q2, q3, k0, k1);
+                mma_bf16_16816(sh1, q0, q1, k2, k3);
+                mma_bf16_16816(sl1, q2, q3, k2, k3);
+            }
+        }
+        // lane: head fg, tokens 2ft + e (n-tile 0) and 8 + 2ft + e (n-tile 1)
+        const int tb = (pg0 + i) * kPageTokens;
+        float sv[4];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int p0 = tb + 2 * ft + e, p1 = tb + 8 + 2 * ft + e;
+            sv[e] = (ok && hrow && p0 >= t0 && p0 < t1) ? (sh0[e] + sl0[e]) * sm_scale : -INFINITY;
+            sv[2 + e] = (ok && hrow && p1 >= t0 && p1 < t1) ? (sh1[e] + sl1[e]) * sm_scale : -INFINITY;
+        }
+        float mp = fmaxf(fmaxf(sv[0], sv[1]), fmaxf(sv[2], sv[3]));
+        mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 1));
+        mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 2));
+        const float mn = fmaxf(m_run, mp);
+        const float alpha = (m_run == -INFINITY) ? (mn == -INFINITY ? 1.0f : 0.0f) : expf(m_run - mn);
+        float p[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) p[e] = sv[e] == -INFINITY ? 0.0f : expf(sv[e] - mn);
+        l_part = l_part * alpha + ((p[0] + p[1]) + (p[2] + p[3]));
+        m_run = mn;
+        // rescale O^T columns (heads 2ft, 2ft + 1) by their heads' alpha
+        const float a_lo = __shfl_sync(0xffffffffu, alpha, 4 * (2 * ft));
+        const float a_hi = __shfl_sync(0xffffffffu, alpha, 4 * (2 * ft + 1));
+#pragma unroll
+        for (int t = 0; t < KS; ++t) {
+            o[t][0] *= a_lo;
+            o[t][1] *= a_hi;
+            o[t][2] *= a_lo;
+            o[t][3] *= a_hi;
+        }
+        // B fragments of P^T (tokens x heads): b0 = tokens 2ft, 2ft+1 (n-tile 0), b1 = 8 + ...
+        uint32_t bh0, bh1, bl0, bl1;
+        {
+            const uint16_t h00 = f32_to_bf16(p[0]), h01 = f32_to_bf16(p[1]);
+            const uint16_t h10 = f32_to_bf16(p[2]), h11 = f32_to_bf16(p[3]);
+            bh0 = pack_bf16x2(h00, h01);
+            bh1 = pack_bf16x2(h10, h11);
+            bl0 = pack_bf16x2(f32_to_bf16(p[0] - bf16_to_f32(h00)), f32_to_bf16(p[1] - bf16_to_f32(h01)));
+            bl1 = pack_bf16x2(f32_to_bf16(p[2] - bf16_to_f32(h10)), f32_to_bf16(p[3] - bf16_to_f32(h11)));
+        }
+        {
+            // ldmatrix x4 .trans: matrix lane / 8 = (tokens 8 (m >> 1) .., dims 16t + 8 (m & 1) ..)
+            const int mi = lane >> 3;
+            const int vrow = 8 * (mi >> 1) + (lane & 7), vcol = 8 * (mi & 1);
+#pragma unroll
+            for (int t = 0; t < KS; ++t) {
+                uint32_t v0, v1, v2, v3;
+                ldsm_x4_trans(v0, v1, v2, v3, vt + kv_tile_off<D>(vrow, 16 * t + vcol));
+                mma_bf16_16816_full(o[t], v0, v1, v2, v3, bh0, bh1);
+                mma_bf16_16816_full(o[t], v0, v1, v2, v3, bl0, bl1);
+            }
+        }
+        __syncwarp();  // every lane is done with the stage
+        if (lane == 0 && j + kWStages < my_np) {
+            fence_proxy_async_smem();
+            issue(j + kWStages);
+        }
+    }
+    // sum of the head's lanes (ft = 0..3)
+    float l_run = l_part;
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    if (ft == 0 && fg < 8) {
+        wm[warp][fg] = my_np > 0 ? m_run : -INFINITY;
+        wl[warp][fg] = my_np > 0 ? l_run : 0.0f;
+    }
+    __syncthreads();  // every warp out of its loop: the rings are free
+    // ---- merge the warps: weights w_w = exp(m_w - M) of each head ----
+    float* ow = reinterpret_cast<float*>(ring);  // [kWW][GRP][D]
+    const int h0 = 2 * ft, h1 = 2 * ft + 1;
+#pragma unroll
+    for (int t = 0; t < KS; ++t) {
+        const int d0 = 16 * t + fg, d1 = d0 + 8;
+        if (h0 < GRP) {
+            ow[(warp * GRP + h0) * D + d0] = o[t][0];
+            ow[(warp * GRP + h0) * D + d1] = o[t][2];
+        }
+        if (h1 < GRP) {
+            ow[(warp * GRP + h1) * D + d0] = o[t][1];
+            ow[(warp * GRP + h1) * D + d1] = o[t][3];
+        }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < GRP * (D + 2); idx += NT) {
+        const int hh = idx / (D + 2), d = idx % (D + 2);
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kWW; ++w)
+            if (wl[w][hh] > 0.0f) M = fmaxf(M, wm[w][hh]);
+        float acc = 0.0f, L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWW; ++w) {
+            const float ww = wl[w][hh] > 0.0f ? expf(wm[w][hh] - M) : 0.0f;
+            L = fmaf(ww, wl[w][hh], L);
+            if (d < D) acc = fmaf(ww, ow[(w * GRP + hh) * D + d], acc);
+        }
+        float* pp = part_out + (static_cast<size_t>(g * GRP + hh) * kMaxSplits + s) * (D + 2);
+        pp[d] = d < D ? acc : (d == D ? M : L);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(counters + g, 1u);
+        last_flag = prev == static_cast<unsigned>(a.nsplit) - 1;
+        if (last_flag) __threadfence();
+    }
+    __syncthreads();
+    if (!last_flag) {
+        kt_end(a.kt);
+        return;
+    }
+    // ---- the last split of (row, KV head): merge the splits, output gate ----
+    const int ns = a.nsplit;
+    for (int o2 = tid; o2 < GRP * D; o2 += NT) {
+        const int hh = o2 / D, d = o2 % D;
+        const int hq = g * GRP + hh;
+        const float* ph0 = part_out + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
+        float M = -INFINITY;
+        for (int c = 0; c < ns; ++c) {
+            const float lc = __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D + 1);
+            if (lc > 0.0f) M = fmaxf(M, __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D));
+        }
+        float L = 0.0f, acc = 0.0f;
+        for (int c = 0; c < ns; ++c) {
+            const float lc = __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D + 1);
+            const float w = lc > 0.0f ? expf(__ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D) - M) : 0.0f;
+            L = fmaf(w, lc, L);
+            acc = fmaf(w, __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + d), acc);
+        }
+        const float gate = qg_in[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
+        attn_out[static_cast<size_t>(hq) * D + d] = (L > 0.0f ? acc / L : 0.0f) * sigmoid_f(gate);
+    }
+    if (tid == 0) counters[g] = 0u;
+    __syncthreads();
+    kt_end(a.kt);
+}
+
+// Dynamic shared memory of a CTA: the page ring of `stages` pages, and at least 120 KB so
+// that one CTA runs per SM (two would share an SM's issue slots while other SMs idle).
+size_t attn_ring_bytes(int D, int stages) {
+    const size_t ring = static_cast<size_t>(stages) * 2 * kPageTokens * D * 2 + 1024;  // + alignment slack
     return ring > 120 * 1024 ? ring : 120 * 1024;
 }
 
@@ -598,33 +967,49 @@ bool attn_supported(int D, int grp) {
 }
 
 #define DM_ATTN_INSTANCES(X) X(256, 8) X(256, 4) X(128, 8) X(128, 4) X(64, 4) X(64, 8)
-constexpr int kAttnBatchNB = 3;  // pages per scored batch of the batched launch (two batches in flight)
 
-template <int D, int GRP, int NB>
-static cudaError_t attn_attr_one(int max_scores_smem) {
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, GRP, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         max_scores_smem);
+template <int D, int GRP, int NB, int ST>
+static cudaError_t attn_attr_one() {
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<D, GRP, NB, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(attn_ring_bytes(D, ST)));
     if (e == cudaSuccess)  // largest shared-memory carve-out
-        e = cudaFuncSetAttribute(attn_decode_kernel<D, GRP, NB>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        e = cudaFuncSetAttribute(attn_decode_kernel<D, GRP, NB, ST>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     return e;
 }
 
+template <int D, int GRP>
+static cudaError_t attn_warp_attr_one() {
+    return cudaFuncSetAttribute(attn_decode_warp_kernel<D, GRP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(attn_warp_ring_bytes<D>()));
+}
+
 cudaError_t attn_set_attrs(int max_scores_smem) {
+    (void)max_scores_smem;
     cudaError_t e = cudaSuccess;
-#define DM_ATTN_ATTR(DD, GG)                                                    \
-    if (e == cudaSuccess) e = attn_attr_one<DD, GG, kAttnStages>(max_scores_smem); \
-    if (e == cudaSuccess) e = attn_attr_one<DD, GG, kAttnBatchNB>(max_scores_smem);
+#define DM_ATTN_ATTR(DD, GG)                                                                 \
+    if (e == cudaSuccess) e = attn_attr_one<DD, GG, kAttnStages, kAttnStages>();             \
+    if (e == cudaSuccess) e = attn_warp_attr_one<DD, GG>();
     DM_ATTN_INSTANCES(DM_ATTN_ATTR)
 #undef DM_ATTN_ATTR
     return e;
 }
 
-static cudaError_t attn_launch(const LaunchCfg& lc, const Dims& d, const AttnArgs& a, dim3 grid, bool batched) {
+static cudaError_t attn_warp_launch(const LaunchCfg& lc, const Dims& d, const AttnArgs& a, dim3 grid) {
+    const int grp = d.Hq / d.Hkv;
+#define DM_ATTN_WLAUNCH(DD, GG)                                                                             \
+    if (d.D == DD && grp == GG)                                                                             \
+        return launch_kernel(lc, attn_decode_warp_kernel<DD, GG>, grid, dim3(kWW * 32), attn_warp_ring_bytes<DD>(), a);
+    DM_ATTN_INSTANCES(DM_ATTN_WLAUNCH)
+#undef DM_ATTN_WLAUNCH
+    return cudaErrorInvalidValue;
+}
+
+static cudaError_t attn_launch(const LaunchCfg& lc, const Dims& d, const AttnArgs& a, dim3 grid) {
     const int grp = d.Hq / d.Hkv;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kAT);
-    cfg.dynamicSmemBytes = attn_ring_bytes(d.D);
+    cfg.dynamicSmemBytes = attn_ring_bytes(d.D, kAttnStages);
     cfg.stream = lc.stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -637,14 +1022,15 @@ static cudaError_t attn_launch(const LaunchCfg& lc, const Dims& d, const AttnArg
     cfg.numAttrs = 2;
 #define DM_ATTN_LAUNCH(DD, GG)                                                                              \
     if (d.D == DD && grp == GG)                                                                             \
-        return batched ? cudaLaunchKernelEx(&cfg, attn_decode_kernel<DD, GG, kAttnBatchNB>, a)              \
-                       : cudaLaunchKernelEx(&cfg, attn_decode_kernel<DD, GG, kAttnStages>, a);
+        return cudaLaunchKernelEx(&cfg, attn_decode_kernel<DD, GG, kAttnStages, kAttnStages>, a);
     DM_ATTN_INSTANCES(DM_ATTN_LAUNCH)
 #undef DM_ATTN_LAUNCH
     return cudaErrorInvalidValue;
 }
 
 static void attn_common_args(AttnArgs& a, const Dims& d, const LayerW& w, const Buffers& b) {
+    a.kv_map = *static_cast<const CUtensorMap*>(b.kv_tmap);
+    a.kv_row0 = w.sub * d.num_pages * 2 * d.Hkv * kPageTokens;
     a.q_norm = w.q_norm;
     a.k_norm = w.k_norm;
     a.kv = b.kv + static_cast<size_t>(w.sub) * d.num_pages * 2 * d.Hkv * kPageTokens * d.D;
@@ -679,18 +1065,26 @@ cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW&
     a.next_bytes = static_cast<size_t>(d.H) * d.Hq * d.D * 2;
     const dim3 grid(d.Hkv, a.nsplit);
     if (a.cta_trace && grid.x * grid.y * kTrCtaSlots > kTraceSlots - kTrCta) a.cta_trace = nullptr;
-    return attn_launch(lc, d, a, grid, false);
+    return attn_launch(lc, d, a, grid);
 }
 
-// Splits per (row, KV head) of the batched launch: about two CTAs per SM over the whole
-// grid, in whole clusters.
+// Splits per (row, KV head) of the batched launch (one CTA per SM): the count that
+// minimises waves / splits, i.e. the time per unit of work when every CTA does 1/ns of its
+// (row, head); ties go to fewer splits (less merge work).
 int attn_nsplit_batch(int num_sms, int Hkv, int n) {
     const int units = (n > 0 ? n : 1) * (Hkv > 0 ? Hkv : 1);
-    int ns = (2 * num_sms + units - 1) / units;
-    ns = (ns + kAttnCluster - 1) / kAttnCluster * kAttnCluster;
-    if (ns > kMaxSplits) ns = kMaxSplits;
-    if (ns < kAttnCluster) ns = kAttnCluster;
-    return ns;
+    int best = 1;
+    double best_cost = 1e30;
+    for (int ns = 1; ns <= kMaxSplits; ++ns) {
+        const long long ctas = static_cast<long long>(units) * ns;
+        const long long waves = (ctas + num_sms - 1) / num_sms;
+        const double cost = static_cast<double>(waves) / ns;
+        if (cost < best_cost - 1e-12) {
+            best_cost = cost;
+            best = ns;
+        }
+    }
+    return best;
 }
 
 cudaError_t launch_attn_decode_batch(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
@@ -714,7 +1108,7 @@ cudaError_t launch_attn_decode_batch(const LaunchCfg& lc, const Dims& d, const L
     a.kvn_bs = static_cast<size_t>(2) * d.Hkv * d.D;
     a.part_bs = static_cast<size_t>(d.Hq) * kMaxSplits * (d.D + 2);
     a.out_bs = static_cast<size_t>(d.Hq) * d.D;
-    return attn_launch(lc, d, a, dim3(d.Hkv, a.nsplit, n), true);
+    return attn_warp_launch(lc, d, a, dim3(d.Hkv, a.nsplit, n));
 }
 
 }  // namespace dm

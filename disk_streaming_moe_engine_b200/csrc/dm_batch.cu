@@ -216,6 +216,7 @@ struct BRouterArgs {
     float eps;
     float* xn;              // [n][K]
     float* logits;          // [n][E+1]
+    const float* bias;      // [E] logit offsets, or null
 };
 
 template <int K>
@@ -253,8 +254,9 @@ __global__ void __launch_bounds__(kBRThreads, 1) b_router_kernel(const __grid_co
     if (row > a.E) return;
     for (int t = 0; t < nt; ++t) {
         const float* xs = xs_all + static_cast<size_t>(t) * K;
-        const float acc = canon_router_dot<VPL>(wreg, reinterpret_cast<const float4*>(xs),
-                                                reinterpret_cast<const float4*>(xs + K / 2), lane);
+        float acc = canon_router_dot<VPL>(wreg, reinterpret_cast<const float4*>(xs),
+                                          reinterpret_cast<const float4*>(xs + K / 2), lane);
+        if (a.bias && row < a.E) acc = __fadd_rn(acc, a.bias[row]);
         if (lane == 0) a.logits[static_cast<size_t>(b0 + t) * (a.E + 1) + row] = acc;
     }
 }
@@ -263,6 +265,7 @@ cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
                             const float* x, int normalise, int n) {
     BRouterArgs a{};
     a.W = w.w_router;
+    a.bias = w.router_bias;
     a.E = d.E;
     a.n = n;
     a.x = x;
@@ -297,6 +300,7 @@ struct BGroupArgs {
     int* work;            // [0] segments, [1] [2] work counters (reset here)
     int* pair_tok;
     int* pair_of;         // [n][topk+1]
+    unsigned* stats;
     uint32_t* err;
 };
 
@@ -358,6 +362,11 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
     const int e = tid;
     const int cnt = e <= E ? __popcll(mask[e]) : 0;
     const int nsg = (cnt + kSegTok - 1) / kSegTok;
+    __shared__ unsigned s_maxcnt;
+    if (tid == 0) s_maxcnt = 0;
+    __syncthreads();
+    if (e < E && cnt > 0) atomicMax(&s_maxcnt, static_cast<unsigned>(cnt));
+    const int touched = __syncthreads_count(e < E && cnt > 0);
     int total_pairs = 0, total_segs = 0;
     const int p0 = block_excl_scan(cnt, wsum, &total_pairs);
     __syncthreads();
@@ -384,6 +393,10 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
     }
     for (int b = tid; b < n; b += kBGThreads) a.pair_of[b * (topk + 1) + topk] = start[E] + b;
     if (tid == 0) {
+        atomicAdd(a.stats + 0, static_cast<unsigned>(touched));
+        atomicAdd(a.stats + 1, static_cast<unsigned>(total_segs));
+        atomicMax(a.stats + 2, s_maxcnt);
+        atomicAdd(a.stats + 3, 1u);
         if (total_segs > a.max_segs) raise_error(a.err, DM_DEVERR_CAPACITY);
         a.work[0] = min(total_segs, a.max_segs);
         a.work[1] = 0;
@@ -405,6 +418,7 @@ cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchB
     a.work = bb.work;
     a.pair_tok = bb.pair_tok;
     a.pair_of = bb.pair_of;
+    a.stats = bb.stats;
     a.err = b.err;
     const size_t smem = static_cast<size_t>(32) * (d.E + 1) * 4;
     return launch_kernel(lc, b_topk_group_kernel, dim3(1), dim3(kBGThreads), smem, a);

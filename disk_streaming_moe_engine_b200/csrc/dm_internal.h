@@ -63,6 +63,7 @@ struct LayerW {
     const uint16_t* k_norm;          // attn [D]
     const uint16_t* w_out;           // [H][nv*dv] or [H][Hq*D]
     const uint16_t* w_router;        // [E+1][H]
+    const float* router_bias;        // [E] logit offsets of a synthetic workload, or null (none)
     const uint8_t* experts;          // [E] records
     const uint8_t* shared;           // 1 record
 };
@@ -74,6 +75,7 @@ struct Buffers {
     float* ring;          // [n_gdn][max_seqs][4][qkv_dim]
     float* S;             // [n_gdn][max_seqs][nv][dv][dk]
     uint16_t* kv;         // [n_att][num_pages][2][Hkv][16][D]
+    const void* kv_tmap;  // host CUtensorMap: 2-D view of kv (columns D, rows), 16 x 64 boxes
     int* page_table;      // [max_seqs][max_pages]
     int* pos;             // [max_seqs] current length
     int* token;           // [max_seqs] token to embed next
@@ -135,6 +137,9 @@ struct BatchBuffers {
     float* sg;            // [cap] shared-expert gate
     int4* segs;           // [max_segs] (expert, first pair, tokens, 0); expert E = shared
     int* work;            // [4] segments, gate/up work counter, down work counter, spare
+    unsigned* stats;      // [4] routing statistics since the last reset: sum over layer-steps of
+                          //     routed experts touched, sum of segments, max rows of one routed
+                          //     expert, layer-steps
     int* pair_tok;        // [cap (topk + 1)] batch row of each (expert, token) pair
     int* pair_of;         // [cap][topk + 1] pair index of row b's k-th expert (k = topk: shared)
     float* h;             // [cap (topk + 1)][I] SwiGLU activations per pair

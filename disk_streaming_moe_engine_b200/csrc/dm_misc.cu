@@ -110,4 +110,22 @@ cudaError_t launch_synth_f16abs(cudaStream_t st, uint16_t* dst, uint64_t n, uint
     return cudaGetLastError();
 }
 
+// W[r][c] += beta[r] * u[c] for a row-major bf16 matrix (one rounding per element).
+__global__ void rank1_add_bf16_kernel(uint16_t* W, int64_t rows, int cols, const float* beta, const float* u) {
+    const int64_t n = rows * cols;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / cols;
+        const int c = static_cast<int>(i % cols);
+        const float w = __uint_as_float(static_cast<uint32_t>(W[i]) << 16);
+        W[i] = synth_f32_to_bf16(fmaf(beta[r], u[c], w));
+    }
+}
+
+cudaError_t launch_rank1_add_bf16(cudaStream_t st, uint16_t* W, int64_t rows, int cols, const float* beta,
+                                  const float* u) {
+    rank1_add_bf16_kernel<<<grid_for(static_cast<uint64_t>(rows) * cols), 256, 0, st>>>(W, rows, cols, beta, u);
+    return cudaGetLastError();
+}
+
 }  // namespace dm

@@ -37,6 +37,7 @@ struct RouterArgs {
     int* ids;
     float* probs;
     float* shared_g;
+    const float* bias;      // [E] logit offsets, or null
     uint32_t* err;
 };
 
@@ -94,7 +95,8 @@ __global__ void __launch_bounds__(kRouterThreads, 2) router_kernel(const __grid_
     const float4* xlo = reinterpret_cast<const float4*>(xs);
     const float4* xhi = reinterpret_cast<const float4*>(xs + K / 2);
     while (row < r1) {
-        const float acc = canon_router_dot<VPL>(wreg, xlo, xhi, lane);
+        float acc = canon_router_dot<VPL>(wreg, xlo, xhi, lane);
+        if (a.bias && row < a.E) acc = __fadd_rn(acc, a.bias[row]);
         if (lane == 0) lg0[row] = acc;
         row += kRouterThreads / 32;
         if (row < r1) {
@@ -114,6 +116,7 @@ cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
                           const Buffers& b, int slot, int normalise_input) {
     RouterArgs a{};
     a.W = w.w_router;
+    a.bias = w.router_bias;
     a.E = d.E;
     a.topk = d.topk;
     a.x = normalise_input ? b.xmid + static_cast<size_t>(slot) * d.H : b.xn;
@@ -258,6 +261,7 @@ bool moe_supported(int H, int I, int G) {
 //   exit      : the last CTA out resets the flags for the next launch.
 struct MoeFusedArgs {
     const uint16_t* Wr;       // [E+1][H] router rows + shared-gate row
+    const float* rbias;       // [E] logit offsets, or null
     const uint16_t* gamma;    // post-attention norm
     float eps;
     const float* x_mid;       // [H]
@@ -471,6 +475,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 acc = __fmaf_rn(bf16hi(w.w), x1.w, acc);
             }
             acc = warp_sum(acc);
+            if (a.rbias && rrow < a.E) acc = __fadd_rn(acc, a.rbias[rrow]);
             if (lane == 0) {
                 const unsigned bits = __float_as_uint(acc);
                 st_relaxed_u32(reinterpret_cast<unsigned*>(a.logits) + rrow, bits == kLogitEmpty ? 0x7FFFFFFFu : bits);
@@ -887,6 +892,7 @@ cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w
                              const void* next_w, size_t next_bytes) {
     MoeFusedArgs a{};
     a.Wr = w.w_router;
+    a.rbias = w.router_bias;
     a.gamma = w.post_norm;
     a.eps = d.eps;
     a.x_mid = b.xmid + static_cast<size_t>(slot) * d.H;

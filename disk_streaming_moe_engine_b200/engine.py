@@ -324,6 +324,41 @@ class Engine:
         t = np.ascontiguousarray(tokens, np.int32)
         self._ok(self.lib.dm_enqueue_decode_batch(self.ctx, _ptr(s), _ptr(t), s.size, n_steps))
 
+    def batch_read_generated(self, n: int, n_steps: int) -> np.ndarray:
+        out = np.empty((n_steps, n), np.int32)
+        self._ok(self.lib.dm_batch_read_generated(self.ctx, n, n_steps, _ptr(out)))
+        return out
+
+    def batch_stats(self, reset: bool = False) -> dict:
+        """Routing statistics of batched steps since the last reset."""
+        v = np.zeros(4, np.uint32)
+        self._ok(self.lib.dm_batch_stats(self.ctx, int(reset), _ptr(v)))
+        ls = max(int(v[3]), 1)
+        return {"experts_touched_per_layer": float(v[0]) / ls, "segments_per_layer": float(v[1]) / ls,
+                "max_rows_one_expert": int(v[2]), "layer_steps": int(v[3])}
+
+    def time_batch_kernel(self, n: int, which: int, layer: int, iters: int):
+        ms, by = C.c_float(), C.c_uint64()
+        self._ok(self.lib.dm_time_batch_kernel(self.ctx, n, which, layer, iters, C.byref(ms), C.byref(by)))
+        return ms.value, by.value
+
+    def set_router_bias(self, layer: int, bias):
+        """Per-expert router logit offsets (None removes them): a synthetic-workload device."""
+        if bias is None:
+            self._ok(self.lib.dm_set_router_bias(self.ctx, layer, None, 0))
+            return
+        b = np.ascontiguousarray(bias, np.float32)
+        self._ok(self.lib.dm_set_router_bias(self.ctx, layer, _ptr(b), b.size))
+
+    def synth_state(self, seed: int, kv_std: float, state_std: float, length: int):
+        """Seeded synthetic state for every slot (KV pool, GDN states, conv windows), length."""
+        self._ok(self.lib.dm_synth_state_device(self.ctx, seed, kv_std, state_std, length))
+
+    def add_rank1(self, layer: int, tensor_id: int, beta: np.ndarray, u: np.ndarray):
+        beta = np.ascontiguousarray(beta, np.float32)
+        u = np.ascontiguousarray(u, np.float32)
+        self._ok(self.lib.dm_tensor_add_rank1(self.ctx, layer, tensor_id, _ptr(beta), beta.size, _ptr(u), u.size))
+
     def batch_kernels_per_step(self, n: int) -> tuple[int, int]:
         own, gemms = C.c_int32(), C.c_int32()
         self._ok(self.lib.dm_batch_kernels_per_step(self.ctx, n, C.byref(own), C.byref(gemms)))

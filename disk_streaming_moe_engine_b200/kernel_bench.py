@@ -2,6 +2,8 @@
 
     python -m disk_streaming_moe_engine_b200.kernel_bench --preset layer --kernel in_proj \
         --layer 0 --iters 20
+    python -m disk_streaming_moe_engine_b200.kernel_bench --preset layer --kernel battn \
+        --batch 16 --ctx 8192 --iters 5
 
 The model is synthesised on the device; with --warm the layer first runs one real token
 (so router ids, activations and the KV position are those of a real step).  Prints one
@@ -22,12 +24,39 @@ from .engine import Engine
 KERNELS = {"in_proj": _lib.DM_KERNEL_MIXER_IN, "out_proj": _lib.DM_KERNEL_MIXER_OUT,
            "core": _lib.DM_KERNEL_MIXER_CORE, "router": _lib.DM_KERNEL_ROUTER, "moe": _lib.DM_KERNEL_MOE,
            "head": _lib.DM_KERNEL_HEAD}
+# kernels of the batched step (--batch N): layer is the preset's attention or GDN layer
+BKERNELS = {"battn": _lib.DM_BKERNEL_ATTN, "bgdn": _lib.DM_BKERNEL_GDN_REC, "bexperts": _lib.DM_BKERNEL_EXPERTS}
+
+
+def batched(a, cfg):
+    """N sequences of --ctx tokens of synthetic state (permuted page pool), one batched step,
+    then the chosen batched kernel timed alone."""
+    pps = (a.ctx + 64 + 15) // 16
+    rt = RuntimeConfig(max_seqs=a.batch, max_pages_per_seq=pps, kv_num_pages=a.batch * pps)
+    with Engine(cfg, rt) as eng:
+        eng.synth_on_device(a.seed)
+        rng = np.random.default_rng(a.seed)
+        perm = rng.permutation(a.batch * pps).astype(np.int32)
+        for s in range(a.batch):
+            eng.set_page_table(s, perm[s * pps:(s + 1) * pps])
+        eng.synth_state(a.seed, 1.0, 0.1, a.ctx)
+        slots = np.arange(a.batch, dtype=np.int32)
+        eng.decode_batch(slots, rng.integers(0, cfg.vocab_size, a.batch).astype(np.int32))
+        layer = a.layer
+        if a.kernel == "battn":
+            layer = next(l for l in range(cfg.num_hidden_layers) if cfg.is_attention_layer(l))
+        elif a.kernel == "bgdn":
+            layer = next(l for l in range(cfg.num_hidden_layers) if not cfg.is_attention_layer(l))
+        ms, nbytes = eng.time_batch_kernel(a.batch, BKERNELS[a.kernel], layer, a.iters)
+        print(json.dumps({"kernel": a.kernel, "batch": a.batch, "ctx": a.ctx, "layer": layer, "us": ms * 1e3,
+                          "bytes": nbytes, "GBps": nbytes / (ms * 1e-3) / 1e9}))
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--preset", default="layer")
-    ap.add_argument("--kernel", default="in_proj", choices=sorted(KERNELS))
+    ap.add_argument("--kernel", default="in_proj", choices=sorted(KERNELS) + sorted(BKERNELS))
+    ap.add_argument("--batch", type=int, default=0, help="batched-step kernels: sequences per step")
     ap.add_argument("--layer", type=int, default=0)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--ctx", type=int, default=0, help="tokens already in the KV cache / GDN state")
@@ -36,6 +65,10 @@ def main():
     ap.add_argument("--seed", type=int, default=1)
     a = ap.parse_args()
     cfg = preset(a.preset)
+    if a.kernel in BKERNELS:
+        if a.batch <= 0:
+            raise SystemExit("--batch N is required for the batched kernels")
+        return batched(a, cfg)
     with Engine(cfg, RuntimeConfig.for_context(a.ctx + 64)) as eng:
         eng.synth_on_device(a.seed)
         eng.seq_reset(0)

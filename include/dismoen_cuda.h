@@ -306,6 +306,10 @@ int32_t dm_enqueue_decode_batch(dm_ctx* ctx, const int32_t* slots_host, const in
 int32_t dm_batch_read_generated(dm_ctx* ctx, int32_t n, int32_t n_steps, int32_t* tokens_out_host);
 /* Launches per batched step: own kernels and library GEMMs. */
 int32_t dm_batch_kernels_per_step(dm_ctx* ctx, int32_t n, int32_t* own_out, int32_t* gemms_out);
+/* Times `iters` launches of one batched kernel (DM_BKERNEL_*) for the n rows of the last
+ * batched call, each alone after an L2-evicting read; bytes = algorithmic bytes/launch. */
+int32_t dm_time_batch_kernel(dm_ctx* ctx, int32_t n, int32_t which, int32_t layer, int32_t iters, float* avg_ms,
+                             uint64_t* bytes);
 
 /* ---- device-resident entry points (for callers that keep data in HBM) ---------------- */
 /* Enqueues n_steps greedy decode steps for `slot` on the context stream with the input
@@ -331,6 +335,10 @@ int32_t dm_kernels_per_step(dm_ctx* ctx, int32_t* out);
 #define DM_KERNEL_ROUTER 3     /* router + top-k alone (the dm_router kernel)           */
 #define DM_KERNEL_MOE 4        /* the whole MoE mixer: router, experts, residual        */
 #define DM_KERNEL_HEAD 6
+/* kernels of the batched step for dm_time_batch_kernel */
+#define DM_BKERNEL_ATTN 0      /* batched paged decode attention of an attention layer  */
+#define DM_BKERNEL_GDN_REC 1   /* batched GDN recurrence of a GDN layer                  */
+#define DM_BKERNEL_EXPERTS 2   /* gate/up + down expert kernels (last layer's grouping)  */
 int32_t dm_time_kernel(dm_ctx* ctx, int32_t which, int32_t layer, int32_t iters, float* avg_ms,
                        uint64_t* bytes);
 
@@ -411,6 +419,21 @@ int32_t dm_synth_u8(uint64_t seed, uint64_t stream_id, uint64_t n, uint8_t* out_
 /* fp16 |N(0, std)| scales */
 int32_t dm_synth_f16_absnormal(uint64_t seed, uint64_t stream_id, uint64_t n, float std,
                                uint16_t* out_host);
+/* Seeded synthetic sequence state for every slot (benchmarks): the whole KV page pool bf16
+ * N(0, kv_std), every GDN state and conv window fp32 N(0, state_std); every slot's length
+ * becomes len.  Page tables are unchanged. */
+int32_t dm_synth_state_device(dm_ctx* ctx, uint64_t seed, float kv_std, float state_std, int32_t len);
+/* W += beta u^T on an uploaded bf16 dense tensor (rows x cols), one rounding per element. */
+int32_t dm_tensor_add_rank1(dm_ctx* ctx, int32_t layer, int32_t tensor_id, const float* beta_host, int64_t rows,
+                            const float* u_host, int32_t cols);
+/* Routing statistics of batched steps since the last reset: [0] sum over (layer, step) of
+ * routed experts touched, [1] sum of expert segments, [2] max rows of one routed expert,
+ * [3] (layer, step) count.  reset != 0 clears them afterwards; out4 may be NULL. */
+int32_t dm_batch_stats(dm_ctx* ctx, int32_t reset, uint32_t* out4);
+/* Per-expert router logit offsets of layer `layer` (n == num_experts values), added after
+ * the canonical dot product; NULL removes them.  Not part of the reference model (whose
+ * router has no bias): a synthetic-workload device to draw a skewed expert load. */
+int32_t dm_set_router_bias(dm_ctx* ctx, int32_t layer, const float* bias_host, int32_t n);
 /* Fills every weight of the context with the synthetic distributions of the benchmark
  * configs directly on the device (same generator; used for multi-GB models). */
 int32_t dm_synth_model_device(dm_ctx* ctx, uint64_t seed);
