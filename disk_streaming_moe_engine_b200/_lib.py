@@ -25,6 +25,7 @@ DM_ERR_ROUTER = 9
 DM_KERNEL_MIXER_IN, DM_KERNEL_MIXER_OUT, DM_KERNEL_MIXER_CORE = 0, 1, 2
 DM_KERNEL_ROUTER, DM_KERNEL_MOE, DM_KERNEL_HEAD = 3, 4, 6
 DM_BKERNEL_ATTN, DM_BKERNEL_GDN_REC, DM_BKERNEL_EXPERTS = 0, 1, 2
+DM_EP_HANDLE_BYTES = 64
 
 DM_DTYPE_BF16 = 0
 DM_DTYPE_F32 = 1
@@ -114,6 +115,9 @@ SIGNATURES = {
     "dm_tensor_add_rank1": (I32, [P, I32, I32, P, C.c_int64, P, I32]),
     "dm_batch_stats": (I32, [P, I32, P]),
     "dm_set_router_bias": (I32, [P, I32, P, I32]),
+    "dm_ep_ipc_handle": (I32, [P, P]),
+    "dm_ep_attach": (I32, [P, I32, I32, P]),
+    "dm_ep_detach": (I32, [P]),
     "dm_time_batch_kernel": (I32, [P, I32, I32, I32, I32, C.POINTER(F32), C.POINTER(U64)]),
 }
 

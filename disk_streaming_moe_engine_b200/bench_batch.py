@@ -88,91 +88,127 @@ def step_bytes_c3(cfg, B: int, ctx_mid: int, experts_per_layer: float) -> dict:
 
 
 def run(args, rank, local, world):
+    import datetime
+
     import torch
 
-    from . import Engine, RuntimeConfig, _lib, build, preset
+    from . import Engine, RuntimeConfig, _lib, build, ep, preset
     from bench import ClockSampler, measured_peak  # noqa: the repo root is on sys.path (bench.py)
 
     build.build()
-    if world > 1:
-        raise SystemExit("config 3 runs on one GPU here (expert-parallel multi-GPU is not built)")
     torch.cuda.set_device(local)
+    dist = None
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    def rank_max(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
     cfg = preset("full")
     B, L, K, W = args.batch, args.c3_ctx, args.steps, args.warmup
+    rows = ep.rows_of_rank(B, rank, world)   # this rank's sequences
+    n = len(rows)
     pps = (L + W + 2 * K + 64 + 15) // 16
-    rt = RuntimeConfig(max_seqs=B, max_pages_per_seq=pps, kv_num_pages=B * pps)
+    rt = RuntimeConfig(max_seqs=n, max_pages_per_seq=pps, kv_num_pages=n * pps)
     eng = Engine(cfg, rt, device=local)
     t0 = time.perf_counter()
-    eng.synth_on_device(3)
+    eng.synth_on_device(3)             # the same weights on every rank
     eng.weights_check()
     skew = apply_router_skew(eng, cfg, args.router_skew, 3) if args.router_skew > 0 else None
-    rng = np.random.default_rng(3)
-    perm = rng.permutation(B * pps).astype(np.int32)
-    for sl in range(B):
+    rng = np.random.default_rng(3 + rank)
+    perm = rng.permutation(n * pps).astype(np.int32)
+    for sl in range(n):
         eng.set_page_table(sl, perm[sl * pps:(sl + 1) * pps])
-    eng.synth_state(3, 1.0, 0.1, L)
+    eng.synth_state(3 + rank, 1.0, 0.1, L)
+    if dist is not None:
+        ep.attach_group(eng, dist)
     setup_s = time.perf_counter() - t0
-    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
-    slots = np.arange(B, dtype=np.int32)
-    toks = rng.integers(0, cfg.vocab_size, B).astype(np.int32)
+    stream = torch.cuda.ExternalStream(eng.stream(), device=dev)
+    slots = np.arange(n, dtype=np.int32)
+    toks = rng.integers(0, cfg.vocab_size, n).astype(np.int32)
 
     eng.enqueue_decode_batch(slots, toks, W)
     eng.sync()
-    toks = eng.batch_read_generated(B, W)[-1].copy()
+    toks = eng.batch_read_generated(n, W)[-1].copy()
     eng.batch_stats(reset=True)
 
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
+    barrier()
     with ClockSampler(local) as clocks:
         ev0.record(stream)
         eng.enqueue_decode_batch(slots, toks, K)
         ev1.record(stream)
         ev1.synchronize()
     eng.sync()
-    ms = ev0.elapsed_time(ev1)
+    barrier()
+    ms = rank_max(ev0.elapsed_time(ev1))
     routing = eng.batch_stats(reset=True)
-    toks = eng.batch_read_generated(B, K)[-1].copy()
+    toks = eng.batch_read_generated(n, K)[-1].copy()
     value = B * K / (ms / 1e3)
 
     # e2e: one dm_decode_batch call per step, host token buffers in and out
-    torch.cuda.synchronize()
+    barrier()
     with ClockSampler(local, 0.02) as clocks_e2e:
         ev0.record(stream)
         for _ in range(K):
             toks, _ = eng.decode_batch(slots, toks)
         ev1.record(stream)
         ev1.synchronize()
-    ms_e2e = ev0.elapsed_time(ev1)
+    barrier()
+    ms_e2e = rank_max(ev0.elapsed_time(ev1))
     e2e = B * K / (ms_e2e / 1e3)
 
     peak, peak_kind = measured_peak()
-    kernels = {}
-    for name, which, layer in (("attn", _lib.DM_BKERNEL_ATTN, 3), ("gdn_rec", _lib.DM_BKERNEL_GDN_REC, 0),
-                               ("experts", _lib.DM_BKERNEL_EXPERTS, cfg.num_hidden_layers - 1)):
-        kms, kb = eng.time_batch_kernel(B, which, layer, 5)
-        kernels[name] = {"us": round(kms * 1e3, 1), "bytes": kb, "GBps": round(kb / kms / 1e6, 1),
-                         "frac": round(kb / kms / 1e6 / peak, 3)}
-    dom = kernels["attn"]
-    achieved = dom["bytes"] / (dom["us"] * 1e-6) / 1e9
+    kernels = None
+    roofline = None
+    if world == 1:  # kernels timed alone (in a group the ranks would not stay in step)
+        kernels = {}
+        for name, which, layer in (("attn", _lib.DM_BKERNEL_ATTN, 3), ("gdn_rec", _lib.DM_BKERNEL_GDN_REC, 0),
+                                   ("experts", _lib.DM_BKERNEL_EXPERTS, cfg.num_hidden_layers - 1)):
+            kms, kb = eng.time_batch_kernel(n, which, layer, 5)
+            kernels[name] = {"us": round(kms * 1e3, 1), "bytes": kb, "GBps": round(kb / kms / 1e6, 1),
+                             "frac": round(kb / kms / 1e6 / peak, 3)}
+        dom = kernels["attn"]
+        achieved = dom["bytes"] / (dom["us"] * 1e-6) / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                    "traffic": None, "peak_source": peak_kind,
+                    "kernel": "attn_decode_warp_kernel<256,8> (layer 3): every cached K/V byte of the "
+                              f"{n} sequences, timed alone after an L2 flush"}
     ctx_mid = L + W + K // 2
-    sb = step_bytes_c3(cfg, B, ctx_mid, routing["experts_touched_per_layer"])
-    own, gemms = eng.batch_kernels_per_step(B)
+    # bytes one rank moves per step: its sequences' KV and state, the replicated dense
+    # weights, the experts it computes (touched experts counted per rank)
+    sb = step_bytes_c3(cfg, n, ctx_mid, routing["experts_touched_per_layer"])
+    own, gemms = eng.batch_kernels_per_step(n)
+    if world > 1:
+        own += cfg.num_hidden_layers  # the cross-rank barrier kernel of every MoE layer
     line = {
         "metric": "decode tok/s, 35B-A3B-shape 4-bit, bs64", "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights and sequence state on device, seed 3)",
         "config": {"workload": f"config3: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit g64 experts, {B} sequences "
                                f"x {L} cached tokens, paged (16-token pages, permuted pool)",
-                   "global_batch": B, "seq_len": L, "parallelism": "1 GPU",
+                   "global_batch": B, "seq_len": L,
+                   "parallelism": "1 GPU" if world == 1 else
+                   f"expert-parallel x{world}: {n} sequences and {cfg.num_experts // world} experts per GPU, "
+                   "dense weights replicated, dispatch/combine through peer memory",
                    "l2": "inputs larger than L2 (tens of GB of KV per step)",
                    "router_skew": skew},
-        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B + 4},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": None, "peak_source": peak_kind,
-                     "kernel": "attn_decode_kernel<256,8,3> batched (layer 3): every cached K/V byte of the "
-                               f"{B} sequences, timed alone after an L2 flush"},
-        "step_roofline": {"bytes_per_step": sb, "achieved_GBps": sb["total"] / (ms / K / 1e3) / 1e9,
+        "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B + 4 * world},
+        "roofline": roofline,
+        "step_roofline": {"bytes_per_step_per_gpu": sb, "achieved_GBps_per_gpu": sb["total"] / (ms / K / 1e3) / 1e9,
                           "frac": sb["total"] / (ms / K / 1e3) / 1e9 / peak},
         "kernels": kernels,
         "routing": routing,
@@ -182,7 +218,13 @@ def run(args, rank, local, world):
         "library_gemms": gemms * K,
         "context_setup_s": round(setup_s, 2),
     }
+    if dist is not None:
+        barrier()
+        eng.ep_detach()
     eng.close()
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0

@@ -90,6 +90,8 @@ struct dm_ctx {
     std::vector<cudaGraphExec_t> bgraphs;  // [2 * (cap + 1)]
     int* h_bio = nullptr;                  // pinned [4 * kMaxBatch]: slots, tokens in, tokens out
     float* rbias = nullptr;                // [L][E] router logit offsets (dm_set_router_bias)
+    // expert-parallel group: the peers' arenas mapped into this process (null for self)
+    std::vector<uint8_t*> peer_arena;
     bool use_pdl = true;       // programmatic dependent launch between step kernels
     bool gdn_fused = true;     // GDN recurrence + output projection as one kernel
     bool l2_prefetch = false;  // latency-bound kernels prefetch upcoming weights into L2 (off:
@@ -225,6 +227,9 @@ struct Plan {
     }
 };
 
+// The expert-parallel view of a context that is not part of a group: one rank, local buffers.
+static void set_local_ep(dm_ctx* c);
+
 static int plan_memory(dm_ctx* c, bool commit) {
     Dims& d = c->d;
     Plan p;
@@ -288,8 +293,10 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t kmax = std::max({static_cast<size_t>(d.H), static_cast<size_t>(d.z_dim), static_cast<size_t>(d.Hq) * d.D});
     const size_t nmax = std::max({static_cast<size_t>(d.gdn_in_rows), static_cast<size_t>(d.attn_in_rows),
                                   static_cast<size_t>(d.H), static_cast<size_t>(d.V)});
-    const size_t P = BC * (d.topk + 1);
-    const int max_segs = static_cast<int>((P + kSegTok - 1) / kSegTok) + std::min(d.E, static_cast<int>(BC) * d.topk) + 2;
+    // pairs one rank may compute: the routed choices of every row of a full group that land
+    // on its experts, plus its own rows for the shared expert
+    const size_t P = static_cast<size_t>(kMaxRanks) * BC * d.topk + BC;
+    const int max_segs = static_cast<int>((P + kSegTok - 1) / kSegTok) + std::min(d.E, static_cast<int>(P)) + 2;
     const int bgen_cap = 1 << 16;
     const size_t ob_slots = T(BC * 4), ob_tok = T(BC * 4), ob_x = T(BC * H * 4), ob_xm = T(BC * H * 4);
     const size_t ob_xcat = T(2 * BC * kmax * 2), ob_c = T(2 * BC * nmax * 4);
@@ -299,7 +306,8 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t ob_acnt = T(BC * d.Hkv * 4), ob_xn = T(BC * H * 4), ob_lg = T(BC * (d.E + 1) * 4);
     const size_t ob_ids = T(BC * d.topk * 4), ob_pr = T(BC * d.topk * 4), ob_sg = T(BC * 4);
     const size_t ob_segs = T(static_cast<size_t>(max_segs) * 16), ob_work = T(16), ob_stats = T(16);
-    const size_t ob_ptok = T(P * 4), ob_pof = T(P * 4), ob_h = T(P * d.I * 4), ob_epart = T(P * H * 4);
+    const size_t ob_psrc = T(P * 4), ob_h = T(P * d.I * 4), ob_eout = T(BC * (d.topk + 1) * H * 4);
+    const size_t ob_flags = T(2 * kMaxRanks * 4), ob_epoch = T(2 * 4);
     const size_t ob_cv = T(BC * kHeadChunks * 4), ob_ci = T(BC * kHeadChunks * 4), ob_hl = T(BC * d.V * 4);
     const size_t ob_gen = T(static_cast<size_t>(bgen_cap) * 4), ob_genidx = T(4);
     const size_t o_rbias = T(static_cast<size_t>(d.L) * d.E * 4);
@@ -400,16 +408,19 @@ static int plan_memory(dm_ctx* c, bool commit) {
     bb.segs = reinterpret_cast<int4*>(A + ob_segs);
     bb.work = reinterpret_cast<int*>(A + ob_work);
     bb.stats = reinterpret_cast<unsigned*>(A + ob_stats);
-    bb.pair_tok = reinterpret_cast<int*>(A + ob_ptok);
-    bb.pair_of = reinterpret_cast<int*>(A + ob_pof);
+    bb.pair_src = reinterpret_cast<int*>(A + ob_psrc);
+    bb.max_pairs = static_cast<int>(P);
+    bb.ep_flags = reinterpret_cast<unsigned*>(A + ob_flags);
+    bb.ep_epoch = reinterpret_cast<unsigned*>(A + ob_epoch);
     bb.h = reinterpret_cast<float*>(A + ob_h);
-    bb.part = reinterpret_cast<float*>(A + ob_epart);
+    bb.eout = reinterpret_cast<float*>(A + ob_eout);
     bb.cand_val = reinterpret_cast<float*>(A + ob_cv);
     bb.cand_idx = reinterpret_cast<int*>(A + ob_ci);
     bb.head_logits = reinterpret_cast<float*>(A + ob_hl);
     bb.gen_out = reinterpret_cast<int*>(A + ob_gen);
     bb.gen_idx = reinterpret_cast<int*>(A + ob_genidx);
     bb.gen_cap = bgen_cap;
+    set_local_ep(c);
     c->blas_ws = A + ob_ws;
     c->rbias = reinterpret_cast<float*>(A + o_rbias);
     c->blas_ws_bytes = blas_ws;
@@ -461,6 +472,18 @@ static void host_parallel(uint64_t n, F&& f) {
         th.emplace_back([=, &f] { f(a, b); });
     }
     for (auto& x : th) x.join();
+}
+
+static void set_local_ep(dm_ctx* c) {
+    BatchBuffers& bb = c->bb;
+    EpView v{};
+    v.rank = 0;
+    v.world = 1;
+    v.ids[0] = bb.ids;
+    v.xn[0] = bb.xn;
+    v.eout[0] = bb.eout;
+    v.flags[0] = bb.ep_flags;
+    bb.ep = v;
 }
 
 // Tensor map of the KV arena for the attention kernel's page copies: rows of D bf16
@@ -623,6 +646,8 @@ int32_t dm_ctx_destroy(dm_ctx* c) {
         if (g) cudaGraphExecDestroy(g);
     for (auto& g : c->bgraphs)
         if (g) cudaGraphExecDestroy(g);
+    for (uint8_t* pa : c->peer_arena)
+        if (pa) cudaIpcCloseMemHandle(pa);
     if (c->blas) cublasDestroy(c->blas);
     if (c->h_bio) cudaFreeHost(c->h_bio);
     if (c->arena) cudaFree(c->arena);
@@ -1256,6 +1281,7 @@ static cudaError_t enqueue_batch_step(dm_ctx* c, int n, int write_logits) {
         if (e == cudaSuccess) e = launch_b_router(lc, d, w, bb, bb.xm, 1, n);
         if (e == cudaSuccess) e = launch_b_topk_group(lc, d, bb, c->b, n);
         if (e == cudaSuccess) e = launch_b_experts(lc, d, w, bb, c->b, n);
+        if (e == cudaSuccess && bb.ep.world > 1) e = launch_ep_barrier(lc, bb, c->b, 1);
         if (e == cudaSuccess) e = launch_b_combine(lc, d, bb, bb.xm, bb.x, n);
     }
     if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, c->final_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
@@ -1360,6 +1386,77 @@ int32_t dm_set_router_bias(dm_ctx* c, int32_t layer, const float* bias, int32_t 
     if (bias) DM_CUDA(c, cudaMemcpy(dst, bias, sizeof(float) * n, cudaMemcpyHostToDevice), "router");
     drop_graphs(c);
     c->layers[layer].router_bias = bias ? dst : nullptr;
+    return DM_OK;
+}
+
+// ---- expert-parallel group ------------------------------------------------------------
+int32_t dm_ep_ipc_handle(dm_ctx* c, void* handle_out) {
+    if (!c || !handle_out) return DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    cudaIpcMemHandle_t h;
+    DM_CUDA(c, cudaIpcGetMemHandle(&h, c->arena), "ep");
+    static_assert(sizeof(cudaIpcMemHandle_t) == DM_EP_HANDLE_BYTES, "handle size");
+    memcpy(handle_out, &h, sizeof h);
+    return DM_OK;
+}
+
+static void ep_close(dm_ctx* c) {
+    for (uint8_t*& pa : c->peer_arena)
+        if (pa) cudaIpcCloseMemHandle(pa), pa = nullptr;
+    c->peer_arena.clear();
+}
+
+int32_t dm_ep_attach(dm_ctx* c, int32_t rank, int32_t world, const void* handles) {
+    if (!c || !handles) return DM_ERR_INVALID_ARG;
+    const Dims& d = c->d;
+    if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+        return set_err(c, DM_ERR_INVALID_ARG, "EP_ERROR", "ep", -1, "rank %d of %d outside [0, world <= %d)", rank, world, kMaxRanks);
+    if (d.E % world != 0)
+        return set_err(c, DM_ERR_INVALID_ARG, "EP_ERROR", "ep", -1, "num_experts %d not divisible by world %d", d.E, world);
+    cudaSetDevice(c->device);
+    drop_graphs(c);
+    ep_close(c);
+    c->peer_arena.assign(world, nullptr);
+    BatchBuffers& bb = c->bb;
+    const uint8_t* A = c->arena;
+    auto off = [&](const void* p) { return static_cast<size_t>(static_cast<const uint8_t*>(p) - A); };
+    EpView v{};
+    v.rank = rank;
+    v.world = world;
+    for (int q = 0; q < world; ++q) {
+        uint8_t* base = c->arena;
+        if (q != rank) {
+            cudaIpcMemHandle_t h;
+            memcpy(&h, static_cast<const uint8_t*>(handles) + static_cast<size_t>(q) * DM_EP_HANDLE_BYTES, sizeof h);
+            void* p = nullptr;
+            cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess) {
+                ep_close(c);
+                set_local_ep(c);
+                return set_err(c, DM_ERR_CUDA, "EP_ERROR", "ep", -1, "opening rank %d's memory: %s", q, cudaGetErrorString(e));
+            }
+            base = static_cast<uint8_t*>(p);
+            c->peer_arena[q] = base;
+        }
+        v.ids[q] = reinterpret_cast<const int*>(base + off(bb.ids));
+        v.xn[q] = reinterpret_cast<const float*>(base + off(bb.xn));
+        v.eout[q] = reinterpret_cast<float*>(base + off(bb.eout));
+        v.flags[q] = reinterpret_cast<unsigned*>(base + off(bb.ep_flags));
+    }
+    bb.ep = v;
+    // barriers start from zero on every rank (the caller joins the ranks after this call)
+    DM_CUDA(c, cudaMemset(bb.ep_flags, 0, 2 * kMaxRanks * 4), "ep");
+    DM_CUDA(c, cudaMemset(bb.ep_epoch, 0, 2 * 4), "ep");
+    DM_CUDA(c, cudaDeviceSynchronize(), "ep");
+    return DM_OK;
+}
+
+int32_t dm_ep_detach(dm_ctx* c) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    cudaSetDevice(c->device);
+    drop_graphs(c);
+    ep_close(c);
+    set_local_ep(c);
     return DM_OK;
 }
 

@@ -287,24 +287,30 @@ cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
 
 // ---- top-k per row + grouping of the (expert, row) pairs by expert ---------------------
 // One CTA of 1024 threads.  Warp w selects for rows w, w + 32 (canonical softmax/top-k).
-// Then the pairs are grouped by expert in a fixed order: expert ascending (the shared
-// expert, id E, last), rows ascending within an expert (64-bit row masks make the rank of
-// a pair a population count).  Each expert's rows are cut into segments of kSegTok.
+// In an expert-parallel group the ranks then meet at barrier 0 (every rank's ids and
+// normalised rows are published).  Then this rank's experts gather their pairs from the
+// rows of every rank in a fixed order: expert ascending (the shared expert, id E, last, for
+// this rank's own rows), source row ascending (source = rank * n + row; a bit mask of the
+// sources of each expert makes the rank of a pair a population count).  Each expert's
+// pairs are cut into segments of kSegTok.
 struct BGroupArgs {
     const float* logits;  // [n][E+1]
-    int E, topk, n, max_segs;
+    int E, topk, n, max_segs, max_pairs;
     int* ids;
     float* probs;
     float* sg;
     int4* segs;
     int* work;            // [0] segments, [1] [2] work counters (reset here)
-    int* pair_tok;
-    int* pair_of;         // [n][topk+1]
+    int* pair_src;
     unsigned* stats;
+    EpView ep;
+    unsigned* my_flags;   // [2][kMaxRanks]
+    unsigned* epoch;      // [2]
     uint32_t* err;
 };
 
 constexpr int kBGThreads = 1024;
+constexpr int kBGMaskWords = 2048;    // (experts of a rank) x (mask words) <= 2 E <= 2046
 
 // Exclusive prefix sum of v over the 1024 threads (fixed order); *total gets the sum.
 DM_DEV int block_excl_scan(int v, int* wsum, int* total) {
@@ -332,14 +338,63 @@ DM_DEV int block_excl_scan(int v, int* wsum, int* total) {
     return base + incl - v;
 }
 
+DM_DEV void st_release_sys_u32(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+DM_DEV unsigned ld_acquire_sys_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Barrier `kind` of the expert-parallel group, by the first warp of the calling CTA
+// (every thread of the CTA calls it): this rank's epoch advances by one, lane q signals
+// rank q, then waits (bounded) until every rank has signalled this epoch.  False on timeout.
+DM_DEV bool ep_barrier(const EpView& ep, unsigned* my_flags, unsigned* epoch, int kind, uint32_t* err) {
+    __shared__ unsigned s_epoch;
+    __shared__ int s_ok;
+    __threadfence_system();  // this thread's writes before the signal
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        s_epoch = epoch[kind] + 1u;
+        epoch[kind] = s_epoch;
+        s_ok = 1;
+    }
+    __syncthreads();
+    const unsigned e = s_epoch;
+    if (threadIdx.x < 32) {
+        const int q = threadIdx.x;
+        if (q < ep.world) st_release_sys_u32(ep.flags[q] + kind * kMaxRanks + ep.rank, e);
+        if (q < ep.world) {
+            const unsigned* f = my_flags + kind * kMaxRanks + q;
+            if (ld_acquire_sys_u32(f) < e) {
+                const uint64_t t0 = globaltimer_ns();
+                uint32_t it = 0;
+                while (ld_acquire_sys_u32(f) < e) {
+                    if ((++it & 255u) == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
+                        raise_error(err, DM_DEVERR_TIMEOUT);
+                        s_ok = 0;
+                        break;
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    __threadfence_system();  // the peers' writes before their signals are visible from here
+    return s_ok != 0;
+}
+
 __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __grid_constant__ BGroupArgs a) {
-    extern __shared__ __align__(16) float lgw[];   // [32][E+1]
-    __shared__ unsigned long long mask[1024];       // per expert (E <= 1023) + shared
-    __shared__ int sids[kMaxBatch * kMaxTopK];
-    __shared__ int start[1024];
+    extern __shared__ __align__(16) float lgw[];   // [32][E+1], then the ids of every source row
+    __shared__ unsigned long long mask[kBGMaskWords];
+    __shared__ int start[1025];
     __shared__ int wsum[32];
+    __shared__ unsigned s_maxcnt;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int E = a.E, topk = a.topk, n = a.n;
+    const int world = a.ep.world, rank = a.ep.rank;
+    int* sids = reinterpret_cast<int*>(lgw + static_cast<size_t>(32) * (E + 1));  // [world][n][topk]
     pdl_wait();
     for (int b = warp; b < n; b += 32) {
         float* lg = lgw + static_cast<size_t>(warp) * (E + 1);
@@ -347,61 +402,80 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
         for (int e = lane; e <= E; e += 32) lg[e] = src[e];
         __syncwarp();
         canon_softmax_topk_warp(lg, E, topk, a.ids + b * topk, a.probs + b * topk, a.sg + b, a.err);
-        if (lane < topk) sids[b * topk + lane] = a.ids[b * topk + lane];
-        __syncwarp();
     }
-    for (int e = tid; e <= E; e += kBGThreads) mask[e] = 0ull;
-    __syncthreads();
+    if (world > 1) ep_barrier(a.ep, a.my_flags, a.epoch, 0, a.err);
+    else __syncthreads();
     pdl_launch_dependents();
-    for (int i = tid; i < n * topk; i += kBGThreads) {
-        const int e = sids[i];
-        atomicOr(&mask[e], 1ull << (i / topk));
+
+    const int Eo = E / world, e0 = rank * Eo;     // this rank's experts
+    const int nsrc = world * n;
+    const int words = (nsrc + 63) / 64;
+    for (int i = tid; i < nsrc * topk; i += kBGThreads) {
+        const int q = i / (n * topk), r = i % (n * topk);
+        sids[i] = a.ep.ids[q][r];                  // the rows of rank q (local when q == rank)
     }
-    if (tid == 0) mask[E] = n >= 64 ? ~0ull : ((1ull << n) - 1ull);
-    __syncthreads();
-    const int e = tid;
-    const int cnt = e <= E ? __popcll(mask[e]) : 0;
-    const int nsg = (cnt + kSegTok - 1) / kSegTok;
-    __shared__ unsigned s_maxcnt;
+    for (int i = tid; i < Eo * words; i += kBGThreads) mask[i] = 0ull;
     if (tid == 0) s_maxcnt = 0;
     __syncthreads();
-    if (e < E && cnt > 0) atomicMax(&s_maxcnt, static_cast<unsigned>(cnt));
-    const int touched = __syncthreads_count(e < E && cnt > 0);
+    for (int i = tid; i < nsrc * topk; i += kBGThreads) {
+        const int e = sids[i] - e0;
+        if (e >= 0 && e < Eo) {
+            const int src = i / topk;
+            atomicOr(&mask[e * words + (src >> 6)], 1ull << (src & 63));
+        }
+    }
+    __syncthreads();
+    // thread el: routed expert e0 + el (el < Eo) or the shared expert (el == Eo)
+    const int el = tid;
+    int cnt = 0;
+    if (el < Eo)
+        for (int w = 0; w < words; ++w) cnt += __popcll(mask[el * words + w]);
+    else if (el == Eo)
+        cnt = n;
+    const int nsg = (cnt + kSegTok - 1) / kSegTok;
+    if (el < Eo && cnt > 0) atomicMax(&s_maxcnt, static_cast<unsigned>(cnt));
+    const int touched = __syncthreads_count(el < Eo && cnt > 0);
     int total_pairs = 0, total_segs = 0;
     const int p0 = block_excl_scan(cnt, wsum, &total_pairs);
     __syncthreads();
     const int s0 = block_excl_scan(nsg, wsum, &total_segs);
-    if (e <= E) {
-        start[e] = p0;
-        unsigned long long m = mask[e];
-        int j = 0;
-        while (m) {
-            const int b = __ffsll(static_cast<long long>(m)) - 1;
-            m &= m - 1ull;
-            a.pair_tok[p0 + j] = b;
-            ++j;
-        }
-        for (int s = 0; s < nsg; ++s)
-            if (s0 + s < a.max_segs) a.segs[s0 + s] = make_int4(e, p0 + s * kSegTok, min(kSegTok, cnt - s * kSegTok), 0);
+    const bool pairs_ok = total_pairs <= a.max_pairs && total_segs <= a.max_segs;
+    if (el <= Eo) {
+        start[el] = p0;
+        const int gexp = el < Eo ? e0 + el : E;
+        if (pairs_ok)
+            for (int s2 = 0; s2 < nsg; ++s2)
+                a.segs[s0 + s2] = make_int4(gexp, p0 + s2 * kSegTok, min(kSegTok, cnt - s2 * kSegTok), 0);
     }
     __syncthreads();
-    for (int i = tid; i < n * topk; i += kBGThreads) {
-        const int b = i / topk, k = i % topk;
-        const int ex = sids[i];
-        const unsigned long long below = b == 0 ? 0ull : (mask[ex] & (~0ull >> (64 - b)));
-        a.pair_of[b * (topk + 1) + k] = start[ex] + __popcll(below);
+    if (pairs_ok) {
+        for (int i = tid; i < nsrc * topk; i += kBGThreads) {
+            const int e = sids[i] - e0;
+            if (e >= 0 && e < Eo) {
+                const int src = i / topk, k = i % topk;
+                const unsigned long long* m = mask + e * words;
+                int below = 0;
+                for (int w = 0; w < (src >> 6); ++w) below += __popcll(m[w]);
+                below += __popcll(m[src >> 6] & ((1ull << (src & 63)) - 1ull));
+                a.pair_src[start[e] + below] = src * 32 + k;
+            }
+        }
+        for (int b = tid; b < n; b += kBGThreads) a.pair_src[start[Eo] + b] = (rank * n + b) * 32 + topk;
     }
-    for (int b = tid; b < n; b += kBGThreads) a.pair_of[b * (topk + 1) + topk] = start[E] + b;
     if (tid == 0) {
         atomicAdd(a.stats + 0, static_cast<unsigned>(touched));
         atomicAdd(a.stats + 1, static_cast<unsigned>(total_segs));
         atomicMax(a.stats + 2, s_maxcnt);
         atomicAdd(a.stats + 3, 1u);
-        if (total_segs > a.max_segs) raise_error(a.err, DM_DEVERR_CAPACITY);
-        a.work[0] = min(total_segs, a.max_segs);
+        if (!pairs_ok) raise_error(a.err, DM_DEVERR_CAPACITY);
+        a.work[0] = pairs_ok ? total_segs : 0;
         a.work[1] = 0;
         a.work[2] = 0;
     }
+}
+
+size_t b_topk_group_smem(int E, int topk) {
+    return static_cast<size_t>(32) * (E + 1) * 4 + static_cast<size_t>(kMaxRanks) * kMaxBatch * topk * 4;
 }
 
 cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n) {
@@ -411,24 +485,38 @@ cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchB
     a.topk = d.topk;
     a.n = n;
     a.max_segs = bb.max_segs;
+    a.max_pairs = bb.max_pairs;
     a.ids = bb.ids;
     a.probs = bb.probs;
     a.sg = bb.sg;
     a.segs = bb.segs;
     a.work = bb.work;
-    a.pair_tok = bb.pair_tok;
-    a.pair_of = bb.pair_of;
+    a.pair_src = bb.pair_src;
     a.stats = bb.stats;
+    a.ep = bb.ep;
+    a.my_flags = bb.ep_flags;
+    a.epoch = bb.ep_epoch;
     a.err = b.err;
-    const size_t smem = static_cast<size_t>(32) * (d.E + 1) * 4;
-    return launch_kernel(lc, b_topk_group_kernel, dim3(1), dim3(kBGThreads), smem, a);
+    return launch_kernel(lc, b_topk_group_kernel, dim3(1), dim3(kBGThreads), b_topk_group_smem(d.E, d.topk), a);
 }
 
-// ---- combine: out[b] = xm[b] + sum_k p_k part[pair(b,k)] + g_sh part[pair(b,shared)] -----
+// Barrier 1 of the expert-parallel group: every rank's experts have written their results
+// into the source ranks' expert-output buffers.
+__global__ void __launch_bounds__(32) ep_barrier_kernel(const __grid_constant__ EpView ep, unsigned* my_flags,
+                                                        unsigned* epoch, int kind, uint32_t* err) {
+    pdl_wait();
+    ep_barrier(ep, my_flags, epoch, kind, err);
+    pdl_launch_dependents();
+}
+
+cudaError_t launch_ep_barrier(const LaunchCfg& lc, const BatchBuffers& bb, const Buffers& b, int kind) {
+    return launch_kernel(lc, ep_barrier_kernel, dim3(1), dim3(32), 0, bb.ep, bb.ep_flags, bb.ep_epoch, kind, b.err);
+}
+
+// ---- combine: out[b] = xm[b] + sum_k p_k eout[b][k] + g_sh eout[b][topk] -------------------
 struct BCombineArgs {
     const float* xm;
-    const float* part;
-    const int* pair_of;
+    const float* eout;
     const float* probs;
     const float* sg;
     float* out;
@@ -441,11 +529,10 @@ __global__ void __launch_bounds__(256) b_combine_kernel(const __grid_constant__ 
     pdl_wait();
     pdl_launch_dependents();
     if (i >= a.H) return;
-    const int* po = a.pair_of + b * (a.topk + 1);
+    const float* eo = a.eout + static_cast<size_t>(b) * (a.topk + 1) * a.H + i;
     float acc = 0.0f;
-    for (int k = 0; k < a.topk; ++k)
-        acc = fmaf(a.probs[b * a.topk + k], a.part[static_cast<size_t>(po[k]) * a.H + i], acc);
-    acc = fmaf(a.sg[b], a.part[static_cast<size_t>(po[a.topk]) * a.H + i], acc);
+    for (int k = 0; k < a.topk; ++k) acc = fmaf(a.probs[b * a.topk + k], eo[static_cast<size_t>(k) * a.H], acc);
+    acc = fmaf(a.sg[b], eo[static_cast<size_t>(a.topk) * a.H], acc);
     a.out[static_cast<size_t>(b) * a.H + i] = a.xm[static_cast<size_t>(b) * a.H + i] + acc;
 }
 
@@ -453,8 +540,7 @@ cudaError_t launch_b_combine(const LaunchCfg& lc, const Dims& d, const BatchBuff
                              int n) {
     BCombineArgs a{};
     a.xm = xm;
-    a.part = bb.part;
-    a.pair_of = bb.pair_of;
+    a.eout = bb.eout;
     a.probs = bb.probs;
     a.sg = bb.sg;
     a.out = out;
@@ -586,7 +672,8 @@ cudaError_t batch_set_attrs() {
     DM_BR_ATTR(4096)
 #undef DM_BR_ATTR
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(b_topk_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 32 * 1024 * 4);
+        e = cudaFuncSetAttribute(b_topk_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(b_topk_group_smem(1023, kMaxTopK)));
     if (e == cudaSuccess) e = b_experts_set_attrs();
     return e;
 }

@@ -44,11 +44,12 @@ struct BExpArgs {
     const int4* segs;         // (expert, first pair, rows, 0)
     int* work;                // [0] segments; [slot] work counter of this launch
     int work_slot;
-    const int* pair_tok;      // pair -> batch row (gate/up input rows)
-    const float* act;         // gate/up: xn [n][K]; down: h [pairs][K]
-    int act_by_pair;
-    float* out;               // gate/up: h [pairs][I]; down: part [pairs][H]
-    int out_ld;
+    const int* pair_src;      // (source rank * n + row) * 32 + k of each pair
+    int n, topk;
+    EpView ep;                // gate/up reads ep.xn[source rank]; down writes ep.eout[source rank]
+    const float* h_in;        // down: h [pairs][K]
+    float* h_out;             // gate/up: h [pairs][I]
+    int H;
 };
 
 DM_DEV void mma_bf16_m16n8k16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -141,8 +142,14 @@ __global__ void __launch_bounds__(kXThreads, 1) b_expert_kernel(const __grid_con
             const int r = t / (K / 16), c16 = t % (K / 16);
             float v[16];
             if (r < ntok) {
-                const int src_row = a.act_by_pair ? pair0 + r : a.pair_tok[pair0 + r];
-                const float4* src = reinterpret_cast<const float4*>(a.act + static_cast<size_t>(src_row) * K + 16 * c16);
+                const float* row;
+                if (GATEUP) {  // the normalised row of its source rank (peer memory in a group)
+                    const int src = a.pair_src[pair0 + r] >> 5;
+                    row = a.ep.xn[src / a.n] + static_cast<size_t>(src % a.n) * K;
+                } else {
+                    row = a.h_in + static_cast<size_t>(pair0 + r) * K;
+                }
+                const float4* src = reinterpret_cast<const float4*>(row + 16 * c16);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const float4 f = src[i];
@@ -254,10 +261,14 @@ __global__ void __launch_bounds__(kXThreads, 1) b_expert_kernel(const __grid_con
             for (int e = 0; e < 2; ++e) {
                 const int t = 2 * ft + e;
                 if (t < ntok) {
-                    float* dst = a.out + static_cast<size_t>(pair0 + t) * a.out_ld;
                     if (GATEUP) {
-                        dst[8 * c + fg] = silu_f(acc[e]) * acc[2 + e];
-                    } else {
+                        // h row length I = 8 rows per gate/up chunk
+                        a.h_out[static_cast<size_t>(pair0 + t) * (a.n_chunks * 8) + 8 * c + fg] =
+                            silu_f(acc[e]) * acc[2 + e];
+                    } else {  // into the source rank's expert-output row (peer memory in a group)
+                        const int ps = a.pair_src[pair0 + t];
+                        const int src = ps >> 5, k = ps & 31;
+                        float* dst = a.ep.eout[src / a.n] + (static_cast<size_t>(src % a.n) * (a.topk + 1) + k) * a.H;
                         dst[16 * c + fg] = acc[e];
                         dst[16 * c + fg + 8] = acc[2 + e];
                     }
@@ -266,6 +277,7 @@ __global__ void __launch_bounds__(kXThreads, 1) b_expert_kernel(const __grid_con
         }
         __syncthreads();  // staged rows free; s_item read by every thread
     }
+    if (!GATEUP && a.ep.world > 1) __threadfence_system();  // results stored into peers
 }
 
 #define DM_XK_INSTANCES(X) X(128) X(256) X(512) X(1024) X(2048) X(4096)
@@ -298,7 +310,6 @@ static cudaError_t launch_expert_proj(const LaunchCfg& lc, int K, bool gateup, c
 cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
                              const Buffers& b, int n) {
     (void)b;
-    (void)n;
     BExpArgs a{};
     a.experts = w.experts;
     a.shared = w.shared;
@@ -306,16 +317,17 @@ cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.E = d.E;
     a.segs = bb.segs;
     a.work = bb.work;
-    a.pair_tok = bb.pair_tok;
+    a.pair_src = bb.pair_src;
+    a.n = n;
+    a.topk = d.topk;
+    a.ep = bb.ep;
+    a.H = d.H;
     // gate/up: K = H, chunks of 8 gate + 8 up rows
     a.proj_off = 0;
     a.chunk_bytes = d.gu_chunk_bytes;
     a.n_chunks = d.gu_chunks;
     a.work_slot = 1;
-    a.act = bb.xn;
-    a.act_by_pair = 0;
-    a.out = bb.h;
-    a.out_ld = d.I;
+    a.h_out = bb.h;
     cudaError_t e = launch_expert_proj(lc, d.H, true, a);
     if (e != cudaSuccess) return e;
     // down: K = I, chunks of 16 output rows
@@ -323,10 +335,7 @@ cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.chunk_bytes = d.d_chunk_bytes;
     a.n_chunks = d.d_chunks;
     a.work_slot = 2;
-    a.act = bb.h;
-    a.act_by_pair = 1;
-    a.out = bb.part;
-    a.out_ld = d.H;
+    a.h_in = bb.h;
     return launch_expert_proj(lc, d.I, false, a);
 }
 

@@ -110,12 +110,30 @@ struct Buffers {
 // Scratch of the batched decode step: `n` sequences (n <= cap <= kMaxBatch), batch row b
 // decodes one token of sequence slot slots[b].  Per-sequence state (GDN state, conv ring,
 // KV pages, page table, position) stays in Buffers, indexed by the slot.
-constexpr int kMaxBatch = 64;       // token masks of the expert grouping are 64-bit
+constexpr int kMaxBatch = 64;       // rows of one rank's batched step
+constexpr int kMaxRanks = 8;        // expert-parallel group (one process per GPU)
+constexpr int kSrcWords = kMaxBatch * kMaxRanks / 64;  // 64-bit words of a source-row mask
 constexpr int kSegTok = 8;          // tokens of one expert segment (one n8 MMA tile)
 constexpr int kHeadChunks = 32;     // vocabulary chunks of the batched argmax
+
+// The expert-parallel group as seen by one rank: every rank runs the same batched step on
+// its own n rows; expert e is computed by rank e / (E / world) for the rows of every rank
+// (its activation row is read from the source rank's memory, its result written into the
+// source rank's expert-output buffer), the shared expert by each rank for its own rows.
+// Peer pointers are the peers' arenas mapped into this process (same layout on every
+// rank); world == 1 is the single-GPU step with the local buffers.
+struct EpView {
+    int rank = 0, world = 1;
+    const int* ids[kMaxRanks];       // [n][topk] routed experts of each rank's rows
+    const float* xn[kMaxRanks];      // [n][H] normalised MoE inputs of each rank's rows
+    float* eout[kMaxRanks];          // [n][topk + 1][H] expert outputs of each rank's rows
+    unsigned* flags[kMaxRanks];      // [2][kMaxRanks] barrier flags of each rank
+};
+
 struct BatchBuffers {
     int cap = 0;
     int max_segs = 0;
+    int max_pairs = 0;
     int* slots;           // [cap] sequence slot of batch row b
     int* tok;             // [cap] input token of row b, replaced by its argmax
     float* x;             // [cap][H] residual stream (block input / output)
@@ -138,18 +156,20 @@ struct BatchBuffers {
     int4* segs;           // [max_segs] (expert, first pair, tokens, 0); expert E = shared
     int* work;            // [4] segments, gate/up work counter, down work counter, spare
     unsigned* stats;      // [4] routing statistics since the last reset: sum over layer-steps of
-                          //     routed experts touched, sum of segments, max rows of one routed
-                          //     expert, layer-steps
-    int* pair_tok;        // [cap (topk + 1)] batch row of each (expert, token) pair
-    int* pair_of;         // [cap][topk + 1] pair index of row b's k-th expert (k = topk: shared)
-    float* h;             // [cap (topk + 1)][I] SwiGLU activations per pair
-    float* part;          // [cap (topk + 1)][H] expert outputs per pair
+                          //     experts touched (by this rank), sum of segments, max rows of one
+                          //     routed expert, layer-steps
+    int* pair_src;        // [max_pairs] source of each pair: (src rank * cap + row) * 32 + k
+    float* h;             // [max_pairs][I] SwiGLU activations per pair
+    float* eout;          // [cap][topk + 1][H] expert outputs of this rank's rows (k = topk: shared)
+    unsigned* ep_flags;   // [2][kMaxRanks] barrier flags written by the peers
+    unsigned* ep_epoch;   // [2] barriers passed (per kind)
     float* cand_val;      // [cap][kHeadChunks]
     int* cand_idx;        // [cap][kHeadChunks]
     float* head_logits;   // [cap][V] logits (written when requested)
     int* gen_out;         // [gen_cap] tokens of a device loop, [step][n]
     int* gen_idx;         // [1] step counter of the device loop
     int gen_cap = 0;
+    EpView ep;
 };
 
 constexpr int kTraceSlots = 2304;
@@ -243,6 +263,8 @@ cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w
                              const Buffers& b, int n);
 cudaError_t launch_b_combine(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const float* xm, float* out,
                              int n);
+// Cross-rank barrier of the expert-parallel group (kind 0 or 1), one small kernel.
+cudaError_t launch_ep_barrier(const LaunchCfg& lc, const BatchBuffers& bb, const Buffers& b, int kind);
 cudaError_t launch_b_argmax(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n,
                             int write_logits, int record_gen);
 cudaError_t batch_set_attrs();

@@ -359,6 +359,21 @@ class Engine:
         u = np.ascontiguousarray(u, np.float32)
         self._ok(self.lib.dm_tensor_add_rank1(self.ctx, layer, tensor_id, _ptr(beta), beta.size, _ptr(u), u.size))
 
+    # ---- expert-parallel group (one process per GPU) ----
+    def ep_ipc_handle(self) -> bytes:
+        buf = C.create_string_buffer(_lib.DM_EP_HANDLE_BYTES)
+        self._ok(self.lib.dm_ep_ipc_handle(self.ctx, buf))
+        return buf.raw
+
+    def ep_attach(self, rank: int, world: int, handles: list[bytes]):
+        if len(handles) != world or any(len(h) != _lib.DM_EP_HANDLE_BYTES for h in handles):
+            raise ValueError("one handle of DM_EP_HANDLE_BYTES bytes per rank")
+        blob = C.create_string_buffer(b"".join(handles), world * _lib.DM_EP_HANDLE_BYTES)
+        self._ok(self.lib.dm_ep_attach(self.ctx, rank, world, blob))
+
+    def ep_detach(self):
+        self._ok(self.lib.dm_ep_detach(self.ctx))
+
     def batch_kernels_per_step(self, n: int) -> tuple[int, int]:
         own, gemms = C.c_int32(), C.c_int32()
         self._ok(self.lib.dm_batch_kernels_per_step(self.ctx, n, C.byref(own), C.byref(gemms)))

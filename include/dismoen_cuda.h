@@ -304,6 +304,20 @@ int32_t dm_generate_batch(dm_ctx* ctx, const int32_t* slots_host, const int32_t*
 int32_t dm_enqueue_decode_batch(dm_ctx* ctx, const int32_t* slots_host, const int32_t* tokens_in_host, int32_t n,
                                 int32_t n_steps);
 int32_t dm_batch_read_generated(dm_ctx* ctx, int32_t n, int32_t n_steps, int32_t* tokens_out_host);
+/* ---- expert-parallel batched decode (one process per GPU of one node) ------------------
+ * Every rank holds the same weights and runs dm_decode_batch on its own sequences with the
+ * same row count n.  Expert e is computed by rank e / (num_experts / world) for the rows
+ * of every rank: its kernels read the row from the source rank's memory and write the
+ * result into the source rank's memory (CUDA IPC mappings over NVLink), with two
+ * cross-GPU flag barriers per MoE layer (bounded waits, DM_ERR_TIMEOUT on expiry).
+ * dm_ep_ipc_handle gives this context's DM_EP_HANDLE_BYTES-byte handle; the caller
+ * exchanges the handles of all ranks (e.g. with torch.distributed) and passes them in
+ * rank order to dm_ep_attach on every rank, then joins the ranks before the first step.
+ * The world must divide num_experts; world <= 8. */
+#define DM_EP_HANDLE_BYTES 64
+int32_t dm_ep_ipc_handle(dm_ctx* ctx, void* handle_out);
+int32_t dm_ep_attach(dm_ctx* ctx, int32_t rank, int32_t world, const void* handles);
+int32_t dm_ep_detach(dm_ctx* ctx);
 /* Launches per batched step: own kernels and library GEMMs. */
 int32_t dm_batch_kernels_per_step(dm_ctx* ctx, int32_t n, int32_t* own_out, int32_t* gemms_out);
 /* Times `iters` launches of one batched kernel (DM_BKERNEL_*) for the n rows of the last

@@ -1,0 +1,110 @@
+"""Expert-parallel batched decode on 2 GPUs (one process per GPU) against the CPU oracle.
+
+Each rank decodes its own sequences; the experts of each rank serve the rows of both
+ranks through the peers' memory.  Every row must give the oracle's greedy ids and logits
+within 1e-3 relative, exactly as the single-GPU batched step does.  Needs two GPUs (the
+ranks wait on each other across GPUs, so they never share one); skipped otherwise.
+"""
+import datetime
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+KERNEL_TOL = 1e-3
+N_ROWS, STEPS = 3, 4
+
+
+def _gpus() -> int:
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _prompts(cfg, rank):
+    rng = np.random.default_rng(100 + rank)
+    return [rng.integers(0, cfg.vocab_size, 3 + 7 * i + rank).astype(np.int32) for i in range(N_ROWS)]
+
+
+def _rank_main(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    try:
+        import torch
+        import torch.distributed as dist
+
+        from disk_streaming_moe_engine_b200 import Engine, RuntimeConfig, ep, preset, synth
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+        cfg = preset("mini")
+        eng = Engine(cfg, RuntimeConfig.for_context(128, max_seqs=N_ROWS), device=rank)
+        eng.load_model(synth.synth_model(cfg, 0))
+        first = []
+        for i, p in enumerate(_prompts(cfg, rank)):
+            eng.seq_reset(i)
+            _, t = eng.forward(p, slot=i, want_logits=False)
+            first.append(t)
+        ep.attach_group(eng, dist)
+        slots = np.arange(N_ROWS, dtype=np.int32)
+        toks = np.array(first, np.int32)
+        steps = []
+        for _ in range(STEPS):
+            out, lg = eng.decode_batch(slots, toks, want_logits=True)
+            steps.append((toks.copy(), out.copy(), lg.copy()))
+            toks = out
+        dist.barrier()
+        eng.ep_detach()
+        eng.close()
+        dist.destroy_process_group()
+        q.put((rank, "ok", first, steps))
+    except Exception as e:  # reported to the test, never a hang of the parent
+        q.put((rank, "error", repr(e), None))
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_ep_two_gpus_matches_oracle(oracle_lib):
+    import oracle
+    from disk_streaming_moe_engine_b200 import preset, synth
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in range(2):
+        item = q.get(timeout=600)
+        res[item[0]] = item[1:]
+    for p in ps:
+        p.join(120)
+        if p.is_alive():
+            p.kill()
+    for r in (0, 1):
+        assert res[r][0] == "ok", res[r]
+    cfg = preset("mini")
+    om = oracle.OracleModel(synth.synth_model(cfg, 0))
+    for r in (0, 1):
+        _, first, steps = res[r]
+        for i, p in enumerate(_prompts(cfg, r)):
+            st = oracle.OracleState(cfg, 128)
+            tok = None
+            for t in p:
+                tok, _, _ = oracle.decode_step(om, st, int(t))
+            assert tok == first[i]
+            for s, (tin, tout, lg) in enumerate(steps):
+                assert tin[i] == tok
+                tok, lg_o, _ = oracle.decode_step(om, st, int(tin[i]))
+                assert tout[i] == tok, (r, i, s)
+                err = float(np.abs(lg[i] - lg_o).max() / np.abs(lg_o).max())
+                assert err < KERNEL_TOL, (r, i, s, err)
