@@ -1264,8 +1264,7 @@ static cudaError_t enqueue_batch_step(dm_ctx* c, int n, int write_logits) {
             if (e == cudaSuccess) e = bgemm(c, w.w_in, d.attn_in_rows, d.H, n);
             if (e == cudaSuccess) e = launch_b_epi_attn_in(lc, d, bb, n);
             if (e == cudaSuccess) e = launch_attn_decode_batch(lc, d, w, bb, c->b, n);
-            if (e == cudaSuccess)
-                e = launch_b_prep(lc, BPREP_COPY, bb.attn_out, d.Hq * d.D, nullptr, d.eps, nullptr, nullptr, 0, bb.xcat, n);
+            if (e == cudaSuccess) e = launch_attn_merge_batch(lc, d, bb, n);
             if (e == cudaSuccess) e = bgemm(c, w.w_out, d.H, d.Hq * d.D, n);
         } else {
             if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);

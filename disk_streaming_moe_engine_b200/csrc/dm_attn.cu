@@ -624,8 +624,8 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
 //   P V      O^T += V^T P^T: A = V^T straight from the staged tile (ldmatrix .trans),
 //            B = P from the score fragments of the same lane (p = hi + lo bf16), so P
 //            never leaves registers; O^T is 16 x (D/16) fragments of (dims, heads)
-// The warps' partials merge in shared memory into one partial per (row, head, split),
-// and the last split CTA of (row, KV head) merges the splits with the output gate.
+// The warps' partials merge in shared memory into one partial per (row, head, split);
+// attn_merge_kernel merges the splits.
 constexpr int kWW = 4;        // warps per CTA
 constexpr int kWStages = 3;   // ring stages per warp
 
@@ -651,7 +651,6 @@ __global__ void __launch_bounds__(kWW * 32, 1) attn_decode_warp_kernel(const __g
     __shared__ float2 cs_s[D / 2];
     __shared__ int pages[kMaxPagesPerSplit];
     __shared__ float wm[kWW][8], wl[kWW][8];
-    __shared__ int last_flag;
     const int g = blockIdx.x, s = blockIdx.y, bz = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int fg = lane >> 2, ft = lane & 3;
@@ -660,8 +659,6 @@ __global__ void __launch_bounds__(kWW * 32, 1) attn_decode_warp_kernel(const __g
     const float* kvnew_in = a.kvnew + bz * a.kvn_bs;
     const int* page_table = a.page_table + slot * a.pt_ss;
     float* part_out = a.part + bz * a.part_bs;
-    float* attn_out = a.out + bz * a.out_bs;
-    unsigned* counters = a.counters + bz * a.cnt_bs;
 
     kt_start(a.kt);
     const int pos = a.pos[slot];
@@ -903,40 +900,6 @@ __global__ void __launch_bounds__(kWW * 32, 1) attn_decode_warp_kernel(const __g
         pp[d] = d < D ? acc : (d == D ? M : L);
     }
     __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(counters + g, 1u);
-        last_flag = prev == static_cast<unsigned>(a.nsplit) - 1;
-        if (last_flag) __threadfence();
-    }
-    __syncthreads();
-    if (!last_flag) {
-        kt_end(a.kt);
-        return;
-    }
-    // ---- the last split of (row, KV head): merge the splits, output gate ----
-    const int ns = a.nsplit;
-    for (int o2 = tid; o2 < GRP * D; o2 += NT) {
-        const int hh = o2 / D, d = o2 % D;
-        const int hq = g * GRP + hh;
-        const float* ph0 = part_out + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
-        float M = -INFINITY;
-        for (int c = 0; c < ns; ++c) {
-            const float lc = __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D + 1);
-            if (lc > 0.0f) M = fmaxf(M, __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D));
-        }
-        float L = 0.0f, acc = 0.0f;
-        for (int c = 0; c < ns; ++c) {
-            const float lc = __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D + 1);
-            const float w = lc > 0.0f ? expf(__ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D) - M) : 0.0f;
-            L = fmaf(w, lc, L);
-            acc = fmaf(w, __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + d), acc);
-        }
-        const float gate = qg_in[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
-        attn_out[static_cast<size_t>(hq) * D + d] = (L > 0.0f ? acc / L : 0.0f) * sigmoid_f(gate);
-    }
-    if (tid == 0) counters[g] = 0u;
-    __syncthreads();
     kt_end(a.kt);
 }
 
@@ -975,6 +938,66 @@ static cudaError_t attn_attr_one() {
     if (e == cudaSuccess)  // largest shared-memory carve-out
         e = cudaFuncSetAttribute(attn_decode_kernel<D, GRP, NB, ST>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     return e;
+}
+
+// ---- split merge of the batched attention + the output projection's operand ------------
+// One CTA of D threads per (row, query head): the weights w_s = exp(m_s - M) of the head's
+// split partials once in shared memory, then every thread one output dimension:
+// o = (sum_s w_s O_s[d]) / (sum_s w_s l_s) * sigmoid(gate), written as the hi / lo bf16
+// rows of the out-projection GEMM operand (rows b and n + b, column hq * D + d).
+template <int D>
+__global__ void __launch_bounds__(D) attn_merge_kernel(const float* __restrict__ part, size_t part_bs, int nsplit,
+                                                       const float* __restrict__ qg, size_t qg_bs, int Hq,
+                                                       uint16_t* xcat, int n) {
+    const int hq = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    __shared__ float w[kMaxSplits];
+    __shared__ float s_inv_l;
+    pdl_wait();
+    const float* ph = part + b * part_bs + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
+    if (d < 32) {  // one warp: the split weights and the normaliser
+        float m[2], l[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int sp = d + 32 * i;
+            const bool on = sp < nsplit;
+            l[i] = on ? ph[static_cast<size_t>(sp) * (D + 2) + D + 1] : 0.0f;
+            m[i] = (on && l[i] > 0.0f) ? ph[static_cast<size_t>(sp) * (D + 2) + D] : -INFINITY;
+        }
+        const float M = warp_max(fmaxf(m[0], m[1]));
+        float L = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const int sp = d + 32 * i;
+            const float wi = l[i] > 0.0f ? expf(m[i] - M) : 0.0f;
+            if (sp < kMaxSplits) w[sp] = wi;
+            L = fmaf(wi, l[i], L);
+        }
+        L = warp_sum(L);
+        if (d == 0) s_inv_l = L > 0.0f ? 1.0f / L : 0.0f;
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    float acc = 0.0f;
+    for (int sp = 0; sp < nsplit; ++sp) acc = fmaf(w[sp], ph[static_cast<size_t>(sp) * (D + 2) + d], acc);
+    const float gate = qg[b * qg_bs + static_cast<size_t>(Hq) * D + static_cast<size_t>(hq) * D + d];
+    const float y = acc * s_inv_l * sigmoid_f(gate);
+    const int K = Hq * D, col = hq * D + d;
+    const uint16_t hi = f32_to_bf16(y);
+    xcat[static_cast<size_t>(b) * K + col] = hi;
+    xcat[static_cast<size_t>(n + b) * K + col] = f32_to_bf16(y - bf16_to_f32(hi));
+}
+
+cudaError_t launch_attn_merge_batch(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, int n) {
+    const int ns = attn_nsplit_batch(lc.num_sms, d.Hkv, n);
+    const size_t part_bs = static_cast<size_t>(d.Hq) * kMaxSplits * (d.D + 2);
+    const size_t qg_bs = static_cast<size_t>(2) * d.Hq * d.D;
+    const dim3 grid(d.Hq, n);
+    switch (d.D) {
+        case 256: return launch_kernel(lc, attn_merge_kernel<256>, grid, dim3(256), 0, bb.attn_part, part_bs, ns, bb.qg, qg_bs, d.Hq, bb.xcat, n);
+        case 128: return launch_kernel(lc, attn_merge_kernel<128>, grid, dim3(128), 0, bb.attn_part, part_bs, ns, bb.qg, qg_bs, d.Hq, bb.xcat, n);
+        case 64: return launch_kernel(lc, attn_merge_kernel<64>, grid, dim3(64), 0, bb.attn_part, part_bs, ns, bb.qg, qg_bs, d.Hq, bb.xcat, n);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 template <int D, int GRP>

@@ -254,6 +254,9 @@ cudaError_t launch_gdn_rec_batch(const LaunchCfg& lc, const Dims& d, const Layer
 cudaError_t launch_attn_decode_batch(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
                                      const Buffers& b, int n);
 int attn_nsplit_batch(int num_sms, int Hkv, int n);
+// merges the batched attention's split partials, output gate, into the out-projection's
+// hi / lo GEMM operand rows
+cudaError_t launch_attn_merge_batch(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, int n);
 // MoE of one layer for n rows: router (canonical), top-k + grouping, experts, combine.
 cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
                             const float* x, int normalise, int n);
