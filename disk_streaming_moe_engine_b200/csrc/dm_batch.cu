@@ -202,28 +202,38 @@ cudaError_t launch_b_epi_resid(const LaunchCfg& lc, const float* c, int N, const
 
 // ---- batched router (canonical arithmetic, bit-identical logits to the one-token router)
 // Grid (ceil((E+1)/16), ceil(n/kBRTok)), 512 threads: warp w owns router row 16 bx + w
-// (weights in registers before griddepcontrol.wait); the CTA normalises its kBRTok rows
-// one after another into shared memory (split layout), then every warp dots its row with
-// each of them.  CTAs of row block 0 also write the normalised rows (the experts' input).
+// (weights in registers before griddepcontrol.wait); the CTA loads its kBRTok input rows
+// at once, normalises them into shared memory (split layout), then every warp dots its
+// row with each of them.  CTAs of row block 0 also write the normalised rows (the
+// experts' input).  The last CTA of a block of rows to finish (counter per row block)
+// computes their softmax and top-k, one warp per row.
 constexpr int kBRThreads = 512;
 constexpr int kBRTok = 8;
 
 struct BRouterArgs {
     const uint16_t* W;      // [E+1][K]
-    int E, n;
+    int E, n, topk;
     const float* x;         // [n][K]
     const uint16_t* gamma;  // nullptr: x is already normalised
     float eps;
     float* xn;              // [n][K]
     float* logits;          // [n][E+1]
     const float* bias;      // [E] logit offsets, or null
+    unsigned* cnt;          // [ceil(cap / kBRTok)] finished CTAs per row block (reset by the last)
+    int* ids;               // [n][topk]
+    float* probs;           // [n][topk]
+    float* sg;              // [n]
+    uint32_t* err;
 };
 
 template <int K>
 __global__ void __launch_bounds__(kBRThreads, 1) b_router_kernel(const __grid_constant__ BRouterArgs a) {
     constexpr int VPL = K / 256;
-    extern __shared__ __align__(16) float xs_all[];  // [kBRTok][K]
+    constexpr int XPT = (K + kBRThreads - 1) / kBRThreads;  // elements of a row per thread
+    constexpr int RB = K <= 2048 ? kBRTok : kBRTok / 2;       // rows loaded together
+    extern __shared__ __align__(16) float xs_all[];  // [kBRTok][K]; then the top-k scratch
     __shared__ float red[kBRThreads / 32];
+    __shared__ int s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int row = blockIdx.x * (kBRThreads / 32) + warp;
     const int b0 = blockIdx.y * kBRTok;
@@ -235,30 +245,71 @@ __global__ void __launch_bounds__(kBRThreads, 1) b_router_kernel(const __grid_co
         for (int i = 0; i < VPL; ++i) wreg[i] = ldg_nc_v4(wr + lane + 32 * i);
     }
     pdl_wait();
-    for (int t = 0; t < nt; ++t) {
-        float* xs = xs_all + static_cast<size_t>(t) * K;
-        const float* x = a.x + static_cast<size_t>(b0 + t) * K;
-        float* xn = blockIdx.x == 0 ? a.xn + static_cast<size_t>(b0 + t) * K : nullptr;
-        if (a.gamma) {
-            canon_rmsnorm_split<K, kBRThreads>(x, a.gamma, a.eps, xs, xn, red);
-        } else {
-            for (int k = tid; k < K; k += kBRThreads) {
-                const float v = x[k];
-                xs_store_split(xs, K, k, v);
-                if (xn) xn[k] = v;
+    for (int t0 = 0; t0 < nt; t0 += RB) {
+        float xv[RB][XPT];
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+#pragma unroll
+            for (int i = 0; i < XPT; ++i) {
+                const int k = i * kBRThreads + tid;
+                xv[r][i] = (t0 + r < nt && k < K) ? a.x[static_cast<size_t>(b0 + t0 + r) * K + k] : 0.0f;
+            }
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+            const int t = t0 + r;
+            if (t < nt) {  // uniform over the CTA
+                float* xs = xs_all + static_cast<size_t>(t) * K;
+                float* xn = blockIdx.x == 0 ? a.xn + static_cast<size_t>(b0 + t) * K : nullptr;
+                if (a.gamma) {
+                    canon_rmsnorm_split_loaded<K, kBRThreads>(xv[r], a.gamma, a.eps, xs, xn, red);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < XPT; ++i) {
+                        const int k = i * kBRThreads + tid;
+                        if (k < K) {
+                            xs_store_split(xs, K, k, xv[r][i]);
+                            if (xn) xn[k] = xv[r][i];
+                        }
+                    }
+                }
+                __syncthreads();  // xs complete; red free for the next row
             }
         }
-        __syncthreads();  // xs complete; red free for the next row
     }
     pdl_launch_dependents();
-    if (row > a.E) return;
-    for (int t = 0; t < nt; ++t) {
-        const float* xs = xs_all + static_cast<size_t>(t) * K;
-        float acc = canon_router_dot<VPL>(wreg, reinterpret_cast<const float4*>(xs),
-                                          reinterpret_cast<const float4*>(xs + K / 2), lane);
-        if (a.bias && row < a.E) acc = __fadd_rn(acc, a.bias[row]);
-        if (lane == 0) a.logits[static_cast<size_t>(b0 + t) * (a.E + 1) + row] = acc;
+    if (row <= a.E) {
+        for (int t = 0; t < nt; ++t) {
+            const float* xs = xs_all + static_cast<size_t>(t) * K;
+            float acc = canon_router_dot<VPL>(wreg, reinterpret_cast<const float4*>(xs),
+                                              reinterpret_cast<const float4*>(xs + K / 2), lane);
+            if (a.bias && row < a.E) acc = __fadd_rn(acc, a.bias[row]);
+            if (lane == 0) a.logits[static_cast<size_t>(b0 + t) * (a.E + 1) + row] = acc;
+        }
     }
+    // ---- the last CTA of this row block: softmax + top-k of its rows ----
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned prev = atomicAdd(a.cnt + blockIdx.y, 1u);
+        s_last = prev == gridDim.x - 1;
+        if (s_last) __threadfence();
+    }
+    __syncthreads();
+    if (!s_last) return;
+    if (warp < nt) {
+        float* lg = xs_all + static_cast<size_t>(warp) * (a.E + 1);
+        const float* src = a.logits + static_cast<size_t>(b0 + warp) * (a.E + 1);
+        for (int e = lane; e <= a.E; e += 32) lg[e] = __ldcg(src + e);
+        __syncwarp();
+        const int b = b0 + warp;
+        canon_softmax_topk_warp(lg, a.E, a.topk, a.ids + b * a.topk, a.probs + b * a.topk, a.sg + b, a.err);
+    }
+    if (tid == 0) a.cnt[blockIdx.y] = 0u;
+}
+
+static size_t b_router_smem(int K, int E) {
+    const size_t xs = static_cast<size_t>(kBRTok) * K * 4, lg = static_cast<size_t>(kBRTok) * (E + 1) * 4;
+    return xs > lg ? xs : lg;
 }
 
 cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
@@ -268,13 +319,19 @@ cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.bias = w.router_bias;
     a.E = d.E;
     a.n = n;
+    a.topk = d.topk;
     a.x = x;
     a.gamma = normalise ? w.post_norm : nullptr;
     a.eps = d.eps;
     a.xn = bb.xn;
     a.logits = bb.logits;
+    a.cnt = bb.rcnt;
+    a.ids = bb.ids;
+    a.probs = bb.probs;
+    a.sg = bb.sg;
+    a.err = bb.err;
     const dim3 grid((d.E + 1 + kBRThreads / 32 - 1) / (kBRThreads / 32), (n + kBRTok - 1) / kBRTok);
-    const size_t smem = static_cast<size_t>(kBRTok) * d.H * 4;
+    const size_t smem = b_router_smem(d.H, d.E);
     switch (d.H) {
         case 256: return launch_kernel(lc, b_router_kernel<256>, grid, dim3(kBRThreads), smem, a);
         case 512: return launch_kernel(lc, b_router_kernel<512>, grid, dim3(kBRThreads), smem, a);
@@ -386,7 +443,7 @@ DM_DEV bool ep_barrier(const EpView& ep, unsigned* my_flags, unsigned* epoch, in
 }
 
 __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __grid_constant__ BGroupArgs a) {
-    extern __shared__ __align__(16) float lgw[];   // [32][E+1], then the ids of every source row
+    extern __shared__ __align__(16) float lgw[];   // the ids of every source row
     __shared__ unsigned long long mask[kBGMaskWords];
     __shared__ int start[1025];
     __shared__ int wsum[32];
@@ -394,15 +451,8 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int E = a.E, topk = a.topk, n = a.n;
     const int world = a.ep.world, rank = a.ep.rank;
-    int* sids = reinterpret_cast<int*>(lgw + static_cast<size_t>(32) * (E + 1));  // [world][n][topk]
-    pdl_wait();
-    for (int b = warp; b < n; b += 32) {
-        float* lg = lgw + static_cast<size_t>(warp) * (E + 1);
-        const float* src = a.logits + static_cast<size_t>(b) * (E + 1);
-        for (int e = lane; e <= E; e += 32) lg[e] = src[e];
-        __syncwarp();
-        canon_softmax_topk_warp(lg, E, topk, a.ids + b * topk, a.probs + b * topk, a.sg + b, a.err);
-    }
+    int* sids = reinterpret_cast<int*>(lgw);  // [world][n][topk]
+    pdl_wait();  // the router's last CTAs wrote this rank's ids
     if (world > 1) ep_barrier(a.ep, a.my_flags, a.epoch, 0, a.err);
     else __syncthreads();
     pdl_launch_dependents();
@@ -475,7 +525,8 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
 }
 
 size_t b_topk_group_smem(int E, int topk) {
-    return static_cast<size_t>(32) * (E + 1) * 4 + static_cast<size_t>(kMaxRanks) * kMaxBatch * topk * 4;
+    (void)E;
+    return static_cast<size_t>(kMaxRanks) * kMaxBatch * topk * 4;
 }
 
 cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n) {
@@ -664,7 +715,8 @@ cudaError_t batch_set_attrs() {
     cudaError_t e = cudaSuccess;
 #define DM_BR_ATTR(KK)                                                                                      \
     if (e == cudaSuccess)                                                                                   \
-        e = cudaFuncSetAttribute(b_router_kernel<KK>, cudaFuncAttributeMaxDynamicSharedMemorySize, kBRTok * KK * 4);
+        e = cudaFuncSetAttribute(b_router_kernel<KK>, cudaFuncAttributeMaxDynamicSharedMemorySize,            \
+                                 static_cast<int>(b_router_smem(KK, 1023)));
     DM_BR_ATTR(256)
     DM_BR_ATTR(512)
     DM_BR_ATTR(1024)

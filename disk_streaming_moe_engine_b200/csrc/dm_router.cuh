@@ -50,6 +50,31 @@ DM_DEV void canon_rmsnorm_split(const float* x, const uint16_t* gamma, float eps
     }
 }
 
+// The same RMSNorm with this thread's elements (k = t, t + NT, ...) already loaded into xv,
+// so that the loads of several rows can be in flight together.
+template <int K, int NT>
+DM_DEV void canon_rmsnorm_split_loaded(const float (&xv)[(K + NT - 1) / NT], const uint16_t* gamma, float eps,
+                                       float* xs, float* xn_out, float* red) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i * NT + tid < K; ++i) acc = __fmaf_rn(xv[i], xv[i], acc);
+    acc = warp_sum(acc);
+    if (lane == 0) red[warp] = acc;
+    __syncthreads();
+    float ss = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) ss = __fadd_rn(ss, red[w]);
+    const float denom = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps));
+#pragma unroll
+    for (int i = 0; i * NT + tid < K; ++i) {
+        const int k = i * NT + tid;
+        const float y = __fmul_rn(__fdiv_rn(xv[i], denom), bf16_to_f32(gamma[k]));
+        xs_store_split(xs, K, k, y);
+        if (xn_out) xn_out[k] = y;
+    }
+}
+
 // Canonical dot of one bf16 router row (VPL 16-byte vectors per lane, vector i of lane l
 // holding elements 8(l + 32i) .. +7) with x in the split layout; every lane gets the sum.
 template <int VPL>
