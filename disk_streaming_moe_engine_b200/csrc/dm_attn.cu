@@ -616,9 +616,10 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
 // ---------------------------------------------------------------------------------------
 // Batched decode attention for long histories ("flash-decoding" per warp).
 // Grid (Hkv, nsplit, rows), kWW warps per CTA, one CTA per SM.  The CTA prepares the new
-// token as the one-sequence kernel does; then every warp streams its own pages (page
-// i of the split goes to warp i % kWW) through its own kWStages-deep ring of tensor-map
-// copies and keeps its own online softmax, so the main loop has no block barrier:
+// token as the one-sequence kernel does; then page i of the split goes to warp i % kWW
+// through stage i % kWRing of a shared ring of tensor-map copies (the warp that consumes
+// a stage refills it with page i + kWRing), and every warp keeps its own online softmax,
+// so the main loop has no block barrier:
 //   scores   S = Q K^T (8 query heads in rows 0..7 of the m16 tile, q = hi + lo bf16),
 //            the lane holding head fg keeps the running max / partial sum of that head
 //   P V      O^T += V^T P^T: A = V^T straight from the staged tile (ldmatrix .trans),
@@ -626,12 +627,12 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
 //            never leaves registers; O^T is 16 x (D/16) fragments of (dims, heads)
 // The warps' partials merge in shared memory into one partial per (row, head, split);
 // attn_merge_kernel merges the splits.
-constexpr int kWW = 4;        // warps per CTA
-constexpr int kWStages = 3;   // ring stages per warp
+constexpr int kWW = 8;        // warps per CTA (two per scheduler)
+constexpr int kWRing = 12;    // ring stages (pages in flight) per CTA
 
 template <int D>
 constexpr size_t attn_warp_ring_bytes() {
-    return static_cast<size_t>(kWW) * kWStages * AttnGeom<D>::STAGE + 1024;
+    return static_cast<size_t>(kWRing) * AttnGeom<D>::STAGE + 1024;
 }
 
 template <int D, int GRP>
@@ -642,7 +643,10 @@ __global__ void __launch_bounds__(kWW * 32, 1) attn_decode_warp_kernel(const __g
     static_assert(GRP <= 8, "heads of a KV group are rows 0..7 of the m16 tile");
     extern __shared__ __align__(1024) uint8_t ring_raw[];
     uint8_t* ring = ring_raw + ((1024u - (smem_u32(ring_raw) & 1023u)) & 1023u);
-    __shared__ __align__(8) uint64_t bar[kWW][kWStages];
+    __shared__ __align__(8) uint64_t bar[kWRing];
+    // fills issued per stage: the owner of page i waits for fill i / kWRing + 1 to be issued
+    // before it waits on the stage's mbarrier, so a parity wait never runs a phase ahead
+    __shared__ int filled[kWRing];
     __shared__ __align__(16) float qsm[GRP][D + 4];
     __shared__ __align__(16) uint16_t qh[GRP][D + 8], ql[GRP][D + 8];
     __shared__ __align__(16) float knew[D], vnew[D];
@@ -673,34 +677,37 @@ __global__ void __launch_bounds__(kWW * 32, 1) attn_decode_warp_kernel(const __g
     const int t1 = min(n_tok, pg1 * kPageTokens);
     for (int i = tid; i < np && i < kMaxPagesPerSplit; i += NT) pages[i] = page_table[pg0 + i];
     if (tid == 0) {
-        for (int i = 0; i < kWW * kWStages; ++i) mbar_init(&bar[i / kWStages][i % kWStages], 1);
+        for (int i = 0; i < kWRing; ++i) {
+            mbar_init(&bar[i], 1);
+            filled[i] = 0;
+        }
         mbar_fence_init();
     }
     __syncthreads();
-    uint8_t* my_ring = ring + static_cast<size_t>(warp) * kWStages * AG::STAGE;
-    // local page j of this warp = page warp + kWW j of the split, into stage j % kWStages
-    auto issue = [&](int j) {
-        const int i = warp + kWW * j;
-        const int st = j % kWStages;
+    // page i of the split into stage i % kWRing (a single thread issues)
+    auto issue = [&](int i) {
+        const int st = i % kWRing;
         const int page = i < kMaxPagesPerSplit ? pages[i] : page_table[pg0 + i];
         const bool good = page >= 0 && page < a.num_pages;
         if (good) {
-            mbar_arrive_expect_tx(&bar[warp][st], 2 * kPageTokens * D * 2);
-            uint8_t* dst = my_ring + static_cast<size_t>(st) * AG::STAGE;
+            mbar_arrive_expect_tx(&bar[st], 2 * kPageTokens * D * 2);
+            uint8_t* dst = ring + static_cast<size_t>(st) * AG::STAGE;
 #pragma unroll
             for (int kv = 0; kv < 2; ++kv) {
                 const int y = a.kv_row0 + ((page * 2 + kv) * a.Hkv + g) * kPageTokens;
 #pragma unroll
-                for (int c = 0; c < D / 64; ++c) tma_load_2d(dst + kv * AG::TILE + c * AG::CHUNK, &a.kv_map, 64 * c, y, &bar[warp][st]);
+                for (int c = 0; c < D / 64; ++c) tma_load_2d(dst + kv * AG::TILE + c * AG::CHUNK, &a.kv_map, 64 * c, y, &bar[st]);
             }
         } else {
             raise_error(a.err, DM_DEVERR_PAGE);
-            mbar_arrive(&bar[warp][st]);
+            mbar_arrive(&bar[st]);
         }
+        __threadfence_block();
+        *reinterpret_cast<volatile int*>(&filled[st]) = i / kWRing + 1;
     };
     const int my_np = np > warp ? (np - warp + kWW - 1) / kWW : 0;
-    if (lane == 0)
-        for (int j = 0; j < my_np && j < kWStages; ++j) issue(j);
+    if (tid == 0)
+        for (int i = 0; i < np && i < kWRing; ++i) issue(i);
     for (int i = tid; i < D; i += NT) {
         qn_s[i] = bf16_to_f32(a.q_norm[i]);
         kn_s[i] = bf16_to_f32(a.k_norm[i]);
@@ -760,9 +767,25 @@ __global__ void __launch_bounds__(kWW * 32, 1) attn_decode_warp_kernel(const __g
     const int ip_new = pos / kPageTokens - pg0;
     for (int j = 0; j < my_np; ++j) {
         const int i = warp + kWW * j;
-        const int st = j % kWStages;
-        const bool ok = mbar_wait_bounded(&bar[warp][st], (j / kWStages) & 1, a.err, nullptr);
-        uint8_t* kt = my_ring + static_cast<size_t>(st) * AG::STAGE;
+        const int st = i % kWRing;
+        bool ok = true;
+        {  // this page's fill issued (the previous owner of the stage is done with it)
+            const volatile int* f = &filled[st];
+            const int want = i / kWRing + 1;
+            if (*f < want) {
+                const uint64_t t0 = globaltimer_ns();
+                uint32_t it = 0;
+                while (*f < want) {
+                    if ((++it & 255u) == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
+                        raise_error(a.err, DM_DEVERR_TIMEOUT);
+                        ok = false;
+                        break;
+                    }
+                }
+            }
+        }
+        ok = ok && mbar_wait_bounded(&bar[st], (i / kWRing) & 1, a.err, nullptr);
+        uint8_t* kt = ring + static_cast<size_t>(st) * AG::STAGE;
         uint8_t* vt = kt + AG::TILE;
         if (i == ip_new) {  // the staged copy of the page holding pos predates the append
             const int r = pos % kPageTokens;
@@ -853,9 +876,9 @@ __global__ void __launch_bounds__(kWW * 32, 1) attn_decode_warp_kernel(const __g
             }
         }
         __syncwarp();  // every lane is done with the stage
-        if (lane == 0 && j + kWStages < my_np) {
+        if (lane == 0 && i + kWRing < np) {
             fence_proxy_async_smem();
-            issue(j + kWStages);
+            issue(i + kWRing);
         }
     }
     // sum of the head's lanes (ft = 0..3)
@@ -1092,16 +1115,17 @@ cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW&
 }
 
 // Splits per (row, KV head) of the batched launch (one CTA per SM): the count that
-// minimises waves / splits, i.e. the time per unit of work when every CTA does 1/ns of its
-// (row, head); ties go to fewer splits (less merge work).
+// minimises waves x (1 / ns + c), the time of a wave being the split's share of a row's
+// pages plus a fixed per-CTA cost c (prologue, partial merge) taken as 1 % of a row.
 int attn_nsplit_batch(int num_sms, int Hkv, int n) {
     const int units = (n > 0 ? n : 1) * (Hkv > 0 ? Hkv : 1);
+    constexpr double kCtaCost = 0.01;
     int best = 1;
     double best_cost = 1e30;
     for (int ns = 1; ns <= kMaxSplits; ++ns) {
         const long long ctas = static_cast<long long>(units) * ns;
         const long long waves = (ctas + num_sms - 1) / num_sms;
-        const double cost = static_cast<double>(waves) / ns;
+        const double cost = static_cast<double>(waves) * (1.0 / ns + kCtaCost);
         if (cost < best_cost - 1e-12) {
             best_cost = cost;
             best = ns;
