@@ -54,6 +54,7 @@ using namespace dm;
 
 struct dm_ctx {
     CUtensorMap kv_map{};  // 2-D tiled view of the KV arena for the attention page copies
+    std::vector<CUtensorMap> xmaps;  // [L][2] the expert pools' nibble rows (gate/up, down)
     dm_model_config mc{};
     dm_runtime_config rc{};
     Dims d{};
@@ -492,20 +493,68 @@ static void set_local_ep(dm_ctx* c) {
 // Tensor map of the KV arena for the attention kernel's page copies: rows of D bf16
 // ([att][page][K|V][Hkv][16] flattened), boxes of 16 rows x 64 columns (128 bytes, the
 // swizzle span), 128-byte swizzle.  The encoder comes from the driver entry point table.
-static bool encode_kv_map(dm_ctx* c) {
-    c->b.kv_tmap = &c->kv_map;
-    const Dims& d = c->d;
-    if (d.n_att == 0) return true;
-    typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn encode_fn() {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q{};
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn ||
         q != cudaDriverEntryPointSuccess) {
         fprintf(stderr, "dm_ctx_create: cuTensorMapEncodeTiled unavailable\n");
-        return false;
+        return nullptr;
     }
+    return reinterpret_cast<EncodeTiledFn>(fn);
+}
+
+// Tensor maps of every layer's expert pool for the batched expert kernels: the nibble rows
+// of one projection as a 4-D byte tensor (row bytes, 16 rows of a chunk, chunks of a record,
+// records; the shared expert's record follows the E routed ones), boxes of 16 rows x 128
+// bytes (the swizzle span), 128-byte swizzle.  A layer whose shared record does not follow
+// its pool keeps null maps (the kernels then use plain loads).
+static bool encode_expert_maps(dm_ctx* c) {
+    const Dims& d = c->d;
+    c->xmaps.assign(static_cast<size_t>(d.L) * 2, CUtensorMap{});
+    const bool gu_ok = expert_tma_supported(d.H), dn_ok = expert_tma_supported(d.I);
+    if (!gu_ok && !dn_ok) return true;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    for (int l = 0; l < d.L; ++l) {
+        LayerW& w = c->layers[l];
+        w.tm_gu = w.tm_dn = nullptr;
+        if (w.shared != w.experts + static_cast<int64_t>(d.E) * d.expert_bytes) continue;
+        for (int proj = 0; proj < 2; ++proj) {
+            if (proj == 0 ? !gu_ok : !dn_ok) continue;
+            const int K = proj == 0 ? d.H : d.I;
+            const int64_t chunk = proj == 0 ? d.gu_chunk_bytes : d.d_chunk_bytes;
+            const int nch = proj == 0 ? d.gu_chunks : d.d_chunks;
+            uint8_t* base = const_cast<uint8_t*>(w.experts) + (proj == 0 ? 0 : static_cast<int64_t>(d.gu_chunks) * d.gu_chunk_bytes);
+            const cuuint64_t dims[4] = {static_cast<cuuint64_t>(K / 2), 16, static_cast<cuuint64_t>(nch),
+                                        static_cast<cuuint64_t>(d.E + 1)};
+            const cuuint64_t strides[3] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(chunk),
+                                           static_cast<cuuint64_t>(d.expert_bytes)};
+            const cuuint32_t box[4] = {128, 16, 1, 1};
+            const cuuint32_t estr[4] = {1, 1, 1, 1};
+            CUtensorMap* m = &c->xmaps[static_cast<size_t>(l) * 2 + proj];
+            const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, dims, strides, box, estr,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) {
+                fprintf(stderr, "dm_ctx_create: expert tensor map of layer %d failed (%d)\n", l, static_cast<int>(r));
+                return false;
+            }
+            (proj == 0 ? w.tm_gu : w.tm_dn) = m;
+        }
+    }
+    return true;
+}
+
+static bool encode_kv_map(dm_ctx* c) {
+    c->b.kv_tmap = &c->kv_map;
+    const Dims& d = c->d;
+    if (d.n_att == 0) return true;
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
     const uint64_t rows = static_cast<uint64_t>(d.n_att) * d.num_pages * 2 * d.Hkv * kPageTokens;
     if (rows >= (1ull << 31)) {
         fprintf(stderr, "dm_ctx_create: KV arena of %llu rows exceeds the 2^31 tensor-map coordinate range\n",
@@ -516,7 +565,7 @@ static bool encode_kv_map(dm_ctx* c) {
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.D) * 2};
     const cuuint32_t box[2] = {64, kPageTokens};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = reinterpret_cast<EncodeFn>(fn)(&c->kv_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c->b.kv, dims, strides,
+    const CUresult r = fn(&c->kv_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c->b.kv, dims, strides,
                                                       box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
@@ -599,6 +648,7 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     if (e == cudaSuccess) e = cudaMallocHost(&c->h_io, 64);
     if (e == cudaSuccess) e = cudaMallocHost(&c->h_bio, 4 * kMaxBatch * sizeof(int));
     if (e == cudaSuccess && !encode_kv_map(c)) e = cudaErrorInvalidValue;
+    if (e == cudaSuccess && !encode_expert_maps(c)) e = cudaErrorInvalidValue;
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) {
         fprintf(stderr, "dm_ctx_create: %s\n", cudaGetErrorString(e));

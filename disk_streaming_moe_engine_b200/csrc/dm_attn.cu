@@ -147,7 +147,6 @@ DM_DEV void mma_bf16_16816_full(float (&c)[4], uint32_t a0, uint32_t a1, uint32_
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 DM_DEV uint32_t pack_bf16x2(uint16_t lo, uint16_t hi) { return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16); }
-DM_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ---- per-CTA preparation of the new token (shared by the decode kernels) ---------------
 // q heads of KV group g, new k, new v: one parallel load, per-head RMSNorm (q_norm / k_norm)

@@ -170,6 +170,10 @@ DM_DEV void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint6
         : "memory");
 #endif
 }
+// Orders this thread's generic-proxy accesses of shared memory before later async-proxy
+// (bulk / tensor copy) writes into the same bytes.
+DM_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // L2 prefetch of a global range (no shared memory involved).
 DM_DEV void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes)

@@ -64,6 +64,8 @@ struct LayerW {
     const uint16_t* w_out;           // [H][nv*dv] or [H][Hq*D]
     const uint16_t* w_router;        // [E+1][H]
     const float* router_bias;        // [E] logit offsets of a synthetic workload, or null (none)
+    const void* tm_gu;               // host CUtensorMaps of the pool's gate/up and down nibble
+    const void* tm_dn;               // rows (4-D: row bytes, 16 rows, chunk, expert), or null
     const uint8_t* experts;          // [E] records
     const uint8_t* shared;           // 1 record
 };
@@ -273,4 +275,5 @@ cudaError_t launch_ep_barrier(const LaunchCfg& lc, const BatchBuffers& bb, const
 cudaError_t launch_b_argmax(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n,
                             int write_logits, int record_gen);
 cudaError_t batch_set_attrs();
+bool expert_tma_supported(int K);
 }  // namespace dm
