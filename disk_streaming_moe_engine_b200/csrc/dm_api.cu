@@ -1657,6 +1657,16 @@ int32_t dm_router(dm_ctx* c, int32_t layer, const float* x, int32_t n, int32_t* 
     cudaSetDevice(c->device);
     const Dims& d = c->d;
     const LaunchCfg lc = lcfg(c);
+    if (n > 1 && n <= c->bb.cap) {  // several rows: the batched router (same canonical bits)
+        BatchBuffers& bb = c->bb;
+        DM_CUDA(c, cudaMemcpyAsync(bb.xm, x, sizeof(float) * n * d.H, cudaMemcpyHostToDevice, c->stream), "router");
+        DM_CUDA(c, launch_b_router(lc, d, c->layers[layer], bb, bb.xm, 0, n), "router");
+        DM_CUDA(c, cudaMemcpyAsync(ids, bb.ids, sizeof(int) * n * d.topk, cudaMemcpyDeviceToHost, c->stream), "router");
+        DM_CUDA(c, cudaMemcpyAsync(probs, bb.probs, sizeof(float) * n * d.topk, cudaMemcpyDeviceToHost, c->stream), "router");
+        if (sg) DM_CUDA(c, cudaMemcpyAsync(sg, bb.sg, sizeof(float) * n, cudaMemcpyDeviceToHost, c->stream), "router");
+        DM_CUDA(c, cudaStreamSynchronize(c->stream), "router");
+        return check_device_error(c, "router");
+    }
     for (int t = 0; t < n; ++t) {
         DM_CUDA(c, cudaMemcpyAsync(c->b.xn, x + static_cast<size_t>(t) * d.H, sizeof(float) * d.H, cudaMemcpyHostToDevice, c->stream), "router");
         DM_CUDA(c, launch_router(lc, d, c->layers[layer], c->b, 0, 0), "router");

@@ -85,7 +85,9 @@ __global__ void __launch_bounds__(kPrepThreads) b_prep_kernel(const __grid_const
         const float* z = a.z + static_cast<size_t>(b) * a.K;
         const int nh = a.K / a.dv;
         pdl_launch_dependents();
-        for (int h = warp; h < nh; h += kPrepThreads / 32) {
+        // grid.y slices the heads: CTA y takes heads 8 y .. 8 y + 7, one per warp
+        for (int h = blockIdx.y * (kPrepThreads / 32) + warp; h < nh && h < (blockIdx.y + 1) * (kPrepThreads / 32);
+             h += kPrepThreads / 32) {
             const float* oh = x + h * a.dv;
             float acc = 0.0f;
             for (int dd = lane; dd < a.dv; dd += 32) acc = fmaf(oh[dd], oh[dd], acc);
@@ -112,7 +114,10 @@ cudaError_t launch_b_prep(const LaunchCfg& lc, int mode, const float* x, int K, 
     a.n = n;
     a.xcat = xcat;
     if (mode == BPREP_RMS) return launch_kernel(lc, b_prep_kernel<BPREP_RMS>, dim3(n), dim3(kPrepThreads), 0, a);
-    if (mode == BPREP_HEADNORM) return launch_kernel(lc, b_prep_kernel<BPREP_HEADNORM>, dim3(n), dim3(kPrepThreads), 0, a);
+    if (mode == BPREP_HEADNORM) {
+        const int nh = K / dv, per = kPrepThreads / 32;
+        return launch_kernel(lc, b_prep_kernel<BPREP_HEADNORM>, dim3(n, (nh + per - 1) / per), dim3(kPrepThreads), 0, a);
+    }
     return launch_kernel(lc, b_prep_kernel<BPREP_COPY>, dim3(n), dim3(kPrepThreads), 0, a);
 }
 

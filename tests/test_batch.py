@@ -134,3 +134,27 @@ def test_batch_rejects_bad_input(lib):
         out, _ = eng.decode_batch([2, 0], [7, 9])
         assert out.shape == (2,)
         assert eng.seq_len(2) == 1 and eng.seq_len(0) == 1
+
+
+@pytest.mark.parametrize("which", ["mini", "layer"])
+def test_batched_router_bit_exact(which, lib, oracle_lib):
+    """The batched router (rows normalised by one warp each, emulating the canonical
+    512-thread reduction order) gives the oracle's ids and probabilities bit for bit, and
+    the same bits as the one-row router."""
+    import oracle
+    cfg = preset(which)
+    m = synth.synth_model(cfg, 3, head=False)
+    rng = np.random.default_rng(21)
+    with Engine(cfg, RuntimeConfig.for_context(64, max_seqs=10)) as eng:
+        eng.load_model(m)
+        om = oracle.OracleModel(m)
+        for layer in range(cfg.num_hidden_layers):
+            xs = rng.standard_normal((10, cfg.hidden_size)).astype(np.float32)
+            info = eng.router_forward(xs, layer)            # 10 rows: batched kernel
+            for t in range(xs.shape[0]):
+                ids, probs, sg, _ = oracle.router(om, layer, xs[t])
+                np.testing.assert_array_equal(info.selected_experts[t], ids)
+                assert np.array_equal(info.routing_weights[t].view(np.uint32), probs.view(np.uint32))
+                one = eng.router_forward(xs[t], layer)      # 1 row: the one-token kernel
+                np.testing.assert_array_equal(one.selected_experts[0], info.selected_experts[t])
+                assert np.array_equal(one.routing_weights[0].view(np.uint32), info.routing_weights[t].view(np.uint32))
