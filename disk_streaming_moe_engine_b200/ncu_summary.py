@@ -1,7 +1,15 @@
-"""Summarises an ncu launch list (`--metrics gpu__time_duration.sum --csv --log-file F`) of
-`bench.py` into per-kernel launches, total time and share of the timed decode steps.
+"""Summarises ncu output for profiles/:
+
+* a launch list (`--metrics gpu__time_duration.sum --csv --log-file F`) of `bench.py` into
+  per-kernel launches, total time and share of the timed decode steps:
 
     python -m disk_streaming_moe_engine_b200.ncu_summary launches.csv --warmup 3 --steps 4
+    (batched step: --marker b_embed_kernel)
+
+* a full capture (`ncu -i rep --page raw --csv > raw.csv`) into the figures a roofline
+  needs, per captured launch, and the top warp stall reasons:
+
+    python -m disk_streaming_moe_engine_b200.ncu_summary --full raw.csv --alg-bytes N
 
 A decode step starts with its embedding kernel, so the launches of the timed steps are
 those from the (warmup+1)-th `embed_kernel` up to the (warmup+steps+1)-th.  ncu serialises
@@ -38,8 +46,8 @@ def short_name(k: str) -> str:
     return k.replace("dm::", "")
 
 
-def summarise(launches, warmup: int, steps: int):
-    starts = [i for i, (n, _) in enumerate(launches) if n.startswith("embed_kernel")]
+def summarise(launches, warmup: int, steps: int, marker: str = "embed_kernel"):
+    starts = [i for i, (n, _) in enumerate(launches) if n.startswith(marker)]
     if len(starts) < warmup + steps:
         raise SystemExit(f"only {len(starts)} decode steps in the launch list")
     a = starts[warmup]
@@ -55,13 +63,70 @@ def summarise(launches, warmup: int, steps: int):
     return len(sel), total, [(n, c, t, t / total) for n, (c, t) in rows]
 
 
+FULL_METRICS = [
+    "gpu__time_duration.sum", "dram__bytes_read.sum", "dram__bytes_write.sum",
+    "gpu__dram_throughput.avg.pct_of_peak_sustained_elapsed", "sm__throughput.avg.pct_of_peak_sustained_elapsed",
+    "sm__inst_executed_pipe_tensor_subpipe_hmma.avg.pct_of_peak_sustained_active",
+    "sm__pipe_alu_cycles_active.avg.pct_of_peak_sustained_active",
+    "smsp__issue_active.avg.pct_of_peak_sustained_active", "sm__warps_active.avg.pct_of_peak_sustained_active",
+    "l1tex__data_bank_conflicts_pipe_lsu_mem_shared.sum", "launch__registers_per_thread", "launch__grid_size",
+    "launch__block_size",
+]
+
+
+def summarise_full(path: str, alg_bytes: float | None):
+    """(kernel names, {metric: [value with unit per launch]}, top stall reasons of launch 1)."""
+    rows = list(csv.reader(open(path)))
+    hdr, units, data = rows[0], rows[1], rows[2:]
+    col = {h: i for i, h in enumerate(hdr)}
+    names = [short_name(r[col["Kernel Name"]]) for r in data]
+    table = {m: [f"{r[col[m]]} {units[col[m]]}".strip() for r in data] for m in FULL_METRICS if m in col}
+    stall = []
+    pat = re.compile(r"^smsp__average_warps_issue_stalled_(.+)_per_issue_active\.ratio$")
+    for h, i in col.items():
+        mm = pat.match(h)
+        if mm and data:
+            try:
+                stall.append((float(data[0][i].replace(",", "")), mm.group(1)))
+            except ValueError:
+                pass
+    stall.sort(reverse=True)
+    traffic = None
+    if "dram__bytes_read.sum" in col and data:
+        def to_bytes(v, u):
+            v = float(v.replace(",", ""))
+            return v * {"byte": 1, "Kbyte": 1e3, "Mbyte": 1e6, "Gbyte": 1e9}.get(u, 1)
+        r = data[0]
+        traffic = to_bytes(r[col["dram__bytes_read.sum"]], units[col["dram__bytes_read.sum"]]) + to_bytes(
+            r[col["dram__bytes_write.sum"]], units[col["dram__bytes_write.sum"]])
+    print(f"kernels: {', '.join(dict.fromkeys(names))}")
+    if traffic is not None:
+        print(f"\ndram_bytes_per_launch: {traffic:.0f}")
+        if alg_bytes:
+            print(f"\ntraffic / algorithmic = {traffic / alg_bytes:.3f}")
+    print()
+    print("| metric | " + " | ".join(f"launch {i + 1}" for i in range(len(data))) + " |")
+    print("|---|" + "---|" * len(data))
+    for m, vals in table.items():
+        print(f"| `{m}` | " + " | ".join(vals) + " |")
+    print("\nTop warp stall reasons (cycles per issued instruction, launch 1):\n")
+    for v, name in stall[:8]:
+        print(f"* {name}: {v:.3f}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("csv")
-    ap.add_argument("--warmup", type=int, required=True)
-    ap.add_argument("--steps", type=int, required=True)
+    ap.add_argument("--warmup", type=int, default=0)
+    ap.add_argument("--steps", type=int, default=1)
+    ap.add_argument("--marker", default="embed_kernel", help="first kernel of a step")
+    ap.add_argument("--full", action="store_true", help="csv is a raw page of a full capture")
+    ap.add_argument("--alg-bytes", type=float, default=None)
     a = ap.parse_args()
-    n, total, rows = summarise(read_launches(a.csv), a.warmup, a.steps)
+    if a.full:
+        summarise_full(a.csv, a.alg_bytes)
+        return
+    n, total, rows = summarise(read_launches(a.csv), a.warmup, a.steps, a.marker)
     print(f"timed decode steps: {a.steps}; launches: {n} ({n / a.steps:.0f} per step); "
           f"serialised kernel time {total / 1e3 / a.steps:.1f} us per step")
     print()
