@@ -250,34 +250,33 @@ __global__ void __launch_bounds__(kBRThreads, 1) b_router_kernel(const __grid_co
         for (int i = 0; i < VPL; ++i) wreg[i] = ldg_nc_v4(wr + lane + 32 * i);
     }
     pdl_wait();
-    for (int t0 = 0; t0 < nt; t0 += RB) {
-        float xv[RB][XPT];
+    if (!a.gamma) {  // rows already normalised: stage them all in one pass
+        for (int i = tid; i < nt * K; i += kBRThreads) {
+            const int t = i / K, k = i % K;
+            const float v = a.x[static_cast<size_t>(b0 + t) * K + k];
+            xs_store_split(xs_all + static_cast<size_t>(t) * K, K, k, v);
+            if (blockIdx.x == 0 && a.xn) a.xn[static_cast<size_t>(b0 + t) * K + k] = v;
+        }
+        __syncthreads();
+    } else {
+        for (int t0 = 0; t0 < nt; t0 += RB) {
+            float xv[RB][XPT];
 #pragma unroll
-        for (int r = 0; r < RB; ++r)
+            for (int r = 0; r < RB; ++r)
 #pragma unroll
-            for (int i = 0; i < XPT; ++i) {
-                const int k = i * kBRThreads + tid;
-                xv[r][i] = (t0 + r < nt && k < K) ? a.x[static_cast<size_t>(b0 + t0 + r) * K + k] : 0.0f;
-            }
-#pragma unroll
-        for (int r = 0; r < RB; ++r) {
-            const int t = t0 + r;
-            if (t < nt) {  // uniform over the CTA
-                float* xs = xs_all + static_cast<size_t>(t) * K;
-                float* xn = blockIdx.x == 0 ? a.xn + static_cast<size_t>(b0 + t) * K : nullptr;
-                if (a.gamma) {
-                    canon_rmsnorm_split_loaded<K, kBRThreads>(xv[r], a.gamma, a.eps, xs, xn, red);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < XPT; ++i) {
-                        const int k = i * kBRThreads + tid;
-                        if (k < K) {
-                            xs_store_split(xs, K, k, xv[r][i]);
-                            if (xn) xn[k] = xv[r][i];
-                        }
-                    }
+                for (int i = 0; i < XPT; ++i) {
+                    const int k = i * kBRThreads + tid;
+                    xv[r][i] = (t0 + r < nt && k < K) ? a.x[static_cast<size_t>(b0 + t0 + r) * K + k] : 0.0f;
                 }
-                __syncthreads();  // xs complete; red free for the next row
+#pragma unroll
+            for (int r = 0; r < RB; ++r) {
+                const int t = t0 + r;
+                if (t < nt) {  // uniform over the CTA
+                    float* xs = xs_all + static_cast<size_t>(t) * K;
+                    float* xn = (blockIdx.x == 0 && a.xn) ? a.xn + static_cast<size_t>(b0 + t) * K : nullptr;
+                    canon_rmsnorm_split_loaded<K, kBRThreads>(xv[r], a.gamma, a.eps, xs, xn, red);
+                    __syncthreads();  // xs complete; red free for the next row
+                }
             }
         }
     }
@@ -328,7 +327,7 @@ cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.x = x;
     a.gamma = normalise ? w.post_norm : nullptr;
     a.eps = d.eps;
-    a.xn = bb.xn;
+    a.xn = (!normalise && x == bb.xn) ? nullptr : bb.xn;  // rows normalised in place already
     a.logits = bb.logits;
     a.cnt = bb.rcnt;
     a.ids = bb.ids;
