@@ -21,6 +21,8 @@ DM_ERR_NONFINITE = 6
 DM_ERR_TIMEOUT = 7
 DM_ERR_NOT_READY = 8
 DM_ERR_ROUTER = 9
+DM_ERR_IO = 10
+DM_ERR_FORMAT = 11
 
 DM_KERNEL_MIXER_IN, DM_KERNEL_MIXER_OUT, DM_KERNEL_MIXER_CORE = 0, 1, 2
 DM_KERNEL_ROUTER, DM_KERNEL_MOE, DM_KERNEL_HEAD = 3, 4, 6
@@ -118,6 +120,9 @@ SIGNATURES = {
     "dm_ep_ipc_handle": (I32, [P, P]),
     "dm_ep_attach": (I32, [P, I32, I32, P]),
     "dm_ep_detach": (I32, [P]),
+    "dm_kmss_save": (I32, [P, I32, C.c_char_p, P, I32, I32, P]),
+    "dm_kmss_load": (I32, [P, I32, C.c_char_p, P, I32, C.POINTER(I32)]),
+    "dm_sha256": (I32, [P, U64, P]),
     "dm_time_batch_kernel": (I32, [P, I32, I32, I32, I32, C.POINTER(F32), C.POINTER(U64)]),
 }
 

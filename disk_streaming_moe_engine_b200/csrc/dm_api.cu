@@ -1121,6 +1121,205 @@ int32_t dm_gdn_state_export(dm_ctx* c, int32_t g, int32_t slot, float* S_host, f
     return DM_OK;
 }
 
+// ---- session files (KMSS v1) ------------------------------------------------------------
+// Byte layout of reference src/format/kmss.mojo: header :6-27 / write_kmss_v1 :90-170,
+// payload order :172-215 (KV: kv index, position, attention layer, head, dim), token
+// prefix :217-224, SHA-256 over header || payload :226-240, tmp + rename :242-277; checks
+// of read_kmss_v1 :280-360 in the same order with the same error types.
+
+static void put_u32(uint8_t* b, uint32_t v) {
+    for (int i = 0; i < 4; ++i) b[i] = static_cast<uint8_t>(v >> (8 * i));
+}
+static void put_u64(uint8_t* b, uint64_t v) {
+    for (int i = 0; i < 8; ++i) b[i] = static_cast<uint8_t>(v >> (8 * i));
+}
+static uint32_t get_u32(const uint8_t* b) {
+    return uint32_t(b[0]) | (uint32_t(b[1]) << 8) | (uint32_t(b[2]) << 16) | (uint32_t(b[3]) << 24);
+}
+static uint64_t get_u64(const uint8_t* b) {
+    uint64_t v = 0;
+    for (int i = 0; i < 8; ++i) v |= uint64_t(b[i]) << (8 * i);
+    return v;
+}
+static float bf16_bits_to_f32(uint16_t h) {
+    uint32_t u = static_cast<uint32_t>(h) << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+static uint16_t f32_to_bf16_rne(float f) {  // round to nearest even; NaN stays NaN
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return static_cast<uint16_t>((u >> 16) | 0x40);
+    const uint32_t r = u + 0x7FFFu + ((u >> 16) & 1u);
+    return static_cast<uint16_t>(r >> 16);
+}
+
+int32_t dm_kmss_save(dm_ctx* c, int32_t slot, const char* path, const int32_t* tokens, int32_t n_tokens,
+                     int32_t kv_dtype, const uint8_t* manifest_hash32) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    if (!path || n_tokens < 0 || (n_tokens > 0 && !tokens) || (kv_dtype != 1 && kv_dtype != 2))
+        return set_err(c, DM_ERR_INVALID_ARG, "M5_ERR_INPUT", "session", -1, "invalid session arguments");
+    const Dims& d = c->d;
+    const int len = c->slot_len[slot];
+    for (int a = 0; a < d.n_att; ++a)
+        if (c->att_len[static_cast<size_t>(a) * d.max_seqs + slot] != len)
+            return set_err(c, DM_ERR_POSITION, "M5_ERR_DECODE", "session", -1, "attention layer %d not at the slot length", a);
+    const int seq = std::max(len, static_cast<int>(n_tokens));
+    const int b_kv = kv_dtype == 1 ? 4 : 2;
+    const size_t row = static_cast<size_t>(d.Hkv) * d.D;  // one position of one layer
+    const uint64_t kv_bytes = 2ull * seq * d.n_att * row * b_kv;
+    const uint64_t gdn_dv = static_cast<uint64_t>(d.nv) * d.dv;
+    const uint64_t gdn_bytes = static_cast<uint64_t>(d.n_gdn) * gdn_dv * d.dk * 4;
+    const uint64_t tok_bytes = static_cast<uint64_t>(seq) * 4;
+    uint8_t hdr[128] = {0};
+    memcpy(hdr, "KMSS", 4);
+    put_u32(hdr + 4, 1);
+    put_u32(hdr + 8, 2);
+    if (manifest_hash32) memcpy(hdr + 12, manifest_hash32, 32);
+    put_u32(hdr + 44, seq);
+    put_u32(hdr + 48, d.V);
+    put_u32(hdr + 52, d.n_att);
+    put_u32(hdr + 56, d.Hkv);
+    put_u32(hdr + 60, d.D);
+    put_u32(hdr + 64, kv_dtype);
+    put_u32(hdr + 68, d.n_gdn);
+    put_u32(hdr + 72, static_cast<uint32_t>(gdn_dv));
+    put_u32(hdr + 76, d.dk);
+    put_u32(hdr + 80, 1);
+    put_u64(hdr + 84, kv_bytes);
+    put_u64(hdr + 92, gdn_bytes);
+    put_u64(hdr + 100, tok_bytes);
+    // KV: per attention layer the slot's len positions; positions >= len stay zero
+    std::vector<uint8_t> kv(kv_bytes, 0);
+    std::vector<uint16_t> kb(static_cast<size_t>(len) * row), vb(kb.size());
+    for (int a = 0; a < d.n_att && len > 0; ++a) {
+        if ((rc = dm_kv_export(c, a, slot, kb.data(), vb.data(), len)) != DM_OK) return rc;
+        for (int kvi = 0; kvi < 2; ++kvi) {
+            const uint16_t* src = kvi == 0 ? kb.data() : vb.data();
+            for (int p = 0; p < len; ++p) {
+                const size_t e0 = ((static_cast<size_t>(kvi) * seq + p) * d.n_att + a) * row;
+                for (size_t i = 0; i < row; ++i) {
+                    const uint16_t h = src[static_cast<size_t>(p) * row + i];
+                    if (kv_dtype == 2) {
+                        memcpy(kv.data() + (e0 + i) * 2, &h, 2);
+                    } else {
+                        const float f = bf16_bits_to_f32(h);
+                        memcpy(kv.data() + (e0 + i) * 4, &f, 4);
+                    }
+                }
+            }
+        }
+    }
+    std::vector<uint8_t> gdn(gdn_bytes);
+    for (int g = 0; g < d.n_gdn; ++g)
+        if ((rc = dm_gdn_state_export(c, g, slot, reinterpret_cast<float*>(gdn.data() + static_cast<size_t>(g) * gdn_dv * d.dk * 4),
+                                      nullptr)) != DM_OK)
+            return rc;
+    std::vector<uint8_t> tok(tok_bytes, 0);
+    for (int i = 0; i < seq; ++i) put_u32(tok.data() + 4 * i, i < n_tokens ? static_cast<uint32_t>(tokens[i]) : 0u);
+    uint8_t digest[32];
+    const uint8_t* parts[4] = {hdr, kv.data(), gdn.data(), tok.data()};
+    const size_t sizes[4] = {128, kv.size(), gdn.size(), tok.size()};
+    dm::sha256_parts(parts, sizes, 4, digest);
+    const std::string tmp = std::string(path) + ".tmp";
+    FILE* f = fopen(tmp.c_str(), "wb");
+    if (!f) return set_err(c, DM_ERR_IO, "OUTPUT_WRITE_FAILED", "session", -1, "cannot write temp KMSS file: %s", tmp.c_str());
+    bool ok = true;
+    for (int i = 0; i < 4; ++i) ok = ok && (sizes[i] == 0 || fwrite(parts[i], 1, sizes[i], f) == sizes[i]);
+    ok = ok && fwrite(digest, 1, 32, f) == 32;
+    ok = (fclose(f) == 0) && ok;
+    if (!ok) return set_err(c, DM_ERR_IO, "OUTPUT_WRITE_FAILED", "session", -1, "cannot write temp KMSS file: %s", tmp.c_str());
+    if (rename(tmp.c_str(), path) != 0)
+        return set_err(c, DM_ERR_IO, "OUTPUT_WRITE_FAILED", "session", -1, "atomic rename failed for KMSS: %s", path);
+    return DM_OK;
+}
+
+int32_t dm_kmss_load(dm_ctx* c, int32_t slot, const char* path, int32_t* tokens_out, int32_t cap, int32_t* n_tokens) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    if (!path || cap < 0 || (cap > 0 && !tokens_out))
+        return set_err(c, DM_ERR_INVALID_ARG, "M5_ERR_INPUT", "session", -1, "invalid session arguments");
+    const Dims& d = c->d;
+    FILE* f = fopen(path, "rb");
+    if (!f) return set_err(c, DM_ERR_IO, "SESSION_NOT_FOUND", "session", -1, "session file not found: %s", path);
+    fseek(f, 0, SEEK_END);
+    const long total = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    std::vector<uint8_t> all(total > 0 ? static_cast<size_t>(total) : 0);
+    const bool read_ok = total >= 0 && fread(all.data(), 1, all.size(), f) == all.size();
+    fclose(f);
+    auto fail = [&](const char* type, const char* what) {
+        return set_err(c, DM_ERR_FORMAT, type, "session", -1, "%s", what);
+    };
+    if (!read_ok || all.size() < 160) return fail("CORRUPT_SESSION_CHECKSUM", "file too small for KMSS v1");
+    const uint8_t* h = all.data();
+    if (memcmp(h, "KMSS", 4) != 0) return fail("FORMAT_MISMATCH", "invalid KMSS magic bytes");
+    if (get_u32(h + 4) != 1) return fail("VERSION_MISMATCH", "unsupported KMSS version");
+    if (get_u32(h + 8) != 2) return fail("CONFIG_MISMATCH", "unsupported KMSS architecture_id, expected 2");
+    const uint64_t seq = get_u32(h + 44), kv_layers = get_u32(h + 52), kv_heads = get_u32(h + 56),
+                   head_dim = get_u32(h + 60), kv_dtype = get_u32(h + 64), gdn_layers = get_u32(h + 68),
+                   gdn_dv = get_u32(h + 72), gdn_dk = get_u32(h + 76);
+    const uint64_t kv_bytes = get_u64(h + 84), gdn_bytes = get_u64(h + 92), tok_bytes = get_u64(h + 100);
+    const uint64_t b_kv = kv_dtype == 1 ? 4 : 2;
+    if (kv_bytes != 2 * seq * kv_layers * kv_heads * head_dim * b_kv) return fail("LAYOUT_MISMATCH", "header kv_bytes mismatch dimensions");
+    if (gdn_bytes != gdn_layers * gdn_dv * gdn_dk * 4) return fail("LAYOUT_MISMATCH", "header gdn_bytes mismatch dimensions");
+    if (tok_bytes != seq * 4) return fail("LAYOUT_MISMATCH", "header token_bytes mismatch dimensions");
+    if (all.size() != 128 + kv_bytes + gdn_bytes + tok_bytes + 32)
+        return fail("LAYOUT_MISMATCH", "total file size mismatch expected 160 + payload");
+    uint8_t digest[32];
+    const uint8_t* parts[1] = {all.data()};
+    const size_t sizes[1] = {static_cast<size_t>(128 + kv_bytes + gdn_bytes + tok_bytes)};
+    dm::sha256_parts(parts, sizes, 1, digest);
+    if (memcmp(digest, all.data() + sizes[0], 32) != 0) return fail("CORRUPT_SESSION_CHECKSUM", "checksum mismatch in KMSS file");
+    // this context's model
+    if (kv_layers != static_cast<uint64_t>(d.n_att) || kv_heads != static_cast<uint64_t>(d.Hkv) ||
+        head_dim != static_cast<uint64_t>(d.D) || gdn_layers != static_cast<uint64_t>(d.n_gdn) ||
+        gdn_dv != static_cast<uint64_t>(d.nv) * d.dv || gdn_dk != static_cast<uint64_t>(d.dk) ||
+        (kv_dtype != 1 && kv_dtype != 2))
+        return fail("CONFIG_MISMATCH", "KMSS dimensions do not match the model of this context");
+    if (seq > static_cast<uint64_t>(d.max_pages) * kPageTokens)
+        return set_err(c, DM_ERR_CAPACITY, "M5_ERR_CONTEXT_SIZE", "session", -1, "session of %llu tokens exceeds the slot capacity",
+                       static_cast<unsigned long long>(seq));
+    const uint8_t* kvp = all.data() + 128;
+    const uint8_t* gdp = kvp + kv_bytes;
+    const uint8_t* tkp = gdp + gdn_bytes;
+    if ((rc = dm_seq_reset(c, slot)) != DM_OK) return rc;
+    const size_t row = static_cast<size_t>(d.Hkv) * d.D;
+    std::vector<uint16_t> kb(seq * row), vb(seq * row);
+    for (int a = 0; a < d.n_att && seq > 0; ++a) {
+        for (int kvi = 0; kvi < 2; ++kvi) {
+            uint16_t* dst = kvi == 0 ? kb.data() : vb.data();
+            for (uint64_t p = 0; p < seq; ++p) {
+                const size_t e0 = ((static_cast<size_t>(kvi) * seq + p) * d.n_att + a) * row;
+                for (size_t i = 0; i < row; ++i) {
+                    uint16_t hb;
+                    if (kv_dtype == 2) {
+                        memcpy(&hb, kvp + (e0 + i) * 2, 2);
+                    } else {
+                        float fv;
+                        memcpy(&fv, kvp + (e0 + i) * 4, 4);
+                        hb = f32_to_bf16_rne(fv);  // the cache's single rounding to bf16
+                    }
+                    dst[p * row + i] = hb;
+                }
+            }
+        }
+        if ((rc = dm_kv_import(c, a, slot, kb.data(), vb.data(), static_cast<int32_t>(seq))) != DM_OK) return rc;
+    }
+    c->slot_len[slot] = static_cast<int>(seq);
+    c->dev_pos_valid[slot] = 0;
+    std::vector<float> S(static_cast<size_t>(gdn_dv) * gdn_dk);
+    for (int g = 0; g < d.n_gdn; ++g) {
+        memcpy(S.data(), gdp + static_cast<size_t>(g) * S.size() * 4, S.size() * 4);
+        if ((rc = dm_gdn_state_import(c, g, slot, S.data(), nullptr)) != DM_OK) return rc;  // conv window: zero
+    }
+    for (uint64_t i = 0; i < seq && static_cast<int64_t>(i) < cap; ++i) tokens_out[i] = static_cast<int32_t>(get_u32(tkp + 4 * i));
+    if (n_tokens) *n_tokens = static_cast<int32_t>(seq);
+    return DM_OK;
+}
+
 // ---- compute ------------------------------------------------------------------------
 static cudaError_t enqueue_mixer(dm_ctx* c, int layer, int slot) {
     const LayerW& w = c->layers[layer];

@@ -276,4 +276,6 @@ cudaError_t launch_b_argmax(const LaunchCfg& lc, const Dims& d, const BatchBuffe
                             int write_logits, int record_gen);
 cudaError_t batch_set_attrs();
 bool expert_tma_supported(int K);
+// SHA-256 (FIPS 180-4) of the concatenation of n buffers (dm_sha256.cu).
+void sha256_parts(const uint8_t* const* parts, const size_t* sizes, int n, uint8_t out[32]);
 }  // namespace dm

@@ -359,6 +359,24 @@ class Engine:
         u = np.ascontiguousarray(u, np.float32)
         self._ok(self.lib.dm_tensor_add_rank1(self.ctx, layer, tensor_id, _ptr(beta), beta.size, _ptr(u), u.size))
 
+    # ---- session files (reference KMSS v1, src/format/kmss.mojo) ----
+    def save_session(self, path: str, tokens, slot: int = 0, kv_dtype: int = 1, manifest_hash: bytes | None = None):
+        """write_kmss_v1 (kmss.mojo:90): the slot's KV cache and GDN states + the token prefix."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        mh = None
+        if manifest_hash is not None:
+            if len(manifest_hash) != 32:
+                raise ValueError("manifest hash: 32 bytes")
+            mh = C.create_string_buffer(bytes(manifest_hash), 32)
+        self._ok(self.lib.dm_kmss_save(self.ctx, slot, path.encode(), _ptr(t) if t.size else None, t.size, kv_dtype, mh))
+
+    def load_session(self, path: str, slot: int = 0, max_tokens: int = 1 << 20) -> np.ndarray:
+        """read_kmss_v1 (kmss.mojo:280) into `slot`; returns the token prefix."""
+        out = np.empty(max_tokens, np.int32)
+        n = C.c_int32()
+        self._ok(self.lib.dm_kmss_load(self.ctx, slot, path.encode(), _ptr(out), out.size, C.byref(n)))
+        return out[:min(n.value, out.size)].copy()
+
     # ---- expert-parallel group (one process per GPU) ----
     def ep_ipc_handle(self) -> bytes:
         buf = C.create_string_buffer(_lib.DM_EP_HANDLE_BYTES)

@@ -44,6 +44,8 @@ extern "C" {
 #define DM_ERR_TIMEOUT 7       /* a bounded device-side wait ran out                   */
 #define DM_ERR_NOT_READY 8     /* weights missing for the requested computation        */
 #define DM_ERR_ROUTER 9        /* router contract violated (e.g. norm_topk_prob)       */
+#define DM_ERR_IO 10           /* a session file could not be read or written          */
+#define DM_ERR_FORMAT 11       /* a session file failed its format / checksum checks   */
 
 /* ---- configuration ----------------------------------------------------------------- */
 /* Field names and meaning follow the reference ModelConfig
@@ -448,6 +450,25 @@ int32_t dm_batch_stats(dm_ctx* ctx, int32_t reset, uint32_t* out4);
  * the canonical dot product; NULL removes them.  Not part of the reference model (whose
  * router has no bias): a synthetic-workload device to draw a skewed expert load. */
 int32_t dm_set_router_bias(dm_ctx* ctx, int32_t layer, const float* bias_host, int32_t n);
+/* ---- session files (reference format KMSS v1, src/format/kmss.mojo) -------------------
+ * Header 128 B (magic "KMSS", version 1, architecture 2, manifest hash, dimensions, byte
+ * counts), KV cache [K|V][pos][attention layer][kv head][head_dim] as fp32 (kv_dtype 1) or
+ * bf16 (2), GDN states [gdn layer][nv * dv][dk] fp32 (the reference's [layers][dv][dk]
+ * with the V heads stacked), token ids u32, SHA-256 of all of it; written to path.tmp and
+ * renamed.  seq_len = max(the slot's length, n_tokens).  Loading checks magic, version,
+ * architecture, byte counts, file size and checksum (reference error types
+ * FORMAT_MISMATCH, VERSION_MISMATCH, CONFIG_MISMATCH, LAYOUT_MISMATCH,
+ * CORRUPT_SESSION_CHECKSUM) and that the dimensions match this context, then imports the
+ * KV pages and GDN states into `slot` and sets its length.  The format has no field for
+ * the GDN conv window: a loaded slot starts with it zero.  tokens_out receives up to cap
+ * ids; *n_tokens the file's seq_len. */
+int32_t dm_kmss_save(dm_ctx* ctx, int32_t slot, const char* path, const int32_t* tokens, int32_t n_tokens,
+                     int32_t kv_dtype, const uint8_t* manifest_hash32);
+int32_t dm_kmss_load(dm_ctx* ctx, int32_t slot, const char* path, int32_t* tokens_out, int32_t cap,
+                     int32_t* n_tokens);
+/* SHA-256 of n bytes (FIPS 180-4); needs no device. */
+int32_t dm_sha256(const uint8_t* data, uint64_t n, uint8_t* out32);
+
 /* Fills every weight of the context with the synthetic distributions of the benchmark
  * configs directly on the device (same generator; used for multi-GB models). */
 int32_t dm_synth_model_device(dm_ctx* ctx, uint64_t seed);
