@@ -29,6 +29,10 @@ DM_KERNEL_ROUTER, DM_KERNEL_MOE, DM_KERNEL_HEAD = 3, 4, 6
 DM_BKERNEL_ATTN, DM_BKERNEL_GDN_REC, DM_BKERNEL_EXPERTS = 0, 1, 2
 DM_EP_HANDLE_BYTES = 64
 
+DM_GGML_F32, DM_GGML_F16, DM_GGML_Q8_0, DM_GGML_Q3_K, DM_GGML_Q4_K, DM_GGML_BF16 = 0, 1, 8, 11, 12, 30
+DM_GGUF_Q4K_MOJO = 1
+DM_LOAD_REQUANT = 2
+
 DM_DTYPE_BF16 = 0
 DM_DTYPE_F32 = 1
 DM_PROJ_GATE, DM_PROJ_UP, DM_PROJ_DOWN = 0, 1, 2
@@ -59,6 +63,19 @@ class DmRuntimeConfig(C.Structure):
                 ("kv_num_pages", C.c_int32), ("max_pages_per_seq", C.c_int32)]
 
 
+class DmGgufTensorInfo(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("ndim", C.c_int32), ("ggml_type", C.c_int32),
+                ("dims", C.c_uint64 * 8), ("offset", C.c_uint64), ("file_offset", C.c_uint64),
+                ("num_elements", C.c_uint64), ("raw_bytes", C.c_uint64)]
+
+
+class DmQuantTensorInfo(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_char_p), ("ndim", C.c_int32), ("group_size", C.c_int32),
+                ("shape", C.c_uint64 * 8), ("num_groups", C.c_uint64), ("num_elements", C.c_uint64),
+                ("record_offset", C.c_uint64), ("scales_offset", C.c_uint64), ("data_offset", C.c_uint64),
+                ("scales_bytes", C.c_uint64), ("weights_bytes", C.c_uint64)]
+
+
 P = C.c_void_p
 I32 = C.c_int32
 U64 = C.c_uint64
@@ -75,6 +92,8 @@ SIGNATURES = {
     "dm_upload_tensor": (I32, [P, I32, I32, I32, P, U64]),
     "dm_expert_upload": (I32, [P, I32, I32, I32, P, P, P]),
     "dm_weights_check": (I32, [P]),
+    "dm_tensor_download": (I32, [P, I32, I32, I32, P, U64]),
+    "dm_expert_download": (I32, [P, I32, I32, I32, P, P, P]),
     "dm_dequant_q4": (I32, [P, P, P, P, I32, I32, I32, P]),
     "dm_dequant_sym4": (I32, [P, P, P, C.c_int64, I32, P, P]),
     "dm_seq_reset": (I32, [P, I32]),
@@ -123,6 +142,31 @@ SIGNATURES = {
     "dm_kmss_save": (I32, [P, I32, C.c_char_p, P, I32, I32, P]),
     "dm_kmss_load": (I32, [P, I32, C.c_char_p, P, I32, C.POINTER(I32)]),
     "dm_sha256": (I32, [P, U64, P]),
+    "dm_gguf_open": (I32, [C.c_char_p, C.POINTER(P), C.c_char_p, U64]),
+    "dm_gguf_close": (None, [P]),
+    "dm_gguf_summary": (I32, [P, C.POINTER(C.c_uint32), C.POINTER(U64), C.POINTER(U64), C.POINTER(U64),
+                              C.POINTER(U64), C.POINTER(U64)]),
+    "dm_gguf_tensor": (I32, [P, C.c_int64, C.POINTER(DmGgufTensorInfo)]),
+    "dm_gguf_find": (C.c_int64, [P, C.c_char_p]),
+    "dm_gguf_meta_key": (I32, [P, C.c_int64, C.c_char_p, U64]),
+    "dm_gguf_meta": (I32, [P, C.c_char_p, C.c_char_p, U64]),
+    "dm_gguf_read": (I32, [P, C.c_int64, U64, P, U64]),
+    "dm_ggml_block_spec": (I32, [I32, C.POINTER(I32), C.POINTER(I32)]),
+    "dm_gguf_dequant": (I32, [P, I32, P, U64, U64, C.c_uint32, P, P]),
+    "dm_gguf_load_tensor": (I32, [P, P, C.c_char_p, I32, I32, C.c_uint32]),
+    "dm_gguf_load_expert": (I32, [P, P, C.c_char_p, C.c_int64, C.c_int64, I32, I32, I32, C.c_uint32,
+                                  C.POINTER(F32)]),
+    "dm_quant_file_open": (I32, [C.c_char_p, C.POINTER(P), C.c_char_p, U64]),
+    "dm_quant_file_close": (None, [P]),
+    "dm_quant_file_summary": (I32, [P, C.POINTER(I32), C.POINTER(I32), C.POINTER(C.c_int64), C.POINTER(U64),
+                                    C.c_char_p, U64]),
+    "dm_quant_file_tensor": (I32, [P, C.c_int64, C.POINTER(DmQuantTensorInfo)]),
+    "dm_quant_file_find": (C.c_int64, [P, C.c_char_p]),
+    "dm_quant_file_read": (I32, [P, C.c_int64, I32, U64, P, U64]),
+    "dm_quant_file_load_tensor": (I32, [P, P, C.c_char_p, I32, I32]),
+    "dm_quant_file_load_expert": (I32, [P, P, C.c_char_p, C.c_int64, C.c_int64, I32, I32, I32, C.c_uint32,
+                                        C.POINTER(F32)]),
+    "dm_quant_file_load": (I32, [P, P, C.c_uint32]),
     "dm_time_batch_kernel": (I32, [P, I32, I32, I32, I32, C.POINTER(F32), C.POINTER(U64)]),
 }
 

@@ -48,6 +48,14 @@ cudaError_t launch_rank1_add_bf16(cudaStream_t st, uint16_t* W, int64_t rows, in
                                   const float* u);
 cudaError_t launch_synth_f16abs(cudaStream_t st, uint16_t* dst, uint64_t n, uint64_t seed,
                                 uint64_t stream_id, float std);
+bool gguf_type_supported(int type);
+cudaError_t launch_gguf_dequant(cudaStream_t st, int type, const uint8_t* raw, int64_t n, unsigned flags,
+                                float* out_f32, uint16_t* out_bf16);
+cudaError_t launch_sym4_to_pool(cudaStream_t st, const uint8_t* packed, const uint16_t* scales, int64_t e0, int rows,
+                                int cols, int gf, int gp, uint8_t* q_out, uint16_t* s_out, uint8_t* z_out,
+                                unsigned* flags);
+cudaError_t launch_requant_pool(cudaStream_t st, const float* w, int rows, int cols, int gp, uint8_t* q_out,
+                                uint16_t* s_out, uint8_t* z_out, unsigned* flags, unsigned* max_err_bits);
 }  // namespace dm
 
 using namespace dm;
@@ -72,6 +80,12 @@ struct dm_ctx {
     uint8_t* stage_q = nullptr;
     uint16_t* stage_s = nullptr;
     uint8_t* stage_z = nullptr;
+    // quant-file loader staging (allocated on first use): pinned host chunk, device chunk,
+    // an fp32 projection buffer and two status words
+    void* ld_host = nullptr;
+    uint8_t* ld_dev = nullptr;
+    float* ld_f32 = nullptr;
+    unsigned* ld_word = nullptr;
     // pinned host staging for per-step transfers
     int* h_io = nullptr;  // [0] token in, [1] token out, [2] error word, [3] pos
     // coverage
@@ -706,6 +720,8 @@ int32_t dm_ctx_destroy(dm_ctx* c) {
     if (c->arena) cudaFree(c->arena);
     if (c->flush_buf) cudaFree(c->flush_buf);
     if (c->h_io) cudaFreeHost(c->h_io);
+    if (c->ld_host) cudaFreeHost(c->ld_host);
+    if (c->ld_dev) cudaFree(c->ld_dev);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
     return DM_OK;
@@ -833,6 +849,48 @@ int32_t dm_expert_upload(dm_ctx* c, int32_t layer, int32_t expert, int32_t proj,
     return DM_OK;
 }
 
+int32_t dm_tensor_download(dm_ctx* c, int32_t layer, int32_t id, int32_t dtype, void* out, uint64_t n) {
+    if (!c || !out) return DM_ERR_INVALID_ARG;
+    void* src = nullptr;
+    size_t bytes = 0;
+    int rc = tensor_target(c, layer, id, dtype, n, &src, &bytes);
+    if (rc != DM_OK) return rc;
+    cudaSetDevice(c->device);
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
+    DM_CUDA(c, cudaMemcpy(out, src, bytes, cudaMemcpyDeviceToHost), "loader");
+    return DM_OK;
+}
+
+// Inverse of the row repack (repack_rows_kernel): the record's chunks -> canonical rows.
+int32_t dm_expert_download(dm_ctx* c, int32_t layer, int32_t expert, int32_t proj, uint8_t* q, uint16_t* s,
+                           uint8_t* z) {
+    if (!c || !q || !s || !z) return DM_ERR_INVALID_ARG;
+    const Dims& d = c->d;
+    if (layer < 0 || layer >= d.L || expert < -1 || expert >= d.E || proj < 0 || proj > 2)
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer, "expert index out of range");
+    const int rows = proj == DM_PROJ_DOWN ? d.H : d.I;
+    const int cols = proj == DM_PROJ_DOWN ? d.I : d.H;
+    const int ng = cols / d.G;
+    const size_t qb = cols / 2, sb = static_cast<size_t>(ng) * 2, zb = ng / 2;
+    const size_t chunk_bytes = 16 * (qb + sb + zb);
+    const int nchunks = proj == DM_PROJ_DOWN ? rows / 16 : rows / 8;
+    uint8_t* rec = expert_record(c, layer, expert);
+    const uint8_t* src = proj == DM_PROJ_DOWN ? rec + static_cast<size_t>(d.gu_chunks) * d.gu_chunk_bytes : rec;
+    std::vector<uint8_t> h(chunk_bytes * nchunks);
+    cudaSetDevice(c->device);
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
+    DM_CUDA(c, cudaMemcpy(h.data(), src, h.size(), cudaMemcpyDeviceToHost), "loader");
+    for (int r = 0; r < rows; ++r) {
+        const int chunk = proj == DM_PROJ_DOWN ? r / 16 : r / 8;
+        const int rin = proj == DM_PROJ_DOWN ? r % 16 : (proj == DM_PROJ_UP ? 8 : 0) + r % 8;
+        const uint8_t* cb = h.data() + chunk * chunk_bytes;
+        memcpy(q + static_cast<size_t>(r) * qb, cb + rin * qb, qb);
+        memcpy(s + static_cast<size_t>(r) * ng, cb + 16 * qb + rin * sb, sb);
+        memcpy(z + static_cast<size_t>(r) * zb, cb + 16 * qb + 16 * sb + rin * zb, zb);
+    }
+    return DM_OK;
+}
+
 static const char* tensor_name(int id) {
     static const char* names[DM_T_COUNT] = {
         "input_layernorm.weight", "post_attention_layernorm.weight", "linear_attn.in_proj_qkv.weight",
@@ -946,6 +1004,414 @@ int32_t dm_dequant_sym4(dm_ctx* c, const uint8_t* packed, const uint16_t* scales
     if (bad)
         return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1,
                        "reserved nibble 0b1000 (-8) encountered");
+    return DM_OK;
+}
+
+// ---- quant-file loaders ---------------------------------------------------------------
+// Chunks of at most kLdBytes go file -> pinned host -> device -> dequant/convert kernel;
+// dense tensors land in their weights directly, expert projections go through the stage
+// buffers and the row repack of dm_expert_upload.
+static constexpr size_t kLdBytes = 32u << 20;
+static constexpr size_t kLdScaleOff = 24u << 20;  // scales of a custom-format chunk
+static constexpr uint64_t kLdSym4Elems = 32ull << 20;  // elements per custom-format chunk
+
+static int slot_dtype(int id) { return (id == DM_T_GDN_DT_BIAS || id == DM_T_GDN_A_LOG) ? DM_DTYPE_F32 : DM_DTYPE_BF16; }
+
+static int loader_staging(dm_ctx* c) {
+    if (c->ld_host) return DM_OK;
+    cudaSetDevice(c->device);
+    const size_t f32_elems = static_cast<size_t>(c->d.I) * c->d.H;
+    void* h = nullptr;
+    uint8_t* dv = nullptr;
+    DM_CUDA(c, cudaMallocHost(&h, kLdBytes), "loader");
+    const cudaError_t e = cudaMalloc(&dv, kLdBytes + f32_elems * 4 + 256);
+    if (e != cudaSuccess) {
+        cudaFreeHost(h);
+        return set_err(c, DM_ERR_OOM, "CUDA_ERROR", "loader", -1, "loader staging: %s", cudaGetErrorString(e));
+    }
+    c->ld_host = h;
+    c->ld_dev = dv;
+    c->ld_f32 = reinterpret_cast<float*>(dv + kLdBytes);
+    c->ld_word = reinterpret_cast<unsigned*>(dv + kLdBytes + f32_elems * 4);
+    return DM_OK;
+}
+
+static int expert_geometry(dm_ctx* c, int layer, int expert, int proj, int* rows, int* cols) {
+    const Dims& d = c->d;
+    if (layer < 0 || layer >= d.L || expert < -1 || expert >= d.E || proj < 0 || proj > 2)
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer, "expert index out of range");
+    *rows = proj == DM_PROJ_DOWN ? d.H : d.I;
+    *cols = proj == DM_PROJ_DOWN ? d.I : d.H;
+    if (*cols % (2 * d.G) != 0)
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                       "row length %d is not a multiple of two pool groups", *cols);
+    return DM_OK;
+}
+
+// stage buffers (q, s, z of rows x cols) -> the expert record
+static int pool_commit(dm_ctx* c, int rows, int cols, int layer, int expert, int proj) {
+    const Dims& d = c->d;
+    uint8_t* rec = expert_record(c, layer, expert);
+    uint8_t* dst = proj == DM_PROJ_DOWN ? rec + static_cast<size_t>(d.gu_chunks) * d.gu_chunk_bytes : rec;
+    DM_CUDA(c, launch_repack_rows(c->stream, c->stage_q, c->stage_s, c->stage_z, rows, cols, d.G, proj, dst), "loader");
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
+    c->have_expert[(static_cast<size_t>(layer) * (d.E + 1) + (expert + 1)) * 3 + proj] = 1;
+    return DM_OK;
+}
+
+// c->ld_f32 (rows x cols fp32) -> re-quantised stage buffers -> the expert record
+static int requant_commit(dm_ctx* c, int rows, int cols, int layer, int expert, int proj, float* max_err) {
+    unsigned w[2] = {0, 0};
+    DM_CUDA(c, cudaMemsetAsync(c->ld_word, 0, 8, c->stream), "loader");
+    DM_CUDA(c, launch_requant_pool(c->stream, c->ld_f32, rows, cols, c->d.G, c->stage_q, c->stage_s, c->stage_z,
+                                   c->ld_word, c->ld_word + 1), "loader");
+    DM_CUDA(c, cudaMemcpyAsync(w, c->ld_word, 8, cudaMemcpyDeviceToHost, c->stream), "loader");
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
+    if (w[0] & 8u)
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                       "non-finite weight in expert %d projection %d", expert, proj);
+    float e;
+    memcpy(&e, &w[1], 4);
+    if (max_err) *max_err = e;
+    return pool_commit(c, rows, cols, layer, expert, proj);
+}
+
+// Elements [first, first + n) of GGUF tensor ti dequantised into out_f32 / out_bf16
+// (device pointers), chunk by chunk.
+static int gguf_stream(dm_ctx* c, const dm_gguf* g, int64_t ti, const dm_gguf_tensor_info& info, uint64_t first,
+                       uint64_t n, float* out_f32, uint16_t* out_bf16, unsigned flags, int layer) {
+    int bs, bpb;
+    dm_ggml_block_spec(info.ggml_type, &bs, &bpb);
+    if (first % bs || n % bs)
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                       "tensor %s: range [%llu, +%llu) is not whole %d-element blocks", info.name,
+                       (unsigned long long)first, (unsigned long long)n, bs);
+    int rc = loader_staging(c);
+    if (rc != DM_OK) return rc;
+    const uint64_t per = kLdBytes / bpb;
+    const uint64_t b_end = (first + n) / bs;
+    for (uint64_t b0 = first / bs; b0 < b_end; b0 += per) {
+        const uint64_t nb = b_end - b0 < per ? b_end - b0 : per;
+        rc = dm_gguf_read(g, ti, b0 * bpb, c->ld_host, nb * bpb);
+        if (rc != DM_OK)
+            return set_err(c, DM_ERR_IO, "GGUF_READ_ERROR", "loader", layer, "truncated read for tensor %s", info.name);
+        DM_CUDA(c, cudaMemcpyAsync(c->ld_dev, c->ld_host, nb * bpb, cudaMemcpyHostToDevice, c->stream), "loader");
+        const uint64_t o = b0 * bs - first;
+        DM_CUDA(c, launch_gguf_dequant(c->stream, info.ggml_type, c->ld_dev, static_cast<int64_t>(nb * bs), flags,
+                                       out_f32 ? out_f32 + o : nullptr, out_bf16 ? out_bf16 + o : nullptr), "loader");
+        DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
+    }
+    return DM_OK;
+}
+
+static int gguf_lookup(dm_ctx* c, const dm_gguf* g, const char* name, int layer, int64_t* ti,
+                       dm_gguf_tensor_info* info) {
+    if (!g || !name) return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer, "null argument");
+    *ti = dm_gguf_find(g, name);
+    if (*ti < 0)
+        return set_err(c, DM_ERR_NOT_READY, "WEIGHT_LOAD_FAILED", "loader", layer, "tensor not found in GGUF index: %s", name);
+    dm_gguf_tensor(g, *ti, info);
+    if (!gguf_type_supported(info->ggml_type))
+        return set_err(c, DM_ERR_INVALID_ARG, "GGUF_UNSUPPORTED_DTYPE", "loader", layer,
+                       "unsupported GGML type %d for tensor %s", info->ggml_type, name);
+    return DM_OK;
+}
+
+int32_t dm_gguf_dequant(dm_ctx* c, int32_t type, const void* raw, uint64_t raw_bytes, uint64_t n, uint32_t flags,
+                        float* out_f32, uint16_t* out_bf16) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    if (!raw || (!out_f32 && !out_bf16))
+        return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1, "null buffer");
+    if (!gguf_type_supported(type))
+        return set_err(c, DM_ERR_INVALID_ARG, "GGUF_UNSUPPORTED_DTYPE", "dequant", -1, "unsupported GGML type %d", type);
+    int bs, bpb;
+    dm_ggml_block_spec(type, &bs, &bpb);
+    if (n == 0 || n % bs)
+        return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1,
+                       "%llu elements is not a positive multiple of the %d-element block", (unsigned long long)n, bs);
+    const uint64_t need = n / bs * bpb;
+    if (raw_bytes < need)
+        return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "dequant", -1, "%llu raw bytes, %llu needed",
+                       (unsigned long long)raw_bytes, (unsigned long long)need);
+    cudaSetDevice(c->device);
+    const size_t o_f = (need + 255) & ~size_t(255);
+    const size_t o_b = o_f + (out_f32 ? ((n * 4 + 255) & ~size_t(255)) : 0);
+    const size_t total = o_b + (out_bf16 ? n * 2 : 0) + 256;
+    uint8_t* tmp = nullptr;
+    DM_CUDA(c, cudaMalloc(&tmp, total), "dequant");
+    float* df = out_f32 ? reinterpret_cast<float*>(tmp + o_f) : nullptr;
+    uint16_t* db = out_bf16 ? reinterpret_cast<uint16_t*>(tmp + o_b) : nullptr;
+    cudaError_t e = cudaMemcpyAsync(tmp, raw, need, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = launch_gguf_dequant(c->stream, type, tmp, static_cast<int64_t>(n), flags, df, db);
+    if (e == cudaSuccess && df) e = cudaMemcpyAsync(out_f32, df, n * 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess && db) e = cudaMemcpyAsync(out_bf16, db, n * 2, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "dequant", -1, "%s", cudaGetErrorString(e));
+    return DM_OK;
+}
+
+int32_t dm_gguf_load_tensor(dm_ctx* c, const dm_gguf* g, const char* name, int32_t layer, int32_t id, uint32_t flags) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    int64_t ti;
+    dm_gguf_tensor_info info;
+    int rc = gguf_lookup(c, g, name, layer, &ti, &info);
+    if (rc != DM_OK) return rc;
+    const int dt = slot_dtype(id);
+    void* dst = nullptr;
+    size_t bytes = 0;
+    rc = tensor_target(c, layer, id, dt, info.num_elements, &dst, &bytes);
+    if (rc != DM_OK) return rc;
+    cudaSetDevice(c->device);
+    rc = gguf_stream(c, g, ti, info, 0, info.num_elements, dt == DM_DTYPE_F32 ? static_cast<float*>(dst) : nullptr,
+                     dt == DM_DTYPE_BF16 ? static_cast<uint16_t*>(dst) : nullptr, flags, layer);
+    if (rc != DM_OK) return rc;
+    c->have_dense[static_cast<size_t>(layer + 1) * DM_T_COUNT + id] = 1;
+    return DM_OK;
+}
+
+// first element of a (slab, row0) slice of a tensor whose innermost length is `inner`
+// and whose slabs hold `slab_elems` elements
+static int slice_start(dm_ctx* c, const char* name, int layer, uint64_t inner, uint64_t slab_elems, uint64_t total,
+                       int64_t slab, int64_t row0, int rows, int cols, uint64_t* first) {
+    if (inner != static_cast<uint64_t>(cols))
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                       "tensor %s: rows of %llu elements, the projection has %d", name, (unsigned long long)inner, cols);
+    if (slab < 0 || row0 < 0)
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer, "negative slab or row");
+    const uint64_t f = static_cast<uint64_t>(slab) * slab_elems + static_cast<uint64_t>(row0) * cols;
+    const uint64_t n = static_cast<uint64_t>(rows) * cols;
+    if (static_cast<uint64_t>(row0) * cols + n > slab_elems || f + n > total)
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                       "tensor %s: slice (slab %lld, row %lld, %d rows) is outside the tensor", name,
+                       (long long)slab, (long long)row0, rows);
+    *first = f;
+    return DM_OK;
+}
+
+int32_t dm_gguf_load_expert(dm_ctx* c, const dm_gguf* g, const char* name, int64_t slab, int64_t row0, int32_t layer,
+                            int32_t expert, int32_t proj, uint32_t flags, float* max_err) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    int rows, cols;
+    int rc = expert_geometry(c, layer, expert, proj, &rows, &cols);
+    if (rc != DM_OK) return rc;
+    int64_t ti;
+    dm_gguf_tensor_info info;
+    rc = gguf_lookup(c, g, name, layer, &ti, &info);
+    if (rc != DM_OK) return rc;
+    const uint64_t slab_elems = info.ndim >= 2 ? info.dims[0] * info.dims[1] : info.num_elements;
+    uint64_t first;
+    rc = slice_start(c, name, layer, info.dims[0], slab_elems, info.num_elements, slab, row0, rows, cols, &first);
+    if (rc != DM_OK) return rc;
+    if (!(flags & DM_LOAD_REQUANT))
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                       "tensor %s: GGML type %d is not representable exactly in the 4-bit g%d expert pool "
+                       "(re-quantisation needs DM_LOAD_REQUANT)", name, info.ggml_type, c->d.G);
+    cudaSetDevice(c->device);
+    if ((rc = loader_staging(c)) != DM_OK) return rc;  // c->ld_f32 exists from here on
+    rc = gguf_stream(c, g, ti, info, first, static_cast<uint64_t>(rows) * cols, c->ld_f32, nullptr, flags, layer);
+    if (rc != DM_OK) return rc;
+    return requant_commit(c, rows, cols, layer, expert, proj, max_err);
+}
+
+static int qf_lookup(dm_ctx* c, const dm_quant_file* q, const char* name, int layer, int64_t* ti,
+                     dm_quant_tensor_info* info) {
+    if (!q || !name) return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer, "null argument");
+    *ti = dm_quant_file_find(q, name);
+    if (*ti < 0)
+        return set_err(c, DM_ERR_NOT_READY, "WEIGHT_LOAD_FAILED", "loader", layer, "tensor not found in quant model: %s",
+                       name);
+    dm_quant_file_tensor(q, *ti, info);
+    return DM_OK;
+}
+
+// Elements [first, first + n) of a custom-format tensor (first, n multiples of its group)
+// into ld_host: the scales at kLdScaleOff, the nibbles at 0; then onto the device at the
+// same offsets.  Every scale is checked first (validate_quant_payload,
+// quant_reader.mojo:464-494).
+static int qf_stage(dm_ctx* c, const dm_quant_file* q, int64_t ti, const dm_quant_tensor_info& info, uint64_t first,
+                    uint64_t n, int layer) {
+    const uint64_t G = static_cast<uint64_t>(info.group_size);
+    auto* h = static_cast<uint8_t*>(c->ld_host);
+    if (dm_quant_file_read(q, ti, 0, first / G * 2, h + kLdScaleOff, n / G * 2) != DM_OK ||
+        dm_quant_file_read(q, ti, 1, first / 2, h, n / 2) != DM_OK)
+        return set_err(c, DM_ERR_IO, "WEIGHT_LOAD_FAILED", "loader", layer, "short read of tensor %s", info.name);
+    const uint16_t* s = reinterpret_cast<const uint16_t*>(h + kLdScaleOff);
+    for (uint64_t i = 0; i < n / G; ++i) {
+        if (((s[i] >> 10) & 0x1F) == 0x1F)
+            return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "loader", layer, "scale is NaN or Inf in tensor: %s",
+                           info.name);
+        if ((s[i] & 0x8000u) || (s[i] & 0x7FFFu) == 0)
+            return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "loader", layer, "scale is non-positive in tensor: %s",
+                           info.name);
+    }
+    DM_CUDA(c, cudaMemcpyAsync(c->ld_dev, h, n / 2, cudaMemcpyHostToDevice, c->stream), "loader");
+    DM_CUDA(c, cudaMemcpyAsync(c->ld_dev + kLdScaleOff, h + kLdScaleOff, n / G * 2, cudaMemcpyHostToDevice, c->stream),
+            "loader");
+    return DM_OK;
+}
+
+int32_t dm_quant_file_load_tensor(dm_ctx* c, const dm_quant_file* q, const char* name, int32_t layer, int32_t id) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    int64_t ti;
+    dm_quant_tensor_info info;
+    int rc = qf_lookup(c, q, name, layer, &ti, &info);
+    if (rc != DM_OK) return rc;
+    const int dt = slot_dtype(id);
+    void* dst = nullptr;
+    size_t bytes = 0;
+    rc = tensor_target(c, layer, id, dt, info.num_elements, &dst, &bytes);
+    if (rc != DM_OK) return rc;
+    cudaSetDevice(c->device);
+    if ((rc = loader_staging(c)) != DM_OK) return rc;
+    const uint64_t N = info.num_elements;
+    for (uint64_t e0 = 0; e0 < N; e0 += kLdSym4Elems) {
+        const uint64_t n = N - e0 < kLdSym4Elems ? N - e0 : kLdSym4Elems;
+        if ((rc = qf_stage(c, q, ti, info, e0, n, layer)) != DM_OK) return rc;
+        DM_CUDA(c, cudaMemsetAsync(c->ld_word, 0, 4, c->stream), "loader");
+        DM_CUDA(c, launch_dequant_sym4(c->stream, c->ld_dev, reinterpret_cast<const uint16_t*>(c->ld_dev + kLdScaleOff),
+                                       static_cast<int64_t>(n), info.group_size,
+                                       dt == DM_DTYPE_BF16 ? static_cast<uint16_t*>(dst) + e0 : nullptr,
+                                       dt == DM_DTYPE_F32 ? static_cast<float*>(dst) + e0 : nullptr, c->ld_word),
+                "loader");
+        unsigned badw = 0;
+        DM_CUDA(c, cudaMemcpyAsync(&badw, c->ld_word, 4, cudaMemcpyDeviceToHost, c->stream), "loader");
+        DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
+        if (badw)
+            return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "loader", layer,
+                           "reserved nibble 0x8 (-8) in tensor: %s", info.name);
+    }
+    c->have_dense[static_cast<size_t>(layer + 1) * DM_T_COUNT + id] = 1;
+    return DM_OK;
+}
+
+int32_t dm_quant_file_load_expert(dm_ctx* c, const dm_quant_file* q, const char* name, int64_t slab, int64_t row0,
+                                  int32_t layer, int32_t expert, int32_t proj, uint32_t flags, float* max_err) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    int rows, cols;
+    int rc = expert_geometry(c, layer, expert, proj, &rows, &cols);
+    if (rc != DM_OK) return rc;
+    int64_t ti;
+    dm_quant_tensor_info info;
+    rc = qf_lookup(c, q, name, layer, &ti, &info);
+    if (rc != DM_OK) return rc;
+    const int nd = info.ndim;
+    const uint64_t inner = info.shape[nd - 1];
+    const uint64_t slab_elems = nd >= 2 ? info.shape[nd - 1] * info.shape[nd - 2] : info.num_elements;
+    uint64_t first;
+    rc = slice_start(c, name, layer, inner, slab_elems, info.num_elements, slab, row0, rows, cols, &first);
+    if (rc != DM_OK) return rc;
+    const uint64_t n = static_cast<uint64_t>(rows) * cols;
+    if (first % info.group_size || n % info.group_size)
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                       "tensor %s: the slice does not start on a group boundary", name);
+    cudaSetDevice(c->device);
+    if ((rc = loader_staging(c)) != DM_OK) return rc;
+    if ((rc = qf_stage(c, q, ti, info, first, n, layer)) != DM_OK) return rc;
+    const uint16_t* ds = reinterpret_cast<const uint16_t*>(c->ld_dev + kLdScaleOff);
+    unsigned w = 0;
+    DM_CUDA(c, cudaMemsetAsync(c->ld_word, 0, 4, c->stream), "loader");
+    DM_CUDA(c, launch_sym4_to_pool(c->stream, c->ld_dev, ds, 0, rows, cols, info.group_size, c->d.G, c->stage_q,
+                                   c->stage_s, c->stage_z, c->ld_word), "loader");
+    DM_CUDA(c, cudaMemcpyAsync(&w, c->ld_word, 4, cudaMemcpyDeviceToHost, c->stream), "loader");
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
+    if (w & 1u)
+        return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "loader", layer, "reserved nibble 0x8 (-8) in tensor: %s",
+                       name);
+    if (w & 2u)
+        return set_err(c, DM_ERR_INVALID_ARG, "DEQUANT_ERROR", "loader", layer, "invalid scale in tensor: %s", name);
+    if (!(w & 4u)) {
+        if (max_err) *max_err = 0.0f;
+        return pool_commit(c, rows, cols, layer, expert, proj);
+    }
+    if (!(flags & DM_LOAD_REQUANT))
+        return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", layer,
+                       "tensor %s: groups of %d with different scales inside one pool group of %d are not "
+                       "representable exactly (re-quantisation needs DM_LOAD_REQUANT)", name, info.group_size, c->d.G);
+    DM_CUDA(c, cudaMemsetAsync(c->ld_word, 0, 4, c->stream), "loader");
+    DM_CUDA(c, launch_dequant_sym4(c->stream, c->ld_dev, ds, static_cast<int64_t>(n), info.group_size, nullptr,
+                                   c->ld_f32, c->ld_word), "loader");
+    return requant_commit(c, rows, cols, layer, expert, proj, max_err);
+}
+
+int32_t dm_quant_file_load(dm_ctx* c, const dm_quant_file* q, uint32_t flags) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    if (!q) return set_err(c, DM_ERR_INVALID_ARG, "WEIGHT_LOAD_FAILED", "loader", -1, "null quant file");
+    const Dims& d = c->d;
+    auto has = [&](const std::string& s) { return dm_quant_file_find(q, s.c_str()) >= 0; };
+    auto pick = [&](std::initializer_list<std::string> names) -> std::string {
+        for (const std::string& s : names)
+            if (has(s)) return s;
+        return std::string();
+    };
+    auto missing = [&](int layer, const std::string& what) {
+        return set_err(c, DM_ERR_NOT_READY, "WEIGHT_LOAD_FAILED", "loader", layer, "tensor not found in quant model: %s",
+                       what.c_str());
+    };
+    struct G { int id; const char* a; const char* b; };
+    const G globals[] = {{DM_T_EMBED, "model.language_model.embed_tokens.weight", "model.embed_tokens.weight"},
+                         {DM_T_FINAL_NORM, "model.language_model.norm.weight", "model.norm.weight"},
+                         {DM_T_LM_HEAD, "lm_head.weight", "lm_head.weight"}};
+    // a weight the file lacks may have been uploaded before (e.g. tensors too small for the
+    // format's groups); only what is still missing is an error
+    auto have_dense = [&](int layer, int id) { return c->have_dense[static_cast<size_t>(layer + 1) * DM_T_COUNT + id] != 0; };
+    auto have_expert = [&](int layer, int e, int p) {
+        return c->have_expert[(static_cast<size_t>(layer) * (d.E + 1) + (e + 1)) * 3 + p] != 0;
+    };
+    int rc;
+    for (const G& gl : globals) {
+        const std::string nm = pick({gl.a, gl.b});
+        if (nm.empty() && have_dense(-1, gl.id)) continue;
+        if (nm.empty()) return missing(-1, gl.a);
+        if ((rc = dm_quant_file_load_tensor(c, q, nm.c_str(), -1, gl.id)) != DM_OK) return rc;
+    }
+    const int gdn_ids[] = {DM_T_INPUT_NORM, DM_T_POST_NORM, DM_T_GDN_QKV, DM_T_GDN_CONV, DM_T_GDN_Z, DM_T_GDN_A,
+                           DM_T_GDN_B, DM_T_GDN_DT_BIAS, DM_T_GDN_A_LOG, DM_T_GDN_NORM, DM_T_GDN_OUT,
+                           DM_T_ROUTER, DM_T_SHARED_GATE};
+    const int att_ids[] = {DM_T_INPUT_NORM, DM_T_POST_NORM, DM_T_ATTN_Q, DM_T_ATTN_K, DM_T_ATTN_V,
+                           DM_T_ATTN_Q_NORM, DM_T_ATTN_K_NORM, DM_T_ATTN_O, DM_T_ROUTER, DM_T_SHARED_GATE};
+    static const char* proj_names[3] = {"gate_proj.weight", "up_proj.weight", "down_proj.weight"};
+    for (int l = 0; l < d.L; ++l) {
+        const std::string p1 = "model.language_model.layers." + std::to_string(l) + ".";
+        const std::string p2 = "model.layers." + std::to_string(l) + ".";
+        const bool att = c->layers[l].is_attn;
+        const int* ids = att ? att_ids : gdn_ids;
+        const int nids = att ? 10 : 13;
+        for (int i = 0; i < nids; ++i) {
+            const std::string nm = pick({p1 + tensor_name(ids[i]), p2 + tensor_name(ids[i])});
+            if (nm.empty() && have_dense(l, ids[i])) continue;
+            if (nm.empty()) return missing(l, p2 + tensor_name(ids[i]));
+            if ((rc = dm_quant_file_load_tensor(c, q, nm.c_str(), l, ids[i])) != DM_OK) return rc;
+        }
+        for (int p = 0; p < 3; ++p) {
+            const std::string nm = pick({p1 + "mlp.shared_expert." + proj_names[p], p2 + "mlp.shared_expert." + proj_names[p]});
+            if (nm.empty() && have_expert(l, -1, p)) continue;
+            if (nm.empty()) return missing(l, p2 + "mlp.shared_expert." + proj_names[p]);
+            if ((rc = dm_quant_file_load_expert(c, q, nm.c_str(), 0, 0, l, -1, p, flags, nullptr)) != DM_OK) return rc;
+        }
+        const std::string gu = pick({p1 + "mlp.experts.gate_up_proj", p2 + "mlp.experts.gate_up_proj",
+                                     p1 + "mlp.experts.gate_up_proj.weight", p2 + "mlp.experts.gate_up_proj.weight"});
+        const std::string dn = pick({p1 + "mlp.experts.down_proj", p2 + "mlp.experts.down_proj",
+                                     p1 + "mlp.experts.down_proj.weight", p2 + "mlp.experts.down_proj.weight"});
+        for (int e = 0; e < d.E; ++e) {
+            const std::string pe = "mlp.experts." + std::to_string(e) + ".";
+            for (int p = 0; p < 3; ++p) {
+                const std::string nm = pick({p1 + pe + proj_names[p], p2 + pe + proj_names[p]});
+                if (!nm.empty()) {
+                    rc = dm_quant_file_load_expert(c, q, nm.c_str(), 0, 0, l, e, p, flags, nullptr);
+                } else if (p < 2 && !gu.empty()) {
+                    rc = dm_quant_file_load_expert(c, q, gu.c_str(), e, p == DM_PROJ_UP ? d.I : 0, l, e, p, flags, nullptr);
+                } else if (p == 2 && !dn.empty()) {
+                    rc = dm_quant_file_load_expert(c, q, dn.c_str(), e, 0, l, e, p, flags, nullptr);
+                } else if (have_expert(l, e, p)) {
+                    rc = DM_OK;
+                } else {
+                    return missing(l, p2 + pe + proj_names[p]);
+                }
+                if (rc != DM_OK) return rc;
+            }
+        }
+    }
     return DM_OK;
 }
 

@@ -195,6 +195,76 @@ class Engine:
                                           None if ob is None else _ptr(ob), None if of is None else _ptr(of)))
         return ob, of
 
+    def tensor_download(self, layer: int, tensor_id: int, n: int) -> np.ndarray:
+        """A dense weight as uploaded: bf16 bits (uint16) or fp32 for dt_bias / A_log."""
+        f32 = tensor_id in (_lib.DM_T_GDN_DT_BIAS, _lib.DM_T_GDN_A_LOG)
+        out = np.empty(n, np.float32 if f32 else np.uint16)
+        self._ok(self.lib.dm_tensor_download(self.ctx, layer, tensor_id,
+                                             _lib.DM_DTYPE_F32 if f32 else _lib.DM_DTYPE_BF16, _ptr(out), n))
+        return out
+
+    def expert_download(self, layer: int, expert: int, proj: int):
+        """(q [rows, cols/2], scales [rows, cols/g], zeros [rows, cols/g/2]) of one projection."""
+        cfg = self.cfg
+        H, I, G = cfg.hidden_size, cfg.moe_intermediate_size, cfg.quant_group_size
+        rows, cols = (H, I) if proj == _lib.DM_PROJ_DOWN else (I, H)
+        q = np.empty((rows, cols // 2), np.uint8)
+        s = np.empty((rows, cols // G), np.uint16)
+        z = np.empty((rows, cols // G // 2), np.uint8)
+        self._ok(self.lib.dm_expert_download(self.ctx, layer, expert, proj, _ptr(q), _ptr(s), _ptr(z)))
+        return q, s, z
+
+    # ---- quant-file loaders (formats.py parses; these dequantise / load on the device) ----
+    def gguf_dequant(self, raw: bytes, ggml_type: int, n: int, q4k_mojo: bool = False,
+                     want_f32: bool = True, want_bf16: bool = False):
+        """GGML blocks -> (fp32 [n] or None, bf16 bits [n] or None) on the GPU
+        (dequantize_q8_0 / _q4_k / _q3_k, gguf.mojo:414-561)."""
+        buf = np.frombuffer(bytes(raw), np.uint8)
+        of = np.empty(n, np.float32) if want_f32 else None
+        ob = np.empty(n, np.uint16) if want_bf16 else None
+        flags = _lib.DM_GGUF_Q4K_MOJO if q4k_mojo else 0
+        self._ok(self.lib.dm_gguf_dequant(self.ctx, ggml_type, _ptr(buf), buf.size, n, flags,
+                                          None if of is None else _ptr(of), None if ob is None else _ptr(ob)))
+        return of, ob
+
+    def load_gguf_tensor(self, index, name: str, layer: int, tensor_id: int, q4k_mojo: bool = False):
+        """One GGUF tensor -> dense weight (layer, tensor_id) (stream_gguf_tensor_f32, gguf.mojo:563)."""
+        flags = _lib.DM_GGUF_Q4K_MOJO if q4k_mojo else 0
+        self._ok(self.lib.dm_gguf_load_tensor(self.ctx, index.handle, name.encode(), layer, tensor_id, flags))
+
+    def load_gguf_expert(self, index, name: str, layer: int, expert: int, proj: int, slab: int = 0,
+                         row0: int = 0, requant: bool = False, q4k_mojo: bool = False) -> float:
+        """One expert projection from a GGUF tensor, re-quantised into the pool; returns the
+        largest |w - w'|."""
+        flags = (_lib.DM_LOAD_REQUANT if requant else 0) | (_lib.DM_GGUF_Q4K_MOJO if q4k_mojo else 0)
+        err = C.c_float()
+        self._ok(self.lib.dm_gguf_load_expert(self.ctx, index.handle, name.encode(), slab, row0, layer, expert, proj,
+                                              flags, C.byref(err)))
+        return err.value
+
+    def load_quant_tensor(self, index, name: str, layer: int, tensor_id: int):
+        """load_one_quant_tensor_bf16 / _f32 (quant_loader.mojo:27-58) into a dense weight."""
+        self._ok(self.lib.dm_quant_file_load_tensor(self.ctx, index.handle, name.encode(), layer, tensor_id))
+
+    def load_quant_expert(self, index, name: str, layer: int, expert: int, proj: int, slab: int = 0,
+                          row0: int = 0, requant: bool = False) -> float:
+        """One expert projection from a quant-file tensor (exact when the groups allow)."""
+        err = C.c_float()
+        self._ok(self.lib.dm_quant_file_load_expert(self.ctx, index.handle, name.encode(), slab, row0, layer, expert,
+                                                    proj, _lib.DM_LOAD_REQUANT if requant else 0, C.byref(err)))
+        return err.value
+
+    def load_quant_file(self, path_or_index, requant: bool = False):
+        """Every weight of the configured model from the reference's custom 4-bit quant file
+        (checkpoint names; per-expert or stacked experts)."""
+        from .formats import scan_quant_file
+        idx = scan_quant_file(path_or_index) if isinstance(path_or_index, str) else path_or_index
+        try:
+            self._ok(self.lib.dm_quant_file_load(self.ctx, idx.handle, _lib.DM_LOAD_REQUANT if requant else 0))
+        finally:
+            if isinstance(path_or_index, str):
+                idx.close()
+
     # ---- sequence state (KV-cache object, GDN state) ----
     def seq_reset(self, slot: int = 0):
         self._ok(self.lib.dm_seq_reset(self.ctx, slot))

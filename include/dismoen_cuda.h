@@ -44,8 +44,8 @@ extern "C" {
 #define DM_ERR_TIMEOUT 7       /* a bounded device-side wait ran out                   */
 #define DM_ERR_NOT_READY 8     /* weights missing for the requested computation        */
 #define DM_ERR_ROUTER 9        /* router contract violated (e.g. norm_topk_prob)       */
-#define DM_ERR_IO 10           /* a session file could not be read or written          */
-#define DM_ERR_FORMAT 11       /* a session file failed its format / checksum checks   */
+#define DM_ERR_IO 10           /* a session or weight file could not be read / written */
+#define DM_ERR_FORMAT 11       /* a session or weight file failed its format checks    */
 
 /* ---- configuration ----------------------------------------------------------------- */
 /* Field names and meaning follow the reference ModelConfig
@@ -163,6 +163,13 @@ int32_t dm_upload_tensor(dm_ctx* ctx, int32_t layer, int32_t tensor_id, int32_t 
 int32_t dm_expert_upload(dm_ctx* ctx, int32_t layer, int32_t expert, int32_t proj,
                          const uint8_t* q_host, const uint16_t* scales_host,
                          const uint8_t* zeros_host);
+
+/* Read-back of what the loaders wrote: a dense weight (dtype and n as for the upload) and
+ * one expert projection in the upload format above. */
+int32_t dm_tensor_download(dm_ctx* ctx, int32_t layer, int32_t tensor_id, int32_t dtype, void* out_host,
+                           uint64_t n_elems);
+int32_t dm_expert_download(dm_ctx* ctx, int32_t layer, int32_t expert, int32_t proj, uint8_t* q_host,
+                           uint16_t* scales_host, uint8_t* zeros_host);
 
 /* Coverage check over every tensor the configured model needs (the role of
  * validate_gguf_port_coverage, reference gguf_port_loader.mojo:70).  DM_ERR_NOT_READY
@@ -472,6 +479,131 @@ int32_t dm_sha256(const uint8_t* data, uint64_t n, uint8_t* out32);
 /* Fills every weight of the context with the synthetic distributions of the benchmark
  * configs directly on the device (same generator; used for multi-GB models). */
 int32_t dm_synth_model_device(dm_ctx* ctx, uint64_t seed);
+
+/* ---- quant-file loaders: the reference's on-disk weight formats ----------------------
+ * GGUF v2/v3 (reference src/format/gguf.mojo) and the reference's custom 4-bit quant file
+ * (src/format/quant_reader.mojo), parsed on the host and streamed into the HBM pool:
+ * dense tensors are dequantised on the GPU straight into the context's weights, experts
+ * are converted into the pool's asymmetric 4-bit form (exactly for the custom format with
+ * group >= the pool group; otherwise by round-to-nearest re-quantisation, which the
+ * caller has to ask for).  The index functions need no device and no context; `err`
+ * receives the reference-shaped error JSON. */
+#define DM_GGML_F32 0
+#define DM_GGML_F16 1
+#define DM_GGML_Q8_0 8
+#define DM_GGML_Q3_K 11
+#define DM_GGML_Q4_K 12
+#define DM_GGML_BF16 30
+/* Q4_K sub-blocks 4..7: read scale and min as gguf.mojo:478-485 does (byte j-4 and byte j
+ * of the 12 scale bytes) instead of the GGUF layout oracle_port.py:108-112 follows
+ * (bytes j-4, j and j+4).  The two agree when those bytes are equal. */
+#define DM_GGUF_Q4K_MOJO 1u
+/* Expert loads may re-quantise (lossy) what the pool cannot hold exactly. */
+#define DM_LOAD_REQUANT 2u
+
+typedef struct dm_gguf dm_gguf;
+typedef struct {
+    const char* name;      /* valid until dm_gguf_close */
+    int32_t ndim;
+    int32_t ggml_type;
+    uint64_t dims[8];      /* GGUF order: dims[0] is the innermost (contiguous) axis */
+    uint64_t offset;       /* relative to the data section */
+    uint64_t file_offset;  /* absolute */
+    uint64_t num_elements;
+    uint64_t raw_bytes;
+} dm_gguf_tensor_info;
+
+/* parse_gguf_index (gguf.mojo:257-411): magic, version 2 or 3, tensor count <= 100000,
+ * metadata (general.alignment), tensor directory (ndim 1..8), data section aligned, every
+ * tensor inside the file, and the exact file size data_start + max tensor end.
+ * DM_ERR_IO when the file cannot be read, DM_ERR_FORMAT with error_type
+ * GGUF_FILE_CORRUPT and the reference's message otherwise. */
+int32_t dm_gguf_open(const char* path, dm_gguf** out, char* err, uint64_t err_size);
+void dm_gguf_close(dm_gguf* g);
+int32_t dm_gguf_summary(const dm_gguf* g, uint32_t* version, uint64_t* tensor_count, uint64_t* kv_count,
+                        uint64_t* alignment, uint64_t* data_offset, uint64_t* file_size);
+int32_t dm_gguf_tensor(const dm_gguf* g, int64_t index, dm_gguf_tensor_info* out);
+int64_t dm_gguf_find(const dm_gguf* g, const char* name); /* -1 when absent */
+/* Metadata as the reference's index.metadata strings: integers (and f32/f64 as their raw
+ * bit patterns) in decimal, strings verbatim, arrays "[Array of N elements]". */
+int32_t dm_gguf_meta_key(const dm_gguf* g, int64_t index, char* buf, uint64_t size);
+int32_t dm_gguf_meta(const dm_gguf* g, const char* key, char* buf, uint64_t size);
+/* Raw bytes [byte_offset, byte_offset + n) of tensor `index` (pread). */
+int32_t dm_gguf_read(const dm_gguf* g, int64_t index, uint64_t byte_offset, void* dst, uint64_t n);
+/* (elements, bytes) per block of a GGML type (get_ggml_block_specs, gguf.mojo:76-102). */
+int32_t dm_ggml_block_spec(int32_t type, int32_t* block_elems, int32_t* block_bytes);
+
+/* Dequantises n elements of GGML blocks on the GPU (dequantize_q8_0 / _q4_k / _q3_k,
+ * gguf.mojo:414-561, oracle_port.py:68-159; F32, F16, BF16 converted): fp32 with the
+ * reference's roundings into out_f32_host and/or its bf16 rounding (nearest even) into
+ * out_bf16_host.  raw_bytes must hold the n / block elements blocks; n a multiple of the
+ * block.  flags: DM_GGUF_Q4K_MOJO. */
+int32_t dm_gguf_dequant(dm_ctx* ctx, int32_t ggml_type, const void* raw_host, uint64_t raw_bytes,
+                        uint64_t n_elements, uint32_t flags, float* out_f32_host, uint16_t* out_bf16_host);
+/* GGUF tensor `name` -> dense weight (layer, tensor_id) of the context (the role of
+ * stream_gguf_tensor_f32, gguf.mojo:563-626, for one weight): element counts must match;
+ * bf16 weights take the fp32 value rounded to nearest even, fp32 weights take it as is. */
+int32_t dm_gguf_load_tensor(dm_ctx* ctx, const dm_gguf* g, const char* name, int32_t layer, int32_t tensor_id,
+                            uint32_t flags);
+/* One expert projection from a GGUF tensor: rows x cols = the projection's shape, taken
+ * from element slab * slab_elems + row0 * cols, slab_elems = the product of the inner two
+ * dims (slab = 0 and row0 = 0 for a 2-D tensor; for stacked experts [E][rows][cols]
+ * slab = expert).  The pool cannot hold GGML blocks exactly, so this needs
+ * DM_LOAD_REQUANT; *max_abs_err (may be NULL) receives the largest |w - w'|. */
+int32_t dm_gguf_load_expert(dm_ctx* ctx, const dm_gguf* g, const char* name, int64_t slab, int64_t row0,
+                            int32_t layer, int32_t expert, int32_t proj, uint32_t flags, float* max_abs_err);
+
+typedef struct dm_quant_file dm_quant_file;
+typedef struct {
+    const char* name;  /* valid until dm_quant_file_close */
+    const char* dtype; /* the source dtype the record names ("BF16") */
+    int32_t ndim;
+    int32_t group_size;
+    uint64_t shape[8]; /* numpy order: shape[ndim-1] is contiguous */
+    uint64_t num_groups;
+    uint64_t num_elements;
+    uint64_t record_offset;
+    uint64_t scales_offset; /* absolute: fp16 scales, num_groups of them */
+    uint64_t data_offset;   /* absolute: packed nibbles, low nibble first */
+    uint64_t scales_bytes;
+    uint64_t weights_bytes;
+} dm_quant_tensor_info;
+
+/* scan_quant_file (quant_reader.mojo:520-662): 256-byte JSON header (version 1, format
+ * "4-bit per-group", scale dtype FP16, group in {32, 64, 128, 256}, num_tensors,
+ * total_bytes == file size), then records [u32 meta_len][meta JSON][scales][nibbles]
+ * back to back to the end of the file.  DM_ERR_FORMAT (error_type QUANT_FILE_CORRUPT)
+ * with the reference's message on any violation. */
+int32_t dm_quant_file_open(const char* path, dm_quant_file** out, char* err, uint64_t err_size);
+void dm_quant_file_close(dm_quant_file* q);
+int32_t dm_quant_file_summary(const dm_quant_file* q, int32_t* version, int32_t* group_size, int64_t* num_tensors,
+                              uint64_t* total_bytes, char* model, uint64_t model_size);
+int32_t dm_quant_file_tensor(const dm_quant_file* q, int64_t index, dm_quant_tensor_info* out);
+int64_t dm_quant_file_find(const dm_quant_file* q, const char* name);
+/* part 0: scale bytes, 1: nibble bytes; [byte_offset, byte_offset + n) of that part. */
+int32_t dm_quant_file_read(const dm_quant_file* q, int64_t index, int32_t part, uint64_t byte_offset, void* dst,
+                           uint64_t n);
+/* Quant-file tensor -> dense weight (load_one_quant_tensor_bf16 / _f32,
+ * src/layers/quant_loader.mojo:27-58): bf16 weights take dequant_kernel_simd's bits
+ * bf16(fp32(s) q), fp32 weights fp32(s) q; the reference's rejections apply. */
+int32_t dm_quant_file_load_tensor(dm_ctx* ctx, const dm_quant_file* q, const char* name, int32_t layer,
+                                  int32_t tensor_id);
+/* Quant-file tensor slice -> one expert projection (slab / row0 as in
+ * dm_gguf_load_expert).  Exact (nibble n -> n XOR 8, zero 8, the group's scale) when the
+ * file's group is a multiple of the pool group, or when the file's groups inside each
+ * pool group share one scale; otherwise DM_LOAD_REQUANT re-quantises. */
+int32_t dm_quant_file_load_expert(dm_ctx* ctx, const dm_quant_file* q, const char* name, int64_t slab, int64_t row0,
+                                  int32_t layer, int32_t expert, int32_t proj, uint32_t flags, float* max_abs_err);
+/* Every weight of the configured model from a quant file, by checkpoint names: prefix
+ * "model.language_model.layers.<l>." or "model.layers.<l>." + the names of enum
+ * dm_tensor_id; experts as "mlp.experts.<e>.{gate,up,down}_proj.weight" or the stacked
+ * "mlp.experts.gate_up_proj" [E][2I][H] (gate rows first) and "mlp.experts.down_proj"
+ * [E][H][I]; the shared expert "mlp.shared_expert.{gate,up,down}_proj.weight"; globals
+ * "[model.language_model.|model.]embed_tokens.weight", "[...]norm.weight",
+ * "lm_head.weight".  A weight the file lacks but that was uploaded before is kept (the
+ * format's groups of >= 32 cannot hold e.g. a 4-element dt_bias); DM_ERR_NOT_READY names
+ * the first weight that is still missing. */
+int32_t dm_quant_file_load(dm_ctx* ctx, const dm_quant_file* q, uint32_t flags);
 
 #ifdef __cplusplus
 }

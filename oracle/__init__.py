@@ -63,6 +63,16 @@ def load() -> C.CDLL:
         lib.or_dequant_q4.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, P]
         lib.or_dequant_sym4.restype = C.c_int
         lib.or_dequant_sym4.argtypes = [P, P, C.c_longlong, C.c_int, P, P]
+        lib.or_gguf_dequant.restype = C.c_int
+        lib.or_gguf_dequant.argtypes = [C.c_int, P, C.c_longlong, C.c_uint, P]
+        lib.or_sym4_to_pool.restype = C.c_uint
+        lib.or_sym4_to_pool.argtypes = [P, P, C.c_longlong, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P]
+        lib.or_requant_pool.restype = C.c_uint
+        lib.or_requant_pool.argtypes = [P, C.c_int, C.c_int, C.c_int, P, P, P, C.POINTER(C.c_float)]
+        lib.or_f32_to_f16.restype = C.c_uint16
+        lib.or_f32_to_f16.argtypes = [C.c_float]
+        lib.or_f16_to_f32.restype = C.c_float
+        lib.or_f16_to_f32.argtypes = [C.c_uint16]
         lib.or_head.restype = C.c_int
         lib.or_head.argtypes = [C.POINTER(OrModel), P, P]
         lib.or_det_exp.restype = C.c_float
@@ -190,6 +200,43 @@ def dequant_sym4(packed, scales_f16_bits, n, group=128):
     rc = load().or_dequant_sym4(_p(np.ascontiguousarray(packed, np.uint8)),
                                 _p(np.ascontiguousarray(scales_f16_bits, np.uint16)), n, group, _p(ob), _p(of))
     return ob, of, rc
+
+
+def gguf_dequant(raw: bytes, ggml_type: int, n: int, q4k_mojo: bool = False) -> np.ndarray:
+    """fp32 [n] of GGML blocks (or_formats.c); raises on an unsupported type or a ragged n."""
+    buf = np.frombuffer(bytes(raw), np.uint8)
+    out = np.empty(n, np.float32)
+    rc = load().or_gguf_dequant(ggml_type, _p(buf), n, 1 if q4k_mojo else 0, _p(out))
+    if rc != 0:
+        raise ValueError(f"or_gguf_dequant: status {rc}")
+    return out
+
+
+def sym4_to_pool(packed, scales, e0: int, rows: int, cols: int, gf: int, gp: int = 64):
+    """(q [rows, cols/2], s [rows, cols/gp], z [rows, cols/gp/2], flags) of the exact
+    custom-4-bit -> pool conversion."""
+    q = np.empty((rows, cols // 2), np.uint8)
+    s = np.empty((rows, cols // gp), np.uint16)
+    z = np.empty((rows, cols // gp // 2), np.uint8)
+    f = load().or_sym4_to_pool(_p(np.ascontiguousarray(packed, np.uint8)), _p(np.ascontiguousarray(scales, np.uint16)),
+                               e0, rows, cols, gf, gp, _p(q), _p(s), _p(z))
+    return q, s, z, f
+
+
+def requant_pool(w, gp: int = 64):
+    """(q, s, z, flags, max_err) of the round-to-nearest re-quantisation of w [rows, cols]."""
+    w = np.ascontiguousarray(w, np.float32)
+    rows, cols = w.shape
+    q = np.zeros((rows, cols // 2), np.uint8)
+    s = np.empty((rows, cols // gp), np.uint16)
+    z = np.zeros((rows, cols // gp // 2), np.uint8)
+    err = C.c_float()
+    f = load().or_requant_pool(_p(w), rows, cols, gp, _p(q), _p(s), _p(z), C.byref(err))
+    return q, s, z, f, err.value
+
+
+def f32_to_f16_bits(x: float) -> int:
+    return load().or_f32_to_f16(x)
 
 
 def det_exp(x: float) -> float:

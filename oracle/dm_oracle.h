@@ -93,6 +93,18 @@ void or_dequant_q4(const uint8_t* q, const uint16_t* s, const uint8_t* z, int ro
 int or_dequant_sym4(const uint8_t* packed, const uint16_t* scales, long long n, int group, uint16_t* out_bf16,
                     float* out_f32);
 
+/* On-disk weight formats (or_formats.c): GGUF block dequantisation (type = GGML type id;
+ * flags bit 0 = the Q4_K reading of gguf.mojo; returns -1 for an unsupported type, -2 when
+ * n is not a multiple of the block), the exact custom-4-bit -> pool conversion and the
+ * round-to-nearest re-quantisation into the pool; fp16 conversions. */
+float or_f16_to_f32(uint16_t h);
+uint16_t or_f32_to_f16(float f);
+int or_gguf_dequant(int type, const uint8_t* raw, long long n, unsigned flags, float* out);
+unsigned or_sym4_to_pool(const uint8_t* packed, const uint16_t* scales, long long e0, int rows, int cols, int gf,
+                         int gp, uint8_t* q, uint16_t* s, uint8_t* z);
+unsigned or_requant_pool(const float* w, int rows, int cols, int gp, uint8_t* q, uint16_t* s, uint8_t* z,
+                         float* max_err);
+
 /* MoE sublayer with residual: x_out = x_mid + moe(norm(x_mid)); ids optional [topk]. */
 void or_moe_block(const or_dims* d, const or_layer* w, const float* x_mid, float* x_out, int* ids_out,
                   float* probs_out);
