@@ -59,9 +59,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-steps", type=int, default=2)
     ap.add_argument("--timeline", default="", help="also trace one decode step; write its launch timeline here")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c3"],
+    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "spill"],
                     help="c2: bs1 decode (BASELINE config 2); c3: batched decode of 64 sequences at 32768 "
-                         "cached tokens each (config 3)")
+                         "cached tokens each (config 3); spill: bs1 decode with the expert pool spilled to host "
+                         "memory (--expert-slots per layer in HBM)")
+    ap.add_argument("--expert-slots", type=int, default=64, help="spill: routed expert records per layer in HBM")
     ap.add_argument("--batch", type=int, default=64, help="c3: sequences per step")
     ap.add_argument("--c3-ctx", type=int, default=32768, help="c3: cached tokens per sequence")
     ap.add_argument("--router-skew", type=float, default=1.1,
@@ -470,6 +472,9 @@ def main():
     if args.workload == "c3":
         from disk_streaming_moe_engine_b200 import bench_batch
         return bench_batch.run(args, rank, local, world)
+    if args.workload == "spill":
+        from disk_streaming_moe_engine_b200 import bench_spill
+        return bench_spill.run(args)
     return run_ours(args, rank, local, world)
 
 

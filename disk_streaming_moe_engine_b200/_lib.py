@@ -60,7 +60,8 @@ class DmModelConfig(C.Structure):
 
 class DmRuntimeConfig(C.Structure):
     _fields_ = [("max_seqs", C.c_int32), ("kv_page_tokens", C.c_int32),
-                ("kv_num_pages", C.c_int32), ("max_pages_per_seq", C.c_int32)]
+                ("kv_num_pages", C.c_int32), ("max_pages_per_seq", C.c_int32),
+                ("expert_cache_slots", C.c_int32)]
 
 
 class DmGgufTensorInfo(C.Structure):
@@ -142,6 +143,9 @@ SIGNATURES = {
     "dm_kmss_save": (I32, [P, I32, C.c_char_p, P, I32, I32, P]),
     "dm_kmss_load": (I32, [P, I32, C.c_char_p, P, I32, C.POINTER(I32)]),
     "dm_sha256": (I32, [P, U64, P]),
+    "dm_spill_stats": (I32, [P, C.POINTER(C.c_uint64)]),
+    "dm_spill_pin": (I32, [P, I32, I32, C.POINTER(I32)]),
+    "dm_spill_simulate": (I32, [I32, I32, I32, I32, I32, I32, P, P, I32, C.POINTER(C.c_uint64), P]),
     "dm_gguf_open": (I32, [C.c_char_p, C.POINTER(P), C.c_char_p, U64]),
     "dm_gguf_close": (None, [P]),
     "dm_gguf_summary": (I32, [P, C.POINTER(C.c_uint32), C.POINTER(U64), C.POINTER(U64), C.POINTER(U64),

@@ -131,6 +131,7 @@ class RuntimeConfig:
     kv_page_tokens: int = 16
     kv_num_pages: int = 0          # 0: max_seqs * max_pages_per_seq
     max_pages_per_seq: int = 64
+    expert_cache_slots: int = 0    # 0: all experts in HBM; C: C per layer in HBM, the rest in host memory
 
     @classmethod
     def for_context(cls, max_ctx: int, max_seqs: int = 1, extra_pages: int = 0) -> "RuntimeConfig":
@@ -139,7 +140,8 @@ class RuntimeConfig:
 
     def to_c(self) -> _lib.DmRuntimeConfig:
         n = self.kv_num_pages or self.max_seqs * self.max_pages_per_seq
-        return _lib.DmRuntimeConfig(self.max_seqs, self.kv_page_tokens, n, self.max_pages_per_seq)
+        return _lib.DmRuntimeConfig(self.max_seqs, self.kv_page_tokens, n, self.max_pages_per_seq,
+                                    self.expert_cache_slots)
 
 
 def preset(name: str) -> ModelConfig:

@@ -84,6 +84,15 @@ struct dm_ctx {
     // an fp32 projection buffer and two status words
     void* ld_host = nullptr;
     uint8_t* ld_dev = nullptr;
+    // spilling expert pool (expert_cache_slots > 0): every routed record in pinned host
+    // memory, the residency policy, the device slot table and its pinned host mirror
+    uint8_t* host_pool = nullptr;   // [L][E] records
+    uint8_t* scratch_rec = nullptr; // device staging record of uploads
+    int* d_slot_of = nullptr;       // [L][E] device
+    int* h_slot_of = nullptr;       // [L][E] pinned host
+    int* h_sids = nullptr;          // [kMaxBatch * topk] pinned host: the routed ids of a layer
+    SpillPolicy spill;
+    uint64_t spill_bytes = 0;
     float* ld_f32 = nullptr;
     unsigned* ld_word = nullptr;
     // pinned host staging for per-step transfers
@@ -211,6 +220,7 @@ static Dims make_dims(const dm_model_config& m, const dm_runtime_config& r) {
     d.gdn_in_rows = d.qkv_dim + d.z_dim + 2 * d.nv;
     d.attn_in_rows = 2 * d.Hq * d.D + 2 * d.Hkv * d.D;
     d.E = m.num_experts;
+    d.E_res = (r.expert_cache_slots > 0 && r.expert_cache_slots < m.num_experts) ? r.expert_cache_slots : m.num_experts;
     d.topk = m.num_experts_per_tok;
     d.I = m.moe_intermediate_size;
     d.G = m.quant_group_size;
@@ -276,12 +286,16 @@ static int plan_memory(dm_ctx* c, bool commit) {
             o.w_out = T(H * d.z_dim * 2);
         }
         o.router = T(static_cast<size_t>(d.E + 1) * H * 2);
-        o.experts = T(static_cast<size_t>(d.E) * d.expert_bytes);
+        o.experts = T(static_cast<size_t>(d.E_res) * d.expert_bytes);
         o.shared = T(static_cast<size_t>(d.expert_bytes));
     }
     const size_t o_embed = T(static_cast<size_t>(d.V) * H * 2);
     const size_t o_fnorm = T(H * 2);
     const size_t o_head = T(static_cast<size_t>(d.V) * H * 2);
+    // a spilling pool: one staging record for uploads and the [L][E] slot table
+    const bool spill = d.E_res < d.E;
+    const size_t o_scr = spill ? T(static_cast<size_t>(d.expert_bytes)) : 0;
+    const size_t o_slot = spill ? T(static_cast<size_t>(d.L) * d.E * 4) : 0;
     const size_t S = d.max_seqs;
     const size_t o_xres = T(S * H * 4), o_xmid = T(S * H * 4);
     const size_t o_ring = T(static_cast<size_t>(d.n_gdn) * S * kConvRing * d.qkv_dim * 4);
@@ -358,6 +372,8 @@ static int plan_memory(dm_ctx* c, bool commit) {
         w.shared = A + o.shared;
     }
     c->embed = reinterpret_cast<uint16_t*>(A + o_embed);
+    c->scratch_rec = spill ? A + o_scr : nullptr;
+    c->d_slot_of = spill ? reinterpret_cast<int*>(A + o_slot) : nullptr;
     c->final_norm = reinterpret_cast<uint16_t*>(A + o_fnorm);
     c->lm_head = reinterpret_cast<uint16_t*>(A + o_head);
     Buffers& b = c->b;
@@ -536,7 +552,7 @@ static bool encode_expert_maps(dm_ctx* c) {
     for (int l = 0; l < d.L; ++l) {
         LayerW& w = c->layers[l];
         w.tm_gu = w.tm_dn = nullptr;
-        if (w.shared != w.experts + static_cast<int64_t>(d.E) * d.expert_bytes) continue;
+        if (w.shared != w.experts + static_cast<int64_t>(d.E_res) * d.expert_bytes) continue;
         for (int proj = 0; proj < 2; ++proj) {
             if (proj == 0 ? !gu_ok : !dn_ok) continue;
             const int K = proj == 0 ? d.H : d.I;
@@ -544,7 +560,7 @@ static bool encode_expert_maps(dm_ctx* c) {
             const int nch = proj == 0 ? d.gu_chunks : d.d_chunks;
             uint8_t* base = const_cast<uint8_t*>(w.experts) + (proj == 0 ? 0 : static_cast<int64_t>(d.gu_chunks) * d.gu_chunk_bytes);
             const cuuint64_t dims[4] = {static_cast<cuuint64_t>(K / 2), 16, static_cast<cuuint64_t>(nch),
-                                        static_cast<cuuint64_t>(d.E + 1)};
+                                        static_cast<cuuint64_t>(d.E_res + 1)};
             const cuuint64_t strides[3] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(chunk),
                                            static_cast<cuuint64_t>(d.expert_bytes)};
             const cuuint32_t box[4] = {128, 16, 1, 1};
@@ -617,6 +633,11 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     }
     if (rt->max_seqs <= 0 || rt->kv_page_tokens != kPageTokens || rt->kv_num_pages <= 0 || rt->max_pages_per_seq <= 0)
         return DM_ERR_INVALID_ARG;
+    if (rt->expert_cache_slots < 0 ||
+        (rt->expert_cache_slots > 0 && rt->expert_cache_slots < model->num_experts_per_tok)) {
+        fprintf(stderr, "dm_ctx_create: expert_cache_slots must be 0 or at least num_experts_per_tok\n");
+        return DM_ERR_INVALID_ARG;
+    }
     dm_ctx* c = new dm_ctx();
     // tuning knobs (environment, read once): DISMOEN_PDL=0 launches every kernel without
     // programmatic dependent launch; DISMOEN_L2_PREFETCH=1 enables the L2 prefetch of
@@ -661,6 +682,18 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
         e = launch_rope_table(c->stream, c->b.rope, c->d.max_pages * kPageTokens, c->d.rot_dim, c->d.theta);
     if (e == cudaSuccess) e = cudaMallocHost(&c->h_io, 64);
     if (e == cudaSuccess) e = cudaMallocHost(&c->h_bio, 4 * kMaxBatch * sizeof(int));
+    if (e == cudaSuccess && c->d.E_res < c->d.E) {  // the spilling pool's host side
+        const Dims& d = c->d;
+        e = cudaHostAlloc(reinterpret_cast<void**>(&c->host_pool), static_cast<size_t>(d.L) * d.E * d.expert_bytes,
+                          cudaHostAllocDefault);
+        if (e == cudaSuccess) e = cudaMallocHost(&c->h_slot_of, static_cast<size_t>(d.L) * d.E * 4);
+        if (e == cudaSuccess) e = cudaMallocHost(&c->h_sids, static_cast<size_t>(kMaxBatch) * d.topk * 4);
+        if (e == cudaSuccess) e = cudaMemsetAsync(c->d_slot_of, 0xFF, static_cast<size_t>(d.L) * d.E * 4, c->stream);
+        if (e == cudaSuccess) {
+            memset(c->host_pool, 0, static_cast<size_t>(d.L) * d.E * d.expert_bytes);
+            c->spill.init(d.L, d.E, d.E_res);
+        }
+    }
     if (e == cudaSuccess && !encode_kv_map(c)) e = cudaErrorInvalidValue;
     if (e == cudaSuccess && !encode_expert_maps(c)) e = cudaErrorInvalidValue;
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
@@ -668,6 +701,9 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
         fprintf(stderr, "dm_ctx_create: %s\n", cudaGetErrorString(e));
         if (c->h_io) cudaFreeHost(c->h_io);
         if (c->h_bio) cudaFreeHost(c->h_bio);
+        if (c->host_pool) cudaFreeHost(c->host_pool);
+        if (c->h_slot_of) cudaFreeHost(c->h_slot_of);
+        if (c->h_sids) cudaFreeHost(c->h_sids);
         cudaFree(c->arena);
         delete c;
         return DM_ERR_CUDA;
@@ -681,6 +717,9 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
             if (c->blas) cublasDestroy(c->blas);
             cudaFreeHost(c->h_io);
             cudaFreeHost(c->h_bio);
+            if (c->host_pool) cudaFreeHost(c->host_pool);
+            if (c->h_slot_of) cudaFreeHost(c->h_slot_of);
+            if (c->h_sids) cudaFreeHost(c->h_sids);
             cudaFree(c->arena);
             delete c;
             return DM_ERR_CUDA;
@@ -722,6 +761,9 @@ int32_t dm_ctx_destroy(dm_ctx* c) {
     if (c->h_io) cudaFreeHost(c->h_io);
     if (c->ld_host) cudaFreeHost(c->ld_host);
     if (c->ld_dev) cudaFree(c->ld_dev);
+    if (c->host_pool) cudaFreeHost(c->host_pool);
+    if (c->h_slot_of) cudaFreeHost(c->h_slot_of);
+    if (c->h_sids) cudaFreeHost(c->h_sids);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
     return DM_OK;
@@ -822,9 +864,34 @@ int32_t dm_upload_tensor(dm_ctx* c, int32_t layer, int32_t id, int32_t dtype, co
 }
 
 static uint8_t* expert_record(dm_ctx* c, int layer, int expert) {
+    if (expert >= 0 && c->scratch_rec) return c->scratch_rec;  // a spilling pool stages routed records
     LayerW& w = c->layers[layer];
     return expert < 0 ? const_cast<uint8_t*>(w.shared)
                       : const_cast<uint8_t*>(w.experts) + static_cast<size_t>(expert) * c->d.expert_bytes;
+}
+
+// A spilling pool keeps its routed records in pinned host memory: the projection just
+// repacked into the staging record is copied there.  Gate and up share chunks (rows 0-7
+// and 8-15 of each chunk's nibble, scale and zero arrays), so each copies only its own
+// 8-row blocks; the down projection is one contiguous region.
+static cudaError_t spill_store(dm_ctx* c, int layer, int expert, int proj) {
+    if (!c->scratch_rec || expert < 0) return cudaSuccess;
+    const Dims& d = c->d;
+    uint8_t* host = c->host_pool + (static_cast<size_t>(layer) * d.E + expert) * d.expert_bytes;
+    const uint8_t* dev = c->scratch_rec;
+    if (proj == DM_PROJ_DOWN) {
+        const size_t off = static_cast<size_t>(d.gu_chunks) * d.gu_chunk_bytes;
+        return cudaMemcpyAsync(host + off, dev + off, static_cast<size_t>(d.d_chunks) * d.d_chunk_bytes,
+                               cudaMemcpyDeviceToHost, c->stream);
+    }
+    const size_t ng = d.H / d.G, qb = d.H / 2, sb = ng * 2, zb = ng / 2;
+    const size_t r0 = proj == DM_PROJ_UP ? 8 : 0;
+    const size_t part[3][2] = {{r0 * qb, 8 * qb}, {16 * qb + r0 * sb, 8 * sb}, {16 * qb + 16 * sb + r0 * zb, 8 * zb}};
+    cudaError_t e = cudaSuccess;
+    for (int i = 0; i < 3 && e == cudaSuccess; ++i)
+        e = cudaMemcpy2DAsync(host + part[i][0], d.gu_chunk_bytes, dev + part[i][0], d.gu_chunk_bytes, part[i][1],
+                              d.gu_chunks, cudaMemcpyDeviceToHost, c->stream);
+    return e;
 }
 
 int32_t dm_expert_upload(dm_ctx* c, int32_t layer, int32_t expert, int32_t proj, const uint8_t* q,
@@ -844,6 +911,7 @@ int32_t dm_expert_upload(dm_ctx* c, int32_t layer, int32_t expert, int32_t proj,
     uint8_t* rec = expert_record(c, layer, expert);
     uint8_t* dst = proj == DM_PROJ_DOWN ? rec + static_cast<size_t>(d.gu_chunks) * d.gu_chunk_bytes : rec;
     DM_CUDA(c, launch_repack_rows(c->stream, c->stage_q, c->stage_s, c->stage_z, rows, cols, d.G, proj, dst), "loader");
+    DM_CUDA(c, spill_store(c, layer, expert, proj), "loader");
     DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
     c->have_expert[(static_cast<size_t>(layer) * (d.E + 1) + (expert + 1)) * 3 + proj] = 1;
     return DM_OK;
@@ -879,7 +947,12 @@ int32_t dm_expert_download(dm_ctx* c, int32_t layer, int32_t expert, int32_t pro
     std::vector<uint8_t> h(chunk_bytes * nchunks);
     cudaSetDevice(c->device);
     DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
-    DM_CUDA(c, cudaMemcpy(h.data(), src, h.size(), cudaMemcpyDeviceToHost), "loader");
+    if (c->scratch_rec && expert >= 0) {  // a spilling pool: the record lives in host memory
+        const uint8_t* rec_h = c->host_pool + (static_cast<size_t>(layer) * d.E + expert) * d.expert_bytes;
+        memcpy(h.data(), rec_h + (src - rec), h.size());
+    } else {
+        DM_CUDA(c, cudaMemcpy(h.data(), src, h.size(), cudaMemcpyDeviceToHost), "loader");
+    }
     for (int r = 0; r < rows; ++r) {
         const int chunk = proj == DM_PROJ_DOWN ? r / 16 : r / 8;
         const int rin = proj == DM_PROJ_DOWN ? r % 16 : (proj == DM_PROJ_UP ? 8 : 0) + r % 8;
@@ -1054,6 +1127,7 @@ static int pool_commit(dm_ctx* c, int rows, int cols, int layer, int expert, int
     uint8_t* rec = expert_record(c, layer, expert);
     uint8_t* dst = proj == DM_PROJ_DOWN ? rec + static_cast<size_t>(d.gu_chunks) * d.gu_chunk_bytes : rec;
     DM_CUDA(c, launch_repack_rows(c->stream, c->stage_q, c->stage_s, c->stage_z, rows, cols, d.G, proj, dst), "loader");
+    DM_CUDA(c, spill_store(c, layer, expert, proj), "loader");
     DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
     c->have_expert[(static_cast<size_t>(layer) * (d.E + 1) + (expert + 1)) * 3 + proj] = 1;
     return DM_OK;
@@ -1889,8 +1963,14 @@ int32_t dm_set_token(dm_ctx* c, int32_t slot, int32_t token) {
     return DM_OK;
 }
 
+static bool spilling(const dm_ctx* c);
+static int spill_reject(dm_ctx* c, const char* what);
+static int spill_decode(dm_ctx* c, const int32_t* slots, const int32_t* tokens, int n, int n_steps,
+                        int32_t* tokens_out, float* logits);
+
 int32_t dm_enqueue_decode(dm_ctx* c, int32_t slot, int32_t n_steps) {
     if (n_steps < 0) return DM_ERR_INVALID_ARG;
+    if (c && spilling(c)) return spill_reject(c, "dm_enqueue_decode");
     int rc = prepare_decode(c, slot, n_steps);
     if (rc != DM_OK) return rc;
     for (int i = 0; i < n_steps; ++i) DM_CUDA(c, cudaGraphLaunch(c->graphs[slot], c->stream), "decode");
@@ -1905,6 +1985,8 @@ int32_t dm_sync(dm_ctx* c) {
 }
 
 int32_t dm_decode_step(dm_ctx* c, int32_t slot, int32_t token_in, int32_t* token_out, float* logits) {
+    // a spilling pool decodes through the batched step (one row)
+    if (c && spilling(c)) return spill_decode(c, &slot, &token_in, 1, 1, token_out, logits);
     int rc = prepare_decode(c, slot, 1);
     if (rc != DM_OK) return rc;
     if ((rc = dm_set_token(c, slot, token_in)) != DM_OK) return rc;
@@ -1922,6 +2004,7 @@ int32_t dm_decode_step(dm_ctx* c, int32_t slot, int32_t token_in, int32_t* token
 
 int32_t dm_generate(dm_ctx* c, int32_t slot, int32_t token_in, int32_t n_steps, int32_t* out) {
     if (!c || !out || n_steps <= 0 || n_steps > c->b.gen_capacity) return DM_ERR_INVALID_ARG;
+    if (spilling(c)) return dm_generate_batch(c, &slot, &token_in, 1, n_steps, out);
     int rc = prepare_decode(c, slot, n_steps);
     if (rc != DM_OK) return rc;
     if ((rc = dm_set_token(c, slot, token_in)) != DM_OK) return rc;
@@ -1934,6 +2017,15 @@ int32_t dm_generate(dm_ctx* c, int32_t slot, int32_t token_in, int32_t n_steps, 
 
 int32_t dm_forward(dm_ctx* c, int32_t slot, const int32_t* tokens, int32_t n, float* logits, int32_t* next) {
     if (!c || !tokens || n <= 0) return DM_ERR_INVALID_ARG;
+    if (spilling(c)) {  // one batched step per prompt token
+        int32_t nx = 0;
+        for (int i = 0; i < n; ++i) {
+            const int rc = spill_decode(c, &slot, tokens + i, 1, 1, &nx, i == n - 1 ? logits : nullptr);
+            if (rc != DM_OK) return rc;
+        }
+        if (next) *next = nx;
+        return DM_OK;
+    }
     int rc = prepare_decode(c, slot, n);
     if (rc != DM_OK) return rc;
     for (int i = 0; i < n; ++i)
@@ -1970,41 +2062,163 @@ static cudaError_t bgemm(dm_ctx* c, const uint16_t* W, int N, int K, int n) {
     return s == CUBLAS_STATUS_SUCCESS ? cudaSuccess : cudaErrorUnknown;
 }
 
+// The token mixer of layer l for n rows, through its residual: x -> xm.
+static cudaError_t enqueue_b_mixer(dm_ctx* c, int l, int n) {
+    const Dims& d = c->d;
+    BatchBuffers& bb = c->bb;
+    const LaunchCfg lc = lcfg(c);
+    const LayerW& w = c->layers[l];
+    cudaError_t e = cudaSuccess;
+    if (w.is_attn) {
+        if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
+        if (e == cudaSuccess) e = bgemm(c, w.w_in, d.attn_in_rows, d.H, n);
+        if (e == cudaSuccess) e = launch_b_epi_attn_in(lc, d, bb, n);
+        if (e == cudaSuccess) e = launch_attn_decode_batch(lc, d, w, bb, c->b, n);
+        if (e == cudaSuccess) e = launch_attn_merge_batch(lc, d, bb, n);
+        if (e == cudaSuccess) e = bgemm(c, w.w_out, d.H, d.Hq * d.D, n);
+    } else {
+        if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
+        if (e == cudaSuccess) e = bgemm(c, w.w_in, d.gdn_in_rows, d.H, n);
+        if (e == cudaSuccess) e = launch_b_epi_gdn_in(lc, d, w, bb, c->b, n);
+        if (e == cudaSuccess) e = launch_gdn_rec_batch(lc, d, w, bb, c->b, n);
+        if (e == cudaSuccess)
+            e = launch_b_prep(lc, BPREP_HEADNORM, bb.o, d.z_dim, nullptr, d.eps, bb.z, w.gdn_norm, d.dv, bb.xcat, n);
+        if (e == cudaSuccess) e = bgemm(c, w.w_out, d.H, d.z_dim, n);
+    }
+    if (e == cudaSuccess) e = launch_b_epi_resid(lc, bb.c, d.H, bb.x, bb.xm, n);
+    return e;
+}
+
+// The MoE of layer l after its router: top-k + grouping, experts, weighted combine +
+// residual (xm -> x).  slot_of: the layer's slot table when the pool spills.
+static cudaError_t enqueue_b_moe_tail(dm_ctx* c, int l, int n, const int* slot_of) {
+    const Dims& d = c->d;
+    BatchBuffers& bb = c->bb;
+    const LaunchCfg lc = lcfg(c);
+    cudaError_t e = launch_b_topk_group(lc, d, bb, c->b, n, slot_of);
+    if (e == cudaSuccess) e = launch_b_experts(lc, d, c->layers[l], bb, c->b, n);
+    if (e == cudaSuccess && bb.ep.world > 1) e = launch_ep_barrier(lc, bb, c->b, 1);
+    if (e == cudaSuccess) e = launch_b_combine(lc, d, bb, bb.xm, bb.x, n);
+    return e;
+}
+
+static cudaError_t enqueue_b_head(dm_ctx* c, int n, int write_logits) {
+    const Dims& d = c->d;
+    BatchBuffers& bb = c->bb;
+    const LaunchCfg lc = lcfg(c);
+    cudaError_t e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, c->final_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
+    if (e == cudaSuccess) e = bgemm(c, c->lm_head, d.V, d.H, n);
+    if (e == cudaSuccess) e = launch_b_argmax(lc, d, bb, c->b, n, write_logits, 1);
+    return e;
+}
+
 static cudaError_t enqueue_batch_step(dm_ctx* c, int n, int write_logits) {
     const Dims& d = c->d;
     BatchBuffers& bb = c->bb;
     const LaunchCfg lc = lcfg(c);
     cudaError_t e = launch_b_embed(lc, d, c->embed, bb, c->b, n);
     for (int l = 0; l < d.L && e == cudaSuccess; ++l) {
-        const LayerW& w = c->layers[l];
-        if (w.is_attn) {
-            if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
-            if (e == cudaSuccess) e = bgemm(c, w.w_in, d.attn_in_rows, d.H, n);
-            if (e == cudaSuccess) e = launch_b_epi_attn_in(lc, d, bb, n);
-            if (e == cudaSuccess) e = launch_attn_decode_batch(lc, d, w, bb, c->b, n);
-            if (e == cudaSuccess) e = launch_attn_merge_batch(lc, d, bb, n);
-            if (e == cudaSuccess) e = bgemm(c, w.w_out, d.H, d.Hq * d.D, n);
-        } else {
-            if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
-            if (e == cudaSuccess) e = bgemm(c, w.w_in, d.gdn_in_rows, d.H, n);
-            if (e == cudaSuccess) e = launch_b_epi_gdn_in(lc, d, w, bb, c->b, n);
-            if (e == cudaSuccess) e = launch_gdn_rec_batch(lc, d, w, bb, c->b, n);
-            if (e == cudaSuccess)
-                e = launch_b_prep(lc, BPREP_HEADNORM, bb.o, d.z_dim, nullptr, d.eps, bb.z, w.gdn_norm, d.dv, bb.xcat, n);
-            if (e == cudaSuccess) e = bgemm(c, w.w_out, d.H, d.z_dim, n);
-        }
-        if (e == cudaSuccess) e = launch_b_epi_resid(lc, bb.c, d.H, bb.x, bb.xm, n);
+        e = enqueue_b_mixer(c, l, n);
         // MoE: canonical router, top-k + grouping, experts, weighted combine + residual
-        if (e == cudaSuccess) e = launch_b_router(lc, d, w, bb, bb.xm, 1, n);
-        if (e == cudaSuccess) e = launch_b_topk_group(lc, d, bb, c->b, n);
-        if (e == cudaSuccess) e = launch_b_experts(lc, d, w, bb, c->b, n);
-        if (e == cudaSuccess && bb.ep.world > 1) e = launch_ep_barrier(lc, bb, c->b, 1);
-        if (e == cudaSuccess) e = launch_b_combine(lc, d, bb, bb.xm, bb.x, n);
+        if (e == cudaSuccess) e = launch_b_router(lc, d, c->layers[l], bb, bb.xm, 1, n);
+        if (e == cudaSuccess) e = enqueue_b_moe_tail(c, l, n, nullptr);
     }
-    if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, c->final_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
-    if (e == cudaSuccess) e = bgemm(c, c->lm_head, d.V, d.H, n);
-    if (e == cudaSuccess) e = launch_b_argmax(lc, d, bb, c->b, n, write_logits, 1);
+    if (e == cudaSuccess) e = enqueue_b_head(c, n, write_logits);
     return e;
+}
+
+// ---- spilling expert pool -----------------------------------------------------------
+static int prepare_batch(dm_ctx* c, const int32_t* slots, const int32_t* tokens, int n, int n_steps);
+static bool spilling(const dm_ctx* c) { return c->host_pool != nullptr; }
+
+static int spill_reject(dm_ctx* c, const char* what) {
+    return set_err(c, DM_ERR_INVALID_ARG, "SPILL_UNSUPPORTED", "decode", -1,
+                   "%s needs every expert resident (expert_cache_slots = 0)", what);
+}
+
+// Host -> HBM copies of the (expert, slot) loads of layer l, then the layer's slot table.
+static cudaError_t spill_apply(dm_ctx* c, int l, const std::vector<std::pair<int, int>>& loads) {
+    if (loads.empty()) return cudaSuccess;
+    const Dims& d = c->d;
+    const size_t eb = d.expert_bytes;
+    uint8_t* dev = const_cast<uint8_t*>(c->layers[l].experts);
+    cudaError_t e = cudaSuccess;
+    for (const auto& ld : loads)
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(dev + static_cast<size_t>(ld.second) * eb,
+                                c->host_pool + (static_cast<size_t>(l) * d.E + ld.first) * eb, eb, cudaMemcpyHostToDevice,
+                                c->stream);
+    int* row = c->h_slot_of + static_cast<size_t>(l) * d.E;
+    memcpy(row, c->spill.slot_of.data() + static_cast<size_t>(l) * d.E, sizeof(int) * d.E);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(c->d_slot_of + static_cast<size_t>(l) * d.E, row, sizeof(int) * d.E, cudaMemcpyHostToDevice,
+                            c->stream);
+    c->spill_bytes += loads.size() * eb;
+    c->spill.stats[4] += loads.size();
+    return e;
+}
+
+// One batched step over a spilling pool (not captured: the host decides residency between
+// each layer's router and its experts).  Per layer: mixer and router on the device, the
+// routed ids back to the host, the residency policy makes the selected experts resident
+// (host -> HBM on the context stream, ordered before the expert kernels), then the rest of
+// the MoE.  Earlier copies of a slot table row have completed by the time the row changes
+// again: every layer synchronises the stream before its residency decision.
+static int spill_step(dm_ctx* c, int n, int write_logits) {
+    const Dims& d = c->d;
+    BatchBuffers& bb = c->bb;
+    const LaunchCfg lc = lcfg(c);
+    std::vector<std::pair<int, int>> loads;
+    cudaError_t e = launch_b_embed(lc, d, c->embed, bb, c->b, n);
+    for (int l = 0; l < d.L && e == cudaSuccess; ++l) {
+        e = enqueue_b_mixer(c, l, n);
+        if (e == cudaSuccess) e = launch_b_router(lc, d, c->layers[l], bb, bb.xm, 1, n);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(c->h_sids, bb.ids, sizeof(int) * n * d.topk, cudaMemcpyDeviceToHost, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) break;
+        for (int i = 0; i < n * d.topk; ++i)
+            c->h_sids[i] = std::min(std::max(c->h_sids[i], 0), d.E - 1);
+        if (!c->spill.resolve(l, c->h_sids, n * d.topk, loads))
+            return set_err(c, DM_ERR_CAPACITY, "SPILL_CAPACITY", "decode", l,
+                           "expert cache of %d slots cannot hold the experts of this step", d.E_res);
+        e = spill_apply(c, l, loads);
+        if (e == cudaSuccess) e = enqueue_b_moe_tail(c, l, n, c->d_slot_of + static_cast<size_t>(l) * d.E);
+    }
+    if (e == cudaSuccess) e = enqueue_b_head(c, n, write_logits);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "decode", -1, "%s", cudaGetErrorString(e));
+    return DM_OK;
+}
+
+// n_steps batched steps over a spilling pool; tokens fed back on the device as in the
+// captured step.  The cache must be able to hold one step's experts next to the pinned
+// ones: n * top-k + pinned <= slots, checked before any work.
+static int spill_decode(dm_ctx* c, const int32_t* slots, const int32_t* tokens, int n, int n_steps,
+                        int32_t* tokens_out, float* logits) {
+    int rc = prepare_batch(c, slots, tokens, n, n_steps);
+    if (rc != DM_OK) return rc;
+    const Dims& d = c->d;
+    int pinned = 0;
+    for (int l = 0; l < d.L; ++l) pinned = std::max(pinned, c->spill.pinned_count[l]);
+    if (n * d.topk + pinned > d.E_res)
+        return set_err(c, DM_ERR_CAPACITY, "SPILL_CAPACITY", "decode", -1,
+                       "%d rows x top-%d experts + %d pinned exceed the %d cache slots of a layer", n, d.topk, pinned,
+                       d.E_res);
+    for (int i = 0; i < n_steps; ++i) {
+        rc = spill_step(c, n, (logits && i == n_steps - 1) ? 1 : 0);
+        if (rc != DM_OK) return rc;
+    }
+    DM_CUDA(c, cudaMemcpyAsync(c->h_bio + 2 * kMaxBatch, c->bb.tok, sizeof(int) * n, cudaMemcpyDeviceToHost, c->stream),
+            "decode");
+    if (logits)
+        DM_CUDA(c, cudaMemcpyAsync(logits, c->bb.head_logits, sizeof(float) * n * d.V, cudaMemcpyDeviceToHost, c->stream),
+                "decode");
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "decode");
+    for (int i = 0; i < n; ++i) advance_lens(c, slots[i], n_steps);
+    rc = check_device_error(c, "decode");
+    if (rc == DM_OK && tokens_out)
+        for (int i = 0; i < n; ++i) tokens_out[i] = c->h_bio[2 * kMaxBatch + i];
+    return rc;
 }
 
 static int ensure_bgraph(dm_ctx* c, int n, int write_logits) {
@@ -2125,6 +2339,7 @@ static void ep_close(dm_ctx* c) {
 
 int32_t dm_ep_attach(dm_ctx* c, int32_t rank, int32_t world, const void* handles) {
     if (!c || !handles) return DM_ERR_INVALID_ARG;
+    if (spilling(c)) return spill_reject(c, "an expert-parallel group");
     const Dims& d = c->d;
     if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
         return set_err(c, DM_ERR_INVALID_ARG, "EP_ERROR", "ep", -1, "rank %d of %d outside [0, world <= %d)", rank, world, kMaxRanks);
@@ -2185,6 +2400,7 @@ int32_t dm_batch_capacity(dm_ctx* c, int32_t* cap) {
 
 int32_t dm_decode_batch(dm_ctx* c, const int32_t* slots, const int32_t* tokens_in, int32_t n, int32_t* tokens_out,
                         float* logits) {
+    if (c && spilling(c)) return spill_decode(c, slots, tokens_in, n, 1, tokens_out, logits);
     int rc = prepare_batch(c, slots, tokens_in, n, 1);
     if (rc != DM_OK) return rc;
     const int wl = logits ? 1 : 0;
@@ -2203,6 +2419,8 @@ int32_t dm_decode_batch(dm_ctx* c, const int32_t* slots, const int32_t* tokens_i
 }
 
 int32_t dm_enqueue_decode_batch(dm_ctx* c, const int32_t* slots, const int32_t* tokens_in, int32_t n, int32_t n_steps) {
+    // a spilling pool runs the steps here (the host takes part in every layer)
+    if (c && spilling(c)) return spill_decode(c, slots, tokens_in, n, n_steps, nullptr, nullptr);
     int rc = prepare_batch(c, slots, tokens_in, n, n_steps);
     if (rc != DM_OK) return rc;
     if ((rc = ensure_bgraph(c, n, 0)) != DM_OK) return rc;
@@ -2224,6 +2442,29 @@ int32_t dm_generate_batch(dm_ctx* c, const int32_t* slots, const int32_t* tokens
     int rc = dm_enqueue_decode_batch(c, slots, tokens_in, n, n_steps);
     if (rc != DM_OK) return rc;
     return dm_batch_read_generated(c, n, n_steps, out);
+}
+
+int32_t dm_spill_stats(dm_ctx* c, uint64_t* out8) {
+    if (!c || !out8) return DM_ERR_INVALID_ARG;
+    memcpy(out8, c->spill.stats, sizeof(uint64_t) * 6);
+    out8[6] = c->spill_bytes;
+    out8[7] = spilling(c) ? static_cast<uint64_t>(c->d.E_res) : 0;
+    return DM_OK;
+}
+
+int32_t dm_spill_pin(dm_ctx* c, int32_t layer, int32_t expert, int32_t* pinned) {
+    if (!c) return DM_ERR_INVALID_ARG;
+    if (!spilling(c)) return set_err(c, DM_ERR_INVALID_ARG, "SPILL_UNSUPPORTED", "loader", layer, "the expert pool does not spill");
+    if (layer < 0 || layer >= c->d.L || expert < 0 || expert >= c->d.E)
+        return set_err(c, DM_ERR_INVALID_ARG, "SPILL_ERROR", "loader", layer, "expert index out of range");
+    std::vector<std::pair<int, int>> loads;
+    const int r = c->spill.pin(layer, expert, loads);
+    if (r < 0) return set_err(c, DM_ERR_CAPACITY, "SPILL_CAPACITY", "loader", layer, "no slot can hold expert %d", expert);
+    cudaSetDevice(c->device);
+    DM_CUDA(c, spill_apply(c, layer, loads), "loader");
+    DM_CUDA(c, cudaStreamSynchronize(c->stream), "loader");
+    if (pinned) *pinned = r;
+    return DM_OK;
 }
 
 int32_t dm_batch_stats(dm_ctx* c, int32_t reset, uint32_t* out4) {
@@ -2296,6 +2537,7 @@ int32_t dm_mixer_block(dm_ctx* c, int32_t layer, int32_t slot, int32_t pos_offse
 }
 
 int32_t dm_block_forward(dm_ctx* c, int32_t layer, int32_t slot, int32_t pos_offset, const float* x, int32_t n, float* y) {
+    if (c && spilling(c)) return spill_reject(c, "dm_block_forward");
     int rc = layer_args_ok(c, layer, x, n, y);
     if (rc == DM_OK) rc = check_slot(c, slot);
     if (rc != DM_OK) return rc;
@@ -2303,6 +2545,7 @@ int32_t dm_block_forward(dm_ctx* c, int32_t layer, int32_t slot, int32_t pos_off
 }
 
 int32_t dm_moe_block(dm_ctx* c, int32_t layer, const float* x_mid, int32_t n, float* y) {
+    if (c && spilling(c)) return spill_reject(c, "dm_moe_block");
     int rc = layer_args_ok(c, layer, x_mid, n, y);
     if (rc != DM_OK) return rc;
     cudaSetDevice(c->device);
@@ -2382,6 +2625,7 @@ int32_t dm_trace_timeline(dm_ctx* c, uint64_t* rec_host, int32_t* kinds_host, in
 // ---- kernel timing (roofline measurement) ----------------------------------------------
 int32_t dm_time_kernel(dm_ctx* c, int32_t which, int32_t layer, int32_t iters, float* avg_ms, uint64_t* bytes) {
     if (!c || !avg_ms || !bytes || iters <= 0) return DM_ERR_INVALID_ARG;
+    if (spilling(c)) return spill_reject(c, "dm_time_kernel");
     const Dims& d = c->d;
     if (layer < 0 || layer >= d.L) return set_err(c, DM_ERR_INVALID_ARG, "PROFILE", "profile", layer, "layer out of range");
     const LayerW& w = c->layers[layer];
@@ -2461,6 +2705,7 @@ int32_t dm_time_kernel(dm_ctx* c, int32_t which, int32_t layer, int32_t iters, f
 int32_t dm_time_batch_kernel(dm_ctx* c, int32_t n, int32_t which, int32_t layer, int32_t iters, float* avg_ms,
                              uint64_t* bytes) {
     if (!c || !avg_ms || !bytes || iters <= 0 || n <= 0 || n > c->bb.cap) return DM_ERR_INVALID_ARG;
+    if (spilling(c)) return spill_reject(c, "dm_time_batch_kernel");
     const Dims& d = c->d;
     if (layer < 0 || layer >= d.L) return set_err(c, DM_ERR_INVALID_ARG, "PROFILE", "profile", layer, "layer out of range");
     const LayerW& w = c->layers[layer];
@@ -2689,6 +2934,7 @@ int32_t dm_synth_model_device(dm_ctx* c, uint64_t seed) {
                 uint8_t* rec = expert_record(c, l, e);
                 uint8_t* dst = p == DM_PROJ_DOWN ? rec + static_cast<size_t>(d.gu_chunks) * d.gu_chunk_bytes : rec;
                 if (ce == cudaSuccess) ce = launch_repack_rows(c->stream, c->stage_q, c->stage_s, c->stage_z, rows, cols, d.G, p, dst);
+                if (ce == cudaSuccess) ce = spill_store(c, l, e, p);
                 if (ce != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "synth", l, "%s", cudaGetErrorString(ce));
                 c->have_expert[(static_cast<size_t>(l) * (d.E + 1) + (e + 1)) * 3 + p] = 1;
             }

@@ -367,6 +367,8 @@ struct BGroupArgs {
     EpView ep;
     unsigned* my_flags;   // [2][kMaxRanks]
     unsigned* epoch;      // [2]
+    const int* slot_of;   // [E] HBM slot of each routed expert when the pool spills, else null
+    int E_res;            // resident routed records (the shared expert's record index)
     uint32_t* err;
 };
 
@@ -496,7 +498,9 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
     const bool pairs_ok = total_pairs <= a.max_pairs && total_segs <= a.max_segs;
     if (el <= Eo) {
         start[el] = p0;
-        const int gexp = el < Eo ? e0 + el : E;
+        // the record index the expert kernels address: the expert itself, its cache slot
+        // when the pool spills, or the shared expert's record after the routed ones
+        const int gexp = el < Eo ? (a.slot_of ? a.slot_of[e0 + el] : e0 + el) : a.E_res;
         if (pairs_ok)
             for (int s2 = 0; s2 < nsg; ++s2)
                 a.segs[s0 + s2] = make_int4(gexp, p0 + s2 * kSegTok, min(kSegTok, cnt - s2 * kSegTok), 0);
@@ -533,7 +537,8 @@ size_t b_topk_group_smem(int E, int topk) {
     return static_cast<size_t>(kMaxRanks) * kMaxBatch * topk * 4;
 }
 
-cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n) {
+cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n,
+                                const int* slot_of) {
     BGroupArgs a{};
     a.logits = bb.logits;
     a.E = d.E;
@@ -551,6 +556,8 @@ cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchB
     a.ep = bb.ep;
     a.my_flags = bb.ep_flags;
     a.epoch = bb.ep_epoch;
+    a.slot_of = slot_of;
+    a.E_res = d.E_res;
     a.err = b.err;
     return launch_kernel(lc, b_topk_group_kernel, dim3(1), dim3(kBGThreads), b_topk_group_smem(d.E, d.topk), a);
 }

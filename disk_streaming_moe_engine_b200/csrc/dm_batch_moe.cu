@@ -595,7 +595,7 @@ cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.experts = w.experts;
     a.shared = w.shared;
     a.expert_bytes = d.expert_bytes;
-    a.E = d.E;
+    a.E = d.E_res;  // routed records before the shared one
     a.segs = bb.segs;
     a.work = bb.work;
     a.pair_src = bb.pair_src;

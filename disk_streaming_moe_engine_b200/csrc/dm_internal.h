@@ -15,6 +15,8 @@
 //   KV cache        bf16 pages [att_layer][page][K|V][Hkv][16][D], page table per slot.
 #pragma once
 #include <cstdint>
+#include <utility>
+#include <vector>
 #include <cuda_runtime.h>
 
 // Device error word bits (OR-ed by kernels, read by the host after a step).
@@ -42,6 +44,8 @@ struct Dims {
     int qkv_dim, z_dim, gdn_in_rows;     // 2*nk*dk + nv*dv, nv*dv, qkv+z+2nv
     int attn_in_rows;                    // 2*Hq*D + 2*Hkv*D
     int E, topk, I, G;
+    int E_res;                           // routed expert records resident in HBM per layer
+                                         // (E, or the cache slots when the pool spills)
     int max_seqs, num_pages, max_pages;
     int n_gdn, n_att;
     // expert record geometry (bytes)
@@ -264,8 +268,9 @@ cudaError_t launch_attn_merge_batch(const LaunchCfg& lc, const Dims& d, const Ba
 // MoE of one layer for n rows: router (canonical), top-k + grouping, experts, combine.
 cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
                             const float* x, int normalise, int n);
+// slot_of: [E] record slot of each routed expert of this layer when the pool spills, else null
 cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b,
-                                int n);
+                                int n, const int* slot_of = nullptr);
 cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
                              const Buffers& b, int n);
 cudaError_t launch_b_combine(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const float* xm, float* out,
@@ -278,4 +283,27 @@ cudaError_t batch_set_attrs();
 bool expert_tma_supported(int K);
 // SHA-256 (FIPS 180-4) of the concatenation of n buffers (dm_sha256.cu).
 void sha256_parts(const uint8_t* const* parts, const size_t* sizes, int n, uint8_t out[32]);
+
+// Residency of the expert cache when the pool spills to host memory (dm_spill.cu).
+// stats: [0] accesses, [1] hits, [2] misses, [3] evictions, [4] records loaded,
+// [5] pin requests kept unpinned (over the 25 % budget).
+struct SpillPolicy {
+    int L = 0, E = 0, C = 0;
+    uint64_t clock = 0;
+    std::vector<int> slot_of;        // [L][E] slot or -1
+    std::vector<int> expert_in;      // [L][C] expert or -1
+    std::vector<uint64_t> stamp;     // [L][C] last use
+    std::vector<uint8_t> pinned;     // [L][C]
+    std::vector<uint8_t> in_use;     // [C] needed by the step being resolved
+    std::vector<int> pinned_count;   // [L]
+    uint64_t stats[6] = {};
+    void init(int L, int E, int C);
+    // the distinct experts of ids[0..count) for layer l become resident; (expert, slot)
+    // loads to perform are returned in order; false when the cache cannot hold them all
+    bool resolve(int l, const int* ids, int count, std::vector<std::pair<int, int>>& loads);
+    // 1 pinned, 0 kept unpinned (budget), -1 no slot
+    int pin(int l, int e, std::vector<std::pair<int, int>>& loads);
+    int victim(int l) const;
+    int place(int l, int e, std::vector<std::pair<int, int>>& loads);
+};
 }  // namespace dm

@@ -214,6 +214,20 @@ class Engine:
         self._ok(self.lib.dm_expert_download(self.ctx, layer, expert, proj, _ptr(q), _ptr(s), _ptr(z)))
         return q, s, z
 
+    # ---- spilling expert pool (RuntimeConfig.expert_cache_slots > 0) ----
+    SPILL_KEYS = ("accesses", "hits", "misses", "evictions", "loads", "pins_kept_unpinned", "bytes_h2d", "slots")
+
+    def spill_stats(self) -> dict:
+        out = (C.c_uint64 * 8)()
+        self._ok(self.lib.dm_spill_stats(self.ctx, out))
+        return dict(zip(self.SPILL_KEYS, (int(v) for v in out)))
+
+    def spill_pin(self, layer: int, expert: int) -> bool:
+        """Makes the expert resident and pins it (False: kept unpinned, over the 25 % budget)."""
+        r = C.c_int32()
+        self._ok(self.lib.dm_spill_pin(self.ctx, layer, expert, C.byref(r)))
+        return bool(r.value)
+
     # ---- quant-file loaders (formats.py parses; these dequantise / load on the device) ----
     def gguf_dequant(self, raw: bytes, ggml_type: int, n: int, q4k_mojo: bool = False,
                      want_f32: bool = True, want_bf16: bool = False):

@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define DM_ABI_VERSION 1
+#define DM_ABI_VERSION 2
 
 /* ---- status codes ------------------------------------------------------------------ */
 #define DM_OK 0
@@ -83,6 +83,10 @@ typedef struct dm_runtime_config {
     int32_t kv_page_tokens;    /* tokens per KV page; must be 16                       */
     int32_t kv_num_pages;      /* pages in the shared pool (per attention layer)       */
     int32_t max_pages_per_seq; /* page-table width; capacity = this * 16 tokens        */
+    int32_t expert_cache_slots; /* 0: every expert resident in HBM.  C in
+                                 * [num_experts_per_tok, num_experts): C routed expert
+                                 * records per layer in HBM, all of them in pinned host
+                                 * memory, loaded on demand (see dm_spill_stats)         */
 } dm_runtime_config;
 
 typedef struct dm_ctx dm_ctx;
@@ -475,6 +479,28 @@ int32_t dm_kmss_load(dm_ctx* ctx, int32_t slot, const char* path, int32_t* token
                      int32_t* n_tokens);
 /* SHA-256 of n bytes (FIPS 180-4); needs no device. */
 int32_t dm_sha256(const uint8_t* data, uint64_t n, uint8_t* out32);
+
+/* ---- spilling expert pool (expert_cache_slots = C > 0) --------------------------------
+ * The routed experts of every layer live in pinned host memory; C of them per layer are
+ * resident in HBM.  Each batched step brings, per layer, the experts its rows selected into
+ * HBM before the expert kernels run (host -> device copies on the context stream) and
+ * evicts the least recently used unpinned ones (the contract of the reference's expert
+ * cache, src/io/lru_cache.mojo:225-610).  Single-sequence decode (dm_decode_step,
+ * dm_forward, dm_generate) runs as one-row batched steps; dm_enqueue_decode,
+ * dm_block_forward, dm_moe_block, the kernel timers and expert-parallel groups need every
+ * expert resident and return DM_ERR_INVALID_ARG.  A step needs n * top-k + pinned <= C
+ * (DM_ERR_CAPACITY otherwise, before any work).
+ * out8: accesses, hits, misses, evictions, records loaded, pins kept unpinned (over the
+ * 25 % pin budget), bytes copied host -> device, C (0 when the pool does not spill). */
+int32_t dm_spill_stats(dm_ctx* ctx, uint64_t* out8);
+/* Makes expert `expert` of `layer` resident and pins it while the pinned records of the
+ * layer stay within 25 % of C; *pinned = 1 if pinned, 0 if kept unpinned. */
+int32_t dm_spill_pin(dm_ctx* ctx, int32_t layer, int32_t expert, int32_t* pinned);
+/* The residency policy alone on a trace of routed ids ([steps][L][n][topk]) after the
+ * given (layer, expert) pins, no device: stats_out as out8[0..5]; slot_of_out [L][E] the
+ * final slot of every expert (-1 = host only).  Either output may be NULL. */
+int32_t dm_spill_simulate(int32_t L, int32_t E, int32_t C, int32_t steps, int32_t n, int32_t topk, const int32_t* ids,
+                          const int32_t* pins, int32_t npins, uint64_t* stats_out, int32_t* slot_of_out);
 
 /* Fills every weight of the context with the synthetic distributions of the benchmark
  * configs directly on the device (same generator; used for multi-GB models). */

@@ -28,7 +28,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version(lib):
-    assert lib.dm_abi_version() == 1
+    assert lib.dm_abi_version() == 2
 
 
 def _validate(lib, cfg):
