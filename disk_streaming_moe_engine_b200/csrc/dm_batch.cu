@@ -237,7 +237,7 @@ __global__ void __launch_bounds__(kBRThreads, 1) b_router_kernel(const __grid_co
     constexpr int XPT = (K + kBRThreads - 1) / kBRThreads;  // elements of a row per thread
     constexpr int RB = K <= 2048 ? kBRTok : kBRTok / 2;       // rows loaded together
     extern __shared__ __align__(16) float xs_all[];  // [kBRTok][K]; then the top-k scratch
-    __shared__ float red[kBRThreads / 32];
+    __shared__ float red[kBRTok * (kBRThreads / 32)];
     __shared__ int s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int row = blockIdx.x * (kBRThreads / 32) + warp;
@@ -268,16 +268,11 @@ __global__ void __launch_bounds__(kBRThreads, 1) b_router_kernel(const __grid_co
                     const int k = i * kBRThreads + tid;
                     xv[r][i] = (t0 + r < nt && k < K) ? a.x[static_cast<size_t>(b0 + t0 + r) * K + k] : 0.0f;
                 }
-#pragma unroll
-            for (int r = 0; r < RB; ++r) {
-                const int t = t0 + r;
-                if (t < nt) {  // uniform over the CTA
-                    float* xs = xs_all + static_cast<size_t>(t) * K;
-                    float* xn = (blockIdx.x == 0 && a.xn) ? a.xn + static_cast<size_t>(b0 + t) * K : nullptr;
-                    canon_rmsnorm_split_loaded<K, kBRThreads>(xv[r], a.gamma, a.eps, xs, xn, red);
-                    __syncthreads();  // xs complete; red free for the next row
-                }
-            }
+            // the RB rows' reductions together (one barrier), each row in the canonical order
+            float* xn = (blockIdx.x == 0 && a.xn) ? a.xn + static_cast<size_t>(b0 + t0) * K : nullptr;
+            canon_rmsnorm_split_loaded_rows<K, kBRThreads, RB>(xv, min(RB, nt - t0), a.gamma, a.eps,
+                                                               xs_all + static_cast<size_t>(t0) * K, xn, red);
+            __syncthreads();  // xs complete; red free for the next rows
         }
     }
     pdl_launch_dependents();

@@ -57,14 +57,6 @@ struct BExpArgs {
     uint32_t* err;
 };
 
-DM_DEV void mma_bf16_m16n8k16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                              uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 
 // (q_j, q_{j+4}) of a word of 8 nibbles as bf16 (128 + q) pairs, minus the zero pair.
 DM_DEV uint32_t nib_pair_minus(uint32_t w, int shift, uint32_t zpair) {
@@ -322,8 +314,6 @@ DM_DEV void tma_load_4d(void* smem_dst, const CUtensorMap* map, int x, int y, in
         : "memory");
 }
 
-// (q_j, q_{j+4}) of a word of 8 nibbles as the bf16 pair (128 + q_j, 128 + q_{j+4})
-DM_DEV uint32_t nib_pair128(uint32_t w) { return (w & 0x000F000Fu) | 0x43004300u; }
 
 template <int K, bool GATEUP>
 __global__ void __launch_bounds__(kXThreads, 1) b_expert_tma_kernel(const __grid_constant__ BExpArgs a) {

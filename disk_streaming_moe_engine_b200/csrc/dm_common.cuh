@@ -216,6 +216,21 @@ DM_DEV float bf16lo(uint32_t u) { return __uint_as_float(u << 16); }
 DM_DEV float bf16hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
 
 DM_DEV float bf16_to_f32(uint16_t b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
+
+// D = A B + D on the tensor cores, bf16 inputs, fp32 accumulation (m16n8k16, A row-major,
+// B column-major; fragment layouts of the PTX ISA for mma.sync .m16n8k16).
+DM_DEV void mma_bf16_m16n8k16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                              uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// (q_j, q_{j+4}) of a word of 8 nibbles as the bf16 pair (128 + q_j, 128 + q_{j+4}): the
+// nibble becomes the low mantissa bits of 128.0, an exact integer
+DM_DEV uint32_t nib_pair128(uint32_t w) { return (w & 0x000F000Fu) | 0x43004300u; }
 // fp32 -> bf16 round-to-nearest-even (NaN stays NaN).
 DM_DEV uint16_t f32_to_bf16(float f) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(f));

@@ -75,6 +75,47 @@ DM_DEV void canon_rmsnorm_split_loaded(const float (&xv)[(K + NT - 1) / NT], con
     }
 }
 
+// The same RMSNorm for RB rows at once (rows r < nr valid): every row's sum of squares is
+// formed exactly as above (thread fma order, warp butterfly, warp partials in warp order),
+// so each row gets the bits of canon_rmsnorm_split_loaded, with one block barrier for all
+// RB rows instead of one per row.  red holds RB * NT/32 floats; xs / xn_out row r at
+// xs + r * K (xn_out may be null).  The caller synchronises before xs is read.
+template <int K, int NT, int RB>
+DM_DEV void canon_rmsnorm_split_loaded_rows(const float (&xv)[RB][(K + NT - 1) / NT], int nr, const uint16_t* gamma,
+                                            float eps, float* xs, float* xn_out, float* red) {
+    constexpr int XPT = (K + NT - 1) / NT;
+    constexpr int NW = NT / 32;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float acc[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+        acc[r] = 0.0f;
+#pragma unroll
+        for (int i = 0; i * NT + tid < K && i < XPT; ++i) acc[r] = __fmaf_rn(xv[r][i], xv[r][i], acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < RB; ++r) acc[r] = warp_sum(acc[r]);
+    if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < RB; ++r) red[r * NW + warp] = acc[r];
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+        if (r >= nr) break;
+        float ss = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) ss = __fadd_rn(ss, red[r * NW + w]);
+        const float denom = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps));
+#pragma unroll
+        for (int i = 0; i * NT + tid < K && i < XPT; ++i) {
+            const int k = i * NT + tid;
+            const float y = __fmul_rn(__fdiv_rn(xv[r][i], denom), bf16_to_f32(gamma[k]));
+            xs_store_split(xs + static_cast<size_t>(r) * K, K, k, y);
+            if (xn_out) xn_out[static_cast<size_t>(r) * K + k] = y;
+        }
+    }
+}
+
 // Canonical dot of one bf16 router row (VPL 16-byte vectors per lane, vector i of lane l
 // holding elements 8(l + 32i) .. +7) with x in the split layout; every lane gets the sum.
 template <int VPL>
