@@ -335,7 +335,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t ob_acnt = T(BC * d.Hkv * 4), ob_xn = T(BC * H * 4), ob_lg = T(BC * (d.E + 1) * 4);
     const size_t ob_ids = T(BC * d.topk * 4), ob_pr = T(BC * d.topk * 4), ob_sg = T(BC * 4);
     const size_t ob_segs = T(static_cast<size_t>(max_segs) * 16), ob_work = T(16), ob_stats = T(16);
-    const size_t ob_rcnt = T((BC / 8 + 1) * 4);
+    const size_t ob_rcnt = T((BC + 1) * 4);  // one counter per router row block (down to one row)
     const size_t ob_psrc = T(P * 4), ob_h = T(P * d.I * 4), ob_eout = T(BC * (d.topk + 1) * H * 4);
     const size_t ob_flags = T(2 * kMaxRanks * 4), ob_epoch = T(2 * 4);
     const size_t ob_cv = T(BC * kHeadChunks * 4), ob_ci = T(BC * kHeadChunks * 4), ob_hl = T(BC * d.V * 4);

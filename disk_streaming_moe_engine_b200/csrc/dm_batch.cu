@@ -206,8 +206,9 @@ cudaError_t launch_b_epi_resid(const LaunchCfg& lc, const float* c, int N, const
 }
 
 // ---- batched router (canonical arithmetic, bit-identical logits to the one-token router)
-// Grid (ceil((E+1)/16), ceil(n/kBRTok)), 512 threads: warp w owns router row 16 bx + w
-// (weights in registers before griddepcontrol.wait); the CTA loads its kBRTok input rows
+// Grid (ceil((E+1)/16), ceil(n/tpc)), 512 threads: warp w owns router row 16 bx + w
+// (weights in registers before griddepcontrol.wait); the CTA loads its tpc <= kBRTok input
+// rows (fewer rows per CTA for small batches, so that more CTAs share the work)
 // at once, normalises them into shared memory (split layout), then every warp dots its
 // row with each of them.  CTAs of row block 0 also write the normalised rows (the
 // experts' input).  The last CTA of a block of rows to finish (counter per row block)
@@ -224,7 +225,8 @@ struct BRouterArgs {
     float* xn;              // [n][K]
     float* logits;          // [n][E+1]
     const float* bias;      // [E] logit offsets, or null
-    unsigned* cnt;          // [ceil(cap / kBRTok)] finished CTAs per row block (reset by the last)
+    unsigned* cnt;          // [ceil(cap / tpc)] finished CTAs per row block (reset by the last)
+    int tpc;                // batch rows per CTA (<= kBRTok)
     int* ids;               // [n][topk]
     float* probs;           // [n][topk]
     float* sg;              // [n]
@@ -241,8 +243,8 @@ __global__ void __launch_bounds__(kBRThreads, 1) b_router_kernel(const __grid_co
     __shared__ int s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int row = blockIdx.x * (kBRThreads / 32) + warp;
-    const int b0 = blockIdx.y * kBRTok;
-    const int nt = min(kBRTok, a.n - b0);
+    const int b0 = blockIdx.y * a.tpc;
+    const int nt = min(a.tpc, a.n - b0);
     uint4 wreg[VPL];
     if (row <= a.E) {
         const uint4* wr = reinterpret_cast<const uint4*>(a.W + static_cast<size_t>(row) * K);
@@ -325,11 +327,13 @@ cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.xn = (!normalise && x == bb.xn) ? nullptr : bb.xn;  // rows normalised in place already
     a.logits = bb.logits;
     a.cnt = bb.rcnt;
+    // rows per CTA: enough CTAs to spread the work over the GPU at small batches
+    a.tpc = n <= 8 ? 1 : (n <= 16 ? 2 : (n <= 32 ? 4 : kBRTok));
     a.ids = bb.ids;
     a.probs = bb.probs;
     a.sg = bb.sg;
     a.err = bb.err;
-    const dim3 grid((d.E + 1 + kBRThreads / 32 - 1) / (kBRThreads / 32), (n + kBRTok - 1) / kBRTok);
+    const dim3 grid((d.E + 1 + kBRThreads / 32 - 1) / (kBRThreads / 32), (n + a.tpc - 1) / a.tpc);
     const size_t smem = b_router_smem(d.H, d.E);
     switch (d.H) {
         case 256: return launch_kernel(lc, b_router_kernel<256>, grid, dim3(kBRThreads), smem, a);

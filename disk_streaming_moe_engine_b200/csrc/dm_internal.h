@@ -159,7 +159,7 @@ struct BatchBuffers {
     int* ids;             // [cap][topk]
     float* probs;         // [cap][topk]
     float* sg;            // [cap] shared-expert gate
-    unsigned* rcnt;       // [cap / 8 + 1] finished router CTAs per block of rows
+    unsigned* rcnt;       // [cap + 1] finished router CTAs per block of rows
     uint32_t* err;        // the context's device error word
     int4* segs;           // [max_segs] (expert, first pair, tokens, 0); expert E = shared
     int* work;            // [4] segments, gate/up work counter, down work counter, spare
