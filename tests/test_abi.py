@@ -84,3 +84,40 @@ def test_synth_is_counter_based(lib):
 def test_expert_bytes_match_baseline_figure():
     # 4.3125 bits/weight: 1,695,744 B per full-shape expert (gate + up + down)
     assert preset("full").expert_bytes() == 1695744
+
+
+def test_plain_c_host_links_and_calls(tmp_path, lib):
+    """The library as a plain C host links it (gcc, the header only): config validation,
+    SHA-256, the GGUF and quant-file parsers and the spill policy answer without a device."""
+    import hashlib
+    import json as _json
+    import shutil
+    import subprocess
+
+    import numpy as np
+
+    import formats_util as fu
+    from disk_streaming_moe_engine_b200 import _lib as L
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = str(tmp_path / "harness")
+    libdir = os.path.dirname(L.LIB_PATH)
+    subprocess.run([gcc, "-O1", "-std=c11", "-I", os.path.join(repo, "include"),
+                    os.path.join(repo, "tests", "c_abi", "harness.c"), "-o", exe, "-L", libdir, "-ldismoen_cuda",
+                    f"-Wl,-rpath,{libdir}", "-Wl,-rpath,/usr/local/cuda/lib64"], check=True)
+    gg = tmp_path / "m.gguf"
+    gg.write_bytes(fu.write_gguf([("general.architecture", 8, "qwen3.6")],
+                                 [("tok", [32, 4], 8, fu.random_blocks(8, 128, np.random.default_rng(0)))]))
+    s, p = fu.sym4_quantize(np.linspace(-1, 1, 128, dtype=np.float32), 64)
+    qf = tmp_path / "m.q4"
+    qf.write_bytes(fu.quant_file("m", [fu.quant_record("w", [2, 64], s, p, 64)]))
+    out = subprocess.run([exe, str(gg), str(qf)], check=True, capture_output=True, text=True).stdout
+    r = _json.loads(out)
+    assert r["abi"] == 2 and r["cfg_ok"] == 0 and r["cfg_bad"] != 0
+    assert r["sha_abc"] == hashlib.sha256(b"abc").hexdigest()
+    assert r["gguf"][:3] == [0, 3, 1] and r["gguf"][5:] == ["tok", 8]
+    assert r["quant"] == [0, 1, 64, 1]
+    # 4 slots: step 1 {0,1,2,3} misses 4; step 2 {2,3,4,5} hits 2, misses 2, evicts 0 and 1
+    assert r["spill"] == [0, 8, 2, 6, 2]
