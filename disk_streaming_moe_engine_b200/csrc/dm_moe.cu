@@ -259,10 +259,13 @@ bool moe_supported(int H, int I, int G) {
 //               flag.
 //   issue     : every CTA bulk-copies its routed gate/up chunks and its 16-row down
 //               chunk of every selected expert (the down data lands during phase 2).
-//   phase 2   : gate/up GEMVs, h = SiLU(g) * u to global; grid barrier.
+//   phase 2   : gate/up GEMVs, h = SiLU(g) * u to global; grid barrier (arrivals on a
+//               64-bit counter that is never reset: the target is the launch generation
+//               read at the start, plus one, times the grid).
 //   phase 3   : CTAs 0..H/16-1 reduce their 16 output rows over all experts (two warp
 //               groups split the experts, combined in a fixed order) + residual.
-//   exit      : the last CTA out resets the flags for the next launch.
+//   exit      : nothing to reset (generation-tagged flags; the router logit slots are
+//               emptied by CTA 0 once read), so the grid ends as its last rows are stored.
 struct MoeFusedArgs {
     const uint16_t* Wr;       // [E+1][H] router rows + shared-gate row
     const float* rbias;       // [E] logit offsets, or null
@@ -280,8 +283,8 @@ struct MoeFusedArgs {
     float* probs;
     float* shared_g;
     float* h;                 // [(topk+1)][I]
-    unsigned* sync;           // [4]: router count, (unused), up count, exit count
-    unsigned long long* idflag; // [4] released words: marker bit 63 | 4 ids x 15 bits
+    unsigned long long* arrivals; // up-phase arrivals of every launch so far (never reset)
+    unsigned long long* idflag; // [4] released words: launch tag in bit 63 | 4 ids x 15 bits
     uint64_t* trace;          // phase stamps of CTA 0 and of the last CTA, or null
     uint64_t* cta_trace;      // per-CTA stamps (kTrMoeCtaSlots per CTA, thread 0) or null
     uint64_t* kt;             // launch timeline record or null
@@ -297,6 +300,14 @@ DM_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+DM_DEV unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+DM_DEV void red_release_add_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 DM_DEV unsigned ld_relaxed_u32(const unsigned* p) {
     unsigned v;
@@ -325,15 +336,28 @@ DM_DEV float poll_logit(const float* p, uint32_t* err) {
     }
 }
 
-// Bounded wait until bit 63 of *p is set; returns the word.
-DM_DEV unsigned long long spin_marker(const unsigned long long* p, uint32_t* err) {
+// Bounded wait until *p >= target (64-bit counter); false on timeout.
+DM_DEV bool spin_geq_u64(const unsigned long long* p, unsigned long long target, uint32_t* err) {
+    if (ld_acquire_u64(p) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; ++n) {
+        if (ld_acquire_u64(p) >= target) return true;
+        if (n % 256 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
+            raise_error(err, DM_DEVERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
+// Bounded wait until bit 63 of *p equals tag; returns the word.
+DM_DEV unsigned long long spin_marker(const unsigned long long* p, unsigned tag, uint32_t* err) {
     unsigned long long v = ld_acquire_u64(p);
-    if (v >> 63) return v;
+    if ((v >> 63) == tag) return v;
     const uint64_t t0 = globaltimer_ns();
     uint32_t n = 0;
     while (true) {
         v = ld_acquire_u64(p);
-        if (v >> 63) return v;
+        if ((v >> 63) == tag) return v;
         if (++n % 256 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
             raise_error(err, DM_DEVERR_TIMEOUT);
             return 0;
@@ -367,6 +391,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     __shared__ int sid[kMaxTopK];
     __shared__ float sp[kMaxTopK + 1];
     __shared__ float red[kMoeThreads / 32];
+    __shared__ unsigned long long s_gen;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int nblk = gridDim.x, c = blockIdx.x;
     const int nexp = a.topk + 1;
@@ -425,6 +450,12 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     kt_ready(a.kt);
     trace_stamp(tr, 1);
     trace_stamp(ct, 1);
+    // Launch generation: the arrival counter grows by nblk per launch and is never reset,
+    // and this CTA reads it before it arrives itself, when fewer than nblk arrivals of this
+    // launch can have happened, so the quotient is the number of earlier launches.  The id
+    // words carry its parity, flipped, as their tag, so the previous launch's words never
+    // match: no flag needs resetting at exit.
+    if (tid == 0) s_gen = ld_relaxed_u64(a.arrivals) / static_cast<unsigned long long>(nblk);
     // residual of this warp's output row (phase 3), fetched now, off the critical path
     const float xm_row = (has_down && lane == 0) ? a.x_mid[16 * c + warp] : 0.0f;
 
@@ -685,7 +716,8 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
                 // Relaxed stores: no fence on the critical path.
         #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                    if (k < (a.topk + 3) / 4) st_relaxed_u64(&a.idflag[k], words[k] | (1ull << 63));
+                    if (k < (a.topk + 3) / 4)
+                        st_relaxed_u64(&a.idflag[k], words[k] | (static_cast<unsigned long long>(1u - (s_gen & 1u)) << 63));
                 trace_stamp(tr ? tr + 20 : nullptr, 3);
             }
             // every slot has been read: empty them for the next launch
@@ -694,7 +726,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         __syncthreads();
     } else {
         if (tid < (a.topk + 3) / 4) {
-            const unsigned long long w = spin_marker(&a.idflag[tid], a.err);
+            const unsigned long long w = spin_marker(&a.idflag[tid], 1u - static_cast<unsigned>(s_gen & 1u), a.err);
             for (int r = 4 * tid; r < a.topk && r < 4 * tid + 4; ++r)
                 sid[r] = min(static_cast<int>((w >> (15 * (r & 3))) & 0x7FFF), a.E - 1);
         }
@@ -763,8 +795,9 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     trace_stamp(tr, 6);
     trace_stamp(ct, 4);
     if (tid == 0) {
-        red_release_add(&a.sync[2], 1u);
-        if (has_down) spin_geq(&a.sync[2], static_cast<unsigned>(nblk), a.err);
+        const unsigned long long target = (s_gen + 1) * static_cast<unsigned long long>(nblk);
+        red_release_add_u64(a.arrivals, 1ull);
+        if (has_down) spin_geq_u64(a.arrivals, target, a.err);
     }
     __syncthreads();
     trace_stamp(tr, 7);
@@ -862,22 +895,10 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         // no down rows here: drain this CTA's own shared-expert chunk copies (none issued)
     }
 
-    // ---- exit: the last CTA resets the flags for the next launch ----
     __syncthreads();
     trace_stamp(tr, 8);
     trace_stamp(ct, 6);
     kt_end(a.kt);
-    if (tid == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(&a.sync[3], 1u);
-        if (prev == static_cast<unsigned>(nblk) - 1) {
-            a.sync[0] = 0u;
-            a.sync[2] = 0u;
-            for (int k = 0; k < 4; ++k) a.idflag[k] = 0ull;
-            a.sync[3] = 0u;
-            __threadfence();
-        }
-    }
 }
 
 template <int K, int KI, int G>
@@ -916,7 +937,7 @@ cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.probs = b.topk_p;
     a.shared_g = b.shared_g;
     a.h = b.h;
-    a.sync = b.counters + kCntMoeSync;
+    a.arrivals = reinterpret_cast<unsigned long long*>(b.counters + kCntMoeSync);
     a.idflag = reinterpret_cast<unsigned long long*>(b.counters + kCntMoeFlag);
     a.trace = b.trace ? b.trace + kTrMoe : nullptr;
     a.cta_trace = b.trace ? b.trace + kTrMoeCta : nullptr;
