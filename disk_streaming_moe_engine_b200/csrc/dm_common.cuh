@@ -126,6 +126,34 @@ DM_DEV unsigned ld_acquire_u32(const unsigned* p) {
 DM_DEV void red_release_add(unsigned* p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// 64-bit grid counters that are never reset: a launch reads the count before it
+// arrives itself and waits for (count / grid + 1) * grid.
+DM_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+DM_DEV unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+DM_DEV void red_release_add_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Bounded wait until *p >= target (64-bit counter); false on timeout.
+DM_DEV bool spin_geq_u64(const unsigned long long* p, unsigned long long target, uint32_t* err) {
+    if (ld_acquire_u64(p) >= target) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t n = 1;; ++n) {
+        if (ld_acquire_u64(p) >= target) return true;
+        if (n % 256 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
+            raise_error(err, DM_DEVERR_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 // Bounded wait until *p >= target (thread-level; callers use one thread per CTA).
 DM_DEV bool spin_geq(const unsigned* p, unsigned target, uint32_t* err) {
     if (ld_acquire_u32(p) >= target) return true;

@@ -227,7 +227,7 @@ struct GdnFusedArgs {
     const float* x_res;     // [H]
     float* x_mid;           // [H]
     int H, rmax;
-    unsigned* sync;         // [2]: arrivals, exits
+    unsigned long long* arrivals;  // grid-barrier arrivals of every launch so far (never reset)
     uint32_t* err;
 };
 
@@ -242,6 +242,7 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
     extern __shared__ __align__(128) uint8_t gsm[];
     __shared__ float qs[4][DK], ks[4][DK], vs[4][RB];
     __shared__ __align__(8) uint64_t wbar;
+    __shared__ unsigned long long s_gen;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int grp = warp >> 2, gw = warp & 3, gt = tid & 127;
     const int c = blockIdx.x, G = gridDim.x;
@@ -285,6 +286,9 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
     }
     pdl_wait();
     kt_ready(a.kt);
+    // launch generation: the arrival count (grown by G per launch, never reset) read before
+    // this CTA arrives, when fewer than G arrivals of this launch can have happened
+    if (tid == 0) s_gen = ld_relaxed_u64(f.arrivals) / static_cast<unsigned long long>(G);
 
     // ---- phase 1: recurrence ----
     if (has_item) {
@@ -347,9 +351,10 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
     __syncthreads();
     pdl_launch_dependents();
     if (tid == 0) {
+        const unsigned long long target = (s_gen + 1) * static_cast<unsigned long long>(G);
         __threadfence();
-        red_release_add(&f.sync[0], 1u);
-        spin_geq(&f.sync[0], static_cast<unsigned>(G), f.err);
+        red_release_add_u64(f.arrivals, 1ull);
+        spin_geq_u64(f.arrivals, target, f.err);
     }
     __syncthreads();
 
@@ -403,15 +408,7 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
         if (lane == 0) f.x_mid[r0 + r] = f.x_res[r0 + r] + (wok ? acc : 0.0f);
     }
     __syncthreads();
-    kt_end(a.kt);
-    if (tid == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(&f.sync[1], 1u);
-        if (prev == static_cast<unsigned>(G) - 1) {
-            f.sync[0] = 0u;
-            f.sync[1] = 0u;
-        }
-    }
+    kt_end(a.kt);  // nothing to reset: the barrier counter is generation-based
 }
 
 static size_t gdn_fused_smem(const Dims& d, int G) {
@@ -461,7 +458,7 @@ cudaError_t launch_gdn_core_out(const LaunchCfg& lc, const Dims& d, const LayerW
     f.H = d.H;
     const int G = lc.num_sms;
     f.rmax = (d.H + G - 1) / G;
-    f.sync = b.counters + kCntGdnSync;
+    f.arrivals = reinterpret_cast<unsigned long long*>(b.counters + kCntGdnSync);
     f.err = b.err;
     const size_t smem = gdn_fused_smem(d, G);
     if (d.dk == 128) return launch_kernel(lc, gdn_core_out_kernel<128>, dim3(G), dim3(kGfThreads), smem, f);

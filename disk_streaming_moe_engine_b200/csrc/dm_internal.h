@@ -194,8 +194,8 @@ constexpr int kMaxCtas = 1024;
 constexpr int kCntRouter = 0;
 constexpr int kCntHead = 1;
 constexpr int kCntAttnBase = 8;   // + kv head (< 32)
-constexpr int kCntGdnSync = 40;   // 2 words: arrivals / exits of the fused GDN core + out kernel
-constexpr int kCntMoeSync = 48;   // 4 words of grid-wide counters of the fused MoE kernel
+constexpr int kCntGdnSync = 40;   // 2 words: u64 grid-barrier arrivals of the fused GDN core + out kernel
+constexpr int kCntMoeSync = 48;   // 2 words: u64 up-phase arrivals of the fused MoE kernel (2 spare)
 constexpr int kCntMoeFlag = 56;   // 8 words (4 x u64, 8-byte aligned) of released id words
 
 struct Ctx;  // host-side context (dm_api.cu)

@@ -296,19 +296,6 @@ struct MoeFusedArgs {
 DM_DEV void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-DM_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-DM_DEV unsigned long long ld_relaxed_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-DM_DEV void red_release_add_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
 DM_DEV unsigned ld_relaxed_u32(const unsigned* p) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -336,18 +323,6 @@ DM_DEV float poll_logit(const float* p, uint32_t* err) {
     }
 }
 
-// Bounded wait until *p >= target (64-bit counter); false on timeout.
-DM_DEV bool spin_geq_u64(const unsigned long long* p, unsigned long long target, uint32_t* err) {
-    if (ld_acquire_u64(p) >= target) return true;
-    const uint64_t t0 = globaltimer_ns();
-    for (uint32_t n = 1;; ++n) {
-        if (ld_acquire_u64(p) >= target) return true;
-        if (n % 256 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
-            raise_error(err, DM_DEVERR_TIMEOUT);
-            return false;
-        }
-    }
-}
 
 // Bounded wait until bit 63 of *p equals tag; returns the word.
 DM_DEV unsigned long long spin_marker(const unsigned long long* p, unsigned tag, uint32_t* err) {
