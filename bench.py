@@ -257,7 +257,11 @@ def step_timeline(eng, steps: int):
               "moe_topk_round_cycles": int(ph[60]),
               "attn_pages": [round((int(v) - int(ph[0])) / 1e3, 2) if v else None for v in ph[40:56]],
               "moe_cta0": [round((int(v) - int(ph[16])) / 1e3, 2) if v else None for v in ph[16:25]],
-              "moe_last_cta": [round((int(v) - int(ph[26])) / 1e3, 2) if v else None for v in ph[26:35]]}
+              "moe_last_cta": [round((int(v) - int(ph[26])) / 1e3, 2) if v else None for v in ph[26:35]],
+              # fused GDN kernel of the last GDN layer: start, ready, recurrence done, barrier
+              # passed, head norm done, out-projection rows landed, end (CTA 0; latest CTA)
+              "gdn_cta0": [round((int(v) - int(ph[2208])) / 1e3, 2) if v else None for v in ph[2208:2215]],
+              "gdn_latest": [round((int(v) - int(ph[2208])) / 1e3, 2) if v else None for v in ph[2216:2223]]}
     mc = ph[1024:1024 + 8 * 148].reshape(-1, 8)
     mc = mc[mc[:, 0] != 0]
     if len(mc):  # fused MoE of the last layer, per CTA (start-relative): quantiles and the slowest

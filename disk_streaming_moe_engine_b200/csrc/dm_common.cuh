@@ -173,8 +173,10 @@ DM_DEV bool spin_geq(const unsigned* p, unsigned target, uint32_t* err) {
 // layout: every chunk is a multiple of 16 bytes and every base is 256-byte aligned).
 // DM_L2_HINT=1 builds the weight and KV streams (read once per step, far more bytes than
 // the L2 holds) with an L2 evict-first policy.  Measured in the decode step: 0.3 % slower
-// than plain loads on the same box (the kernel code that the hint was meant to keep hot
-// is lost from the SM's own instruction caches, not from the L2), so it is off.
+// than plain loads on the same box, and again with the generation-tagged MoE flags and
+// the later MoE trigger: 580.4 vs 579.9 tok/s (noise).  The kernel code that the hint was
+// meant to keep hot is lost from the SM's own instruction caches, not from the L2, so it
+// is off.
 #ifndef DM_L2_HINT
 #define DM_L2_HINT 0
 #endif

@@ -228,10 +228,21 @@ struct GdnFusedArgs {
     float* x_mid;           // [H]
     int H, rmax;
     unsigned long long* arrivals;  // grid-barrier arrivals of every launch so far (never reset)
+    uint64_t* trace;        // phase stamps: [0..7] CTA 0, [8..15] latest over the CTAs; or null
     uint32_t* err;
 };
 
 constexpr int kGfThreads = 512;
+
+// Phase k of the fused GDN kernel reached by this CTA (thread 0): CTA 0's time in slot k,
+// the latest CTA's in slot 8 + k.  Phases: 0 start, 1 wait released, 2 recurrence done,
+// 3 grid barrier passed, 4 head norm done, 5 out-projection rows landed, 6 end.
+DM_DEV void gdn_stamp(uint64_t* tr, int k) {
+    if (tr == nullptr || threadIdx.x != 0) return;
+    const unsigned long long t = globaltimer_ns();
+    if (blockIdx.x == 0) tr[k] = t;
+    atomicMax(reinterpret_cast<unsigned long long*>(tr + 8 + k), t);
+}
 
 template <int DK>
 __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __grid_constant__ GdnFusedArgs f) {
@@ -253,6 +264,7 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
     uint8_t* wsm = gsm;                                                       // [rmax][KO] bf16
     float* xs = reinterpret_cast<float*>(gsm + static_cast<size_t>(f.rmax) * KO * 2);  // [KO]
     kt_start(a.kt);
+    gdn_stamp(f.trace, 0);
 
     if (tid == 0) {
         mbar_init(&wbar, 1);
@@ -286,6 +298,7 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
     }
     pdl_wait();
     kt_ready(a.kt);
+    gdn_stamp(f.trace, 1);
     // launch generation: the arrival count (grown by G per launch, never reset) read before
     // this CTA arrives, when fewer than G arrivals of this launch can have happened
     if (tid == 0) s_gen = ld_relaxed_u64(f.arrivals) / static_cast<unsigned long long>(G);
@@ -349,6 +362,7 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
         }
     }
     __syncthreads();
+    gdn_stamp(f.trace, 2);
     pdl_launch_dependents();
     if (tid == 0) {
         const unsigned long long target = (s_gen + 1) * static_cast<unsigned long long>(G);
@@ -357,36 +371,55 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
         spin_geq_u64(f.arrivals, target, f.err);
     }
     __syncthreads();
+    gdn_stamp(f.trace, 3);
 
-    // ---- phase 2: head RMSNorm * w * SiLU(z) of the whole o (each warp a head at a time;
-    // dv <= 128, one batch of loads per head), then this CTA's rows ----
+    // ---- phase 2: head RMSNorm * w * SiLU(z) of the whole o (dv <= 128).  Warp w takes
+    // heads w and w + 16 and issues the loads of both before reducing either, so the
+    // phase waits for one L2 round trip, not two ----
     float* xlo = xs;
     float* xhi = xs + KO / 2;
-    for (int hh = warp; hh < a.nv; hh += kGfThreads / 32) {
-        float ov[4], zv[4], wv[4];
+    constexpr int NW = kGfThreads / 32;
+    for (int hh0 = warp; hh0 < a.nv; hh0 += 2 * NW) {
+        float ov[2][4], zv[2][4], wv[4];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int hh = hh0 + u * NW;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int d = lane + 32 * i;
+                const bool on = d < DV && hh < a.nv;
+                ov[u][i] = on ? __ldcg(a.o + hh * DV + d) : 0.0f;
+                zv[u][i] = on ? __ldcg(f.z + hh * DV + d) : 0.0f;
+            }
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int d = lane + 32 * i;
-            ov[i] = d < DV ? __ldcg(a.o + hh * DV + d) : 0.0f;
-            zv[i] = d < DV ? __ldcg(f.z + hh * DV + d) : 0.0f;
             wv[i] = d < DV ? bf16_to_f32(f.gnorm[d]) : 0.0f;
         }
-        float acc = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc = fmaf(ov[i], ov[i], acc);
-        acc = warp_sum(acc);
-        const float rs = 1.0f / sqrtf(acc / static_cast<float>(DV) + a.eps);
+        for (int u = 0; u < 2; ++u) {
+            const int hh = hh0 + u * NW;
+            if (hh >= a.nv) break;
+            float acc = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int d = lane + 32 * i;
-            if (d < DV) {
-                const int k = hh * DV + d;  // element 8j + e goes to (e < 4 ? xlo : xhi)[4j + e % 4]
-                (((k & 7) < 4) ? xlo : xhi)[(k >> 3) * 4 + (k & 3)] = ov[i] * rs * wv[i] * zv[i];
+            for (int i = 0; i < 4; ++i) acc = fmaf(ov[u][i], ov[u][i], acc);
+            acc = warp_sum(acc);
+            const float rs = 1.0f / sqrtf(acc / static_cast<float>(DV) + a.eps);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int d = lane + 32 * i;
+                if (d < DV) {
+                    const int k = hh * DV + d;  // element 8j + e goes to (e < 4 ? xlo : xhi)[4j + e % 4]
+                    (((k & 7) < 4) ? xlo : xhi)[(k >> 3) * 4 + (k & 3)] = ov[u][i] * rs * wv[i] * zv[u][i];
+                }
             }
         }
     }
     __syncthreads();
+    gdn_stamp(f.trace, 4);
     const bool wok = mbar_wait_bounded(&wbar, 0, f.err, nullptr);
+    gdn_stamp(f.trace, 5);
     const float4* x4lo = reinterpret_cast<const float4*>(xlo);
     const float4* x4hi = reinterpret_cast<const float4*>(xhi);
     for (int r = warp; r < nr; r += kGfThreads / 32) {
@@ -408,6 +441,7 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
         if (lane == 0) f.x_mid[r0 + r] = f.x_res[r0 + r] + (wok ? acc : 0.0f);
     }
     __syncthreads();
+    gdn_stamp(f.trace, 6);
     kt_end(a.kt);  // nothing to reset: the barrier counter is generation-based
 }
 
@@ -460,6 +494,7 @@ cudaError_t launch_gdn_core_out(const LaunchCfg& lc, const Dims& d, const LayerW
     f.rmax = (d.H + G - 1) / G;
     f.arrivals = reinterpret_cast<unsigned long long*>(b.counters + kCntGdnSync);
     f.err = b.err;
+    f.trace = b.trace ? b.trace + kTrGdn : nullptr;
     const size_t smem = gdn_fused_smem(d, G);
     if (d.dk == 128) return launch_kernel(lc, gdn_core_out_kernel<128>, dim3(G), dim3(kGfThreads), smem, f);
     return launch_kernel(lc, gdn_core_out_kernel<64>, dim3(G), dim3(kGfThreads), smem, f);

@@ -188,6 +188,7 @@ constexpr int kTrMoeCtaSlots = 8; // start, ready, ids known, up data in, up don
 // trace slot bases per kernel kind
 constexpr int kTrAttn = 0;   // 8 stamps
 constexpr int kTrMoe = 16;   // 16 stamps
+constexpr int kTrGdn = 2208; // fused GDN kernel: 8 stamps of CTA 0, 8 latest over the CTAs
 
 constexpr int kMaxCtas = 1024;
 // counter slots
