@@ -262,8 +262,9 @@ bool moe_supported(int H, int I, int G) {
 //   phase 2   : gate/up GEMVs, h = SiLU(g) * u to global; grid barrier (arrivals on a
 //               64-bit counter that is never reset: the target is the launch generation
 //               read at the start, plus one, times the grid).
-//   phase 3   : CTAs 0..H/16-1 reduce their 16 output rows over all experts (two warp
-//               groups split the experts, combined in a fixed order) + residual.
+//   phase 3   : CTAs 0..H/16-1 produce their 16 output rows, one warp per row over all
+//               experts (even and odd experts in two accumulators, added in a fixed
+//               order) + residual.
 //   exit      : nothing to reset (generation-tagged flags; the router logit slots are
 //               emptied by CTA 0 once read), so the grid ends as its last rows are stored.
 struct MoeFusedArgs {
