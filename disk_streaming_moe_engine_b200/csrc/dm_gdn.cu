@@ -422,11 +422,18 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
     gdn_stamp(f.trace, 5);
     const float4* x4lo = reinterpret_cast<const float4*>(xlo);
     const float4* x4hi = reinterpret_cast<const float4*>(xhi);
-    for (int r = warp; r < nr; r += kGfThreads / 32) {
+    // warp w takes rows w and w + RH (RH = ceil(nr / 2)), so each activation vector read
+    // from shared memory serves two rows (the phase is bound by shared-memory reads)
+    const int RH = (nr + 1) / 2;
+    for (int r = warp; r < RH; r += kGfThreads / 32) {
+        const int r2 = r + RH;
+        const bool two = r2 < nr;
         const uint4* wr = reinterpret_cast<const uint4*>(wsm + static_cast<size_t>(r) * KO * 2);
-        float s0 = 0.0f, s1 = 0.0f;
+        const uint4* wr2 = reinterpret_cast<const uint4*>(wsm + static_cast<size_t>(two ? r2 : r) * KO * 2);
+        float s0 = 0.0f, s1 = 0.0f, t0 = 0.0f, t1 = 0.0f;
         for (int j = lane; j < KO / 8; j += 32) {
             const uint4 w = wr[j];
+            const uint4 v = two ? wr2[j] : make_uint4(0u, 0u, 0u, 0u);
             const float4 lo = x4lo[j], hi = x4hi[j];
             s0 = fmaf(bf16lo(w.x), lo.x, s0);
             s1 = fmaf(bf16hi(w.x), lo.y, s1);
@@ -436,9 +443,21 @@ __global__ void __launch_bounds__(kGfThreads, 1) gdn_core_out_kernel(const __gri
             s1 = fmaf(bf16hi(w.z), hi.y, s1);
             s0 = fmaf(bf16lo(w.w), hi.z, s0);
             s1 = fmaf(bf16hi(w.w), hi.w, s1);
+            t0 = fmaf(bf16lo(v.x), lo.x, t0);
+            t1 = fmaf(bf16hi(v.x), lo.y, t1);
+            t0 = fmaf(bf16lo(v.y), lo.z, t0);
+            t1 = fmaf(bf16hi(v.y), lo.w, t1);
+            t0 = fmaf(bf16lo(v.z), hi.x, t0);
+            t1 = fmaf(bf16hi(v.z), hi.y, t1);
+            t0 = fmaf(bf16lo(v.w), hi.z, t0);
+            t1 = fmaf(bf16hi(v.w), hi.w, t1);
         }
         const float acc = warp_sum(s0 + s1);
-        if (lane == 0) f.x_mid[r0 + r] = f.x_res[r0 + r] + (wok ? acc : 0.0f);
+        const float acc2 = warp_sum(t0 + t1);
+        if (lane == 0) {
+            f.x_mid[r0 + r] = f.x_res[r0 + r] + (wok ? acc : 0.0f);
+            if (two) f.x_mid[r0 + r2] = f.x_res[r0 + r2] + (wok ? acc2 : 0.0f);
+        }
     }
     __syncthreads();
     gdn_stamp(f.trace, 6);
