@@ -189,6 +189,9 @@ def cpu_sample(cfg_full, seed: int, ctx_len: int, steps: int):
 
     import oracle
     from disk_streaming_moe_engine_b200 import synth
+    # every CPU this process may run on: torchrun sets OMP_NUM_THREADS=1 for its ranks,
+    # which would otherwise time the CPU restatement on one thread
+    oracle.set_threads(max(1, len(os.sched_getaffinity(0))))
     cyc = dataclasses.replace(cfg_full, num_hidden_layers=4)
     m = synth.synth_model(cyc, seed)
     om = oracle.OracleModel(m)
