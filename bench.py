@@ -20,12 +20,17 @@ context length only, and this keeps the run short enough for an ncu launch list;
            flush with CUDA events on the library stream, against MEASURED_PEAKS.json;
            `kernels` lists the same figure for every kernel kind.
 
-Multi-GPU (torchrun, one process per GPU): batch-1 decode does not shard; every rank runs
-its own replica (scaling "weak"); value = total tokens of all ranks / max-over-ranks time.
+Workload selection: a plain `python bench.py [--gpus 1]` runs config 2 (batch-1 decode on
+one GPU).  Under torchrun (any world size, 1 included) or with --gpus > 1 the default is
+config 3 (`bench_batch.py`): batched decode of 64 sequences x 32768 cached tokens, expert
+parallel over the ranks (scaling "strong": the 64 sequences and 256 experts are split over
+the GPUs; value = 64 K / max-over-ranks time).  `--workload c2` under torchrun runs bs1
+replicas instead (batch-1 decode does not shard; scaling "weak").
 
 `--impl reference` times the CPU restatement of the reference engine (oracle/liboracle.so,
-all host threads) on a bounded sample of the same workload; the reference Mojo engine
-cannot be built here.
+all host threads, weights from the oracle's own copy of the seeded generator) on the same
+workload: W untimed then K timed real 40-block decode tokens of one sequence at the
+workload's context length (K capped at 64); the reference Mojo engine cannot be built here.
 """
 from __future__ import annotations
 
@@ -57,12 +62,14 @@ def parse():
     ap.add_argument("--context", default="synthetic", choices=["synthetic", "prefill"])
     ap.add_argument("--seed", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-sample-steps", type=int, default=2)
+    ap.add_argument("--cpu-sample-steps", type=int, default=3,
+                    help="real 40-block CPU tokens timed for the cpu_baseline key (median)")
     ap.add_argument("--timeline", default="", help="also trace one decode step; write its launch timeline here")
-    ap.add_argument("--workload", default="c2", choices=["c2", "c3", "spill"],
-                    help="c2: bs1 decode (BASELINE config 2); c3: batched decode of 64 sequences at 32768 "
-                         "cached tokens each (config 3); spill: bs1 decode with the expert pool spilled to host "
-                         "memory (--expert-slots per layer in HBM)")
+    ap.add_argument("--workload", default=None, choices=["c2", "c3", "spill"],
+                    help="c2: bs1 decode (BASELINE config 2; default of a plain run); c3: batched decode of 64 "
+                         "sequences at 32768 cached tokens each (config 3; default under torchrun or with "
+                         "--gpus > 1); spill: bs1 decode with the expert pool spilled to host memory "
+                         "(--expert-slots per layer in HBM)")
     ap.add_argument("--expert-slots", type=int, default=64, help="spill: routed expert records per layer in HBM")
     ap.add_argument("--batch", type=int, default=64, help="c3: sequences per step")
     ap.add_argument("--c3-ctx", type=int, default=32768, help="c3: cached tokens per sequence")
@@ -74,6 +81,15 @@ def parse():
 def dist_env():
     return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
             int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def resolve_workload(args, world: int) -> str:
+    """Config 2 for a plain single-process run; config 3 (the expert-parallel batched step
+    whose 1 -> 8 GPU curve the scaling target is set on) under torchrun or on several GPUs."""
+    if args.workload:
+        return args.workload
+    under_torchrun = "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_WORLD_SIZE" in os.environ
+    return "c3" if (under_torchrun or world > 1 or args.gpus > 1) else "c2"
 
 
 # ---- multi-rank timing (one process per GPU) ---------------------------------------------
@@ -182,49 +198,47 @@ def profiled_traffic(name: str):
 
 
 # ---- CPU baseline: the oracle port on host cores ----------------------------------------
-def cpu_sample(cfg_full, seed: int, ctx_len: int, steps: int):
-    """Times one [GDN, GDN, GDN, GatedAttn] cycle at full shape and the lm_head on the host
-    (all OpenMP threads); a 40-block token costs 10 cycles + 1 head."""
-    import dataclasses
-
+def cpu_decode_tokens(cfg, seed: int, ctx_len: int, tokens: int, warmup: int = 1):
+    """Real 40-block decode tokens of one sequence through the CPU restatement of the
+    reference decode step (oracle/liboracle.so, OpenMP over every CPU this process may run
+    on), at `ctx_len` cached tokens: bf16 N(0, 1) K/V in every attention layer, fp32
+    N(0, 0.05) GDN states and conv windows.  The weights come from the oracle's copy of the
+    seeded generator, so the CUDA library is never loaded.  Returns the per-token seconds
+    of the `tokens` timed steps (after `warmup` untimed ones) and the thread count."""
     import oracle
     from disk_streaming_moe_engine_b200 import synth
-    # every CPU this process may run on: torchrun sets OMP_NUM_THREADS=1 for its ranks,
-    # which would otherwise time the CPU restatement on one thread
+    # torchrun sets OMP_NUM_THREADS=1 for its ranks, which would otherwise time the CPU
+    # restatement on one thread
     oracle.set_threads(max(1, len(os.sched_getaffinity(0))))
-    cyc = dataclasses.replace(cfg_full, num_hidden_layers=4)
-    m = synth.synth_model(cyc, seed)
+    m = synth.synth_model(cfg, seed, lib=oracle.SynthLib())
     om = oracle.OracleModel(m)
-    st = oracle.OracleState(cyc, ctx_len + steps + 4)
+    st = oracle.OracleState(cfg, ctx_len + warmup + tokens + 1)
     rng = np.random.default_rng(seed)
-    kv = rng.standard_normal(st.k[0, :ctx_len].shape).astype(np.float32)
-    st.k[0, :ctx_len] = synth.f32_to_bf16(kv)
-    st.v[0, :ctx_len] = synth.f32_to_bf16(kv[::-1].copy())
+    for a in range(cfg.num_attention_layers()):
+        st.k[a, :ctx_len] = synth.f32_to_bf16(rng.standard_normal(st.k[a, :ctx_len].shape, dtype=np.float32))
+        st.v[a, :ctx_len] = synth.f32_to_bf16(rng.standard_normal(st.v[a, :ctx_len].shape, dtype=np.float32))
+    st.S[:] = rng.standard_normal(st.S.shape, dtype=np.float32) * np.float32(0.05)
+    st.conv[:] = rng.standard_normal(st.conv.shape, dtype=np.float32) * np.float32(0.05)
     st.st.len = ctx_len
-    lib = oracle.load()
-    x = np.zeros(cyc.hidden_size, np.float32)
-    y = np.zeros_like(x)
-    logits = np.empty(cyc.vocab_size, np.float32)
-    t_cycle, t_head = [], []
-    for i in range(steps + 1):
-        x[:] = synth.bf16_to_f32(m["embed"][(7 * i) % cyc.vocab_size])
+    tok = int(rng.integers(0, cfg.vocab_size))
+    times = []
+    for i in range(warmup + tokens):
         t0 = time.perf_counter()
-        for l in range(4):
-            lib.or_block_forward(oracle.C.byref(om.model), oracle.C.byref(st.st), l, x.ctypes.data, y.ctypes.data,
-                                 None)
-            x[:] = y
-        t1 = time.perf_counter()
-        lib.or_head(oracle.C.byref(om.model), x.ctypes.data, logits.ctypes.data)
-        t2 = time.perf_counter()
-        st.st.len += 1
-        if i > 0:  # the first iteration warms caches
-            t_cycle.append(t1 - t0)
-            t_head.append(t2 - t1)
-    tc = statistics.median(t_cycle)
-    th = statistics.median(t_head)
-    per_token = 10 * tc + th
-    return {"per_token_s": per_token, "cycle_s": tc, "head_s": th, "cores": oracle.get_threads(),
-            "steps": steps}
+        tok, _, _ = oracle.decode_step(om, st, tok)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    return times, oracle.get_threads()
+
+
+def cpu_baseline_line(cfg, seed: int, ctx_len: int, tokens: int) -> dict:
+    """The cpu_baseline key of our arm: median of `tokens` real CPU decode tokens."""
+    from disk_streaming_moe_engine_b200 import build
+    build.build_oracle()
+    times, cores = cpu_decode_tokens(cfg, seed, ctx_len, max(3, tokens), 1)
+    med = statistics.median(times)
+    return {"value": 1.0 / med, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"oracle/liboracle.so on host cores: median of {len(times)} real 40-block decode tokens of "
+                      f"one sequence at {ctx_len} cached tokens (after 1 untimed)"}
 
 
 def step_timeline(eng, steps: int):
@@ -311,30 +325,56 @@ def synthetic_context(eng, cfg, n: int, seed: int) -> int:
     return int(rng.integers(0, cfg.vocab_size))
 
 
+REF_MAX_STEPS = 64
+
+
 def run_reference(args, rank, world):
+    """The reference arm: the CPU restatement of the reference decode step on this box's
+    host cores, on the same workload, metric and config as our arm (rank 0 only)."""
     if rank != 0:
         return 0
     from disk_streaming_moe_engine_b200 import build, preset
+    from disk_streaming_moe_engine_b200.bench_batch import c3_config, c3_metric
     build.build_oracle()
     cfg = preset("full")
-    k = max(1, min(args.steps, 8))
-    s = cpu_sample(cfg, args.seed, args.prompt_len, k)
-    tps = 1.0 / s["per_token_s"]
+    wl = resolve_workload(args, world)
+    k = max(1, min(args.steps, REF_MAX_STEPS))
+    w = max(0, min(args.warmup, 8))
+    if wl == "c3":
+        ctx, seed, metric, scaling = args.c3_ctx, 3, c3_metric(args.batch), "strong"
+        config = c3_config(args, world, cfg)
+    else:
+        ctx, seed, metric, scaling = args.prompt_len, args.seed, C2_METRIC, "weak"
+        config = c2_config(args, world)
+    times, cores = cpu_decode_tokens(cfg, seed, ctx, k, w)
+    total = sum(times)
+    tps = k / total
     line = {
-        "impl": "reference", "metric": "decode tok/s, 35B-A3B-shape 4-bit, bs1", "value": tps, "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": s["steps"], "warmup": 1, "ms_per_step": s["per_token_s"] * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit experts, bs1, ctx 4096",
-                   "global_batch": 1, "seq_len": args.prompt_len, "parallelism": "host threads"},
-        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": s["cores"], "kind": "port",
-                         "sample": f"CPU restatement (oracle/liboracle.so) of the reference decode step: one "
-                                   f"[GDN,GDN,GDN,Attn] cycle at full shape + lm_head, median of {s['steps']} "
-                                   f"tokens at ctx {args.prompt_len}; token time = 10 x cycle + head "
-                                   f"(cycle {s['cycle_s']*1e3:.1f} ms, head {s['head_s']*1e3:.1f} ms)"},
+        "impl": "reference", "metric": metric, "value": tps, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": k, "warmup": w, "ms_per_step": total / k * 1e3,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config,
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"CPU restatement (oracle/liboracle.so) of the reference decode step: {k} real "
+                                   f"40-block tokens of one sequence at {ctx} cached tokens after {w} untimed "
+                                   f"(the reference decodes one sequence per process); median token "
+                                   f"{statistics.median(times) * 1e3:.0f} ms"},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+C2_METRIC = "decode tok/s, 35B-A3B-shape 4-bit, bs1"
+
+
+def c2_config(args, world: int) -> dict:
+    """The config object of a config-2 line (both arms of bench.py print the same one)."""
+    return {"workload": "config2: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit g64 experts, bs1",
+            "global_batch": world, "seq_len": args.prompt_len, "parallelism": f"replicas x{world}",
+            "context": ("synthetic KV pages + GDN state imported" if args.context == "synthetic"
+                        else "random prompt prefilled through the decode graph"),
+            "l2": "inputs larger than L2 (4 GB of weights per step)"}
 
 
 def run_ours(args, rank, local, world):
@@ -423,11 +463,7 @@ def run_ours(args, rank, local, world):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        build.build_oracle()
-        s = cpu_sample(cfg, args.seed, args.prompt_len, args.cpu_sample_steps)
-        cpu = {"value": 1.0 / s["per_token_s"], "unit": "tokens/s", "cores": s["cores"], "kind": "port",
-               "sample": f"oracle/liboracle.so on host cores: one full-shape [GDN,GDN,GDN,Attn] cycle + lm_head, "
-                         f"median of {s['steps']} tokens at ctx {args.prompt_len}; token = 10 x cycle + head"}
+        cpu = cpu_baseline_line(cfg, args.seed, args.prompt_len, args.cpu_sample_steps)
 
     timeline = None
     moe_in_step = None
@@ -449,15 +485,11 @@ def run_ours(args, rank, local, world):
     kps = eng.kernels_per_step()
     c = clocks.summary()
     line = {
-        "metric": "decode tok/s, 35B-A3B-shape 4-bit, bs1", "value": value, "unit": "tokens/s",
+        "metric": C2_METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights on device, seed 2)",
-        "config": {"workload": "config2: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit g64 experts, bs1",
-                   "global_batch": world, "seq_len": args.prompt_len, "parallelism": f"replicas x{world}",
-                   "context": ("synthetic KV pages + GDN state imported" if args.context == "synthetic"
-                               else "random prompt prefilled through the decode graph"),
-                   "l2": "inputs larger than L2 (4 GB of weights per step)"},
+        "config": c2_config(args, world),
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_source": peak_kind,
@@ -488,6 +520,7 @@ def main():
     rank, local, world = dist_env()
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    args.workload = resolve_workload(args, world)
     if args.workload == "c3":
         from disk_streaming_moe_engine_b200 import bench_batch
         return bench_batch.run(args, rank, local, world)

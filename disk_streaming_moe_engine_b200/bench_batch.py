@@ -58,6 +58,29 @@ def calibrate_offsets(E: int, k: int, s: float, seed: int, samples: int = 8192, 
     return b.astype(np.float32)
 
 
+def c3_metric(B: int) -> str:
+    return f"decode tok/s, 35B-A3B-shape 4-bit, bs{B}"
+
+
+def c3_workload(B: int, L: int) -> str:
+    return (f"config3: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit g64 experts, {B} sequences x {L} cached "
+            "tokens, paged (16-token pages, permuted pool)")
+
+
+def c3_config(args, world: int, cfg) -> dict:
+    """The config object of a config-3 line (both arms of bench.py print the same one)."""
+    B, L = args.batch, args.c3_ctx
+    skew = None
+    if args.router_skew > 0:
+        b = calibrate_offsets(cfg.num_experts, cfg.num_experts_per_tok, args.router_skew, 3)
+        skew = {"zipf_s": args.router_skew, "offset_range": [float(b.min()), float(b.max())]}
+    return {"workload": c3_workload(B, L), "global_batch": B, "seq_len": L,
+            "parallelism": "1 GPU" if world == 1 else
+            f"expert-parallel x{world}: {B // world} sequences and {cfg.num_experts // world} experts per GPU, "
+            "dense weights replicated, dispatch/combine through peer memory",
+            "l2": "inputs larger than L2 (tens of GB of KV per step)", "router_skew": skew}
+
+
 def apply_router_skew(eng, cfg, s: float, seed: int) -> dict:
     E, k = cfg.num_experts, cfg.num_experts_per_tok
     b = calibrate_offsets(E, k, s, seed)
@@ -93,7 +116,7 @@ def run(args, rank, local, world):
     import torch
 
     from . import Engine, RuntimeConfig, _lib, build, ep, preset
-    from bench import ClockSampler, measured_peak  # noqa: the repo root is on sys.path (bench.py)
+    from bench import ClockSampler, cpu_baseline_line, measured_peak  # noqa: the repo root is on sys.path
 
     build.build()
     torch.cuda.set_device(local)
@@ -193,35 +216,33 @@ def run(args, rank, local, world):
     own, gemms = eng.batch_kernels_per_step(n)
     if world > 1:
         own += cfg.num_hidden_layers  # the cross-rank barrier kernel of every MoE layer
+    if dist is not None:
+        barrier()
+        eng.ep_detach()
+    eng.close()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_line(cfg, 3, L, args.cpu_sample_steps)
     line = {
-        "metric": "decode tok/s, 35B-A3B-shape 4-bit, bs64", "value": value, "unit": "tokens/s",
+        "metric": c3_metric(B), "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": ms / K, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init weights and sequence state on device, seed 3)",
-        "config": {"workload": f"config3: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit g64 experts, {B} sequences "
-                               f"x {L} cached tokens, paged (16-token pages, permuted pool)",
-                   "global_batch": B, "seq_len": L,
-                   "parallelism": "1 GPU" if world == 1 else
-                   f"expert-parallel x{world}: {n} sequences and {cfg.num_experts // world} experts per GPU, "
-                   "dense weights replicated, dispatch/combine through peer memory",
-                   "l2": "inputs larger than L2 (tens of GB of KV per step)",
-                   "router_skew": skew},
+        "config": c3_config(args, world, cfg),
         "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 8 * B, "d2h_bytes_per_step": 4 * B + 4 * world},
         "roofline": roofline,
         "step_roofline": {"bytes_per_step_per_gpu": sb, "achieved_GBps_per_gpu": sb["total"] / (ms / K / 1e3) / 1e9,
                           "frac": sb["total"] / (ms / K / 1e3) / 1e9 / peak},
         "kernels": kernels,
+        "cpu_baseline": cpu,
         "routing": routing,
         "clocks": clocks.summary(),
         "clocks_e2e": clocks_e2e.summary(),
         "gpu_launches": own * K,
         "library_gemms": gemms * K,
         "context_setup_s": round(setup_s, 2),
+        "router_skew_applied": skew,
     }
-    if dist is not None:
-        barrier()
-        eng.ep_detach()
-    eng.close()
     if dist is not None:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()

@@ -116,10 +116,7 @@ struct dm_ctx {
     float* rbias = nullptr;                // [L][E] router logit offsets (dm_set_router_bias)
     // expert-parallel group: the peers' arenas mapped into this process (null for self)
     std::vector<uint8_t*> peer_arena;
-    bool use_pdl = true;       // programmatic dependent launch between step kernels
-    bool gdn_fused = true;     // GDN recurrence + output projection as one kernel
-    bool l2_prefetch = false;  // latency-bound kernels prefetch upcoming weights into L2 (off:
-                               // measured slower, the prefetch competes with the step's reads)
+    bool gdn_fused = false;  // the fused GDN kernel's grid fits one CTA per SM (set at creation)
     uint64_t* trace_buf = nullptr;
     uint64_t* ktrace_buf = nullptr;
     uint8_t* flush_buf = nullptr;  // L2 flush target of dm_time_kernel (allocated on first use)
@@ -462,7 +459,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
 }
 
 static LaunchCfg lcfg(const dm_ctx* c) {
-    return LaunchCfg{c->stream, c->num_sms, c->use_pdl, nullptr, c->l2_prefetch};
+    return LaunchCfg{c->stream, c->num_sms, true, nullptr};
 }
 
 // Launch config for the next kernel of a traced sequence (timeline record n of kind k).
@@ -639,12 +636,6 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
         return DM_ERR_INVALID_ARG;
     }
     dm_ctx* c = new dm_ctx();
-    // tuning knobs (environment, read once): DISMOEN_PDL=0 launches every kernel without
-    // programmatic dependent launch; DISMOEN_L2_PREFETCH=1 enables the L2 prefetch of
-    // upcoming weights by the latency-bound kernels
-    if (const char* v = getenv("DISMOEN_PDL")) c->use_pdl = atoi(v) != 0;
-    if (const char* v = getenv("DISMOEN_GDN_FUSED")) c->gdn_fused = atoi(v) != 0;
-    if (const char* v = getenv("DISMOEN_L2_PREFETCH")) c->l2_prefetch = atoi(v) != 0;
     c->mc = *model;
     c->rc = *rt;
     c->d = make_dims(*model, *rt);
@@ -660,10 +651,19 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     // per-context value that a later, smaller context would lower
     if (e == cudaSuccess) e = attn_set_attrs(kAttnMaxScoreSmem);
     if (e == cudaSuccess) e = batch_set_attrs();
+    bool moe_fits = false;
+    if (e == cudaSuccess) e = moe_fused_fits(c->d, c->num_sms, &moe_fits);
+    if (e == cudaSuccess) c->gdn_fused = gdn_fused_fits(c->d, c->num_sms);
     if (e != cudaSuccess) {
         fprintf(stderr, "dm_ctx_create: %s\n", cudaGetErrorString(e));
         delete c;
         return DM_ERR_CUDA;
+    }
+    if (!moe_fits) {
+        fprintf(stderr, "dm_ctx_create: the fused MoE kernel for hidden %d / intermediate %d cannot keep one CTA "
+                "resident on each of the %d SMs\n", c->d.H, c->d.I, c->num_sms);
+        delete c;
+        return DM_ERR_INVALID_ARG;
     }
     plan_memory(c, false);
     e = cudaMalloc(&c->arena, c->arena_bytes);
@@ -781,7 +781,7 @@ int32_t dm_get_stream(dm_ctx* c, void** s) {
     return DM_OK;
 }
 
-static bool gdn_fused_on(const dm_ctx* c) { return c->gdn_fused && gdn_fused_supported(c->d, c->num_sms); }
+static bool gdn_fused_on(const dm_ctx* c) { return c->gdn_fused; }
 
 int32_t dm_kernels_per_step(dm_ctx* c, int32_t* out) {
     if (!c || !out) return DM_ERR_INVALID_ARG;
@@ -1877,15 +1877,7 @@ static cudaError_t enqueue_mixer(dm_ctx* c, int layer, int slot) {
 
 static cudaError_t enqueue_moe(dm_ctx* c, int layer, int slot) {
     const LayerW& w = c->layers[layer];
-    // the next layer's input projection is the next large stream: start it into L2
-    const void* next_w = nullptr;
-    size_t next_bytes = 0;
-    if (layer + 1 < c->d.L && c->l2_prefetch) {
-        const LayerW& nw = c->layers[layer + 1];
-        next_w = nw.w_in;
-        next_bytes = static_cast<size_t>(nw.is_attn ? c->d.attn_in_rows : c->d.gdn_in_rows) * c->d.H * 2;
-    }
-    return launch_moe_fused(lcfg_traced(c, TK_MOE, layer), c->d, w, c->b, slot, next_w, next_bytes);
+    return launch_moe_fused(lcfg_traced(c, TK_MOE, layer), c->d, w, c->b, slot);
 }
 
 static cudaError_t enqueue_step(dm_ctx* c, int slot) {

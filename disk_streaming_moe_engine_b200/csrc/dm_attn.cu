@@ -45,8 +45,6 @@ struct AttnArgs {
     uint64_t* trace;          // phase stamps (CTA (0, last split), thread 0) or null
     uint64_t* cta_trace;      // per-CTA stamps (kTrCtaSlots per CTA, thread 0) or null
     uint64_t* kt;             // launch timeline record or null
-    const void* next_w;       // o_proj weights, prefetched into L2
-    size_t next_bytes;
     uint32_t* err;
     // 2-D tiled view of the whole KV arena (all attention layers): columns D, rows
     // [att][page][K|V][Hkv][16]; boxes of 16 rows x 64 columns, 128-byte swizzle
@@ -313,7 +311,6 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     };
     if (warp == 0)
         for (int i = 0; i < np && i < kAttnStages; ++i) issue(i);
-    prefetch_l2_share(a.next_w, a.next_bytes, s * gridDim.x + g, gridDim.x * gridDim.y, tid);
     if (tid < GRP) {
         m_run[tid] = -INFINITY;
         l_run[tid] = 0.0f;
@@ -1106,8 +1103,6 @@ cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW&
     a.trace = b.trace ? b.trace + kTrAttn : nullptr;
     a.cta_trace = b.trace ? b.trace + kTrCta : nullptr;
     a.kt = lc.kt;
-    a.next_w = lc.l2_prefetch ? w.w_out : nullptr;
-    a.next_bytes = static_cast<size_t>(d.H) * d.Hq * d.D * 2;
     const dim3 grid(d.Hkv, a.nsplit);
     if (a.cta_trace && grid.x * grid.y * kTrCtaSlots > kTraceSlots - kTrCta) a.cta_trace = nullptr;
     return attn_launch(lc, d, a, grid);

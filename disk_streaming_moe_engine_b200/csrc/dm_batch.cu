@@ -458,7 +458,10 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
     const int world = a.ep.world, rank = a.ep.rank;
     int* sids = reinterpret_cast<int*>(lgw);  // [world][n][topk]
     pdl_wait();  // the router's last CTAs wrote this rank's ids
-    if (world > 1) ep_barrier(a.ep, a.my_flags, a.epoch, 0, a.err);
+    // a barrier that ran out leaves the peers' ids unpublished: the step then computes no
+    // expert work (the host reports DM_ERR_TIMEOUT from the error word)
+    bool ep_ok = true;
+    if (world > 1) ep_ok = ep_barrier(a.ep, a.my_flags, a.epoch, 0, a.err);
     else __syncthreads();
     pdl_launch_dependents();
 
@@ -525,7 +528,7 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
         atomicMax(a.stats + 2, s_maxcnt);
         atomicAdd(a.stats + 3, 1u);
         if (!pairs_ok) raise_error(a.err, DM_DEVERR_CAPACITY);
-        a.work[0] = pairs_ok ? total_segs : 0;
+        a.work[0] = (pairs_ok && ep_ok) ? total_segs : 0;
         a.work[1] = 0;
         a.work[2] = 0;
     }

@@ -31,8 +31,6 @@ struct GdnRecArgs {
     const int* pos;
     int nk, nv, qkv_dim;
     float eps;
-    const void* next_w;     // out_proj weights, prefetched into L2
-    size_t next_bytes;
     uint64_t* kt;
     // batched launch (grid.z = batch rows): row b works on sequence slots[b]; ring, S and
     // pos advance by the slot, ab and o by the row.  slots == nullptr: one sequence.
@@ -63,8 +61,6 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
     float* o_out = a.o + bz * a.o_bs;
 
     kt_start(a.kt);
-    prefetch_l2_share(a.next_w, a.next_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y,
-                      threadIdx.x);
     // ---- prologue: this CTA's state rows (4 per warp) into registers ----
     float* Sh = a.S + slot * a.S_ss + static_cast<size_t>(h) * DV * DK;
     float srow[4][CPL];
@@ -171,8 +167,6 @@ cudaError_t launch_gdn_rec(const LaunchCfg& lc, const Dims& d, const LayerW& w,
     a.nv = d.nv;
     a.qkv_dim = d.qkv_dim;
     a.eps = d.eps;
-    a.next_w = lc.l2_prefetch ? w.w_out : nullptr;
-    a.next_bytes = static_cast<size_t>(d.H) * d.z_dim * 2;
     a.kt = lc.kt;
     const dim3 grid(d.nv, d.dv / 16);
     if (d.dk == 128) return launch_kernel(lc, gdn_rec_kernel<128>, grid, dim3(128), 0, a);
@@ -483,6 +477,18 @@ cudaError_t gdn_set_attrs() {
         e = cudaFuncSetAttribute(gdn_core_out_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(kGdnFusedMaxSmem));
     return e;
+}
+
+// One CTA per SM with a grid-wide barrier between its phases: every CTA must fit on an SM
+// at once (queried once per context; the separate-kernel path is used otherwise).
+bool gdn_fused_fits(const Dims& d, int num_sms) {
+    if (!gdn_fused_supported(d, num_sms)) return false;
+    int per_sm = 0;
+    const size_t smem = gdn_fused_smem(d, num_sms);
+    const cudaError_t e = d.dk == 128
+        ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gdn_core_out_kernel<128>, kGfThreads, smem)
+        : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gdn_core_out_kernel<64>, kGfThreads, smem);
+    return e == cudaSuccess && per_sm >= 1;
 }
 
 cudaError_t launch_gdn_core_out(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot) {

@@ -263,31 +263,17 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __grid
 template <int K, int PRO>
 static cudaError_t launch_gemv_t(const LaunchCfg& lc, GemvArgs a) {
     a.kt = lc.kt;
-    // L2 look-ahead rows (environment DISMOEN_GEMV_PF, 0..8; default 1).  Lane 0 of every
-    // warp prefetches the row one grid stride ahead, before the wait too, so that during
-    // the predecessor's latency-bound tail (the MoE's top-k and id broadcast) each warp's
-    // second row is already on its way to L2.  Measured in the decode step: 0 rows 558.4,
-    // 1 row 566.6, 2 rows 558.7 tok/s (two rows crowd the MoE's routed-expert copies).
-    static const int pf = [] {
-        const char* v = getenv("DISMOEN_GEMV_PF");
-        const int n = v ? atoi(v) : 1;
-        return n < 0 ? 0 : (n > 8 ? 8 : n);
-    }();
-    a.pf = pf;
+    // L2 look-ahead: lane 0 of every warp prefetches the row one grid stride ahead, before
+    // the wait too, so that during the predecessor's latency-bound tail (the MoE's top-k
+    // and id broadcast) each warp's second row is already on its way to L2.  Measured in
+    // the decode step: 0 rows 558.4, 1 row 566.6, 2 rows 558.7 tok/s (two rows crowd the
+    // MoE's routed-expert copies).
+    a.pf = 1;
     const int want = (a.N + kGemvWarps - 1) / kGemvWarps;
-    // CTAs per SM (environment DISMOEN_GEMV_CTAS_PER_SM, 1 or 2; default 2: measured faster
-    // in the decode step although one CTA per SM leaves room for the next kernel's prologue)
-    static const int per_sm = [] {
-        const char* v = getenv("DISMOEN_GEMV_CTAS_PER_SM");
-        const int n = v ? atoi(v) : 2;
-        return n == 1 ? 1 : 2;
-    }();
-    static const int per_sm_wide = [] {  // K > 2048 (output projections); 0 = same as above
-        const char* v = getenv("DISMOEN_GEMV_CTAS_PER_SM_WIDE");
-        const int n = v ? atoi(v) : 0;
-        return (n == 1 || n == 2) ? n : 0;
-    }();
-    const int cap = lc.num_sms * ((K > 2048 && per_sm_wide) ? per_sm_wide : per_sm);
+    // two CTAs per SM: measured faster in the decode step than one, although one CTA per
+    // SM leaves room for the next kernel's prologue (588.0 vs 588.0 tok/s for the attention
+    // out-projection alone at one CTA per SM, slower for the input projections)
+    const int cap = lc.num_sms * 2;
     int grid = want < cap ? want : cap;
     if (a.counter && grid > kMaxCtas) grid = kMaxCtas;
     return launch_kernel(lc, gemv_bf16_kernel<K, PRO>, dim3(grid), dim3(kGemvThreads), 0, a);

@@ -206,7 +206,6 @@ struct LaunchCfg {
     int num_sms;
     bool pdl;
     uint64_t* kt;   // timeline record of this launch (start, inputs ready, end) or null
-    bool l2_prefetch = true;
 };
 
 // Timeline record kinds (dm_trace_timeline)
@@ -229,6 +228,8 @@ cudaError_t launch_gdn_core_out(const LaunchCfg& lc, const Dims& d, const LayerW
                                 const Buffers& b, int slot);
 bool gdn_fused_supported(const Dims& d, int num_sms);
 cudaError_t gdn_set_attrs();
+bool gdn_fused_fits(const Dims& d, int num_sms);
+cudaError_t moe_fused_fits(const Dims& d, int num_sms, bool* ok);
 cudaError_t launch_attn_in(const LaunchCfg& lc, const Dims& d, const LayerW& w,
                            const Buffers& b, int slot);
 cudaError_t launch_attn_decode(const LaunchCfg& lc, const Dims& d, const LayerW& w,
@@ -239,8 +240,7 @@ cudaError_t launch_attn_out(const LaunchCfg& lc, const Dims& d, const LayerW& w,
 cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
                           const Buffers& b, int slot, int normalise_input);
 // Whole MoE mixer of one layer (router, experts, residual) in one kernel; x_mid -> xres.
-cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot,
-                             const void* next_w = nullptr, size_t next_bytes = 0);
+cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot);
 cudaError_t launch_head(const LaunchCfg& lc, const Dims& d, const uint16_t* final_norm,
                         const uint16_t* lm_head, const Buffers& b, int slot, int advance,
                         int record_gen);

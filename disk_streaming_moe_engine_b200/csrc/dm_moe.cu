@@ -289,8 +289,6 @@ struct MoeFusedArgs {
     uint64_t* trace;          // phase stamps of CTA 0 and of the last CTA, or null
     uint64_t* cta_trace;      // per-CTA stamps (kTrMoeCtaSlots per CTA, thread 0) or null
     uint64_t* kt;             // launch timeline record or null
-    const void* next_w;
-    size_t next_bytes;
     uint32_t* err;
 };
 
@@ -389,7 +387,6 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     trace_stamp(ct, 0);
     kt_start(a.kt);
     // ---- pre-wait: nothing here depends on the previous kernel ----
-    prefetch_l2_share(a.next_w, a.next_bytes, c, nblk, tid);
     const int rrow = c * 16 + warp;
     const bool router_cta = c < R;
     uint4 wreg[VPL];
@@ -889,8 +886,7 @@ static cudaError_t launch_moe_fused_t(const LaunchCfg& lc, MoeFusedArgs a) {
     return launch_kernel(lc, moe_fused_kernel<K, KI, G>, dim3(grid), dim3(kMoeThreads), smem, a);
 }
 
-cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot,
-                             const void* next_w, size_t next_bytes) {
+cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot) {
     MoeFusedArgs a{};
     a.Wr = w.w_router;
     a.rbias = w.router_bias;
@@ -918,8 +914,6 @@ cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.trace = b.trace ? b.trace + kTrMoe : nullptr;
     a.cta_trace = b.trace ? b.trace + kTrMoeCta : nullptr;
     a.kt = lc.kt;
-    a.next_w = next_w;
-    a.next_bytes = next_bytes;
     a.err = b.err;
     if (d.G != 64) return cudaErrorInvalidValue;
     if (d.H == 2048 && d.I == 512) return launch_moe_fused_t<2048, 512, 64>(lc, a);
@@ -931,6 +925,33 @@ cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w
 }
 
 #define DM_MOE_INSTANCES(X) X(2048, 512) X(256, 128) X(1024, 256) X(2048, 256) X(4096, 512)
+
+template <int K, int KI, int G>
+static cudaError_t moe_fused_fits_t(const Dims& d, int num_sms, bool* ok) {
+    const int nexp = d.topk + 1;
+    const int up_slots = (nexp * d.gu_chunks + num_sms - 1) / num_sms;
+    *ok = false;
+    if (up_slots > kMoeMaxSlots || d.d_chunks > num_sms || (d.E + 16) / 16 > num_sms) return cudaSuccess;
+    int per_sm = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &per_sm, moe_fused_kernel<K, KI, G>, kMoeThreads, MoeFusedSmem<K, KI, G>::total(up_slots, nexp));
+    *ok = e == cudaSuccess && per_sm >= 1;
+    return e;
+}
+
+// The fused kernel runs one CTA per SM and its phases wait on each other across the
+// grid, so every CTA must be able to be resident at once: true when one CTA (with this
+// shape's shared memory) fits on an SM and the grid covers the work.  An unsupported
+// shape gives false.
+cudaError_t moe_fused_fits(const Dims& d, int num_sms, bool* ok) {
+    *ok = false;
+    if (d.G != 64) return cudaSuccess;
+#define DM_MOE_FITS(KK, II) \
+    if (d.H == KK && d.I == II) return moe_fused_fits_t<KK, II, 64>(d, num_sms, ok);
+    DM_MOE_INSTANCES(DM_MOE_FITS)
+#undef DM_MOE_FITS
+    return cudaSuccess;
+}
 
 cudaError_t moe_set_attrs() {
     cudaError_t e = cudaSuccess;

@@ -46,6 +46,10 @@ struct NoAllocDevice {
 };
 static NoAllocDevice g_dev[kMaxDevices];
 static std::mutex g_dev_mu;
+// Held for a whole call (enqueue through the final stream synchronisation): two threads of
+// one process never have this entry point's kernels in flight at once, since they would
+// share the scratch array.  Calls from other processes on the same device are not covered.
+static std::mutex g_call_mu;
 
 static int na_err(char* buf, uint64_t size, int code, const char* type, const char* fmt, ...) {
     if (buf && size > 0) {
@@ -127,8 +131,16 @@ extern "C" int32_t dm_moe_layer_noalloc(int32_t H, int32_t I, int32_t E, int32_t
     NoAllocDevice sd{};
     int rc = setup_device(dev, &sd, err_buf, err_buf_size);
     if (rc != DM_OK) return rc;
+    // the call waits for its stream at the end, which a capturing stream does not allow
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &cap);
+    if (e != cudaSuccess || cap != cudaStreamCaptureStatusNone)
+        return na_err(err_buf, err_buf_size, DM_ERR_INVALID_ARG, "INVALID_ARG",
+                      "the stream is being captured (or cannot be queried: %s); this call synchronises its stream",
+                      cudaGetErrorString(e));
 
     Dims d{};
+    d.max_seqs = 1;
     d.H = H;
     d.I = I;
     d.E = E;
@@ -140,6 +152,19 @@ extern "C" int32_t dm_moe_layer_noalloc(int32_t H, int32_t I, int32_t E, int32_t
     d.gu_chunks = I / 8;
     d.d_chunks = H / 16;
     d.expert_bytes = d.gu_chunks * d.gu_chunk_bytes + d.d_chunks * d.d_chunk_bytes;
+
+    // one CTA per SM, its phases waiting on each other: the shape must have a kernel
+    // instance, at most one 16-row down chunk per SM and one resident CTA on every SM
+    bool fits = false;
+    e = moe_fused_fits(d, sd.num_sms, &fits);
+    if (e != cudaSuccess)
+        return na_err(err_buf, err_buf_size, DM_ERR_CUDA, "CUDA_ERROR", "occupancy query: %s", cudaGetErrorString(e));
+    if (!fits)
+        return na_err(err_buf, err_buf_size, DM_ERR_INVALID_ARG, "CONFIG_ERROR",
+                      "no fused MoE kernel for hidden %d / intermediate %d on %d SMs (instances (hidden, "
+                      "intermediate): (256,128) (1024,256) (2048,256) (2048,512), and (4096,512) on GPUs with at "
+                      "least 256 SMs; the kernel needs hidden/16 <= SMs and one resident CTA per SM)",
+                      H, I, sd.num_sms);
 
     LayerW w{};
     w.post_norm = post_norm_dev;
@@ -172,17 +197,15 @@ extern "C" int32_t dm_moe_layer_noalloc(int32_t H, int32_t I, int32_t E, int32_t
     lc.num_sms = sd.num_sms;
     lc.pdl = false;
     lc.kt = nullptr;
-    lc.l2_prefetch = false;
 
+    std::lock_guard<std::mutex> call_lock(g_call_mu);
     e = cudaMemsetAsync(base, 0, kCtlBytes, lc.stream);
     // router logit slots start empty (all-ones NaN pattern; the kernel polls them)
     if (e == cudaSuccess) e = cudaMemsetAsync(lg, 0xFF, static_cast<size_t>(E + 1) * 4, lc.stream);
-    if (e == cudaSuccess) e = launch_moe_fused(lc, d, w, b, 0, nullptr, 0);
+    if (e == cudaSuccess) e = launch_moe_fused(lc, d, w, b, 0);
     if (e != cudaSuccess)
         return na_err(err_buf, err_buf_size, e == cudaErrorInvalidValue ? DM_ERR_INVALID_ARG : DM_ERR_CUDA,
-                      "CUDA_ERROR", "launch: %s (supported (hidden, intermediate): (256,128) (1024,256) "
-                      "(2048,256) (2048,512) (4096,512))",
-                      cudaGetErrorString(e));
+                      "CUDA_ERROR", "launch: %s", cudaGetErrorString(e));
     uint32_t word = 0;
     e = cudaMemcpyAsync(&word, base + kErrOffset, 4, cudaMemcpyDeviceToHost, lc.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(lc.stream);

@@ -77,6 +77,12 @@ def load() -> C.CDLL:
         lib.or_head.argtypes = [C.POINTER(OrModel), P, P]
         lib.or_det_exp.restype = C.c_float
         lib.or_det_exp.argtypes = [C.c_float]
+        U64 = C.c_uint64
+        for name, extra in (("or_synth_bf16", [C.c_float, C.c_float]), ("or_synth_f32", [C.c_float, C.c_float]),
+                            ("or_synth_u8", []), ("or_synth_f16_absnormal", [C.c_float])):
+            fn = getattr(lib, name)
+            fn.restype = C.c_int
+            fn.argtypes = [U64, U64, U64, *extra, P]
         lib.or_set_threads.argtypes = [C.c_int]
         lib.or_get_threads.restype = C.c_int
         _LIB = lib
@@ -85,6 +91,19 @@ def load() -> C.CDLL:
 
 def _p(a):
     return None if a is None else a.ctypes.data
+
+
+class SynthLib:
+    """The oracle's restatement of the seeded generator under the names the product's
+    `synth` module calls (dm_synth_*), so a synthetic model can be built without loading
+    the CUDA library: synth.synth_model(cfg, seed, lib=oracle.SynthLib())."""
+
+    def __init__(self):
+        lib = load()
+        self.dm_synth_bf16 = lib.or_synth_bf16
+        self.dm_synth_f32 = lib.or_synth_f32
+        self.dm_synth_u8 = lib.or_synth_u8
+        self.dm_synth_f16_absnormal = lib.or_synth_f16_absnormal
 
 
 def dims_from_cfg(cfg, kv_bf16: bool = True) -> OrDims:

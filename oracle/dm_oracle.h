@@ -127,6 +127,13 @@ int or_decode_step(const or_model* m, or_state* st, int token, float* logits, fl
 /* Final RMSNorm + lm_head + argmax (first maximum) of one hidden state. */
 int or_head(const or_model* m, const float* x, float* logits);
 
+/* The seeded synthetic-checkpoint generator (or_synth.c), bit-identical to the library's
+ * host generator; same signatures and distributions as dm_synth_* in dismoen_cuda.h. */
+int or_synth_bf16(uint64_t seed, uint64_t sid, uint64_t n, float mean, float std, uint16_t* out);
+int or_synth_f32(uint64_t seed, uint64_t sid, uint64_t n, float mean, float std, float* out);
+int or_synth_u8(uint64_t seed, uint64_t sid, uint64_t n, uint8_t* out);
+int or_synth_f16_absnormal(uint64_t seed, uint64_t sid, uint64_t n, float std, uint16_t* out);
+
 /* Deterministic exponential shared with the device router (include/dismoen_detmath.h). */
 float or_det_exp(float x);
 

@@ -1,8 +1,9 @@
 """Generates the golden vectors that pin the CPU oracle to the reference implementation.
 
-Run in a container where the reference repository is mounted (default /root/reference):
+Run where a checkout of the reference repository is available, giving its path as an
+argument or in the environment variable DISMOEN_REFERENCE:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 The reference's own PyTorch fp32 oracle (tools/oracle/oracle_full.py: forward_gdn_step,
 forward_attn_step, forward_moe_step) is imported from the reference checkout and run on
@@ -73,8 +74,11 @@ def deq_np(q, s, z, group=64):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("DISMOEN_REFERENCE", ""),
+                    help="reference checkout (default: $DISMOEN_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference or not os.path.isdir(args.reference):
+        raise SystemExit("make_golden.py: give the reference checkout with --reference or DISMOEN_REFERENCE")
     sys.path.insert(0, os.path.join(args.reference, "tools", "oracle"))
     import torch
     import oracle_full as ref  # the reference's fp32 oracle

@@ -163,3 +163,32 @@ def test_oracle_decode_deterministic_across_threads(lib, oracle_lib):
     oracle.set_threads(0)
     assert outs[0][0] == outs[1][0]
     assert np.array_equal(outs[0][1], outs[1][1])
+
+
+def test_oracle_generator_matches_library_generator(lib, oracle_lib):
+    """The oracle's restatement of the seeded generator (used by the CPU baseline so that
+    it never maps the CUDA library) gives the library's host generator's bits: every
+    tensor of a config-0 model, and long streams of each distribution."""
+    import oracle
+    cfg = preset("mini")
+    a = synth.synth_model(cfg, 5, lib=lib)
+    b = synth.synth_model(cfg, 5, lib=oracle.SynthLib())
+    for key in ("embed", "final_norm", "lm_head"):
+        assert np.array_equal(a[key], b[key]), key
+    for l in a["layers"]:
+        for name, arr in a["layers"][l].items():
+            assert np.array_equal(arr.view(np.uint8), b["layers"][l][name].view(np.uint8)), (l, name)
+    olib = oracle.SynthLib()
+    n = 1 << 18
+    for seed, sid in ((2, 0x5eed0001), (3, (1 << 40) | 7)):
+        x, y = np.empty(n, np.uint16), np.empty(n, np.uint16)
+        assert lib.dm_synth_bf16(seed, sid, n, 0.0, 1.0, x.ctypes.data) == 0
+        assert olib.dm_synth_bf16(seed, sid, n, 0.0, 1.0, y.ctypes.data) == 0
+        assert np.array_equal(x, y)
+        f, g = np.empty(n, np.float32), np.empty(n, np.float32)
+        assert lib.dm_synth_f32(seed, sid, n, 0.5, 0.1, f.ctypes.data) == 0
+        assert olib.dm_synth_f32(seed, sid, n, 0.5, 0.1, g.ctypes.data) == 0
+        assert np.array_equal(f.view(np.uint32), g.view(np.uint32))
+        assert lib.dm_synth_f16_absnormal(seed, sid, n, 0.02, x.ctypes.data) == 0
+        assert olib.dm_synth_f16_absnormal(seed, sid, n, 0.02, y.ctypes.data) == 0
+        assert np.array_equal(x, y)

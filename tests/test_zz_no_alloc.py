@@ -4,8 +4,10 @@ against dm_moe_block (the context entry point) on the same layer weights and inp
 The GPU test makes two calls in a row with different tokens: the second call starts from
 whatever the first left in the scratch array, so a missed reset would show there.  Both
 entry points run the same fused kernel, so the outputs agree to within NOALLOC_TOL
-(rel = max|a - b| / max|b| on the MoE update y - x).  This file is collected last so the
-test also runs after every other GPU test in the same process."""
+(rel = max|a - b| / max|b| on the MoE update y - x), and the routing (top-k ids and their
+probabilities) is the same bit for bit as the context's router and the CPU oracle's on the
+same input.  This file is collected last so the test also runs after every other GPU test
+in the same process."""
 import numpy as np
 import pytest
 
@@ -42,8 +44,10 @@ def _device_layer(torch, cfg, t):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", ["mini", "layer"])
-def test_noalloc_matches_moe_block_two_calls(lib, name):
+def test_noalloc_matches_moe_block_two_calls(lib, oracle_lib, name):
     import torch
+
+    import oracle
     cfg = preset(name)
     m = synth.synth_model(cfg, 3, layers=[0], head=False)
     t = m["layers"][0]
@@ -51,9 +55,13 @@ def test_noalloc_matches_moe_block_two_calls(lib, name):
     assert noalloc.scratch_bytes(H, I, k) <= noalloc.SCRATCH_BYTES
     x = (np.random.default_rng(7).standard_normal((2, H)) * 3).astype(np.float32)
 
+    om = oracle.OracleModel(m)
     with Engine(cfg, RuntimeConfig.for_context(64)) as eng:
         eng.load_model(m)
         want = eng.moe_block(x, 0)
+        # the context's router on the canonically normalised input (the fused kernel's order)
+        ctx_route = eng.router_forward(np.stack([oracle.rmsnorm(x[i], t["post_norm"], cfg.rms_norm_eps)
+                                                 for i in range(2)]), 0)
 
     w = _device_layer(torch, cfg, t)
     stream = torch.cuda.current_stream().cuda_stream
@@ -69,5 +77,8 @@ def test_noalloc_matches_moe_block_two_calls(lib, name):
         assert np.isfinite(got).all()
         assert rel(got - x[i], want[i] - x[i]) < NOALLOC_TOL, (name, i)
         sel, pr = id_d.cpu().numpy(), p_d.cpu().numpy()
-        assert len(set(sel.tolist())) == k and sel.min() >= 0 and sel.max() < E
-        assert np.all(np.diff(pr) <= 0) and pr[0] > 0
+        _, o_ids, o_probs = oracle.moe_block(om, 0, x[i])
+        np.testing.assert_array_equal(sel, o_ids)
+        assert np.array_equal(pr.view(np.uint32), o_probs.view(np.uint32)), (name, i)
+        np.testing.assert_array_equal(sel, ctx_route.selected_experts[i])
+        assert np.array_equal(pr.view(np.uint32), ctx_route.routing_weights[i].view(np.uint32)), (name, i)
