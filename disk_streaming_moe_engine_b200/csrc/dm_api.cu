@@ -333,7 +333,10 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t ob_ids = T(BC * d.topk * 4), ob_pr = T(BC * d.topk * 4), ob_sg = T(BC * 4);
     const size_t ob_segs = T(static_cast<size_t>(max_segs) * 16), ob_work = T(16), ob_stats = T(16);
     const size_t ob_rcnt = T((BC + 1) * 4);  // one counter per router row block (down to one row)
-    const size_t ob_psrc = T(P * 4), ob_h = T(P * d.I * 4), ob_eout = T(BC * (d.topk + 1) * H * 4);
+    // staged expert operands: 2 rows (hi, lo) per pair, every segment padded to 16 rows
+    const size_t max_cols = 2 * P + 16 * static_cast<size_t>(max_segs);
+    const size_t ob_psrc = T(P * 4), ob_eout = T(BC * (d.topk + 1) * H * 4);
+    const size_t ob_xgu = T(max_cols * H * 2), ob_xdn = T(max_cols * d.I * 2);
     const size_t ob_flags = T(2 * kMaxRanks * 4), ob_epoch = T(2 * 4);
     const size_t ob_cv = T(BC * kHeadChunks * 4), ob_ci = T(BC * kHeadChunks * 4), ob_hl = T(BC * d.V * 4);
     const size_t ob_gen = T(static_cast<size_t>(bgen_cap) * 4), ob_genidx = T(4);
@@ -443,7 +446,9 @@ static int plan_memory(dm_ctx* c, bool commit) {
     bb.max_pairs = static_cast<int>(P);
     bb.ep_flags = reinterpret_cast<unsigned*>(A + ob_flags);
     bb.ep_epoch = reinterpret_cast<unsigned*>(A + ob_epoch);
-    bb.h = reinterpret_cast<float*>(A + ob_h);
+    bb.max_cols = static_cast<int>(max_cols);
+    bb.xgu = A + ob_xgu;
+    bb.xdn = A + ob_xdn;
     bb.eout = reinterpret_cast<float*>(A + ob_eout);
     bb.cand_val = reinterpret_cast<float*>(A + ob_cv);
     bb.cand_idx = reinterpret_cast<int*>(A + ob_ci);
@@ -542,7 +547,7 @@ static EncodeTiledFn encode_fn() {
 static bool encode_expert_maps(dm_ctx* c) {
     const Dims& d = c->d;
     c->xmaps.assign(static_cast<size_t>(d.L) * 2, CUtensorMap{});
-    const bool gu_ok = expert_tma_supported(d.H), dn_ok = expert_tma_supported(d.I);
+    const bool gu_ok = expert_tc_supported(d.H), dn_ok = expert_tc_supported(d.I);
     if (!gu_ok && !dn_ok) return true;
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
@@ -560,11 +565,15 @@ static bool encode_expert_maps(dm_ctx* c) {
                                         static_cast<cuuint64_t>(d.E_res + 1)};
             const cuuint64_t strides[3] = {static_cast<cuuint64_t>(K / 2), static_cast<cuuint64_t>(chunk),
                                            static_cast<cuuint64_t>(d.expert_bytes)};
-            const cuuint32_t box[4] = {128, 16, 1, 1};
+            // boxes of 16 rows x 128 bytes (256 columns) with the 128-byte swizzle; a 128-column
+            // projection is one unswizzled box of 16 rows x 64 bytes
+            const bool wide = K >= 256;
+            const cuuint32_t box[4] = {wide ? 128u : 64u, 16, 1, 1};
             const cuuint32_t estr[4] = {1, 1, 1, 1};
             CUtensorMap* m = &c->xmaps[static_cast<size_t>(l) * 2 + proj];
             const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, base, dims, strides, box, estr,
-                                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                   wide ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             if (r != CUDA_SUCCESS) {
                 fprintf(stderr, "dm_ctx_create: expert tensor map of layer %d failed (%d)\n", l, static_cast<int>(r));

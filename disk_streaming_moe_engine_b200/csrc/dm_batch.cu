@@ -352,10 +352,12 @@ cudaError_t launch_b_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
 // rows of every rank in a fixed order: expert ascending (the shared expert, id E, last, for
 // this rank's own rows), source row ascending (source = rank * n + row; a bit mask of the
 // sources of each expert makes the rank of a pair a population count).  Each expert's
-// pairs are cut into segments of kSegTok.
+// pairs are cut into segments of kSegTok.  Each segment also gets the first row of its
+// staged expert operand: a segment of T tokens takes 2T rows (hi, lo) rounded up to 16,
+// segments in the same order.
 struct BGroupArgs {
     const float* logits;  // [n][E+1]
-    int E, topk, n, max_segs, max_pairs;
+    int E, topk, n, max_segs, max_pairs, max_cols;
     int* ids;
     float* probs;
     float* sg;
@@ -491,21 +493,31 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
     else if (el == Eo)
         cnt = n;
     const int nsg = (cnt + kSegTok - 1) / kSegTok;
+    auto seg_rows = [](int tokens) { return (2 * tokens + 15) / 16 * 16; };
+    int ncol = 0;  // staged operand rows of this expert's segments
+    for (int s2 = 0; s2 < nsg; ++s2) ncol += seg_rows(min(kSegTok, cnt - s2 * kSegTok));
     if (el < Eo && cnt > 0) atomicMax(&s_maxcnt, static_cast<unsigned>(cnt));
     const int touched = __syncthreads_count(el < Eo && cnt > 0);
-    int total_pairs = 0, total_segs = 0;
+    int total_pairs = 0, total_segs = 0, total_cols = 0;
     const int p0 = block_excl_scan(cnt, wsum, &total_pairs);
     __syncthreads();
     const int s0 = block_excl_scan(nsg, wsum, &total_segs);
-    const bool pairs_ok = total_pairs <= a.max_pairs && total_segs <= a.max_segs;
+    __syncthreads();
+    const int c0 = block_excl_scan(ncol, wsum, &total_cols);
+    const bool pairs_ok = total_pairs <= a.max_pairs && total_segs <= a.max_segs && total_cols <= a.max_cols;
     if (el <= Eo) {
         start[el] = p0;
         // the record index the expert kernels address: the expert itself, its cache slot
         // when the pool spills, or the shared expert's record after the routed ones
         const int gexp = el < Eo ? (a.slot_of ? a.slot_of[e0 + el] : e0 + el) : a.E_res;
-        if (pairs_ok)
-            for (int s2 = 0; s2 < nsg; ++s2)
-                a.segs[s0 + s2] = make_int4(gexp, p0 + s2 * kSegTok, min(kSegTok, cnt - s2 * kSegTok), 0);
+        if (pairs_ok) {
+            int col = c0;
+            for (int s2 = 0; s2 < nsg; ++s2) {
+                const int tk = min(kSegTok, cnt - s2 * kSegTok);
+                a.segs[s0 + s2] = make_int4(gexp, p0 + s2 * kSegTok, tk, col);
+                col += seg_rows(tk);
+            }
+        }
     }
     __syncthreads();
     if (pairs_ok) {
@@ -548,6 +560,7 @@ cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchB
     a.n = n;
     a.max_segs = bb.max_segs;
     a.max_pairs = bb.max_pairs;
+    a.max_cols = bb.max_cols;
     a.ids = bb.ids;
     a.probs = bb.probs;
     a.sg = bb.sg;

@@ -119,7 +119,7 @@ struct Buffers {
 constexpr int kMaxBatch = 64;       // rows of one rank's batched step
 constexpr int kMaxRanks = 8;        // expert-parallel group (one process per GPU)
 constexpr int kSrcWords = kMaxBatch * kMaxRanks / 64;  // 64-bit words of a source-row mask
-constexpr int kSegTok = 8;          // tokens of one expert segment (one n8 MMA tile)
+constexpr int kSegTok = 64;         // tokens of one expert segment (hi + lo rows: one 128-column accumulator)
 constexpr int kHeadChunks = 32;     // vocabulary chunks of the batched argmax
 
 // The expert-parallel group as seen by one rank: every rank runs the same batched step on
@@ -167,7 +167,9 @@ struct BatchBuffers {
                           //     experts touched (by this rank), sum of segments, max rows of one
                           //     routed expert, layer-steps
     int* pair_src;        // [max_pairs] source of each pair: (src rank * cap + row) * 32 + k
-    float* h;             // [max_pairs][I] SwiGLU activations per pair
+    int max_cols = 0;     // staged operand rows: every segment's hi/lo rows padded to 16
+    uint8_t* xgu;         // [max_cols][H] bf16: staged gate/up operand (64-column swizzled tiles per segment)
+    uint8_t* xdn;         // [max_cols][I] bf16: staged down operand (SwiGLU activations, hi/lo)
     float* eout;          // [cap][topk + 1][H] expert outputs of this rank's rows (k = topk: shared)
     unsigned* ep_flags;   // [2][kMaxRanks] barrier flags written by the peers
     unsigned* ep_epoch;   // [2] barriers passed (per kind)
@@ -281,7 +283,7 @@ cudaError_t launch_ep_barrier(const LaunchCfg& lc, const BatchBuffers& bb, const
 cudaError_t launch_b_argmax(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n,
                             int write_logits, int record_gen);
 cudaError_t batch_set_attrs();
-bool expert_tma_supported(int K);
+bool expert_tc_supported(int K);
 // SHA-256 (FIPS 180-4) of the concatenation of n buffers (dm_sha256.cu).
 void sha256_parts(const uint8_t* const* parts, const size_t* sizes, int n, uint8_t out[32]);
 
