@@ -493,6 +493,9 @@ static int check_device_error(dm_ctx* c, const char* stage) {
     if (w & DM_DEVERR_CAPACITY) return set_err(c, DM_ERR_CAPACITY, "M5_ERR_CONTEXT_SIZE", stage, -1, "KV cache capacity exceeded on token append");
     if (w & DM_DEVERR_PAGE) return set_err(c, DM_ERR_CAPACITY, "KV_PAGE_ERROR", stage, -1, "page table entry outside the page pool");
     if (w & DM_DEVERR_TOKEN) return set_err(c, DM_ERR_INVALID_ARG, "M4_ERR_INPUT", stage, -1, "token id out of range [0, vocab)");
+    if (w & DM_DEVERR_RANGE)
+        return set_err(c, DM_ERR_NONFINITE, "NONFINITE_ERROR", stage, -1,
+                       "a batched expert activation exceeded the fp16 operand range (|x| > 65504)");
     return set_err(c, DM_ERR_NONFINITE, "NONFINITE_ERROR", stage, -1, "non-finite value detected (word 0x%x)", w);
 }
 

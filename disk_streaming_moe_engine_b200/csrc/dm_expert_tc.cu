@@ -1,6 +1,5 @@
 // dm_expert_tc.cu — routed + shared experts of the batched decode step on the 5th-generation
-// tensor cores (tcgen05, accumulators in tensor memory), fed by TMA, with the 4-bit weights
-// dequantised exactly in shared memory.
+// tensor cores (tcgen05), fed by TMA, with the 4-bit weights expanded into tensor memory.
 //
 // Reference: parallel_moe_experts (src/core/worker_pool.mojo:383) running swiglu_forward
 // (src/layers/swiglu.mojo:52) per expert over the tokens routed to it; weights in the
@@ -8,26 +7,62 @@
 // group of 64 along K, nibbles low first (quant_format.md:831-854).
 //
 // Work.  The (token, expert) pairs of a layer are grouped by expert into segments of at
-// most kSegTok = 64 tokens.  A segment's activations are staged once, before the expert
-// kernels, as a bf16 operand of 2T rows (row 2t = hi(x_t), row 2t + 1 = lo(x_t) with
-// x = hi + lo to 2^-16), padded to N = a multiple of 16 rows, in 64-column group tiles
-// laid out exactly as the MMA reads them (128-byte swizzle).  An item is one segment and
-// one M-tile of 128 weight rows; CTAs take items c, c + grid, ... in order.
+// most kSegTok = 32 tokens.  A segment's activations are staged once, before the expert
+// kernels, as an fp16 operand B of 2T rows (row 2t = hi(x_t), row 2t + 1 = lo(x_t) with
+// x = hi + lo to about 2^-22), padded to N = a multiple of 16 rows, in 64-column group
+// tiles laid out as the MMA reads them from shared memory (128-byte swizzle).  Inside each
+// 8-column unit the columns are stored in the order [0,4,1,5,2,6,3,7]: the order in which
+// one 32-bit word of 8 nibbles yields its pairs (below); A uses the same order, so every
+// dot product is unchanged.  An item is one segment and one M-tile of 128 weight rows;
+// CTAs take items c, c + grid, ... in order.
 //
-// Per 64-column group g of the item (one fp16 scale per row):
-//   producer warp   TMA: the 8 chunks' nibble boxes of the current 256-column K-block,
-//                   the group's B tile (1-D bulk copy of N x 128 bytes), and once per item
-//                   the 8 chunks' scales and zeros;
-//   math warps 0-3  thread r owns weight row r: A[r][k] = bf16(q - z), exact (integers in
-//                   -15..15), written into a swizzled 128 x 64 tile; then, for the group
-//                   before, acc[n] += s[r][g] * D[r][n] read from tensor memory (fp32);
-//   MMA warp        one thread: D = A B^T over K = 64 (4 x tcgen05.mma, M = 128, N) into
-//                   one of 4 tensor-memory accumulators (128 columns each), committed to
-//                   mbarriers that release the accumulator, the A tile and the B tile.
-// Every product is exact and accumulates in fp32; the group scale multiplies the group's
-// fp32 partial, as the format defines.  Each wait is bounded (1 s of %globaltimer): on a
-// timeout the kernel raises the error bit, every role stops, the producer waits for its
-// copies in flight, the MMA thread for its MMAs, and the tensor memory is freed.
+// Arithmetic.  A nibble pair becomes the fp16 pair (1024 + q_j, 1024 + q_{j+4}) by one
+// shift and one LOP3 ((w >> 4j) & 0x000F000F | 0x64006400), the packed subtraction of
+// 1024 + z gives q - z exactly, and one packed multiply by the group's fp16 scale gives
+// w = fp16(s (q - z)): the exact product rounded once (relative error <= 2^-12; the
+// reference's own 4-bit path rounds its dequantised weights to bf16, 2^-9).  The tensor
+// cores then accumulate w x over the whole K of the item in fp32 in one chain: one
+// accumulator per item, read once.
+//
+// Why this shape.  Measured on the way (tcgen05.mma probes and %globaltimer stamps of the
+// pipeline): a chain of 4 MMAs (M = 128, N = 16) plus its commit costs ~435 SM cycles,
+// whatever the operands' placement, while longer chains cost ~48 cycles per MMA; keeping
+// the per-group scale outside the MMA (one chain per 64 columns, drained into registers)
+// ran at ~0.5 us per group.  A lives in tensor memory (tcgen05.st from the expanding
+// thread's registers into its own lane), so shared memory only carries the nibbles and B.
+//
+// Roles (704 threads; K is processed in K-blocks of 256 columns (4 groups), held in a ring
+// of 3 slots: slot j has a nibble stage, 4 A buffers in tensor memory (columns 128 + 128 j
+// ..) and 4 B tiles; D buffers are tensor-memory columns [0, 128)):
+//   producer warp 20   per K-block: waits for the slot's previous MMAs, then TMA-loads the
+//                      8 chunks' nibble boxes and, with one 1-D bulk copy, the 4 groups' B
+//                      tiles (consecutive in the staged operand); per item the 8 chunks'
+//                      scales and zeros;
+//   expand warps 0-15  four sets of four (one warp per sub-partition); set s expands the
+//                      groups q with q % 4 == s, warp 4 s + p rows 32 p .. 32 p + 31, a whole
+//                      row per thread, into the group's A buffer.  Four groups are expanded
+//                      at once: one group's chain (shared-memory loads -> ALU -> tensor-memory
+//                      store -> arrive) is latency-bound (with three sets the MMA thread still
+//                      waited ~450 cycles per K-block for its inputs);
+//   MMA warp 21        one thread: per K-block one wait (A of the 4 groups expanded and B
+//                      landed: one barrier), 16 tcgen05.mma (M = 128, N, K = 16; A from
+//                      tensor memory, B from shared memory) accumulating into the item's D
+//                      buffer, one commit that frees the slot; at the item's end a commit
+//                      hands D to the drain;
+//   drain warps 16-19  warp 16 + p owns rows 32 p .. 32 p + 31: reads the item's D buffer
+//                      16 columns at a time, runs the epilogue on them, frees the buffer.
+// Measured on the way (tcgen05.mma probes, SM-cycle stamps of the pipeline): a chain of 4
+// MMAs (N = 16) with its commit costs ~435 cycles, long chains ~70 cycles per MMA; an
+// mbarrier wait in the busy kernel costs the MMA thread 200-400 cycles even when the phase
+// has long completed, so the single-thread roles wait once per K-block, not per group.
+// A slot cannot be reused early: the producer refills slot j for K-block kb + 3 only after
+// the MMAs of kb, which need every expander's arrival for kb, so the nibbles of kb have
+// been read and its A buffers and B tiles consumed; each waiter's next phase needs its own
+// progress first, so no wait can miss a phase.
+// Each wait is bounded (1 s of %globaltimer): on a timeout the kernel raises the error bit,
+// every role stops, the producer waits for its copies in flight, the MMA thread for its
+// MMAs, and the tensor memory is freed.  An activation outside the fp16 range raises
+// DM_DEVERR_RANGE (the host reports an error instead of an overflowed result).
 //
 // gate/up (K = H): chunk c of a record holds gate rows 8c..8c+7, then up rows 8c..8c+7, so
 //   tile t covers intermediate indices 64t..64t+63 and lane r + 8 holds the up row of the
@@ -43,15 +78,24 @@
 
 namespace dm {
 
-constexpr int kTcThreads = 192;   // warps 0-3 math, warp 4 producer, warp 5 MMA + allocator
-constexpr int kTcNKS = 3;         // nibble K-block stages
-constexpr int kTcNAS = 3;         // dequantised A tiles
-constexpr int kTcNBS = 4;         // B group tiles
-constexpr int kTcNACC = 4;        // tensor-memory accumulators
-constexpr int kTcAccCols = 128;   // columns of one accumulator (N <= 128: 64 tokens, hi + lo)
-constexpr int kTcTile = 16384;    // bytes of one A or B tile buffer (128 rows x 128 bytes)
+constexpr int kTcSets = 4;                    // expand sets: groups expanded at once
+constexpr int kTcExpWarps = 4 * kTcSets;      // one warp per sub-partition and set
+constexpr int kTcExp = kTcExpWarps * 32;
+constexpr int kTcDrainWarp0 = kTcExpWarps;    // drain warps, one per sub-partition
+constexpr int kTcDrain = 128;
+constexpr int kTcProdWarp = kTcExpWarps + 4;
+constexpr int kTcMmaWarp = kTcProdWarp + 1;
+constexpr int kTcThreads = (kTcMmaWarp + 1) * 32;
+constexpr int kTcNKS = 3;                     // K-block slots
+constexpr int kTcNACC = 2;                    // D buffers (items in flight between MMA and drain)
+constexpr int kTcDCols = 64;
+constexpr int kTcACols = 32;                  // one group's A buffer
+constexpr int kTcACol0 = kTcNACC * kTcDCols;  // first A column
+constexpr int kTcBTile = 8192;                // <= 64 rows x 128 bytes
+constexpr int kTcGPBMax = 4;                  // groups per K-block
 
-static_assert(2 * kSegTok <= kTcAccCols, "a segment's hi and lo rows fit one accumulator");
+static_assert(2 * kSegTok <= kTcDCols, "a segment's hi and lo rows fit one D buffer");
+static_assert(kTcACol0 + kTcNKS * kTcGPBMax * kTcACols <= 512, "tensor memory columns");
 
 template <int K>
 struct TcGeom {
@@ -66,9 +110,9 @@ struct TcGeom {
     static constexpr int SZC = 16 * NG * 2 + 16 * NG / 2;  // scales + zeros of one chunk
     static constexpr int SZ = 8 * SZC;
     static constexpr int S_OFF = 16 * K / 2;               // scales inside a chunk
-    static constexpr int A_OFF = 0;
-    static constexpr int B_OFF = A_OFF + kTcNAS * kTcTile;
-    static constexpr int N_OFF = B_OFF + kTcNBS * kTcTile;
+    static constexpr int B_OFF = 0;                        // slot j: B tiles of its 4 groups
+    static constexpr int B_SLOT = kTcGPBMax * kTcBTile;
+    static constexpr int N_OFF = B_OFF + kTcNKS * B_SLOT;
     static constexpr int SZ_OFF = N_OFF + kTcNKS * NIB_AL;
     static constexpr size_t SMEM = SZ_OFF + 2 * SZ + 1024;  // + alignment slack
     static_assert(K % 128 == 0 && K >= 128, "whole zero bytes and 64-column groups");
@@ -79,19 +123,88 @@ struct TcGeom {
 struct TcExpArgs {
     const uint8_t* experts;   // record 0 of the layer's pool; the shared record follows the routed ones
     int64_t expert_bytes, proj_off, chunk_bytes;
-    const int4* segs;         // (record, first pair, tokens, first staged column)
+    const int4* segs;         // (record, first pair, tokens, first staged row)
     const int* work;          // [0] segments
     const int* pair_src;      // (source rank * n + row) * 32 + k of each pair
     int n, topk, H, I;
     int tiles;                // M-tiles (128 weight rows) per segment
-    const uint8_t* bstage;    // this projection's staged operand: [columns][K] bf16 in group tiles
+    const uint8_t* bstage;    // this projection's staged operand: [rows][K] fp16 in group tiles
     uint8_t* hstage;          // gate/up: the down projection's staged operand
     EpView ep;                // down: expert outputs of each source rank
     CUtensorMap wmap;         // nibble rows of the pool: (row bytes, 16 rows, chunk, record)
+    uint64_t* trace;          // CTA 0's pipeline stamps of its first kTcTraceGroups groups, or null
     uint32_t* err;
 };
 
+// Pipeline trace (CTA 0, group q < kTcTraceGroups, SM cycles), stamps per group:
+// 0 producer issues the group's K-block, 1 the MMA thread starts the group's MMAs, 2 the
+// expanding warp of sub-partition 0 starts (nibbles landed), 3 its tensor-memory stores are
+// done, 4 it has arrived; for the last group of an item: 5 the first drain warp starts
+// waiting, 6 the accumulator is ready, 7 the epilogue is done; 8 the MMA thread has issued
+// the K-block's commit, 9 its wait for the K-block's inputs returned.
+constexpr int kTcTraceGroups = 32;
+constexpr int kTcTraceSlots = 10;
+// Stamps are SM clock cycles (clock64): all of them come from CTA 0's SM, and reading
+// %globaltimer per group slowed the traced kernel down by half.
+DM_DEV void tc_stamp(uint64_t* tr, uint32_t q, int k) {
+    if (tr && blockIdx.x == 0 && q < kTcTraceGroups) tr[kTcTraceSlots * q + k] = static_cast<uint64_t>(clock64());
+}
+
 DM_DEV int seg_cols(int tokens) { return (2 * tokens + 15) / 16 * 16; }
+
+// Position in an mbarrier ring of N stages: the stage index and the parity of its current
+// use (a "full" barrier is waited with `ph`, an "empty" one with ph ^ 1).  Kept as counters
+// so that the single-thread roles do no division per group.
+template <int N>
+struct RingPos {
+    uint32_t i = 0, ph = 0;
+    DM_DEV void next() {
+        if (++i == N) {
+            i = 0;
+            ph ^= 1u;
+        }
+    }
+};
+
+// Item sequence of a CTA: items c, c + grid, ...; the segment record of the next item is
+// loaded one item ahead.
+struct ItemIter {
+    int item, nitems, tiles, t;
+    int4 sg, nx;
+    DM_DEV ItemIter(const int4* segs, int n, int tiles_) : item(blockIdx.x), nitems(n), tiles(tiles_) {
+        t = item % tiles;
+        sg = make_int4(0, 0, 0, 0);
+        nx = sg;
+        if (item < nitems) sg = segs[item / tiles];
+        const int n2 = item + static_cast<int>(gridDim.x);
+        if (n2 < nitems) nx = segs[n2 / tiles];
+    }
+    DM_DEV bool valid() const { return item < nitems; }
+    DM_DEV void next(const int4* segs) {
+        item += gridDim.x;
+        t = item % tiles;
+        sg = nx;
+        const int n2 = item + static_cast<int>(gridDim.x);
+        if (n2 < nitems) nx = segs[n2 / tiles];
+    }
+};
+
+// Staged position of element e (0..7) of an 8-column unit: [0,4,1,5,2,6,3,7] holds e.
+DM_DEV int unit_pos(int e) { return e < 4 ? 2 * e : 2 * (e - 4) + 1; }
+
+// Byte offset of element k (0..63) of row n of a staged group tile.
+DM_DEV uint32_t stage_off(int n, int k) {
+    return static_cast<uint32_t>((n >> 3) * 1024 + (n & 7) * 128 + ((((k >> 3) ^ (n & 7)) & 7) << 4) +
+                                 unit_pos(k & 7) * 2);
+}
+
+// x as fp16 hi + lo (lo = fp16(x - hi)); raises DM_DEVERR_RANGE outside the fp16 range.
+DM_DEV void split_f16(float x, uint16_t& hi, uint16_t& lo, uint32_t* err) {
+    if (!(fabsf(x) <= 65504.0f)) raise_error(err, DM_DEVERR_RANGE);
+    const __half h = __float2half_rn(x);
+    hi = __half_as_ushort(h);
+    lo = __half_as_ushort(__float2half_rn(x - __half2float(h)));
+}
 
 DM_DEV void tma_load_4d_tc(void* smem_dst, const CUtensorMap* map, int x, int y, int z, int w, uint64_t* bar) {
     asm volatile(
@@ -101,21 +214,15 @@ DM_DEV void tma_load_4d_tc(void* smem_dst, const CUtensorMap* map, int x, int y,
         : "memory");
 }
 
-DM_DEV void sts128(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(smem_u32(p)), "r"(a), "r"(b), "r"(c), "r"(d)
-                 : "memory");
-}
-
-// Four nibble pairs of one 32-bit word (bytes b0..b3, low nibble first) as bf16 pairs
-// (q_lo - z, q_hi - z): the nibble becomes the low mantissa bits of 128.0 (exact), and the
-// packed subtraction of 128 + z is exact.
-DM_DEV void nib_word_minus_zero(uint32_t w, uint32_t zpair, uint32_t (&out)[4]) {
-    const uint32_t lo4 = w & 0x0F0F0F0Fu, hi4 = (w >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const uint32_t p = (__byte_perm(lo4, hi4, static_cast<uint32_t>(k | ((4 + k) << 8))) & 0x000F000Fu) | 0x43004300u;
-        asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(out[k]) : "r"(p), "r"(zpair));
-    }
+// Pair j of a word of 8 nibbles (after the word was shifted right by 4j): the fp16 pair
+// fp16(s (q_j - z)), fp16(s (q_{j+4} - z)); (1024 + q) - (1024 + z) is exact, the
+// multiply rounds once.
+DM_DEV uint32_t nib_pair_w(uint32_t w, uint32_t zpair, uint32_t spair) {
+    uint32_t p, d, m;
+    asm("lop3.b32 %0, %1, 0x000F000F, 0x64006400, 0xEA;" : "=r"(p) : "r"(w));  // (a & b) | c
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(p), "r"(zpair));
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(m) : "r"(d), "r"(spair));
+    return m;
 }
 
 template <int K, bool GATEUP>
@@ -123,8 +230,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) b_expert_tc_kernel(const __grid
     using G = TcGeom<K>;
     extern __shared__ __align__(1024) uint8_t tsm_raw[];
     uint8_t* sm = tsm_raw + ((1024u - (smem_u32(tsm_raw) & 1023u)) & 1023u);
-    __shared__ __align__(8) uint64_t nib_full[kTcNKS], nib_empty[kTcNKS], a_full[kTcNAS], a_empty[kTcNAS],
-        b_full[kTcNBS], b_empty[kTcNBS], acc_full[kTcNACC], acc_empty[kTcNACC], sz_full[2], sz_empty[2], done_bar;
+    __shared__ __align__(8) uint64_t nib_full[kTcNKS], in_full[kTcNKS], mma_done[kTcNKS], acc_full[kTcNACC],
+        acc_empty[kTcNACC], sz_full[2], sz_empty[2], done_bar;
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
@@ -132,29 +239,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) b_expert_tc_kernel(const __grid
     if (tid == 0) {
         for (int i = 0; i < kTcNKS; ++i) {
             mbar_init(&nib_full[i], 1);
-            mbar_init(&nib_empty[i], 128);
-        }
-        for (int i = 0; i < kTcNAS; ++i) {
-            mbar_init(&a_full[i], 128);
-            mbar_init(&a_empty[i], 1);
-        }
-        for (int i = 0; i < kTcNBS; ++i) {
-            mbar_init(&b_full[i], 1);
-            mbar_init(&b_empty[i], 1);
+            mbar_init(&in_full[i], 128 * G::GPB + 1);  // every group's expanding set + the B copy
+            mbar_init(&mma_done[i], 1);
         }
         for (int i = 0; i < kTcNACC; ++i) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 128);
+            mbar_init(&acc_empty[i], kTcDrain);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&sz_full[i], 1);
-            mbar_init(&sz_empty[i], 128);
+            mbar_init(&sz_empty[i], kTcExp);  // every set, every item
         }
         mbar_init(&done_bar, 1);
         mbar_fence_init();
         s_abort = 0;
     }
-    if (warp == 5) tc_alloc(&s_tmem, kTcNACC * kTcAccCols);
+    if (warp == kTcMmaWarp) tc_alloc(&s_tmem, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -164,207 +264,221 @@ __global__ void __launch_bounds__(kTcThreads, 1) b_expert_tc_kernel(const __grid
     const int nitems = a.work[0] * a.tiles;
     pdl_launch_dependents();
 
-    if (warp == 4) {
-        // ---------------- producer: TMA nibble stages, B tiles, scales + zeros ----------------
+    if (warp == kTcProdWarp) {
+        // ---------------- producer: per K-block the nibble stage and the 4 B tiles ----------------
         if (lane == 0) {
-            uint32_t kbq = 0, q = 0, it = 0;
-            for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++it) {
-                const int4 sg = a.segs[item / a.tiles];
-                const int t = item % a.tiles;
-                const int N = seg_cols(sg.z);
+            RingPos<kTcNKS> kq;
+            RingPos<2> zq;
+            uint32_t n_kb = 0, n_sz = 0, q = 0;
+            bool ok = true;
+            for (ItemIter itr(a.segs, nitems, a.tiles); itr.valid() && ok; itr.next(a.segs)) {
+                const int4 sg = itr.sg;
+                const int t = itr.t;
+                const uint32_t bbytes = static_cast<uint32_t>(seg_cols(sg.z)) * 128u;
                 const uint8_t* rec = a.experts + static_cast<int64_t>(sg.x) * a.expert_bytes + a.proj_off;
-                const int sb = it & 1;
-                if (!mbar_wait_bounded(&sz_empty[sb], ring_parity(it, 2) ^ 1u, a.err, abort_flag)) break;
-                mbar_arrive_expect_tx(&sz_full[sb], G::SZ);
+                if (!(ok = mbar_wait_bounded(&sz_empty[zq.i], zq.ph ^ 1u, a.err, abort_flag))) break;
+                mbar_arrive_expect_tx(&sz_full[zq.i], G::SZ);
                 for (int c = 0; c < 8; ++c)
-                    bulk_g2s(sm + G::SZ_OFF + sb * G::SZ + c * G::SZC,
-                             rec + static_cast<int64_t>(8 * t + c) * a.chunk_bytes + G::S_OFF, G::SZC, &sz_full[sb]);
-                const uint8_t* bst = a.bstage + static_cast<size_t>(sg.w) * K * 2;
-                bool ok = true;
-                for (int g = 0; g < G::NG && ok; ++g, ++q) {
-                    if (g % G::GPB == 0) {
-                        const int s = kbq % kTcNKS;
-                        if (!(ok = mbar_wait_bounded(&nib_empty[s], ring_parity(kbq, kTcNKS) ^ 1u, a.err, abort_flag)))
-                            break;
-                        fence_proxy_async_smem();
-                        mbar_arrive_expect_tx(&nib_full[s], G::NIB);
-                        for (int c = 0; c < 8; ++c)
-                            tma_load_4d_tc(sm + G::N_OFF + s * G::NIB_AL + c * G::BOX, &a.wmap, G::RB * (g / G::GPB), 0,
-                                           8 * t + c, sg.x, &nib_full[s]);
-                        ++kbq;
-                    }
-                    const int bs = q % kTcNBS;
-                    if (!(ok = mbar_wait_bounded(&b_empty[bs], ring_parity(q, kTcNBS) ^ 1u, a.err, abort_flag))) break;
-                    mbar_arrive_expect_tx(&b_full[bs], static_cast<uint32_t>(N) * 128u);
-                    bulk_g2s(sm + G::B_OFF + bs * kTcTile, bst + static_cast<size_t>(g) * N * 128,
-                             static_cast<uint32_t>(N) * 128u, &b_full[bs]);
+                    bulk_g2s(sm + G::SZ_OFF + zq.i * G::SZ + c * G::SZC,
+                             rec + static_cast<int64_t>(8 * t + c) * a.chunk_bytes + G::S_OFF, G::SZC, &sz_full[zq.i]);
+                zq.next();
+                ++n_sz;
+                const uint8_t* bsrc = a.bstage + static_cast<size_t>(sg.w) * K * 2;
+                for (int kb = 0; kb < G::NG / G::GPB; ++kb, q += G::GPB) {
+                    if (!(ok = mbar_wait_bounded(&mma_done[kq.i], kq.ph ^ 1u, a.err, abort_flag))) break;
+                    tc_stamp(a.trace, q, 0);
+                    fence_proxy_async_smem();
+                    mbar_arrive_expect_tx(&nib_full[kq.i], G::NIB);
+                    uint8_t* dst = sm + G::N_OFF + kq.i * G::NIB_AL;
+                    for (int c = 0; c < 8; ++c)
+                        tma_load_4d_tc(dst + c * G::BOX, &a.wmap, G::RB * kb, 0, 8 * t + c, sg.x, &nib_full[kq.i]);
+                    mbar_arrive_expect_tx(&in_full[kq.i], G::GPB * bbytes);
+                    bulk_g2s(sm + G::B_OFF + kq.i * G::B_SLOT, bsrc, G::GPB * bbytes, &in_full[kq.i]);
+                    bsrc += G::GPB * bbytes;
+                    kq.next();
+                    ++n_kb;
                 }
-                if (!ok) break;
             }
             // every copy this thread issued has landed before the CTA may leave (bounded)
-            for (uint32_t u = kbq > kTcNKS ? kbq - kTcNKS : 0; u < kbq; ++u)
-                mbar_wait_bounded(&nib_full[u % kTcNKS], ring_parity(u, kTcNKS), a.err, nullptr);
-            for (uint32_t u = q > kTcNBS ? q - kTcNBS : 0; u < q; ++u)
-                mbar_wait_bounded(&b_full[u % kTcNBS], ring_parity(u, kTcNBS), a.err, nullptr);
-            for (uint32_t u = it > 2 ? it - 2 : 0; u < it; ++u)
-                mbar_wait_bounded(&sz_full[u % 2], ring_parity(u, 2), a.err, nullptr);
+            for (uint32_t u = n_kb > kTcNKS ? n_kb - kTcNKS : 0; u < n_kb; ++u)
+                mbar_wait_bounded(&nib_full[u % kTcNKS], (u / kTcNKS) & 1u, a.err, nullptr);
+            for (uint32_t u = n_sz > 2 ? n_sz - 2 : 0; u < n_sz; ++u)
+                mbar_wait_bounded(&sz_full[u % 2], (u / 2) & 1u, a.err, nullptr);
+            // (the B copies of a K-block complete the slot's in_full phase together with the
+            //  expanders; the MMA thread's final wait covers the last ones)
         }
-    } else if (warp == 5) {
-        // ---------------- MMA issue (one thread) ----------------
+    } else if (warp == kTcMmaWarp) {
+        // ---------------- MMA issue (one thread): one accumulation chain per item ----------------
         if (lane == 0) {
+            RingPos<kTcNKS> kq;      // K-block slot
+            RingPos<kTcNACC> dq;     // D buffer of the item
             uint32_t q = 0;
             bool ok = true;
-            for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
-                const int4 sg = a.segs[item / a.tiles];
-                const uint32_t idesc = tc_idesc_bf16(128, seg_cols(sg.z));
-                for (int g = 0; g < G::NG; ++g, ++q) {
-                    const int as = q % kTcNAS, bs = q % kTcNBS, ab = q % kTcNACC;
-                    ok = mbar_wait_bounded(&a_full[as], ring_parity(q, kTcNAS), a.err, abort_flag) &&
-                         mbar_wait_bounded(&b_full[bs], ring_parity(q, kTcNBS), a.err, abort_flag) &&
-                         mbar_wait_bounded(&acc_empty[ab], ring_parity(q, kTcNACC) ^ 1u, a.err, abort_flag);
-                    if (!ok) break;
+            const uint32_t b0 = smem_u32(sm + G::B_OFF);
+            for (ItemIter itr(a.segs, nitems, a.tiles); itr.valid() && ok; itr.next(a.segs)) {
+                const int N = seg_cols(itr.sg.z);
+                const uint32_t idesc = tc_idesc_f16(128, N);
+                if (!mbar_try_wait(&acc_empty[dq.i], dq.ph ^ 1u) &&
+                    !(ok = mbar_wait_bounded(&acc_empty[dq.i], dq.ph ^ 1u, a.err, abort_flag)))
+                    break;
+                const uint32_t d = tmem + dq.i * kTcDCols;
+                for (int kb = 0; kb < G::NG / G::GPB; ++kb) {
+                    if (!mbar_try_wait(&in_full[kq.i], kq.ph) &&
+                        !(ok = mbar_wait_bounded(&in_full[kq.i], kq.ph, a.err, abort_flag)))
+                        break;
+                    tc_stamp(a.trace, q, 9);
                     tc_fence_after();
-                    const uint64_t ad = tc_desc_sw128(smem_u32(sm + G::A_OFF + as * kTcTile));
-                    const uint64_t bd = tc_desc_sw128(smem_u32(sm + G::B_OFF + bs * kTcTile));
-                    const uint32_t d = tmem + static_cast<uint32_t>(ab * kTcAccCols);
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) tc_mma_bf16(d, ad + 2 * k, bd + 2 * k, idesc, k > 0);
-                    tc_commit(&acc_full[ab]);
-                    tc_commit(&a_empty[as]);
-                    tc_commit(&b_empty[bs]);
+                    const uint32_t bslot = b0 + kq.i * G::B_SLOT;
+                    for (int gk = 0; gk < G::GPB; ++gk, ++q) {
+                        tc_stamp(a.trace, q, 1);
+                        const uint32_t at = tmem + static_cast<uint32_t>(kTcACol0 + (kq.i * kTcGPBMax + gk) * kTcACols);
+                        const uint64_t bd = tc_desc_sw128(bslot + gk * N * 128);
+                        tc_mma_bf16_ts(d, at, bd, idesc, kb > 0 || gk > 0);
+                        tc_mma_bf16_ts(d, at + 8, bd + 2, idesc, true);
+                        tc_mma_bf16_ts(d, at + 16, bd + 4, idesc, true);
+                        tc_mma_bf16_ts(d, at + 24, bd + 6, idesc, true);
+                    }
+                    tc_commit(&mma_done[kq.i]);
+                    tc_stamp(a.trace, q - 1, 8);
+                    kq.next();
                 }
+                if (!ok) break;
+                tc_commit(&acc_full[dq.i]);
+                dq.next();
             }
             tc_commit(&done_bar);  // every MMA issued above has completed once this arrives
             mbar_wait_bounded(&done_bar, 0, a.err, nullptr);
         }
     } else {
-        // ---------------- math warps: dequantise, drain, epilogue ----------------
-        const int r = tid;  // weight row of the tile = tensor-memory lane
-        uint32_t kbq = 0, q = 0, it = 0;
-        float acc[kTcAccCols];
-        bool ok = true;
-        // waits of the math warps are made warp-uniform: the tensor-memory loads after them
-        // are .sync.aligned and need every lane
+        // waits are warp-uniform: the tensor-memory accesses after them are .sync.aligned
         auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
             return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, a.err, abort_flag));
         };
-        for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++it) {
-            const int4 sg = a.segs[item / a.tiles];
-            const int t = item % a.tiles;
-            const int T = sg.z;
-            const int N = seg_cols(T);
-            const int sb = it & 1;
-            if (!(ok = wwait(&sz_full[sb], ring_parity(it, 2)))) break;
-            const uint8_t* szc = sm + G::SZ_OFF + sb * G::SZ + (r >> 4) * G::SZC;
-            const uint16_t* srow = reinterpret_cast<const uint16_t*>(szc + (r & 15) * G::NG * 2);
-            const uint8_t* zrow = szc + 16 * G::NG * 2 + (r & 15) * (G::NG / 2);
+        const int sp = warp & 3;
+        const int r = 32 * sp + lane;  // weight row of the tile = tensor-memory lane
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * sp) << 16);
+        bool ok = true;
+        if (warp < kTcExpWarps) {
+            // ---------------- expand warps: nibbles -> fp16 s (q - z) pairs in tensor memory ----------------
+            const int set = warp >> 2;
+            RingPos<kTcNKS> kq;
+            RingPos<2> zq;
+            RingPos<kTcSets> mine;  // mine.i == set: this set expands the group
+            uint32_t q = 0;
+            for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+                const int sb = zq.i;
+                if (!(ok = wwait(&sz_full[sb], zq.ph))) break;
+                const uint8_t* szc = sm + G::SZ_OFF + sb * G::SZ + (r >> 4) * G::SZC;
+                const uint16_t* srow = reinterpret_cast<const uint16_t*>(szc + (r & 15) * G::NG * 2);
+                const uint8_t* zrow = szc + 16 * G::NG * 2 + (r & 15) * (G::NG / 2);
+                for (int g = 0; g < G::NG; ++g, ++q) {
+                    const int gk = g % G::GPB;
+                    if (static_cast<int>(mine.i) == set) {
+                        const int s = kq.i;
+                        if (!(ok = wwait(&nib_full[s], kq.ph))) break;  // also: the slot's A buffers are free
+                        tc_fence_after();
+                        if (tid == 32 * 4 * set) tc_stamp(a.trace, q, 2);
+                        // row r, group g: 64 nibbles -> 32 columns of pairs
+                        const uint8_t* nrow = sm + G::N_OFF + s * G::NIB_AL + (r >> 4) * G::BOX + (r & 15) * G::RB;
+                        const int u0 = 2 * gk, u1 = 2 * gk + 1;  // 16-byte units of the row's group bytes
+                        const uint4 w0 = *reinterpret_cast<const uint4*>(nrow + ((G::SWZ ? (u0 ^ (r & 7)) : u0) << 4));
+                        const uint4 w1 = *reinterpret_cast<const uint4*>(nrow + ((G::SWZ ? (u1 ^ (r & 7)) : u1) << 4));
+                        const uint32_t z = (zrow[g >> 1] >> (4 * (g & 1))) & 15u;
+                        const uint32_t zpair = (0x6400u | z) * 0x10001u;
+                        const uint32_t spair = static_cast<uint32_t>(srow[g]) * 0x10001u;
+                        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                        uint32_t c0[16], c1[16];
 #pragma unroll
-            for (int j = 0; j < kTcAccCols; ++j) acc[j] = 0.0f;
-            uint8_t* arow = sm + G::A_OFF + (r >> 3) * 1024 + (r & 7) * 128;
-            const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
-
-            auto drain = [&](uint32_t qq, int gg) -> bool {
-                const int ab = qq % kTcNACC;
-                if (!wwait(&acc_full[ab], ring_parity(qq, kTcNACC))) return false;
-                tc_fence_after();
-                const float sc = __half2float(__ushort_as_half(srow[gg]));
-                const uint32_t ta = lane_base + static_cast<uint32_t>(ab * kTcAccCols);
-#pragma unroll
-                for (int c = 0; c < kTcAccCols / 16; ++c) {
-                    if (c * 16 < N) {
-                        float v[16];
-                        tc_ld16(ta + 16 * c, v);
-                        tc_wait_ld();
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) acc[16 * c + j] = fmaf(sc, v[j], acc[16 * c + j]);
+                        for (int v = 0; v < 4; ++v) {
+                            c0[4 * v] = nib_pair_w(words[v], zpair, spair);
+                            c0[4 * v + 1] = nib_pair_w(words[v] >> 4, zpair, spair);
+                            c0[4 * v + 2] = nib_pair_w(words[v] >> 8, zpair, spair);
+                            c0[4 * v + 3] = nib_pair_w(words[v] >> 12, zpair, spair);
+                            c1[4 * v] = nib_pair_w(words[4 + v], zpair, spair);
+                            c1[4 * v + 1] = nib_pair_w(words[4 + v] >> 4, zpair, spair);
+                            c1[4 * v + 2] = nib_pair_w(words[4 + v] >> 8, zpair, spair);
+                            c1[4 * v + 3] = nib_pair_w(words[4 + v] >> 12, zpair, spair);
+                        }
+                        const uint32_t acol =
+                            lane_base + static_cast<uint32_t>(kTcACol0 + (s * kTcGPBMax + gk) * kTcACols);
+                        tc_st16(acol, c0);
+                        tc_st16(acol + 16, c1);
+                        tc_wait_st();
+                        if (tid == 32 * 4 * set) tc_stamp(a.trace, q, 3);
+                        tc_fence_before();
+                        mbar_arrive(&in_full[s]);
+                        if (tid == 32 * 4 * set) tc_stamp(a.trace, q, 4);
                     }
+                    mine.next();
+                    if (gk == G::GPB - 1) kq.next();
                 }
-                tc_fence_before();
-                mbar_arrive(&acc_empty[ab]);
-                return true;
-            };
-
-            for (int g = 0; g < G::NG; ++g, ++q) {
-                const int s = kbq % kTcNKS;
-                const int gk = g % G::GPB;
-                if (gk == 0 && !(ok = wwait(&nib_full[s], ring_parity(kbq, kTcNKS)))) break;
-                const int as = q % kTcNAS;
-                if (!(ok = wwait(&a_empty[as], ring_parity(q, kTcNAS) ^ 1u))) break;
-                // row r, group g: 32 nibble bytes -> 64 bf16 (q - z)
-                const uint8_t* nrow = sm + G::N_OFF + s * G::NIB_AL + (r >> 4) * G::BOX + (r & 15) * G::RB;
-                uint4 w0, w1;
-                if (G::SWZ) {
-                    w0 = *reinterpret_cast<const uint4*>(nrow + (((2 * gk) ^ (r & 7)) << 4));
-                    w1 = *reinterpret_cast<const uint4*>(nrow + (((2 * gk + 1) ^ (r & 7)) << 4));
-                } else {
-                    w0 = *reinterpret_cast<const uint4*>(nrow + 32 * gk);
-                    w1 = *reinterpret_cast<const uint4*>(nrow + 32 * gk + 16);
-                }
-                const uint32_t z = (zrow[g >> 1] >> (4 * (g & 1))) & 15u;
-                const uint32_t zpair = (0x4300u | z) * 0x10001u;
-                const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-                uint8_t* adst = arow + as * kTcTile;
-#pragma unroll
-                for (int v = 0; v < 8; ++v) {
-                    uint32_t o[4];
-                    nib_word_minus_zero(words[v], zpair, o);
-                    sts128(adst + ((v ^ (r & 7)) << 4), o[0], o[1], o[2], o[3]);
-                }
-                fence_proxy_async_smem();  // generic writes before the tensor cores read the tile
-                mbar_arrive(&a_full[as]);
-                if (gk == G::GPB - 1) {
-                    mbar_arrive(&nib_empty[s]);
-                    ++kbq;
-                }
-                if (g > 0 && !(ok = drain(q - 1, g - 1))) break;
+                mbar_arrive(&sz_empty[sb]);
+                zq.next();
             }
-            if (ok) ok = drain(q - 1, G::NG - 1);
-            mbar_arrive(&sz_empty[sb]);
-            if (!ok) break;
-
-            // ---------------- epilogue: hi + lo columns of every token ----------------
-            if (GATEUP) {
+        } else {
+            // ---------------- drain warps: the item's accumulator, 16 columns (8 tokens) at a time ----------------
+            RingPos<kTcNACC> dq;
+            uint32_t q_end = 0;
+            for (ItemIter itr(a.segs, nitems, a.tiles); itr.valid() && ok; itr.next(a.segs)) {
+                const int4 sg = itr.sg;
+                const int t = itr.t;
+                const int T = sg.z;
+                const int N = seg_cols(T);
+                q_end += G::NG;
+                const bool stamp = tid == kTcDrainWarp0 * 32;
+                if (stamp) tc_stamp(a.trace, q_end - 1, 5);
+                if (!(ok = wwait(&acc_full[dq.i], dq.ph))) break;
+                if (stamp) tc_stamp(a.trace, q_end - 1, 6);
+                tc_fence_after();
+                const uint32_t ta = lane_base + static_cast<uint32_t>(dq.i * kTcDCols);
                 const int j = r & 15;
-                const int i_loc = 8 * (r >> 4) + (j & 7);  // intermediate index inside the tile's 64
-                uint8_t* hst = a.hstage + static_cast<size_t>(sg.w) * a.I * 2 + static_cast<size_t>(t) * N * 128;
+                const int i_loc = 8 * (r >> 4) + (j & 7);  // gate/up: intermediate index inside the tile's 64
+                uint8_t* hst = GATEUP ? a.hstage + static_cast<size_t>(sg.w) * a.I * 2 + static_cast<size_t>(t) * N * 128
+                                      : nullptr;
+                for (int c = 0; c * 16 < N; ++c) {
+                    float dv[16];
+                    tc_ld16(ta + 16 * c, dv);
+                    tc_wait_ld();
 #pragma unroll
-                for (int tok = 0; tok < kSegTok; ++tok) {
-                    if (tok < T) {
-                        const float y = acc[2 * tok] + acc[2 * tok + 1];
-                        const float u = __shfl_down_sync(0xffffffffu, y, 8);
-                        if (j < 8) {
-                            const float h = silu_f(y) * u;
-                            const uint16_t hi = f32_to_bf16(h);
-                            const uint16_t lo = f32_to_bf16(h - bf16_to_f32(hi));
-                            *reinterpret_cast<uint16_t*>(hst + sw128_off(2 * tok, i_loc)) = hi;
-                            *reinterpret_cast<uint16_t*>(hst + sw128_off(2 * tok + 1, i_loc)) = lo;
+                    for (int e = 0; e < 8; ++e) {
+                        const int tok = 8 * c + e;
+                        if (tok < T) {
+                            const float y = dv[2 * e] + dv[2 * e + 1];
+                            if (GATEUP) {
+                                const float up = __shfl_down_sync(0xffffffffu, y, 8);
+                                if (j < 8) {
+                                    uint16_t hi, lo;
+                                    split_f16(silu_f(y) * up, hi, lo, a.err);
+                                    *reinterpret_cast<uint16_t*>(hst + stage_off(2 * tok, i_loc)) = hi;
+                                    *reinterpret_cast<uint16_t*>(hst + stage_off(2 * tok + 1, i_loc)) = lo;
+                                }
+                            } else {
+                                const int ps = a.pair_src[sg.y + tok];
+                                const int src = ps >> 5, k = ps & 31;
+                                float* dst =
+                                    a.ep.eout[src / a.n] + (static_cast<size_t>(src % a.n) * (a.topk + 1) + k) * a.H;
+                                dst[128 * t + r] = y;
+                            }
                         }
                     }
                 }
-            } else {
-                const int o = 128 * t + r;
-#pragma unroll
-                for (int tok = 0; tok < kSegTok; ++tok) {
-                    if (tok < T) {
-                        const int ps = a.pair_src[sg.y + tok];
-                        const int src = ps >> 5, k = ps & 31;
-                        float* dst = a.ep.eout[src / a.n] + (static_cast<size_t>(src % a.n) * (a.topk + 1) + k) * a.H;
-                        dst[o] = acc[2 * tok] + acc[2 * tok + 1];
-                    }
-                }
+                tc_fence_before();
+                mbar_arrive(&acc_empty[dq.i]);
+                dq.next();
+                if (stamp) tc_stamp(a.trace, q_end - 1, 7);
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kTcMmaWarp) {
         tc_fence_after();
-        tc_dealloc(tmem, kTcNACC * kTcAccCols);
+        tc_dealloc(tmem, 512);
     }
     if (!GATEUP && a.ep.world > 1) __threadfence_system();
 }
 
-// ---- staging of the gate/up operand: each segment's token rows as hi/lo bf16 tiles ----
+// ---- staging of the gate/up operand: each segment's token rows as hi/lo fp16 tiles ----
 struct XStageArgs {
     const int4* segs;
     const int* work;
@@ -372,6 +486,7 @@ struct XStageArgs {
     int n, K;
     EpView ep;          // the normalised MoE inputs of every source rank (peer memory: plain loads)
     uint8_t* stage;
+    uint32_t* err;
 };
 
 __global__ void __launch_bounds__(256) b_xstage_kernel(const __grid_constant__ XStageArgs a) {
@@ -379,23 +494,26 @@ __global__ void __launch_bounds__(256) b_xstage_kernel(const __grid_constant__ X
     const int nseg = a.work[0];
     pdl_launch_dependents();
     const int units = a.K / 8;
-    for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < nseg * units; f += gridDim.x * blockDim.x) {
-        const int s = f / units, v = f % units;
+    // segments over grid.y, (token, 16-byte unit) over grid.x: every row unit is one thread
+    for (int s = blockIdx.y; s < nseg; s += gridDim.y) {
         const int4 sg = a.segs[s];
         const int N = seg_cols(sg.z);
-        uint8_t* tile = a.stage + static_cast<size_t>(sg.w) * a.K * 2 + static_cast<size_t>(v >> 3) * N * 128;
-        const int u = v & 7;
-        for (int tok = 0; tok < sg.z; ++tok) {
+        for (int f = blockIdx.x * blockDim.x + threadIdx.x; f < sg.z * units; f += gridDim.x * blockDim.x) {
+            const int tok = f / units, v = f % units;
+            uint8_t* tile = a.stage + static_cast<size_t>(sg.w) * a.K * 2 + static_cast<size_t>(v >> 3) * N * 128;
+            const int u = v & 7;
             const int src = a.pair_src[sg.y + tok] >> 5;
-            const float4* row = reinterpret_cast<const float4*>(a.ep.xn[src / a.n] + static_cast<size_t>(src % a.n) * a.K + 8 * v);
+            const float4* row =
+                reinterpret_cast<const float4*>(a.ep.xn[src / a.n] + static_cast<size_t>(src % a.n) * a.K + 8 * v);
             const float4 f0 = row[0], f1 = row[1];
-            const float x[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+            // the staged order inside a unit: elements [0,4,1,5,2,6,3,7]
+            const float x[8] = {f0.x, f1.x, f0.y, f1.y, f0.z, f1.z, f0.w, f1.w};
             uint32_t hw[4], lw[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const uint16_t h0 = f32_to_bf16(x[2 * i]), h1 = f32_to_bf16(x[2 * i + 1]);
-                const uint16_t l0 = f32_to_bf16(x[2 * i] - bf16_to_f32(h0));
-                const uint16_t l1 = f32_to_bf16(x[2 * i + 1] - bf16_to_f32(h1));
+                uint16_t h0, l0, h1, l1;
+                split_f16(x[2 * i], h0, l0, a.err);
+                split_f16(x[2 * i + 1], h1, l1, a.err);
                 hw[i] = static_cast<uint32_t>(h0) | (static_cast<uint32_t>(h1) << 16);
                 lw[i] = static_cast<uint32_t>(l0) | (static_cast<uint32_t>(l1) << 16);
             }
@@ -451,7 +569,8 @@ cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w
     xs.K = d.H;
     xs.ep = bb.ep;
     xs.stage = bb.xgu;
-    cudaError_t e = launch_kernel(lc, b_xstage_kernel, dim3(4 * lc.num_sms), dim3(256), 0, xs);
+    xs.err = b.err;
+    cudaError_t e = launch_kernel(lc, b_xstage_kernel, dim3(8, lc.num_sms), dim3(256), 0, xs);
     if (e != cudaSuccess) return e;
     TcExpArgs a{};
     a.experts = w.experts;
@@ -465,6 +584,7 @@ cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.I = d.I;
     a.ep = bb.ep;
     a.err = b.err;
+    a.trace = b.trace ? b.trace + kTrCta : nullptr;
     // gate/up: K = H, tiles of 8 chunks (64 gate + 64 up rows)
     a.proj_off = 0;
     a.chunk_bytes = d.gu_chunk_bytes;
@@ -480,6 +600,7 @@ cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.tiles = d.H / 128;
     a.bstage = bb.xdn;
     a.hstage = nullptr;
+    a.trace = b.trace ? b.trace + kTrCta + kTcTraceSlots * kTcTraceGroups : nullptr;
     a.wmap = *static_cast<const CUtensorMap*>(w.tm_dn);
     return launch_tc_proj(lc, d.I, false, a);
 }

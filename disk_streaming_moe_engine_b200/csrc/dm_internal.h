@@ -25,6 +25,7 @@
 #define DM_DEVERR_CAPACITY 0x4u
 #define DM_DEVERR_PAGE 0x8u
 #define DM_DEVERR_TOKEN 0x10u
+#define DM_DEVERR_RANGE 0x20u   // a batched expert operand exceeded the fp16 range (|x| > 65504)
 
 namespace dm {
 
@@ -119,7 +120,7 @@ struct Buffers {
 constexpr int kMaxBatch = 64;       // rows of one rank's batched step
 constexpr int kMaxRanks = 8;        // expert-parallel group (one process per GPU)
 constexpr int kSrcWords = kMaxBatch * kMaxRanks / 64;  // 64-bit words of a source-row mask
-constexpr int kSegTok = 64;         // tokens of one expert segment (hi + lo rows: one 128-column accumulator)
+constexpr int kSegTok = 32;         // tokens of one expert segment (hi + lo rows: 64 accumulator columns)
 constexpr int kHeadChunks = 32;     // vocabulary chunks of the batched argmax
 
 // The expert-parallel group as seen by one rank: every rank runs the same batched step on

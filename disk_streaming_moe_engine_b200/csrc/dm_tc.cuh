@@ -31,6 +31,11 @@ DM_DEV uint32_t tc_idesc_bf16(int M, int N) {
            (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// The same with A and B fp16 (bits [7,10) and [10,13) = 0).
+DM_DEV uint32_t tc_idesc_f16(int M, int N) {
+    return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
 DM_DEV void tc_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, bool accumulate) {
     asm volatile(
@@ -38,6 +43,19 @@ DM_DEV void tc_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint3
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, issued by one thread (kind::f16: bf16 or fp16 operands,
+// as the instruction descriptor says).  A (M = 128) sits in tensor memory with row m in
+// lane m and two consecutive 16-bit K elements per 32-bit column (the lower one in the low
+// half); one K = 16 step reads 8 columns.
+DM_DEV void tc_mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
         : "memory");
 }
 
@@ -74,6 +92,16 @@ DM_DEV void tc_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+// This thread's lane, 16 consecutive 32-bit columns from registers.
+DM_DEV void tc_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+DM_DEV void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 DM_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Byte offset of element k (0..63) of row r in a 128-byte-swizzled K-major tile.

@@ -48,8 +48,22 @@ def batched(a, cfg):
         elif a.kernel == "bgdn":
             layer = next(l for l in range(cfg.num_hidden_layers) if not cfg.is_attention_layer(l))
         ms, nbytes = eng.time_batch_kernel(a.batch, BKERNELS[a.kernel], layer, a.iters)
+        pipe = None
+        if a.trace and a.kernel == "bexperts":
+            # CTA 0's first 32 groups of each expert kernel, SM cycles after the kernel's first
+            # stamp: B issued, MMAs issued, expand start / stores done / arrived, drain waits /
+            # accumulator ready / epilogue done, MMAs issued, commit issued, A ready, B ready
+            eng.trace_enable(True)
+            eng.time_batch_kernel(a.batch, BKERNELS[a.kernel], layer, 1)
+            t = eng.trace_read(64 + 640).astype(np.int64)[64:]
+            eng.trace_enable(False)
+            pipe = {}
+            for name, blk in (("gate_up", t[:320]), ("down", t[320:640])):
+                st = blk.reshape(-1, 10)
+                base = st[st > 0].min() if (st > 0).any() else 0
+                pipe[name] = [[int(v) - int(base) if v else None for v in row] for row in st]
         print(json.dumps({"kernel": a.kernel, "batch": a.batch, "ctx": a.ctx, "layer": layer, "us": ms * 1e3,
-                          "bytes": nbytes, "GBps": nbytes / (ms * 1e-3) / 1e9}))
+                          "bytes": nbytes, "GBps": nbytes / (ms * 1e-3) / 1e9, "pipeline_us": pipe}))
 
 
 def main():

@@ -1,9 +1,9 @@
 """GPU parity of the batched decode step (B sequences, one token each per step).
 
 Each batch row is checked against the CPU oracle run on its own sequence (same seeded
-weights and prompts): identical greedy ids, logits within 1e-3 relative (the batched
-dense projections use the hi/lo bf16 split of fp32 activations, the experts exact
-integer nibbles on the tensor cores).  The rows also agree with the single-sequence
+weights and prompts): identical greedy ids, logits within BATCH_TOL relative (the batched
+dense projections use the hi/lo bf16 split of fp32 activations; the experts run on the
+tcgen05 tensor cores with each weight rounded once to fp16 and fp16 hi/lo activations).  The rows also agree with the single-sequence
 decode step of the same context.  rel(a, b) = max|a - b| / max|b|.
 """
 import numpy as np
@@ -14,6 +14,12 @@ from disk_streaming_moe_engine_b200 import DmError, Engine, RuntimeConfig, _lib,
 pytestmark = pytest.mark.gpu
 
 KERNEL_TOL = 1e-3
+# The batched step's experts round each dequantised weight once to fp16, w = fp16(s (q - z))
+# (relative error <= 2^-12, finer than the reference's own bf16 dequantisation), so that
+# the tensor cores accumulate a whole expert row in one chain; its logits are held to
+# BATCH_TOL against the fp32 oracle (greedy ids identical; the north-star bar on hidden
+# states is 1e-2).
+BATCH_TOL = 3e-3
 
 
 def rel(a, b):
@@ -50,7 +56,7 @@ def _run_batch_vs_oracle(cfg, m, eng, prompt_lens, steps, seed):
         for i in range(n):
             tok_o, lg_o, _ = oracle.decode_step(om, states[i], int(toks[i]))
             assert out[i] == tok_o, (step, i)
-            assert rel(lg[i], lg_o) < KERNEL_TOL, (step, i, rel(lg[i], lg_o))
+            assert rel(lg[i], lg_o) < BATCH_TOL, (step, i, rel(lg[i], lg_o))
         toks = out
     for i, L in enumerate(prompt_lens):
         assert eng.seq_len(i) == L + steps

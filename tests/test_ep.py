@@ -16,6 +16,12 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 KERNEL_TOL = 1e-3
+# The batched step's experts round each dequantised weight once to fp16, w = fp16(s (q - z))
+# (relative error <= 2^-12, finer than the reference's own bf16 dequantisation), so that
+# the tensor cores accumulate a whole expert row in one chain; its logits are held to
+# BATCH_TOL against the fp32 oracle (greedy ids identical; the north-star bar on hidden
+# states is 1e-2).
+BATCH_TOL = 3e-3
 N_ROWS, STEPS = 3, 4
 
 
@@ -107,4 +113,4 @@ def test_ep_two_gpus_matches_oracle(oracle_lib):
                 tok, lg_o, _ = oracle.decode_step(om, st, int(tin[i]))
                 assert tout[i] == tok, (r, i, s)
                 err = float(np.abs(lg[i] - lg_o).max() / np.abs(lg_o).max())
-                assert err < KERNEL_TOL, (r, i, s, err)
+                assert err < BATCH_TOL, (r, i, s, err)

@@ -22,6 +22,12 @@ from disk_streaming_moe_engine_b200 import Engine, RuntimeConfig, preset, synth
 pytestmark = pytest.mark.gpu
 
 KERNEL_TOL = 1e-3
+# The batched step's experts round each dequantised weight once to fp16, w = fp16(s (q - z))
+# (relative error <= 2^-12, finer than the reference's own bf16 dequantisation), so that
+# the tensor cores accumulate a whole expert row in one chain; its logits are held to
+# BATCH_TOL against the fp32 oracle (greedy ids identical; the north-star bar on hidden
+# states is 1e-2).
+BATCH_TOL = 3e-3
 HIDDEN_TOL = 1e-2
 
 
@@ -33,7 +39,7 @@ def test_batched_long_context_permuted_pages_matches_oracle(lib, oracle_lib):
     """Full block shapes (2 blocks: GDN, attention 16/2 x 256), 4 rows with 32768, 8192,
     8195 and 12000 cached tokens (random bf16 K/V, random GDN states and conv windows),
     page tables drawn from one permutation of the pool; 3 batched steps.  Every row:
-    the oracle's greedy ids, logits within 1e-3, the appended K/V within one bf16
+    the oracle's greedy ids, logits within BATCH_TOL, the appended K/V within one bf16
     rounding, the GDN state within 1e-3."""
     import oracle
     cfg = preset("layer")
@@ -78,7 +84,7 @@ def test_batched_long_context_permuted_pages_matches_oracle(lib, oracle_lib):
             for i in range(n):
                 tok_o, lg_o, _ = oracle.decode_step(om, states[i], int(toks[i]))
                 assert out[i] == tok_o, (step, i)
-                assert rel(lg[i], lg_o) < KERNEL_TOL, (step, i, rel(lg[i], lg_o))
+                assert rel(lg[i], lg_o) < BATCH_TOL, (step, i, rel(lg[i], lg_o))
             toks = out
         for i, L in enumerate(lens):
             assert eng.seq_len(i) == L + steps
