@@ -22,8 +22,6 @@ LIB_PATH = os.path.join(PKG_DIR, "libdismoen_cuda.so")
 INCLUDE = os.path.join(REPO_DIR, "include")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-# cuBLAS (the batched step's dense projections) resolves from the toolkit when no other
-# copy of the library is loaded in the process
 CUDA_LIB = "/usr/local/cuda/lib64"
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
               "--expt-relaxed-constexpr", "-diag-suppress", "177"]
@@ -72,7 +70,7 @@ def build(verbose: bool = False, force: bool = False, extra_flags: list[str] | N
             if verbose and out.strip():
                 print(out)
     if jobs or not os.path.exists(LIB_PATH):
-        cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", LIB_PATH, *objs, "-lcudart", "-lcublas",
+        cmd = [nvcc, *ARCH_FLAGS, "-shared", "-o", LIB_PATH, *objs, "-lcudart",
                "-Xlinker", "-rpath," + CUDA_LIB]
         run(cmd)
     return LIB_PATH

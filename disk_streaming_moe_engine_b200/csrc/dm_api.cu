@@ -5,7 +5,6 @@
 // kernels are issued on the context stream with programmatic dependent launch; the decode
 // step (embedding, all blocks, head) is captured once per sequence slot into a CUDA graph
 // and replayed per token.
-#include <cublas_v2.h>
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -63,6 +62,7 @@ using namespace dm;
 struct dm_ctx {
     CUtensorMap kv_map{};  // 2-D tiled view of the KV arena for the attention page copies
     std::vector<CUtensorMap> xmaps;  // [L][2] the expert pools' nibble rows (gate/up, down)
+    std::vector<CUtensorMap> dmaps;  // [L][2] + 1: dense weights (input, output projection; lm_head last)
     dm_model_config mc{};
     dm_runtime_config rc{};
     Dims d{};
@@ -108,9 +108,6 @@ struct dm_ctx {
     // batched decode: scratch, the GEMM library handle on the context stream (workspace in
     // the arena, so capture into a graph allocates nothing), one graph per (rows, logits)
     BatchBuffers bb{};
-    cublasHandle_t blas = nullptr;
-    void* blas_ws = nullptr;
-    size_t blas_ws_bytes = 0;
     std::vector<cudaGraphExec_t> bgraphs;  // [2 * (cap + 1)]
     int* h_bio = nullptr;                  // pinned [4 * kMaxBatch]: slots, tokens in, tokens out
     float* rbias = nullptr;                // [L][E] router logit offsets (dm_set_router_bias)
@@ -325,7 +322,9 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const int max_segs = static_cast<int>((P + kSegTok - 1) / kSegTok) + std::min(d.E, static_cast<int>(P)) + 2;
     const int bgen_cap = 1 << 16;
     const size_t ob_slots = T(BC * 4), ob_tok = T(BC * 4), ob_x = T(BC * H * 4), ob_xm = T(BC * H * 4);
-    const size_t ob_xcat = T(2 * BC * kmax * 2), ob_c = T(2 * BC * nmax * 4);
+    // GEMM operand rows rounded up to 16 (the tensor map's box never leaves the buffer)
+    const size_t xrows = (2 * BC + 15) / 16 * 16;
+    const size_t ob_xcat = T(xrows * kmax * 2), ob_c = T(2 * BC * nmax * 4);
     const size_t ob_z = T(BC * d.z_dim * 4), ob_ab = T(BC * 2 * d.nv * 4), ob_o = T(BC * d.z_dim * 4);
     const size_t ob_qg = T(BC * 2 * d.Hq * d.D * 4), ob_kvn = T(BC * 2 * d.Hkv * d.D * 4);
     const size_t ob_part = T(BC * d.Hq * kMaxSplits * (d.D + 2) * 4), ob_aout = T(BC * d.Hq * d.D * 4);
@@ -341,8 +340,6 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t ob_cv = T(BC * kHeadChunks * 4), ob_ci = T(BC * kHeadChunks * 4), ob_hl = T(BC * d.V * 4);
     const size_t ob_gen = T(static_cast<size_t>(bgen_cap) * 4), ob_genidx = T(4);
     const size_t o_rbias = T(static_cast<size_t>(d.L) * d.E * 4);
-    const size_t blas_ws = static_cast<size_t>(32) << 20;
-    const size_t ob_ws = T(blas_ws);
     c->arena_bytes = p.off;
     if (!commit) return DM_OK;
 
@@ -457,9 +454,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     bb.gen_idx = reinterpret_cast<int*>(A + ob_genidx);
     bb.gen_cap = bgen_cap;
     set_local_ep(c);
-    c->blas_ws = A + ob_ws;
     c->rbias = reinterpret_cast<float*>(A + o_rbias);
-    c->blas_ws_bytes = blas_ws;
     return DM_OK;
 }
 
@@ -588,6 +583,46 @@ static bool encode_expert_maps(dm_ctx* c) {
     return true;
 }
 
+// Tensor maps of every dense weight matrix for the batched step's tensor-core GEMMs: bf16
+// rows of K elements, boxes of 128 rows x 64 columns (128 bytes) with the 128-byte swizzle.
+static bool encode_dense_maps(dm_ctx* c) {
+    const Dims& d = c->d;
+    c->dmaps.assign(static_cast<size_t>(d.L) * 2 + 1, CUtensorMap{});
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    auto one = [&](CUtensorMap* m, const uint16_t* w, int N, int K) {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+        const cuuint32_t box[2] = {64, 128};
+        const cuuint32_t estr[2] = {1, 1};
+        return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(w), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    for (int l = 0; l < d.L; ++l) {
+        const LayerW& w = c->layers[l];
+        const int nin = w.is_attn ? d.attn_in_rows : d.gdn_in_rows;
+        const int kout = w.is_attn ? d.Hq * d.D : d.z_dim;
+        if (!one(&c->dmaps[2 * l], w.w_in, nin, d.H) || !one(&c->dmaps[2 * l + 1], w.w_out, d.H, kout)) return false;
+    }
+    return one(&c->dmaps[2 * d.L], c->lm_head, d.V, d.H);
+}
+
+// The batched step's GEMM operand rows (xcat: 2n rows of K bf16, packed with row stride K by
+// the prep and merge kernels) as a tensor map with boxes of ntile rows x 64 columns.
+static bool encode_operand_map(dm_ctx* c, int K, int ncols, CUtensorMap* m) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const int rows = (2 * c->bb.cap + 15) / 16 * 16;  // the buffer holds rows x kmax >= rows x K elements
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>((ncols + 15) / 16 * 16)};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c->bb.xcat, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static bool encode_kv_map(dm_ctx* c) {
     c->b.kv_tmap = &c->kv_map;
     const Dims& d = c->d;
@@ -663,6 +698,7 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     // per-context value that a later, smaller context would lower
     if (e == cudaSuccess) e = attn_set_attrs(kAttnMaxScoreSmem);
     if (e == cudaSuccess) e = batch_set_attrs();
+    if (e == cudaSuccess) e = tc_gemm_set_attrs();
     bool moe_fits = false;
     if (e == cudaSuccess) e = moe_fused_fits(c->d, c->num_sms, &moe_fits);
     if (e == cudaSuccess) c->gdn_fused = gdn_fused_fits(c->d, c->num_sms);
@@ -708,6 +744,7 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     }
     if (e == cudaSuccess && !encode_kv_map(c)) e = cudaErrorInvalidValue;
     if (e == cudaSuccess && !encode_expert_maps(c)) e = cudaErrorInvalidValue;
+    if (e == cudaSuccess && !encode_dense_maps(c)) e = cudaErrorInvalidValue;
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     if (e != cudaSuccess) {
         fprintf(stderr, "dm_ctx_create: %s\n", cudaGetErrorString(e));
@@ -719,23 +756,6 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
         cudaFree(c->arena);
         delete c;
         return DM_ERR_CUDA;
-    }
-    {
-        cublasStatus_t bs = cublasCreate(&c->blas);
-        if (bs == CUBLAS_STATUS_SUCCESS) bs = cublasSetStream(c->blas, c->stream);
-        if (bs == CUBLAS_STATUS_SUCCESS) bs = cublasSetWorkspace(c->blas, c->blas_ws, c->blas_ws_bytes);
-        if (bs != CUBLAS_STATUS_SUCCESS) {
-            fprintf(stderr, "dm_ctx_create: cuBLAS set-up failed (status %d)\n", static_cast<int>(bs));
-            if (c->blas) cublasDestroy(c->blas);
-            cudaFreeHost(c->h_io);
-            cudaFreeHost(c->h_bio);
-            if (c->host_pool) cudaFreeHost(c->host_pool);
-            if (c->h_slot_of) cudaFreeHost(c->h_slot_of);
-            if (c->h_sids) cudaFreeHost(c->h_sids);
-            cudaFree(c->arena);
-            delete c;
-            return DM_ERR_CUDA;
-        }
     }
     c->bgraphs.assign(2 * (c->bb.cap + 1), nullptr);
     c->have_dense.assign(static_cast<size_t>(c->d.L + 1) * DM_T_COUNT, 0);
@@ -766,7 +786,6 @@ int32_t dm_ctx_destroy(dm_ctx* c) {
         if (g) cudaGraphExecDestroy(g);
     for (uint8_t* pa : c->peer_arena)
         if (pa) cudaIpcCloseMemHandle(pa);
-    if (c->blas) cublasDestroy(c->blas);
     if (c->h_bio) cudaFreeHost(c->h_bio);
     if (c->arena) cudaFree(c->arena);
     if (c->flush_buf) cudaFree(c->flush_buf);
@@ -2054,16 +2073,21 @@ int32_t dm_forward(dm_ctx* c, int32_t slot, const int32_t* tokens, int32_t n, fl
 }
 
 // ---- batched decode ---------------------------------------------------------------------
-// One step of n sequences (rows): dense projections as bf16 tensor-core GEMMs of the hi/lo
-// split rows (cuBLAS, plain library GEMMs), the per-row kernels of dm_batch.cu, the GDN
-// recurrence and the attention with a row dimension, the experts on the tensor cores.
-static cudaError_t bgemm(dm_ctx* c, const uint16_t* W, int N, int K, int n) {
-    const float one = 1.0f, zero = 0.0f;
-    // C[2n][N] (row-major) = Xcat[2n][K] . W[N][K]^T, i.e. column-major C^T = W^T-op . Xcat
-    const cublasStatus_t s = cublasGemmEx(c->blas, CUBLAS_OP_T, CUBLAS_OP_N, N, 2 * n, K, &one, W, CUDA_R_16BF, K,
-                                          c->bb.xcat, CUDA_R_16BF, K, &zero, c->bb.c, CUDA_R_32F, N,
-                                          CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-    return s == CUBLAS_STATUS_SUCCESS ? cudaSuccess : cudaErrorUnknown;
+// One step of n sequences (rows): dense projections on the tensor cores (dm_gemm_tc.cu:
+// weights streamed once per step, the rows' hi/lo operand as the MMA's N), the per-row
+// kernels of dm_batch.cu, the GDN recurrence and the attention with a row dimension, the
+// experts on the tensor cores (dm_expert_tc.cu).
+// C = Xcat . W^T for dense matrix `map` ([N][K]) into bb.c as *splits partials.
+static cudaError_t bgemm(dm_ctx* c, int map, int N, int K, int n, int* splits, int max_splits = 16) {
+    CUtensorMap xm;
+    if (!encode_operand_map(c, K, 2 * n, &xm)) return cudaErrorInvalidValue;
+    const size_t nmax = std::max({static_cast<size_t>(c->d.gdn_in_rows), static_cast<size_t>(c->d.attn_in_rows),
+                                  static_cast<size_t>(c->d.H), static_cast<size_t>(c->d.V)});
+    // the partials share the result buffer: S x 2n x N <= 2 cap x nmax
+    const int max_s = static_cast<int>(std::min<size_t>(max_splits, (2 * static_cast<size_t>(c->bb.cap) * nmax) /
+                                                                (2 * static_cast<size_t>(n) * N)));
+    *splits = tc_gemm_splits((N + 127) / 128, K, c->num_sms, std::max(1, max_s));
+    return launch_tc_gemm(lcfg(c), &c->dmaps[map], &xm, c->bb.c, N, K, 2 * n, *splits, c->b.err);
 }
 
 // The token mixer of layer l for n rows, through its residual: x -> xm.
@@ -2073,23 +2097,24 @@ static cudaError_t enqueue_b_mixer(dm_ctx* c, int l, int n) {
     const LaunchCfg lc = lcfg(c);
     const LayerW& w = c->layers[l];
     cudaError_t e = cudaSuccess;
+    int sp = 1;
     if (w.is_attn) {
         if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
-        if (e == cudaSuccess) e = bgemm(c, w.w_in, d.attn_in_rows, d.H, n);
-        if (e == cudaSuccess) e = launch_b_epi_attn_in(lc, d, bb, n);
+        if (e == cudaSuccess) e = bgemm(c, 2 * l, d.attn_in_rows, d.H, n, &sp);
+        if (e == cudaSuccess) e = launch_b_epi_attn_in(lc, d, bb, n, sp);
         if (e == cudaSuccess) e = launch_attn_decode_batch(lc, d, w, bb, c->b, n);
         if (e == cudaSuccess) e = launch_attn_merge_batch(lc, d, bb, n);
-        if (e == cudaSuccess) e = bgemm(c, w.w_out, d.H, d.Hq * d.D, n);
+        if (e == cudaSuccess) e = bgemm(c, 2 * l + 1, d.H, d.Hq * d.D, n, &sp);
     } else {
         if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
-        if (e == cudaSuccess) e = bgemm(c, w.w_in, d.gdn_in_rows, d.H, n);
-        if (e == cudaSuccess) e = launch_b_epi_gdn_in(lc, d, w, bb, c->b, n);
+        if (e == cudaSuccess) e = bgemm(c, 2 * l, d.gdn_in_rows, d.H, n, &sp);
+        if (e == cudaSuccess) e = launch_b_epi_gdn_in(lc, d, w, bb, c->b, n, sp);
         if (e == cudaSuccess) e = launch_gdn_rec_batch(lc, d, w, bb, c->b, n);
         if (e == cudaSuccess)
             e = launch_b_prep(lc, BPREP_HEADNORM, bb.o, d.z_dim, nullptr, d.eps, bb.z, w.gdn_norm, d.dv, bb.xcat, n);
-        if (e == cudaSuccess) e = bgemm(c, w.w_out, d.H, d.z_dim, n);
+        if (e == cudaSuccess) e = bgemm(c, 2 * l + 1, d.H, d.z_dim, n, &sp);
     }
-    if (e == cudaSuccess) e = launch_b_epi_resid(lc, bb.c, d.H, bb.x, bb.xm, n);
+    if (e == cudaSuccess) e = launch_b_epi_resid(lc, bb.c, d.H, bb.x, bb.xm, n, sp);
     return e;
 }
 
@@ -2111,7 +2136,9 @@ static cudaError_t enqueue_b_head(dm_ctx* c, int n, int write_logits) {
     BatchBuffers& bb = c->bb;
     const LaunchCfg lc = lcfg(c);
     cudaError_t e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, c->final_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
-    if (e == cudaSuccess) e = bgemm(c, c->lm_head, d.V, d.H, n);
+    int sp = 1;
+    if (e == cudaSuccess) e = bgemm(c, 2 * d.L, d.V, d.H, n, &sp, 1);
+    if (e == cudaSuccess && sp != 1) e = cudaErrorInvalidValue;  // the argmax reads one product
     if (e == cudaSuccess) e = launch_b_argmax(lc, d, bb, c->b, n, write_logits, 1);
     return e;
 }
@@ -2485,11 +2512,12 @@ int32_t dm_batch_stats(dm_ctx* c, int32_t reset, uint32_t* out4) {
 
 int32_t dm_batch_kernels_per_step(dm_ctx* c, int32_t n, int32_t* own, int32_t* gemms) {
     if (!c || !own || !gemms || n <= 0 || n > c->bb.cap) return DM_ERR_INVALID_ARG;
-    // embed; per block: prep, epilogue, mixer core (recurrence or attention), prep,
-    // residual epilogue, router, top-k + grouping, gate/up, down, combine; head: prep,
-    // two argmax kernels.  GEMMs: two per block and the head.
-    *own = 1 + 10 * c->d.L + 3;
-    *gemms = 2 * c->d.L + 1;
+    // embed; per block: prep, input GEMM, epilogue, mixer core (recurrence, or attention +
+    // split merge), (head-norm prep,) output GEMM, residual epilogue, router, top-k +
+    // grouping, operand staging, gate/up, down, combine = 13; head: prep, GEMM, two argmax
+    // kernels.  No library GEMMs.
+    *own = 1 + 13 * c->d.L + 4;
+    *gemms = 0;
     return DM_OK;
 }
 

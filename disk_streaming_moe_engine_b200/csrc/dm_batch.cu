@@ -123,8 +123,8 @@ cudaError_t launch_b_prep(const LaunchCfg& lc, int mode, const float* x, int K, 
 
 // ---- GEMM epilogues: v = C[b][col] + C[n + b][col] -------------------------------------
 struct BEpiArgs {
-    const float* c;    // [2n][N]
-    int N, n;
+    const float* c;    // [S][2n][N]: S partial products over slices of K
+    int N, n, splits;
     // GDN input projection: [qkv | z | a b] -> conv ring slot pos % 4, SiLU(z), a b
     float* ring;       // layer base [max_seqs][4][qkv_dim]
     const int* slots;
@@ -148,7 +148,12 @@ __global__ void __launch_bounds__(256) b_epi_kernel(const __grid_constant__ BEpi
     pdl_wait();
     pdl_launch_dependents();
     if (col >= a.N) return;
-    const float v = a.c[static_cast<size_t>(b) * a.N + col] + a.c[static_cast<size_t>(a.n + b) * a.N + col];
+    // the S slices in order, hi + lo of each: the sum does not depend on timing
+    float v = 0.0f;
+    for (int s = 0; s < a.splits; ++s) {
+        const float* cs = a.c + static_cast<size_t>(s) * 2 * a.n * a.N;
+        v += cs[static_cast<size_t>(b) * a.N + col] + cs[static_cast<size_t>(a.n + b) * a.N + col];
+    }
     if (MODE == BEPI_GDN_IN) {
         if (col < a.qkv_dim) {
             const int slot = a.slots[b];
@@ -169,11 +174,12 @@ __global__ void __launch_bounds__(256) b_epi_kernel(const __grid_constant__ BEpi
 }
 
 cudaError_t launch_b_epi_gdn_in(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
-                                const Buffers& b, int n) {
+                                const Buffers& b, int n, int splits) {
     BEpiArgs a{};
     a.c = bb.c;
     a.N = d.gdn_in_rows;
     a.n = n;
+    a.splits = splits;
     a.ring = b.ring + static_cast<size_t>(w.sub) * d.max_seqs * kConvRing * d.qkv_dim;
     a.slots = bb.slots;
     a.pos = b.pos;
@@ -184,22 +190,25 @@ cudaError_t launch_b_epi_gdn_in(const LaunchCfg& lc, const Dims& d, const LayerW
     return launch_kernel(lc, b_epi_kernel<BEPI_GDN_IN>, dim3((a.N + 255) / 256, n), dim3(256), 0, a);
 }
 
-cudaError_t launch_b_epi_attn_in(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, int n) {
+cudaError_t launch_b_epi_attn_in(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, int n, int splits) {
     BEpiArgs a{};
     a.c = bb.c;
     a.N = d.attn_in_rows;
     a.n = n;
+    a.splits = splits;
     a.qg = bb.qg;
     a.kvnew = bb.kvnew;
     a.qg_rows = 2 * d.Hq * d.D;
     return launch_kernel(lc, b_epi_kernel<BEPI_ATTN_IN>, dim3((a.N + 255) / 256, n), dim3(256), 0, a);
 }
 
-cudaError_t launch_b_epi_resid(const LaunchCfg& lc, const float* c, int N, const float* res, float* out, int n) {
+cudaError_t launch_b_epi_resid(const LaunchCfg& lc, const float* c, int N, const float* res, float* out, int n,
+                              int splits) {
     BEpiArgs a{};
     a.c = c;
     a.N = N;
     a.n = n;
+    a.splits = splits;
     a.res = res;
     a.out = out;
     return launch_kernel(lc, b_epi_kernel<BEPI_RESID>, dim3((N + 255) / 256, n), dim3(256), 0, a);

@@ -258,9 +258,16 @@ cudaError_t launch_b_embed(const LaunchCfg& lc, const Dims& d, const uint16_t* e
 cudaError_t launch_b_prep(const LaunchCfg& lc, int mode, const float* x, int K, const uint16_t* gamma, float eps,
                           const float* z, const uint16_t* hw, int dv, uint16_t* xcat, int n);
 cudaError_t launch_b_epi_gdn_in(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
-                                const Buffers& b, int n);
-cudaError_t launch_b_epi_attn_in(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, int n);
-cudaError_t launch_b_epi_resid(const LaunchCfg& lc, const float* c, int N, const float* res, float* out, int n);
+                                const Buffers& b, int n, int splits);
+cudaError_t launch_b_epi_attn_in(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, int n, int splits);
+cudaError_t launch_b_epi_resid(const LaunchCfg& lc, const float* c, int N, const float* res, float* out, int n,
+                              int splits);
+// Dense projection of the batched step on the tensor cores: c[S][ncols][N] partials of
+// X[ncols][K] . W[N][K]^T (tensor maps of W and of the operand rows, see dm_gemm_tc.cu).
+cudaError_t tc_gemm_set_attrs();
+int tc_gemm_splits(int tiles, int K, int num_sms, int max_splits);
+cudaError_t launch_tc_gemm(const LaunchCfg& lc, const void* wmap, const void* xmap, float* c, int N, int K, int ncols,
+                           int splits, uint32_t* err);
 cudaError_t launch_gdn_rec_batch(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
                                  const Buffers& b, int n);
 cudaError_t launch_attn_decode_batch(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
