@@ -26,7 +26,7 @@ DM_ERR_FORMAT = 11
 
 DM_KERNEL_MIXER_IN, DM_KERNEL_MIXER_OUT, DM_KERNEL_MIXER_CORE = 0, 1, 2
 DM_KERNEL_ROUTER, DM_KERNEL_MOE, DM_KERNEL_HEAD = 3, 4, 6
-DM_BKERNEL_ATTN, DM_BKERNEL_GDN_REC, DM_BKERNEL_EXPERTS = 0, 1, 2
+DM_BKERNEL_ATTN, DM_BKERNEL_GDN_REC, DM_BKERNEL_EXPERTS, DM_BKERNEL_ROUTER, DM_BKERNEL_GEMM_IN = 0, 1, 2, 3, 4
 DM_EP_HANDLE_BYTES = 64
 
 DM_GGML_F32, DM_GGML_F16, DM_GGML_Q8_0, DM_GGML_Q3_K, DM_GGML_Q4_K, DM_GGML_BF16 = 0, 1, 8, 11, 12, 30
@@ -110,6 +110,8 @@ SIGNATURES = {
     "dm_mixer_block": (I32, [P, I32, I32, I32, P, I32, P]),
     "dm_block_forward": (I32, [P, I32, I32, I32, P, I32, P]),
     "dm_forward": (I32, [P, I32, P, I32, P, C.POINTER(I32)]),
+    "dm_prefill": (I32, [P, I32, P, I32, P, C.POINTER(I32)]),
+    "dm_prefill_rows": (I32, [P, C.POINTER(I32), C.POINTER(I32)]),
     "dm_decode_step": (I32, [P, I32, I32, C.POINTER(I32), P]),
     "dm_generate": (I32, [P, I32, I32, I32, P]),
     "dm_enqueue_decode": (I32, [P, I32, I32]),

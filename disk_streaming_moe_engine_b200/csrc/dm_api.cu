@@ -108,6 +108,7 @@ struct dm_ctx {
     // batched decode: scratch, the GEMM library handle on the context stream (workspace in
     // the arena, so capture into a graph allocates nothing), one graph per (rows, logits)
     BatchBuffers bb{};
+    BatchBuffers pb{};  // prefill chunk scratch (rows = prompt tokens of one sequence)
     std::vector<cudaGraphExec_t> bgraphs;  // [2 * (cap + 1)]
     int* h_bio = nullptr;                  // pinned [4 * kMaxBatch]: slots, tokens in, tokens out
     float* rbias = nullptr;                // [L][E] router logit offsets (dm_set_router_bias)
@@ -340,6 +341,29 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t ob_cv = T(BC * kHeadChunks * 4), ob_ci = T(BC * kHeadChunks * 4), ob_hl = T(BC * d.V * 4);
     const size_t ob_gen = T(static_cast<size_t>(bgen_cap) * 4), ob_genidx = T(4);
     const size_t o_rbias = T(static_cast<size_t>(d.L) * d.E * 4);
+    // prefill chunk scratch: PR rows (prompt tokens of one sequence), no more than the
+    // grouping kernel takes or the context can hold
+    const size_t PR = static_cast<size_t>(std::min({kPfMaxRows, b_group_max_rows(d.E),
+                                                    (d.max_pages * kPageTokens + 15) / 16 * 16}));
+    const size_t nmax_dense = std::max({static_cast<size_t>(d.gdn_in_rows), static_cast<size_t>(d.attn_in_rows),
+                                        static_cast<size_t>(d.H)});
+    const size_t PP = PR * d.topk + PR;
+    const int pmax_segs = static_cast<int>((PP + kSegTok - 1) / kSegTok) + std::min(d.E, static_cast<int>(PP)) + 2;
+    const size_t pmax_cols = 2 * PP + 16 * static_cast<size_t>(pmax_segs);
+    const size_t pc_cap = std::max(2 * PR * nmax_dense, 2 * static_cast<size_t>(d.V));  // the head: one row
+    const size_t op_slots = T(PR * 4), op_tok = T(PR * 4), op_x = T(PR * H * 4), op_xm = T(PR * H * 4);
+    const size_t op_xcat = T((2 * PR + 15) / 16 * 16 * kmax * 2), op_c = T(pc_cap * 4);
+    const size_t op_z = T(PR * d.z_dim * 4), op_ab = T(PR * 2 * d.nv * 4), op_o = T(PR * d.z_dim * 4);
+    const size_t op_qg = T(PR * 2 * d.Hq * d.D * 4), op_kvn = T(PR * 2 * d.Hkv * d.D * 4);
+    const size_t op_part = T(PR * d.Hq * kPfMaxSplits * (d.D + 2) * 4);
+    const size_t op_xn = T(PR * H * 4), op_lg = T(PR * (d.E + 1) * 4);
+    const size_t op_ids = T(PR * d.topk * 4), op_pr = T(PR * d.topk * 4), op_sg = T(PR * 4);
+    const size_t op_segs = T(static_cast<size_t>(pmax_segs) * 16), op_work = T(16), op_stats = T(16);
+    const size_t op_rcnt = T((PR + 1) * 4), op_psrc = T(PP * 4), op_eout = T(PR * (d.topk + 1) * H * 4);
+    const size_t op_xgu = T(pmax_cols * H * 2), op_xdn = T(pmax_cols * d.I * 2);
+    const size_t op_cv = T(kHeadChunks * 4), op_ci = T(kHeadChunks * 4), op_hl = T(static_cast<size_t>(d.V) * 4);
+    const size_t op_gen = T(16), op_genidx = T(4);
+    const size_t op_raw = T(PR * d.qkv_dim * 4), op_qhi = T(PR * d.Hq * d.D * 2), op_qlo = T(PR * d.Hq * d.D * 2);
     c->arena_bytes = p.off;
     if (!commit) return DM_OK;
 
@@ -453,6 +477,52 @@ static int plan_memory(dm_ctx* c, bool commit) {
     bb.gen_out = reinterpret_cast<int*>(A + ob_gen);
     bb.gen_idx = reinterpret_cast<int*>(A + ob_genidx);
     bb.gen_cap = bgen_cap;
+    bb.c_cap = 2 * BC * nmax;
+    BatchBuffers& pb = c->pb;
+    pb.cap = static_cast<int>(PR);
+    pb.max_segs = pmax_segs;
+    pb.max_pairs = static_cast<int>(PP);
+    pb.max_cols = static_cast<int>(pmax_cols);
+    pb.c_cap = pc_cap;
+    pb.slots = reinterpret_cast<int*>(A + op_slots);
+    pb.tok = reinterpret_cast<int*>(A + op_tok);
+    pb.x = reinterpret_cast<float*>(A + op_x);
+    pb.xm = reinterpret_cast<float*>(A + op_xm);
+    pb.xcat = reinterpret_cast<uint16_t*>(A + op_xcat);
+    pb.c = reinterpret_cast<float*>(A + op_c);
+    pb.z = reinterpret_cast<float*>(A + op_z);
+    pb.ab = reinterpret_cast<float*>(A + op_ab);
+    pb.o = reinterpret_cast<float*>(A + op_o);
+    pb.qg = reinterpret_cast<float*>(A + op_qg);
+    pb.kvnew = reinterpret_cast<float*>(A + op_kvn);
+    pb.attn_part = reinterpret_cast<float*>(A + op_part);
+    pb.attn_out = nullptr;
+    pb.attn_cnt = nullptr;
+    pb.xn = reinterpret_cast<float*>(A + op_xn);
+    pb.logits = reinterpret_cast<float*>(A + op_lg);
+    pb.ids = reinterpret_cast<int*>(A + op_ids);
+    pb.probs = reinterpret_cast<float*>(A + op_pr);
+    pb.sg = reinterpret_cast<float*>(A + op_sg);
+    pb.segs = reinterpret_cast<int4*>(A + op_segs);
+    pb.work = reinterpret_cast<int*>(A + op_work);
+    pb.stats = reinterpret_cast<unsigned*>(A + op_stats);
+    pb.rcnt = reinterpret_cast<unsigned*>(A + op_rcnt);
+    pb.err = b.err;
+    pb.pair_src = reinterpret_cast<int*>(A + op_psrc);
+    pb.ep_flags = bb.ep_flags;
+    pb.ep_epoch = bb.ep_epoch;
+    pb.xgu = A + op_xgu;
+    pb.xdn = A + op_xdn;
+    pb.eout = reinterpret_cast<float*>(A + op_eout);
+    pb.cand_val = reinterpret_cast<float*>(A + op_cv);
+    pb.cand_idx = reinterpret_cast<int*>(A + op_ci);
+    pb.head_logits = reinterpret_cast<float*>(A + op_hl);
+    pb.gen_out = reinterpret_cast<int*>(A + op_gen);
+    pb.gen_idx = reinterpret_cast<int*>(A + op_genidx);
+    pb.gen_cap = 0;
+    pb.pf_raw = reinterpret_cast<float*>(A + op_raw);
+    pb.pf_qhi = reinterpret_cast<uint16_t*>(A + op_qhi);
+    pb.pf_qlo = reinterpret_cast<uint16_t*>(A + op_qlo);
     set_local_ep(c);
     c->rbias = reinterpret_cast<float*>(A + o_rbias);
     return DM_OK;
@@ -518,6 +588,15 @@ static void set_local_ep(dm_ctx* c) {
     v.eout[0] = bb.eout;
     v.flags[0] = bb.ep_flags;
     bb.ep = v;
+    BatchBuffers& pb = c->pb;  // prefill: always this rank alone
+    EpView pv{};
+    pv.rank = 0;
+    pv.world = 1;
+    pv.ids[0] = pb.ids;
+    pv.xn[0] = pb.xn;
+    pv.eout[0] = pb.eout;
+    pv.flags[0] = pb.ep_flags;
+    pb.ep = pv;
 }
 
 // Tensor map of the KV arena for the attention kernel's page copies: rows of D bf16
@@ -610,15 +689,16 @@ static bool encode_dense_maps(dm_ctx* c) {
 
 // The batched step's GEMM operand rows (xcat: 2n rows of K bf16, packed with row stride K by
 // the prep and merge kernels) as a tensor map with boxes of ntile rows x 64 columns.
-static bool encode_operand_map(dm_ctx* c, int K, int ncols, CUtensorMap* m) {
+static bool encode_operand_map(const BatchBuffers& bb, int K, int ncols, CUtensorMap* m) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
-    const int rows = (2 * c->bb.cap + 15) / 16 * 16;  // the buffer holds rows x kmax >= rows x K elements
+    const int rows = (2 * bb.cap + 15) / 16 * 16;  // the buffer holds rows x kmax >= rows x K elements
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>((ncols + 15) / 16 * 16)};
+    // one column tile of at most 128 rows (the GEMM loads tile ct at row 128 ct)
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(ncols > 128 ? 128 : (ncols + 15) / 16 * 16)};
     const cuuint32_t estr[2] = {1, 1};
-    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c->bb.xcat, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, bb.xcat, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -698,6 +778,7 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     // per-context value that a later, smaller context would lower
     if (e == cudaSuccess) e = attn_set_attrs(kAttnMaxScoreSmem);
     if (e == cudaSuccess) e = batch_set_attrs();
+    if (e == cudaSuccess) e = pf_attn_set_attrs();
     if (e == cudaSuccess) e = tc_gemm_set_attrs();
     bool moe_fits = false;
     if (e == cudaSuccess) e = moe_fused_fits(c->d, c->num_sms, &moe_fits);
@@ -2072,22 +2153,64 @@ int32_t dm_forward(dm_ctx* c, int32_t slot, const int32_t* tokens, int32_t n, fl
     return rc;
 }
 
+static cudaError_t enqueue_pf_chunk(dm_ctx* c, int slot, int pos0, int n, bool head, int write_logits);
+static int pf_kernels_per_chunk(const Dims& d);
+
+int32_t dm_prefill(dm_ctx* c, int32_t slot, const int32_t* tokens, int32_t n, float* logits, int32_t* next) {
+    if (!c || !tokens || n <= 0) return DM_ERR_INVALID_ARG;
+    if (spilling(c)) return spill_reject(c, "dm_prefill");
+    int rc = prepare_decode(c, slot, n);
+    if (rc != DM_OK) return rc;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= c->d.V)
+            return set_err(c, DM_ERR_INVALID_ARG, "M4_ERR_INPUT", "input", -1, "token %d at index %d out of range [0, %d)",
+                           tokens[i], i, c->d.V);
+    const int R = c->pb.cap;
+    const int pos_start = c->slot_len[slot];
+    c->h_io[4] = slot;
+    c->h_io[5] = pos_start + n;
+    cudaError_t e = cudaMemcpyAsync(c->pb.slots, &c->h_io[4], 4, cudaMemcpyHostToDevice, c->stream);
+    for (int t0 = 0; t0 < n && e == cudaSuccess; t0 += R) {
+        const int m = std::min(R, n - t0);
+        e = cudaMemcpyAsync(c->pb.tok, tokens + t0, sizeof(int) * m, cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess) e = enqueue_pf_chunk(c, slot, pos_start + t0, m, t0 + m == n, logits != nullptr);
+    }
+    // the device position after the prompt (the decode kernels read it)
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c->b.pos + slot, &c->h_io[5], 4, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess && logits)
+        e = cudaMemcpyAsync(logits, c->pb.head_logits, sizeof(float) * c->d.V, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&c->h_io[1], c->b.token + slot, 4, cudaMemcpyDeviceToHost, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "prefill", -1, "%s", cudaGetErrorString(e));
+    advance_lens(c, slot, n);
+    rc = check_device_error(c, "prefill");
+    if (rc == DM_OK && next) *next = c->h_io[1];
+    return rc;
+}
+
+int32_t dm_prefill_rows(dm_ctx* c, int32_t* rows_out, int32_t* kernels_per_chunk_out) {
+    if (!c || !rows_out) return DM_ERR_INVALID_ARG;
+    *rows_out = c->pb.cap;
+    if (kernels_per_chunk_out) *kernels_per_chunk_out = pf_kernels_per_chunk(c->d);
+    return DM_OK;
+}
+
 // ---- batched decode ---------------------------------------------------------------------
 // One step of n sequences (rows): dense projections on the tensor cores (dm_gemm_tc.cu:
 // weights streamed once per step, the rows' hi/lo operand as the MMA's N), the per-row
 // kernels of dm_batch.cu, the GDN recurrence and the attention with a row dimension, the
 // experts on the tensor cores (dm_expert_tc.cu).
-// C = Xcat . W^T for dense matrix `map` ([N][K]) into bb.c as *splits partials.
-static cudaError_t bgemm(dm_ctx* c, int map, int N, int K, int n, int* splits, int max_splits = 16) {
+// C = Xcat . W^T for dense matrix `map` ([N][K]) into bb.c as *splits partials (bb: the
+// decode step's or the prefill chunk's scratch).
+static cudaError_t bgemm(dm_ctx* c, const BatchBuffers& bb, int map, int N, int K, int n, int* splits,
+                         int max_splits = 16) {
     CUtensorMap xm;
-    if (!encode_operand_map(c, K, 2 * n, &xm)) return cudaErrorInvalidValue;
-    const size_t nmax = std::max({static_cast<size_t>(c->d.gdn_in_rows), static_cast<size_t>(c->d.attn_in_rows),
-                                  static_cast<size_t>(c->d.H), static_cast<size_t>(c->d.V)});
-    // the partials share the result buffer: S x 2n x N <= 2 cap x nmax
-    const int max_s = static_cast<int>(std::min<size_t>(max_splits, (2 * static_cast<size_t>(c->bb.cap) * nmax) /
-                                                                (2 * static_cast<size_t>(n) * N)));
-    *splits = tc_gemm_splits((N + 127) / 128, K, c->num_sms, std::max(1, max_s));
-    return launch_tc_gemm(lcfg(c), &c->dmaps[map], &xm, c->bb.c, N, K, 2 * n, *splits, c->b.err);
+    if (!encode_operand_map(bb, K, 2 * n, &xm)) return cudaErrorInvalidValue;
+    // the partials share the result buffer: S x 2n x N <= c_cap
+    const int max_s = static_cast<int>(std::min<size_t>(max_splits, bb.c_cap / (2 * static_cast<size_t>(n) * N)));
+    if (max_s < 1) return cudaErrorInvalidValue;
+    *splits = tc_gemm_splits(((N + 127) / 128) * ((2 * n + 127) / 128), K, c->num_sms, max_s);
+    return launch_tc_gemm(lcfg(c), &c->dmaps[map], &xm, bb.c, N, K, 2 * n, *splits, c->b.err);
 }
 
 // The token mixer of layer l for n rows, through its residual: x -> xm.
@@ -2100,19 +2223,19 @@ static cudaError_t enqueue_b_mixer(dm_ctx* c, int l, int n) {
     int sp = 1;
     if (w.is_attn) {
         if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
-        if (e == cudaSuccess) e = bgemm(c, 2 * l, d.attn_in_rows, d.H, n, &sp);
+        if (e == cudaSuccess) e = bgemm(c, bb, 2 * l, d.attn_in_rows, d.H, n, &sp);
         if (e == cudaSuccess) e = launch_b_epi_attn_in(lc, d, bb, n, sp);
         if (e == cudaSuccess) e = launch_attn_decode_batch(lc, d, w, bb, c->b, n);
         if (e == cudaSuccess) e = launch_attn_merge_batch(lc, d, bb, n);
-        if (e == cudaSuccess) e = bgemm(c, 2 * l + 1, d.H, d.Hq * d.D, n, &sp);
+        if (e == cudaSuccess) e = bgemm(c, bb, 2 * l + 1, d.H, d.Hq * d.D, n, &sp);
     } else {
         if (e == cudaSuccess) e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
-        if (e == cudaSuccess) e = bgemm(c, 2 * l, d.gdn_in_rows, d.H, n, &sp);
+        if (e == cudaSuccess) e = bgemm(c, bb, 2 * l, d.gdn_in_rows, d.H, n, &sp);
         if (e == cudaSuccess) e = launch_b_epi_gdn_in(lc, d, w, bb, c->b, n, sp);
         if (e == cudaSuccess) e = launch_gdn_rec_batch(lc, d, w, bb, c->b, n);
         if (e == cudaSuccess)
             e = launch_b_prep(lc, BPREP_HEADNORM, bb.o, d.z_dim, nullptr, d.eps, bb.z, w.gdn_norm, d.dv, bb.xcat, n);
-        if (e == cudaSuccess) e = bgemm(c, 2 * l + 1, d.H, d.z_dim, n, &sp);
+        if (e == cudaSuccess) e = bgemm(c, bb, 2 * l + 1, d.H, d.z_dim, n, &sp);
     }
     if (e == cudaSuccess) e = launch_b_epi_resid(lc, bb.c, d.H, bb.x, bb.xm, n, sp);
     return e;
@@ -2137,7 +2260,7 @@ static cudaError_t enqueue_b_head(dm_ctx* c, int n, int write_logits) {
     const LaunchCfg lc = lcfg(c);
     cudaError_t e = launch_b_prep(lc, BPREP_RMS, bb.x, d.H, c->final_norm, d.eps, nullptr, nullptr, 0, bb.xcat, n);
     int sp = 1;
-    if (e == cudaSuccess) e = bgemm(c, 2 * d.L, d.V, d.H, n, &sp, 1);
+    if (e == cudaSuccess) e = bgemm(c, bb, 2 * d.L, d.V, d.H, n, &sp, 1);
     if (e == cudaSuccess && sp != 1) e = cudaErrorInvalidValue;  // the argmax reads one product
     if (e == cudaSuccess) e = launch_b_argmax(lc, d, bb, c->b, n, write_logits, 1);
     return e;
@@ -2156,6 +2279,59 @@ static cudaError_t enqueue_batch_step(dm_ctx* c, int n, int write_logits) {
     }
     if (e == cudaSuccess) e = enqueue_b_head(c, n, write_logits);
     return e;
+}
+
+// ---- prefill ---------------------------------------------------------------------------
+// A prompt of n tokens for one slot, as chunks of up to pb.cap rows: each chunk runs the
+// layers with its tokens as the rows of the batched kernels (dense projections on the
+// tcgen05 GEMM, router, grouping and the tcgen05 experts), the GDN recurrence over the
+// chunk's tokens (launch_pf_gdn) and the causal attention over the cache plus the chunk
+// (launch_pf_attn); the final norm, lm_head and argmax run for the prompt's last token only.
+static cudaError_t enqueue_pf_chunk(dm_ctx* c, int slot, int pos0, int n, bool head, int write_logits) {
+    const Dims& d = c->d;
+    BatchBuffers& pb = c->pb;
+    const LaunchCfg lc = lcfg(c);
+    cudaError_t e = launch_b_embed(lc, d, c->embed, pb, c->b, n);
+    for (int l = 0; l < d.L && e == cudaSuccess; ++l) {
+        const LayerW& w = c->layers[l];
+        int sp = 1;
+        e = launch_b_prep(lc, BPREP_RMS, pb.x, d.H, w.in_norm, d.eps, nullptr, nullptr, 0, pb.xcat, n);
+        if (w.is_attn) {
+            if (e == cudaSuccess) e = bgemm(c, pb, 2 * l, d.attn_in_rows, d.H, n, &sp);
+            if (e == cudaSuccess) e = launch_b_epi_attn_in(lc, d, pb, n, sp);
+            if (e == cudaSuccess) e = launch_pf_attn(lc, d, w, pb, c->b, slot, pos0, n);
+            if (e == cudaSuccess) e = bgemm(c, pb, 2 * l + 1, d.H, d.Hq * d.D, n, &sp);
+        } else {
+            if (e == cudaSuccess) e = bgemm(c, pb, 2 * l, d.gdn_in_rows, d.H, n, &sp);
+            if (e == cudaSuccess) e = launch_b_epi_gdn_pf(lc, d, pb, n, sp);
+            if (e == cudaSuccess) e = launch_pf_gdn(lc, d, w, pb, c->b, slot, pos0, n);
+            if (e == cudaSuccess)
+                e = launch_b_prep(lc, BPREP_HEADNORM, pb.o, d.z_dim, nullptr, d.eps, pb.z, w.gdn_norm, d.dv, pb.xcat, n);
+            if (e == cudaSuccess) e = bgemm(c, pb, 2 * l + 1, d.H, d.z_dim, n, &sp);
+        }
+        if (e == cudaSuccess) e = launch_b_epi_resid(lc, pb.c, d.H, pb.x, pb.xm, n, sp);
+        if (e == cudaSuccess) e = launch_b_router(lc, d, w, pb, pb.xm, 1, n);
+        if (e == cudaSuccess) e = launch_b_topk_group(lc, d, pb, c->b, n);
+        if (e == cudaSuccess) e = launch_b_experts(lc, d, w, pb, c->b, n);
+        if (e == cudaSuccess) e = launch_b_combine(lc, d, pb, pb.xm, pb.x, n);
+    }
+    if (head && e == cudaSuccess) {
+        e = launch_b_prep(lc, BPREP_RMS, pb.x + static_cast<size_t>(n - 1) * d.H, d.H, c->final_norm, d.eps, nullptr,
+                          nullptr, 0, pb.xcat, 1);
+        int sp = 1;
+        if (e == cudaSuccess) e = bgemm(c, pb, 2 * d.L, d.V, d.H, 1, &sp, 1);
+        if (e == cudaSuccess && sp != 1) e = cudaErrorInvalidValue;  // the argmax reads one product
+        if (e == cudaSuccess) e = launch_b_argmax(lc, d, pb, c->b, 1, write_logits, 0, 0);
+    }
+    return e;
+}
+
+// Kernel launches of one prefill chunk (the head excluded).
+static int pf_kernels_per_chunk(const Dims& d) {
+    // embed + per GDN layer 14 (prep, gemm, epi, scan, ring, prep, gemm, resid, router,
+    // group, xstage, 2 experts, combine) + per attention layer 13 (prep, gemm, epi, attn
+    // prep, attn, merge, gemm, resid, router, group, xstage, 2 experts, combine)
+    return 1 + 14 * d.n_gdn + 13 * d.n_att;
 }
 
 // ---- spilling expert pool -----------------------------------------------------------
@@ -2762,6 +2938,12 @@ int32_t dm_time_batch_kernel(dm_ctx* c, int32_t n, int32_t which, int32_t layer,
         for (int v : ids)
             if (v >= 0 && v < d.E && !seen[v]) seen[v] = 1, ++uniq;
         by = static_cast<uint64_t>(uniq + 1) * d.expert_bytes;  // + the shared expert
+    } else if (which == DM_BKERNEL_ROUTER) {
+        by = static_cast<uint64_t>(d.E + 1) * d.H * 2;  // router rows + the shared-expert gate row
+    } else if (which == DM_BKERNEL_GEMM_IN) {
+        // weights once, the 2n hi/lo operand rows, the fp32 partial products
+        const int N = w.is_attn ? d.attn_in_rows : d.gdn_in_rows;
+        by = static_cast<uint64_t>(N) * d.H * 2 + 2ull * n * d.H * 2 + 2ull * n * N * 4;
     } else {
         return DM_ERR_INVALID_ARG;
     }
@@ -2770,6 +2952,11 @@ int32_t dm_time_batch_kernel(dm_ctx* c, int32_t n, int32_t which, int32_t layer,
     auto launch = [&]() -> cudaError_t {
         if (which == DM_BKERNEL_ATTN) return launch_attn_decode_batch(lc, d, w, c->bb, c->b, n);
         if (which == DM_BKERNEL_GDN_REC) return launch_gdn_rec_batch(lc, d, w, c->bb, c->b, n);
+        if (which == DM_BKERNEL_ROUTER) return launch_b_router(lc, d, w, c->bb, c->bb.xm, 0, n);
+        if (which == DM_BKERNEL_GEMM_IN) {
+            int sp = 1;
+            return bgemm(c, c->bb, 2 * layer, w.is_attn ? d.attn_in_rows : d.gdn_in_rows, d.H, n, &sp);
+        }
         cudaError_t e = cudaMemsetAsync(c->bb.work + 1, 0, 8, c->stream);
         return e == cudaSuccess ? launch_b_experts(lc, d, wl, c->bb, c->b, n) : e;
     };

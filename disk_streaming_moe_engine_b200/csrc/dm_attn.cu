@@ -966,13 +966,13 @@ static cudaError_t attn_attr_one() {
 // rows of the out-projection GEMM operand (rows b and n + b, column hq * D + d).
 template <int D>
 __global__ void __launch_bounds__(D) attn_merge_kernel(const float* __restrict__ part, size_t part_bs, int nsplit,
-                                                       const float* __restrict__ qg, size_t qg_bs, int Hq,
+                                                       int msplit, const float* __restrict__ qg, size_t qg_bs, int Hq,
                                                        uint16_t* xcat, int n) {
     const int hq = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     __shared__ float w[kMaxSplits];
     __shared__ float s_inv_l;
     pdl_wait();
-    const float* ph = part + b * part_bs + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
+    const float* ph = part + b * part_bs + static_cast<size_t>(hq) * msplit * (D + 2);
     if (d < 32) {  // one warp: the split weights and the normaliser
         float m[2], l[2];
 #pragma unroll
@@ -1012,9 +1012,9 @@ cudaError_t launch_attn_merge_batch(const LaunchCfg& lc, const Dims& d, const Ba
     const size_t qg_bs = static_cast<size_t>(2) * d.Hq * d.D;
     const dim3 grid(d.Hq, n);
     switch (d.D) {
-        case 256: return launch_kernel(lc, attn_merge_kernel<256>, grid, dim3(256), 0, bb.attn_part, part_bs, ns, bb.qg, qg_bs, d.Hq, bb.xcat, n);
-        case 128: return launch_kernel(lc, attn_merge_kernel<128>, grid, dim3(128), 0, bb.attn_part, part_bs, ns, bb.qg, qg_bs, d.Hq, bb.xcat, n);
-        case 64: return launch_kernel(lc, attn_merge_kernel<64>, grid, dim3(64), 0, bb.attn_part, part_bs, ns, bb.qg, qg_bs, d.Hq, bb.xcat, n);
+        case 256: return launch_kernel(lc, attn_merge_kernel<256>, grid, dim3(256), 0, bb.attn_part, part_bs, ns, kMaxSplits, bb.qg, qg_bs, d.Hq, bb.xcat, n);
+        case 128: return launch_kernel(lc, attn_merge_kernel<128>, grid, dim3(128), 0, bb.attn_part, part_bs, ns, kMaxSplits, bb.qg, qg_bs, d.Hq, bb.xcat, n);
+        case 64: return launch_kernel(lc, attn_merge_kernel<64>, grid, dim3(64), 0, bb.attn_part, part_bs, ns, kMaxSplits, bb.qg, qg_bs, d.Hq, bb.xcat, n);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -1150,6 +1150,350 @@ cudaError_t launch_attn_decode_batch(const LaunchCfg& lc, const Dims& d, const L
     a.part_bs = static_cast<size_t>(d.Hq) * kMaxSplits * (d.D + 2);
     a.out_bs = static_cast<size_t>(d.Hq) * d.D;
     return attn_warp_launch(lc, d, a, dim3(d.Hkv, a.nsplit, n));
+}
+
+// ---- prefill: a chunk of n prompt tokens of one sequence ---------------------------------
+// Reference: forward_attention_qwen36 (src/layers/attention.mojo:219-435) over a prompt,
+// causal softmax over every earlier position (:356-421), the prompt's K/V kept in the cache
+// (LayerKVCache.store_prefill, kv_cache.mojo:245; appended at current_len, :302).  Row r of
+// the chunk is position pos0 + r.
+//   pf_attn_prep_kernel  per (row, KV group): the decode kernels' token preparation
+//                        (q/k RMSNorm, partial RoPE, k/v to bf16), k/v appended to the
+//                        paged cache, q stored as bf16 hi + lo
+//   pf_attn_kernel       per (16-row query block, KV group, split of the causal key range):
+//                        one warp per query head (rows = the block's 16 tokens), one
+//                        producer warp streaming the key pages through a 4-stage ring of
+//                        tensor-map copies shared by the group's warps; S = Q K^T and
+//                        O += P V on the tensor cores (mma.sync m16n8k16, q and p as hi + lo
+//                        bf16 terms), online softmax per row in registers; unnormalised
+//                        partials (O, max, sum) per (row, head, split)
+//   attn_merge_kernel    (above) merges the splits, applies sigmoid(gate), writes the
+//                        out-projection operand rows.
+struct PfAttnArgs {
+    const float* qg;          // [n][2 Hq D] q | gate projections of the chunk's rows
+    const float* kvnew;       // [n][2 Hkv D] k | v projections
+    const uint16_t* q_norm;   // [D]
+    const uint16_t* k_norm;   // [D]
+    uint16_t* kv;             // layer base [num_pages][2][Hkv][16][D]
+    const int* page_table;    // [max_pages] of the slot
+    const float2* rope;       // [capacity][rot_dim / 2]
+    int n, pos0, Hq, Hkv, rot_dim, max_pages, num_pages, nsplit, msplit;
+    float eps;
+    uint16_t* qhi;            // [n][Hq][D]
+    uint16_t* qlo;
+    float* part;              // [n][Hq][msplit][D + 2]
+    CUtensorMap kv_map;
+    int kv_row0;
+    uint32_t* err;
+};
+
+constexpr int kPfStages = 4;
+
+template <int D, int GRP>
+__global__ void __launch_bounds__(256) pf_attn_prep_kernel(const __grid_constant__ PfAttnArgs a) {
+    constexpr int NT = 256;
+    __shared__ __align__(16) float qsm[GRP][D + 4];
+    __shared__ __align__(16) uint16_t qh[GRP][D + 8], ql[GRP][D + 8];
+    __shared__ __align__(16) float knew[D], vnew[D];
+    __shared__ __align__(16) uint16_t kbits[D], vbits[D];
+    __shared__ float qn_s[D], kn_s[D];
+    __shared__ float2 cs_s[D / 2];
+    const int r = blockIdx.x, g = blockIdx.y, tid = threadIdx.x;
+    const int pos = a.pos0 + r;
+    for (int i = tid; i < D; i += NT) {
+        qn_s[i] = bf16_to_f32(a.q_norm[i]);
+        kn_s[i] = bf16_to_f32(a.k_norm[i]);
+    }
+    for (int i = tid; i < a.rot_dim / 2; i += NT) cs_s[i] = a.rope[static_cast<size_t>(pos) * (a.rot_dim / 2) + i];
+    pdl_wait();
+    const float* qg = a.qg + static_cast<size_t>(r) * 2 * a.Hq * D;
+    const float* kvn = a.kvnew + static_cast<size_t>(r) * 2 * a.Hkv * D;
+    attn_prepare<D, GRP, NT>(qg + static_cast<size_t>(g * GRP) * D, kvn + static_cast<size_t>(g) * D,
+                             kvn + static_cast<size_t>(a.Hkv + g) * D, qn_s, kn_s, cs_s, a.rot_dim, a.eps, qsm, knew,
+                             vnew, kbits, vbits, qh, ql);
+    pdl_launch_dependents();
+    const int page = a.page_table[pos / kPageTokens];
+    if (page < 0 || page >= a.num_pages) {
+        if (tid == 0) raise_error(a.err, DM_DEVERR_PAGE);
+    } else {
+        uint16_t* kd = a.kv + ((static_cast<size_t>(page) * 2 + 0) * a.Hkv + g) * kPageTokens * D +
+                       static_cast<size_t>(pos % kPageTokens) * D;
+        uint16_t* vd = a.kv + ((static_cast<size_t>(page) * 2 + 1) * a.Hkv + g) * kPageTokens * D +
+                       static_cast<size_t>(pos % kPageTokens) * D;
+        for (int d = tid; d < D; d += NT) {
+            kd[d] = kbits[d];
+            vd[d] = vbits[d];
+        }
+    }
+    for (int i = tid; i < GRP * D; i += NT) {
+        const size_t o = (static_cast<size_t>(r) * a.Hq + g * GRP + i / D) * D + i % D;
+        a.qhi[o] = qh[i / D][i % D];
+        a.qlo[o] = ql[i / D][i % D];
+    }
+}
+
+template <int D, int GRP>
+constexpr size_t pf_attn_smem() {
+    return static_cast<size_t>(kPfStages) * AttnGeom<D>::STAGE + 2ull * GRP * 16 * (D + 8) * 2 + 1024;
+}
+
+template <int D, int GRP>
+__global__ void __launch_bounds__((GRP + 1) * 32, 1) pf_attn_kernel(const __grid_constant__ PfAttnArgs a) {
+    using AG = AttnGeom<D>;
+    constexpr int KS = D / 16;   // k-steps of Q K^T
+    constexpr int NTL = D / 8;   // n-tiles of O
+    constexpr int QP = D + 8;    // padded q row (bf16 elements): conflict-free ldmatrix rows
+    extern __shared__ __align__(1024) uint8_t pf_smem[];
+    uint8_t* ring = pf_smem + ((1024u - (smem_u32(pf_smem) & 1023u)) & 1023u);
+    uint16_t* qhs = reinterpret_cast<uint16_t*>(ring + kPfStages * AG::STAGE);  // [GRP][16][QP]
+    uint16_t* qls = qhs + GRP * 16 * QP;
+    __shared__ __align__(8) uint64_t full[kPfStages], empty[kPfStages];
+    __shared__ int s_abort;
+    volatile int* abort_flag = &s_abort;
+    const int qb = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = qb * 16;
+    const int rmax = min(a.n, r0 + 16) - 1;
+    const int n_pg = (a.pos0 + rmax) / kPageTokens + 1;  // pages of keys 0 .. pos0 + rmax
+    const int pg0 = static_cast<int>(static_cast<long long>(s) * n_pg / a.nsplit);
+    const int pg1 = static_cast<int>(static_cast<long long>(s + 1) * n_pg / a.nsplit);
+    const int np = pg1 - pg0;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kPfStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], GRP);
+        }
+        mbar_fence_init();
+        s_abort = 0;
+    }
+    __syncthreads();
+    pdl_wait();  // q and the chunk's own keys come from the preparation kernel
+    for (int i = threadIdx.x; i < GRP * 16 * (D / 8); i += (GRP + 1) * 32) {
+        const int hh = i / (16 * (D / 8)), rr = (i / (D / 8)) % 16, c8 = i % (D / 8);
+        uint4 vh = make_uint4(0u, 0u, 0u, 0u), vl = vh;
+        if (r0 + rr < a.n) {
+            const size_t o = (static_cast<size_t>(r0 + rr) * a.Hq + g * GRP + hh) * D + c8 * 8;
+            vh = *reinterpret_cast<const uint4*>(a.qhi + o);
+            vl = *reinterpret_cast<const uint4*>(a.qlo + o);
+        }
+        *reinterpret_cast<uint4*>(qhs + (hh * 16 + rr) * QP + c8 * 8) = vh;
+        *reinterpret_cast<uint4*>(qls + (hh * 16 + rr) * QP + c8 * 8) = vl;
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+    if (warp == GRP) {
+        // ---- producer: page i of the split into stage i % kPfStages ----
+        if (lane == 0) {
+            bool ok = true;
+            for (int i = 0; i < np && ok; ++i) {
+                const int st = i % kPfStages;
+                if (i >= kPfStages) {
+                    ok = mbar_wait_bounded(&empty[st], ((i / kPfStages) - 1) & 1, a.err, abort_flag);
+                    if (!ok) break;
+                    fence_proxy_async_smem();
+                }
+                const int page = a.page_table[pg0 + i];
+                if (page < 0 || page >= a.num_pages) {
+                    raise_error(a.err, DM_DEVERR_PAGE);
+                    mbar_arrive(&full[st]);
+                    continue;
+                }
+                mbar_arrive_expect_tx(&full[st], 2 * kPageTokens * D * 2);
+                uint8_t* dst = ring + static_cast<size_t>(st) * AG::STAGE;
+#pragma unroll
+                for (int kv = 0; kv < 2; ++kv) {
+                    const int y = a.kv_row0 + ((page * 2 + kv) * a.Hkv + g) * kPageTokens;
+#pragma unroll
+                    for (int c = 0; c < D / 64; ++c) tma_load_2d(dst + kv * AG::TILE + c * AG::CHUNK, &a.kv_map, 64 * c, y, &full[st]);
+                }
+            }
+            // the copies still in flight land before the CTA exits
+            for (int u = np > kPfStages ? np - kPfStages : 0; u < np; ++u)
+                mbar_wait_bounded(&full[u % kPfStages], (u / kPfStages) & 1, a.err, nullptr);
+        }
+        return;
+    }
+    // ---- consumer warp: query head g GRP + warp, rows = the block's 16 tokens ----
+    const int fg = lane >> 2, ft = lane & 3;
+    const uint16_t* qh_w = qhs + warp * 16 * QP;
+    const uint16_t* ql_w = qls + warp * 16 * QP;
+    const int qp0 = a.pos0 + r0 + fg, qp1 = qp0 + 8;  // positions of this lane's two rows
+    const bool rv0 = r0 + fg < a.n, rv1 = r0 + fg + 8 < a.n;
+    const float sm_scale = 1.0f / sqrtf(static_cast<float>(D));
+    float o[NTL][4];
+#pragma unroll
+    for (int t = 0; t < NTL; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_part[2] = {0.0f, 0.0f};
+    const int mi = lane >> 3;
+    const int krow = 8 * (mi >> 1) + (lane & 7), kcol = 8 * (mi & 1);       // K fragments (B)
+    const int arow = (lane & 7) + 8 * (mi & 1), acol = 8 * (mi >> 1);       // Q fragments (A)
+    bool ok = true;
+    for (int i = 0; i < np; ++i) {
+        const int st = i % kPfStages;
+        ok = ok && mbar_wait_bounded(&full[st], (i / kPfStages) & 1, a.err, abort_flag);
+        const uint8_t* kt = ring + static_cast<size_t>(st) * AG::STAGE;
+        const uint8_t* vt = kt + AG::TILE;
+        float sh0[4] = {0.f, 0.f, 0.f, 0.f}, sl0[4] = {0.f, 0.f, 0.f, 0.f};
+        float sh1[4] = {0.f, 0.f, 0.f, 0.f}, sl1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            uint32_t k0, k1, k2, k3, h0, h1, h2, h3, l0, l1, l2, l3;
+            ldsm_x4(k0, k1, k2, k3, kt + kv_tile_off<D>(krow, 16 * ks + kcol));
+            ldsm_x4(h0, h1, h2, h3, qh_w + arow * QP + 16 * ks + acol);
+            ldsm_x4(l0, l1, l2, l3, ql_w + arow * QP + 16 * ks + acol);
+            mma_bf16_16816_full(sh0, h0, h1, h2, h3, k0, k1);
+            mma_bf16_16816_full(sl0, l0, l1, l2, l3, k0, k1);
+            mma_bf16_16816_full(sh1, h0, h1, h2, h3, k2, k3);
+            mma_bf16_16816_full(sl1, l0, l1, l2, l3, k2, k3);
+        }
+        // sv[4 hf + j]: row fg + 8 hf, keys 2ft, 2ft + 1, 8 + 2ft, 9 + 2ft of the page
+        const int kb = (pg0 + i) * kPageTokens;
+        float sv[8];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int key0 = kb + 2 * ft + e, key1 = kb + 8 + 2 * ft + e;
+            sv[e] = (ok && rv0 && key0 <= qp0) ? (sh0[e] + sl0[e]) * sm_scale : -INFINITY;
+            sv[2 + e] = (ok && rv0 && key1 <= qp0) ? (sh1[e] + sl1[e]) * sm_scale : -INFINITY;
+            sv[4 + e] = (ok && rv1 && key0 <= qp1) ? (sh0[2 + e] + sl0[2 + e]) * sm_scale : -INFINITY;
+            sv[6 + e] = (ok && rv1 && key1 <= qp1) ? (sh1[2 + e] + sl1[2 + e]) * sm_scale : -INFINITY;
+        }
+        float p[8], alpha[2];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            float mp = fmaxf(fmaxf(sv[4 * hf], sv[4 * hf + 1]), fmaxf(sv[4 * hf + 2], sv[4 * hf + 3]));
+            mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 1));
+            mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 2));
+            const float mn = fmaxf(m_run[hf], mp);
+            alpha[hf] = (m_run[hf] == -INFINITY) ? (mn == -INFINITY ? 1.0f : 0.0f) : expf(m_run[hf] - mn);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) p[4 * hf + e] = sv[4 * hf + e] == -INFINITY ? 0.0f : expf(sv[4 * hf + e] - mn);
+            l_part[hf] = l_part[hf] * alpha[hf] + ((p[4 * hf] + p[4 * hf + 1]) + (p[4 * hf + 2] + p[4 * hf + 3]));
+            m_run[hf] = mn;
+        }
+#pragma unroll
+        for (int t = 0; t < NTL; ++t) {
+            o[t][0] *= alpha[0];
+            o[t][1] *= alpha[0];
+            o[t][2] *= alpha[1];
+            o[t][3] *= alpha[1];
+        }
+        // P as A fragments: a0 = row fg keys 2ft.., a1 = row fg + 8, a2 / a3 = keys 8 + 2ft..
+        uint32_t ah[4], al[4];
+        {
+            const int idx[4][2] = {{0, 1}, {4, 5}, {2, 3}, {6, 7}};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint16_t x0 = f32_to_bf16(p[idx[q][0]]), x1 = f32_to_bf16(p[idx[q][1]]);
+                ah[q] = pack_bf16x2(x0, x1);
+                al[q] = pack_bf16x2(f32_to_bf16(p[idx[q][0]] - bf16_to_f32(x0)), f32_to_bf16(p[idx[q][1]] - bf16_to_f32(x1)));
+            }
+        }
+        // V as B fragments (.trans): matrices (keys 0-7 | 8-15) x (dims 16 j .. | 16 j + 8 ..)
+        const int vrow = (lane & 7) + 8 * (mi & 1), vcol = 8 * (mi >> 1);
+#pragma unroll
+        for (int j = 0; j < NTL / 2; ++j) {
+            uint32_t v0, v1, v2, v3;
+            ldsm_x4_trans(v0, v1, v2, v3, vt + kv_tile_off<D>(vrow, 16 * j + vcol));
+            mma_bf16_16816_full(o[2 * j], ah[0], ah[1], ah[2], ah[3], v0, v1);
+            mma_bf16_16816_full(o[2 * j], al[0], al[1], al[2], al[3], v0, v1);
+            mma_bf16_16816_full(o[2 * j + 1], ah[0], ah[1], ah[2], ah[3], v2, v3);
+            mma_bf16_16816_full(o[2 * j + 1], al[0], al[1], al[2], al[3], v2, v3);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    const int hq = g * GRP + warp;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        float l = l_part[hf];
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        const int r = r0 + fg + 8 * hf;
+        if (r < a.n) {
+            float* pp = a.part + ((static_cast<size_t>(r) * a.Hq + hq) * a.msplit + s) * (D + 2);
+#pragma unroll
+            for (int t = 0; t < NTL; ++t) {
+                pp[8 * t + 2 * ft] = o[t][2 * hf];
+                pp[8 * t + 2 * ft + 1] = o[t][2 * hf + 1];
+            }
+            if (ft == 0) {
+                pp[D] = m_run[hf];
+                pp[D + 1] = l;
+            }
+        }
+    }
+}
+
+template <int D, int GRP>
+static cudaError_t pf_attn_attr_one() {
+    return cudaFuncSetAttribute(pf_attn_kernel<D, GRP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(pf_attn_smem<D, GRP>()));
+}
+
+cudaError_t pf_attn_set_attrs() {
+    cudaError_t e = cudaSuccess;
+#define DM_PF_ATTR(DD, GG) \
+    if (e == cudaSuccess) e = pf_attn_attr_one<DD, GG>();
+    DM_ATTN_INSTANCES(DM_PF_ATTR)
+#undef DM_PF_ATTR
+    return e;
+}
+
+// Splits of the causal key range per (query block, KV group): about two CTAs per SM.
+int pf_attn_nsplit(int num_sms, int Hkv, int n) {
+    const int units = ((n + 15) / 16) * (Hkv > 0 ? Hkv : 1);
+    int ns = (2 * num_sms + units - 1) / units;
+    if (ns > kPfMaxSplits) ns = kPfMaxSplits;
+    return ns < 1 ? 1 : ns;
+}
+
+cudaError_t launch_pf_attn(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& pb,
+                           const Buffers& b, int slot, int pos0, int n) {
+    PfAttnArgs a{};
+    a.qg = pb.qg;
+    a.kvnew = pb.kvnew;
+    a.q_norm = w.q_norm;
+    a.k_norm = w.k_norm;
+    a.kv = b.kv + static_cast<size_t>(w.sub) * d.num_pages * 2 * d.Hkv * kPageTokens * d.D;
+    a.page_table = b.page_table + static_cast<size_t>(slot) * d.max_pages;
+    a.rope = b.rope;
+    a.n = n;
+    a.pos0 = pos0;
+    a.Hq = d.Hq;
+    a.Hkv = d.Hkv;
+    a.rot_dim = d.rot_dim;
+    a.max_pages = d.max_pages;
+    a.num_pages = d.num_pages;
+    a.nsplit = pf_attn_nsplit(lc.num_sms, d.Hkv, n);
+    a.msplit = kPfMaxSplits;
+    a.eps = d.eps;
+    a.qhi = pb.pf_qhi;
+    a.qlo = pb.pf_qlo;
+    a.part = pb.attn_part;
+    a.kv_map = *static_cast<const CUtensorMap*>(b.kv_tmap);
+    a.kv_row0 = w.sub * d.num_pages * 2 * d.Hkv * kPageTokens;
+    a.err = b.err;
+    const int grp = d.Hq / d.Hkv;
+    cudaError_t e = cudaErrorInvalidValue;
+#define DM_PF_LAUNCH(DD, GG)                                                                                         \
+    if (d.D == DD && grp == GG) {                                                                                    \
+        e = launch_kernel(lc, pf_attn_prep_kernel<DD, GG>, dim3(n, d.Hkv), dim3(256), 0, a);                         \
+        if (e == cudaSuccess)                                                                                        \
+            e = launch_kernel(lc, pf_attn_kernel<DD, GG>, dim3((n + 15) / 16, d.Hkv, a.nsplit), dim3((GG + 1) * 32),  \
+                              pf_attn_smem<DD, GG>(), a);                                                            \
+    }
+    DM_ATTN_INSTANCES(DM_PF_LAUNCH)
+#undef DM_PF_LAUNCH
+    if (e != cudaSuccess) return e;
+    const size_t part_bs = static_cast<size_t>(d.Hq) * kPfMaxSplits * (d.D + 2);
+    const size_t qg_bs = static_cast<size_t>(2) * d.Hq * d.D;
+    const dim3 grid(d.Hq, n);
+    switch (d.D) {
+        case 256: return launch_kernel(lc, attn_merge_kernel<256>, grid, dim3(256), 0, pb.attn_part, part_bs, a.nsplit, kPfMaxSplits, pb.qg, qg_bs, d.Hq, pb.xcat, n);
+        case 128: return launch_kernel(lc, attn_merge_kernel<128>, grid, dim3(128), 0, pb.attn_part, part_bs, a.nsplit, kPfMaxSplits, pb.qg, qg_bs, d.Hq, pb.xcat, n);
+        case 64: return launch_kernel(lc, attn_merge_kernel<64>, grid, dim3(64), 0, pb.attn_part, part_bs, a.nsplit, kPfMaxSplits, pb.qg, qg_bs, d.Hq, pb.xcat, n);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace dm

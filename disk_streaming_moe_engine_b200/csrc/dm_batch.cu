@@ -127,6 +127,7 @@ struct BEpiArgs {
     int N, n, splits;
     // GDN input projection: [qkv | z | a b] -> conv ring slot pos % 4, SiLU(z), a b
     float* ring;       // layer base [max_seqs][4][qkv_dim]
+    float* raw;        // prefill: [n][qkv_dim] pre-conv rows of the chunk
     const int* slots;
     const int* pos;
     int qkv_dim, z_dim;
@@ -165,6 +166,15 @@ __global__ void __launch_bounds__(256) b_epi_kernel(const __grid_constant__ BEpi
             const int nab = a.N - a.qkv_dim - a.z_dim;
             a.ab[static_cast<size_t>(b) * nab + (col - a.qkv_dim - a.z_dim)] = v;
         }
+    } else if (MODE == BEPI_GDN_PF) {
+        if (col < a.qkv_dim) {
+            a.raw[static_cast<size_t>(b) * a.qkv_dim + col] = v;
+        } else if (col < a.qkv_dim + a.z_dim) {
+            a.z[static_cast<size_t>(b) * a.z_dim + (col - a.qkv_dim)] = silu_f(v);
+        } else {
+            const int nab = a.N - a.qkv_dim - a.z_dim;
+            a.ab[static_cast<size_t>(b) * nab + (col - a.qkv_dim - a.z_dim)] = v;
+        }
     } else if (MODE == BEPI_ATTN_IN) {
         if (col < a.qg_rows) a.qg[static_cast<size_t>(b) * a.qg_rows + col] = v;
         else a.kvnew[static_cast<size_t>(b) * (a.N - a.qg_rows) + (col - a.qg_rows)] = v;
@@ -188,6 +198,20 @@ cudaError_t launch_b_epi_gdn_in(const LaunchCfg& lc, const Dims& d, const LayerW
     a.z = bb.z;
     a.ab = bb.ab;
     return launch_kernel(lc, b_epi_kernel<BEPI_GDN_IN>, dim3((a.N + 255) / 256, n), dim3(256), 0, a);
+}
+
+cudaError_t launch_b_epi_gdn_pf(const LaunchCfg& lc, const Dims& d, const BatchBuffers& pb, int n, int splits) {
+    BEpiArgs a{};
+    a.c = pb.c;
+    a.N = d.gdn_in_rows;
+    a.n = n;
+    a.splits = splits;
+    a.raw = pb.pf_raw;
+    a.qkv_dim = d.qkv_dim;
+    a.z_dim = d.z_dim;
+    a.z = pb.z;
+    a.ab = pb.ab;
+    return launch_kernel(lc, b_epi_kernel<BEPI_GDN_PF>, dim3((a.N + 255) / 256, n), dim3(256), 0, a);
 }
 
 cudaError_t launch_b_epi_attn_in(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, int n, int splits) {
@@ -555,6 +579,12 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
     }
 }
 
+int b_group_max_rows(int E) {
+    const int words = kBGMaskWords / (E > 0 ? E : 1);  // mask words per expert
+    const int by_mask = 64 * words, by_ids = kMaxRanks * kMaxBatch;
+    return by_mask < by_ids ? by_mask : by_ids;
+}
+
 size_t b_topk_group_smem(int E, int topk) {
     (void)E;
     return static_cast<size_t>(kMaxRanks) * kMaxBatch * topk * 4;
@@ -644,7 +674,7 @@ struct BArgmaxArgs {
     float* logits_out;    // [n][V] or null
     int* tok;             // [n]
     const int* slots;
-    int* pos;             // [max_seqs], advanced by one per row
+    int* pos;             // [max_seqs], advanced by one per row (null: not advanced)
     int* token;           // [max_seqs]
     int* gen_out;         // [gen_cap] or null
     int* gen_idx;
@@ -714,7 +744,7 @@ __global__ void __launch_bounds__(1024) b_argmax_final_kernel(const __grid_const
             const int slot = a.slots[b];
             a.tok[b] = bi;
             a.token[slot] = bi;
-            a.pos[slot] += 1;
+            if (a.pos) a.pos[slot] += 1;
             if (a.gen_out && (step + 1) * a.n <= a.gen_cap) a.gen_out[step * a.n + b] = bi;
         }
     }
@@ -723,7 +753,7 @@ __global__ void __launch_bounds__(1024) b_argmax_final_kernel(const __grid_const
 }
 
 cudaError_t launch_b_argmax(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n,
-                            int write_logits, int record_gen) {
+                            int write_logits, int record_gen, int advance) {
     BArgmaxArgs a{};
     a.c = bb.c;
     a.V = d.V;
@@ -733,7 +763,7 @@ cudaError_t launch_b_argmax(const LaunchCfg& lc, const Dims& d, const BatchBuffe
     a.logits_out = write_logits ? bb.head_logits : nullptr;
     a.tok = bb.tok;
     a.slots = bb.slots;
-    a.pos = b.pos;
+    a.pos = advance ? b.pos : nullptr;
     a.token = b.token;
     a.gen_out = record_gen ? bb.gen_out : nullptr;
     a.gen_idx = bb.gen_idx;

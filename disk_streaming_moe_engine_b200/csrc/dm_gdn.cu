@@ -525,4 +525,179 @@ cudaError_t launch_gdn_core_out(const LaunchCfg& lc, const Dims& d, const LayerW
     return launch_kernel(lc, gdn_core_out_kernel<64>, dim3(G), dim3(kGfThreads), smem, f);
 }
 
+// ---- prefill: the recurrence over a chunk of n prompt tokens of one sequence ------------
+// The semantics above applied token after token (reference forward_gdn_block runs its
+// recurrence scan token by token, gdn.mojo:1040-1133), with the same arithmetic and order as
+// gdn_rec_kernel, so a prompt prefilled here leaves the state a token-by-token decode would.
+// Grid (nv, dv / 16), 128 threads: each CTA owns 16 state rows of one head in registers for
+// the whole chunk.  Tokens go in blocks of kPfTok: all threads first compute the block's
+// causal conv + SiLU (q, k of the head's QK head, this CTA's 16 v channels), k
+// normalisation, decay and beta into shared memory; then every warp runs its 4 rows through
+// the block's tokens (delta-rule update and o = S q, no block barrier in between).
+// Pre-conv inputs of position p: p < 0 zero, p < pos0 the conv window (ring slot p % 4),
+// else row p - pos0 of the chunk.
+constexpr int kPfTok = 16;
+
+struct PfGdnArgs {
+    const float* raw;       // [n][qkv_dim]
+    const float* ring;      // [4][qkv_dim] of (layer, slot)
+    const uint16_t* conv_w;
+    float* S;               // [nv][dv][dk] of (layer, slot)
+    const float* a_log;
+    const float* dt_bias;
+    const float* ab;        // [n][2 nv]
+    float* o;               // [n][nv dv]
+    int n, pos0, nk, nv, qkv_dim;
+    float eps;
+};
+
+template <int DK>
+__global__ void __launch_bounds__(128) pf_gdn_kernel(const __grid_constant__ PfGdnArgs a) {
+    constexpr int DV = DK;
+    constexpr int RB = 16;
+    constexpr int CPL = DK / 32;
+    constexpr int NCH = 2 * DK + RB;  // conv channels of this CTA: q, k, its v rows
+    __shared__ __align__(16) float qs[kPfTok][DK], ks[kPfTok][DK];
+    __shared__ float vs[kPfTok][RB], gs[kPfTok], bs[kPfTok];
+    const int h = blockIdx.x, rb = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int g_qk = h / (a.nv / a.nk);
+    float* Sh = a.S + static_cast<size_t>(h) * DV * DK;
+    float srow[4][CPL];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float* src = Sh + static_cast<size_t>(rb * RB + warp * 4 + i) * DK + lane * CPL;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) srow[i][c] = src[c];
+    }
+    const float alog = a.a_log[h], dtb = a.dt_bias[h];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int q0 = g_qk * DK, k0 = a.nk * DK + g_qk * DK, v0 = 2 * a.nk * DK + h * DV + rb * RB;
+    for (int t0 = 0; t0 < a.n; t0 += kPfTok) {
+        const int nt = min(kPfTok, a.n - t0);
+        // ---- conv + SiLU of the block's tokens ----
+        for (int idx = tid; idx < nt * NCH; idx += 128) {
+            const int tt = idx / NCH, t = idx % NCH;
+            const int ch = t < DK ? q0 + t : (t < 2 * DK ? k0 + (t - DK) : v0 + (t - 2 * DK));
+            const uint16_t* w = a.conv_w + static_cast<size_t>(ch) * 4;
+            const int pos = a.pos0 + t0 + tt;
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int tp = pos - 3 + j;
+                if (tp >= 0) {
+                    const float pre = tp < a.pos0 ? a.ring[static_cast<size_t>(tp & 3) * a.qkv_dim + ch]
+                                                  : a.raw[static_cast<size_t>(tp - a.pos0) * a.qkv_dim + ch];
+                    acc += bf16_to_f32(w[j]) * pre;
+                }
+            }
+            const float u = silu_f(acc);
+            if (t < DK) qs[tt][t] = u;
+            else if (t < 2 * DK) ks[tt][t - DK] = u;
+            else vs[tt][t - 2 * DK] = u;
+        }
+        if (tid < nt) {
+            const float* ab = a.ab + static_cast<size_t>(t0 + tid) * 2 * a.nv;
+            gs[tid] = expf(-expf(alog) * softplus_ref(ab[h] + dtb));
+            bs[tid] = sigmoid_f(ab[a.nv + h]);
+        }
+        __syncthreads();
+        // ---- k / (||k|| + eps): warp w normalises tokens w, w + 4, ... ----
+        for (int tt = warp; tt < nt; tt += 4) {
+            float kl[CPL];
+            float ss = 0.0f;
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) {
+                kl[c] = ks[tt][lane * CPL + c];
+                ss = fmaf(kl[c], kl[c], ss);
+            }
+            ss = warp_sum(ss);
+            const float inv_nk = 1.0f / (sqrtf(ss) + a.eps);
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) ks[tt][lane * CPL + c] = kl[c] * inv_nk;
+        }
+        __syncthreads();
+        // ---- the warp's 4 rows through the block's tokens ----
+        for (int tt = 0; tt < nt; ++tt) {
+            float kl[CPL], ql[CPL];
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) {
+                kl[c] = ks[tt][lane * CPL + c];
+                ql[c] = qs[tt][lane * CPL + c];
+            }
+            const float g = gs[tt], beta = bs[tt];
+            float* o_out = a.o + static_cast<size_t>(t0 + tt) * a.nv * DV + h * DV;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int rl = warp * 4 + i;
+                float sk = 0.0f;
+#pragma unroll
+                for (int c = 0; c < CPL; ++c) sk = fmaf(srow[i][c], kl[c], sk);
+                sk = warp_sum(sk);
+                const float vr = vs[tt][rl];
+                const float bsk = beta * sk, bvr = beta * vr;
+                float oacc = 0.0f;
+#pragma unroll
+                for (int c = 0; c < CPL; ++c) {
+                    const float sn = g * (srow[i][c] - bsk * kl[c]) + bvr * kl[c];
+                    srow[i][c] = sn;
+                    oacc = fmaf(sn, ql[c], oacc);
+                }
+                oacc = warp_sum(oacc);
+                if (lane == 0) o_out[rb * RB + rl] = oacc;
+            }
+        }
+        __syncthreads();  // the block's shared inputs are consumed before the next block
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float* dst = Sh + static_cast<size_t>(rb * RB + warp * 4 + i) * DK + lane * CPL;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) dst[c] = srow[i][c];
+    }
+}
+
+// The conv window after the chunk: the pre-conv rows of its last min(n, 4) positions into
+// their ring slots (after pf_gdn_kernel, which reads the window the chunk started from).
+__global__ void __launch_bounds__(256) pf_ring_kernel(const float* __restrict__ raw, float* ring, int n, int pos0,
+                                                      int qkv_dim) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int j = blockIdx.y;  // 0..3: position pos0 + n - 4 + j
+    const int p = pos0 + n - 4 + j;
+    if (p < pos0) return;
+    const float* src = raw + static_cast<size_t>(p - pos0) * qkv_dim;
+    float* dst = ring + static_cast<size_t>(p & 3) * qkv_dim;
+    for (int c = blockIdx.x * 256 + threadIdx.x; c < qkv_dim; c += gridDim.x * 256) dst[c] = src[c];
+}
+
+cudaError_t launch_pf_gdn(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& pb,
+                          const Buffers& b, int slot, int pos0, int n) {
+    PfGdnArgs a{};
+    const size_t ls = static_cast<size_t>(w.sub) * d.max_seqs + slot;
+    float* ring = b.ring + ls * kConvRing * d.qkv_dim;
+    a.raw = pb.pf_raw;
+    a.ring = ring;
+    a.conv_w = w.conv_w;
+    a.S = b.S + ls * static_cast<size_t>(d.nv) * d.dv * d.dk;
+    a.a_log = w.a_log;
+    a.dt_bias = w.dt_bias;
+    a.ab = pb.ab;
+    a.o = pb.o;
+    a.n = n;
+    a.pos0 = pos0;
+    a.nk = d.nk;
+    a.nv = d.nv;
+    a.qkv_dim = d.qkv_dim;
+    a.eps = d.eps;
+    const dim3 grid(d.nv, d.dv / 16);
+    cudaError_t e = cudaErrorInvalidValue;
+    if (d.dk == 128) e = launch_kernel(lc, pf_gdn_kernel<128>, grid, dim3(128), 0, a);
+    else if (d.dk == 64) e = launch_kernel(lc, pf_gdn_kernel<64>, grid, dim3(128), 0, a);
+    if (e != cudaSuccess) return e;
+    return launch_kernel(lc, pf_ring_kernel, dim3((d.qkv_dim + 255) / 256, 4), dim3(256), 0, pb.pf_raw, ring, n, pos0,
+                         d.qkv_dim);
+}
+
 }  // namespace dm

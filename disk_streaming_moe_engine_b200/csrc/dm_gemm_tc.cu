@@ -9,11 +9,13 @@
 // C[col][row] = sum_k X[col][k] W[row][k]: W is a bf16 weight matrix [N][K] (row-major as
 // loaded), X the step's operand rows [2n][K] in bf16 (rows 0..n-1 = hi(x), n..2n-1 =
 // lo(x), x = hi + lo to 2^-16; written by the prep kernels), C fp32.  The weight rows are
-// the MMA's M (128 per tile), the operand rows its N (2n rounded up to 16, <= 128), so the
-// weights stream from HBM once per step whatever n is.
+// the MMA's M (128 per tile), the operand rows its N (2n rounded up to 16, <= 128 per column
+// tile), so the weights stream from HBM once per step whatever n is.
 //
-// Work: an item is one 128-row weight tile and one of S slices of K; CTAs (one per SM,
-// persistent) take items c, c + grid, ...  S is chosen per GEMM so that tiles x S fills the
+// Work: an item is one 128-row weight tile, one 128-row column tile of the operand (one for
+// a decode step; a prefill chunk of up to 512 rows has up to 8, the items of one weight tile
+// adjacent so that its re-reads hit L2) and one of S slices of K; CTAs (one per SM,
+// persistent) take items c, c + grid, ...  S is chosen per GEMM so that the items fill the
 // SMs' waves (a 2048-row output projection has only 16 tiles), and each slice writes its own
 // fp32 partial C_s; the kernels that consume C add the S partials (and hi + lo) in a fixed
 // order: the result does not depend on timing (no atomics).
@@ -47,7 +49,7 @@ struct TcGemmArgs {
     CUtensorMap wmap;   // W [N][K] bf16: dims {K, N}, box {64, 128}, 128-byte swizzle
     CUtensorMap xmap;   // X [rows][K] bf16: dims {K, rows}, box {64, ntile}, 128-byte swizzle
     float* c;           // [S][ncols][N] fp32 partials
-    int N, K, ncols, ntile, tiles, splits;
+    int N, K, ncols, ntile, tiles, ctiles, splits;
     uint32_t* err;
 };
 
@@ -85,7 +87,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) tc_gemm_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    const int nitems = a.tiles * a.splits;
+    const int nitems = a.tiles * a.ctiles * a.splits;
     const int kb_total = a.K / kGtKB;
 
     if (warp == 0) {
@@ -97,7 +99,7 @@ __global__ void __launch_bounds__(kGtThreads, 1) tc_gemm_kernel(const __grid_con
             const uint32_t bbytes = static_cast<uint32_t>(a.ntile) * kGtKB * 2;
             bool ok = true;
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
-                const int tile = item / a.splits, sp = item % a.splits;
+                const int tile = item / (a.ctiles * a.splits), ct = (item / a.splits) % a.ctiles, sp = item % a.splits;
                 // slice sp of K: [sp kbt / S, (sp + 1) kbt / S), at least 2 stages (S <= kbt / 2)
                 const int kb0 = sp * kb_total / a.splits, kb1 = (sp + 1) * kb_total / a.splits;
                 for (int kb = kb0; kb < kb1; ++kb) {
@@ -106,8 +108,8 @@ __global__ void __launch_bounds__(kGtThreads, 1) tc_gemm_kernel(const __grid_con
                     mbar_arrive_expect_tx(&full[si], kGtA + bbytes);
                     tma_load_2d(st, &a.wmap, kb * kGtKB, tile * 128, &full[si]);
                     tma_load_2d(st + kGtA / 2, &a.wmap, kb * kGtKB + 64, tile * 128, &full[si]);
-                    tma_load_2d(st + kGtA, &a.xmap, kb * kGtKB, 0, &full[si]);
-                    tma_load_2d(st + kGtA + bbytes / 2, &a.xmap, kb * kGtKB + 64, 0, &full[si]);
+                    tma_load_2d(st + kGtA, &a.xmap, kb * kGtKB, ct * 128, &full[si]);
+                    tma_load_2d(st + kGtA + bbytes / 2, &a.xmap, kb * kGtKB + 64, ct * 128, &full[si]);
                     ++issued;
                     if (++si == kGtStages) {
                         si = 0;
@@ -167,19 +169,20 @@ __global__ void __launch_bounds__(kGtThreads, 1) tc_gemm_kernel(const __grid_con
         const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * sp4) << 16);
         uint32_t di = 0, dph = 0;
         for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
-            const int tile = item / a.splits, sp = item % a.splits;
+            const int tile = item / (a.ctiles * a.splits), ct = (item / a.splits) % a.ctiles, sp = item % a.splits;
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[di], dph, a.err, abort_flag))) break;
             tc_fence_after();
             const int row = tile * 128 + r;
-            float* cs = a.c + static_cast<size_t>(sp) * a.ncols * a.N;
-            for (int c0 = 0; c0 < a.ncols; c0 += 16) {
+            float* cs = a.c + (static_cast<size_t>(sp) * a.ncols + ct * 128) * a.N;
+            const int nc = min(a.ntile, a.ncols - ct * 128);  // columns of this tile
+            for (int c0 = 0; c0 < nc; c0 += 16) {
                 float v[16];
                 tc_ld16(lane_base + di * 128 + c0, v);
                 tc_wait_ld();
                 if (row < a.N) {
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
-                        if (c0 + j < a.ncols) cs[static_cast<size_t>(c0 + j) * a.N + row] = v[j];
+                        if (c0 + j < nc) cs[static_cast<size_t>(c0 + j) * a.N + row] = v[j];
                 }
             }
             tc_fence_before();
@@ -222,7 +225,7 @@ int tc_gemm_splits(int tiles, int K, int num_sms, int max_splits) {
 
 cudaError_t launch_tc_gemm(const LaunchCfg& lc, const void* wmap, const void* xmap, float* c, int N, int K, int ncols,
                            int splits, uint32_t* err) {
-    if (ncols < 1 || ncols > 128 || K % kGtKB != 0 || splits < 1) return cudaErrorInvalidValue;
+    if (ncols < 1 || ncols > 2 * kPfMaxRows || K % kGtKB != 0 || splits < 1) return cudaErrorInvalidValue;
     TcGemmArgs a{};
     a.wmap = *static_cast<const CUtensorMap*>(wmap);
     a.xmap = *static_cast<const CUtensorMap*>(xmap);
@@ -230,12 +233,13 @@ cudaError_t launch_tc_gemm(const LaunchCfg& lc, const void* wmap, const void* xm
     a.N = N;
     a.K = K;
     a.ncols = ncols;
-    a.ntile = (ncols + 15) / 16 * 16;
+    a.ntile = ncols > 128 ? 128 : (ncols + 15) / 16 * 16;
     a.tiles = (N + 127) / 128;
+    a.ctiles = (ncols + 127) / 128;
     a.splits = splits;
     if (splits > 1 && splits > K / kGtKB / 2) return cudaErrorInvalidValue;
     a.err = err;
-    const int items = a.tiles * splits;
+    const int items = a.tiles * a.ctiles * splits;
     const int grid = items < lc.num_sms ? items : lc.num_sms;
     return launch_kernel(lc, tc_gemm_kernel, dim3(grid), dim3(kGtThreads), kGtSmem, a);
 }

@@ -33,6 +33,8 @@ constexpr int kPageTokens = 16;
 constexpr int kConvRing = 4;       // ring slots for the causal conv window (kernel 4)
 constexpr int kMaxTopK = 16;
 constexpr int kMaxSplits = 64;     // split-K partitions of decode attention
+constexpr int kPfMaxSplits = 8;    // key-range splits of the prefill attention (partial slots per row and head)
+constexpr int kPfMaxRows = 512;    // rows (prompt tokens) of one prefill chunk: the grouping kernel's source-row limit
 constexpr int kGemvRowsPerStage = 4;
 constexpr int kAttnMaxScoreSmem = 160 * 1024;  // dynamic smem bound of the decode attention
 
@@ -141,6 +143,7 @@ struct BatchBuffers {
     int cap = 0;
     int max_segs = 0;
     int max_pairs = 0;
+    size_t c_cap = 0;     // floats of c (the GEMM partials share it: S x 2n x N <= c_cap)
     int* slots;           // [cap] sequence slot of batch row b
     int* tok;             // [cap] input token of row b, replaced by its argmax
     float* x;             // [cap][H] residual stream (block input / output)
@@ -172,6 +175,10 @@ struct BatchBuffers {
     uint8_t* xgu;         // [max_cols][H] bf16: staged gate/up operand (64-column swizzled tiles per segment)
     uint8_t* xdn;         // [max_cols][I] bf16: staged down operand (SwiGLU activations, hi/lo)
     float* eout;          // [cap][topk + 1][H] expert outputs of this rank's rows (k = topk: shared)
+    // prefill only (rows = prompt tokens of one sequence)
+    float* pf_raw;        // [cap][qkv_dim] pre-conv GDN projections of the chunk's tokens
+    uint16_t* pf_qhi;     // [cap][Hq][D] prepared q, bf16 hi
+    uint16_t* pf_qlo;     // [cap][Hq][D] bf16 lo
     unsigned* ep_flags;   // [2][kMaxRanks] barrier flags written by the peers
     unsigned* ep_epoch;   // [2] barriers passed (per kind)
     float* cand_val;      // [cap][kHeadChunks]
@@ -251,7 +258,7 @@ cudaError_t launch_head(const LaunchCfg& lc, const Dims& d, const uint16_t* fina
 // ---- batched decode step (dm_batch.cu, dm_batch_moe.cu and the batched variants of the
 // GDN recurrence and the attention).  n = batch rows of this step.
 enum BPrepMode { BPREP_RMS = 0, BPREP_HEADNORM = 1, BPREP_COPY = 2 };
-enum BEpiMode { BEPI_GDN_IN = 0, BEPI_ATTN_IN = 1, BEPI_RESID = 2 };
+enum BEpiMode { BEPI_GDN_IN = 0, BEPI_ATTN_IN = 1, BEPI_RESID = 2, BEPI_GDN_PF = 3 };
 cudaError_t launch_b_embed(const LaunchCfg& lc, const Dims& d, const uint16_t* embed, const BatchBuffers& bb,
                            const Buffers& b, int n);
 // xcat rows from x [n][K]: RMSNorm with gamma, head norm (o = x, z, w), or a copy
@@ -288,9 +295,24 @@ cudaError_t launch_b_combine(const LaunchCfg& lc, const Dims& d, const BatchBuff
                              int n);
 // Cross-rank barrier of the expert-parallel group (kind 0 or 1), one small kernel.
 cudaError_t launch_ep_barrier(const LaunchCfg& lc, const BatchBuffers& bb, const Buffers& b, int kind);
+// advance: the rows' sequence positions grow by one (decode); 0 leaves them (prefill)
 cudaError_t launch_b_argmax(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const Buffers& b, int n,
-                            int write_logits, int record_gen);
+                            int write_logits, int record_gen, int advance = 1);
 cudaError_t batch_set_attrs();
+// rows (sources x 1) the top-k grouping kernel can take for E experts on one rank
+int b_group_max_rows(int E);
+// ---- prefill of one sequence: n prompt tokens (rows) at positions pos0 .. pos0 + n - 1 ----
+// GDN input-projection epilogue of a prefill chunk: pre-conv rows -> pf_raw, SiLU(z), a b
+cudaError_t launch_b_epi_gdn_pf(const LaunchCfg& lc, const Dims& d, const BatchBuffers& pb, int n, int splits);
+// GDN recurrence over the chunk's tokens (state and conv window of (layer, slot)), then the
+// conv window advanced to the chunk's last positions
+cudaError_t launch_pf_gdn(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& pb,
+                          const Buffers& b, int slot, int pos0, int n);
+// causal attention of the chunk: preparation + append, split partials, merge + gate into pb.xcat
+cudaError_t launch_pf_attn(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& pb,
+                           const Buffers& b, int slot, int pos0, int n);
+int pf_attn_nsplit(int num_sms, int Hkv, int n);
+cudaError_t pf_attn_set_attrs();
 bool expert_tc_supported(int K);
 // SHA-256 (FIPS 180-4) of the concatenation of n buffers (dm_sha256.cu).
 void sha256_parts(const uint8_t* const* parts, const size_t* sizes, int n, uint8_t out[32]);

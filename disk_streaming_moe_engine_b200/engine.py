@@ -356,6 +356,22 @@ class Engine:
                                      C.byref(nxt)))
         return logits, nxt.value
 
+    def prefill(self, tokens, slot: int = 0, want_logits: bool = True):
+        """The prompt `tokens` appended to `slot` as chunked prefill (dm_prefill: chunks of
+        prefill_rows() tokens through every layer together) -> (logits, argmax)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(self.cfg.vocab_size, np.float32) if want_logits else None
+        nxt = C.c_int32()
+        self._ok(self.lib.dm_prefill(self.ctx, slot, _ptr(t), t.size, None if logits is None else _ptr(logits),
+                                     C.byref(nxt)))
+        return logits, nxt.value
+
+    def prefill_rows(self):
+        """(rows of one prefill chunk, kernel launches of a chunk without the head)."""
+        r, k = C.c_int32(), C.c_int32()
+        self._ok(self.lib.dm_prefill_rows(self.ctx, C.byref(r), C.byref(k)))
+        return r.value, k.value
+
     def decode_step(self, token: int, slot: int = 0, want_logits: bool = False):
         logits = np.empty(self.cfg.vocab_size, np.float32) if want_logits else None
         out = C.c_int32()

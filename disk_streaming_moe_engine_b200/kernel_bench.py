@@ -13,6 +13,7 @@ the small-case driver for ncu captures of a single kernel.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 
 import numpy as np
@@ -25,7 +26,8 @@ KERNELS = {"in_proj": _lib.DM_KERNEL_MIXER_IN, "out_proj": _lib.DM_KERNEL_MIXER_
            "core": _lib.DM_KERNEL_MIXER_CORE, "router": _lib.DM_KERNEL_ROUTER, "moe": _lib.DM_KERNEL_MOE,
            "head": _lib.DM_KERNEL_HEAD}
 # kernels of the batched step (--batch N): layer is the preset's attention or GDN layer
-BKERNELS = {"battn": _lib.DM_BKERNEL_ATTN, "bgdn": _lib.DM_BKERNEL_GDN_REC, "bexperts": _lib.DM_BKERNEL_EXPERTS}
+BKERNELS = {"battn": _lib.DM_BKERNEL_ATTN, "bgdn": _lib.DM_BKERNEL_GDN_REC, "bexperts": _lib.DM_BKERNEL_EXPERTS,
+            "brouter": _lib.DM_BKERNEL_ROUTER, "bgemm": _lib.DM_BKERNEL_GEMM_IN}
 
 
 def batched(a, cfg):
@@ -77,8 +79,11 @@ def main():
     ap.add_argument("--warm", action="store_true")
     ap.add_argument("--trace", action="store_true", help="also report the kernel's phase stamps")
     ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--vocab", type=int, default=0, help="override the preset's vocabulary (e.g. 151936 for the head)")
     a = ap.parse_args()
     cfg = preset(a.preset)
+    if a.vocab:
+        cfg = dataclasses.replace(cfg, vocab_size=a.vocab)
     if a.kernel in BKERNELS:
         if a.batch <= 0:
             raise SystemExit("--batch N is required for the batched kernels")

@@ -284,6 +284,19 @@ int32_t dm_block_forward(dm_ctx* ctx, int32_t layer, int32_t slot, int32_t pos_o
 int32_t dm_forward(dm_ctx* ctx, int32_t slot, const int32_t* tokens_host, int32_t n,
                    float* logits_host, int32_t* next_token);
 
+/* The same call as dm_forward for a prompt (reference cmd_decode.mojo:1958-1971: the prefill
+ * call of forward_port_macro_scheduler_gguf with seq = n; cmd_forward.mojo:1221), run as
+ * chunked prefill: chunks of up to dm_prefill_rows tokens go through every layer together
+ * (dense projections and experts as tensor-core GEMMs over the chunk's tokens, the GDN
+ * recurrence over the chunk, causal attention over the cache plus the chunk), the K/V of every
+ * prompt token appended and the GDN state and conv window advanced as n decode steps would.
+ * Numerics are those of the batched step (experts with fp16-rounded weights).  logits_host
+ * [V] receives the last token's logits (may be NULL), next_token their argmax. */
+int32_t dm_prefill(dm_ctx* ctx, int32_t slot, const int32_t* tokens_host, int32_t n, float* logits_host,
+                   int32_t* next_token);
+/* Rows (prompt tokens) of one prefill chunk, and the kernel launches of a chunk. */
+int32_t dm_prefill_rows(dm_ctx* ctx, int32_t* rows_out, int32_t* kernels_per_chunk_out);
+
 /* One decode step (the per-step call of reference cmd_decode.mojo:2014-2045): embeds
  * token_in at the slot's current position, runs every block and the head, appends KV,
  * advances the slot by one and returns the greedy next token (and logits if non-NULL). */
@@ -366,6 +379,8 @@ int32_t dm_kernels_per_step(dm_ctx* ctx, int32_t* out);
 #define DM_BKERNEL_ATTN 0      /* batched paged decode attention of an attention layer  */
 #define DM_BKERNEL_GDN_REC 1   /* batched GDN recurrence of a GDN layer                  */
 #define DM_BKERNEL_EXPERTS 2   /* gate/up + down expert kernels (last layer's grouping)  */
+#define DM_BKERNEL_ROUTER 3    /* canonical RMSNorm + router rows + softmax/top-k        */
+#define DM_BKERNEL_GEMM_IN 4   /* the layer's input projection on the tensor-core GEMM  */
 int32_t dm_time_kernel(dm_ctx* ctx, int32_t which, int32_t layer, int32_t iters, float* avg_ms,
                        uint64_t* bytes);
 
