@@ -65,10 +65,12 @@ def parse():
     ap.add_argument("--cpu-sample-steps", type=int, default=3,
                     help="real 40-block CPU tokens timed for the cpu_baseline key (median)")
     ap.add_argument("--timeline", default="", help="also trace one decode step; write its launch timeline here")
-    ap.add_argument("--workload", default=None, choices=["c2", "c3", "spill"],
+    ap.add_argument("--workload", default=None, choices=["c2", "c3", "c4", "spill"],
                     help="c2: bs1 decode (BASELINE config 2; default of a plain run); c3: batched decode of 64 "
                          "sequences at 32768 cached tokens each (config 3; default under torchrun or with "
-                         "--gpus > 1); spill: bs1 decode with the expert pool spilled to host memory "
+                         "--gpus > 1); c4: prefill of 8 x 8192 random tokens (config 4; its long-context "
+                         "decode half is c3 with --batch 4 --c3-ctx 131072 --router-skew 0); "
+                         "spill: bs1 decode with the expert pool spilled to host memory "
                          "(--expert-slots per layer in HBM)")
     ap.add_argument("--expert-slots", type=int, default=64, help="spill: routed expert records per layer in HBM")
     ap.add_argument("--batch", type=int, default=64, help="c3: sequences per step")
@@ -177,13 +179,15 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-def measured_peak():
+def measured_peak(key: str = "hbm_gbs"):
+    """(peak, "measured" | "fallback"): HBM copy GB/s or bf16 GEMM TFLOP/s of this pool."""
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             j = json.load(f)
-        return float(j["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        if key in j:
+            return float(j[key]), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}[key], "fallback"
 
 
 def profiled_traffic(name: str):
@@ -529,6 +533,9 @@ def main():
     if args.workload == "spill":
         from disk_streaming_moe_engine_b200 import bench_spill
         return bench_spill.run(args)
+    if args.workload == "c4":
+        from disk_streaming_moe_engine_b200 import bench_prefill
+        return bench_prefill.run(args, rank, local, world)
     return run_ours(args, rank, local, world)
 
 

@@ -63,7 +63,8 @@ def c3_metric(B: int) -> str:
 
 
 def c3_workload(B: int, L: int) -> str:
-    return (f"config3: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit g64 experts, {B} sequences x {L} cached "
+    name = "config4 long-context decode" if (B, L) == (4, 131072) else "config3"
+    return (f"{name}: 40-block Qwen3.6-35B-A3B-shape decode, 4-bit g64 experts, {B} sequences x {L} cached "
             "tokens, paged (16-token pages, permuted pool)")
 
 

@@ -363,6 +363,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t op_xgu = T(pmax_cols * H * 2), op_xdn = T(pmax_cols * d.I * 2);
     const size_t op_cv = T(kHeadChunks * 4), op_ci = T(kHeadChunks * 4), op_hl = T(static_cast<size_t>(d.V) * 4);
     const size_t op_gen = T(16), op_genidx = T(4);
+    const size_t op_u = T(PR * d.qkv_dim * 4);
     const size_t op_raw = T(PR * d.qkv_dim * 4), op_qhi = T(PR * d.Hq * d.D * 2), op_qlo = T(PR * d.Hq * d.D * 2);
     c->arena_bytes = p.off;
     if (!commit) return DM_OK;
@@ -521,6 +522,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     pb.gen_idx = reinterpret_cast<int*>(A + op_genidx);
     pb.gen_cap = 0;
     pb.pf_raw = reinterpret_cast<float*>(A + op_raw);
+    pb.pf_u = reinterpret_cast<float*>(A + op_u);
     pb.pf_qhi = reinterpret_cast<uint16_t*>(A + op_qhi);
     pb.pf_qlo = reinterpret_cast<uint16_t*>(A + op_qlo);
     set_local_ep(c);
@@ -2159,6 +2161,9 @@ static int pf_kernels_per_chunk(const Dims& d);
 int32_t dm_prefill(dm_ctx* c, int32_t slot, const int32_t* tokens, int32_t n, float* logits, int32_t* next) {
     if (!c || !tokens || n <= 0) return DM_ERR_INVALID_ARG;
     if (spilling(c)) return spill_reject(c, "dm_prefill");
+    if (!pf_gdn_supported(c->d))
+        return set_err(c, DM_ERR_INVALID_ARG, "PREFILL_UNSUPPORTED", "prefill", -1,
+                       "GDN head dimension %d has no prefill kernel (64 or 128)", c->d.dk);
     int rc = prepare_decode(c, slot, n);
     if (rc != DM_OK) return rc;
     for (int i = 0; i < n; ++i)
@@ -2303,7 +2308,7 @@ static cudaError_t enqueue_pf_chunk(dm_ctx* c, int slot, int pos0, int n, bool h
             if (e == cudaSuccess) e = bgemm(c, pb, 2 * l + 1, d.H, d.Hq * d.D, n, &sp);
         } else {
             if (e == cudaSuccess) e = bgemm(c, pb, 2 * l, d.gdn_in_rows, d.H, n, &sp);
-            if (e == cudaSuccess) e = launch_b_epi_gdn_pf(lc, d, pb, n, sp);
+            if (e == cudaSuccess) e = launch_b_epi_gdn_pf(lc, d, w, pb, n, sp);
             if (e == cudaSuccess) e = launch_pf_gdn(lc, d, w, pb, c->b, slot, pos0, n);
             if (e == cudaSuccess)
                 e = launch_b_prep(lc, BPREP_HEADNORM, pb.o, d.z_dim, nullptr, d.eps, pb.z, w.gdn_norm, d.dv, pb.xcat, n);
@@ -2328,10 +2333,10 @@ static cudaError_t enqueue_pf_chunk(dm_ctx* c, int slot, int pos0, int n, bool h
 
 // Kernel launches of one prefill chunk (the head excluded).
 static int pf_kernels_per_chunk(const Dims& d) {
-    // embed + per GDN layer 14 (prep, gemm, epi, scan, ring, prep, gemm, resid, router,
-    // group, xstage, 2 experts, combine) + per attention layer 13 (prep, gemm, epi, attn
+    // embed + per GDN layer 15 (prep, gemm, epi, conv, scan, ring, prep, gemm, resid,
+    // router, group, xstage, 2 experts, combine) + per attention layer 13 (prep, gemm, epi, attn
     // prep, attn, merge, gemm, resid, router, group, xstage, 2 experts, combine)
-    return 1 + 14 * d.n_gdn + 13 * d.n_att;
+    return 1 + 15 * d.n_gdn + 13 * d.n_att;
 }
 
 // ---- spilling expert pool -----------------------------------------------------------

@@ -128,6 +128,8 @@ struct BEpiArgs {
     // GDN input projection: [qkv | z | a b] -> conv ring slot pos % 4, SiLU(z), a b
     float* ring;       // layer base [max_seqs][4][qkv_dim]
     float* raw;        // prefill: [n][qkv_dim] pre-conv rows of the chunk
+    const float* a_log;    // prefill: [nv] of the layer (decay g written instead of a)
+    const float* dt_bias;  // prefill: [nv]
     const int* slots;
     const int* pos;
     int qkv_dim, z_dim;
@@ -171,9 +173,9 @@ __global__ void __launch_bounds__(256) b_epi_kernel(const __grid_constant__ BEpi
             a.raw[static_cast<size_t>(b) * a.qkv_dim + col] = v;
         } else if (col < a.qkv_dim + a.z_dim) {
             a.z[static_cast<size_t>(b) * a.z_dim + (col - a.qkv_dim)] = silu_f(v);
-        } else {
-            const int nab = a.N - a.qkv_dim - a.z_dim;
-            a.ab[static_cast<size_t>(b) * nab + (col - a.qkv_dim - a.z_dim)] = v;
+        } else {  // the recurrence's decay g and beta of every V head
+            const int nab = a.N - a.qkv_dim - a.z_dim, nv = nab / 2, j = col - a.qkv_dim - a.z_dim;
+            a.ab[static_cast<size_t>(b) * nab + j] = j < nv ? gdn_decay(v, a.a_log[j], a.dt_bias[j]) : sigmoid_f(v);
         }
     } else if (MODE == BEPI_ATTN_IN) {
         if (col < a.qg_rows) a.qg[static_cast<size_t>(b) * a.qg_rows + col] = v;
@@ -200,8 +202,11 @@ cudaError_t launch_b_epi_gdn_in(const LaunchCfg& lc, const Dims& d, const LayerW
     return launch_kernel(lc, b_epi_kernel<BEPI_GDN_IN>, dim3((a.N + 255) / 256, n), dim3(256), 0, a);
 }
 
-cudaError_t launch_b_epi_gdn_pf(const LaunchCfg& lc, const Dims& d, const BatchBuffers& pb, int n, int splits) {
+cudaError_t launch_b_epi_gdn_pf(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& pb, int n,
+                                int splits) {
     BEpiArgs a{};
+    a.a_log = w.a_log;
+    a.dt_bias = w.dt_bias;
     a.c = pb.c;
     a.N = d.gdn_in_rows;
     a.n = n;

@@ -291,5 +291,23 @@ DM_DEV float sigmoid_f(float z) {
     return 1.0f / (1.0f + expf(-z));
 }
 DM_DEV float silu_f(float z) { return z * sigmoid_f(z); }
+// softplus with the reference's +-20 thresholds (_gdn_softplus, gdn.mojo:889-894)
+DM_DEV float softplus_ref(float v) {
+    if (v > 20.0f) return v;
+    if (v < -20.0f) return expf(v);
+    return logf(1.0f + expf(v));
+}
+// GDN decay of head h: exp(-exp(A_log) * softplus(a + dt_bias))
+DM_DEV float gdn_decay(float a, float a_log, float dt_bias) { return expf(-expf(a_log) * softplus_ref(a + dt_bias)); }
+
+// ---- cp.async (per-thread asynchronous global -> shared copies) -----------------------
+DM_DEV void cp_async16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+DM_DEV void cp_async4(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+DM_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+DM_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 }  // namespace dm

@@ -39,11 +39,6 @@ struct GdnRecArgs {
     int ab_bs, o_bs;
 };
 
-__device__ __forceinline__ float softplus_ref(float v) {
-    if (v > 20.0f) return v;
-    if (v < -20.0f) return expf(v);
-    return logf(1.0f + expf(v));
-}
 
 template <int DK>
 __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ GdnRecArgs a) {
@@ -527,139 +522,178 @@ cudaError_t launch_gdn_core_out(const LaunchCfg& lc, const Dims& d, const LayerW
 
 // ---- prefill: the recurrence over a chunk of n prompt tokens of one sequence ------------
 // The semantics above applied token after token (reference forward_gdn_block runs its
-// recurrence scan token by token, gdn.mojo:1040-1133), with the same arithmetic and order as
-// gdn_rec_kernel, so a prompt prefilled here leaves the state a token-by-token decode would.
-// Grid (nv, dv / 16), 128 threads: each CTA owns 16 state rows of one head in registers for
-// the whole chunk.  Tokens go in blocks of kPfTok: all threads first compute the block's
-// causal conv + SiLU (q, k of the head's QK head, this CTA's 16 v channels), k
-// normalisation, decay and beta into shared memory; then every warp runs its 4 rows through
-// the block's tokens (delta-rule update and o = S q, no block barrier in between).
-// Pre-conv inputs of position p: p < 0 zero, p < pos0 the conv window (ring slot p % 4),
-// else row p - pos0 of the chunk.
+// recurrence token by token, gdn.mojo:1040-1133), in two kernels:
+//   pf_conv_kernel  every (token, channel) at once: causal conv + SiLU of the pre-conv rows
+//                   (position p < 0: zero; p < pos0: the conv window, ring slot p % 4; else
+//                   row p - pos0 of the chunk), each k head divided by (||k|| + eps)
+//                   -> pf_u [n][qkv_dim]
+//   pf_gdn_kernel   grid (nv, dv / 16), 128 threads: 16 state rows of one head stay in
+//                   registers for the whole chunk, 8 lanes per row (dk / 8 columns each).
+//                   Tokens go in blocks of kPfTok: the block's q, k, this CTA's v channels,
+//                   decay and beta (computed by the projection's epilogue) are copied into
+//                   shared memory with cp.async while the previous block is scanned (two
+//                   buffers, one block barrier per block); every warp runs its 4 rows through
+//                   the block: sk = S k, sq = S q and k.q from one pass over the row (one
+//                   3-level butterfly for the three sums), S <- g (S - beta sk k^T) + beta v
+//                   k^T, and o = S_new q = g sq + beta (k.q) (v - g sk).
+// pf_ring_kernel then moves the conv window to the chunk's last positions.
 constexpr int kPfTok = 16;
 
-struct PfGdnArgs {
-    const float* raw;       // [n][qkv_dim]
+struct PfConvArgs {
+    const float* raw;       // [n][qkv_dim] pre-conv rows of the chunk
     const float* ring;      // [4][qkv_dim] of (layer, slot)
-    const uint16_t* conv_w;
-    float* S;               // [nv][dv][dk] of (layer, slot)
-    const float* a_log;
-    const float* dt_bias;
-    const float* ab;        // [n][2 nv]
-    float* o;               // [n][nv dv]
-    int n, pos0, nk, nv, qkv_dim;
+    const uint16_t* conv_w; // [qkv_dim][4]
+    float* u;               // [n][qkv_dim]
+    int n, pos0, qkv_dim, k0, k1, dk;
     float eps;
+};
+
+__global__ void __launch_bounds__(256) pf_conv_kernel(const __grid_constant__ PfConvArgs a) {
+    __shared__ float red[8];
+    const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ch = blockIdx.y * 256 + tid;
+    pdl_wait();
+    pdl_launch_dependents();
+    const int pos = a.pos0 + t;
+    float u = 0.0f;
+    if (ch < a.qkv_dim) {
+        const uint16_t* w = a.conv_w + static_cast<size_t>(ch) * 4;
+        float acc = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int tp = pos - 3 + j;
+            if (tp >= 0) {
+                const float pre = tp < a.pos0 ? a.ring[static_cast<size_t>(tp & 3) * a.qkv_dim + ch]
+                                              : a.raw[static_cast<size_t>(tp - a.pos0) * a.qkv_dim + ch];
+                acc += bf16_to_f32(w[j]) * pre;
+            }
+        }
+        u = silu_f(acc);
+    }
+    const int blk0 = blockIdx.y * 256;
+    if (blk0 + 256 > a.k0 && blk0 < a.k1) {  // the block holds k channels (uniform per block)
+        const bool isk = ch >= a.k0 && ch < a.k1;
+        const float ss = warp_sum(isk ? u * u : 0.0f);
+        if (lane == 0) red[warp] = ss;
+        __syncthreads();
+        const int wpg = a.dk / 32, g0 = (warp / wpg) * wpg;  // the warps of this thread's head
+        float tot = 0.0f;
+        for (int i = 0; i < wpg; ++i) tot += red[g0 + i];
+        if (isk) u *= 1.0f / (sqrtf(tot) + a.eps);
+    }
+    if (ch < a.qkv_dim) a.u[static_cast<size_t>(t) * a.qkv_dim + ch] = u;
+}
+
+
+struct PfGdnArgs {
+    const float* u;         // [n][qkv_dim] conv outputs (k normalised)
+    float* S;               // [nv][dv][dk] of (layer, slot)
+    const float* gb;        // [n][2 nv]: decay g, then beta, of every V head
+    float* o;               // [n][nv dv]
+    int n, nk, nv, qkv_dim;
 };
 
 template <int DK>
 __global__ void __launch_bounds__(128) pf_gdn_kernel(const __grid_constant__ PfGdnArgs a) {
     constexpr int DV = DK;
-    constexpr int RB = 16;
-    constexpr int CPL = DK / 32;
-    constexpr int NCH = 2 * DK + RB;  // conv channels of this CTA: q, k, its v rows
-    __shared__ __align__(16) float qs[kPfTok][DK], ks[kPfTok][DK];
-    __shared__ float vs[kPfTok][RB], gs[kPfTok], bs[kPfTok];
+    constexpr int RB = 16;          // state rows per CTA
+    constexpr int CPL = DK / 8;     // columns per lane (8 lanes per row)
+    constexpr int NF4 = CPL / 4;    // float4 groups per lane: columns 4 sub + 32 m + i
+    static_assert(CPL % 4 == 0, "whole float4 groups");
+    // two buffers of one token block: q, k [kPfTok][DK], v [kPfTok][RB], g, beta [kPfTok]
+    constexpr int BUF = kPfTok * (2 * DK + RB + 2);
+    __shared__ __align__(16) float sm[2 * BUF];
     const int h = blockIdx.x, rb = blockIdx.y;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int sub = lane & 7, rr = lane >> 3;
+    const int rl = warp * 4 + rr;  // row of the CTA
+    const int row = rb * RB + rl;
     const int g_qk = h / (a.nv / a.nk);
-    float* Sh = a.S + static_cast<size_t>(h) * DV * DK;
-    float srow[4][CPL];
+    float* Srow = a.S + (static_cast<size_t>(h) * DV + row) * DK;
+    float s[CPL];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float* src = Sh + static_cast<size_t>(rb * RB + warp * 4 + i) * DK + lane * CPL;
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) srow[i][c] = src[c];
+    for (int m = 0; m < NF4; ++m) {
+        const float4 t = *reinterpret_cast<const float4*>(Srow + 4 * sub + 32 * m);
+        s[4 * m] = t.x; s[4 * m + 1] = t.y; s[4 * m + 2] = t.z; s[4 * m + 3] = t.w;
     }
-    const float alog = a.a_log[h], dtb = a.dt_bias[h];
     pdl_wait();
     pdl_launch_dependents();
-    const int q0 = g_qk * DK, k0 = a.nk * DK + g_qk * DK, v0 = 2 * a.nk * DK + h * DV + rb * RB;
-    for (int t0 = 0; t0 < a.n; t0 += kPfTok) {
-        const int nt = min(kPfTok, a.n - t0);
-        // ---- conv + SiLU of the block's tokens ----
-        for (int idx = tid; idx < nt * NCH; idx += 128) {
-            const int tt = idx / NCH, t = idx % NCH;
-            const int ch = t < DK ? q0 + t : (t < 2 * DK ? k0 + (t - DK) : v0 + (t - 2 * DK));
-            const uint16_t* w = a.conv_w + static_cast<size_t>(ch) * 4;
-            const int pos = a.pos0 + t0 + tt;
-            float acc = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int tp = pos - 3 + j;
-                if (tp >= 0) {
-                    const float pre = tp < a.pos0 ? a.ring[static_cast<size_t>(tp & 3) * a.qkv_dim + ch]
-                                                  : a.raw[static_cast<size_t>(tp - a.pos0) * a.qkv_dim + ch];
-                    acc += bf16_to_f32(w[j]) * pre;
-                }
-            }
-            const float u = silu_f(acc);
-            if (t < DK) qs[tt][t] = u;
-            else if (t < 2 * DK) ks[tt][t - DK] = u;
-            else vs[tt][t - 2 * DK] = u;
+    const float* uq = a.u + g_qk * DK;
+    const float* uk = a.u + a.nk * DK + g_qk * DK;
+    const float* uv = a.u + 2 * a.nk * DK + h * DV + rb * RB;
+    auto stage = [&](int blk, int buf) {
+        const int t0 = blk * kPfTok, nt = min(kPfTok, a.n - t0);
+        float* qs = sm + buf * BUF;
+        float* ks = qs + kPfTok * DK;
+        float* vs = ks + kPfTok * DK;
+        float* gs = vs + kPfTok * RB;
+        for (int i = tid; i < nt * (DK / 4); i += 128) {
+            const int tt = i / (DK / 4), c4 = i % (DK / 4);
+            const size_t off = static_cast<size_t>(t0 + tt) * a.qkv_dim + 4 * c4;
+            cp_async16(qs + tt * DK + 4 * c4, uq + off);
+            cp_async16(ks + tt * DK + 4 * c4, uk + off);
         }
-        if (tid < nt) {
-            const float* ab = a.ab + static_cast<size_t>(t0 + tid) * 2 * a.nv;
-            gs[tid] = expf(-expf(alog) * softplus_ref(ab[h] + dtb));
-            bs[tid] = sigmoid_f(ab[a.nv + h]);
+        for (int i = tid; i < nt * (RB / 4); i += 128) {
+            const int tt = i / (RB / 4), c4 = i % (RB / 4);
+            cp_async16(vs + tt * RB + 4 * c4, uv + static_cast<size_t>(t0 + tt) * a.qkv_dim + 4 * c4);
         }
-        __syncthreads();
-        // ---- k / (||k|| + eps): warp w normalises tokens w, w + 4, ... ----
-        for (int tt = warp; tt < nt; tt += 4) {
-            float kl[CPL];
-            float ss = 0.0f;
-#pragma unroll
-            for (int c = 0; c < CPL; ++c) {
-                kl[c] = ks[tt][lane * CPL + c];
-                ss = fmaf(kl[c], kl[c], ss);
-            }
-            ss = warp_sum(ss);
-            const float inv_nk = 1.0f / (sqrtf(ss) + a.eps);
-#pragma unroll
-            for (int c = 0; c < CPL; ++c) ks[tt][lane * CPL + c] = kl[c] * inv_nk;
+        for (int i = tid; i < 2 * nt; i += 128) {
+            const int tt = i >> 1, which = i & 1;
+            cp_async4(gs + which * kPfTok + tt, a.gb + static_cast<size_t>(t0 + tt) * 2 * a.nv + which * a.nv + h);
         }
-        __syncthreads();
-        // ---- the warp's 4 rows through the block's tokens ----
+        cp_async_commit();
+    };
+    const int nblk = (a.n + kPfTok - 1) / kPfTok;
+    stage(0, 0);
+    for (int blk = 0; blk < nblk; ++blk) {
+        cp_async_wait_all();
+        __syncthreads();  // block blk has landed; every warp is done with the other buffer
+        if (blk + 1 < nblk) stage(blk + 1, (blk + 1) & 1);
+        const float* qs = sm + (blk & 1) * BUF;
+        const float* ks = qs + kPfTok * DK;
+        const float* vs = ks + kPfTok * DK;
+        const float* gs = vs + kPfTok * RB;
+        const int t0 = blk * kPfTok, nt = min(kPfTok, a.n - t0);
         for (int tt = 0; tt < nt; ++tt) {
             float kl[CPL], ql[CPL];
 #pragma unroll
-            for (int c = 0; c < CPL; ++c) {
-                kl[c] = ks[tt][lane * CPL + c];
-                ql[c] = qs[tt][lane * CPL + c];
+            for (int m = 0; m < NF4; ++m) {
+                const float4 k4 = *reinterpret_cast<const float4*>(ks + tt * DK + 4 * sub + 32 * m);
+                const float4 q4 = *reinterpret_cast<const float4*>(qs + tt * DK + 4 * sub + 32 * m);
+                kl[4 * m] = k4.x; kl[4 * m + 1] = k4.y; kl[4 * m + 2] = k4.z; kl[4 * m + 3] = k4.w;
+                ql[4 * m] = q4.x; ql[4 * m + 1] = q4.y; ql[4 * m + 2] = q4.z; ql[4 * m + 3] = q4.w;
             }
-            const float g = gs[tt], beta = bs[tt];
-            float* o_out = a.o + static_cast<size_t>(t0 + tt) * a.nv * DV + h * DV;
+            float sk0 = 0.0f, sk1 = 0.0f, sq0 = 0.0f, sq1 = 0.0f, kq = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int rl = warp * 4 + i;
-                float sk = 0.0f;
-#pragma unroll
-                for (int c = 0; c < CPL; ++c) sk = fmaf(srow[i][c], kl[c], sk);
-                sk = warp_sum(sk);
-                const float vr = vs[tt][rl];
-                const float bsk = beta * sk, bvr = beta * vr;
-                float oacc = 0.0f;
-#pragma unroll
-                for (int c = 0; c < CPL; ++c) {
-                    const float sn = g * (srow[i][c] - bsk * kl[c]) + bvr * kl[c];
-                    srow[i][c] = sn;
-                    oacc = fmaf(sn, ql[c], oacc);
-                }
-                oacc = warp_sum(oacc);
-                if (lane == 0) o_out[rb * RB + rl] = oacc;
+            for (int c = 0; c < CPL; c += 2) {
+                sk0 = fmaf(s[c], kl[c], sk0);
+                sk1 = fmaf(s[c + 1], kl[c + 1], sk1);
+                sq0 = fmaf(s[c], ql[c], sq0);
+                sq1 = fmaf(s[c + 1], ql[c + 1], sq1);
+                kq = fmaf(kl[c], ql[c], fmaf(kl[c + 1], ql[c + 1], kq));
             }
+            float sk = sk0 + sk1, sq = sq0 + sq1;
+#pragma unroll
+            for (int m = 4; m >= 1; m >>= 1) {
+                sk += __shfl_xor_sync(0xffffffffu, sk, m);
+                sq += __shfl_xor_sync(0xffffffffu, sq, m);
+                kq += __shfl_xor_sync(0xffffffffu, kq, m);
+            }
+            const float g = gs[tt], beta = gs[kPfTok + tt], vr = vs[tt * RB + rl];
+            const float bsk = beta * sk, bvr = beta * vr;
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) s[c] = g * (s[c] - bsk * kl[c]) + bvr * kl[c];
+            if (sub == 0)
+                a.o[static_cast<size_t>(t0 + tt) * a.nv * DV + h * DV + row] = g * sq + beta * kq * (vr - g * sk);
         }
-        __syncthreads();  // the block's shared inputs are consumed before the next block
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float* dst = Sh + static_cast<size_t>(rb * RB + warp * 4 + i) * DK + lane * CPL;
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) dst[c] = srow[i][c];
-    }
+    for (int m = 0; m < NF4; ++m)
+        *reinterpret_cast<float4*>(Srow + 4 * sub + 32 * m) = make_float4(s[4 * m], s[4 * m + 1], s[4 * m + 2], s[4 * m + 3]);
 }
 
 // The conv window after the chunk: the pre-conv rows of its last min(n, 4) positions into
-// their ring slots (after pf_gdn_kernel, which reads the window the chunk started from).
+// their ring slots (after pf_conv_kernel, which read the window the chunk started from).
 __global__ void __launch_bounds__(256) pf_ring_kernel(const float* __restrict__ raw, float* ring, int n, int pos0,
                                                       int qkv_dim) {
     pdl_wait();
@@ -672,29 +706,41 @@ __global__ void __launch_bounds__(256) pf_ring_kernel(const float* __restrict__ 
     for (int c = blockIdx.x * 256 + threadIdx.x; c < qkv_dim; c += gridDim.x * 256) dst[c] = src[c];
 }
 
+bool pf_gdn_supported(const Dims& d) {
+    return (d.dk == 128 || d.dk == 64) && d.dv == d.dk && 256 % d.dk == 0 && d.qkv_dim % 32 == 0;
+}
+
 cudaError_t launch_pf_gdn(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& pb,
                           const Buffers& b, int slot, int pos0, int n) {
-    PfGdnArgs a{};
+    if (!pf_gdn_supported(d)) return cudaErrorInvalidValue;
     const size_t ls = static_cast<size_t>(w.sub) * d.max_seqs + slot;
     float* ring = b.ring + ls * kConvRing * d.qkv_dim;
-    a.raw = pb.pf_raw;
-    a.ring = ring;
-    a.conv_w = w.conv_w;
+    PfConvArgs c{};
+    c.raw = pb.pf_raw;
+    c.ring = ring;
+    c.conv_w = w.conv_w;
+    c.u = pb.pf_u;
+    c.n = n;
+    c.pos0 = pos0;
+    c.qkv_dim = d.qkv_dim;
+    c.k0 = d.nk * d.dk;
+    c.k1 = 2 * d.nk * d.dk;
+    c.dk = d.dk;
+    c.eps = d.eps;
+    cudaError_t e = launch_kernel(lc, pf_conv_kernel, dim3(n, (d.qkv_dim + 255) / 256), dim3(256), 0, c);
+    if (e != cudaSuccess) return e;
+    PfGdnArgs a{};
+    a.u = pb.pf_u;
     a.S = b.S + ls * static_cast<size_t>(d.nv) * d.dv * d.dk;
-    a.a_log = w.a_log;
-    a.dt_bias = w.dt_bias;
-    a.ab = pb.ab;
+    a.gb = pb.ab;
     a.o = pb.o;
     a.n = n;
-    a.pos0 = pos0;
     a.nk = d.nk;
     a.nv = d.nv;
     a.qkv_dim = d.qkv_dim;
-    a.eps = d.eps;
     const dim3 grid(d.nv, d.dv / 16);
-    cudaError_t e = cudaErrorInvalidValue;
-    if (d.dk == 128) e = launch_kernel(lc, pf_gdn_kernel<128>, grid, dim3(128), 0, a);
-    else if (d.dk == 64) e = launch_kernel(lc, pf_gdn_kernel<64>, grid, dim3(128), 0, a);
+    e = d.dk == 128 ? launch_kernel(lc, pf_gdn_kernel<128>, grid, dim3(128), 0, a)
+                    : launch_kernel(lc, pf_gdn_kernel<64>, grid, dim3(128), 0, a);
     if (e != cudaSuccess) return e;
     return launch_kernel(lc, pf_ring_kernel, dim3((d.qkv_dim + 255) / 256, 4), dim3(256), 0, pb.pf_raw, ring, n, pos0,
                          d.qkv_dim);

@@ -177,6 +177,7 @@ struct BatchBuffers {
     float* eout;          // [cap][topk + 1][H] expert outputs of this rank's rows (k = topk: shared)
     // prefill only (rows = prompt tokens of one sequence)
     float* pf_raw;        // [cap][qkv_dim] pre-conv GDN projections of the chunk's tokens
+    float* pf_u;          // [cap][qkv_dim] their causal conv + SiLU (k heads normalised)
     uint16_t* pf_qhi;     // [cap][Hq][D] prepared q, bf16 hi
     uint16_t* pf_qlo;     // [cap][Hq][D] bf16 lo
     unsigned* ep_flags;   // [2][kMaxRanks] barrier flags written by the peers
@@ -302,8 +303,10 @@ cudaError_t batch_set_attrs();
 // rows (sources x 1) the top-k grouping kernel can take for E experts on one rank
 int b_group_max_rows(int E);
 // ---- prefill of one sequence: n prompt tokens (rows) at positions pos0 .. pos0 + n - 1 ----
-// GDN input-projection epilogue of a prefill chunk: pre-conv rows -> pf_raw, SiLU(z), a b
-cudaError_t launch_b_epi_gdn_pf(const LaunchCfg& lc, const Dims& d, const BatchBuffers& pb, int n, int splits);
+// GDN input-projection epilogue of a prefill chunk: pre-conv rows -> pf_raw, SiLU(z), the
+// decay g and beta of every V head -> pb.ab
+cudaError_t launch_b_epi_gdn_pf(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& pb, int n,
+                                int splits);
 // GDN recurrence over the chunk's tokens (state and conv window of (layer, slot)), then the
 // conv window advanced to the chunk's last positions
 cudaError_t launch_pf_gdn(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& pb,
@@ -312,6 +315,7 @@ cudaError_t launch_pf_gdn(const LaunchCfg& lc, const Dims& d, const LayerW& w, c
 cudaError_t launch_pf_attn(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& pb,
                            const Buffers& b, int slot, int pos0, int n);
 int pf_attn_nsplit(int num_sms, int Hkv, int n);
+bool pf_gdn_supported(const Dims& d);
 cudaError_t pf_attn_set_attrs();
 bool expert_tc_supported(int K);
 // SHA-256 (FIPS 180-4) of the concatenation of n buffers (dm_sha256.cu).
