@@ -112,6 +112,9 @@ SIGNATURES = {
     "dm_forward": (I32, [P, I32, P, I32, P, C.POINTER(I32)]),
     "dm_prefill": (I32, [P, I32, P, I32, P, C.POINTER(I32)]),
     "dm_prefill_rows": (I32, [P, C.POINTER(I32), C.POINTER(I32)]),
+    "dm_kmss_save_conv": (I32, [P, I32, C.c_char_p, C.c_char_p]),
+    "dm_kmss_load_conv": (I32, [P, I32, C.c_char_p, C.c_char_p]),
+    "dm_seq_copy": (I32, [P, I32, I32]),
     "dm_decode_step": (I32, [P, I32, I32, C.POINTER(I32), P]),
     "dm_generate": (I32, [P, I32, I32, I32, P]),
     "dm_enqueue_decode": (I32, [P, I32, I32]),

@@ -38,6 +38,8 @@ cudaError_t launch_dequant_sym4(cudaStream_t st, const uint8_t* packed, const ui
 cudaError_t launch_l2_flush_read(cudaStream_t st, const void* buf, size_t bytes, int num_sms);
 cudaError_t launch_kv_copy(cudaStream_t st, uint16_t* kv_layer, const int* page_table_row, int Hkv,
                            int D, uint16_t* k, uint16_t* v, int n_tokens, int to_cache);
+cudaError_t launch_kv_seq_copy(cudaStream_t st, uint16_t* kv_layer, const int* pt_src, const int* pt_dst, int Hkv,
+                               int D, int num_pages, int n_tokens, uint32_t* err);
 cudaError_t launch_synth_bf16(cudaStream_t st, uint16_t* dst, uint64_t n, uint64_t seed,
                               uint64_t stream_id, float mean, float std);
 cudaError_t launch_synth_f32(cudaStream_t st, float* dst, uint64_t n, uint64_t seed, uint64_t stream_id,
@@ -1750,6 +1752,11 @@ int32_t dm_gdn_state_import(dm_ctx* c, int32_t g, int32_t slot, const float* S_h
     return DM_OK;
 }
 
+// The conv window alone (positions len-3 .. len-1 from conv_host [3][qkv_dim]); S untouched.
+static int dm_gdn_state_import_conv(dm_ctx* c, int g, int slot, const float* conv_host) {
+    return dm_gdn_state_import(c, g, slot, nullptr, conv_host);
+}
+
 int32_t dm_gdn_state_export(dm_ctx* c, int32_t g, int32_t slot, float* S_host, float* conv_host) {
     int rc = check_slot(c, slot);
     if (rc != DM_OK) return rc;
@@ -1807,6 +1814,136 @@ static uint16_t f32_to_bf16_rne(float f) {  // round to nearest even; NaN stays 
     if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return static_cast<uint16_t>((u >> 16) | 0x40);
     const uint32_t r = u + 0x7FFFu + ((u >> 16) & 1u);
     return static_cast<uint16_t>(r >> 16);
+}
+
+int32_t dm_seq_copy(dm_ctx* c, int32_t src, int32_t dst) {
+    int rc = check_slot(c, src);
+    if (rc == DM_OK) rc = check_slot(c, dst);
+    if (rc != DM_OK) return rc;
+    if (src == dst) return DM_OK;
+    const Dims& d = c->d;
+    const int L = c->slot_len[src];
+    for (int a = 0; a < d.n_att; ++a)
+        if (c->att_len[static_cast<size_t>(a) * d.max_seqs + src] != L)
+            return set_err(c, DM_ERR_POSITION, "M5_ERR_DECODE", "seq_copy", -1,
+                           "source slot %d: attention layer %d holds %d positions, the sequence %d", src, a,
+                           c->att_len[static_cast<size_t>(a) * d.max_seqs + src], L);
+    cudaSetDevice(c->device);
+    const size_t kv_layer = static_cast<size_t>(d.num_pages) * 2 * d.Hkv * kPageTokens * d.D;
+    cudaError_t e = cudaSuccess;
+    for (int a = 0; a < d.n_att && e == cudaSuccess; ++a)
+        e = launch_kv_seq_copy(c->stream, c->b.kv + a * kv_layer, c->b.page_table + static_cast<size_t>(src) * d.max_pages,
+                               c->b.page_table + static_cast<size_t>(dst) * d.max_pages, d.Hkv, d.D, d.num_pages, L,
+                               c->b.err);
+    const size_t s_bytes = sizeof(float) * d.nv * d.dv * d.dk, r_bytes = sizeof(float) * kConvRing * d.qkv_dim;
+    if (e == cudaSuccess && d.n_gdn > 0)
+        e = cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(c->b.S) + dst * s_bytes, d.max_seqs * s_bytes,
+                              reinterpret_cast<uint8_t*>(c->b.S) + src * s_bytes, d.max_seqs * s_bytes, s_bytes, d.n_gdn,
+                              cudaMemcpyDeviceToDevice, c->stream);
+    if (e == cudaSuccess && d.n_gdn > 0)
+        e = cudaMemcpy2DAsync(reinterpret_cast<uint8_t*>(c->b.ring) + dst * r_bytes, d.max_seqs * r_bytes,
+                              reinterpret_cast<uint8_t*>(c->b.ring) + src * r_bytes, d.max_seqs * r_bytes, r_bytes, d.n_gdn,
+                              cudaMemcpyDeviceToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c->b.token + dst, c->b.token + src, 4, cudaMemcpyDeviceToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", "seq_copy", -1, "%s", cudaGetErrorString(e));
+    if ((rc = check_device_error(c, "seq_copy")) != DM_OK) return rc;
+    c->slot_len[dst] = L;
+    for (int a = 0; a < d.n_att; ++a) c->att_len[static_cast<size_t>(a) * d.max_seqs + dst] = L;
+    c->dev_pos_valid[dst] = 0;
+    return DM_OK;
+}
+
+// ---- GDN conv-window sidecar of a session file -----------------------------------------
+// KMSS v1 carries the recurrent states but not the causal-conv window (the last 3 pre-conv
+// projections of every GDN layer), so a resumed full-shape sequence would start from a zero
+// window.  The sidecar holds that window, bound to one KMSS file by its SHA-256 trailer:
+//   "KMCV" | u32 version 1 | u32 gdn layers | u32 qkv_dim | u32 sequence length |
+//   32-byte trailer of the KMSS file | fp32 [layers][3][qkv_dim] | SHA-256 of all the above
+static bool read_file(const char* path, std::vector<uint8_t>* out) {
+    FILE* f = fopen(path, "rb");
+    if (!f) return false;
+    fseek(f, 0, SEEK_END);
+    const long n = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    out->resize(n > 0 ? static_cast<size_t>(n) : 0);
+    const bool ok = n >= 0 && fread(out->data(), 1, out->size(), f) == out->size();
+    fclose(f);
+    return ok;
+}
+
+static void push_u32(std::vector<uint8_t>& b, uint32_t v) {
+    for (int i = 0; i < 4; ++i) b.push_back(static_cast<uint8_t>(v >> (8 * i)));
+}
+
+int32_t dm_kmss_save_conv(dm_ctx* c, int32_t slot, const char* kmss_path, const char* conv_path) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    if (!kmss_path || !conv_path) return DM_ERR_INVALID_ARG;
+    std::vector<uint8_t> kmss;
+    if (!read_file(kmss_path, &kmss) || kmss.size() < 32)
+        return set_err(c, DM_ERR_IO, "SESSION_NOT_FOUND", "session", -1, "session file not found: %s", kmss_path);
+    const Dims& d = c->d;
+    std::vector<uint8_t> b;
+    b.insert(b.end(), {'K', 'M', 'C', 'V'});
+    push_u32(b, 1);
+    push_u32(b, static_cast<uint32_t>(d.n_gdn));
+    push_u32(b, static_cast<uint32_t>(d.qkv_dim));
+    push_u32(b, static_cast<uint32_t>(c->slot_len[slot]));
+    b.insert(b.end(), kmss.end() - 32, kmss.end());
+    std::vector<float> conv(static_cast<size_t>(3) * d.qkv_dim);
+    for (int g = 0; g < d.n_gdn; ++g) {
+        if ((rc = dm_gdn_state_export(c, g, slot, nullptr, conv.data())) != DM_OK) return rc;
+        const uint8_t* p = reinterpret_cast<const uint8_t*>(conv.data());
+        b.insert(b.end(), p, p + conv.size() * 4);
+    }
+    uint8_t digest[32];
+    const uint8_t* parts[1] = {b.data()};
+    const size_t sizes[1] = {b.size()};
+    dm::sha256_parts(parts, sizes, 1, digest);
+    b.insert(b.end(), digest, digest + 32);
+    FILE* f = fopen(conv_path, "wb");
+    if (!f) return set_err(c, DM_ERR_IO, "IO_ERROR", "session", -1, "cannot write %s", conv_path);
+    const bool ok = fwrite(b.data(), 1, b.size(), f) == b.size();
+    fclose(f);
+    return ok ? DM_OK : set_err(c, DM_ERR_IO, "IO_ERROR", "session", -1, "short write to %s", conv_path);
+}
+
+int32_t dm_kmss_load_conv(dm_ctx* c, int32_t slot, const char* kmss_path, const char* conv_path) {
+    int rc = check_slot(c, slot);
+    if (rc != DM_OK) return rc;
+    if (!kmss_path || !conv_path) return DM_ERR_INVALID_ARG;
+    const Dims& d = c->d;
+    std::vector<uint8_t> kmss, b;
+    if (!read_file(kmss_path, &kmss) || kmss.size() < 32)
+        return set_err(c, DM_ERR_IO, "SESSION_NOT_FOUND", "session", -1, "session file not found: %s", kmss_path);
+    if (!read_file(conv_path, &b))
+        return set_err(c, DM_ERR_IO, "SESSION_NOT_FOUND", "session", -1, "conv-window file not found: %s", conv_path);
+    const size_t body = static_cast<size_t>(d.n_gdn) * 3 * d.qkv_dim * 4;
+    auto fail = [&](const char* type, const char* what) {
+        return set_err(c, DM_ERR_FORMAT, type, "session", -1, "%s", what);
+    };
+    if (b.size() != 52 + body + 32) return fail("LAYOUT_MISMATCH", "conv-window file size does not match the model");
+    if (memcmp(b.data(), "KMCV", 4) != 0) return fail("FORMAT_MISMATCH", "invalid conv-window magic bytes");
+    auto u32 = [&](size_t o) { return b[o] | (b[o + 1] << 8) | (b[o + 2] << 16) | (static_cast<uint32_t>(b[o + 3]) << 24); };
+    if (u32(4) != 1) return fail("VERSION_MISMATCH", "unsupported conv-window version");
+    if (u32(8) != static_cast<uint32_t>(d.n_gdn) || u32(12) != static_cast<uint32_t>(d.qkv_dim))
+        return fail("CONFIG_MISMATCH", "conv-window dimensions do not match the model of this context");
+    uint8_t digest[32];
+    const uint8_t* parts[1] = {b.data()};
+    const size_t sizes[1] = {52 + body};
+    dm::sha256_parts(parts, sizes, 1, digest);
+    if (memcmp(digest, b.data() + 52 + body, 32) != 0) return fail("CORRUPT_SESSION_CHECKSUM", "checksum mismatch in conv-window file");
+    if (memcmp(b.data() + 20, kmss.data() + kmss.size() - 32, 32) != 0)
+        return fail("SESSION_MISMATCH", "conv-window file belongs to another session file");
+    if (u32(16) != static_cast<uint32_t>(c->slot_len[slot]))
+        return fail("SESSION_MISMATCH", "conv-window sequence length differs from the slot's");
+    for (int g = 0; g < d.n_gdn; ++g) {
+        const float* conv = reinterpret_cast<const float*>(b.data() + 52 + static_cast<size_t>(g) * 3 * d.qkv_dim * 4);
+        std::vector<float> tmp(conv, conv + static_cast<size_t>(3) * d.qkv_dim);  // aligned copy
+        if ((rc = dm_gdn_state_import_conv(c, g, slot, tmp.data())) != DM_OK) return rc;
+    }
+    return DM_OK;
 }
 
 int32_t dm_kmss_save(dm_ctx* c, int32_t slot, const char* path, const int32_t* tokens, int32_t n_tokens,

@@ -53,6 +53,41 @@ cudaError_t launch_l2_flush_read(cudaStream_t st, const void* buf, size_t bytes,
     return cudaGetLastError();
 }
 
+// K/V rows of positions 0..n-1 of one attention layer from the pages of one sequence to
+// those of another (16-byte words; a page id outside [0, num_pages) sets the page error bit).
+__global__ void kv_seq_copy_kernel(uint16_t* kv, const int* pt_src, const int* pt_dst, int Hkv, int D, int num_pages,
+                                   int n_tokens, uint32_t* err) {
+    const int w_per_row = D / 8;  // 16-byte words of one head's row
+    const int64_t total = static_cast<int64_t>(n_tokens) * 2 * Hkv * w_per_row;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int w = static_cast<int>(i % w_per_row);
+        const int64_t r = i / w_per_row;
+        const int h = static_cast<int>(r % Hkv);
+        const int kvi = static_cast<int>((r / Hkv) % 2);
+        const int t = static_cast<int>(r / (2 * Hkv));
+        const int ps = pt_src[t / kPageTokens], pd = pt_dst[t / kPageTokens];
+        if (ps < 0 || ps >= num_pages || pd < 0 || pd >= num_pages) {
+            if (err) atomicOr(err, DM_DEVERR_PAGE);
+            continue;
+        }
+        const size_t in_page = ((static_cast<size_t>(kvi) * Hkv + h) * kPageTokens + t % kPageTokens) * D;
+        const uint4* src = reinterpret_cast<const uint4*>(kv + static_cast<size_t>(ps) * 2 * Hkv * kPageTokens * D + in_page);
+        uint4* dst = reinterpret_cast<uint4*>(kv + static_cast<size_t>(pd) * 2 * Hkv * kPageTokens * D + in_page);
+        dst[w] = src[w];
+    }
+}
+
+cudaError_t launch_kv_seq_copy(cudaStream_t st, uint16_t* kv_layer, const int* pt_src, const int* pt_dst, int Hkv,
+                               int D, int num_pages, int n_tokens, uint32_t* err) {
+    if (n_tokens <= 0) return cudaSuccess;
+    const int64_t total = static_cast<int64_t>(n_tokens) * 2 * Hkv * (D / 8);
+    int blocks = static_cast<int>((total + 255) / 256);
+    if (blocks > 8192) blocks = 8192;
+    kv_seq_copy_kernel<<<blocks, 256, 0, st>>>(kv_layer, pt_src, pt_dst, Hkv, D, num_pages, n_tokens, err);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_kv_copy(cudaStream_t st, uint16_t* kv_layer, const int* page_table_row, int Hkv, int D,
                            uint16_t* k, uint16_t* v, int n_tokens, int to_cache) {
     const int64_t total = static_cast<int64_t>(n_tokens) * Hkv * D;

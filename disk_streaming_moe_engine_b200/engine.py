@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import ctypes as C
 import dataclasses
+import os
 
 import numpy as np
 
@@ -460,8 +461,11 @@ class Engine:
         self._ok(self.lib.dm_tensor_add_rank1(self.ctx, layer, tensor_id, _ptr(beta), beta.size, _ptr(u), u.size))
 
     # ---- session files (reference KMSS v1, src/format/kmss.mojo) ----
-    def save_session(self, path: str, tokens, slot: int = 0, kv_dtype: int = 1, manifest_hash: bytes | None = None):
-        """write_kmss_v1 (kmss.mojo:90): the slot's KV cache and GDN states + the token prefix."""
+    def save_session(self, path: str, tokens, slot: int = 0, kv_dtype: int = 1, manifest_hash: bytes | None = None,
+                     conv_window: bool = True):
+        """write_kmss_v1 (kmss.mojo:90): the slot's KV cache and GDN states + the token prefix;
+        with conv_window also the GDN conv window in the sidecar `path + ".conv"`
+        (dm_kmss_save_conv), so that a resumed sequence decodes exactly as an uninterrupted one."""
         t = np.ascontiguousarray(tokens, np.int32)
         mh = None
         if manifest_hash is not None:
@@ -469,13 +473,22 @@ class Engine:
                 raise ValueError("manifest hash: 32 bytes")
             mh = C.create_string_buffer(bytes(manifest_hash), 32)
         self._ok(self.lib.dm_kmss_save(self.ctx, slot, path.encode(), _ptr(t) if t.size else None, t.size, kv_dtype, mh))
+        if conv_window:
+            self._ok(self.lib.dm_kmss_save_conv(self.ctx, slot, path.encode(), (path + ".conv").encode()))
 
     def load_session(self, path: str, slot: int = 0, max_tokens: int = 1 << 20) -> np.ndarray:
-        """read_kmss_v1 (kmss.mojo:280) into `slot`; returns the token prefix."""
+        """read_kmss_v1 (kmss.mojo:280) into `slot`; returns the token prefix.  A sidecar
+        `path + ".conv"` written with the file restores the GDN conv window as well."""
         out = np.empty(max_tokens, np.int32)
         n = C.c_int32()
         self._ok(self.lib.dm_kmss_load(self.ctx, slot, path.encode(), _ptr(out), out.size, C.byref(n)))
+        if os.path.exists(path + ".conv"):
+            self._ok(self.lib.dm_kmss_load_conv(self.ctx, slot, path.encode(), (path + ".conv").encode()))
         return out[:min(n.value, out.size)].copy()
+
+    def seq_copy(self, src_slot: int, dst_slot: int):
+        """The whole sequence state of src_slot into dst_slot, on the device (dm_seq_copy)."""
+        self._ok(self.lib.dm_seq_copy(self.ctx, src_slot, dst_slot))
 
     # ---- expert-parallel group (one process per GPU) ----
     def ep_ipc_handle(self) -> bytes:

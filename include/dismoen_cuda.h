@@ -499,6 +499,19 @@ int32_t dm_kmss_save(dm_ctx* ctx, int32_t slot, const char* path, const int32_t*
                      int32_t kv_dtype, const uint8_t* manifest_hash32);
 int32_t dm_kmss_load(dm_ctx* ctx, int32_t slot, const char* path, int32_t* tokens_out, int32_t cap,
                      int32_t* n_tokens);
+/* Lossless resume: the GDN conv window (not a KMSS v1 field) in a sidecar file bound to the
+ * KMSS file by its SHA-256 trailer ("KMCV", version, layers, qkv_dim, length, the KMSS
+ * trailer, fp32 [layers][3][qkv_dim], SHA-256).  save: after dm_kmss_save of the same slot;
+ * load: after dm_kmss_load into the slot (rejects another file's sidecar, a length or size
+ * mismatch and a corrupted file).  Without a sidecar a loaded slot starts from a zero window,
+ * as the reference's port semantics have none. */
+int32_t dm_kmss_save_conv(dm_ctx* ctx, int32_t slot, const char* kmss_path, const char* conv_path);
+int32_t dm_kmss_load_conv(dm_ctx* ctx, int32_t slot, const char* kmss_path, const char* conv_path);
+/* Copies the whole sequence state of slot src into slot dst on the device (K/V of every
+ * position through both page tables, GDN states and conv windows, length, next token): the
+ * snapshot and restore of the prefix cache (reference PrefixCache, core/prefix_cache.mojo:102,
+ * whose entries hold a copy of the KV cache and GDN state). */
+int32_t dm_seq_copy(dm_ctx* ctx, int32_t src_slot, int32_t dst_slot);
 /* SHA-256 of n bytes (FIPS 180-4); needs no device. */
 int32_t dm_sha256(const uint8_t* data, uint64_t n, uint8_t* out32);
 
