@@ -93,21 +93,41 @@ __global__ void __launch_bounds__(kGtThreads, 1) tc_gemm_kernel(const __grid_con
     if (warp == 0) {
         // ---------------- producer ----------------
         if (lane == 0) {
-            pdl_wait();  // the operand rows come from the kernel before; the weights do not
-            pdl_launch_dependents();
             uint32_t si = 0, sph = 0, issued = 0;
             const uint32_t bbytes = static_cast<uint32_t>(a.ntile) * kGtKB * 2;
             bool ok = true;
+            // The weights do not depend on the kernel before: the first item's first stages
+            // (as many as the ring holds) get their weight boxes before griddepcontrol.wait,
+            // so they stream while that kernel finishes; their operand boxes follow the wait.
+            int pre = 0;
+            if (blockIdx.x < nitems) {
+                const int item = blockIdx.x;
+                const int tile = item / (a.ctiles * a.splits), sp = item % a.splits;
+                const int kb0 = sp * kb_total / a.splits, kb1 = (sp + 1) * kb_total / a.splits;
+                pre = min(kb1 - kb0, kGtStages);
+                for (int p = 0; p < pre; ++p) {  // fresh stages: no empty wait
+                    uint8_t* st = sm + p * kGtStage;
+                    mbar_arrive_expect_tx(&full[p], kGtA + bbytes);
+                    tma_load_2d(st, &a.wmap, (kb0 + p) * kGtKB, tile * 128, &full[p]);
+                    tma_load_2d(st + kGtA / 2, &a.wmap, (kb0 + p) * kGtKB + 64, tile * 128, &full[p]);
+                }
+            }
+            pdl_wait();  // the operand rows come from the kernel before
+            pdl_launch_dependents();
             for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
                 const int tile = item / (a.ctiles * a.splits), ct = (item / a.splits) % a.ctiles, sp = item % a.splits;
                 // slice sp of K: [sp kbt / S, (sp + 1) kbt / S), at least 2 stages (S <= kbt / 2)
                 const int kb0 = sp * kb_total / a.splits, kb1 = (sp + 1) * kb_total / a.splits;
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!(ok = mbar_wait_bounded(&empty[si], sph ^ 1u, a.err, abort_flag))) break;
                     uint8_t* st = sm + si * kGtStage;
-                    mbar_arrive_expect_tx(&full[si], kGtA + bbytes);
-                    tma_load_2d(st, &a.wmap, kb * kGtKB, tile * 128, &full[si]);
-                    tma_load_2d(st + kGtA / 2, &a.wmap, kb * kGtKB + 64, tile * 128, &full[si]);
+                    if (pre > 0) {  // weights already in flight: the operand boxes only
+                        --pre;
+                    } else {
+                        if (!(ok = mbar_wait_bounded(&empty[si], sph ^ 1u, a.err, abort_flag))) break;
+                        mbar_arrive_expect_tx(&full[si], kGtA + bbytes);
+                        tma_load_2d(st, &a.wmap, kb * kGtKB, tile * 128, &full[si]);
+                        tma_load_2d(st + kGtA / 2, &a.wmap, kb * kGtKB + 64, tile * 128, &full[si]);
+                    }
                     tma_load_2d(st + kGtA, &a.xmap, kb * kGtKB, ct * 128, &full[si]);
                     tma_load_2d(st + kGtA + bbytes / 2, &a.xmap, kb * kGtKB + 64, ct * 128, &full[si]);
                     ++issued;
