@@ -40,10 +40,14 @@ struct GdnRecArgs {
 };
 
 
-template <int DK>
-__global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ GdnRecArgs a) {
+// RPW state rows per warp, NW warps: RB = RPW * NW rows of one head per CTA (the batched
+// step takes all dv rows in one CTA, so the conv, the k norm and the gates of a (row, head)
+// are computed once instead of once per 16-row block).
+template <int DK, int RPW = 4, int NW = 4>
+__global__ void __launch_bounds__(NW * 32) gdn_rec_kernel(const __grid_constant__ GdnRecArgs a) {
     constexpr int DV = DK;
-    constexpr int RB = 16;          // state rows per CTA
+    constexpr int RB = RPW * NW;    // state rows per CTA
+    constexpr int NT = NW * 32;
     constexpr int CPL = DK / 32;    // columns per lane
     __shared__ float qs[DK], ks[DK], vs[RB];
     const int h = blockIdx.x, rb = blockIdx.y;
@@ -58,10 +62,10 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
     kt_start(a.kt);
     // ---- prologue: this CTA's state rows (4 per warp) into registers ----
     float* Sh = a.S + slot * a.S_ss + static_cast<size_t>(h) * DV * DK;
-    float srow[4][CPL];
+    float srow[RPW][CPL];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int r = rb * RB + warp * 4 + i;
+    for (int i = 0; i < RPW; ++i) {
+        const int r = rb * RB + warp * RPW + i;
         const float* src = Sh + static_cast<size_t>(r) * DK + lane * CPL;
         if (CPL == 4) {
             const float4 t = *reinterpret_cast<const float4*>(src);
@@ -79,7 +83,7 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
 
     // ---- causal conv + SiLU for q (DK), k (DK) and this CTA's 16 v channels ----
     const int q0 = g_qk * DK, k0 = a.nk * DK + g_qk * DK, v0 = 2 * a.nk * DK + h * DV + rb * RB;
-    for (int t = threadIdx.x; t < 2 * DK + RB; t += 128) {
+    for (int t = threadIdx.x; t < 2 * DK + RB; t += NT) {
         const int ch = t < DK ? q0 + t : (t < 2 * DK ? k0 + (t - DK) : v0 + (t - 2 * DK));
         const uint16_t* w = a.conv_w + static_cast<size_t>(ch) * 4;
         float acc = 0.0f;
@@ -114,8 +118,8 @@ __global__ void __launch_bounds__(128) gdn_rec_kernel(const __grid_constant__ Gd
 
     // ---- delta-rule update and o = S q, one row at a time per warp ----
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int rl = warp * 4 + i;
+    for (int i = 0; i < RPW; ++i) {
+        const int rl = warp * RPW + i;
         const int r = rb * RB + rl;
         float sk = 0.0f;
 #pragma unroll
@@ -191,9 +195,10 @@ cudaError_t launch_gdn_rec_batch(const LaunchCfg& lc, const Dims& d, const Layer
     a.S_ss = static_cast<size_t>(d.nv) * d.dv * d.dk;
     a.ab_bs = 2 * d.nv;
     a.o_bs = d.z_dim;
-    const dim3 grid(d.nv, d.dv / 16, n);
-    if (d.dk == 128) return launch_kernel(lc, gdn_rec_kernel<128>, grid, dim3(128), 0, a);
-    if (d.dk == 64) return launch_kernel(lc, gdn_rec_kernel<64>, grid, dim3(128), 0, a);
+    // one CTA per (row, head): all dv state rows, 16 warps x dv / 16 rows
+    const dim3 grid(d.nv, 1, n);
+    if (d.dk == 128 && d.dv == 128) return launch_kernel(lc, gdn_rec_kernel<128, 8, 16>, grid, dim3(512), 0, a);
+    if (d.dk == 64 && d.dv == 64) return launch_kernel(lc, gdn_rec_kernel<64, 4, 16>, grid, dim3(512), 0, a);
     return cudaErrorInvalidValue;
 }
 
