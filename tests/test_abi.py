@@ -121,3 +121,47 @@ def test_plain_c_host_links_and_calls(tmp_path, lib):
     assert r["quant"] == [0, 1, 64, 1]
     # 4 slots: step 1 {0,1,2,3} misses 4; step 2 {2,3,4,5} hits 2, misses 2, evicts 0 and 1
     assert r["spill"] == [0, 8, 2, 6, 2]
+
+
+@pytest.mark.gpu
+def test_c_host_drives_the_decode_path(lib, oracle_lib, tmp_path):
+    """tests/c_abi/decode.c: a plain C program creates a context, synthesises the config-0
+    model on the device and runs dm_forward, dm_generate, dm_prefill and dm_decode_batch;
+    its ids equal the oracle's on the host generator's weights (the device generator is the
+    same), and a bad token comes back as an error status with the reference's error type."""
+    import json as _json
+    import shutil
+    import subprocess
+
+    import numpy as np
+
+    import oracle
+    from disk_streaming_moe_engine_b200 import _lib as L, preset, synth
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = str(tmp_path / "decode")
+    libdir = os.path.dirname(L.LIB_PATH)
+    subprocess.run([gcc, "-O1", "-std=c11", "-I", os.path.join(repo, "include"),
+                    os.path.join(repo, "tests", "c_abi", "decode.c"), "-o", exe, "-L", libdir, "-ldismoen_cuda",
+                    f"-Wl,-rpath,{libdir}", "-Wl,-rpath,/usr/local/cuda/lib64"], check=True)
+    cfg = preset("mini")
+    prompt = [int(t) for t in np.random.default_rng(7).integers(0, cfg.vocab_size, 11)]
+    out = subprocess.run([exe] + [str(t) for t in prompt], check=True, capture_output=True, text=True).stdout
+    r = _json.loads(out)
+    om = oracle.OracleModel(synth.synth_model(cfg, 0))
+    st = oracle.OracleState(cfg, 64)
+    tok = None
+    for t in prompt:
+        tok, _, _ = oracle.decode_step(om, st, t)
+    assert r["next_forward"] == tok and r["next_prefill"] == tok
+    gen = []
+    for _ in range(8):
+        tok, _, _ = oracle.decode_step(om, st, tok)
+        gen.append(tok)
+    assert r["generate"] == gen
+    assert r["len"] == [len(prompt) + 8, len(prompt)]
+    nxt, _, _ = oracle.decode_step(om, st, gen[7])
+    assert r["batch"] == [nxt, gen[0]]
+    assert r["bad_rc"] != 0 and "M4_ERR_INPUT" in r["bad_msg"]
