@@ -306,7 +306,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t o_qg = T(2 * d.Hq * d.D * 4), o_kvnew = T(2 * d.Hkv * d.D * 4);
     const size_t o_part = T(static_cast<size_t>(d.Hq) * kMaxSplits * (d.D + 2) * 4);
     const size_t o_aout = T(std::max(d.Hq * d.D, d.H) * 4);
-    const size_t o_xn = T(H * 4), o_rl = T((d.E + 1) * 4), o_ids = T(kMaxTopK * 4), o_p = T(kMaxTopK * 4);
+    const size_t o_xn = T(H * 4), o_rl = T((d.E + 1) * 8), o_ids = T(kMaxTopK * 4), o_p = T(kMaxTopK * 4);
     const size_t o_sg = T(4), o_h = T(static_cast<size_t>(d.topk + 1) * d.I * 4), o_logits = T(static_cast<size_t>(d.V) * 4);
     const size_t o_cv = T(kMaxCtas * 4), o_ci = T(kMaxCtas * 4), o_cnt = T(64 * 4), o_err = T(4);
     const size_t o_trace = T(kTraceSlots * 8);
@@ -421,7 +421,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     b.attn_part = reinterpret_cast<float*>(A + o_part);
     b.attn_out = reinterpret_cast<float*>(A + o_aout);
     b.xn = reinterpret_cast<float*>(A + o_xn);
-    b.rlogits = reinterpret_cast<float*>(A + o_rl);
+    b.rslots = reinterpret_cast<unsigned long long*>(A + o_rl);
     b.topk_ids = reinterpret_cast<int*>(A + o_ids);
     b.topk_p = reinterpret_cast<float*>(A + o_p);
     b.shared_g = reinterpret_cast<float*>(A + o_sg);
@@ -556,8 +556,8 @@ static int check_device_error(dm_ctx* c, const char* stage) {
     if (e != cudaSuccess) return set_err(c, DM_ERR_CUDA, "CUDA_ERROR", stage, -1, "%s", cudaGetErrorString(e));
     if (w == 0) return DM_OK;
     cudaMemset(c->b.err, 0, 4);
-    // a launch that gave up waiting may have left router logit slots filled
-    cudaMemset(c->b.rlogits, 0xFF, static_cast<size_t>(c->d.E + 1) * 4);
+    // a launch that gave up waiting may have left router logit words of its generation
+    cudaMemset(c->b.rslots, 0, static_cast<size_t>(c->d.E + 1) * 8);
     if (w & DM_DEVERR_TIMEOUT) return set_err(c, DM_ERR_TIMEOUT, "DEVICE_TIMEOUT", stage, -1, "a bounded device wait ran out (word 0x%x)", w);
     if (w & DM_DEVERR_CAPACITY) return set_err(c, DM_ERR_CAPACITY, "M5_ERR_CONTEXT_SIZE", stage, -1, "KV cache capacity exceeded on token append");
     if (w & DM_DEVERR_PAGE) return set_err(c, DM_ERR_CAPACITY, "KV_PAGE_ERROR", stage, -1, "page table entry outside the page pool");
@@ -809,8 +809,6 @@ int32_t dm_ctx_create(const dm_model_config* model, const dm_runtime_config* rt,
     plan_memory(c, true);
     // zero everything (weights stay zero until uploaded; state starts empty)
     e = cudaMemsetAsync(c->arena, 0, c->arena_bytes, c->stream);
-    // router logit slots start empty (all-ones NaN pattern; the MoE kernel polls them)
-    if (e == cudaSuccess) e = cudaMemsetAsync(c->b.rlogits, 0xFF, static_cast<size_t>(c->d.E + 1) * 4, c->stream);
     if (e == cudaSuccess)
         e = launch_rope_table(c->stream, c->b.rope, c->d.max_pages * kPageTokens, c->d.rot_dim, c->d.theta);
     if (e == cudaSuccess) e = cudaMallocHost(&c->h_io, 64);

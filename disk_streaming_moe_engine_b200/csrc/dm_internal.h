@@ -101,7 +101,7 @@ struct Buffers {
     float* attn_part;     // [Hq][kMaxSplits][D + 2]
     float* attn_out;      // [Hq*D]    gated attention output
     float* xn;            // [H]       post-attention RMSNorm output (MoE input)
-    float* rlogits;       // [E+1]     router logits + shared gate logit
+    unsigned long long* rslots; // [E+1] router logit words: launch tag << 32 | fp32 bits (zero: empty)
     int* topk_ids;        // [topk]
     float* topk_p;        // [topk]
     float* shared_g;      // [1]

@@ -235,6 +235,64 @@ __device__ __forceinline__ float q4_partial_smem(const uint8_t* chunk, int r, in
     return acc;
 }
 
+// Rows rA and rB of one chunk at once (one lane group per row pair, LPR == 32): the
+// activation loads serve both rows.  Each row's arithmetic is q4_partial_smem's, in the
+// same order, so the results are the same bits.
+template <int K, int G>
+__device__ __forceinline__ void q4_partial2_smem(const uint8_t* chunk, int rA, int rB, int vl, const float4* x4,
+                                                 float& outA, float& outB) {
+    using Q = Q4<K, G>;
+    const uint8_t* qa = chunk + rA * (K / 2);
+    const uint8_t* qb = chunk + rB * (K / 2);
+    const uint16_t* sa = reinterpret_cast<const uint16_t*>(chunk + Q::S_OFF) + rA * (K / G);
+    const uint16_t* sb = reinterpret_cast<const uint16_t*>(chunk + Q::S_OFF) + rB * (K / G);
+    const uint8_t* za = chunk + Q::Z_OFF + rA * (K / G / 2);
+    const uint8_t* zb = chunk + Q::Z_OFF + rB * (K / G / 2);
+    float accA = 0.0f, accB = 0.0f;
+#pragma unroll
+    for (int i = 0; i < Q::VPL; ++i) {
+        const int v = vl + Q::LPR * i;
+        const int g = (v * 32) / G;
+        const uint4 q0 = *reinterpret_cast<const uint4*>(qa + 16 * v);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(qb + 16 * v);
+        const float s0 = __half2float(__ushort_as_half(sa[g]));
+        const float s1 = __half2float(__ushort_as_half(sb[g]));
+        const uint32_t zb0 = za[g >> 1], zb1 = zb[g >> 1];
+        const float fz0 = __uint_as_float(0x4B000000u | ((g & 1) ? (zb0 >> 4) : (zb0 & 15u)));
+        const float fz1 = __uint_as_float(0x4B000000u | ((g & 1) ? (zb1 >> 4) : (zb1 & 15u)));
+        const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w};
+        const uint32_t w1[4] = {q1.x, q1.y, q1.z, q1.w};
+        float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+#pragma unroll
+        for (int wd = 0; wd < 4; ++wd) {
+            const uint32_t lo0 = w0[wd] & 0x0F0F0F0Fu, hi0 = (w0[wd] >> 4) & 0x0F0F0F0Fu;
+            const uint32_t lo1 = w1[wd] & 0x0F0F0F0Fu, hi1 = (w1[wd] >> 4) & 0x0F0F0F0Fu;
+            const float4 xa = x4[(2 * wd) * Q::NV + v];
+            const float4 xb = x4[(2 * wd + 1) * Q::NV + v];
+            a0 = fmaf(nib(lo0, 0) - fz0, xa.x, a0);
+            a1 = fmaf(nib(hi0, 0) - fz0, xa.y, a1);
+            b0 = fmaf(nib(lo1, 0) - fz1, xa.x, b0);
+            b1 = fmaf(nib(hi1, 0) - fz1, xa.y, b1);
+            a0 = fmaf(nib(lo0, 1) - fz0, xa.z, a0);
+            a1 = fmaf(nib(hi0, 1) - fz0, xa.w, a1);
+            b0 = fmaf(nib(lo1, 1) - fz1, xa.z, b0);
+            b1 = fmaf(nib(hi1, 1) - fz1, xa.w, b1);
+            a0 = fmaf(nib(lo0, 2) - fz0, xb.x, a0);
+            a1 = fmaf(nib(hi0, 2) - fz0, xb.y, a1);
+            b0 = fmaf(nib(lo1, 2) - fz1, xb.x, b0);
+            b1 = fmaf(nib(hi1, 2) - fz1, xb.y, b1);
+            a0 = fmaf(nib(lo0, 3) - fz0, xb.z, a0);
+            a1 = fmaf(nib(hi0, 3) - fz0, xb.w, a1);
+            b0 = fmaf(nib(lo1, 3) - fz1, xb.z, b0);
+            b1 = fmaf(nib(hi1, 3) - fz1, xb.w, b1);
+        }
+        accA = fmaf(s0, a0 + a1, accA);
+        accB = fmaf(s1, b0 + b1, accB);
+    }
+    outA = accA;
+    outB = accB;
+}
+
 constexpr int kMoeMaxSlots = 16;   // gate/up chunk slots (mbarriers) per CTA
 
 bool moe_supported(int H, int I, int G) {
@@ -250,13 +308,14 @@ bool moe_supported(int H, int I, int G) {
 //               CTA into shared memory (bulk copies); next layer's input projection into
 //               L2.  Then griddepcontrol.wait.
 //   phase 1   : every CTA normalises x_mid (canonical order); CTAs 0..R-1 compute the
-//               router logits (canonical order); then every CTA lets the next kernel
-//               launch (its weight preloads overlap the top-k and the id broadcast, and
-//               stay clear of the router phase and of the routed-expert copies: measured
-//               against triggering right after the wait, after the norm, after the ids
-//               and after phase 2, this point is the fastest by 1-8 %); CTA 0 waits for
-//               the logits, runs the softmax / top-k and publishes ids with a release
-//               flag.
+//               router logits (canonical order) and store each as a tagged word; then
+//               every CTA lets the next kernel launch (its weight preloads overlap the
+//               top-k and stay clear of the router phase and of the routed-expert copies:
+//               measured against triggering right after the wait, after the norm, after
+//               the ids and after phase 2, this point is the fastest by 1-8 %).
+//   phase 1b  : every CTA polls the E + 1 logit words and runs the softmax and the top-k
+//               itself with all its threads (no id broadcast: the same arithmetic on the
+//               same words gives every CTA the same ids).
 //   issue     : every CTA bulk-copies its routed gate/up chunks and its 16-row down
 //               chunk of every selected expert (the down data lands during phase 2).
 //   phase 2   : gate/up GEMVs, h = SiLU(g) * u to global; grid barrier (arrivals on a
@@ -265,8 +324,8 @@ bool moe_supported(int H, int I, int G) {
 //   phase 3   : CTAs 0..H/16-1 produce their 16 output rows, one warp per row over all
 //               experts (even and odd experts in two accumulators, added in a fixed
 //               order) + residual.
-//   exit      : nothing to reset (generation-tagged flags; the router logit slots are
-//               emptied by CTA 0 once read), so the grid ends as its last rows are stored.
+//   exit      : nothing to reset (the barrier counter and the logit words carry the
+//               launch generation), so the grid ends as its last rows are stored.
 struct MoeFusedArgs {
     const uint16_t* Wr;       // [E+1][H] router rows + shared-gate row
     const float* rbias;       // [E] logit offsets, or null
@@ -279,13 +338,12 @@ struct MoeFusedArgs {
     const uint8_t* shared;
     int64_t expert_bytes, gu_part_bytes;
     int E, topk, I, gu_chunks, d_chunks, up_slots;
-    float* logits;            // [E+1]
+    unsigned long long* lslots; // [E+1] router logit words (launch tag << 32 | fp32 bits)
     int* ids;
     float* probs;
     float* shared_g;
     float* h;                 // [(topk+1)][I]
     unsigned long long* arrivals; // up-phase arrivals of every launch so far (never reset)
-    unsigned long long* idflag; // [4] released words: launch tag in bit 63 | 4 ids x 15 bits
     uint64_t* trace;          // phase stamps of CTA 0 and of the last CTA, or null
     uint64_t* cta_trace;      // per-CTA stamps (kTrMoeCtaSlots per CTA, thread 0) or null
     uint64_t* kt;             // launch timeline record or null
@@ -303,18 +361,17 @@ DM_DEV unsigned ld_relaxed_u32(const unsigned* p) {
 DM_DEV void st_relaxed_u32(unsigned* p, unsigned v) {
     asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Router logit slots hold kLogitEmpty (a NaN pattern the arithmetic never produces: NaN
-// results are 0x7FFFFFFF) until their router CTA stores the logit; CTA 0 polls the slots
-// themselves and puts kLogitEmpty back once it has read them.
-constexpr unsigned kLogitEmpty = 0xFFFFFFFFu;
-DM_DEV float poll_logit(const float* p, uint32_t* err) {
-    const unsigned* q = reinterpret_cast<const unsigned*>(p);
-    unsigned v = ld_relaxed_u32(q);
-    if (v != kLogitEmpty) return __uint_as_float(v);
+// Router logit slots: one 64-bit word per row, the launch tag (generation + 1, never 0) in
+// the high half and the fp32 logit bits in the low half, written with one store.  A reader
+// polls a slot until its tag matches this launch's: the previous launch's words never match,
+// so nothing is emptied between launches (slots start as zero words).
+DM_DEV float poll_slot(const unsigned long long* p, unsigned tag, uint32_t* err) {
+    unsigned long long v = ld_relaxed_u64(p);
+    if (static_cast<unsigned>(v >> 32) == tag) return __uint_as_float(static_cast<unsigned>(v));
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t n = 1;; ++n) {
-        v = ld_relaxed_u32(q);
-        if (v != kLogitEmpty) return __uint_as_float(v);
+        v = ld_relaxed_u64(p);
+        if (static_cast<unsigned>(v >> 32) == tag) return __uint_as_float(static_cast<unsigned>(v));
         if (n % 256 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
             raise_error(err, DM_DEVERR_TIMEOUT);
             return 0.0f;
@@ -322,24 +379,8 @@ DM_DEV float poll_logit(const float* p, uint32_t* err) {
     }
 }
 
-
-// Bounded wait until bit 63 of *p equals tag; returns the word.
-DM_DEV unsigned long long spin_marker(const unsigned long long* p, unsigned tag, uint32_t* err) {
-    unsigned long long v = ld_acquire_u64(p);
-    if ((v >> 63) == tag) return v;
-    const uint64_t t0 = globaltimer_ns();
-    uint32_t n = 0;
-    while (true) {
-        v = ld_acquire_u64(p);
-        if ((v >> 63) == tag) return v;
-        if (++n % 256 == 0 && globaltimer_ns() - t0 > DM_WAIT_NS) {
-            raise_error(err, DM_DEVERR_TIMEOUT);
-            return 0;
-        }
-    }
-}
-
 constexpr int kMoeThreads = 512;
+constexpr int kMoeMaxE = kMoeThreads;  // phase 1b: one thread per expert
 
 template <int K, int KI, int G>
 struct MoeFusedSmem {
@@ -350,7 +391,12 @@ struct MoeFusedSmem {
     __host__ __device__ static size_t xn_off(int up_slots, int nexp) { return dn_off(up_slots) + static_cast<size_t>(nexp) * QD::CHUNK; }
     __host__ __device__ static size_t xs_off(int up_slots, int nexp) { return xn_off(up_slots, nexp) + K * 4; }
     __host__ __device__ static size_t h_off(int up_slots, int nexp) { return xs_off(up_slots, nexp) + K * 4; }
-    __host__ __device__ static size_t total(int up_slots, int nexp) { return h_off(up_slots, nexp) + static_cast<size_t>(nexp) * KI * 4; }
+    // the h region also holds phase 1b's logits and candidates (16 bytes per expert)
+    __host__ __device__ static size_t h_bytes(int nexp, int E) {
+        const size_t hb = static_cast<size_t>(nexp) * KI * 4, tb = static_cast<size_t>(E + 2) * 16;
+        return hb > tb ? hb : tb;
+    }
+    __host__ __device__ static size_t total(int up_slots, int nexp, int E) { return h_off(up_slots, nexp) + h_bytes(nexp, E); }
 };
 
 template <int K, int KI, int G>
@@ -366,6 +412,12 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     __shared__ float sp[kMaxTopK + 1];
     __shared__ float red[kMoeThreads / 32];
     __shared__ unsigned long long s_gen;
+    __shared__ float s_wred[kMoeThreads / 32];
+    __shared__ int s_wcnt[kMoeThreads / 32];
+    __shared__ int s_wcnt_b[kMoeThreads / 32];
+    __shared__ uint32_t s_g8[kMoeMaxE / 8];
+    __shared__ uint32_t s_thr;
+    __shared__ float s_inv;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int nblk = gridDim.x, c = blockIdx.x;
     const int nexp = a.topk + 1;
@@ -462,6 +514,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     }
     __syncthreads();
     trace_stamp(tr, 2);
+    const unsigned tag = static_cast<unsigned>(s_gen & 0x7FFFFFFFull) + 1u;  // this launch's slot tag
     if (router_cta) {
         if (rrow < nrows) {
             const float4* xlo = reinterpret_cast<const float4*>(xsr);
@@ -483,227 +536,136 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             }
             acc = warp_sum(acc);
             if (a.rbias && rrow < a.E) acc = __fadd_rn(acc, a.rbias[rrow]);
-            if (lane == 0) {
-                const unsigned bits = __float_as_uint(acc);
-                st_relaxed_u32(reinterpret_cast<unsigned*>(a.logits) + rrow, bits == kLogitEmpty ? 0x7FFFFFFFu : bits);
-            }
+            if (lane == 0)
+                st_relaxed_u64(a.lslots + rrow, (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(acc));
         }
     }
     trace_stamp(tr, 3);
     pdl_launch_dependents();  // the next kernel's preloads overlap the top-k
-    if (c == 0) {
-        trace_stamp(tr, 4);
-        if (warp == 0) {
-            // softmax in the canonical order; lane l owns experts l, l+32, ... (<= 32 each)
-            const int E = a.E;
-            constexpr int PL = 8;  // register slots per lane: E <= 256 here, larger E below
-            float pv[PL];
-            float m = -INFINITY;
-            // poll the logit slots: every load of a round is in flight at once; a round
-            // repeats only the slots still empty
-            const unsigned* lg = reinterpret_cast<const unsigned*>(a.logits);
-            unsigned raw[PL + 1];
-        #pragma unroll
-            for (int i = 0; i <= PL; ++i) {
-                const int e = i < PL ? lane + 32 * i : E;  // slot E: shared-expert gate
-                raw[i] = e <= E ? ld_relaxed_u32(lg + e) : 0u;
-            }
-            {
-                const uint64_t t0 = globaltimer_ns();
-                for (uint32_t n = 0;; ++n) {
-                    bool miss = false;
-        #pragma unroll
-                    for (int i = 0; i <= PL; ++i) miss |= raw[i] == kLogitEmpty;
-                    if (!__any_sync(0xffffffffu, miss)) break;
-                    if (n % 64 == 63 && globaltimer_ns() - t0 > DM_WAIT_NS) {
-                        if (lane == 0) raise_error(a.err, DM_DEVERR_TIMEOUT);
-                        break;
-                    }
-        #pragma unroll
-                    for (int i = 0; i <= PL; ++i) {
-                        const int e = i < PL ? lane + 32 * i : E;
-                        if (raw[i] == kLogitEmpty) raw[i] = ld_relaxed_u32(lg + e);
-                    }
-                }
-            }
-        #pragma unroll
-            for (int i = 0; i < PL; ++i) {
-                const int e = lane + 32 * i;
-                pv[i] = e < E ? __uint_as_float(raw[i]) : -INFINITY;
-                m = fmaxf(m, pv[i]);
-            }
-            for (int e = lane + 32 * PL; e < E; e += 32) m = fmaxf(m, poll_logit(a.logits + e, a.err));
-            const float zs = __uint_as_float(raw[PL]);  // shared-expert gate logit
-            m = warp_max(m);
-            if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 0);
-            float s = 0.0f;
-        #pragma unroll
-            for (int i = 0; i < PL; ++i) {
-                const int e = lane + 32 * i;
-                if (e < E) {
-                    pv[i] = dm_det_exp(DM_DET_SUB(pv[i], m));
-                    s = DM_DET_ADD(s, pv[i]);
-                } else {
-                    pv[i] = -2.0f;
-                }
-            }
-            float* pe = h4;  // experts beyond 32*PL per lane live in shared memory
-            for (int e = lane + 32 * PL; e < E; e += 32) {
-                const float ev = dm_det_exp(DM_DET_SUB(poll_logit(a.logits + e, a.err), m));
-                pe[e] = ev;
-                s = DM_DET_ADD(s, ev);
-            }
-            s = warp_sum(s);
-            const float inv = DM_DET_DIV(1.0f, s);
-        #pragma unroll
-            for (int i = 0; i < PL; ++i)
-                if (lane + 32 * i < E) pv[i] = DM_DET_MUL(pv[i], inv);
-            if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 1);
-            for (int e = lane + 32 * PL; e < E; e += 32) pe[e] = DM_DET_MUL(pe[e], inv);
-            __syncwarp();
-            // top-k on probabilities, ties to the lower expert id.  The probabilities are
-            // >= 0, so their bit patterns order like the values.
-            const int topk = a.topk;
-            int my_id = 0;      // lane r < topk ends with the round-r result
-            uint32_t my_p = 0u;
-            bool bad = false;
-            if (E <= 32 * PL) {
-                // each lane sorts its 8 (probability, id) pairs (compare-exchange network);
-                // every round the warp takes the maximum over the lanes' heads and the lowest
-                // id holding it, and the owning lane pops its head.  Branch-free rounds:
-                // divergence ahead of the warp reductions costs more than the selects.
-                uint32_t kb[PL];
-                int ki[PL];
-        #pragma unroll
-                for (int i = 0; i < PL; ++i) {
-                    const int e = lane + 32 * i;
-                    kb[i] = (e < E && pv[i] > 0.0f) ? __float_as_uint(pv[i]) : 0u;
-                    ki[i] = e < E ? e : 0x7fffffff;
-                }
-        #define DM_CX(x, y)                                                                        \
-            {                                                                                      \
-        const bool sw = kb[y] > kb[x] || (kb[y] == kb[x] && ki[y] < ki[x]);                \
-        const uint32_t tb = sw ? kb[y] : kb[x];                                            \
-        const int ti = sw ? ki[y] : ki[x];                                                 \
-        kb[y] = sw ? kb[x] : kb[y];                                                        \
-        ki[y] = sw ? ki[x] : ki[y];                                                        \
-        kb[x] = tb;                                                                        \
-        ki[x] = ti;                                                                        \
-            }
-                // Batcher odd-even merge sort network for 8 elements (19 compare-exchanges)
-                DM_CX(0, 1) DM_CX(2, 3) DM_CX(4, 5) DM_CX(6, 7)
-                DM_CX(0, 2) DM_CX(1, 3) DM_CX(4, 6) DM_CX(5, 7)
-                DM_CX(1, 2) DM_CX(5, 6)
-                DM_CX(0, 4) DM_CX(1, 5) DM_CX(2, 6) DM_CX(3, 7)
-                DM_CX(2, 4) DM_CX(3, 5)
-                DM_CX(1, 2) DM_CX(3, 4) DM_CX(5, 6)
-        #undef DM_CX
-                        const long long tk0 = clock64();
+    // ---- phase 1b, in every CTA: the E + 1 logits, softmax and top-k.  Every CTA runs the
+    // same arithmetic on the same words, so all reach the same ids without a broadcast ----
+    {
+        const int E = a.E, topk = a.topk;
+        float* s_lg = h4;                                              // [E + 1] logits, then e^(z - m)
+        uint2* s_cand = reinterpret_cast<uint2*>(h4 + ((E + 2) & ~1));  // [E] (key, id) of the candidates
+        for (int e = tid; e <= E; e += kMoeThreads) s_lg[e] = poll_slot(a.lslots + e, tag, a.err);
+        __syncthreads();
+        trace_stamp(tr ? tr + 20 : nullptr, 0);
+        // softmax in the canonical order: m = max; e = det_exp(z - m); lane l of one warp sums
+        // e[l], e[l + 32], ... in order; butterfly; p = e * (1 / sum)
+        const float z = tid < E ? s_lg[tid] : -INFINITY;
+        const float mw = warp_max(fmaxf(-INFINITY, z));
+        if (lane == 0) s_wred[warp] = mw;
+        __syncthreads();
+        float m = s_wred[0];
 #pragma unroll
-                for (int r = 0; r < kMaxTopK; ++r) {
-                    if (r >= topk) break;
-                    const uint32_t mb = __reduce_max_sync(0xffffffffu, kb[0]);
-                    const int cand = kb[0] == mb ? ki[0] : 0x7fffffff;
-                    const int bi = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(cand)));
-                    const bool pop = ki[0] == bi;
-        #pragma unroll
-                    for (int i = 0; i < PL - 1; ++i) {
-                        kb[i] = pop ? kb[i + 1] : kb[i];
-                        ki[i] = pop ? ki[i + 1] : ki[i];
-                    }
-                    kb[PL - 1] = pop ? 0u : kb[PL - 1];
-                    ki[PL - 1] = pop ? 0x7fffffff : ki[PL - 1];
-                    const bool oob = bi < 0 || bi >= E;
-                    bad |= oob;
-                    my_id = lane == r ? (oob ? r : bi) : my_id;
-                    my_p = lane == r ? (oob ? 0u : mb) : my_p;
-                }
-                if (lane == 0 && tr && c == 0) tr[44] = static_cast<uint64_t>(clock64() - tk0);  // rounds, SM cycles (slot 60)
-            } else {
-                // E > 256: experts beyond 32*PL per lane live in shared memory (taken = -2);
-                // each round every lane offers its best untaken one
-                unsigned avail = 0;
-        #pragma unroll
-                for (int i = 0; i < PL; ++i)
-                    if (lane + 32 * i < E) avail |= 1u << i;
-                for (int r = 0; r < topk; ++r) {
-                    uint32_t hb = 0u;
-                    int hi = 0x7fffffff, hslot = -1;
-        #pragma unroll
-                    for (int i = 0; i < PL; ++i) {
-                        const uint32_t b = pv[i] > 0.0f ? __float_as_uint(pv[i]) : 0u;
-                        if (((avail >> i) & 1u) && (hslot < 0 || b > hb)) {
-                            hb = b;
-                            hi = lane + 32 * i;
-                            hslot = i;
-                        }
-                    }
-                    for (int e = lane + 32 * PL; e < E; e += 32) {
-                        const float v = pe[e];
-                        const uint32_t b = v > 0.0f ? __float_as_uint(v) : 0u;
-                        if (v >= 0.0f && (hi == 0x7fffffff || b > hb || (b == hb && e < hi))) {
-                            hb = b;
-                            hi = e;
-                            hslot = PL;
-                        }
-                    }
-                    const uint32_t mb = __reduce_max_sync(0xffffffffu, hb);
-                    const int cand = (hi != 0x7fffffff && hb == mb) ? hi : 0x7fffffff;
-                    const int bi = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(cand)));
-                    if (hi == bi) {
-                        if (hslot == PL) pe[bi] = -2.0f;
-                        else avail &= ~(1u << hslot);
-                    }
-                    const bool oob = bi < 0 || bi >= E;
-                    bad |= oob;
-                    if (lane == (r & 31) && r < 32) {
-                        my_id = oob ? r : bi;
-                        my_p = oob ? 0u : mb;
-                    }
-                    __syncwarp();
-                }
-            }
-            if (lane < topk) {
-                sid[lane] = my_id;
-                sp[lane] = __uint_as_float(my_p);
-                a.probs[lane] = __uint_as_float(my_p);
-            }
-            if (bad && lane == 0) raise_error(a.err, DM_DEVERR_NONFINITE);
-            __syncwarp();
-            if (lane == 0) trace_stamp(tr ? tr + 20 : nullptr, 2);
+        for (int w = 1; w < kMoeThreads / 32; ++w) m = fmaxf(m, s_wred[w]);
+        float p = 0.0f;
+        if (tid < E) {
+            p = dm_det_exp(DM_DET_SUB(z, m));
+            s_lg[tid] = p;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            float sum = 0.0f;
+            for (int e = lane; e < E; e += 32) sum = DM_DET_ADD(sum, s_lg[e]);
+            sum = warp_sum(sum);
             if (lane == 0) {
-                const float sgv = sigmoid_f(zs);
-                *a.shared_g = sgv;
-                sp[a.topk] = sgv;
-                if (s != s || isinf(s)) raise_error(a.err, DM_DEVERR_NONFINITE);
-                unsigned long long words[4] = {0ull, 0ull, 0ull, 0ull};
-        #pragma unroll
-                for (int r = 0; r < kMaxTopK; ++r)
-                    if (r < a.topk) {
-                        a.ids[r] = sid[r];
-                        words[r >> 2] |= static_cast<unsigned long long>(sid[r]) << (15 * (r & 3));
-                    }
-                // publish: each 64-bit word carries its ids and the marker, so readers need
-                // nothing else from this thread before phase 3; probs and the shared gate
-                // reach phase 3 through this thread's release of the up-phase barrier.
-                // Relaxed stores: no fence on the critical path.
-        #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (k < (a.topk + 3) / 4)
-                        st_relaxed_u64(&a.idflag[k], words[k] | (static_cast<unsigned long long>(1u - (s_gen & 1u)) << 63));
-                trace_stamp(tr ? tr + 20 : nullptr, 3);
+                s_inv = DM_DET_DIV(1.0f, sum);
+                if (c == 0 && (sum != sum || isinf(sum))) raise_error(a.err, DM_DEVERR_NONFINITE);
             }
-            // every slot has been read: empty them for the next launch
-            for (int e = lane; e <= E; e += 32) reinterpret_cast<unsigned*>(a.logits)[e] = kLogitEmpty;
         }
         __syncthreads();
-    } else {
-        if (tid < (a.topk + 3) / 4) {
-            const unsigned long long w = spin_marker(&a.idflag[tid], 1u - static_cast<unsigned>(s_gen & 1u), a.err);
-            for (int r = 4 * tid; r < a.topk && r < 4 * tid + 4; ++r)
-                sid[r] = min(static_cast<int>((w >> (15 * (r & 3))) & 0x7FFF), a.E - 1);
+        trace_stamp(tr ? tr + 20 : nullptr, 1);
+        const long long tk0 = clock64();
+        // keys: probability bits (probabilities >= 0 order like their bits); 0 for p <= 0
+        // or NaN.  Order: larger key first, ties to the lower id.
+        uint32_t key = 0u;
+        if (tid < E) {
+            p = DM_DET_MUL(p, s_inv);
+            key = p > 0.0f ? __float_as_uint(p) : 0u;
+        }
+        // threshold: each group of 8 consecutive experts offers its largest key; with at
+        // least topk groups, thr = the topk-th largest of these maxima is held by topk
+        // distinct experts, so every expert below thr ranks >= topk.  The top-k are then
+        // A = {key > thr} (at most topk - 1 groups lie above thr: <= 8 (topk - 1) experts),
+        // ranked among themselves, followed by B = {key == thr} in id order.
+        const int ng8 = (E + 7) / 8;
+        {
+            uint32_t gm = key;
+#pragma unroll
+            for (int m = 1; m < 8; m <<= 1) gm = max(gm, __shfl_xor_sync(0xffffffffu, gm, m));
+            if ((lane & 7) == 0 && tid < E) s_g8[tid >> 3] = gm;
         }
         __syncthreads();
+        if (tid < ng8) {
+            uint32_t t = 0u;  // fewer groups than topk: every expert is in A or B
+            if (ng8 >= topk) {
+                const uint32_t me = s_g8[tid];
+                int r = 0;
+                for (int j = 0; j < ng8; ++j) {
+                    const uint32_t o = s_g8[j];
+                    r += (o > me || (o == me && j < tid)) ? 1 : 0;
+                }
+                if (r == topk - 1) s_thr = me;
+            } else if (tid == 0) {
+                s_thr = t;
+            }
+        }
+        __syncthreads();
+        const uint32_t thr = s_thr;
+        const bool in_a = tid < E && key > thr, in_b = tid < E && key == thr;
+        const unsigned bal_a = __ballot_sync(0xffffffffu, in_a), bal_b = __ballot_sync(0xffffffffu, in_b);
+        if (lane == 0) {
+            s_wcnt[warp] = __popc(bal_a);
+            s_wcnt_b[warp] = __popc(bal_b);
+        }
+        __syncthreads();
+        int base_a = 0, na = 0, base_b = 0;
+#pragma unroll
+        for (int w = 0; w < kMoeThreads / 32; ++w) {
+            const int n = s_wcnt[w];
+            base_a += w < warp ? n : 0;
+            base_b += w < warp ? s_wcnt_b[w] : 0;
+            na += n;
+        }
+        const unsigned below = (1u << lane) - 1u;
+        if (in_a) s_cand[base_a + __popc(bal_a & below)] = make_uint2(key, static_cast<unsigned>(tid));
+        // B in id order: the first topk - na of them complete the selection
+        if (in_b) {
+            const int r = na + base_b + __popc(bal_b & below);
+            if (r < topk) {
+                sid[r] = tid;
+                sp[r] = __uint_as_float(key);
+            }
+        }
+        __syncthreads();
+        trace_stamp(tr ? tr + 20 : nullptr, 2);
+        // A's ranks among A are its ranks among all experts
+        for (int i = tid; i < na; i += kMoeThreads) {
+            const uint2 me = s_cand[i];
+            int r = 0;
+#pragma unroll 4
+            for (int j = 0; j < na; ++j) {
+                const uint2 o = s_cand[j];
+                r += (o.x > me.x || (o.x == me.x && o.y < me.y)) ? 1 : 0;
+            }
+            if (r < topk) {
+                sid[r] = static_cast<int>(me.y);
+                sp[r] = __uint_as_float(me.x);
+            }
+        }
+        if (tid == 0) sp[topk] = sigmoid_f(s_lg[E]);
+        __syncthreads();
+        if (tr && c == 0 && tid == 0) tr[44] = static_cast<uint64_t>(clock64() - tk0);  // top-k, SM cycles (slot 60)
+        trace_stamp(tr ? tr + 20 : nullptr, 3);
+        if (c == 0) {  // the selection, for inspection
+            if (tid < topk) {
+                a.ids[tid] = sid[tid];
+                a.probs[tid] = sp[tid];
+            }
+            if (tid == 0) *a.shared_g = sp[topk];
+        }
     }
     trace_stamp(tr, 5);
     trace_stamp(ct, 2);
@@ -743,10 +705,16 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             const int item = i0 + k;
             const int j = item / a.gu_chunks, cc = item % a.gu_chunks;
             const bool ok = mbar_wait_bounded(&bar_up[k], 0, a.err, nullptr);
-            trace_stamp(ct, 3);
+            if (k == 0) trace_stamp(ct, 3);  // the CTA's first item landed
             if (late_down && k == 0 && warp == 0 && has_down && lane < a.topk) issue_down(lane);
             const uint8_t* chunk = up_s + static_cast<size_t>(k) * QU::CHUNK;
             float dots[2];
+            if (QU::RPP == 1) {  // gate row wg and up row 8 + wg together
+                float g = 0.0f, u = 0.0f;
+                if (ok) q4_partial2_smem<K, G>(chunk, wg, 8 + wg, lane, xv4, g, u);
+                dots[0] = lane_group_sum<QU::LPR>(g);
+                dots[1] = lane_group_sum<QU::LPR>(u);
+            } else
 #pragma unroll
             for (int p = 0; p < 2; p += QU::RPP) {
                 const int sub = lane / QU::LPR, vl = lane % QU::LPR;
@@ -790,10 +758,6 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         constexpr int WPL = KI / 32;   // weights per lane
         constexpr int F4L = WPL / 4;   // float4 of h per lane
         static_assert(WPL >= 4 && WPL % 4 == 0 && WPL <= G, "down-row lane geometry");
-        if (c != 0) {
-            if (tid < a.topk) sp[tid] = __ldcg(a.probs + tid);
-            if (tid == 0) sp[a.topk] = __ldcg(a.shared_g);
-        }
         {
             constexpr int HPT = ((kMaxTopK + 1) * KI + kMoeThreads - 1) / kMoeThreads;
             const int nh = nexp * KI;
@@ -880,9 +844,10 @@ static cudaError_t launch_moe_fused_t(const LaunchCfg& lc, MoeFusedArgs a) {
     const int grid = lc.num_sms;
     const int n_items = nexp * a.gu_chunks;
     a.up_slots = (n_items + grid - 1) / grid;
-    if (a.up_slots > kMoeMaxSlots || a.d_chunks > grid || (a.E + 16) / 16 > grid) return cudaErrorInvalidValue;
+    if (a.up_slots > kMoeMaxSlots || a.d_chunks > grid || (a.E + 16) / 16 > grid || a.E > kMoeMaxE || a.topk > a.E)
+        return cudaErrorInvalidValue;
     if (a.cta_trace && grid * kTrMoeCtaSlots > kTraceSlots - kTrMoeCta) a.cta_trace = nullptr;
-    const size_t smem = MoeFusedSmem<K, KI, G>::total(a.up_slots, nexp);
+    const size_t smem = MoeFusedSmem<K, KI, G>::total(a.up_slots, nexp, a.E);
     return launch_kernel(lc, moe_fused_kernel<K, KI, G>, dim3(grid), dim3(kMoeThreads), smem, a);
 }
 
@@ -904,13 +869,12 @@ cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.I = d.I;
     a.gu_chunks = d.gu_chunks;
     a.d_chunks = d.d_chunks;
-    a.logits = b.rlogits;
+    a.lslots = b.rslots;
     a.ids = b.topk_ids;
     a.probs = b.topk_p;
     a.shared_g = b.shared_g;
     a.h = b.h;
     a.arrivals = reinterpret_cast<unsigned long long*>(b.counters + kCntMoeSync);
-    a.idflag = reinterpret_cast<unsigned long long*>(b.counters + kCntMoeFlag);
     a.trace = b.trace ? b.trace + kTrMoe : nullptr;
     a.cta_trace = b.trace ? b.trace + kTrMoeCta : nullptr;
     a.kt = lc.kt;
@@ -931,10 +895,12 @@ static cudaError_t moe_fused_fits_t(const Dims& d, int num_sms, bool* ok) {
     const int nexp = d.topk + 1;
     const int up_slots = (nexp * d.gu_chunks + num_sms - 1) / num_sms;
     *ok = false;
-    if (up_slots > kMoeMaxSlots || d.d_chunks > num_sms || (d.E + 16) / 16 > num_sms) return cudaSuccess;
+    if (up_slots > kMoeMaxSlots || d.d_chunks > num_sms || (d.E + 16) / 16 > num_sms || d.E > kMoeMaxE ||
+        d.topk > d.E)
+        return cudaSuccess;
     int per_sm = 0;
     const cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, moe_fused_kernel<K, KI, G>, kMoeThreads, MoeFusedSmem<K, KI, G>::total(up_slots, nexp));
+        &per_sm, moe_fused_kernel<K, KI, G>, kMoeThreads, MoeFusedSmem<K, KI, G>::total(up_slots, nexp, d.E));
     *ok = e == cudaSuccess && per_sm >= 1;
     return e;
 }

@@ -13,12 +13,12 @@
 //     0  control block (512 B, cleared on the stream before every launch): the 64-word
 //        counter array in the layout a context uses (phase counters and released id
 //        words of the fused kernel), then the device error word at 256
-//   512  router logits  [E + 1] fp32                     (<= 4 KiB for E <= 1023)
-//   512 + 4 KiB  top-k ids, probabilities, shared gate   (256 B)
+//   512  router logit words [E + 1] u64 (launch tag << 32 | fp32 bits; 8 KiB for E <= 512)
+//   512 + 8 KiB  top-k ids, probabilities, shared gate   (256 B)
 //   then normalised input [H] fp32 and SwiGLU activations [(k + 1) * I] fp32.
-// The array keeps what the last call left in it; the control block has to start at zero
-// and the router logit slots empty (all-ones bytes): the entry point sets both before each
-// launch.
+// The array keeps what the last call left in it; the control block and the router logit
+// words have to start at zero (the kernel's launch generation restarts at 0 with the
+// control block): the entry point clears both before each launch.
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -73,7 +73,7 @@ static int64_t q4_chunk_bytes(int cols) {  // 16 rows: nibbles, fp16 scales, uin
 
 // Scratch bytes a layer of these dimensions needs (control block, logits, top-k, x_norm, h).
 static size_t scratch_need(int H, int I, int E, int topk) {
-    return kCtlBytes + 4096 + 256 + static_cast<size_t>(H) * 4 + static_cast<size_t>(topk + 1) * I * 4;
+    return kCtlBytes + 8192 + 256 + static_cast<size_t>(H) * 4 + static_cast<size_t>(topk + 1) * I * 4;
 }
 
 // Once per device, with that device current: the scratch address and the kernel attributes.
@@ -112,10 +112,10 @@ extern "C" int32_t dm_moe_layer_noalloc(int32_t H, int32_t I, int32_t E, int32_t
         return na_err(err_buf, err_buf_size, DM_ERR_INVALID_ARG, "INVALID_ARG", "null device pointer");
     if (x_out_dev < x_mid_dev + H && x_mid_dev < x_out_dev + H)
         return na_err(err_buf, err_buf_size, DM_ERR_INVALID_ARG, "INVALID_ARG", "x_out overlaps x_mid");
-    if (!(eps > 0.0f) || H <= 0 || I <= 0 || E <= 0 || topk <= 0 || topk > E || topk > kMaxTopK || E > 1023 ||
+    if (!(eps > 0.0f) || H <= 0 || I <= 0 || E <= 0 || topk <= 0 || topk > E || topk > kMaxTopK || E > 512 ||
         H % 64 != 0 || I % 64 != 0)
         return na_err(err_buf, err_buf_size, DM_ERR_INVALID_ARG, "CONFIG_ERROR",
-                      "need eps > 0, 0 < num_experts_per_tok <= min(num_experts, 16), num_experts <= 1023, "
+                      "need eps > 0, 0 < num_experts_per_tok <= min(num_experts, 16), num_experts <= 512, "
                       "hidden and intermediate sizes multiples of 64");
     const size_t need = scratch_need(H, I, E, topk);
     if (need > kNoAllocScratchBytes)
@@ -173,8 +173,8 @@ extern "C" int32_t dm_moe_layer_noalloc(int32_t H, int32_t I, int32_t E, int32_t
     w.shared = shared_dev;
 
     unsigned char* base = sd.scratch;
-    float* lg = reinterpret_cast<float*>(base + kCtlBytes);
-    unsigned char* small = base + kCtlBytes + 4096;
+    unsigned long long* lg = reinterpret_cast<unsigned long long*>(base + kCtlBytes);
+    unsigned char* small = base + kCtlBytes + 8192;
     float* xn = reinterpret_cast<float*>(small + 256);
     Buffers b{};
     // x_mid / x_out are addressed as slot 0 of the mixer / residual buffers
@@ -182,7 +182,7 @@ extern "C" int32_t dm_moe_layer_noalloc(int32_t H, int32_t I, int32_t E, int32_t
     b.xres = x_out_dev;
     b.xn = xn;
     b.h = xn + H;
-    b.rlogits = lg;
+    b.rslots = lg;
     b.topk_ids = ids_dev ? ids_dev : reinterpret_cast<int*>(small);
     b.topk_p = probs_dev ? probs_dev : reinterpret_cast<float*>(small + 64);
     b.shared_g = reinterpret_cast<float*>(small + 128);
@@ -200,8 +200,8 @@ extern "C" int32_t dm_moe_layer_noalloc(int32_t H, int32_t I, int32_t E, int32_t
 
     std::lock_guard<std::mutex> call_lock(g_call_mu);
     e = cudaMemsetAsync(base, 0, kCtlBytes, lc.stream);
-    // router logit slots start empty (all-ones NaN pattern; the kernel polls them)
-    if (e == cudaSuccess) e = cudaMemsetAsync(lg, 0xFF, static_cast<size_t>(E + 1) * 4, lc.stream);
+    // router logit words start empty (tag 0 matches no launch)
+    if (e == cudaSuccess) e = cudaMemsetAsync(lg, 0, static_cast<size_t>(E + 1) * 8, lc.stream);
     if (e == cudaSuccess) e = launch_moe_fused(lc, d, w, b, 0);
     if (e != cudaSuccess)
         return na_err(err_buf, err_buf_size, e == cudaErrorInvalidValue ? DM_ERR_INVALID_ARG : DM_ERR_CUDA,

@@ -418,11 +418,11 @@ int32_t dm_trace_timeline(dm_ctx* ctx, uint64_t* rec_host, int32_t* kinds_host, 
  * allocate during a step.  No dm_ctx is involved.
  *
  * Scratch: one fixed array of DM_NOALLOC_SCRATCH_BYTES (64 KiB) compiled into the library,
- * per device.  A layer needs 512 + 4096 + 256 + 4*H + 4*(k + 1)*I bytes of it; larger
+ * per device.  A layer needs 512 + 8192 + 256 + 4*H + 4*(k + 1)*I bytes of it; larger
  * layers are rejected with DM_ERR_INVALID_ARG and a SCRATCH_LIMIT message.  Supported
  * (hidden, intermediate) pairs: (256,128) (1024,256) (2048,256) (2048,512), and
  * (4096,512) only on a GPU with at least 256 SMs (the kernel needs hidden/16 <= SMs; a
- * B200 has 148); num_experts <= 1023, num_experts_per_tok <= 16, group size 64.  Other
+ * B200 has 148); num_experts <= 512, num_experts_per_tok <= 16, group size 64.  Other
  * shapes are rejected with DM_ERR_INVALID_ARG and a CONFIG_ERROR message.
  *   - Calls that overlap on the GPU share the one array and race.  Within one process
  *     the library serialises them (a mutex held from the first enqueue to the final
