@@ -2124,9 +2124,23 @@ static cudaError_t enqueue_mixer(dm_ctx* c, int layer, int slot) {
     return launch_gdn_out(lcfg_traced(c, TK_GDN_OUT, layer), c->d, w, c->b, slot);
 }
 
+// The MoE kernel prefetches into L2 the weights of the kernel after it: the next layer's
+// input projection, or (after the last layer) the head's first rows, as much of it as the
+// L2 can keep beside the step's other traffic.
 static cudaError_t enqueue_moe(dm_ctx* c, int layer, int slot) {
     const LayerW& w = c->layers[layer];
-    return launch_moe_fused(lcfg_traced(c, TK_MOE, layer), c->d, w, c->b, slot);
+    const Dims& d = c->d;
+    const void* next = nullptr;
+    uint64_t bytes = 0;
+    if (layer + 1 < d.L) {
+        const LayerW& n = c->layers[layer + 1];
+        next = n.w_in;
+        bytes = static_cast<uint64_t>(n.is_attn ? d.attn_in_rows : d.gdn_in_rows) * d.H * 2;
+    } else {
+        next = c->lm_head;
+        bytes = std::min<uint64_t>(static_cast<uint64_t>(d.V) * d.H * 2, 48ull << 20);
+    }
+    return launch_moe_fused(lcfg_traced(c, TK_MOE, layer), d, w, c->b, slot, next, bytes);
 }
 
 static cudaError_t enqueue_step(dm_ctx* c, int slot) {

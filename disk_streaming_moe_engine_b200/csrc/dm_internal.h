@@ -251,7 +251,10 @@ cudaError_t launch_attn_out(const LaunchCfg& lc, const Dims& d, const LayerW& w,
 cudaError_t launch_router(const LaunchCfg& lc, const Dims& d, const LayerW& w,
                           const Buffers& b, int slot, int normalise_input);
 // Whole MoE mixer of one layer (router, experts, residual) in one kernel; x_mid -> xres.
-cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot);
+// l2_next / l2_next_bytes: the weights of the kernel that follows (prefetched into L2 while
+// the MoE's latency-bound phases leave HBM idle), or null.
+cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot,
+                             const void* l2_next = nullptr, uint64_t l2_next_bytes = 0);
 cudaError_t launch_head(const LaunchCfg& lc, const Dims& d, const uint16_t* final_norm,
                         const uint16_t* lm_head, const Buffers& b, int slot, int advance,
                         int record_gen);

@@ -178,119 +178,144 @@ struct Q4 {
     static_assert(G % 32 == 0 && K % (2 * G) == 0, "group geometry");
 };
 
-// x4 layout of an activation vector for the 4-bit dot: x4[c * NV + v] = x[32v+4c .. +3].
+// ---- 4-bit rows times a vector on the tensor cores: integer mma.sync m16n8k32 (u8 x s8,
+// s32 accumulation, exact) ----
+// A: a chunk's 16 rows as their raw nibbles q.  B: the vector v as two signed 8-bit digits
+// per element with a scale per scale group g (the 64 columns that share a row's scale s
+// and zero point z): S_g = max |v| over the group, u = v * 127 / S_g, d0 = rint(u),
+// d1 = rint((u - d0) * 254), so v = unit_g (254 d0 + d1) with unit_g = S_g / (127 * 254),
+// to within unit_g / 2 (1.6e-5 S_g).  Per group the integer sums C_i = sum q d_i are exact
+// and the zero point enters exactly as C_i - z D_i (D_i = sum of the group's digits i):
+//   row += s * unit_g * ((C_0 - z D_0) * 254 + (C_1 - z D_1))      (|.| < 2^25)
+//
+// Sets of four groups (256 columns, 128 bytes of a row) are eight MMAs into one
+// accumulator.  Lane (r = lane / 4, t = lane % 4) supplies group t of the set: its 32
+// bytes of rows r and r + 8, byte word m (columns 8m .. 8m + 7 of the group) to MMA m,
+// low nibbles (even columns) at the lane's k positions 4t..4t+3, high nibbles (odd
+// columns) at 4t+16..4t+19.  B column 2j + i carries digit i of group j at group j's k
+// positions and zeros elsewhere, so after the set lane (r, t) holds C_0 and C_1 of group
+// t for rows r and r + 8 and finishes that group itself.
+//
+// Rows are K/2 bytes apart (a multiple of 128): the same bytes of different rows share
+// banks.  Lane (r, t) reads its two 16-byte units in the order (2t + (r & 1), the other),
+// so each quarter-warp's 16-byte loads cover 8 different units (conflict-free), then
+// swaps them back for odd rows.
+//
+// Vector fragments, per set S of four groups and MMA pair q = m / 2: 128 bytes, 16 for
+// each (group t, digit i) at (2t + i) * 16, holding MMA 2q then 2q + 1: b0 = digit i of
+// columns 8m + {0, 2, 4, 6}, b1 = of 8m + {1, 3, 5, 7}.  2 bytes per element.
+constexpr int kQ4G = 64;  // the only group size these kernels take
+// bytes of a K-element vector's fragments (whole sets of four groups)
+__host__ __device__ constexpr int vfrag_bytes(int K) { return (K / kQ4G + 3) / 4 * 512; }
+DM_DEV void mma_u8s8_16832(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                           uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Per-group vector data beside the fragments, kept per half (the 32 elements one warp
+// holds) so that every slot has one writer and nothing needs an atomic.
+struct VGroup {
+    int d0[2], d1[2];  // digit sums of each half
+    float unit;        // S_g / (127 * 254)
+    uint32_t pad[3];
+};
+static_assert(sizeof(VGroup) == 32, "VGroup layout");
+
+// Element k of a vector (whole warps: lane l holds k = 32w + l of a 32-aligned run, which
+// lies in one scale group) given v = its value and vp = the value at k ^ 32, the other
+// half of its group: the group max, its two digits into the fragments, and the half's
+// digit sums and the group's unit into the group record (lane 0).  One pass, no barrier:
+// both halves' warps compute the same maximum.  A zero group gives zero digits; a
+// non-finite group max gives a non-finite unit, so non-finite inputs reach the outputs.
+DM_DEV void vgroup_build(int8_t* vf, VGroup* vg, int k, float v, float vp) {
+    const float S = __uint_as_float(
+        __reduce_max_sync(0xffffffffu, max(__float_as_uint(fabsf(v)), __float_as_uint(fabsf(vp)))));
+    const float inv = S > 0.0f && S <= 3.0e38f ? 127.0f / S : 0.0f;
+    // round to nearest even through 1.5 * 2^23 (|u|, |e| <= 127.5): the sum's low bits are
+    // the integer
+    constexpr float kRound = 12582912.0f;
+    const float u = v * inv;
+    const float t0 = u + kRound;
+    const int d0 = __float_as_int(t0) - 0x4B400000;
+    const float t1 = (u - (t0 - kRound)) * 254.0f + kRound;
+    const int d1 = __float_as_int(t1) - 0x4B400000;
+    const int grp = k / kQ4G, col = k & (kQ4G - 1), m = col >> 3, p = col & 7;
+    const int o = (((grp >> 2) * 4 + (m >> 1)) * 128) + ((grp & 3) * 2) * 16 + (m & 1) * 8 + (p & 1) * 4 + (p >> 1);
+    vf[o] = static_cast<int8_t>(d0);
+    vf[o + 16] = static_cast<int8_t>(d1);  // digit 1: the next 16 bytes
+    // both sums in one reduction: |sum d0|, |sum d1| <= 32 * 127 < 2^15
+    const int pk = __reduce_add_sync(0xffffffffu, d0 + d1 * 65536);
+    if ((threadIdx.x & 31) == 0) {
+        VGroup& g = vg[grp];
+        const int h = (k >> 5) & 1;
+        const int s0 = static_cast<int16_t>(pk & 0xFFFF);
+        g.d0[h] = s0;
+        g.d1[h] = (pk - s0) >> 16;
+        g.unit = S * (1.0f / (127.0f * 254.0f));  // both halves store the same value
+    }
+}
+
+// Set S (groups 4S .. 4S + ng - 1, ng <= 4) of a chunk's 16 rows (Q4 layout in shared
+// memory) against the vector fragments: adds s * unit * T of group 4S + lane % 4 (if
+// < ng) to rows lane / 4 (ya) and lane / 4 + 8 (yb).  The caller sums the four lanes of
+// each row.
 template <int K>
-__device__ __forceinline__ void x4_store(float* x4, int k, float v) {
-    constexpr int NV = K / 32;
-    const int vv = k >> 5, c = (k >> 2) & 7, e = k & 3;
-    x4[(c * NV + vv) * 4 + e] = v;
-}
-
-__device__ __forceinline__ float nib(uint32_t word_masked, int b) {
-    return __uint_as_float(__byte_perm(word_masked, 0x4B000000u, 0x7540u | b));
-}
-
-template <int LPR>
-__device__ __forceinline__ float lane_group_sum(float v) {
-#pragma unroll
-    for (int m = LPR / 2; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
-    return v;
-}
-
-template <int K, int G>
-__device__ __forceinline__ float q4_partial_smem(const uint8_t* chunk, int r, int vl, const float4* x4) {
-    using Q = Q4<K, G>;
-    const uint8_t* qrow = chunk + r * (K / 2);
-    const uint16_t* srow = reinterpret_cast<const uint16_t*>(chunk + Q::S_OFF) + r * (K / G);
-    const uint8_t* zrow = chunk + Q::Z_OFF + r * (K / G / 2);
-    float acc = 0.0f;
-#pragma unroll
-    for (int i = 0; i < Q::VPL; ++i) {
-        const int v = vl + Q::LPR * i;
-        const int g = (v * 32) / G;
-        const uint4 q = *reinterpret_cast<const uint4*>(qrow + 16 * v);
-        const float s = __half2float(__ushort_as_half(srow[g]));
-        const uint32_t zb = zrow[g >> 1];
-        const uint32_t z = (g & 1) ? (zb >> 4) : (zb & 15u);
-        const float fz = __uint_as_float(0x4B000000u | z);
-        const uint32_t words[4] = {q.x, q.y, q.z, q.w};
-        float av0 = 0.0f, av1 = 0.0f;  // two chains (low / high nibbles) halve the latency
-#pragma unroll
-        for (int wd = 0; wd < 4; ++wd) {
-            const uint32_t lo = words[wd] & 0x0F0F0F0Fu;
-            const uint32_t hi = (words[wd] >> 4) & 0x0F0F0F0Fu;
-            const float4 xa = x4[(2 * wd) * Q::NV + v];
-            const float4 xb = x4[(2 * wd + 1) * Q::NV + v];
-            av0 = fmaf(nib(lo, 0) - fz, xa.x, av0);
-            av1 = fmaf(nib(hi, 0) - fz, xa.y, av1);
-            av0 = fmaf(nib(lo, 1) - fz, xa.z, av0);
-            av1 = fmaf(nib(hi, 1) - fz, xa.w, av1);
-            av0 = fmaf(nib(lo, 2) - fz, xb.x, av0);
-            av1 = fmaf(nib(hi, 2) - fz, xb.y, av1);
-            av0 = fmaf(nib(lo, 3) - fz, xb.z, av0);
-            av1 = fmaf(nib(hi, 3) - fz, xb.w, av1);
+DM_DEV void q4_set_mma(const uint8_t* chunk, const uint4* vf, const VGroup* vg, int S, int ng, int lane, float& ya,
+                       float& yb) {
+    using Q = Q4<K, kQ4G>;
+    constexpr int NG = K / kQ4G, RB = K / 2;
+    const int r = lane >> 2, t = lane & 3;
+    const bool have = t < ng;
+    const int g = 4 * S + t;  // this lane's group
+    // A: 32 bytes of rows r and r + 8 (units in row-parity order, then swapped back)
+    uint4 a0 = make_uint4(0u, 0u, 0u, 0u), a1 = a0, b0 = a0, b1 = a0;
+    if (have) {
+        const int u0 = r & 1;
+        const uint8_t* pa = chunk + r * RB + g * 32;
+        const uint8_t* pb = chunk + (r + 8) * RB + g * 32;
+        a0 = *reinterpret_cast<const uint4*>(pa + 16 * u0);
+        a1 = *reinterpret_cast<const uint4*>(pa + 16 * (1 - u0));
+        b0 = *reinterpret_cast<const uint4*>(pb + 16 * u0);
+        b1 = *reinterpret_cast<const uint4*>(pb + 16 * (1 - u0));
+        if (u0) {
+            const uint4 x = a0; a0 = a1; a1 = x;
+            const uint4 y = b0; b0 = b1; b1 = y;
         }
-        acc = fmaf(s, av0 + av1, acc);
     }
-    return acc;
-}
-
-// Rows rA and rB of one chunk at once (one lane group per row pair, LPR == 32): the
-// activation loads serve both rows.  Each row's arithmetic is q4_partial_smem's, in the
-// same order, so the results are the same bits.
-template <int K, int G>
-__device__ __forceinline__ void q4_partial2_smem(const uint8_t* chunk, int rA, int rB, int vl, const float4* x4,
-                                                 float& outA, float& outB) {
-    using Q = Q4<K, G>;
-    const uint8_t* qa = chunk + rA * (K / 2);
-    const uint8_t* qb = chunk + rB * (K / 2);
-    const uint16_t* sa = reinterpret_cast<const uint16_t*>(chunk + Q::S_OFF) + rA * (K / G);
-    const uint16_t* sb = reinterpret_cast<const uint16_t*>(chunk + Q::S_OFF) + rB * (K / G);
-    const uint8_t* za = chunk + Q::Z_OFF + rA * (K / G / 2);
-    const uint8_t* zb = chunk + Q::Z_OFF + rB * (K / G / 2);
-    float accA = 0.0f, accB = 0.0f;
+    const uint32_t wa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    const uint32_t wb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    // B: lanes (n, t) with n / 2 == t carry digit n % 2 of their group; the rest zeros
+    const bool bl = (r >> 1) == t && have;
+    int c[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int i = 0; i < Q::VPL; ++i) {
-        const int v = vl + Q::LPR * i;
-        const int g = (v * 32) / G;
-        const uint4 q0 = *reinterpret_cast<const uint4*>(qa + 16 * v);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(qb + 16 * v);
-        const float s0 = __half2float(__ushort_as_half(sa[g]));
-        const float s1 = __half2float(__ushort_as_half(sb[g]));
-        const uint32_t zb0 = za[g >> 1], zb1 = zb[g >> 1];
-        const float fz0 = __uint_as_float(0x4B000000u | ((g & 1) ? (zb0 >> 4) : (zb0 & 15u)));
-        const float fz1 = __uint_as_float(0x4B000000u | ((g & 1) ? (zb1 >> 4) : (zb1 & 15u)));
-        const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w};
-        const uint32_t w1[4] = {q1.x, q1.y, q1.z, q1.w};
-        float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+    for (int q = 0; q < 4; ++q) {
+        const uint4 v = bl ? vf[(S * 4 + q) * 8 + r] : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-        for (int wd = 0; wd < 4; ++wd) {
-            const uint32_t lo0 = w0[wd] & 0x0F0F0F0Fu, hi0 = (w0[wd] >> 4) & 0x0F0F0F0Fu;
-            const uint32_t lo1 = w1[wd] & 0x0F0F0F0Fu, hi1 = (w1[wd] >> 4) & 0x0F0F0F0Fu;
-            const float4 xa = x4[(2 * wd) * Q::NV + v];
-            const float4 xb = x4[(2 * wd + 1) * Q::NV + v];
-            a0 = fmaf(nib(lo0, 0) - fz0, xa.x, a0);
-            a1 = fmaf(nib(hi0, 0) - fz0, xa.y, a1);
-            b0 = fmaf(nib(lo1, 0) - fz1, xa.x, b0);
-            b1 = fmaf(nib(hi1, 0) - fz1, xa.y, b1);
-            a0 = fmaf(nib(lo0, 1) - fz0, xa.z, a0);
-            a1 = fmaf(nib(hi0, 1) - fz0, xa.w, a1);
-            b0 = fmaf(nib(lo1, 1) - fz1, xa.z, b0);
-            b1 = fmaf(nib(hi1, 1) - fz1, xa.w, b1);
-            a0 = fmaf(nib(lo0, 2) - fz0, xb.x, a0);
-            a1 = fmaf(nib(hi0, 2) - fz0, xb.y, a1);
-            b0 = fmaf(nib(lo1, 2) - fz1, xb.x, b0);
-            b1 = fmaf(nib(hi1, 2) - fz1, xb.y, b1);
-            a0 = fmaf(nib(lo0, 3) - fz0, xb.z, a0);
-            a1 = fmaf(nib(hi0, 3) - fz0, xb.w, a1);
-            b0 = fmaf(nib(lo1, 3) - fz1, xb.z, b0);
-            b1 = fmaf(nib(hi1, 3) - fz1, xb.w, b1);
+        for (int h = 0; h < 2; ++h) {
+            const int m = 2 * q + h;
+            mma_u8s8_16832(c, wa[m] & 0x0F0F0F0Fu, wb[m] & 0x0F0F0F0Fu, (wa[m] >> 4) & 0x0F0F0F0Fu,
+                           (wb[m] >> 4) & 0x0F0F0F0Fu, h ? v.z : v.x, h ? v.w : v.y);
         }
-        accA = fmaf(s0, a0 + a1, accA);
-        accB = fmaf(s1, b0 + b1, accB);
     }
-    outA = accA;
-    outB = accB;
+    if (have) {
+        const VGroup G = vg[g];
+        const int D0 = G.d0[0] + G.d0[1], D1 = G.d1[0] + G.d1[1];
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(chunk + Q::S_OFF);
+        const uint8_t* zp = chunk + Q::Z_OFF;
+        const uint32_t zba = zp[r * (NG / 2) + (g >> 1)], zbb = zp[(r + 8) * (NG / 2) + (g >> 1)];
+        const int za = static_cast<int>((g & 1) ? (zba >> 4) : (zba & 15u));
+        const int zb = static_cast<int>((g & 1) ? (zbb >> 4) : (zbb & 15u));
+        const float sa = __half2float(__ushort_as_half(sc[r * NG + g]));
+        const float sb = __half2float(__ushort_as_half(sc[(r + 8) * NG + g]));
+        const int ta = (c[0] - za * D0) * 254 + (c[1] - za * D1);
+        const int tb = (c[2] - zb * D0) * 254 + (c[3] - zb * D1);
+        ya = fmaf(sa * G.unit, static_cast<float>(ta), ya);
+        yb = fmaf(sb * G.unit, static_cast<float>(tb), yb);
+    }
 }
 
 constexpr int kMoeMaxSlots = 16;   // gate/up chunk slots (mbarriers) per CTA
@@ -348,6 +373,8 @@ struct MoeFusedArgs {
     uint64_t* cta_trace;      // per-CTA stamps (kTrMoeCtaSlots per CTA, thread 0) or null
     uint64_t* kt;             // launch timeline record or null
     uint32_t* err;
+    const uint8_t* l2_next;   // the next kernel's weights, prefetched into L2 while this
+    uint64_t l2_next_bytes;   // kernel's phases leave HBM idle (or null / 0)
 };
 
 DM_DEV void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
@@ -380,6 +407,9 @@ DM_DEV float poll_slot(const unsigned long long* p, unsigned tag, uint32_t* err)
 }
 
 constexpr int kMoeThreads = 512;
+// Share (in quarters) of the next kernel's weights prefetched into L2 during the top-k; the
+// rest follows once the routed gate/up bytes are in.
+constexpr int kMoeL2First = 2;
 constexpr int kMoeMaxE = kMoeThreads;  // phase 1b: one thread per expert
 
 template <int K, int KI, int G>
@@ -391,9 +421,11 @@ struct MoeFusedSmem {
     __host__ __device__ static size_t xn_off(int up_slots, int nexp) { return dn_off(up_slots) + static_cast<size_t>(nexp) * QD::CHUNK; }
     __host__ __device__ static size_t xs_off(int up_slots, int nexp) { return xn_off(up_slots, nexp) + K * 4; }
     __host__ __device__ static size_t h_off(int up_slots, int nexp) { return xs_off(up_slots, nexp) + K * 4; }
-    // the h region also holds phase 1b's logits and candidates (16 bytes per expert)
+    // the h region holds phase 1b's logits and candidates (16 bytes per expert), then each
+    // expert's h as vector fragments and scale groups
     __host__ __device__ static size_t h_bytes(int nexp, int E) {
-        const size_t hb = static_cast<size_t>(nexp) * KI * 4, tb = static_cast<size_t>(E + 2) * 16;
+        const size_t hb = static_cast<size_t>(nexp) * (KI * 4 + vfrag_bytes(KI) + (KI / kQ4G) * sizeof(VGroup));
+        const size_t tb = static_cast<size_t>(E + 2) * 16;
         return hb > tb ? hb : tb;
     }
     __host__ __device__ static size_t total(int up_slots, int nexp, int E) { return h_off(up_slots, nexp) + h_bytes(nexp, E); }
@@ -401,13 +433,16 @@ struct MoeFusedSmem {
 
 template <int K, int KI, int G>
 __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_constant__ MoeFusedArgs a) {
-    using QU = Q4<K, G>;
+    using QU = Q4<K, G>;   // global chunk layouts
     using QD = Q4<KI, G>;
+    constexpr int NGU = K / kQ4G, NGD = KI / kQ4G;  // scale groups per gate/up and down row
     using SM = MoeFusedSmem<K, KI, G>;
+    static_assert(G == kQ4G, "group size");
     constexpr int VPL = K / 256;
     extern __shared__ __align__(128) uint8_t dsm[];
     __shared__ __align__(8) uint64_t bar_up[kMoeMaxSlots];
     __shared__ __align__(8) uint64_t bar_dn[kMaxTopK + 1];
+    __shared__ __align__(8) uint64_t bar_h;  // phase 3's copy of h
     __shared__ int sid[kMaxTopK];
     __shared__ float sp[kMaxTopK + 1];
     __shared__ float red[kMoeThreads / 32];
@@ -415,6 +450,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     __shared__ float s_wred[kMoeThreads / 32];
     __shared__ int s_wcnt[kMoeThreads / 32];
     __shared__ int s_wcnt_b[kMoeThreads / 32];
+    __shared__ float s_part[256];  // partial rows: phase 2 [group][quarter][16], phase 3 [warp][16]
     __shared__ uint32_t s_g8[kMoeMaxE / 8];
     __shared__ uint32_t s_thr;
     __shared__ float s_inv;
@@ -429,7 +465,9 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     const bool has_down = c < a.d_chunks;
     uint8_t* up_s = dsm + SM::up_off();
     uint8_t* dn_s = dsm + SM::dn_off(a.up_slots);
-    float* xn4 = reinterpret_cast<float*>(dsm + SM::xn_off(a.up_slots, nexp));
+    // x_norm as vector fragments, then its scale groups
+    int8_t* xvf = reinterpret_cast<int8_t*>(dsm + SM::xn_off(a.up_slots, nexp));
+    VGroup* xvg = reinterpret_cast<VGroup*>(xvf + vfrag_bytes(K));
     float* xsr = reinterpret_cast<float*>(dsm + SM::xs_off(a.up_slots, nexp));
     float* h4 = reinterpret_cast<float*>(dsm + SM::h_off(a.up_slots, nexp));
 
@@ -450,6 +488,7 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     if (tid == 0) {
         for (int k = 0; k < i1 - i0; ++k) mbar_init(&bar_up[k], 1);
         for (int j = 0; j < nexp; ++j) mbar_init(&bar_dn[j], 1);
+        mbar_init(&bar_h, 1);
         mbar_fence_init();
         for (int k = 0; k < i1 - i0; ++k) {
             const int item = i0 + k;
@@ -481,8 +520,8 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     // words carry its parity, flipped, as their tag, so the previous launch's words never
     // match: no flag needs resetting at exit.
     if (tid == 0) s_gen = ld_relaxed_u64(a.arrivals) / static_cast<unsigned long long>(nblk);
-    // residual of this warp's output row (phase 3), fetched now, off the critical path
-    const float xm_row = (has_down && lane == 0) ? a.x_mid[16 * c + warp] : 0.0f;
+    // residual of output row 16c + lane (phase 3, warp 0), fetched now, off the critical path
+    const float xm_row = (has_down && warp == 0 && lane < 16) ? a.x_mid[16 * c + lane] : 0.0f;
 
     // ---- phase 1: canonical RMSNorm (512 threads), router rows ----
     {
@@ -506,7 +545,6 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
             const int k = i * kMoeThreads + tid;
             if (k < K) {
                 const float y = __fmul_rn(__fdiv_rn(xv[i], denom), gv[i]);
-                x4_store<K>(xn4, k, y);
                 xs_store_split(xsr, K, k, y);
                 if (c == 0 && a.xn_out) a.xn_out[k] = y;
             }
@@ -541,7 +579,20 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         }
     }
     trace_stamp(tr, 3);
+    // x_norm's digits, from its split copy; the barriers of phase 1b order them before
+    // phase 2
+#pragma unroll
+    for (int i = 0; i < XPT; ++i) {
+        const int k = i * kMoeThreads + tid;
+        if (k < K) {
+            const int kp = k ^ 32;
+            vgroup_build(xvf, xvg, k, xsr[((k & 7) < 4 ? 0 : K / 2) + (k >> 3) * 4 + (k & 3)],
+                         xsr[((kp & 7) < 4 ? 0 : K / 2) + (kp >> 3) * 4 + (kp & 3)]);
+        }
+    }
     pdl_launch_dependents();  // the next kernel's preloads overlap the top-k
+    // the first part of the next kernel's weights into L2 while the top-k runs (HBM idle)
+    if (warp == 0) prefetch_l2_share(a.l2_next, a.l2_next_bytes * kMoeL2First / 4, c, nblk, lane);
     // ---- phase 1b, in every CTA: the E + 1 logits, softmax and top-k.  Every CTA runs the
     // same arithmetic on the same words, so all reach the same ids without a broadcast ----
     {
@@ -697,40 +748,48 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     const bool late_down = i1 > i0;
     if (!late_down && has_down && tid >= 32 && tid < 32 + a.topk) issue_down(tid - 32);
 
-    // ---- phase 2: gate/up; two warp groups take alternate items ----
+    // ---- phase 2: gate/up on the tensor cores.  Four warps per item (item k to warp
+    // group k % 4), each a quarter of the scale groups; the group's partial rows meet in
+    // shared memory and its first warp forms h = SiLU(gate) * up for the item's 8 rows ----
     {
-        const float4* xv4 = reinterpret_cast<const float4*>(xn4);
-        const int wgrp = warp >> 3, wg = warp & 7;
-        for (int k = wgrp; k < i1 - i0; k += 2) {
+        constexpr int NSU = (NGU + 3) / 4;  // sets of four groups per row
+        const int grp = warp >> 2, qw = warp & 3;
+        const uint4* vf = reinterpret_cast<const uint4*>(xvf);
+        float* part = s_part + grp * 64;  // [quarter][16 rows]
+        for (int k = grp; k < i1 - i0; k += 4) {
             const int item = i0 + k;
             const int j = item / a.gu_chunks, cc = item % a.gu_chunks;
             const bool ok = mbar_wait_bounded(&bar_up[k], 0, a.err, nullptr);
             if (k == 0) trace_stamp(ct, 3);  // the CTA's first item landed
             if (late_down && k == 0 && warp == 0 && has_down && lane < a.topk) issue_down(lane);
             const uint8_t* chunk = up_s + static_cast<size_t>(k) * QU::CHUNK;
-            float dots[2];
-            if (QU::RPP == 1) {  // gate row wg and up row 8 + wg together
-                float g = 0.0f, u = 0.0f;
-                if (ok) q4_partial2_smem<K, G>(chunk, wg, 8 + wg, lane, xv4, g, u);
-                dots[0] = lane_group_sum<QU::LPR>(g);
-                dots[1] = lane_group_sum<QU::LPR>(u);
-            } else
-#pragma unroll
-            for (int p = 0; p < 2; p += QU::RPP) {
-                const int sub = lane / QU::LPR, vl = lane % QU::LPR;
-                const int ri = p + sub;
-                float v = 0.0f;
-                if (ri < 2 && ok) v = q4_partial_smem<K, G>(chunk, ri == 0 ? wg : 8 + wg, vl, xv4);
-                v = lane_group_sum<QU::LPR>(v);
-                if (QU::RPP == 1) dots[p] = v;
-                else {
-                    const float other = __shfl_sync(0xffffffffu, v, QU::LPR);
-                    dots[0] = __shfl_sync(0xffffffffu, v, 0);
-                    dots[1] = other;
-                }
+            float ya = 0.0f, yb = 0.0f;  // rows lane/4 and lane/4 + 8, group lane % 4 of each set
+            if (ok) {
+#pragma unroll 1
+                for (int S = qw; S < NSU; S += 4)
+                    q4_set_mma<K>(chunk, vf, xvg, S, NGU - 4 * S < 4 ? NGU - 4 * S : 4, lane, ya, yb);
             }
-            if (lane == 0) __stcg(a.h + j * a.I + 8 * cc + wg, silu_f(dots[0]) * dots[1]);
+            ya += __shfl_xor_sync(0xffffffffu, ya, 1);
+            yb += __shfl_xor_sync(0xffffffffu, yb, 1);
+            ya += __shfl_xor_sync(0xffffffffu, ya, 2);
+            yb += __shfl_xor_sync(0xffffffffu, yb, 2);
+            if ((lane & 3) == 0) {
+                part[qw * 16 + (lane >> 2)] = ya;
+                part[qw * 16 + (lane >> 2) + 8] = yb;
+            }
+            named_bar_sync(1 + grp, 128);
+            if (qw == 0 && lane < 8) {  // rows 0..7 are gate rows, 8..15 the matching up rows
+                const float gt = ((part[lane] + part[16 + lane]) + part[32 + lane]) + part[48 + lane];
+                const float up = ((part[8 + lane] + part[24 + lane]) + part[40 + lane]) + part[56 + lane];
+                __stcg(a.h + j * a.I + 8 * cc + lane, silu_f(gt) * up);
+            }
+            named_bar_sync(1 + grp, 128);  // the group's partial rows are reused by its next item
         }
+    }
+    // the rest of the next kernel's weights, once this CTA's routed gate/up bytes are in
+    if (warp == 1 && a.l2_next) {
+        const uint64_t first = (a.l2_next_bytes * kMoeL2First / 4) & ~static_cast<uint64_t>(15);
+        prefetch_l2_share(a.l2_next + first, a.l2_next_bytes - first, c, nblk, lane);
     }
     __syncthreads();
     trace_stamp(tr, 6);
@@ -738,7 +797,16 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     if (tid == 0) {
         const unsigned long long target = (s_gen + 1) * static_cast<unsigned long long>(nblk);
         red_release_add_u64(a.arrivals, 1ull);
-        if (has_down) spin_geq_u64(a.arrivals, target, a.err);
+        if (has_down) {
+            spin_geq_u64(a.arrivals, target, a.err);
+            // every CTA's h (written before its release) into shared memory: the acquire above
+            // orders those writes before this thread's bulk (async-proxy) read
+            const uint32_t hb = static_cast<uint32_t>(nexp * KI * 4);
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            fence_proxy_async_smem();  // phase 1b's generic accesses of the region (before the barrier above)
+            mbar_arrive_expect_tx(&bar_h, hb);
+            bulk_g2s(h4, a.h, hb, &bar_h);
+        }
     }
     __syncthreads();
     trace_stamp(tr, 7);
@@ -749,33 +817,27 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         ct[7] = smid;
     }
 
-    // ---- phase 3: 16 output rows of every selected expert + residual.  Warp w owns output
-    // row 16c + w; lane l covers the WPL = I/32 contiguous weights [l*WPL, l*WPL + WPL) of
-    // that row in every expert; the lane accumulates all experts, weighted by the router
-    // probability (the shared expert by its sigmoid gate), and one warp reduction ends the
-    // row.  h is restaged lane-major so every read is conflict-free.
+    // ---- phase 3: this CTA's 16 output rows (16c .. 16c + 15) over every selected
+    // expert, on the tensor cores.  h of each expert becomes vector fragments; the units
+    // (expert, up to four scale groups) are spread over the 16 warps; each adds
+    // p_j * (its 16 rows against h_j), p_j the router probability (the shared expert: its
+    // sigmoid gate); warp 0 sums the warps' partial rows in warp order + residual ----
     if (has_down) {
-        constexpr int WPL = KI / 32;   // weights per lane
-        constexpr int F4L = WPL / 4;   // float4 of h per lane
-        static_assert(WPL >= 4 && WPL % 4 == 0 && WPL <= G, "down-row lane geometry");
-        {
-            constexpr int HPT = ((kMaxTopK + 1) * KI + kMoeThreads - 1) / kMoeThreads;
-            const int nh = nexp * KI;
-            float hv[HPT];
-#pragma unroll
-            for (int i = 0; i < HPT; ++i) {
-                const int t = tid + kMoeThreads * i;
-                hv[i] = t < nh ? __ldcg(a.h + t) : 0.0f;
-            }
-#pragma unroll
-            for (int i = 0; i < HPT; ++i) {
-                const int t = tid + kMoeThreads * i;
-                if (t < nh) {
-                    const int j = t / KI, k = t % KI, l = k / WPL, w = k % WPL;
-                    h4[((j * F4L + (w >> 2)) * 32 + l) * 4 + (w & 3)] = hv[i];
-                }
-            }
-        }
+        constexpr int SETS = (NGD + 3) / 4;  // units per expert
+        constexpr int VFB = vfrag_bytes(KI);
+        const int nh = nexp * KI;
+        // h of every expert (landed by the bulk copy issued at the barrier), then expert j's
+        // fragments at hvf + j * VFB and scale groups at hvg + j * NGD
+        const float* hfl = h4;
+        int8_t* hvf = reinterpret_cast<int8_t*>(h4 + nh);
+        VGroup* hvg = reinterpret_cast<VGroup*>(hvf + nexp * VFB);
+        const bool okh = mbar_wait_bounded(&bar_h, 0, a.err, nullptr);
+        // a warp's 32 consecutive t lie in one scale group of one expert (KI % 64 == 0), and
+        // t ^ 32 is the other half of that group
+#pragma unroll 3
+        for (int t = tid; t < nh; t += kMoeThreads)
+            vgroup_build(hvf + (t / KI) * VFB, hvg + (t / KI) * NGD, t % KI, okh ? hfl[t] : 0.0f,
+                         okh ? hfl[t ^ 32] : 0.0f);
         __syncthreads();
         uint64_t* td = (tr && c == 0) ? tr + 40 : nullptr;  // down-phase detail of CTA 0 (slots 56..59)
         trace_stamp(td, 0);
@@ -783,53 +845,36 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         const bool ok = __all_sync(0xffffffffu, okl);  // lane j waited for expert j's chunk
         trace_stamp(td, 1);
         const long long cyc0 = clock64();
-        const int gl = (lane * WPL) / G;  // this lane's scale group
-        const float4* h4v = reinterpret_cast<const float4*>(h4);
-        // one expert's contribution to this lane: s * sum (F(q) - F(z)) * h, times its weight
-        auto expert_part = [&](int j) -> float {
-            const uint8_t* chunk = dn_s + static_cast<size_t>(j) * QD::CHUNK;
-            const uint8_t* qrow = chunk + warp * (KI / 2) + lane * (WPL / 2);
-            const float s = __half2float(
-                __ushort_as_half(reinterpret_cast<const uint16_t*>(chunk + QD::S_OFF)[warp * (KI / G) + gl]));
-            const uint32_t zb = chunk[QD::Z_OFF + warp * (KI / G / 2) + (gl >> 1)];
-            const float fz = __uint_as_float(0x4B000000u | ((gl & 1) ? (zb >> 4) : (zb & 15u)));
-            uint32_t words[WPL / 8 > 0 ? WPL / 8 : 1];
-            if (WPL == 16) {
-                const uint2 q = *reinterpret_cast<const uint2*>(qrow);
-                words[0] = q.x;
-                words[WPL / 8 - 1] = q.y;
-            } else if (WPL == 8) {
-                words[0] = *reinterpret_cast<const uint32_t*>(qrow);
-            } else {
-                words[0] = *reinterpret_cast<const uint16_t*>(qrow);
-            }
-            float d0 = 0.0f, d1 = 0.0f;
-#pragma unroll
-            for (int f = 0; f < F4L; ++f) {
-                const float4 xv = h4v[(j * F4L + f) * 32 + lane];
-                const uint32_t wd = words[f >> 1] >> (16 * (f & 1));  // 4 weights: 2 bytes
-                const uint32_t lo = wd & 0x0F0Fu, hi = (wd >> 4) & 0x0F0Fu;
-                d0 = fmaf(nib(lo, 0) - fz, xv.x, d0);
-                d1 = fmaf(nib(hi, 0) - fz, xv.y, d1);
-                d0 = fmaf(nib(lo, 1) - fz, xv.z, d0);
-                d1 = fmaf(nib(hi, 1) - fz, xv.w, d1);
-            }
-            return s * (d0 + d1) * (j < a.topk ? sp[j] : sp[a.topk]);
-        };
-        // rolled (the code runs once per launch and is fetched cold), two experts per
-        // iteration so their loads and chains overlap
-        float acc0 = 0.0f, acc1 = 0.0f;
+        float acc0 = 0.0f, acc1 = 0.0f;  // rows lane/4 and lane/4 + 8
+        if (ok) {
 #pragma unroll 1
-        for (int j = 0; j < nexp; j += 2) {
-            acc0 += expert_part(j);
-            if (j + 1 < nexp) acc1 += expert_part(j + 1);
+            for (int u = warp; u < nexp * SETS; u += kMoeThreads / 32) {
+                const int j = u / SETS, S = u % SETS;
+                float ya = 0.0f, yb = 0.0f;
+                q4_set_mma<KI>(dn_s + static_cast<size_t>(j) * QD::CHUNK, reinterpret_cast<const uint4*>(hvf + j * VFB),
+                               hvg + j * NGD, S, NGD - 4 * S < 4 ? NGD - 4 * S : 4, lane, ya, yb);
+                const float pj = j < a.topk ? sp[j] : sp[a.topk];
+                acc0 = fmaf(pj, ya, acc0);
+                acc1 = fmaf(pj, yb, acc1);
+            }
         }
-        const float acc = warp_sum(ok ? acc0 + acc1 : 0.0f);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+        if ((lane & 3) == 0) {
+            s_part[warp * 16 + (lane >> 2)] = acc0;
+            s_part[warp * 16 + (lane >> 2) + 8] = acc1;
+        }
+        __syncthreads();
+        if (warp == 0 && lane < 16) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kMoeThreads / 32; ++w) acc += s_part[w * 16 + lane];
+            a.x_out[16 * c + lane] = acc + xm_row;
+        }
         trace_stamp(td, 2);
         if (td) td[3] = static_cast<uint64_t>(clock64() - cyc0);  // down compute, SM cycles (slot 59)
-        if (lane == 0) a.x_out[16 * c + warp] = acc + xm_row;
-    } else {
-        // no down rows here: drain this CTA's own shared-expert chunk copies (none issued)
     }
 
     __syncthreads();
@@ -851,8 +896,11 @@ static cudaError_t launch_moe_fused_t(const LaunchCfg& lc, MoeFusedArgs a) {
     return launch_kernel(lc, moe_fused_kernel<K, KI, G>, dim3(grid), dim3(kMoeThreads), smem, a);
 }
 
-cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot) {
+cudaError_t launch_moe_fused(const LaunchCfg& lc, const Dims& d, const LayerW& w, const Buffers& b, int slot,
+                             const void* l2_next, uint64_t l2_next_bytes) {
     MoeFusedArgs a{};
+    a.l2_next = static_cast<const uint8_t*>(l2_next);
+    a.l2_next_bytes = l2_next ? l2_next_bytes : 0;
     a.Wr = w.w_router;
     a.rbias = w.router_bias;
     a.gamma = w.post_norm;
