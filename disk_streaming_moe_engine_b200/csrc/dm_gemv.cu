@@ -263,12 +263,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_bf16_kernel(const __grid
 template <int K, int PRO>
 static cudaError_t launch_gemv_t(const LaunchCfg& lc, GemvArgs a) {
     a.kt = lc.kt;
-    // L2 look-ahead: lane 0 of every warp prefetches the row one grid stride ahead, before
-    // the wait too, so that during the predecessor's latency-bound tail (the MoE's top-k
-    // and id broadcast) each warp's second row is already on its way to L2.  Measured in
-    // the decode step: 0 rows 558.4, 1 row 566.6, 2 rows 558.7 tok/s (two rows crowd the
-    // MoE's routed-expert copies).
-    a.pf = 1;
+    // L2 look-ahead (lane 0 of every warp prefetching rows pf grid strides ahead, before the
+    // wait too): off.  The fused MoE kernel before an input projection already prefetches
+    // that projection's weights into L2 while its top-k leaves HBM idle; on top of that the
+    // look-ahead only competes with the MoE's routed-expert copies.  Measured in the decode
+    // step (two repetitions): 0 rows 624.8, 1 row 615.1, 2 rows 614.1 tok/s.  (Before the
+    // MoE prefetched, one row was the best setting: 0 rows 558.4, 1 row 566.6, 2 rows 558.7.)
+    a.pf = 0;
     const int want = (a.N + kGemvWarps - 1) / kGemvWarps;
     // two CTAs per SM: measured faster in the decode step than one, although one CTA per
     // SM leaves room for the next kernel's prologue (588.0 vs 588.0 tok/s for the attention
