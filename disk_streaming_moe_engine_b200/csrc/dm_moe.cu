@@ -579,17 +579,6 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
         }
     }
     trace_stamp(tr, 3);
-    // x_norm's digits, from its split copy; the barriers of phase 1b order them before
-    // phase 2
-#pragma unroll
-    for (int i = 0; i < XPT; ++i) {
-        const int k = i * kMoeThreads + tid;
-        if (k < K) {
-            const int kp = k ^ 32;
-            vgroup_build(xvf, xvg, k, xsr[((k & 7) < 4 ? 0 : K / 2) + (k >> 3) * 4 + (k & 3)],
-                         xsr[((kp & 7) < 4 ? 0 : K / 2) + (kp >> 3) * 4 + (kp & 3)]);
-        }
-    }
     pdl_launch_dependents();  // the next kernel's preloads overlap the top-k
     // the first part of the next kernel's weights into L2 while the top-k runs (HBM idle)
     if (warp == 0) prefetch_l2_share(a.l2_next, a.l2_next_bytes * kMoeL2First / 4, c, nblk, lane);
@@ -747,6 +736,19 @@ __global__ void __launch_bounds__(kMoeThreads, 2) moe_fused_kernel(const __grid_
     };
     const bool late_down = i1 > i0;
     if (!late_down && has_down && tid >= 32 && tid < 32 + a.topk) issue_down(tid - 32);
+
+    // x_norm's digits, from its split copy, while the routed chunks are on their way (off
+    // the path to the ids); the barrier orders them before the MMAs
+#pragma unroll
+    for (int i = 0; i < XPT; ++i) {
+        const int k = i * kMoeThreads + tid;
+        if (k < K) {
+            const int kp = k ^ 32;
+            vgroup_build(xvf, xvg, k, xsr[((k & 7) < 4 ? 0 : K / 2) + (k >> 3) * 4 + (k & 3)],
+                         xsr[((kp & 7) < 4 ? 0 : K / 2) + (kp >> 3) * 4 + (kp & 3)]);
+        }
+    }
+    __syncthreads();
 
     // ---- phase 2: gate/up on the tensor cores.  Four warps per item (item k to warp
     // group k % 4), each a quarter of the scale groups; the group's partial rows meet in
