@@ -572,35 +572,48 @@ __global__ void __launch_bounds__(kAT, 1) attn_decode_kernel(const __grid_consta
     }
 
     // ---- merge 2 (the CTAs of the last cluster, each a slice of the outputs): the
-    // cluster partials of every head of this KV group, output gate; every load of an
-    // output (its partials and their max / sum) is issued in one batch ----
+    // cluster partials of every head of this KV group, output gate.  Each head's cluster
+    // weights w_c = exp(m_c - M) and normaliser 1 / sum w_c l_c are formed once in shared
+    // memory; every thread then loads only its outputs' partials, all in one batch ----
     constexpr int kMaxClusters = kMaxSplits / kAttnCluster;
     const int ns = ccount;
-    for (int o = crank * kAT + tid; o < GRP * D; o += kAttnCluster * kAT) {
-        const int hh = o / D, d = o % D;
-        const int hq = g * GRP + hh;
-        const float* ph0 = part_out + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
-        float pv[kMaxClusters], ml[kMaxClusters], ll[kMaxClusters];
+    __shared__ float mw[GRP][kMaxClusters];
+    __shared__ float minv[GRP];
+    if (tid < GRP) {
+        const float* ph0 = part_out + static_cast<size_t>(g * GRP + tid) * kMaxSplits * (D + 2);
+        float ml[kMaxClusters], ll[kMaxClusters];
 #pragma unroll
         for (int c = 0; c < kMaxClusters; ++c) {
             const bool on = c < ns;
-            pv[c] = on ? __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + d) : 0.0f;
             ml[c] = on ? __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D) : -INFINITY;
             ll[c] = on ? __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + D + 1) : 0.0f;
         }
-        const float gate = qg_in[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
         float M = -INFINITY;
 #pragma unroll
         for (int c = 0; c < kMaxClusters; ++c)
             if (ll[c] > 0.0f) M = fmaxf(M, ml[c]);
-        float L = 0.0f, acc2 = 0.0f;
+        float L = 0.0f;
 #pragma unroll
         for (int c = 0; c < kMaxClusters; ++c) {
             const float w = ll[c] > 0.0f ? expf(ml[c] - M) : 0.0f;
+            mw[tid][c] = w;
             L = fmaf(w, ll[c], L);
-            acc2 = fmaf(w, pv[c], acc2);
         }
-        attn_out[static_cast<size_t>(hq) * D + d] = (L > 0.0f ? acc2 / L : 0.0f) * sigmoid_f(gate);
+        minv[tid] = L > 0.0f ? 1.0f / L : 0.0f;
+    }
+    __syncthreads();
+    for (int o = crank * kAT + tid; o < GRP * D; o += kAttnCluster * kAT) {
+        const int hh = o / D, d = o % D;
+        const int hq = g * GRP + hh;
+        const float* ph0 = part_out + static_cast<size_t>(hq) * kMaxSplits * (D + 2);
+        float pv[kMaxClusters];
+#pragma unroll
+        for (int c = 0; c < kMaxClusters; ++c) pv[c] = c < ns ? __ldcg(ph0 + static_cast<size_t>(c) * (D + 2) + d) : 0.0f;
+        const float gate = qg_in[static_cast<size_t>(a.Hq) * D + static_cast<size_t>(hq) * D + d];
+        float acc2 = 0.0f;
+#pragma unroll
+        for (int c = 0; c < kMaxClusters; ++c) acc2 = fmaf(mw[hh][c], pv[c], acc2);
+        attn_out[static_cast<size_t>(hq) * D + d] = acc2 * minv[hh] * sigmoid_f(gate);
     }
     if (tid == 0 && crank == 0) counters[g] = 0u;
     if (tid == 0 && crank == 0 && a.trace) a.trace[7] = globaltimer_ns();
