@@ -322,7 +322,8 @@ static int plan_memory(dm_ctx* c, bool commit) {
     // pairs one rank may compute: the routed choices of every row of a full group that land
     // on its experts, plus its own rows for the shared expert
     const size_t P = static_cast<size_t>(kMaxRanks) * BC * d.topk + BC;
-    const int max_segs = static_cast<int>((P + kSegTok - 1) / kSegTok) + std::min(d.E, static_cast<int>(P)) + 2;
+    // segments: whole kSegTok runs, one tail per expert (two small-segment pieces at most)
+    const int max_segs = static_cast<int>((P + kSegTok - 1) / kSegTok) + 2 * std::min(d.E + 1, static_cast<int>(P)) + 2;
     const int bgen_cap = 1 << 16;
     const size_t ob_slots = T(BC * 4), ob_tok = T(BC * 4), ob_x = T(BC * H * 4), ob_xm = T(BC * H * 4);
     // GEMM operand rows rounded up to 16 (the tensor map's box never leaves the buffer)
@@ -339,6 +340,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t max_cols = 2 * P + 16 * static_cast<size_t>(max_segs);
     const size_t ob_psrc = T(P * 4), ob_eout = T(BC * (d.topk + 1) * H * 4);
     const size_t ob_xgu = T(max_cols * H * 2), ob_xdn = T(max_cols * d.I * 2);
+    const size_t ob_xrec = T(P * q4_vrec_bytes(d.H)), ob_hrec = T(P * q4_vrec_bytes(d.I));
     const size_t ob_flags = T(2 * kMaxRanks * 4), ob_epoch = T(2 * 4);
     const size_t ob_cv = T(BC * kHeadChunks * 4), ob_ci = T(BC * kHeadChunks * 4), ob_hl = T(BC * d.V * 4);
     const size_t ob_gen = T(static_cast<size_t>(bgen_cap) * 4), ob_genidx = T(4);
@@ -350,7 +352,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t nmax_dense = std::max({static_cast<size_t>(d.gdn_in_rows), static_cast<size_t>(d.attn_in_rows),
                                         static_cast<size_t>(d.H)});
     const size_t PP = PR * d.topk + PR;
-    const int pmax_segs = static_cast<int>((PP + kSegTok - 1) / kSegTok) + std::min(d.E, static_cast<int>(PP)) + 2;
+    const int pmax_segs = static_cast<int>((PP + kSegTok - 1) / kSegTok) + 2 * std::min(d.E + 1, static_cast<int>(PP)) + 2;
     const size_t pmax_cols = 2 * PP + 16 * static_cast<size_t>(pmax_segs);
     const size_t pc_cap = std::max(2 * PR * nmax_dense, 2 * static_cast<size_t>(d.V));  // the head: one row
     const size_t op_slots = T(PR * 4), op_tok = T(PR * 4), op_x = T(PR * H * 4), op_xm = T(PR * H * 4);
@@ -363,6 +365,7 @@ static int plan_memory(dm_ctx* c, bool commit) {
     const size_t op_segs = T(static_cast<size_t>(pmax_segs) * 16), op_work = T(16), op_stats = T(16);
     const size_t op_rcnt = T((PR + 1) * 4), op_psrc = T(PP * 4), op_eout = T(PR * (d.topk + 1) * H * 4);
     const size_t op_xgu = T(pmax_cols * H * 2), op_xdn = T(pmax_cols * d.I * 2);
+    const size_t op_xrec = T(PP * q4_vrec_bytes(d.H)), op_hrec = T(PP * q4_vrec_bytes(d.I));
     const size_t op_cv = T(kHeadChunks * 4), op_ci = T(kHeadChunks * 4), op_hl = T(static_cast<size_t>(d.V) * 4);
     const size_t op_gen = T(16), op_genidx = T(4);
     const size_t op_u = T(PR * d.qkv_dim * 4);
@@ -473,6 +476,8 @@ static int plan_memory(dm_ctx* c, bool commit) {
     bb.max_cols = static_cast<int>(max_cols);
     bb.xgu = A + ob_xgu;
     bb.xdn = A + ob_xdn;
+    bb.xrec = A + ob_xrec;
+    bb.hrec = A + ob_hrec;
     bb.eout = reinterpret_cast<float*>(A + ob_eout);
     bb.cand_val = reinterpret_cast<float*>(A + ob_cv);
     bb.cand_idx = reinterpret_cast<int*>(A + ob_ci);
@@ -516,6 +521,8 @@ static int plan_memory(dm_ctx* c, bool commit) {
     pb.ep_epoch = bb.ep_epoch;
     pb.xgu = A + op_xgu;
     pb.xdn = A + op_xdn;
+    pb.xrec = A + op_xrec;
+    pb.hrec = A + op_hrec;
     pb.eout = reinterpret_cast<float*>(A + op_eout);
     pb.cand_val = reinterpret_cast<float*>(A + op_cv);
     pb.cand_idx = reinterpret_cast<int*>(A + op_ci);
@@ -2844,9 +2851,10 @@ int32_t dm_batch_kernels_per_step(dm_ctx* c, int32_t n, int32_t* own, int32_t* g
     if (!c || !own || !gemms || n <= 0 || n > c->bb.cap) return DM_ERR_INVALID_ARG;
     // embed; per block: prep, input GEMM, epilogue, mixer core (recurrence, or attention +
     // split merge), (head-norm prep,) output GEMM, residual epilogue, router, top-k +
-    // grouping, operand staging, gate/up, down, combine = 13; head: prep, GEMM, two argmax
-    // kernels.  No library GEMMs.
-    *own = 1 + 13 * c->d.L + 4;
+    // grouping, the expert kernels (operand staging; gate/up and down of the small segments;
+    // gate/up and down of the large ones when a step can have them), combine; head: prep,
+    // GEMM, two argmax kernels.  No library GEMMs.
+    *own = 1 + (10 + b_expert_launches(c->d, c->bb, n)) * c->d.L + 4;
     *gemms = 0;
     return DM_OK;
 }

@@ -400,7 +400,7 @@ struct BGroupArgs {
     float* probs;
     float* sg;
     int4* segs;
-    int* work;            // [0] segments, [1] [2] work counters (reset here)
+    int* work;            // [0] large segments, [1] [2] work counters (reset here), [3] all segments
     int* pair_src;
     unsigned* stats;
     EpView ep;
@@ -408,6 +408,7 @@ struct BGroupArgs {
     unsigned* epoch;      // [2]
     const int* slot_of;   // [E] HBM slot of each routed expert when the pool spills, else null
     int E_res;            // resident routed records (the shared expert's record index)
+    int sm_tok;           // segments of at most this many tokens go to the small-segment kernels (0: none)
     uint32_t* err;
 };
 
@@ -531,16 +532,41 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
     else if (el == Eo)
         cnt = n;
     const int nsg = (cnt + kSegTok - 1) / kSegTok;
+    // segments of <= sm_tok tokens (only an expert's last one can be) go to the small-segment
+    // kernels as pieces of <= kSqTok tokens: listed after every large segment, those of 4
+    // tokens first, then 3, 2, 1 (the heaviest items start first), no staged operand rows
+    const int tk_last = nsg > 0 ? cnt - (nsg - 1) * kSegTok : 0;
+    const bool small = nsg > 0 && tk_last <= a.sm_tok;
+    const int nlg = nsg - (small ? 1 : 0);
+    const int pc0 = small ? min(tk_last, kSqTok) : 0;   // first piece
+    const int pc1 = small ? tk_last - pc0 : 0;          // second piece (0: none)
+    static_assert(kSmTok <= 2 * kSqTok, "two pieces at most");
     auto seg_rows = [](int tokens) { return (2 * tokens + 15) / 16 * 16; };
-    int ncol = 0;  // staged operand rows of this expert's segments
-    for (int s2 = 0; s2 < nsg; ++s2) ncol += seg_rows(min(kSegTok, cnt - s2 * kSegTok));
+    int ncol = 0;  // staged operand rows of this expert's large segments
+    for (int s2 = 0; s2 < nlg; ++s2) ncol += seg_rows(min(kSegTok, cnt - s2 * kSegTok));
     if (el < Eo && cnt > 0) atomicMax(&s_maxcnt, static_cast<unsigned>(cnt));
     const int touched = __syncthreads_count(el < Eo && cnt > 0);
     int total_pairs = 0, total_segs = 0, total_cols = 0;
     const int p0 = block_excl_scan(cnt, wsum, &total_pairs);
     __syncthreads();
-    const int s0 = block_excl_scan(nsg, wsum, &total_segs);
+    int total_lg = 0;
+    const int s0 = block_excl_scan(nlg, wsum, &total_lg);
     __syncthreads();
+    // pieces per size bucket (4, 3, 2, 1 tokens), this expert's place in each
+    int bofs[kSqTok], btot[kSqTok];
+#pragma unroll
+    for (int bk = 0; bk < kSqTok; ++bk) {
+        const int sz = kSqTok - bk;
+        bofs[bk] = block_excl_scan((pc0 == sz) + (pc1 == sz), wsum, &btot[bk]);
+        __syncthreads();
+    }
+    total_segs = total_lg;
+    int bbase[kSqTok];
+#pragma unroll
+    for (int bk = 0; bk < kSqTok; ++bk) {
+        bbase[bk] = total_segs;
+        total_segs += btot[bk];
+    }
     const int c0 = block_excl_scan(ncol, wsum, &total_cols);
     const bool pairs_ok = total_pairs <= a.max_pairs && total_segs <= a.max_segs && total_cols <= a.max_cols;
     if (el <= Eo) {
@@ -550,10 +576,19 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
         const int gexp = el < Eo ? (a.slot_of ? a.slot_of[e0 + el] : e0 + el) : a.E_res;
         if (pairs_ok) {
             int col = c0;
-            for (int s2 = 0; s2 < nsg; ++s2) {
+            for (int s2 = 0; s2 < nlg; ++s2) {
                 const int tk = min(kSegTok, cnt - s2 * kSegTok);
                 a.segs[s0 + s2] = make_int4(gexp, p0 + s2 * kSegTok, tk, col);
                 col += seg_rows(tk);
+            }
+            if (small) {
+                const int q0 = p0 + nlg * kSegTok;
+                const int b0 = kSqTok - pc0;
+                a.segs[bbase[b0] + bofs[b0]] = make_int4(gexp, q0, pc0, 0);
+                if (pc1 > 0) {
+                    const int b1 = kSqTok - pc1;
+                    a.segs[bbase[b1] + bofs[b1] + (b1 == b0 ? 1 : 0)] = make_int4(gexp, q0 + pc0, pc1, 0);
+                }
             }
         }
     }
@@ -578,9 +613,10 @@ __global__ void __launch_bounds__(kBGThreads, 1) b_topk_group_kernel(const __gri
         atomicMax(a.stats + 2, s_maxcnt);
         atomicAdd(a.stats + 3, 1u);
         if (!pairs_ok) raise_error(a.err, DM_DEVERR_CAPACITY);
-        a.work[0] = (pairs_ok && ep_ok) ? total_segs : 0;
+        a.work[0] = (pairs_ok && ep_ok) ? total_lg : 0;    // large segments: [0, work[0])
         a.work[1] = 0;
         a.work[2] = 0;
+        a.work[3] = (pairs_ok && ep_ok) ? total_segs : 0;  // small ones: [work[0], work[3])
     }
 }
 
@@ -617,6 +653,7 @@ cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchB
     a.epoch = bb.ep_epoch;
     a.slot_of = slot_of;
     a.E_res = d.E_res;
+    a.sm_tok = expert_q4_supported(d.H, d.I, d.G) ? kSmTok : 0;
     a.err = b.err;
     return launch_kernel(lc, b_topk_group_kernel, dim3(1), dim3(kBGThreads), b_topk_group_smem(d.E, d.topk), a);
 }
@@ -780,6 +817,7 @@ cudaError_t launch_b_argmax(const LaunchCfg& lc, const Dims& d, const BatchBuffe
 }
 
 cudaError_t b_experts_set_attrs();
+cudaError_t b_experts_q4_set_attrs();
 
 cudaError_t batch_set_attrs() {
     cudaError_t e = cudaSuccess;
@@ -797,6 +835,7 @@ cudaError_t batch_set_attrs() {
         e = cudaFuncSetAttribute(b_topk_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(b_topk_group_smem(1023, kMaxTopK)));
     if (e == cudaSuccess) e = b_experts_set_attrs();
+    if (e == cudaSuccess) e = b_experts_q4_set_attrs();
     return e;
 }
 

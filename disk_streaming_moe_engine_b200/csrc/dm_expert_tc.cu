@@ -74,6 +74,7 @@
 #include <cuda.h>
 
 #include "dm_kernels.h"
+#include "dm_q4mma.cuh"
 #include "dm_tc.cuh"
 
 namespace dm {
@@ -478,7 +479,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) b_expert_tc_kernel(const __grid
     if (!GATEUP && a.ep.world > 1) __threadfence_system();
 }
 
-// ---- staging of the gate/up operand: each segment's token rows as hi/lo fp16 tiles ----
+// ---- staging of the gate/up operands: each large segment's token rows as hi/lo fp16
+// tiles; each small segment's token rows as digit records (one per pair) ----
 struct XStageArgs {
     const int4* segs;
     const int* work;
@@ -486,12 +488,13 @@ struct XStageArgs {
     int n, K;
     EpView ep;          // the normalised MoE inputs of every source rank (peer memory: plain loads)
     uint8_t* stage;
+    uint8_t* xrec;      // small segments: [pairs] records of vrec_bytes(K) bytes
     uint32_t* err;
 };
 
 __global__ void __launch_bounds__(256) b_xstage_kernel(const __grid_constant__ XStageArgs a) {
     pdl_wait();
-    const int nseg = a.work[0];
+    const int nseg = a.work[0], nall = a.work[3];
     pdl_launch_dependents();
     const int units = a.K / 8;
     // segments over grid.y, (token, 16-byte unit) over grid.x: every row unit is one thread
@@ -522,6 +525,20 @@ __global__ void __launch_bounds__(256) b_xstage_kernel(const __grid_constant__ X
                 make_uint4(hw[0], hw[1], hw[2], hw[3]);
             *reinterpret_cast<uint4*>(tile + (nl >> 3) * 1024 + (nl & 7) * 128 + ((u ^ (nl & 7)) << 4)) =
                 make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+    }
+    // small segments: one warp per 32 elements of a token row (one half of a scale group,
+    // which takes its own digit unit)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int halves = a.K / 32, rb = vrec_bytes(a.K), vfb = vfrag_bytes(a.K);
+    for (int s = nseg + blockIdx.y; s < nall; s += gridDim.y) {
+        const int4 sg = a.segs[s];
+        for (int u = blockIdx.x * nw + warp; u < sg.z * halves; u += gridDim.x * nw) {
+            const int tok = u / halves, k = (u % halves) * 32 + lane;
+            const int src = a.pair_src[sg.y + tok] >> 5;
+            const float* row = a.ep.xn[src / a.n] + static_cast<size_t>(src % a.n) * a.K;
+            int8_t* vf = reinterpret_cast<int8_t*>(a.xrec + static_cast<size_t>(sg.y + tok) * rb);
+            vgroup_build_half(vf, reinterpret_cast<VGroup*>(vf + vfb), k, row[k]);
         }
     }
 }
@@ -557,6 +574,18 @@ static cudaError_t launch_tc_proj(const LaunchCfg& lc, int K, bool gateup, const
     return cudaErrorInvalidValue;
 }
 
+// Whether a step of n rows per rank can hold a segment of more than kSmTok tokens (the
+// tcgen05 kernels' work): a routed expert takes at most one pair per row of every rank of
+// the group, the shared expert one per row of this rank.
+static bool may_have_large(const Dims& d, const BatchBuffers& bb, int n) {
+    if (!expert_q4_supported(d.H, d.I, d.G)) return true;
+    return static_cast<int64_t>(n) * (bb.ep.world > 1 ? bb.ep.world : 1) > kSmTok;
+}
+
+int b_expert_launches(const Dims& d, const BatchBuffers& bb, int n) {
+    return 1 + (expert_q4_supported(d.H, d.I, d.G) ? 2 : 0) + (may_have_large(d, bb, n) ? 2 : 0);
+}
+
 cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
                              const Buffers& b, int n) {
     if (!w.tm_gu || !w.tm_dn || !expert_tc_supported(d.H) || !expert_tc_supported(d.I) || d.I % 64 || d.H % 128)
@@ -569,9 +598,14 @@ cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w
     xs.K = d.H;
     xs.ep = bb.ep;
     xs.stage = bb.xgu;
+    xs.xrec = bb.xrec;
     xs.err = b.err;
     cudaError_t e = launch_kernel(lc, b_xstage_kernel, dim3(8, lc.num_sms), dim3(256), 0, xs);
     if (e != cudaSuccess) return e;
+    // small segments (integer path), then the large ones (tcgen05), per projection
+    const bool q4 = expert_q4_supported(d.H, d.I, d.G);
+    if (q4 && (e = launch_b_experts_q4(lc, d, w, bb, b, n, true)) != cudaSuccess) return e;
+    if (!may_have_large(d, bb, n)) return q4 ? launch_b_experts_q4(lc, d, w, bb, b, n, false) : cudaSuccess;
     TcExpArgs a{};
     a.experts = w.experts;
     a.expert_bytes = d.expert_bytes;
@@ -594,6 +628,7 @@ cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w
     a.wmap = *static_cast<const CUtensorMap*>(w.tm_gu);
     e = launch_tc_proj(lc, d.H, true, a);
     if (e != cudaSuccess) return e;
+    if (q4 && (e = launch_b_experts_q4(lc, d, w, bb, b, n, false)) != cudaSuccess) return e;
     // down: K = I, tiles of 128 output rows
     a.proj_off = static_cast<int64_t>(d.gu_chunks) * d.gu_chunk_bytes;
     a.chunk_bytes = d.d_chunk_bytes;

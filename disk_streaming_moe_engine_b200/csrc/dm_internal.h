@@ -123,6 +123,8 @@ constexpr int kMaxBatch = 64;       // rows of one rank's batched step
 constexpr int kMaxRanks = 8;        // expert-parallel group (one process per GPU)
 constexpr int kSrcWords = kMaxBatch * kMaxRanks / 64;  // 64-bit words of a source-row mask
 constexpr int kSegTok = 32;         // tokens of one expert segment (hi + lo rows: 64 accumulator columns)
+constexpr int kSmTok = 8;           // segments of at most this many tokens use the small-segment kernels
+constexpr int kSqTok = 4;           // ... split into pieces of at most this many tokens
 constexpr int kHeadChunks = 32;     // vocabulary chunks of the batched argmax
 
 // The expert-parallel group as seen by one rank: every rank runs the same batched step on
@@ -166,7 +168,7 @@ struct BatchBuffers {
     unsigned* rcnt;       // [cap + 1] finished router CTAs per block of rows
     uint32_t* err;        // the context's device error word
     int4* segs;           // [max_segs] (expert, first pair, tokens, 0); expert E = shared
-    int* work;            // [4] segments, gate/up work counter, down work counter, spare
+    int* work;            // [4] large segments, gate/up work counter, down work counter, all segments
     unsigned* stats;      // [4] routing statistics since the last reset: sum over layer-steps of
                           //     experts touched (by this rank), sum of segments, max rows of one
                           //     routed expert, layer-steps
@@ -174,6 +176,8 @@ struct BatchBuffers {
     int max_cols = 0;     // staged operand rows: every segment's hi/lo rows padded to 16
     uint8_t* xgu;         // [max_cols][H] bf16: staged gate/up operand (64-column swizzled tiles per segment)
     uint8_t* xdn;         // [max_cols][I] bf16: staged down operand (SwiGLU activations, hi/lo)
+    uint8_t* xrec;        // [max_pairs] small-segment gate/up inputs as digit records (q4_vrec_bytes(H))
+    uint8_t* hrec;        // [max_pairs] small-segment down inputs (SwiGLU activations, q4_vrec_bytes(I))
     float* eout;          // [cap][topk + 1][H] expert outputs of this rank's rows (k = topk: shared)
     // prefill only (rows = prompt tokens of one sequence)
     float* pf_raw;        // [cap][qkv_dim] pre-conv GDN projections of the chunk's tokens
@@ -196,6 +200,12 @@ constexpr int kTrCta = 64;        // per-CTA region: decode attention, 6 slots p
 constexpr int kTrCtaSlots = 6;    // start, ready, pages done, cluster merged, end, SM id
 constexpr int kTrMoeCta = 1024;   // per-CTA region: fused MoE, 8 slots per CTA
 constexpr int kTrMoeCtaSlots = 8; // start, ready, ids known, up data in, up done, barrier, end, SM id
+// small-segment expert kernels (after the tcgen05 experts' 640 stamps): per kernel 2 stamps
+// per CTA (entry, exit) for up to kTrQ4MaxCtas CTAs, then CTA 0's detail
+constexpr int kTrQ4 = kTrCta + 640;
+constexpr int kTrQ4MaxCtas = 160;
+constexpr int kTrQ4Detail = 40;
+constexpr int kTrQ4Slots = 2 * kTrQ4MaxCtas + kTrQ4Detail;
 // trace slot bases per kernel kind
 constexpr int kTrAttn = 0;   // 8 stamps
 constexpr int kTrMoe = 16;   // 16 stamps
@@ -295,6 +305,7 @@ cudaError_t launch_b_topk_group(const LaunchCfg& lc, const Dims& d, const BatchB
                                 int n, const int* slot_of = nullptr);
 cudaError_t launch_b_experts(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
                              const Buffers& b, int n);
+int b_expert_launches(const Dims& d, const BatchBuffers& bb, int n);  // kernels launch_b_experts launches
 cudaError_t launch_b_combine(const LaunchCfg& lc, const Dims& d, const BatchBuffers& bb, const float* xm, float* out,
                              int n);
 // Cross-rank barrier of the expert-parallel group (kind 0 or 1), one small kernel.
@@ -321,6 +332,11 @@ int pf_attn_nsplit(int num_sms, int Hkv, int n);
 bool pf_gdn_supported(const Dims& d);
 cudaError_t pf_attn_set_attrs();
 bool expert_tc_supported(int K);
+// Small-segment expert kernels (integer mma.sync on the 4-bit rows, dm_expert_q4.cu).
+bool expert_q4_supported(int H, int I, int G);
+size_t q4_vrec_bytes(int K);  // bytes of one K-element input vector as a digit record
+cudaError_t launch_b_experts_q4(const LaunchCfg& lc, const Dims& d, const LayerW& w, const BatchBuffers& bb,
+                                const Buffers& b, int n, bool gateup);
 // SHA-256 (FIPS 180-4) of the concatenation of n buffers (dm_sha256.cu).
 void sha256_parts(const uint8_t* const* parts, const size_t* sizes, int n, uint8_t out[32]);
 

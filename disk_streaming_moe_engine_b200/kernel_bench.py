@@ -25,6 +25,9 @@ from .engine import Engine
 KERNELS = {"in_proj": _lib.DM_KERNEL_MIXER_IN, "out_proj": _lib.DM_KERNEL_MIXER_OUT,
            "core": _lib.DM_KERNEL_MIXER_CORE, "router": _lib.DM_KERNEL_ROUTER, "moe": _lib.DM_KERNEL_MOE,
            "head": _lib.DM_KERNEL_HEAD}
+# trace slots of one small-segment expert kernel: entry and exit of up to 160 CTAs + CTA 0's detail
+Q4_MAX_CTAS = 160
+Q4_SLOTS = 2 * Q4_MAX_CTAS + 40
 # kernels of the batched step (--batch N): layer is the preset's attention or GDN layer
 BKERNELS = {"battn": _lib.DM_BKERNEL_ATTN, "bgdn": _lib.DM_BKERNEL_GDN_REC, "bexperts": _lib.DM_BKERNEL_EXPERTS,
             "brouter": _lib.DM_BKERNEL_ROUTER, "bgemm": _lib.DM_BKERNEL_GEMM_IN}
@@ -57,13 +60,25 @@ def batched(a, cfg):
             # accumulator ready / epilogue done, MMAs issued, commit issued, A ready, B ready
             eng.trace_enable(True)
             eng.time_batch_kernel(a.batch, BKERNELS[a.kernel], layer, 1)
-            t = eng.trace_read(64 + 640).astype(np.int64)[64:]
+            t = eng.trace_read(64 + 640 + 2 * Q4_SLOTS).astype(np.int64)
             eng.trace_enable(False)
             pipe = {}
-            for name, blk in (("gate_up", t[:320]), ("down", t[320:640])):
+            for name, blk in (("gate_up", t[64:384]), ("down", t[384:704])):
                 st = blk.reshape(-1, 10)
                 base = st[st > 0].min() if (st > 0).any() else 0
                 pipe[name] = [[int(v) - int(base) if v else None for v in row] for row in st]
+            # small-segment kernels (%globaltimer ns): every CTA's entry and exit, CTA 0's items
+            for name, off in (("q4_gate_up", 704), ("q4_down", 704 + Q4_SLOTS)):
+                blk = t[off:off + Q4_SLOTS]
+                ee = blk[:2 * Q4_MAX_CTAS].reshape(-1, 2)
+                ee = ee[(ee > 0).all(axis=1)]
+                if not len(ee):
+                    continue
+                base = int(ee[:, 0].min())
+                det = blk[2 * Q4_MAX_CTAS:]
+                pipe[name] = {"entry_max": int(ee[:, 0].max()) - base, "exit_min": int(ee[:, 1].min()) - base,
+                              "exit_med": int(np.median(ee[:, 1])) - base, "exit_max": int(ee[:, 1].max()) - base,
+                              "cta0": [int(v) - base if v else None for v in det[:33]]}
         print(json.dumps({"kernel": a.kernel, "batch": a.batch, "ctx": a.ctx, "layer": layer, "us": ms * 1e3,
                           "bytes": nbytes, "GBps": nbytes / (ms * 1e-3) / 1e9, "pipeline_us": pipe}))
 

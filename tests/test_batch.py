@@ -2,9 +2,11 @@
 
 Each batch row is checked against the CPU oracle run on its own sequence (same seeded
 weights and prompts): identical greedy ids, logits within BATCH_TOL relative (the batched
-dense projections use the hi/lo bf16 split of fp32 activations; the experts run on the
-tcgen05 tensor cores with each weight rounded once to fp16 and fp16 hi/lo activations).  The rows also agree with the single-sequence
-decode step of the same context.  rel(a, b) = max|a - b| / max|b|.
+dense projections use the hi/lo bf16 split of fp32 activations; experts with more than 8
+rows of a step run on the tcgen05 tensor cores with each weight rounded once to fp16 and
+fp16 hi/lo activations, experts with at most 8 on the integer path: raw nibbles times two
+8-bit digits per activation with a unit per 32 elements).  The rows also agree with the
+single-sequence decode step of the same context.  rel(a, b) = max|a - b| / max|b|.
 """
 import numpy as np
 import pytest
@@ -65,7 +67,8 @@ def _run_batch_vs_oracle(cfg, m, eng, prompt_lens, steps, seed):
 
 def test_batch_mini_ragged_matches_oracle(lib, oracle_lib):
     """Config 0 shape, 12 sequences with ragged histories (0..40 tokens, page edges),
-    6 batched steps: more rows than a segment (the shared expert spans two)."""
+    6 batched steps: the shared expert (12 rows) on the tcgen05 path, routed experts of
+    1-8 rows on the integer path (split into pieces of at most 4)."""
     cfg = preset("mini")
     m = synth.synth_model(cfg, 0)
     with Engine(cfg, RuntimeConfig.for_context(128, max_seqs=12)) as eng:
