@@ -3080,7 +3080,9 @@ int32_t dm_time_batch_kernel(dm_ctx* c, int32_t n, int32_t which, int32_t layer,
     if (layer < 0 || layer >= d.L) return set_err(c, DM_ERR_INVALID_ARG, "PROFILE", "profile", layer, "layer out of range");
     const LayerW& w = c->layers[layer];
     LaunchCfg lc = lcfg(c);
-    lc.pdl = false;
+    // a single kernel is timed alone; the experts are a sequence of kernels (staging, gate/up,
+    // down), launched as the step launches them: each lets the next one start early
+    lc.pdl = which == DM_BKERNEL_EXPERTS;
     cudaSetDevice(c->device);
     std::vector<int> slots(n);
     DM_CUDA(c, cudaMemcpy(slots.data(), c->bb.slots, sizeof(int) * n, cudaMemcpyDeviceToHost), "profile");

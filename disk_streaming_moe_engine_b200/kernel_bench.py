@@ -76,7 +76,7 @@ def batched(a, cfg):
                     continue
                 base = int(ee[:, 0].min())
                 det = blk[2 * Q4_MAX_CTAS:]
-                pipe[name] = {"entry_max": int(ee[:, 0].max()) - base, "exit_min": int(ee[:, 1].min()) - base,
+                pipe[name] = {"base_ns": base, "entry_max": int(ee[:, 0].max()) - base, "exit_min": int(ee[:, 1].min()) - base,
                               "exit_med": int(np.median(ee[:, 1])) - base, "exit_max": int(ee[:, 1].max()) - base,
                               "cta0": [int(v) - base if v else None for v in det[:33]]}
         print(json.dumps({"kernel": a.kernel, "batch": a.batch, "ctx": a.ctx, "layer": layer, "us": ms * 1e3,
