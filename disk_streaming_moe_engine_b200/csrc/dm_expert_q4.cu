@@ -17,21 +17,24 @@
 // expert records at the rate the copies allow.
 //
 // Work.  The grouping kernel lists the large segments first (segments [0, work[0]), the
-// tcgen05 kernels) and the small ones after them ([work[0], work[3])).  The staging
-// kernel writes each small-segment pair's input as a digit record (vrec_bytes(H) bytes,
-// pairs of a segment adjacent).  An item is (small segment, tile):
-//   gate/up  tile t = chunks 8t .. 8t + 7 (gate and up rows of intermediate indices
-//            64t .. 64t + 63: one scale group of the down projection's K).  Two warps per
+// tcgen05 kernels) and the small ones after them ([work[0], work[3])) as pieces of at most
+// kSqTok rows, pieces of 4 rows first, then 3, 2, 1.  The staging kernel writes each
+// piece's input rows as digit records (vrec_bytes(H) bytes per pair, the pairs of a piece
+// adjacent).  An item is (piece, tile):
+//   gate/up  tile t = chunks 4t .. 4t + 3 (gate and up rows of intermediate indices
+//            32t .. 32t + 31: one half group of the down projection's K).  Two warps per
 //            chunk, each half of the chunk's sets; the partial rows meet in shared memory
-//            and warps 2j, 2j + 1 form h = SiLU(gate) * up of token j and write its group
-//            straight into the down projection's digit record of the pair;
-//   down     tile t = chunks 16t .. 16t + 15 (output rows 256t .. 256t + 255), one warp
-//            per chunk; each token's rows go to the expert-output rows of its source rank
+//            (bounded mbarriers, no named barrier) and warp q of the group forms h =
+//            SiLU(gate) * up of token q and writes the half group straight into the down
+//            projection's digit record of the pair;
+//   down     tile t = chunks 8t .. 8t + 7 (output rows 128t .. 128t + 127), one warp per
+//            chunk; each token's rows go to the expert-output rows of its source rank
 //            (peer memory in an expert-parallel group: plain stores).
-// Items come from a counter per kernel (the grouping kernel zeroes it), so the CTAs that
-// finish early take more.  A producer warp (one thread) bulk-copies each item's input
-// records (four buffers) and, with one more copy, its chunks (a ring of item slots) ahead
-// of two groups of 8 consumer warps that take alternate items; every wait is bounded
+// Items come from a counter per kernel (work[1], work[2]; the grouping kernel zeroes
+// them), so the CTAs that finish early take more.  A producer warp (one thread) takes the
+// item indices two ahead and bulk-copies each item's input records (four buffers) and,
+// with one more copy, its chunks (adjacent in the record) into an item slot, ahead of two
+// groups of 8 consumer warps that take alternate items; every wait is bounded
 // (DM_WAIT_NS, then the error bit, all roles stop, the producer waits for its copies in
 // flight).
 #include <cuda.h>
