@@ -97,8 +97,8 @@ struct SqArgs {
     EpView ep;                // down: expert outputs of each source rank
     uint64_t* trace;          // %globaltimer stamps or null: [2c] CTA c entry, [2c + 1] exit; at
                               // [2 kTrQ4MaxCtas] CTA 0: 0 after the wait, per item i < 8 of the CTA:
-                              // 1 + 4i records issued, 2 + 4i last chunk issued, 3 + 4i the first
-                              // warp of its group has the chunk, 4 + 4i that warp is done with it
+                              // 1 + 4i records issued, 2 + 4i chunks issued, 3 + 4i the first
+                              // warp of its group has the chunks, 4 + 4i that warp is done with them
     uint32_t* err;
 };
 
@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(kSqThreads, 1) b_expert_q4_kernel(const __grid
 
     if (warp == kSqProdWarp) {
         // ---- producer (one thread): items from the kernel's counter (the lowest first:
-        // the grouping lists the heaviest pieces first), one ahead; per item its record
+        // the grouping lists the heaviest pieces first), indices two ahead; per item its record
         // buffer (ic % 4: group ic % 2 alternates two), the item into shared memory, its
         // input records, then its chunks into the ring.  A slot is refilled once its
         // readers have arrived on its empty barrier: their generic reads are ordered before
@@ -326,8 +326,8 @@ __global__ void __launch_bounds__(kSqThreads, 1) b_expert_q4_kernel(const __grid
     }
 }
 
-// gate/up takes K = H, down K = I; one item's chunks must fit the ring (8 rows of K = 4096
-// or 16 of K = 2048 do not)
+// gate/up takes K = H, down K = I; one item slot per group must fit the shared memory
+// (gate/up items of K = 4096 and down items of K = 2048 do not)
 #define DM_SQ_GU_INSTANCES(X) X(256) X(512) X(1024) X(2048)
 #define DM_SQ_DN_INSTANCES(X) X(128) X(256) X(512) X(1024)
 
