@@ -30,8 +30,9 @@
 //   down     tile t = chunks 8t .. 8t + 7 (output rows 128t .. 128t + 127), one warp per
 //            chunk; each token's rows go to the expert-output rows of its source rank
 //            (peer memory in an expert-parallel group: plain stores).
-// Items come from a counter per kernel (work[1], work[2]; the grouping kernel zeroes
-// them), so the CTAs that finish early take more.  A producer warp (one thread) takes the
+// A CTA's first item is its own index; the later ones come from a counter per kernel
+// (work[1], work[2], zeroed by the grouping kernel; item = grid size + count), so the CTAs
+// that finish early take more.  A producer warp (one thread) takes the
 // item indices two ahead and bulk-copies each item's input records (four buffers) and,
 // with one more copy, its chunks (adjacent in the record) into an item slot, ahead of two
 // groups of 8 consumer warps that take alternate items; every wait is bounded
@@ -171,12 +172,15 @@ __global__ void __launch_bounds__(kSqThreads, 1) b_expert_q4_kernel(const __grid
             int* counter = a.work + (GATEUP ? 1 : 2);
             uint32_t ic = 0, nc = 0;  // items begun, items whose chunks were copied
             bool ok = true;
-            // item indices two ahead, segment records one ahead: neither latency is waited for
-            int item = atomicAdd(counter, 1);
-            int nxt = atomicAdd(counter, 1);
+            // item indices two ahead, segment records one ahead: neither latency is waited for.
+            // A CTA's first item is its own index; the counter hands out the items from the
+            // grid size on (no atomic round trip before the first copy)
+            const int grid = static_cast<int>(gridDim.x);
+            int item = static_cast<int>(blockIdx.x);
+            int nxt = grid + atomicAdd(counter, 1);
             int4 sg = item < nitems ? a.segs[seg0 + item / a.tiles] : make_int4(0, 0, 0, 0);
             while (item < nitems && ok) {
-                const int nxt2 = nxt < nitems ? atomicAdd(counter, 1) : nitems;
+                const int nxt2 = nxt < nitems ? grid + atomicAdd(counter, 1) : nitems;
                 const int4 sg_next = nxt < nitems ? a.segs[seg0 + nxt / a.tiles] : sg;
                 const int t = item % a.tiles;
                 const int T = max(1, min(sg.z, kSqTok));
